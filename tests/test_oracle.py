@@ -1,0 +1,120 @@
+"""Pin the CPU oracle (``oracle/``) to the reference's own PyTorch oracles.
+
+The fixtures in ``tests/golden`` hold outputs and gradients of
+``iso_kdn_naive.py`` / ``diag_kdn_naive.py`` evaluated in float64
+(``tests/golden/make_golden.py``)."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def load(name):
+    with np.load(os.path.join(GOLDEN, f"{name}.npz")) as z:
+        return {k: torch.from_numpy(z[k]) for k in z.files}
+
+
+def close(actual, expected, rtol=1e-9, atol=1e-11):
+    actual = actual.double()
+    expected = expected.double()
+    err = (actual - expected).abs().max().item()
+    assert torch.allclose(actual, expected, rtol=rtol, atol=atol), err
+
+
+@pytest.mark.parametrize("tag", ["s1", "s05"])
+def test_iso_gain_matches_reference(tag):
+    d = load("iso_gain")
+    s = float(d[f"{tag}_posterior_scale"])
+    beta, da, dw, dr, dp = oracle.iso_gain_grads(d["a"], d["omega"], d["r"], d["initial_precision"], d["dbeta"], s)
+    _, _, p_final = oracle.iso_gain(d["a"].double(), d["omega"].double(), d["r"].double(), d["initial_precision"].double(), s)
+    close(beta, d[f"{tag}_beta"])
+    close(1.0 / p_final, d[f"{tag}_final_precision"])
+    close(da, d[f"{tag}_da"])
+    close(dw, d[f"{tag}_domega"])
+    close(dr, d[f"{tag}_dr"])
+    close(dp, d[f"{tag}_dprec"], rtol=1e-8)
+
+
+def test_diag_gain_matches_reference():
+    d = load("diag_gain")
+    raw_w = torch.zeros_like(d["omega"])
+    raw_r = torch.zeros_like(d["r"])
+    kappa, dk, da, dw_raw, dr_raw, dp = oracle.diag_gain_grads(
+        d["k"], d["alpha"], d["omega"], d["r"], d["initial_precision"], raw_w, raw_r, d["dkappa"]
+    )
+    _, p_final = oracle.diag_gain(d["k"].double(), d["alpha"].double(), d["omega"].double(), d["r"].double(), d["initial_precision"].double())
+    close(kappa, d["kappa"])
+    close(1.0 / p_final, d["final_precision"])
+    close(dk, d["dk"])
+    close(da, d["dalpha"])
+    close(dw_raw, d["domega"] * 0.5)  # sigmoid(0) = 1/2
+    close(dr_raw, d["dr"] * 0.5)
+    close(dp, d["dprec"], rtol=1e-8)
+
+
+@pytest.mark.parametrize("tag", ["iso", "diag"])
+def test_memory_recurrence_matches_reference(tag):
+    d = load(f"{tag}_memory")
+    gain = d["gain"]
+    names = ("q", "k", "v", "alpha", "gain", "S0")
+    leaves = {n: d[n].double().clone().requires_grad_(True) for n in names}
+    kappa = leaves["gain"][..., None] * leaves["k"] if tag == "iso" else leaves["gain"]
+    o, S = oracle.memory_recurrence(leaves["q"], leaves["k"], leaves["v"], leaves["alpha"], kappa, leaves["S0"], 0.3)
+    ((o * d["dO"].double()).sum() + (S * d["dS"].double()).sum()).backward()
+    close(o, d["o"])
+    close(S, d["S"])
+    for n in names:
+        close(leaves[n].grad, d["d" + n], rtol=1e-8, atol=1e-10)
+    assert gain.numel() > 0
+
+
+def test_iso_scan_matches_reference():
+    d = load("iso_scan")
+    out = oracle.scan_grads("iso", {k: d[k] for k in ("q", "k", "v", "g_cumsum", "beta")}, d["dO"])
+    close(out["o"], d["o"])
+    close(out["S_T"], d["S"])
+    for name in ("dq", "dk", "dv", "dg", "dbeta"):
+        close(out[name], d[name], rtol=1e-8, atol=1e-10)
+
+
+def test_diag_scan_matches_reference():
+    d = load("diag_scan")
+    out = oracle.scan_grads("diag", {k: d[k] for k in ("q", "k", "kappa", "v", "g_cumsum")}, d["dO"], scale=32 ** -0.5)
+    close(out["o"], d["o"])
+    close(out["S_T"], d["S"])
+    for name in ("dq", "dk", "dv", "dg", "dkappa"):
+        close(out[name], d[name], rtol=1e-8, atol=1e-10)
+
+
+def test_full_recurrences_match_reference():
+    d = load("full")
+    q, k, v, alpha = (d[n].double() for n in ("q", "k", "v", "alpha"))
+    H, K = q.shape[2], q.shape[3]
+    ones = torch.ones(H, dtype=torch.float64)
+    # isotropic: a = mean(alpha^2), unit-norm keys, info_scale = K -> posterior_scale 1
+    beta, _, p_final = oracle.iso_gain((alpha ** 2).mean(-1), d["omega_s"].double(), d["r"].double(), ones, 1.0)
+    S0 = torch.zeros(q.shape[0], H, K, v.shape[-1], dtype=torch.float64)
+    o, S = oracle.memory_recurrence(q, k, v, alpha, beta[..., None] * k, S0, K ** -0.5)
+    # the production gain assumes ||k||^2 = 1; these fp32-normalised keys are
+    # unit only to ~1e-7, which bounds the agreement here
+    close(o, d["iso_o"], rtol=1e-6, atol=1e-7)
+    close(S, d["iso_S"], rtol=1e-6, atol=1e-7)
+    close(1.0 / p_final, d["iso_precision"], rtol=1e-6)
+    kappa, p_diag = oracle.diag_gain(k, alpha, d["omega_v"].double(), d["r"].double(), ones)
+    o, S = oracle.memory_recurrence(q, k, v, alpha, kappa, S0, K ** -0.5)
+    close(o, d["diag_o"], rtol=1e-8)
+    close(S, d["diag_S"], rtol=1e-8)
+    close(1.0 / p_diag, d["diag_precision"], rtol=1e-8)
+
+
+def test_g_cumsum_roundtrip():
+    la = -torch.nn.functional.softplus(torch.randn(2, 100, 3, 4, dtype=torch.float64))
+    for chunk in (32, 64):
+        g = oracle.g_cumsum_from_log_alpha(la, chunk)
+        alpha = oracle.alpha_from_g_cumsum(g * oracle.LN2, chunk)
+        close(alpha.log(), la, rtol=1e-12, atol=1e-12)
