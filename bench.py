@@ -1,0 +1,381 @@
+"""Benchmark of the KDN scan hot path on B200 (the BASELINE.json metric).
+
+Step = one pass of the isotropic KDN hot path over one batch (config 1):
+``iso_kdn_gain`` + ``_chunk_kda_precumsum_paired`` forward and backward at
+B=4, T=4096, H=18, K=V=128, bf16 I/O with fp32 state, through the public
+operators.  Inputs are synthetic (seeded, config-1 distributions) and larger
+than L2 (about 0.5 GB per step), so no explicit L2 flush is needed.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--variant iso|diag] [--impl ours|reference]
+
+Under torchrun each rank runs its own batch of B=4 sequences (weak scaling,
+no collective on the data path); timing is max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (ROOT, os.path.join(ROOT, "kalman-delta-networks_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+METRIC = "KDN scan fwd+bwd Mtok/s/GPU (B4,T4096,H18,d128 bf16), % of roofline"
+B, T, H, D = 4, 4096, 18, 128
+# algorithmic (boundary) bytes per token-head, each tensor read or written once
+ISO_BYTES_PER_TH = {"scan_fwd": 1540, "scan_bwd": 2824, "gain": 48}
+DIAG_BYTES_PER_TH = {"scan_fwd": 2304, "scan_bwd": 4096, "gain_fwd": 2052, "gain_bwd": 3592}
+FLOPS_PER_TH = 540_672  # 3 * 2 * (3 d^2 + 5 C d), C = 64
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p.get("bf16_tflops", 1590.0)), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples = []
+        self._stop = threading.Event()
+        self._thread = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(
+                    ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits"],
+                    capture_output=True, text=True, timeout=5,
+                ).stdout.strip()
+                if out:
+                    self.samples.append([x.strip() for x in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        self._thread.join(timeout=10)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
+        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if s[2 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+# ----------------------------------------------------------------------------- inputs
+
+
+def make_iso(device, seed):
+    g = torch.Generator(device=device).manual_seed(seed)
+    sp = torch.nn.functional.softplus
+    x = {}
+    x["q"] = torch.randn(B, T, H, D, generator=g, device=device).bfloat16()
+    x["k"] = torch.randn(B, T, H, D, generator=g, device=device).bfloat16()
+    x["v"] = torch.randn(B, T, H, D, generator=g, device=device).bfloat16()
+    log_alpha = -sp(torch.randn(B, T, H, D, generator=g, device=device))
+    x["g_cumsum"] = (log_alpha.view(B, T // 64, 64, H, D).cumsum(2) * 1.4426950408889634).view(B, T, H, D).contiguous()
+    x["a"] = torch.exp(2 * log_alpha).mean(-1)
+    x["omega"] = sp(torch.randn(B, T, H, generator=g, device=device))
+    x["r"] = 0.01 + sp(torch.randn(B, T, H, generator=g, device=device))
+    x["prec"] = torch.ones(H, device=device)
+    x["dO"] = torch.randn(B, T, H, D, generator=g, device=device).bfloat16()
+    return x
+
+
+def make_diag(device, seed):
+    g = torch.Generator(device=device).manual_seed(seed)
+    sp = torch.nn.functional.softplus
+    nrm = lambda t: t * torch.rsqrt((t * t).sum(-1, keepdim=True) + 1e-6)  # noqa: E731
+    x = {}
+    x["q"] = nrm(torch.randn(B, T, H, D, generator=g, device=device)).bfloat16()
+    kk = nrm(torch.randn(B, T, H, D, generator=g, device=device))
+    x["k"] = kk.bfloat16()
+    x["k_gain"] = kk.float().contiguous()
+    x["v"] = torch.randn(B, T, H, D, generator=g, device=device).bfloat16()
+    log_alpha = -sp(torch.randn(B, T, H, D, generator=g, device=device))
+    x["alpha"] = torch.exp(log_alpha)
+    x["g_cumsum"] = (log_alpha.view(B, T // 32, 32, H, D).cumsum(2) * 1.4426950408889634).view(B, T, H, D).contiguous()
+    x["omega_raw"] = torch.randn(B, T, H, D, generator=g, device=device).bfloat16()
+    x["r_raw"] = torch.randn(B, T, H, generator=g, device=device).bfloat16()
+    x["omega"] = sp(x["omega_raw"].float())
+    x["r"] = 0.01 + sp(x["r_raw"].float())
+    x["prec"] = torch.ones(H, device=device)
+    x["dO"] = torch.randn(B, T, H, D, generator=g, device=device)
+    return x
+
+
+def leafify(x, names):
+    return {n: (x[n].detach().requires_grad_(True) if n in names else x[n]) for n in x}
+
+
+def step_iso(x):
+    from kdn_b200.iso_kdn_chunk import _chunk_kda_precumsum_paired, iso_kdn_gain
+
+    L = leafify(x, ("q", "k", "v", "g_cumsum", "a", "omega", "r", "prec"))
+    beta = iso_kdn_gain(L["a"], L["omega"], L["r"], L["prec"], head_dim=D, out_dtype=torch.float32)
+    o = _chunk_kda_precumsum_paired(q=L["q"], k=L["k"], v=L["v"], g_cumsum=L["g_cumsum"], beta=beta)
+    o.backward(x["dO"])
+    return L
+
+
+def step_diag(x):
+    from kdn_b200.diag_kdn_chunk import _diag_kdn_gain, chunk_kalman
+
+    L = leafify(x, ("q", "k", "v", "g_cumsum", "k_gain", "alpha", "prec", "omega_raw", "r_raw"))
+    kappa = _diag_kdn_gain(L["k_gain"], L["alpha"], L["omega"], L["r"], L["prec"], L["omega_raw"], L["r_raw"])
+    o = chunk_kalman(L["q"], L["k"], kappa, L["v"], L["g_cumsum"], float(D ** -0.5))
+    o.backward(x["dO"])
+    return L
+
+
+GRAD_NAMES = {"iso": ("q", "k", "v", "g_cumsum", "a", "omega", "r"),
+              "diag": ("q", "k", "v", "g_cumsum", "k_gain", "alpha", "omega_raw", "r_raw")}
+LAUNCHES_PER_STEP = {"iso": 5, "diag": 9}  # gain fwd 1|3, scan fwd 1, scan bwd 2, gain bwd 1|3
+
+
+def time_region(fn, steps, device):
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(device)
+    start.record()
+    for _ in range(steps):
+        fn()
+    stop.record()
+    torch.cuda.synchronize(device)
+    return start.elapsed_time(stop) / steps
+
+
+def per_op_times(variant, x, device, reps=5):
+    """Average device time of each public op call, forward and backward."""
+    from kdn_b200 import _scan
+    from kdn_b200 import _native as N
+
+    out = {}
+    if variant == "iso":
+        from kdn_b200.iso_kdn_chunk import iso_kdn_gain
+
+        beta = iso_kdn_gain(x["a"], x["omega"], x["r"], x["prec"], head_dim=D)
+        args = (N.KDN_ISO, x["q"], x["k"], x["v"], x["g_cumsum"], beta, D ** -0.5)
+        o, _, saved = _scan.scan_forward(*args)
+        out["scan_fwd_ms"] = time_region(lambda: _scan.scan_forward(*args), reps, device)
+        out["scan_bwd_ms"] = time_region(lambda: _scan.scan_backward(*args, saved, x["dO"]), reps, device)
+    else:
+        from kdn_b200.diag_kdn_chunk import _gain_forward
+
+        kappa, carry = _gain_forward(x["k_gain"], x["alpha"], x["omega"], x["r"], x["prec"])
+        out["gain_fwd_ms"] = time_region(
+            lambda: _gain_forward(x["k_gain"], x["alpha"], x["omega"], x["r"], x["prec"]), reps, device)
+        args = (N.KDN_DIAG, x["q"], x["k"], x["v"], x["g_cumsum"], kappa, D ** -0.5)
+        o, _, saved = _scan.scan_forward(*args)
+        out["scan_fwd_ms"] = time_region(lambda: _scan.scan_forward(*args), reps, device)
+        out["scan_bwd_ms"] = time_region(lambda: _scan.scan_backward(*args, saved, x["dO"]), reps, device)
+    return out
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+
+
+def cpu_baseline(variant, seconds_budget=20.0):
+    """The oracle (tokenwise PyTorch restatement of the reference recurrences,
+    fp32, autograd backward) on the host cores: a B=1, H=2 slice of the
+    workload, T grown until it takes a few seconds; tokens/s scaled to all 18
+    heads by (b,h) independence."""
+    import oracle
+
+    threads = torch.get_num_threads()
+    Tc = 256
+    while True:
+        t0 = time.perf_counter()
+        if variant == "iso":
+            d = oracle.make_iso_inputs(1, Tc, 2, seed=0)
+            oracle.scan_grads("iso", {n: d[n] for n in ("q", "k", "v", "g_cumsum", "beta")}, d["dO"],
+                              dtype=torch.float32)
+            oracle.iso_gain_grads(d["a"], d["omega"], d["r"], torch.ones(2), torch.ones(1, Tc, 2), dtype=torch.float32)
+        else:
+            d = oracle.make_diag_inputs(1, Tc, 2, seed=0)
+            kap, *_ = oracle.diag_gain_grads(d["k_gain"], d["alpha"], d["omega"], d["r"], d["initial_precision"],
+                                             d["omega_raw"], d["r_raw"], torch.ones(1, Tc, 2, D), dtype=torch.float32)
+            oracle.scan_grads("diag", {"q": d["q"], "k": d["k"], "kappa": kap.float(), "v": d["v"],
+                                       "g_cumsum": d["g_cumsum"]}, d["dO"], scale=D ** -0.5, dtype=torch.float32)
+        dt = time.perf_counter() - t0
+        if dt > 2.0 or Tc >= T or dt * 2 > seconds_budget:
+            break
+        Tc *= 2
+    token_heads_per_s = (Tc * 2) / dt
+    mtok = token_heads_per_s / H / 1e6
+    return {"value": mtok, "unit": "Mtok/s", "cores": threads, "kind": "port",
+            "sample": f"{variant} oracle fwd+bwd (fp32, autograd) on B=1,H=2,T={Tc}: {dt:.2f} s; "
+                      f"scaled to H=18 by (b,h) independence"}
+
+
+# ----------------------------------------------------------------------------- main
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--variant", choices=("iso", "diag"), default="iso")
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        runs = []
+        for _ in range(warmup):
+            cpu_baseline(args.variant, seconds_budget=5.0)
+        for _ in range(args.steps):
+            runs.append(cpu_baseline(args.variant, seconds_budget=10.0))
+        val = statistics.mean(r["value"] for r in runs)
+        cb = dict(runs[-1])
+        cb["value"] = val
+        print(json.dumps({
+            "impl": "reference", "metric": METRIC, "value": val, "unit": "Mtok/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+            "config": {"workload": f"{args.variant}_kdn gain+scan fwd+bwd, B1 H2 slice of B4 T4096 H18 d128"},
+            "cpu_baseline": cb, "e2e": {"value": val, "unit": "Mtok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }))
+        return
+
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+
+    x = (make_iso if args.variant == "iso" else make_diag)(device, seed=1234 + rank)
+    step = step_iso if args.variant == "iso" else step_diag
+    for _ in range(warmup):
+        step(x)
+    torch.cuda.synchronize(device)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    barrier()
+    torch.cuda.synchronize(device)
+    with ClockSampler(local) as clk:
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(args.steps):
+            step(x)
+        stop.record()
+        torch.cuda.synchronize(device)
+    barrier()
+    ms = start.elapsed_time(stop) / args.steps
+    if dist is not None:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+
+    tokens = B * T * world
+    value = tokens / (ms * 1e-3) / 1e6
+    hbm, tc, peak_kind = load_peaks()
+    th = B * T * H
+
+    # end to end through the public operators with host buffers
+    e2e = None
+    if not args.no_e2e:
+        names = GRAD_NAMES[args.variant]
+        host = {n: v.detach().cpu().pin_memory() for n, v in x.items()}
+        grads_host = {n: torch.empty(x[n].shape, dtype=x[n].dtype).pin_memory() for n in names}
+        h2d = sum(v.numel() * v.element_size() for v in host.values())
+        d2h = sum(v.numel() * v.element_size() for v in grads_host.values())
+
+        def e2e_step():
+            xd = {n: v.to(device, non_blocking=True) for n, v in host.items()}
+            L = step(xd)
+            for n in names:
+                grads_host[n].copy_(L[n].grad, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        barrier()
+        e2e_ms = time_region(e2e_step, max(2, min(args.steps, 5)), device)
+        if dist is not None:
+            t = torch.tensor([e2e_ms], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_ms = t.item()
+        e2e = {"value": tokens / (e2e_ms * 1e-3) / 1e6, "unit": "Mtok/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms}
+
+    ops = per_op_times(args.variant, x, device)
+    per_th = ISO_BYTES_PER_TH if args.variant == "iso" else DIAG_BYTES_PER_TH
+    # dominant kernel call: the scan backward (reverse state sweep + chunk-parallel gradients)
+    bwd_bytes = per_th["scan_bwd"] * th
+    achieved = bwd_bytes / (ops["scan_bwd_ms"] * 1e-3) / 1e9
+    step_bytes = sum(per_th.values()) * th
+    roofline = {
+        "kernel": "kdn_scan_bwd (scan_bwd_state + scan_bwd_chunk)",
+        "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+        "peak_kind": peak_kind, "traffic": None,
+        "step_frac": (step_bytes / (ms * 1e-3) / 1e9) / hbm,
+        "op_ms": ops,
+    }
+
+    out = {
+        "metric": METRIC, "value": value, "unit": "Mtok/s", "n_gpus": world, "steps": args.steps, "warmup": warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"{args.variant}_kdn gain+scan fwd+bwd B4 T4096 H18 d128 (config 1)" if args.variant == "iso"
+                   else "diag_kdn gain+scan fwd+bwd B4 T4096 H18 d128 (config 2)",
+                   "global_batch": B * world, "seq_len": T, "heads": H, "head_dim": D,
+                   "parallelism": f"batch-sharded x{world}", "l2": "inputs > L2 (no flush)"},
+        "gpu_launches": LAUNCHES_PER_STEP[args.variant] * args.steps,
+        "e2e": e2e,
+        "roofline": roofline,
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        out["cpu_baseline"] = cpu_baseline(args.variant)
+    if rank == 0:
+        print(json.dumps(out))
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

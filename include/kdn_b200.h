@@ -1,0 +1,169 @@
+/*
+ * kdn_b200 -- C ABI of the B200 (sm_100a) Kalman Delta Network scan library.
+ *
+ * Every entry point takes plain device pointers, int64 sizes and a CUDA stream.
+ * The library never allocates or frees device memory and never synchronises:
+ * the caller owns every input, output and workspace buffer (workspace sizes
+ * come from the *_workspace_bytes queries) and launches are asynchronous on
+ * `stream`.  Return value: KDN_OK (0) or a negative error code; the message of
+ * the last error on the calling thread is kdn_last_error().
+ *
+ * Tensor layouts follow the reference's kdn_ops boundary: [B,T,H,D] row-major
+ * contiguous for per-token vectors, [B,T,H] for per-token scalars, [H] for the
+ * per-head prior.  bf16 tensors are passed as `const void*` holding
+ * __nv_bfloat16.
+ *
+ * Each function names the reference interface it replaces
+ * (path:line within ngocbh/kalman-delta-networks).
+ */
+#ifndef KDN_B200_H_
+#define KDN_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* kdn_stream_t; /* == cudaStream_t */
+
+enum {
+  KDN_OK = 0,
+  KDN_ERR_INVALID = -1,   /* bad shape, null pointer or unsupported size */
+  KDN_ERR_WORKSPACE = -2, /* workspace smaller than the query returned   */
+  KDN_ERR_CUDA = -3,      /* a CUDA launch or runtime call failed        */
+};
+
+/* Version of this ABI (major * 100 + minor). */
+int kdn_version(void);
+/* Message of the last failed call on this thread ("" if none). */
+const char* kdn_last_error(void);
+
+/* ------------------------------------------------------------------------ *
+ * Isotropic gain scan.  Replaces the launches behind iso_kdn_gain
+ * (lit_gpt/kdn_ops/iso_kdn_chunk.py:1966) -> _iso_kdn_gain_forward (1599) and
+ * _iso_kdn_gain_backward (1797).
+ *
+ *   z_t = a_t p_{t-1} + omega_t,  beta_t = z_t / (r_t + z_t),
+ *   p_t = r_t z_t / (r_t + posterior_scale z_t),  p_{-1} = 1/initial_precision[h]
+ *
+ * a, omega, r, gain, p_prev, da, domega, dr, dgain: fp32 [B,T,H].
+ * initial_precision, d_initial_precision: fp32 [H].  p_prev (the covariance
+ * entering each token) is written by the forward when non-null and is required
+ * by the backward.  p_final (fp32 [B,H], nullable) receives p_{T-1}.
+ * d_initial_precision is overwritten (not accumulated).
+ * ------------------------------------------------------------------------ */
+size_t kdn_iso_gain_workspace_bytes(int64_t B, int64_t T, int64_t H);
+int kdn_iso_gain_fwd(const float* a, const float* omega, const float* r,
+                     const float* initial_precision, float* gain, float* p_prev,
+                     float* p_final, int64_t B, int64_t T, int64_t H,
+                     float posterior_scale, void* workspace,
+                     size_t workspace_bytes, kdn_stream_t stream);
+int kdn_iso_gain_bwd(const float* a, const float* omega, const float* r,
+                     const float* initial_precision, const float* dgain,
+                     const float* p_prev, float* da, float* domega, float* dr,
+                     float* d_initial_precision, int64_t B, int64_t T, int64_t H,
+                     float posterior_scale, void* workspace,
+                     size_t workspace_bytes, kdn_stream_t stream);
+
+/* ------------------------------------------------------------------------ *
+ * Diagonal gain scan.  Replaces _diag_kdn_gain (diag_kdn_chunk.py:2737) ->
+ * _diag_kdn_gain_forward (2499) / _diag_kdn_gain_backward (2569).
+ *
+ *   p_hat = alpha^2 p + omega,  kappa = p_hat k / (r + sum_c p_hat_c k_c^2),
+ *   p <- p_hat / (1 + K k^2 / r * p_hat),  p_{-1} = 1/initial_precision[h]
+ *
+ * k, alpha, omega, kappa, dkappa, dk, dalpha: fp32 [B,T,H,K]; r: fp32 [B,T,H];
+ * omega_raw, domega_raw: bf16 [B,T,H,K]; r_raw, dr_raw: bf16 [B,T,H];
+ * initial_precision, d_initial_precision: fp32 [H].  `carry` (fp32, size from
+ * kdn_diag_gain_carry_elems) is written by the forward and read by the
+ * backward.  p_final (fp32 [B,H,K], nullable) receives the final covariance.
+ * The backward fuses the softplus VJPs: domega_raw = dL/domega *
+ * sigmoid(omega_raw), dr_raw = dL/dr * sigmoid(r_raw).  K must be 64 or 128.
+ * ------------------------------------------------------------------------ */
+int64_t kdn_diag_gain_carry_elems(int64_t B, int64_t T, int64_t H, int64_t K);
+size_t kdn_diag_gain_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t K);
+int kdn_diag_gain_fwd(const float* k, const float* alpha, const float* omega,
+                      const float* r, const float* initial_precision,
+                      float* kappa, float* carry, float* p_final, int64_t B,
+                      int64_t T, int64_t H, int64_t K, void* workspace,
+                      size_t workspace_bytes, kdn_stream_t stream);
+int kdn_diag_gain_bwd(const float* k, const float* alpha, const float* omega,
+                      const float* r, const float* initial_precision,
+                      const void* omega_raw, const void* r_raw,
+                      const float* dkappa, const float* carry, float* dk,
+                      float* dalpha, void* domega_raw, void* dr_raw,
+                      float* d_initial_precision, int64_t B, int64_t T,
+                      int64_t H, int64_t K, void* workspace,
+                      size_t workspace_bytes, kdn_stream_t stream);
+
+/* ------------------------------------------------------------------------ *
+ * Chunked memory scan (both variants).
+ *
+ *   S_hat = Diag(alpha_t) S,  delta = v_t - k_t^T S_hat,
+ *   S = S_hat + kappa_t delta^T,  o_t = scale q_t^T S
+ *
+ * variant KDN_ISO replaces _chunk_kda_precumsum_paired (iso_kdn_chunk.py:2242,
+ * Function 2190): q and k are L2-normalised in the kernel (eps 1e-6),
+ * kappa_t = beta_t k_hat_t, g_cumsum is 64-local, o is bf16.
+ * variant KDN_DIAG replaces chunk_kalman (diag_kdn_chunk.py:3315, Function
+ * 3247): q, k used as given, kappa fp32 [B,T,H,K], g_cumsum 32-local, o fp32.
+ *
+ * q, k, v: bf16 [B,T,H,K|V]; g_cumsum: fp32 [B,T,H,K] (base-2 chunk-local
+ * inclusive prefix of ln alpha).  The backward returns dg in natural-log
+ * coordinates before the reverse chunk cumsum (the reference's paired
+ * cotangent, iso_kdn_chunk.py:2180-2186).
+ *
+ * Saved state (caller-owned, sizes from kdn_scan_saved_bytes): the forward
+ * writes the chunk-start memory states and the per-chunk triangular solve and
+ * query-key scores; the backward reads them.  Optional continuation buffers
+ * (fp32 [B,H,K,V], nullable): initial_state / final_state in the forward,
+ * d_final_state / d_initial_state in the backward (sequence parallelism).
+ * ------------------------------------------------------------------------ */
+enum { KDN_ISO = 0, KDN_DIAG = 1 };
+enum { KDN_PREC_BF16 = 0, KDN_PREC_FP32 = 1 }; /* tensor-core bf16 / fp32 debug */
+
+typedef struct KdnScanArgs {
+  int32_t variant;   /* KDN_ISO or KDN_DIAG */
+  int32_t precision; /* KDN_PREC_BF16 (product) or KDN_PREC_FP32 (debug) */
+  int64_t B, T, H, K, V;
+  float scale;
+  /* forward inputs */
+  const void* q;        /* bf16 [B,T,H,K] */
+  const void* k;        /* bf16 [B,T,H,K] */
+  const void* v;        /* bf16 [B,T,H,V] */
+  const float* g;       /* fp32 [B,T,H,K] */
+  const float* beta;    /* iso: fp32 [B,T,H] */
+  const float* kappa;   /* diag: fp32 [B,T,H,K] */
+  const float* initial_state; /* nullable fp32 [B,H,K,V] */
+  /* forward outputs */
+  void* o;              /* iso: bf16, diag: fp32 [B,T,H,V] */
+  float* final_state;   /* nullable fp32 [B,H,K,V] */
+  /* saved between forward and backward */
+  void* saved;          /* kdn_scan_saved_bytes */
+  /* backward inputs */
+  const void* dO;       /* iso: bf16, diag: fp32 [B,T,H,V] */
+  const float* d_final_state;   /* nullable fp32 [B,H,K,V] */
+  /* backward outputs */
+  void* dq;             /* bf16 [B,T,H,K] */
+  void* dk;             /* bf16 [B,T,H,K] */
+  void* dv;             /* bf16 [B,T,H,V] */
+  float* dg;            /* fp32 [B,T,H,K] */
+  float* dbeta;         /* iso: fp32 [B,T,H] */
+  float* dkappa;        /* diag: fp32 [B,T,H,K] */
+  float* d_initial_state;       /* nullable fp32 [B,H,K,V] */
+  /* scratch */
+  void* workspace;
+  size_t workspace_bytes;
+} KdnScanArgs;
+
+size_t kdn_scan_saved_bytes(const KdnScanArgs* args);
+size_t kdn_scan_workspace_bytes(const KdnScanArgs* args);
+int kdn_scan_fwd(const KdnScanArgs* args, kdn_stream_t stream);
+int kdn_scan_bwd(const KdnScanArgs* args, kdn_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KDN_B200_H_ */

@@ -1,0 +1,95 @@
+"""Host side of the chunked memory scan: buffer allocation and the two calls
+into ``kdn_scan_fwd`` / ``kdn_scan_bwd``.  Shared by the isotropic and the
+diagonal operator modules and by the sequence-parallel driver."""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _native as N
+
+KD = 128
+
+
+@dataclass
+class ScanSaved:
+    """What the forward leaves for the backward (besides the inputs)."""
+
+    saved: torch.Tensor  # uint8: T and Q per chunk (fp32), chunk-start states
+    precision: int
+
+
+def _args(variant, precision, q, v, scale) -> N.KdnScanArgs:
+    B, T, H, K = q.shape
+    a = N.KdnScanArgs()
+    a.variant = variant
+    a.precision = precision
+    a.B, a.T, a.H, a.K, a.V = B, T, H, K, v.shape[-1]
+    a.scale = float(scale)
+    return a
+
+
+def scan_forward(variant, q, k, v, g, gate, scale, initial_state=None, want_final_state=False):
+    """Run the forward.  ``gate`` is beta [B,T,H] (iso) or kappa [B,T,H,K]
+    (diag).  Returns ``(o, final_state or None, ScanSaved)``."""
+    N.require_cuda(q, k, v, g, gate)
+    lib = N.load_library()
+    prec = N.precision()
+    a = _args(variant, prec, q, v, scale)
+    saved = N.byte_buffer(lib.kdn_scan_saved_bytes(ctypes.byref(a)), q.device)
+    ws_bytes = lib.kdn_scan_workspace_bytes(ctypes.byref(a))
+    if prec == N.KDN_PREC_FP32:
+        ws = N.byte_buffer(ws_bytes, q.device)
+    else:
+        ws = None
+    o = torch.empty(v.shape, dtype=torch.bfloat16 if variant == N.KDN_ISO else torch.float32, device=q.device)
+    final = torch.empty(q.shape[0], q.shape[2], KD, v.shape[-1], dtype=torch.float32, device=q.device) if want_final_state else None
+    a.q, a.k, a.v, a.g = q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr()
+    if variant == N.KDN_ISO:
+        a.beta = gate.data_ptr()
+    else:
+        a.kappa = gate.data_ptr()
+    a.initial_state = N.ptr(initial_state)
+    a.o = o.data_ptr()
+    a.final_state = N.ptr(final)
+    a.saved = saved.data_ptr()
+    a.workspace = N.ptr(ws)
+    a.workspace_bytes = ws.numel() if ws is not None else 0
+    N.check(lib.kdn_scan_fwd(ctypes.byref(a), N.stream_of(q)), "kdn_scan_fwd")
+    return o, final, ScanSaved(saved, prec)
+
+
+def scan_backward(variant, q, k, v, g, gate, scale, saved: ScanSaved, dO, d_final_state=None, want_d_initial=False):
+    """Run the backward.  Returns ``(dq, dk, dv, dg, dgate, d_initial_state)``
+    where dgate is dbeta (iso) or dkappa (diag)."""
+    lib = N.load_library()
+    a = _args(variant, saved.precision, q, v, scale)
+    ws = N.byte_buffer(lib.kdn_scan_workspace_bytes(ctypes.byref(a)), q.device)
+    dq = torch.empty_like(q)
+    dk = torch.empty_like(k)
+    dv = torch.empty_like(v)
+    dg = torch.empty_like(g)
+    dgate = torch.empty_like(gate)
+    dS0 = (
+        torch.empty(q.shape[0], q.shape[2], KD, v.shape[-1], dtype=torch.float32, device=q.device)
+        if want_d_initial
+        else None
+    )
+    a.q, a.k, a.v, a.g = q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr()
+    if variant == N.KDN_ISO:
+        a.beta = gate.data_ptr()
+        a.dbeta = dgate.data_ptr()
+    else:
+        a.kappa = gate.data_ptr()
+        a.dkappa = dgate.data_ptr()
+    a.saved = saved.saved.data_ptr()
+    a.dO = dO.data_ptr()
+    a.d_final_state = N.ptr(d_final_state)
+    a.dq, a.dk, a.dv, a.dg = dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dg.data_ptr()
+    a.d_initial_state = N.ptr(dS0)
+    a.workspace = ws.data_ptr()
+    a.workspace_bytes = ws.numel()
+    N.check(lib.kdn_scan_bwd(ctypes.byref(a), N.stream_of(q)), "kdn_scan_bwd")
+    return dq, dk, dv, dg, dgate, dS0

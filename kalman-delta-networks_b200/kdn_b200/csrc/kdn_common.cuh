@@ -1,0 +1,248 @@
+// Shared device infrastructure of the kdn_b200 library (sm_100a).
+//
+// * Warp-level matrix products on mma.sync.m16n8k16 (bf16 operands, fp32
+//   accumulators) with operands staged in shared memory and fetched by
+//   ldmatrix, plus an fp32 SIMT twin with the identical accumulator layout
+//   (the fp32 "debug" precision of the library).
+// * cp.async row copies from HBM into shared memory.
+// * Host-side error state for the C ABI.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <type_traits>
+
+#include "../../../include/kdn_b200.h"
+
+namespace kdn {
+
+using bf16 = __nv_bfloat16;
+
+// ---------------------------------------------------------------------------
+// Host error state (kdn_api.cu)
+// ---------------------------------------------------------------------------
+int set_error(int code, const char* fmt, ...);
+int check_launch(const char* what);
+
+// ---------------------------------------------------------------------------
+// Scalar helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float to_f(float x) { return x; }
+__device__ __forceinline__ float to_f(bf16 x) { return __bfloat162float(x); }
+template <class T> __device__ __forceinline__ T from_f(float x);
+template <> __device__ __forceinline__ float from_f<float>(float x) { return x; }
+template <> __device__ __forceinline__ bf16 from_f<bf16>(float x) { return __float2bfloat16_rn(x); }
+
+__device__ __forceinline__ float ex2(float x) { return exp2f(x); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// ---------------------------------------------------------------------------
+// Tensor-core fragments (mma.sync.m16n8k16, row.col, bf16 x bf16 -> fp32).
+// Accumulator layout per lane (g = lane/4, t = lane%4): c0,c1 at row g,
+// cols 2t,2t+1; c2,c3 at row g+8, same cols.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+
+__device__ __forceinline__ void ldsm_x2(uint32_t (&r)[2], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];\n"
+               : "=r"(r[0]), "=r"(r[1])
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x2_t(uint32_t (&r)[2], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];\n"
+               : "=r"(r[0]), "=r"(r[1])
+               : "r"(smem_u32(p)));
+}
+
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+template <int MT, int NT>
+__device__ __forceinline__ void zero_acc(float (&acc)[MT][NT][4]) {
+#pragma unroll
+  for (int i = 0; i < MT; ++i)
+#pragma unroll
+    for (int j = 0; j < NT; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[i][j][e] = 0.f;
+}
+
+// Warp product acc[MT][NT] += A[m0 : m0+16MT, k0:k1] * B[k0:k1, n0 : n0+8NT].
+//   AK: A(m,k) = A[m*lda + k] (k contiguous), else A(m,k) = A[k*lda + m].
+//   BK: B(k,n) = B[n*ldb + k] (k contiguous), else B(k,n) = B[k*ldb + n].
+// k0, k1 multiples of 16.  bf16 operands live in shared memory with 16-byte
+// aligned rows.
+template <int MT, int NT, bool AK, bool BK>
+__device__ __forceinline__ void wgemm(float (&acc)[MT][NT][4], const bf16* A, int lda, const bf16* B, int ldb,
+                                      int m0, int n0, int k0, int k1) {
+  const int lane = threadIdx.x & 31;
+  const int mi = lane >> 3, r = lane & 7;
+  for (int k = k0; k < k1; k += 16) {
+    uint32_t a[MT][4];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      if constexpr (AK) {
+        ldsm_x4(a[mt], A + (size_t)(m0 + mt * 16 + (lane & 15)) * lda + k + (lane >> 4) * 8);
+      } else {
+        ldsm_x4_t(a[mt], A + (size_t)(k + (mi >> 1) * 8 + r) * lda + m0 + mt * 16 + (mi & 1) * 8);
+      }
+    }
+#pragma unroll
+    for (int nt = 0; nt + 1 < NT; nt += 2) {
+      uint32_t b[4];
+      if constexpr (BK) {
+        ldsm_x4(b, B + (size_t)(n0 + nt * 8 + (mi >> 1) * 8 + r) * ldb + k + (mi & 1) * 8);
+      } else {
+        ldsm_x4_t(b, B + (size_t)(k + (mi & 1) * 8 + r) * ldb + n0 + nt * 8 + (mi >> 1) * 8);
+      }
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        mma_16816(acc[mt][nt], a[mt], b[0], b[1]);
+        mma_16816(acc[mt][nt + 1], a[mt], b[2], b[3]);
+      }
+    }
+    if constexpr (NT % 2 == 1) {
+      constexpr int nt = NT - 1;
+      const int l = lane & 15, mj = l >> 3, rr = l & 7;
+      uint32_t b[2];
+      if constexpr (BK) {
+        ldsm_x2(b, B + (size_t)(n0 + nt * 8 + rr) * ldb + k + mj * 8);
+      } else {
+        ldsm_x2_t(b, B + (size_t)(k + mj * 8 + rr) * ldb + n0 + nt * 8);
+      }
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) mma_16816(acc[mt][nt], a[mt], b[0], b[1]);
+    }
+  }
+}
+
+// fp32 SIMT twin of wgemm: same accumulator layout, operands anywhere.
+template <int MT, int NT, bool AK, bool BK>
+__device__ __forceinline__ void wgemm(float (&acc)[MT][NT][4], const float* A, int lda, const float* B, int ldb,
+                                      int m0, int n0, int k0, int k1) {
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  for (int k = k0; k < k1; ++k) {
+    float alo[MT], ahi[MT];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      const int m = m0 + mt * 16 + g;
+      if constexpr (AK) {
+        alo[mt] = A[(size_t)m * lda + k];
+        ahi[mt] = A[(size_t)(m + 8) * lda + k];
+      } else {
+        alo[mt] = A[(size_t)k * lda + m];
+        ahi[mt] = A[(size_t)k * lda + m + 8];
+      }
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const int n = n0 + nt * 8 + 2 * t;
+      float b0, b1;
+      if constexpr (BK) {
+        b0 = B[(size_t)n * ldb + k];
+        b1 = B[(size_t)(n + 1) * ldb + k];
+      } else {
+        b0 = B[(size_t)k * ldb + n];
+        b1 = B[(size_t)k * ldb + n + 1];
+      }
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        acc[mt][nt][0] = fmaf(alo[mt], b0, acc[mt][nt][0]);
+        acc[mt][nt][1] = fmaf(alo[mt], b1, acc[mt][nt][1]);
+        acc[mt][nt][2] = fmaf(ahi[mt], b0, acc[mt][nt][2]);
+        acc[mt][nt][3] = fmaf(ahi[mt], b1, acc[mt][nt][3]);
+      }
+    }
+  }
+}
+
+// Visit the (row, col) coordinates a lane holds in an accumulator tile.
+// f(mt, nt, e, row, col) for every element.
+template <int MT, int NT, class F>
+__device__ __forceinline__ void for_acc(int m0, int n0, F&& f) {
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) f(mt, nt, e, m0 + mt * 16 + g + (e >> 1) * 8, n0 + nt * 8 + 2 * t + (e & 1));
+}
+
+// Store an accumulator tile to a row-major buffer (ld elements), converting.
+template <class T, int MT, int NT>
+__device__ __forceinline__ void store_acc(T* dst, int ld, const float (&acc)[MT][NT][4], int m0, int n0) {
+  for_acc<MT, NT>(m0, n0, [&](int mt, int nt, int e, int row, int col) {
+    dst[(size_t)row * ld + col] = from_f<T>(acc[mt][nt][e]);
+  });
+}
+
+// ---------------------------------------------------------------------------
+// Asynchronous copies HBM -> shared (16-byte granules, L2-only caching).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(smem)), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::); }
+
+// Copy `rows` rows of `row_bytes` (multiple of 16) from a strided global
+// source into a padded destination.  Rows >= valid are zero-filled.  `smem`
+// selects cp.async (shared destination) or plain copies (global destination,
+// fp32 debug precision).
+template <bool SMEM>
+__device__ __forceinline__ void copy_rows(void* dst, size_t dst_stride, const void* src, size_t src_stride,
+                                          int rows, int valid, int row_bytes) {
+  const int per_row = row_bytes / 16;
+  const int total = rows * per_row;
+  for (int i = threadIdx.x; i < total; i += blockDim.x) {
+    const int row = i / per_row, col = i - row * per_row;
+    char* d = static_cast<char*>(dst) + row * dst_stride + col * 16;
+    if (row < valid) {
+      const char* s = static_cast<const char*>(src) + row * src_stride + col * 16;
+      if constexpr (SMEM) {
+        cp_async16(d, s);
+      } else {
+        *reinterpret_cast<int4*>(d) = *reinterpret_cast<const int4*>(s);
+      }
+    } else {
+      *reinterpret_cast<int4*>(d) = make_int4(0, 0, 0, 0);
+    }
+  }
+}
+
+__host__ __device__ constexpr size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+}  // namespace kdn

@@ -1,0 +1,552 @@
+// Covariance ("gain") scans of the isotropic and diagonal Kalman Delta Network.
+//
+// Both recurrences are Moebius maps of the covariance p, so a stream of T
+// tokens is scanned in three phases: per-segment map composition, a carry over
+// segments, then an exact per-token re-run from the carried covariance.  The
+// backward is the reverse affine adjoint scan lambda_{t-1} = A_t lambda_t + B_t
+// in the same three phases.
+//
+// Isotropic (one CTA per (b,h), one segment per thread, block-level scan of
+// the 2x2 maps): lit_gpt/kdn_ops/iso_kdn_chunk.py:1464-1598 (forward) and
+// 1667-1850 (backward) define the recurrence and its adjoint.
+// Diagonal (one thread per key channel, 64-token segments, per-token channel
+// reductions by warp transpose-reduce): diag_kdn_chunk.py:374-701 and the
+// oracle diag_kdn_naive.py:256-276.
+#include "kdn_common.cuh"
+
+namespace kdn {
+namespace {
+
+constexpr int kIsoThreads = 256;
+constexpr int kDiagSeg = 64;
+
+struct Mob {  // 2x2 Moebius map p -> (A p + B) / (C p + D)
+  float A, B, C, D;
+};
+
+__device__ __forceinline__ Mob mob_mul(const Mob& x, const Mob& y) {  // x after y
+  Mob z{x.A * y.A + x.B * y.C, x.A * y.B + x.B * y.D, x.C * y.A + x.D * y.C, x.C * y.B + x.D * y.D};
+  float m = fmaxf(fmaxf(fabsf(z.A), fabsf(z.B)), fmaxf(fabsf(z.C), fabsf(z.D)));
+  float inv = 1.f / fmaxf(m, 1e-30f);
+  return Mob{z.A * inv, z.B * inv, z.C * inv, z.D * inv};
+}
+__device__ __forceinline__ float mob_apply(const Mob& m, float p) { return (m.A * p + m.B) / (m.C * p + m.D); }
+
+__device__ __forceinline__ Mob shfl_mob(const Mob& m, int delta, bool up) {
+  Mob r;
+  if (up) {
+    r.A = __shfl_up_sync(0xffffffffu, m.A, delta);
+    r.B = __shfl_up_sync(0xffffffffu, m.B, delta);
+    r.C = __shfl_up_sync(0xffffffffu, m.C, delta);
+    r.D = __shfl_up_sync(0xffffffffu, m.D, delta);
+  } else {
+    r.A = __shfl_down_sync(0xffffffffu, m.A, delta);
+    r.B = __shfl_down_sync(0xffffffffu, m.B, delta);
+    r.C = __shfl_down_sync(0xffffffffu, m.C, delta);
+    r.D = __shfl_down_sync(0xffffffffu, m.D, delta);
+  }
+  return r;
+}
+
+// Exclusive prefix (in token order, later maps on the left) of one Moebius
+// map per thread across the block.
+__device__ Mob block_exclusive_mob(Mob x) {
+  __shared__ Mob warp_tot[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  Mob y = x;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    Mob o = shfl_mob(y, d, true);
+    if (lane >= d) y = mob_mul(y, o);
+  }
+  Mob excl = shfl_mob(y, 1, true);
+  if (lane == 0) excl = Mob{1.f, 0.f, 0.f, 1.f};
+  if (lane == 31) warp_tot[warp] = y;
+  __syncthreads();
+  Mob pre{1.f, 0.f, 0.f, 1.f};
+  for (int w = 0; w < warp; ++w) pre = mob_mul(warp_tot[w], pre);
+  return mob_mul(excl, pre);
+}
+
+struct Aff {  // lambda -> A lambda + B
+  float A, B;
+};
+__device__ __forceinline__ Aff aff_after(const Aff& f, const Aff& g) {  // f o g
+  return Aff{f.A * g.A, f.A * g.B + f.B};
+}
+
+// Exclusive suffix (reverse token order) of one affine map per thread: thread
+// i receives F_{i+1} o ... o F_{n-1}.
+__device__ Aff block_exclusive_suffix_aff(Aff x) {
+  __shared__ Aff warp_tot[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  Aff z = x;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    Aff o{__shfl_down_sync(0xffffffffu, z.A, d), __shfl_down_sync(0xffffffffu, z.B, d)};
+    if (lane + d < 32) z = aff_after(z, o);
+  }
+  Aff excl{__shfl_down_sync(0xffffffffu, z.A, 1), __shfl_down_sync(0xffffffffu, z.B, 1)};
+  if (lane == 31) excl = Aff{1.f, 0.f};
+  if (lane == 0) warp_tot[warp] = z;
+  __syncthreads();
+  Aff suf{1.f, 0.f};
+  for (int w = nw - 1; w > warp; --w) suf = aff_after(warp_tot[w], suf);
+  return aff_after(excl, suf);
+}
+
+// ---------------------------------------------------------------------------
+// Isotropic gain
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kIsoThreads) iso_gain_fwd_kernel(const float* __restrict__ a,
+                                                                   const float* __restrict__ omega,
+                                                                   const float* __restrict__ r,
+                                                                   const float* __restrict__ init_prec,
+                                                                   float* __restrict__ gain, float* __restrict__ p_prev,
+                                                                   float* __restrict__ p_final, int T, int H, float s) {
+  const int bh = blockIdx.x, b = bh / H, h = bh - b * H;
+  const int seg = (T + blockDim.x - 1) / blockDim.x;
+  const int t0 = min(threadIdx.x * seg, T), t1 = min(t0 + seg, T);
+  const size_t base = (size_t)b * T * H + h;
+  Mob m{1.f, 0.f, 0.f, 1.f};
+  for (int t = t0; t < t1; ++t) {
+    const size_t off = base + (size_t)t * H;
+    const float at = a[off], wt = omega[off], rt = r[off];
+    m = mob_mul(Mob{rt * at, rt * wt, s * at, rt + s * wt}, m);
+  }
+  const Mob pre = block_exclusive_mob(m);
+  const float p0 = 1.f / init_prec[h];
+  float p = mob_apply(pre, p0);
+  for (int t = t0; t < t1; ++t) {
+    const size_t off = base + (size_t)t * H;
+    const float at = a[off], wt = omega[off], rt = r[off];
+    if (p_prev) p_prev[off] = p;
+    const float z = at * p + wt;
+    const float beta = z / (rt + z);
+    gain[off] = beta;
+    p = (s == 1.f) ? rt * beta : rt * z / (rt + s * z);
+  }
+  if (p_final) {
+    if (T == 0 && threadIdx.x == 0) p_final[bh] = p0;
+    if (t1 == T && t0 < t1) p_final[bh] = p;
+  }
+}
+
+__global__ void __launch_bounds__(kIsoThreads) iso_gain_bwd_kernel(
+    const float* __restrict__ a, const float* __restrict__ omega, const float* __restrict__ r,
+    const float* __restrict__ init_prec, const float* __restrict__ dgain, const float* __restrict__ p_prev,
+    float* __restrict__ da, float* __restrict__ domega, float* __restrict__ dr, float* __restrict__ dinit, int T,
+    int H, float s) {
+  const int bh = blockIdx.x, b = bh / H, h = bh - b * H;
+  const int seg = (T + blockDim.x - 1) / blockDim.x;
+  const int t0 = min(threadIdx.x * seg, T), t1 = min(t0 + seg, T);
+  const size_t base = (size_t)b * T * H + h;
+  Aff f{1.f, 0.f};
+  for (int t = t1 - 1; t >= t0; --t) {
+    const size_t off = base + (size_t)t * H;
+    const float at = a[off], wt = omega[off], rt = r[off], dbt = dgain[off], pp = p_prev[off];
+    const float z = at * pp + wt;
+    const float gi = 1.f / (rt + z);
+    const float pr = rt / (rt + s * z);
+    // lambda_{t-1} = A_t lambda_t + B_t, so the segment map is
+    // F_{t0} o ... o F_{t1-1}; walking t downwards, F_t goes on the outside.
+    f = aff_after(Aff{at * pr * pr, at * dbt * rt * gi * gi}, f);
+  }
+  const Aff suf = block_exclusive_suffix_aff(f);
+  float lam = suf.B;
+  for (int t = t1 - 1; t >= t0; --t) {
+    const size_t off = base + (size_t)t * H;
+    const float at = a[off], wt = omega[off], rt = r[off], dbt = dgain[off], pp = p_prev[off];
+    const float z = at * pp + wt;
+    float zbar, drt;
+    if (s == 1.f) {
+      const float inv = 1.f / (rt + z), inv2 = inv * inv;
+      zbar = (dbt + rt * lam) * rt * inv2;
+      drt = z * (lam * z - dbt) * inv2;
+    } else {
+      const float gi = 1.f / (rt + z), gi2 = gi * gi;
+      const float pi = 1.f / (rt + s * z), pi2 = pi * pi;
+      zbar = dbt * rt * gi2 + lam * rt * rt * pi2;
+      drt = -dbt * z * gi2 + lam * s * z * z * pi2;
+    }
+    da[off] = zbar * pp;
+    domega[off] = zbar;
+    dr[off] = drt;
+    lam = at * zbar;
+  }
+  if (threadIdx.x == 0) {
+    const float ip = init_prec[h];
+    atomicAdd(dinit + h, -lam / (ip * ip));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Diagonal gain
+// ---------------------------------------------------------------------------
+// After this, lane j holds the warp sum of v[j] over the 32 lanes.
+__device__ __forceinline__ float transpose_reduce32(float (&v)[32]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    const bool upper = lane & off;
+#pragma unroll
+    for (int i = 0; i < off; ++i) {
+      const float send = upper ? v[i] : v[i + off];
+      const float keep = upper ? v[i + off] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+  }
+  return v[0];
+}
+
+// Sum of v[j] over all K threads of the block for each of the 32 tokens of a
+// group; result in red[j] (shared) after a barrier.
+template <int K>
+__device__ __forceinline__ void block_token_sums(float (&v)[32], float* red /* [K/32][32] */, float* out /*[32]*/) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  red[warp * 32 + lane] = transpose_reduce32(v);
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < K / 32; ++w) acc += red[w * 32 + threadIdx.x];
+    out[threadIdx.x] = acc;
+  }
+  __syncthreads();
+}
+
+template <int K>
+__global__ void __launch_bounds__(K) diag_gain_map_kernel(const float* __restrict__ k, const float* __restrict__ alpha,
+                                                          const float* __restrict__ omega, const float* __restrict__ r,
+                                                          float4* __restrict__ maps, int T, int H, int nseg) {
+  const int seg = blockIdx.x, bh = blockIdx.y, b = bh / H, h = bh - b * H, c = threadIdx.x;
+  const int t0 = seg * kDiagSeg, t1 = min(t0 + kDiagSeg, T);
+  Mob m{1.f, 0.f, 0.f, 1.f};
+  for (int t = t0; t < t1; ++t) {
+    const size_t row = ((size_t)b * T + t) * H + h;
+    const float kt = k[row * K + c], at = alpha[row * K + c], wt = omega[row * K + c], rt = r[row];
+    const float a2 = at * at, u = (float)K * kt * kt / rt;
+    m = mob_mul(Mob{a2, wt, u * a2, 1.f + u * wt}, m);
+  }
+  maps[((size_t)bh * nseg + seg) * K + c] = make_float4(m.A, m.B, m.C, m.D);
+}
+
+template <int K>
+__global__ void __launch_bounds__(K) diag_gain_carry_kernel(const float4* __restrict__ maps,
+                                                            const float* __restrict__ init_prec,
+                                                            float* __restrict__ carry, float* __restrict__ p_final,
+                                                            int H, int nseg) {
+  const int bh = blockIdx.x, h = bh % H, c = threadIdx.x;
+  float p = 1.f / init_prec[h];
+  for (int s = 0; s < nseg; ++s) {
+    carry[((size_t)bh * nseg + s) * K + c] = p;
+    const float4 m = maps[((size_t)bh * nseg + s) * K + c];
+    p = mob_apply(Mob{m.x, m.y, m.z, m.w}, p);
+  }
+  if (p_final) p_final[(size_t)bh * K + c] = p;
+}
+
+template <int K>
+__global__ void __launch_bounds__(K) diag_gain_emit_kernel(const float* __restrict__ k, const float* __restrict__ alpha,
+                                                           const float* __restrict__ omega,
+                                                           const float* __restrict__ r,
+                                                           const float* __restrict__ carry,
+                                                           float* __restrict__ kappa, int T, int H, int nseg) {
+  __shared__ float red[K];
+  __shared__ float tok[32];
+  const int seg = blockIdx.x, bh = blockIdx.y, b = bh / H, h = bh - b * H, c = threadIdx.x;
+  const int t0 = seg * kDiagSeg, t1 = min(t0 + kDiagSeg, T);
+  float p = carry[((size_t)bh * nseg + seg) * K + c];
+  for (int tg = t0; tg < t1; tg += 32) {
+    float num[32], pk2[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int t = tg + j;
+      num[j] = 0.f;
+      pk2[j] = 0.f;
+      if (t < t1) {
+        const size_t row = ((size_t)b * T + t) * H + h;
+        const float kt = k[row * K + c], at = alpha[row * K + c], wt = omega[row * K + c], rt = r[row];
+        const float ph = at * at * p + wt;
+        const float ksq = kt * kt;
+        num[j] = ph * kt;
+        pk2[j] = ph * ksq;
+        const float u = (float)K * ksq / rt;
+        p = ph / (1.f + u * ph);
+      }
+    }
+    block_token_sums<K>(pk2, red, tok);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int t = tg + j;
+      if (t < t1) {
+        const size_t row = ((size_t)b * T + t) * H + h;
+        kappa[row * K + c] = num[j] / (r[row] + tok[j]);
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// Backward pass A: per segment, re-run the covariance from the saved carry,
+// form the per-token channel reductions D_t = r_t + sum p_hat k^2 and
+// G_t = sum dkappa * kappa, and compose the reverse affine maps.
+template <int K>
+__global__ void __launch_bounds__(K) diag_gain_bwd_map_kernel(
+    const float* __restrict__ k, const float* __restrict__ alpha, const float* __restrict__ omega,
+    const float* __restrict__ r, const float* __restrict__ dkappa, const float* __restrict__ carry,
+    float2* __restrict__ maps, float2* __restrict__ dg_tok, int T, int H, int nseg) {
+  __shared__ float red[K];
+  __shared__ float tok_s1[32], tok_s2[32];
+  __shared__ float pprev_s[32][K];
+  const int seg = blockIdx.x, bh = blockIdx.y, b = bh / H, h = bh - b * H, c = threadIdx.x;
+  const int t0 = seg * kDiagSeg, t1 = min(t0 + kDiagSeg, T);
+  float p = carry[((size_t)bh * nseg + seg) * K + c];
+  Aff comp{1.f, 0.f};
+  for (int tg = t0; tg < t1; tg += 32) {
+    float s1[32], s2[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int t = tg + j;
+      s1[j] = 0.f;
+      s2[j] = 0.f;
+      if (t < t1) {
+        const size_t row = ((size_t)b * T + t) * H + h;
+        const float kt = k[row * K + c], at = alpha[row * K + c], wt = omega[row * K + c], rt = r[row];
+        const float dk = dkappa[row * K + c];
+        pprev_s[j][c] = p;
+        const float ph = at * at * p + wt;
+        s1[j] = ph * kt * kt;
+        s2[j] = dk * ph * kt;
+        const float u = (float)K * kt * kt / rt;
+        p = ph / (1.f + u * ph);
+      }
+    }
+    block_token_sums<K>(s1, red, tok_s1);
+    block_token_sums<K>(s2, red, tok_s2);
+    for (int j = 0; j < 32; ++j) {
+      const int t = tg + j;
+      if (t >= t1) break;
+      const size_t row = ((size_t)b * T + t) * H + h;
+      const float kt = k[row * K + c], at = alpha[row * K + c], wt = omega[row * K + c], rt = r[row];
+      const float dk = dkappa[row * K + c];
+      const float D = rt + tok_s1[j];
+      const float G = tok_s2[j] / D;
+      if (c == 0) dg_tok[(size_t)bh * T + t] = make_float2(D, G);
+      const float a2 = at * at;
+      const float ph = a2 * pprev_s[j][c] + wt;
+      const float hh = 1.f + (float)K * kt * kt / rt * ph;
+      const float pbar_gain = dk * kt / D - kt * kt * G / D;
+      comp = aff_after(comp, Aff{a2 / (hh * hh), a2 * pbar_gain});
+    }
+    __syncthreads();
+  }
+  maps[((size_t)bh * nseg + seg) * K + c] = make_float2(comp.A, comp.B);
+}
+
+template <int K>
+__global__ void __launch_bounds__(K) diag_gain_bwd_carry_kernel(const float2* __restrict__ maps,
+                                                                float* __restrict__ lam_carry, int nseg) {
+  const int bh = blockIdx.x, c = threadIdx.x;
+  float lam = 0.f;
+  for (int s = nseg - 1; s >= 0; --s) {
+    lam_carry[((size_t)bh * nseg + s) * K + c] = lam;
+    const float2 m = maps[((size_t)bh * nseg + s) * K + c];
+    lam = m.x * lam + m.y;
+  }
+}
+
+__device__ __forceinline__ float sigmoidf_(float x) { return 1.f / (1.f + __expf(-x)); }
+
+template <int K>
+__global__ void __launch_bounds__(K) diag_gain_bwd_emit_kernel(
+    const float* __restrict__ k, const float* __restrict__ alpha, const float* __restrict__ omega,
+    const float* __restrict__ r, const float* __restrict__ init_prec, const bf16* __restrict__ omega_raw,
+    const bf16* __restrict__ r_raw, const float* __restrict__ dkappa, const float* __restrict__ carry,
+    const float* __restrict__ lam_carry, const float2* __restrict__ dg_tok, float* __restrict__ dk_out,
+    float* __restrict__ dalpha, bf16* __restrict__ domega_raw, bf16* __restrict__ dr_raw,
+    float* __restrict__ dinit, int T, int H, int nseg) {
+  __shared__ float red[K];
+  __shared__ float tok[32];
+  __shared__ float pprev_s[kDiagSeg][K];
+  const int seg = blockIdx.x, bh = blockIdx.y, b = bh / H, h = bh - b * H, c = threadIdx.x;
+  const int t0 = seg * kDiagSeg, t1 = min(t0 + kDiagSeg, T);
+  const float Kf = (float)K;
+  float p = carry[((size_t)bh * nseg + seg) * K + c];
+  for (int t = t0; t < t1; ++t) {
+    const size_t row = ((size_t)b * T + t) * H + h;
+    const float kt = k[row * K + c], at = alpha[row * K + c], wt = omega[row * K + c], rt = r[row];
+    pprev_s[t - t0][c] = p;
+    const float ph = at * at * p + wt;
+    p = ph / (1.f + Kf * kt * kt / rt * ph);
+  }
+  float lam = lam_carry[((size_t)bh * nseg + seg) * K + c];
+  const int ngroups = (t1 - t0 + 31) / 32;
+  for (int gi = ngroups - 1; gi >= 0; --gi) {
+    const int tg = t0 + gi * 32;
+    float ur[32];
+#pragma unroll
+    for (int jj = 31; jj >= 0; --jj) {
+      const int t = tg + jj;
+      ur[jj] = 0.f;
+      if (t < t1) {
+        const size_t row = ((size_t)b * T + t) * H + h;
+        const float kt = k[row * K + c], at = alpha[row * K + c], wt = omega[row * K + c], rt = r[row];
+        const float dk = dkappa[row * K + c];
+        const float2 DG = dg_tok[(size_t)bh * T + t];
+        const float D = DG.x, G = DG.y;
+        const float pp = pprev_s[t - t0][c];
+        const float a2 = at * at, ksq = kt * kt;
+        const float ph = a2 * pp + wt;
+        const float u = Kf * ksq / rt;
+        const float hh = 1.f + u * ph;
+        const float pnext = ph / hh;
+        const float beta_c = ph / D;
+        const float pbar_gain = dk * kt / D - ksq * G / D;
+        const float kbar_gain = dk * beta_c - 2.f * ph * kt * G / D;
+        const float pbar_tot = pbar_gain + lam / (hh * hh);
+        const float ubar = -lam * pnext * pnext;
+        dk_out[row * K + c] = kbar_gain + ubar * (2.f * Kf * kt / rt);
+        dalpha[row * K + c] = 2.f * at * pp * pbar_tot;
+        domega_raw[row * K + c] = __float2bfloat16_rn(pbar_tot * sigmoidf_(__bfloat162float(omega_raw[row * K + c])));
+        ur[jj] = ubar * (-Kf * ksq / (rt * rt));
+        lam = a2 * pbar_tot;
+      }
+    }
+    block_token_sums<K>(ur, red, tok);
+    if (c < 32) {
+      const int t = tg + c;
+      if (t < t1) {
+        const size_t row = ((size_t)b * T + t) * H + h;
+        const float2 DG = dg_tok[(size_t)bh * T + t];
+        const float drt = -DG.y / DG.x + tok[c];
+        dr_raw[row] = __float2bfloat16_rn(drt * sigmoidf_(__bfloat162float(r_raw[row])));
+      }
+    }
+    __syncthreads();
+  }
+  if (seg == 0 && dinit) {
+    // p_{-1} = 1/mu, so d mu = -sum_c lambda_{-1,c} p_{-1,c}^2
+    const float p0 = pprev_s[0][c];
+    float v = -lam * p0 * p0;
+    v = warp_sum(v);
+    if ((c & 31) == 0) atomicAdd(dinit + h, v);
+  }
+}
+
+}  // namespace
+}  // namespace kdn
+
+using namespace kdn;
+
+extern "C" {
+
+size_t kdn_iso_gain_workspace_bytes(int64_t, int64_t, int64_t) { return 0; }
+
+int kdn_iso_gain_fwd(const float* a, const float* omega, const float* r, const float* init_prec, float* gain,
+                     float* p_prev, float* p_final, int64_t B, int64_t T, int64_t H, float s, void*, size_t,
+                     kdn_stream_t stream) {
+  if (B <= 0 || H <= 0 || T < 0 || !a || !omega || !r || !init_prec || !gain)
+    return set_error(KDN_ERR_INVALID, "kdn_iso_gain_fwd: invalid arguments");
+  if (T > INT32_MAX || B * H > INT32_MAX) return set_error(KDN_ERR_INVALID, "kdn_iso_gain_fwd: size too large");
+  iso_gain_fwd_kernel<<<(unsigned)(B * H), kIsoThreads, 0, (cudaStream_t)stream>>>(a, omega, r, init_prec, gain,
+                                                                                   p_prev, p_final, (int)T, (int)H, s);
+  return check_launch("iso_gain_fwd_kernel");
+}
+
+int kdn_iso_gain_bwd(const float* a, const float* omega, const float* r, const float* init_prec, const float* dgain,
+                     const float* p_prev, float* da, float* domega, float* dr, float* dinit, int64_t B, int64_t T,
+                     int64_t H, float s, void*, size_t, kdn_stream_t stream) {
+  if (B <= 0 || H <= 0 || T < 0 || !a || !omega || !r || !init_prec || !dgain || !da || !domega || !dr || !dinit ||
+      (T > 0 && !p_prev))
+    return set_error(KDN_ERR_INVALID, "kdn_iso_gain_bwd: invalid arguments");
+  if (T > INT32_MAX || B * H > INT32_MAX) return set_error(KDN_ERR_INVALID, "kdn_iso_gain_bwd: size too large");
+  cudaStream_t st = (cudaStream_t)stream;
+  if (cudaMemsetAsync(dinit, 0, sizeof(float) * H, st) != cudaSuccess) return check_launch("memset d_initial_precision");
+  if (T == 0) return KDN_OK;
+  iso_gain_bwd_kernel<<<(unsigned)(B * H), kIsoThreads, 0, st>>>(a, omega, r, init_prec, dgain, p_prev, da, domega,
+                                                                 dr, dinit, (int)T, (int)H, s);
+  return check_launch("iso_gain_bwd_kernel");
+}
+
+int64_t kdn_diag_gain_carry_elems(int64_t B, int64_t T, int64_t H, int64_t K) {
+  const int64_t nseg = (T + kDiagSeg - 1) / kDiagSeg;
+  return B * H * nseg * K;
+}
+
+size_t kdn_diag_gain_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t K) {
+  const int64_t nseg = (T + kDiagSeg - 1) / kDiagSeg;
+  const size_t maps = align_up(sizeof(float4) * B * H * nseg * K, 256);  // forward maps / backward maps+lam carry
+  const size_t bwd = align_up(sizeof(float2) * B * H * nseg * K, 256) + align_up(sizeof(float) * B * H * nseg * K, 256) +
+                     align_up(sizeof(float2) * B * H * T, 256);
+  return maps > bwd ? maps : bwd;
+}
+
+int kdn_diag_gain_fwd(const float* k, const float* alpha, const float* omega, const float* r, const float* init_prec,
+                      float* kappa, float* carry, float* p_final, int64_t B, int64_t T, int64_t H, int64_t K,
+                      void* ws, size_t ws_bytes, kdn_stream_t stream) {
+  if (B <= 0 || H <= 0 || T <= 0 || !k || !alpha || !omega || !r || !init_prec || !kappa || !carry)
+    return set_error(KDN_ERR_INVALID, "kdn_diag_gain_fwd: invalid arguments");
+  if (K != 64 && K != 128) return set_error(KDN_ERR_INVALID, "kdn_diag_gain_fwd: K must be 64 or 128, got %lld", (long long)K);
+  if (T > INT32_MAX || B * H > 65535 * 1024) return set_error(KDN_ERR_INVALID, "kdn_diag_gain_fwd: size too large");
+  if (ws_bytes < kdn_diag_gain_workspace_bytes(B, T, H, K) || !ws)
+    return set_error(KDN_ERR_WORKSPACE, "kdn_diag_gain_fwd: workspace too small");
+  const int nseg = (int)((T + kDiagSeg - 1) / kDiagSeg);
+  cudaStream_t st = (cudaStream_t)stream;
+  float4* maps = static_cast<float4*>(ws);
+  dim3 grid(nseg, (unsigned)(B * H));
+  if (K == 128) {
+    diag_gain_map_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, maps, (int)T, (int)H, nseg);
+    diag_gain_carry_kernel<128><<<(unsigned)(B * H), 128, 0, st>>>(maps, init_prec, carry, p_final, (int)H, nseg);
+    diag_gain_emit_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, carry, kappa, (int)T, (int)H, nseg);
+  } else {
+    diag_gain_map_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, maps, (int)T, (int)H, nseg);
+    diag_gain_carry_kernel<64><<<(unsigned)(B * H), 64, 0, st>>>(maps, init_prec, carry, p_final, (int)H, nseg);
+    diag_gain_emit_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, carry, kappa, (int)T, (int)H, nseg);
+  }
+  return check_launch("diag_gain_fwd kernels");
+}
+
+int kdn_diag_gain_bwd(const float* k, const float* alpha, const float* omega, const float* r, const float* init_prec,
+                      const void* omega_raw, const void* r_raw, const float* dkappa, const float* carry, float* dk,
+                      float* dalpha, void* domega_raw, void* dr_raw, float* dinit, int64_t B, int64_t T, int64_t H,
+                      int64_t K, void* ws, size_t ws_bytes, kdn_stream_t stream) {
+  if (B <= 0 || H <= 0 || T <= 0 || !k || !alpha || !omega || !r || !init_prec || !omega_raw || !r_raw || !dkappa ||
+      !carry || !dk || !dalpha || !domega_raw || !dr_raw)
+    return set_error(KDN_ERR_INVALID, "kdn_diag_gain_bwd: invalid arguments");
+  if (K != 64 && K != 128) return set_error(KDN_ERR_INVALID, "kdn_diag_gain_bwd: K must be 64 or 128, got %lld", (long long)K);
+  if (T > INT32_MAX || B * H > 65535 * 1024) return set_error(KDN_ERR_INVALID, "kdn_diag_gain_bwd: size too large");
+  if (ws_bytes < kdn_diag_gain_workspace_bytes(B, T, H, K) || !ws)
+    return set_error(KDN_ERR_WORKSPACE, "kdn_diag_gain_bwd: workspace too small");
+  const int nseg = (int)((T + kDiagSeg - 1) / kDiagSeg);
+  cudaStream_t st = (cudaStream_t)stream;
+  char* w = static_cast<char*>(ws);
+  float2* maps = reinterpret_cast<float2*>(w);
+  w += align_up(sizeof(float2) * B * H * nseg * K, 256);
+  float* lam = reinterpret_cast<float*>(w);
+  w += align_up(sizeof(float) * B * H * nseg * K, 256);
+  float2* dg_tok = reinterpret_cast<float2*>(w);
+  if (dinit && cudaMemsetAsync(dinit, 0, sizeof(float) * H, st) != cudaSuccess)
+    return check_launch("memset d_initial_precision");
+  dim3 grid(nseg, (unsigned)(B * H));
+  const bf16* wr = static_cast<const bf16*>(omega_raw);
+  const bf16* rr = static_cast<const bf16*>(r_raw);
+  if (K == 128) {
+    diag_gain_bwd_map_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, dkappa, carry, maps, dg_tok, (int)T,
+                                                        (int)H, nseg);
+    diag_gain_bwd_carry_kernel<128><<<(unsigned)(B * H), 128, 0, st>>>(maps, lam, nseg);
+    diag_gain_bwd_emit_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, init_prec, wr, rr, dkappa, carry, lam,
+                                                         dg_tok, dk, dalpha, static_cast<bf16*>(domega_raw),
+                                                         static_cast<bf16*>(dr_raw), dinit, (int)T, (int)H, nseg);
+  } else {
+    diag_gain_bwd_map_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, dkappa, carry, maps, dg_tok, (int)T, (int)H,
+                                                      nseg);
+    diag_gain_bwd_carry_kernel<64><<<(unsigned)(B * H), 64, 0, st>>>(maps, lam, nseg);
+    diag_gain_bwd_emit_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, init_prec, wr, rr, dkappa, carry, lam,
+                                                       dg_tok, dk, dalpha, static_cast<bf16*>(domega_raw),
+                                                       static_cast<bf16*>(dr_raw), dinit, (int)T, (int)H, nseg);
+  }
+  return check_launch("diag_gain_bwd kernels");
+}
+
+}  // extern "C"

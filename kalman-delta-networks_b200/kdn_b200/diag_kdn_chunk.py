@@ -1,0 +1,205 @@
+"""Diagonal KDN operators on B200: drop-in replacements for
+
+* ``_diag_kdn_gain`` (lit_gpt/kdn_ops/diag_kdn_chunk.py:2737)
+* ``chunk_kalman``   (lit_gpt/kdn_ops/diag_kdn_chunk.py:3315)
+
+with the reference's signatures, validation messages, tensor layouts and
+autograd contract, on the sm_100a kernels of ``libkdn_b200.so``.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+from torch.autograd.function import once_differentiable
+
+from . import _native as N
+from ._scan import ScanSaved, scan_backward, scan_forward
+
+_VECTOR_DTYPE = torch.bfloat16
+_STATE_DTYPE = torch.float32
+
+
+def _gain_forward(k, alpha, omega, r, initial_precision):
+    B, T, H, K = k.shape
+    N.require_cuda(k)
+    lib = N.load_library()
+    kappa = torch.empty_like(k, dtype=_STATE_DTYPE)
+    carry = torch.empty(lib.kdn_diag_gain_carry_elems(B, T, H, K), dtype=torch.float32, device=k.device)
+    ws = N.byte_buffer(lib.kdn_diag_gain_workspace_bytes(B, T, H, K), k.device)
+    N.check(
+        lib.kdn_diag_gain_fwd(
+            k.data_ptr(), alpha.data_ptr(), omega.data_ptr(), r.data_ptr(), initial_precision.data_ptr(),
+            kappa.data_ptr(), carry.data_ptr(), None, B, T, H, K, ws.data_ptr(), ws.numel(), N.stream_of(k),
+        ),
+        "kdn_diag_gain_fwd",
+    )
+    return kappa, carry
+
+
+def _gain_backward(k, alpha, omega, r, initial_precision, omega_raw, r_raw, dkappa, carry, need_initial):
+    B, T, H, K = k.shape
+    lib = N.load_library()
+    dkappa = torch.zeros_like(k) if dkappa is None else dkappa.float().contiguous()
+    dk = torch.empty_like(k, dtype=_STATE_DTYPE)
+    dalpha = torch.empty_like(alpha, dtype=_STATE_DTYPE)
+    domega_raw = torch.empty_like(omega_raw)
+    dr_raw = torch.empty_like(r_raw)
+    dinit = torch.empty((H,), dtype=_STATE_DTYPE, device=k.device) if need_initial else None
+    ws = N.byte_buffer(lib.kdn_diag_gain_workspace_bytes(B, T, H, K), k.device)
+    N.check(
+        lib.kdn_diag_gain_bwd(
+            k.data_ptr(), alpha.data_ptr(), omega.data_ptr(), r.data_ptr(), initial_precision.data_ptr(),
+            omega_raw.data_ptr(), r_raw.data_ptr(), dkappa.data_ptr(), carry.data_ptr(), dk.data_ptr(),
+            dalpha.data_ptr(), domega_raw.data_ptr(), dr_raw.data_ptr(), N.ptr(dinit), B, T, H, K,
+            ws.data_ptr(), ws.numel(), N.stream_of(k),
+        ),
+        "kdn_diag_gain_bwd",
+    )
+    return dk, dalpha, domega_raw, dr_raw, dinit
+
+
+class _DiagKdnGainFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, k, alpha, omega, r, initial_precision, omega_raw, r_raw):
+        kappa, carry = _gain_forward(k, alpha, omega, r, initial_precision)
+        ctx.save_for_backward(k, alpha, omega, r, initial_precision, omega_raw, r_raw, carry)
+        ctx.set_materialize_grads(False)
+        return kappa
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, dkappa):
+        k, alpha, omega, r, initial_precision, omega_raw, r_raw, carry = ctx.saved_tensors
+        needs = ctx.needs_input_grad
+        dk, dalpha, domega_raw, dr_raw, dinit = _gain_backward(
+            k, alpha, omega, r, initial_precision, omega_raw, r_raw, dkappa, carry, need_initial=needs[4]
+        )
+        return (
+            dk if needs[0] else None,
+            dalpha if needs[1] else None,
+            None,
+            None,
+            dinit if needs[4] else None,
+            domega_raw if needs[5] else None,
+            dr_raw if needs[6] else None,
+        )
+
+
+def _diag_kdn_gain(k_gain, alpha, omega, r, initial_precision, omega_raw, r_raw):
+    """Fixed-scale FP32 diagonal gain with fused raw-logit VJPs (diag_kdn_chunk.py:2737-2791)."""
+    tensors = {
+        "k_gain": k_gain,
+        "alpha": alpha,
+        "omega": omega,
+        "r": r,
+        "initial_precision": initial_precision,
+        "omega_raw": omega_raw,
+        "r_raw": r_raw,
+    }
+    for name, value in tensors.items():
+        if not isinstance(value, torch.Tensor):
+            raise TypeError(f"{name} must be a torch.Tensor")
+        if not value.is_cuda:
+            raise ValueError(f"{name} must be a CUDA tensor")
+        if value.device != k_gain.device:
+            raise ValueError("all DiagKDN gain inputs must share one CUDA device")
+        if not value.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+    if k_gain.ndim != 4:
+        raise ValueError("k_gain must have rank 4 [B,T,H,K]")
+    B, T, H, K = k_gain.shape
+    if min(B, T, H) <= 0 or K not in (64, 128):
+        raise ValueError("DiagKDN gain requires non-empty B/T/H and K in {64,128}")
+    expected = (B, T, H, K)
+    for name in ("alpha", "omega", "omega_raw"):
+        if tensors[name].shape != expected:
+            raise ValueError(f"{name} must have shape {expected}")
+    if r.shape != (B, T, H) or r_raw.shape != (B, T, H):
+        raise ValueError("r and r_raw must have shape [B,T,H]")
+    if initial_precision.shape != (H,):
+        raise ValueError(f"initial_precision must have shape [{H}]")
+    for name in ("k_gain", "alpha", "omega", "r", "initial_precision"):
+        if tensors[name].dtype != torch.float32:
+            raise TypeError(f"{name} must be torch.float32")
+    if omega_raw.dtype != _VECTOR_DTYPE or r_raw.dtype != _VECTOR_DTYPE:
+        raise TypeError("omega_raw and r_raw must be torch.bfloat16")
+    return _DiagKdnGainFunction.apply(
+        k_gain, alpha, omega.detach(), r.detach(), initial_precision, omega_raw, r_raw
+    )
+
+
+def _validate_diag_kdn_memory_inputs(q, k, kappa, v, g_cumsum, scale):
+    tensors = {"q": q, "k": k, "kappa": kappa, "v": v, "g_cumsum": g_cumsum}
+    for name, value in tensors.items():
+        if not isinstance(value, torch.Tensor):
+            raise TypeError(f"{name} must be a torch.Tensor")
+        if value.ndim != 4:
+            raise ValueError(f"{name} must have rank 4 [B,T,H,D]")
+        if not value.is_cuda:
+            raise ValueError(f"{name} must be a CUDA tensor")
+        if value.device != q.device:
+            raise ValueError("all DiagKDN memory inputs must share one CUDA device")
+        if not value.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+    B, T, H, K = q.shape
+    if min(B, T, H) <= 0 or K not in (64, 128):
+        raise ValueError("DiagKDN memory requires non-empty B/T/H and K in {64,128}")
+    expected = (B, T, H, K)
+    for name in ("k", "kappa", "v", "g_cumsum"):
+        if tensors[name].shape != expected:
+            raise ValueError(f"{name} must have shape {expected}")
+    for name in ("q", "k", "v"):
+        if tensors[name].dtype != _VECTOR_DTYPE:
+            raise TypeError(f"{name} must be torch.bfloat16")
+    if kappa.dtype != _STATE_DTYPE or g_cumsum.dtype != _STATE_DTYPE:
+        raise TypeError("kappa and g_cumsum must be torch.float32")
+    if type(scale) is not float or not math.isfinite(scale):
+        raise TypeError("scale must be an exact finite float")
+    if K != 128:
+        raise ValueError(f"kdn_b200 kernels support K = V = 128, got K={K}")
+    return B, T, H, K
+
+
+class _DiagKdnMemoryFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, kappa, v, g_cumsum, scale):
+        output, _, saved = scan_forward(N.KDN_DIAG, q, k, v, g_cumsum, kappa, scale)
+        ctx.save_for_backward(q, k, kappa, v, g_cumsum, saved.saved)
+        ctx.precision = saved.precision
+        ctx.scale = scale
+        ctx.set_materialize_grads(False)
+        return output
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, do):
+        q, k, kappa, v, g_cumsum, saved = ctx.saved_tensors
+        if do is None:
+            return None, None, None, None, None, None
+        do = do.contiguous()
+        B, T, H, K = _validate_diag_kdn_memory_inputs(q, k, kappa, v, g_cumsum, ctx.scale)
+        if do.shape != (B, T, H, K) or do.dtype != torch.float32:
+            raise TypeError("DiagKDN output cotangent must be FP32 BTHK")
+        dq, dk, dv, dG, dkappa, _ = scan_backward(
+            N.KDN_DIAG, q, k, v, g_cumsum, kappa, ctx.scale, ScanSaved(saved, ctx.precision), do
+        )
+        return dq, dk, dkappa, dv, dG, None
+
+
+def chunk_kalman(
+    q_memory: torch.Tensor,
+    k_memory: torch.Tensor,
+    kappa: torch.Tensor,
+    v: torch.Tensor,
+    g_cumsum: torch.Tensor,
+    scale: float,
+) -> torch.Tensor:
+    """Diagonal KDN memory scan (diag_kdn_chunk.py:3315-3332): fp32 output;
+    backward returns (dq bf16, dk bf16, dkappa fp32, dv bf16, dG fp32, None)
+    with dG the natural-log cotangent before the reverse 32-chunk cumsum."""
+    _validate_diag_kdn_memory_inputs(q_memory, k_memory, kappa, v, g_cumsum, scale)
+    return _DiagKdnMemoryFunction.apply(q_memory, k_memory, kappa, v, g_cumsum, scale)
+
+
+__all__ = ("_diag_kdn_gain", "chunk_kalman")

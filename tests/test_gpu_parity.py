@@ -1,0 +1,154 @@
+"""GPU parity: the sm_100a kernels against the CPU oracle on identical seeded inputs.
+
+Tolerances (stated per the north star):
+* gains (fp32 arithmetic): normalised max-abs error <= 1e-4;
+* scans, fp32 debug precision (``KDN_B200_PRECISION=fp32``): normalised
+  max-abs error <= 1e-4 for o and every gradient;
+* scans, bf16 tensor-core precision (the product): normalised max-abs error
+  <= 2e-2, plus relative Frobenius error <= 1e-2.
+normalised max-abs error = max|x - ref| / max|ref|.
+"""
+import os
+
+import pytest
+import torch
+
+import oracle
+from kdn_b200.diag_kdn_chunk import _diag_kdn_gain, chunk_kalman
+from kdn_b200.iso_kdn_chunk import _chunk_kda_precumsum_paired, iso_kdn_gain
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def nmax(x, ref):
+    x = x.detach().double().cpu()
+    ref = ref.detach().double().cpu()
+    return ((x - ref).abs().max() / ref.abs().max().clamp_min(1e-30)).item()
+
+
+def frob(x, ref):
+    x = x.detach().double().cpu()
+    ref = ref.detach().double().cpu()
+    return ((x - ref).norm() / ref.norm().clamp_min(1e-30)).item()
+
+
+@pytest.fixture
+def precision(request):
+    old = os.environ.get("KDN_B200_PRECISION")
+    os.environ["KDN_B200_PRECISION"] = request.param
+    yield request.param
+    if old is None:
+        os.environ.pop("KDN_B200_PRECISION", None)
+    else:
+        os.environ["KDN_B200_PRECISION"] = old
+
+
+# ----------------------------------------------------------------------------- gains
+
+
+@pytest.mark.parametrize("T", [1, 37, 300, 1000])
+@pytest.mark.parametrize("s", [1.0, 0.5])
+def test_iso_gain_fwd_bwd(T, s):
+    torch.manual_seed(T)
+    B, H = 2, 3
+    a = torch.rand(B, T, H) * 0.98 + 0.01
+    omega = torch.nn.functional.softplus(torch.randn(B, T, H))
+    r = 0.01 + torch.nn.functional.softplus(torch.randn(B, T, H))
+    prec = 0.1 + torch.nn.functional.softplus(torch.randn(H))
+    dbeta = torch.randn(B, T, H)
+    beta_ref, da_ref, dw_ref, dr_ref, dp_ref = oracle.iso_gain_grads(a, omega, r, prec, dbeta, s)
+    leaves = [x.to(DEV).requires_grad_(True) for x in (a, omega, r, prec)]
+    beta = iso_kdn_gain(*leaves, head_dim=128, info_scale=128 * s)
+    beta.backward(dbeta.to(DEV))
+    assert nmax(beta, beta_ref) < 1e-5
+    for got, ref in zip((x.grad for x in leaves), (da_ref, dw_ref, dr_ref, dp_ref)):
+        assert nmax(got, ref) < 1e-4
+
+
+@pytest.mark.parametrize("T,K", [(1, 128), (70, 128), (200, 64), (513, 128)])
+def test_diag_gain_fwd_bwd(T, K):
+    torch.manual_seed(T + K)
+    B, H = 2, 2
+    d = oracle.make_diag_inputs(B, T, H, K=K, V=K, seed=T)
+    prec = 0.1 + torch.nn.functional.softplus(torch.randn(H))
+    dkappa = torch.randn(B, T, H, K)
+    kap_ref, dk_ref, da_ref, dwr_ref, drr_ref, dp_ref = oracle.diag_gain_grads(
+        d["k_gain"], d["alpha"], d["omega"], d["r"], prec, d["omega_raw"], d["r_raw"], dkappa
+    )
+    k = d["k_gain"].to(DEV).requires_grad_(True)
+    alpha = d["alpha"].to(DEV).requires_grad_(True)
+    p = prec.to(DEV).requires_grad_(True)
+    wr = d["omega_raw"].to(DEV).requires_grad_(True)
+    rr = d["r_raw"].to(DEV).requires_grad_(True)
+    kappa = _diag_kdn_gain(k, alpha, d["omega"].to(DEV), d["r"].to(DEV), p, wr, rr)
+    kappa.backward(dkappa.to(DEV))
+    assert nmax(kappa, kap_ref) < 1e-4
+    assert nmax(k.grad, dk_ref) < 1e-4
+    assert nmax(alpha.grad, da_ref) < 1e-4
+    assert nmax(p.grad, dp_ref) < 1e-4
+    # bf16 outputs: one bf16 rounding
+    assert nmax(wr.grad, dwr_ref) < 1e-2
+    assert nmax(rr.grad, drr_ref) < 1e-2
+
+
+# ----------------------------------------------------------------------------- scans
+
+
+def run_iso(d, dO):
+    leaves = {n: d[n].to(DEV).requires_grad_(True) for n in ("q", "k", "v", "g_cumsum", "beta")}
+    o = _chunk_kda_precumsum_paired(leaves["q"], leaves["k"], leaves["v"], leaves["g_cumsum"], leaves["beta"])
+    o.backward(dO.to(DEV))
+    return o, {n: leaves[n].grad for n in leaves}
+
+
+def run_diag(d, dO, kappa, scale):
+    q, k, v, g = (d[n].to(DEV).requires_grad_(True) for n in ("q", "k", "v", "g_cumsum"))
+    kap = kappa.to(DEV).requires_grad_(True)
+    o = chunk_kalman(q, k, kap, v, g, scale)
+    o.backward(dO.to(DEV))
+    return o, {"q": q.grad, "k": k.grad, "kappa": kap.grad, "v": v.grad, "g_cumsum": g.grad}
+
+
+def check(o, grads, ref, names, tol, ftol=None):
+    errs = {"o": nmax(o, ref["o"])}
+    for n in names:
+        key = "dg" if n == "g_cumsum" else "d" + n
+        errs[key] = nmax(grads[n], ref[key])
+    bad = {k: v for k, v in errs.items() if not v < tol}
+    assert not bad, (errs, tol)
+    if ftol is not None:
+        ferrs = {"o": frob(o, ref["o"])}
+        for n in names:
+            key = "dg" if n == "g_cumsum" else "d" + n
+            ferrs[key] = frob(grads[n], ref[key])
+        assert all(v < ftol for v in ferrs.values()), ferrs
+
+
+TOL = {"fp32": (1e-4, None), "bf16": (2e-2, 1e-2)}
+
+
+@pytest.mark.parametrize("precision", ["fp32", "bf16"], indirect=True)
+@pytest.mark.parametrize("B,T,H,decay", [(1, 130, 2, 1.0), (2, 64, 1, 1.0), (1, 3, 1, 1.0), (1, 200, 1, 8.0)])
+def test_iso_scan(precision, B, T, H, decay):
+    d = oracle.make_iso_inputs(B, T, H, seed=T + B, decay_scale=decay)
+    ref = oracle.scan_grads("iso", {n: d[n] for n in ("q", "k", "v", "g_cumsum", "beta")}, d["dO"])
+    o, grads = run_iso(d, d["dO"])
+    tol, ftol = TOL[precision]
+    check(o, grads, ref, ("q", "k", "v", "g_cumsum", "beta"), tol, ftol)
+
+
+@pytest.mark.parametrize("precision", ["fp32", "bf16"], indirect=True)
+@pytest.mark.parametrize("B,T,H,decay", [(1, 70, 2, 1.0), (2, 32, 1, 1.0), (1, 5, 1, 1.0), (1, 100, 1, 12.0)])
+def test_diag_scan(precision, B, T, H, decay):
+    d = oracle.make_diag_inputs(B, T, H, seed=T + 7, decay_scale=decay)
+    # the kernel rounds the fp32 cotangent to bf16 (diag_kdn_chunk.py:3277); feed one that is exact in bf16
+    d["dO"] = d["dO"].bfloat16().float()
+    kappa = oracle.diag_gain(d["k_gain"].double(), d["alpha"].double(), d["omega"].double(), d["r"].double(),
+                             d["initial_precision"].double())[0].float()
+    scale = 128 ** -0.5
+    ref = oracle.scan_grads("diag", {"q": d["q"], "k": d["k"], "kappa": kappa, "v": d["v"], "g_cumsum": d["g_cumsum"]},
+                            d["dO"], scale=scale)
+    o, grads = run_diag(d, d["dO"], kappa, scale)
+    tol, ftol = TOL[precision]
+    check(o, grads, ref, ("q", "k", "kappa", "v", "g_cumsum"), tol, ftol)
