@@ -36,6 +36,45 @@ template <> __device__ __forceinline__ float from_f<float>(float x) { return x; 
 template <> __device__ __forceinline__ bf16 from_f<bf16>(float x) { return __float2bfloat16_rn(x); }
 
 __device__ __forceinline__ float ex2(float x) { return exp2f(x); }
+// Hardware base-2 exponential (MUFU ex2, flushes subnormal results to zero).
+__device__ __forceinline__ float ex2a(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Store two adjacent values (one 32-bit store for bf16, one 64-bit for fp32).
+__device__ __forceinline__ void st_pair(bf16* p, float a, float b) {
+  *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(a, b);
+}
+__device__ __forceinline__ void st_pair(float* p, float a, float b) { *reinterpret_cast<float2*>(p) = make_float2(a, b); }
+
+// 8 consecutive values as fp32 (16-byte aligned source).
+__device__ __forceinline__ void ld8(float (&d)[8], const bf16* p) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    d[2 * i] = f.x;
+    d[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void ld8(float (&d)[8], const float* p) {
+  const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+  d[0] = a.x; d[1] = a.y; d[2] = a.z; d[3] = a.w; d[4] = b.x; d[5] = b.y; d[6] = b.z; d[7] = b.w;
+}
+__device__ __forceinline__ void st8(bf16* p, const float (&s)[8]) {
+  uint4 u;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(s[2 * i], s[2 * i + 1]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+__device__ __forceinline__ void st8(float* p, const float (&s)[8]) {
+  reinterpret_cast<float4*>(p)[0] = make_float4(s[0], s[1], s[2], s[3]);
+  reinterpret_cast<float4*>(p)[1] = make_float4(s[4], s[5], s[6], s[7]);
+}
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -201,12 +240,85 @@ __device__ __forceinline__ void for_acc(int m0, int n0, F&& f) {
       for (int e = 0; e < 4; ++e) f(mt, nt, e, m0 + mt * 16 + g + (e >> 1) * 8, n0 + nt * 8 + 2 * t + (e & 1));
 }
 
-// Store an accumulator tile to a row-major buffer (ld elements), converting.
+// Store an accumulator tile to a row-major buffer (ld elements), converting;
+// adjacent column pairs go out as one store.
 template <class T, int MT, int NT>
 __device__ __forceinline__ void store_acc(T* dst, int ld, const float (&acc)[MT][NT][4], int m0, int n0) {
-  for_acc<MT, NT>(m0, n0, [&](int mt, int nt, int e, int row, int col) {
-    dst[(size_t)row * ld + col] = from_f<T>(acc[mt][nt][e]);
-  });
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int row = m0 + mt * 16 + g + 8 * h, col = n0 + nt * 8 + 2 * t;
+        st_pair(dst + (size_t)row * ld + col, acc[mt][nt][2 * h], acc[mt][nt][2 * h + 1]);
+      }
+}
+
+// Visit accumulator element pairs (adjacent columns): f(mt, nt, h, row, col, v0, v1).
+template <int MT, int NT, class F>
+__device__ __forceinline__ void for_acc_pairs(const float (&acc)[MT][NT][4], int m0, int n0, F&& f) {
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+        f(mt, nt, h, m0 + mt * 16 + g + 8 * h, n0 + nt * 8 + 2 * t, acc[mt][nt][2 * h], acc[mt][nt][2 * h + 1]);
+}
+
+// Two A tiles from different buffers sharing the B fragments:
+// acc[i] += A_i[m0 : m0+16, k] * B[k, n0 : n0+8NT].
+template <int NT, bool AK, bool BK>
+__device__ __forceinline__ void wgemm_dual(float (&acc)[2][NT][4], const bf16* A0, const bf16* A1, int lda,
+                                           const bf16* B, int ldb, int m0, int n0, int k0, int k1) {
+  static_assert(NT % 2 == 0 && AK, "dual-A product: row-major A, even NT");
+  const int lane = threadIdx.x & 31;
+  const int mi = lane >> 3, r = lane & 7;
+  for (int k = k0; k < k1; k += 16) {
+    uint32_t a[2][4];
+    ldsm_x4(a[0], A0 + (size_t)(m0 + (lane & 15)) * lda + k + (lane >> 4) * 8);
+    ldsm_x4(a[1], A1 + (size_t)(m0 + (lane & 15)) * lda + k + (lane >> 4) * 8);
+#pragma unroll
+    for (int nt = 0; nt < NT; nt += 2) {
+      uint32_t b[4];
+      if constexpr (BK) {
+        ldsm_x4(b, B + (size_t)(n0 + nt * 8 + (mi >> 1) * 8 + r) * ldb + k + (mi & 1) * 8);
+      } else {
+        ldsm_x4_t(b, B + (size_t)(k + (mi & 1) * 8 + r) * ldb + n0 + nt * 8 + (mi >> 1) * 8);
+      }
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        mma_16816(acc[i][nt], a[i], b[0], b[1]);
+        mma_16816(acc[i][nt + 1], a[i], b[2], b[3]);
+      }
+    }
+  }
+}
+template <int NT, bool AK, bool BK>
+__device__ __forceinline__ void wgemm_dual(float (&acc)[2][NT][4], const float* A0, const float* A1, int lda,
+                                           const float* B, int ldb, int m0, int n0, int k0, int k1) {
+  float a0[1][NT][4], a1[1][NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      a0[0][nt][e] = acc[0][nt][e];
+      a1[0][nt][e] = acc[1][nt][e];
+    }
+  wgemm<1, NT, AK, BK>(a0, A0, lda, B, ldb, m0, n0, k0, k1);
+  wgemm<1, NT, AK, BK>(a1, A1, lda, B, ldb, m0, n0, k0, k1);
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      acc[0][nt][e] = a0[0][nt][e];
+      acc[1][nt][e] = a1[0][nt][e];
+    }
 }
 
 // ---------------------------------------------------------------------------

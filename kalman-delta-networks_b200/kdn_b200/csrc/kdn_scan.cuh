@@ -60,8 +60,8 @@ struct ScanParams {
   const float* S0;
   void* o;
   float* ST;
-  float* Tsave;  // [BH][NT][C][C]
-  float* Qsave;  // [BH][NT][C][C]
+  void* Tsave;  // [BH][NT][C][C] OpT, the triangular solve of each chunk
+  void* Qsave;  // [BH][NT][C][C] OpT, the query-key scores of each chunk
   void* h;       // [BH][NT][KD][VD] OpT, chunk-start states
   void* dh;      // [BH][NT][KD][VD] OpT, chunk-end state adjoints
   const void* dO;
@@ -198,106 +198,151 @@ __device__ __forceinline__ float rho_col(const Chunk<CF>& ch, int c) {
 }
 
 // Row norms (iso), range check, per-channel factors and the three gated
-// operands.  The caller places the barrier that publishes them.
+// operands.  Thread t handles channels 8*(t%16) .. +7 of rows t/16, t/16 +
+// blockDim/16, ...; the 16 threads of a row are one half-warp, so row norms
+// are half-warp shuffles.  The caller places the barrier that publishes the
+// results.
 template <class CF>
 __device__ void prep_chunk(Chunk<CF>& ch) {
   constexpr int C = CF::C;
+  using OpT = typename CF::OpT;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   const int L = ch.L;
   ch.m = L >= C ? C / 2 : (((L - 1) / 2) & ~15);
-  if constexpr (CF::ISO) {
-    for (int row = warp; row < 2 * C; row += nw) {
-      const bf16* src = row < C ? ch.q + row * kKD : ch.k + (row - C) * kKD;
-      float ss = 0.f;
+  const int c0 = (threadIdx.x & 15) * 8;
+  const int rstep = blockDim.x >> 4;
+  float gm[8];
+  ld8(gm, ch.g + ch.m * kKD + c0);
+  float rng = 0.f;
+  for (int r = threadIdx.x >> 4; r < C; r += rstep) {
+    if constexpr (CF::ISO) {
+      float q8[8], k8[8];
+      ld8(q8, ch.q + r * kKD + c0);
+      ld8(k8, ch.k + r * kKD + c0);
+      float sq = 0.f, sk = 0.f;
 #pragma unroll
-      for (int j = 0; j < kKD / 32; ++j) {
-        const float x = to_f(src[lane + 32 * j]);
-        ss += x * x;
+      for (int i = 0; i < 8; ++i) {
+        sq = fmaf(q8[i], q8[i], sq);
+        sk = fmaf(k8[i], k8[i], sk);
       }
-      ss = warp_sum(ss);
-      if (lane == 0) (row < C ? ch.rq : ch.rk)[row % C] = rsqrtf(ss + 1e-6f);
+#pragma unroll
+      for (int o = 1; o < 16; o <<= 1) {
+        sq += __shfl_xor_sync(0xffffffffu, sq, o);
+        sk += __shfl_xor_sync(0xffffffffu, sk, o);
+      }
+      if ((threadIdx.x & 15) == 0) {
+        ch.rq[r] = rsqrtf(sq + 1e-6f);
+        ch.rk[r] = rsqrtf(sk + 1e-6f);
+      }
+    }
+    if (r < L) {
+      float g8[8];
+      ld8(g8, ch.g + r * kKD + c0);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) rng = fmaxf(rng, fabsf(g8[i] - gm[i]));
     }
   }
-  // range of the gate around the reference row
-  float rng = 0.f;
-  const float* gm = ch.g + ch.m * kKD;
-  for (int e = threadIdx.x; e < L * kKD; e += blockDim.x) rng = fmaxf(rng, fabsf(ch.g[e] - gm[e % kKD]));
   rng = warp_max(rng);
   if (lane == 0) ch.red[warp] = rng;
   __syncthreads();
   float tot = 0.f;
   for (int w = 0; w < nw; ++w) tot = fmaxf(tot, ch.red[w]);
   ch.fast = tot <= kRngMax;
-  for (int c = threadIdx.x; c < kKD; c += blockDim.x) {
-    const float gl = ch.g[(L - 1) * kKD + c];
-    const float rr = rho_row(ch, c), rc = rho_col(ch, c);
-    ch.fr[c] = ex2(rr);
-    ch.fL[c] = ex2(gl - rc);
-    ch.gL[c] = ex2(gl);
-    ch.gmid[c] = ch.g[ch.m * kKD + c];
-    ch.glast[c] = gl;
+  float gl[8], rr[8], rc[8];
+  ld8(gl, ch.g + (L - 1) * kKD + c0);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    rr[i] = ch.fast ? gm[i] : 0.f;
+    rc[i] = ch.fast ? gm[i] : gl[i];
   }
-  using OpT = typename CF::OpT;
-  for (int e = threadIdx.x; e < C * kKD; e += blockDim.x) {
-    const int i = e / kKD, c = e - i * kKD;
-    float kr = 0.f, qr = 0.f, kc = 0.f;
-    if (i < L) {
-      const float gi = ch.g[e];
-      const float er = ex2(gi - rho_row(ch, c));
-      const float ec = ex2(rho_col(ch, c) - gi);
-      kr = khat_at(ch, i, c) * er;
-      qr = qhat_at(ch, i, c) * er;
-      kc = kappa_at(ch, i, c) * ec;
+  if (threadIdx.x < 16) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      ch.fr[c0 + i] = ex2(rr[i]);
+      ch.fL[c0 + i] = ex2(gl[i] - rc[i]);
+      ch.gL[c0 + i] = ex2(gl[i]);
+      ch.gmid[c0 + i] = gm[i];
+      ch.glast[c0 + i] = gl[i];
     }
-    ch.Kr[i * CF::LDK + c] = from_f<OpT>(kr);
-    ch.Qr[i * CF::LDK + c] = from_f<OpT>(qr);
-    ch.Kc[i * CF::LDK + c] = from_f<OpT>(kc);
+  }
+  for (int r = threadIdx.x >> 4; r < C; r += rstep) {
+    float kr[8], qr[8], kc[8];
+    if (r < L) {
+      float g8[8], k8[8], q8[8], kap[8];
+      ld8(g8, ch.g + r * kKD + c0);
+      ld8(k8, ch.k + r * kKD + c0);
+      ld8(q8, ch.q + r * kKD + c0);
+      float ks = 1.f, qs = 1.f, bs = 1.f;
+      if constexpr (CF::ISO) {
+        ks = ch.rk[r];
+        qs = ch.rq[r];
+        bs = ch.beta[r] * ks;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) kap[i] = k8[i];
+      } else {
+        ld8(kap, ch.kap + r * kKD + c0);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float er = ex2a(g8[i] - rr[i]);
+        const float ec = ex2a(rc[i] - g8[i]);
+        kr[i] = k8[i] * ks * er;
+        qr[i] = q8[i] * qs * er;
+        kc[i] = kap[i] * bs * ec;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) kr[i] = qr[i] = kc[i] = 0.f;
+    }
+    st8(ch.Kr + r * CF::LDK + c0, kr);
+    st8(ch.Qr + r * CF::LDK + c0, qr);
+    st8(ch.Kc + r * CF::LDK + c0, kc);
   }
 }
 
-// A (fp32, strictly lower) and Q (OpT operand, lower incl. diagonal; fp32
-// copy to global when Qsave != nullptr).  Ends with a barrier.
+// Strictly lower A (fp32 sA for the diagonal-block inversion, OpT sAb for
+// the tensor-core merges) and lower Q (OpT sQ).  Blocks above the diagonal
+// are never written: the callers zero them once.  Ends with a barrier.
 template <class CF>
-__device__ void chunk_scores(const Chunk<CF>& ch, float* sA, typename CF::OpT* sQ, float* Qsave) {
+__device__ void chunk_scores(const Chunk<CF>& ch, float* sA, typename CF::OpT* sAb, typename CF::OpT* sQ) {
   constexpr int C = CF::C, NB = CF::NB;
   using OpT = typename CF::OpT;
   const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   if (ch.fast) {
     constexpr int ntri = NB * (NB + 1) / 2;
-    for (int job = warp; job < 2 * ntri; job += nw) {
-      const bool isQ = job >= ntri;
-      int tj = isQ ? job - ntri : job, I = 0;
-      while (tj > I) {
-        tj -= I + 1;
+    for (int job = warp; job < ntri; job += nw) {
+      int J = job, I = 0;
+      while (J > I) {
+        J -= I + 1;
         ++I;
       }
-      const int J = tj;
-      float acc[1][2][4];
-      zero_acc(acc);
-      wgemm<1, 2, true, true>(acc, isQ ? ch.Qr : ch.Kr, CF::LDK, ch.Kc, CF::LDK, 16 * I, 16 * J, 0, kKD);
-      for_acc<1, 2>(16 * I, 16 * J, [&](int, int nt, int e, int i, int j) {
-        float x = acc[0][nt][e];
-        if (isQ) {
-          x = j <= i ? x : 0.f;
-          sQ[i * CF::LDC + j] = from_f<OpT>(x);
-          if (Qsave) Qsave[i * C + j] = x;
-        } else {
-          sA[i * CF::LDA + j] = j < i ? x : 0.f;
+      float acc[2][2][4];
+#pragma unroll
+      for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int n = 0; n < 2; ++n)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[i][n][e] = 0.f;
+      wgemm_dual<2, true, true>(acc, ch.Kr, ch.Qr, CF::LDK, ch.Kc, CF::LDK, 16 * I, 16 * J, 0, kKD);
+      const int lane = threadIdx.x & 31;
+      const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int i = 16 * I + g + 8 * h, j = 16 * J + nt * 8 + 2 * t;
+          const float a0 = j < i ? acc[0][nt][2 * h] : 0.f, a1 = j + 1 < i ? acc[0][nt][2 * h + 1] : 0.f;
+          const float q0 = j <= i ? acc[1][nt][2 * h] : 0.f, q1 = j + 1 <= i ? acc[1][nt][2 * h + 1] : 0.f;
+          st_pair(sA + i * CF::LDA + j, a0, a1);
+          st_pair(sAb + i * CF::LDC + j, a0, a1);
+          st_pair(sQ + i * CF::LDC + j, q0, q1);
         }
-      });
-    }
-    // blocks above the diagonal are structurally zero
-    for (int e = threadIdx.x; e < C * C; e += blockDim.x) {
-      const int i = e / C, j = e - i * C;
-      if ((j >> 4) > (i >> 4)) {
-        sQ[i * CF::LDC + j] = from_f<OpT>(0.f);
-        if (Qsave) Qsave[e] = 0.f;
-      }
     }
   } else {
     // exact: 2^(g_i - g_j) <= 1 evaluated per element
     for (int e = threadIdx.x; e < C * C; e += blockDim.x) {
       const int i = e / C, j = e - i * C;
+      if ((j >> 4) > (i >> 4)) continue;
       float a = 0.f, qq = 0.f;
       if (j <= i && i < ch.L) {
         for (int c = 0; c < kKD; ++c) {
@@ -306,28 +351,36 @@ __device__ void chunk_scores(const Chunk<CF>& ch, float* sA, typename CF::OpT* s
           qq = fmaf(qhat_at(ch, i, c), f, qq);
         }
       }
-      sA[i * CF::LDA + j] = j < i ? a : 0.f;
+      a = j < i ? a : 0.f;
+      sA[i * CF::LDA + j] = a;
+      sAb[i * CF::LDC + j] = from_f<OpT>(a);
       sQ[i * CF::LDC + j] = from_f<OpT>(qq);
-      if (Qsave) Qsave[i * C + j] = qq;
     }
   }
   __syncthreads();
 }
 
-// T = (I + A)^-1 for unit lower-triangular I + A (A strictly lower, fp32).
-// Writes sT (fp32, ld LDA, upper zero) and its OpT copy; Tsave (fp32 global)
-// when non-null.  sX: fp32 scratch of (NB-1)*256 floats.  Ends with a barrier.
+// Zero the blocks above the 16x16 block diagonal of a C x C OpT buffer.
 template <class CF>
-__device__ void chunk_solve(const float* sA, float* sT, typename CF::OpT* sTb, float* sX, float* Tsave) {
-  constexpr int C = CF::C, NB = CF::NB, LDA = CF::LDA;
-  using OpT = typename CF::OpT;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // zero everything above the diagonal blocks
+__device__ __forceinline__ void zero_upper_blocks(typename CF::OpT* M) {
+  constexpr int C = CF::C;
   for (int e = threadIdx.x; e < C * C; e += blockDim.x) {
     const int i = e / C, j = e - i * C;
-    if ((j >> 4) > (i >> 4)) sT[i * LDA + j] = 0.f;
+    if ((j >> 4) > (i >> 4)) M[i * CF::LDC + j] = from_f<typename CF::OpT>(0.f);
   }
-  // diagonal 16x16 blocks: one warp per block, one lane per column
+}
+
+// T = (I + A)^-1 for strictly lower A: 16x16 diagonal blocks by forward
+// substitution (fp32, one lane per column), then recursive doubling on the
+// tensor cores, T21 = -T22 (A21 T11), first for 16-row pairs, then for the
+// 32-row halves.  Writes the OpT sTb (upper blocks must be zero already);
+// sXb is OpT scratch of the same shape.  Ends with a barrier.
+template <class CF>
+__device__ void chunk_solve(const float* sA, const typename CF::OpT* sAb, typename CF::OpT* sTb,
+                            typename CF::OpT* sXb) {
+  constexpr int NB = CF::NB, LDA = CF::LDA, LDC = CF::LDC;
+  using OpT = typename CF::OpT;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp < NB && lane < 16) {
     const int o = warp * 16, j = lane;
     float col[16];
@@ -336,49 +389,76 @@ __device__ void chunk_solve(const float* sA, float* sT, typename CF::OpT* sTb, f
       float x = (i == j) ? 1.f : 0.f;
       if (i > j) {
 #pragma unroll
-        for (int l = 0; l < 16; ++l)
-          if (l >= j && l < i) x = fmaf(-sA[(o + i) * LDA + o + l], col[l], x);
+        for (int l = 0; l < i; ++l)
+          if (l >= j) x = fmaf(-sA[(o + i) * LDA + o + l], col[l], x);
       }
       col[i] = x;
     }
 #pragma unroll
-    for (int i = 0; i < 16; ++i) sT[(o + i) * LDA + o + j] = col[i];
+    for (int i = 0; i < 16; ++i) sTb[(o + i) * LDC + o + j] = from_f<OpT>(col[i]);
   }
   __syncthreads();
-  // off-diagonal blocks by distance d: T_IJ = -T_II sum_{K=J}^{I-1} A_IK T_KJ
-  for (int d = 1; d < NB; ++d) {
-    const int nblk = NB - d;
-    for (int e = threadIdx.x; e < nblk * 256; e += blockDim.x) {
-      const int J = e >> 8, I = J + d, r = (e >> 4) & 15, c = e & 15;
-      float x = 0.f;
-      for (int kk = J * 16; kk < I * 16; ++kk) x = fmaf(sA[(I * 16 + r) * LDA + kk], sT[kk * LDA + J * 16 + c], x);
-      sX[e] = x;
-    }
-    __syncthreads();
-    for (int e = threadIdx.x; e < nblk * 256; e += blockDim.x) {
-      const int J = e >> 8, I = J + d, r = (e >> 4) & 15, c = e & 15;
-      float x = 0.f;
-      for (int l = 0; l <= r; ++l) x = fmaf(sT[(I * 16 + r) * LDA + I * 16 + l], sX[(J << 8) + l * 16 + c], x);
-      sT[(I * 16 + r) * LDA + J * 16 + c] = -x;
-    }
-    __syncthreads();
-  }
-  for (int e = threadIdx.x; e < C * C; e += blockDim.x) {
-    const int i = e / C, j = e - i * C;
-    const float x = sT[i * LDA + j];
-    sTb[i * CF::LDC + j] = from_f<OpT>(x);
-    if (Tsave) Tsave[e] = x;
+  // pairs of 16-row blocks
+  if (warp < NB / 2) {
+    const int b0 = 32 * warp, b1 = b0 + 16;
+    float acc[1][2][4];
+    zero_acc(acc);
+    wgemm<1, 2, true, false>(acc, sAb, LDC, sTb, LDC, b1, b0, b0, b1);
+    store_acc(sXb, LDC, acc, b1, b0);
   }
   __syncthreads();
+  if (warp < NB / 2) {
+    const int b0 = 32 * warp, b1 = b0 + 16;
+    float acc[1][2][4];
+    zero_acc(acc);
+    wgemm<1, 2, true, false>(acc, sTb, LDC, sXb, LDC, b1, b0, b1, b1 + 16);
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[0][nt][e] = -acc[0][nt][e];
+    store_acc(sTb, LDC, acc, b1, b0);
+  }
+  __syncthreads();
+  if constexpr (NB == 4) {
+    // 32-row halves: T[32:64, 0:32] = -T[32:64, 32:64] (A[32:64, 0:32] T[0:32, 0:32])
+    const int I = 2 + (warp >> 1), J = warp & 1;
+    if (warp < 4) {
+      float acc[1][2][4];
+      zero_acc(acc);
+      wgemm<1, 2, true, false>(acc, sAb, LDC, sTb, LDC, 16 * I, 16 * J, 16 * J, 32);
+      store_acc(sXb, LDC, acc, 16 * I, 16 * J);
+    }
+    __syncthreads();
+    if (warp < 4) {
+      float acc[1][2][4];
+      zero_acc(acc);
+      wgemm<1, 2, true, false>(acc, sTb, LDC, sXb, LDC, 16 * I, 16 * J, 32, 16 * (I + 1));
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[0][nt][e] = -acc[0][nt][e];
+      store_acc(sTb, LDC, acc, 16 * I, 16 * J);
+    }
+    __syncthreads();
+  }
+  static_assert(NB == 2 || NB == 4, "chunk of 32 or 64 tokens");
 }
 
-// Load a saved fp32 C x C matrix into an OpT operand buffer.
+// Copy a C x C OpT matrix between a padded shared buffer and an unpadded
+// global one (saved T and Q).  Async (cp.async) towards shared memory.
 template <class CF>
-__device__ __forceinline__ void load_cc(typename CF::OpT* dst, const float* src) {
-  for (int e = threadIdx.x; e < CF::C * CF::C; e += blockDim.x) {
-    const int i = e / CF::C, j = e - i * CF::C;
-    dst[i * CF::LDC + j] = from_f<typename CF::OpT>(src[e]);
+__device__ __forceinline__ void store_cc(typename CF::OpT* dst, const typename CF::OpT* src) {
+  constexpr int C = CF::C, VEC = 16 / sizeof(typename CF::OpT), PER = C / VEC;
+  for (int e = threadIdx.x; e < C * PER; e += blockDim.x) {
+    const int i = e / PER, c = (e - i * PER) * VEC;
+    *reinterpret_cast<uint4*>(dst + i * C + c) = *reinterpret_cast<const uint4*>(src + i * CF::LDC + c);
   }
+}
+template <class CF>
+__device__ __forceinline__ void load_cc(typename CF::OpT* dst, const typename CF::OpT* src) {
+  constexpr int C = CF::C;
+  copy_rows<!CF::F32>(dst, CF::LDC * sizeof(typename CF::OpT), src, C * sizeof(typename CF::OpT), C, C,
+                      C * sizeof(typename CF::OpT));
 }
 
 }  // namespace kdn

@@ -33,7 +33,7 @@ bool sizes_of(const KdnScanArgs* a, Sizes* s) {
   s->NT = (a->T + s->C - 1) / s->C;
   s->BH = a->B * a->H;
   s->op = a->precision == KDN_PREC_FP32 ? 4 : 2;
-  s->tq = align_up(sizeof(float) * s->BH * s->NT * s->C * s->C, 256);
+  s->tq = align_up((size_t)s->op * s->BH * s->NT * s->C * s->C, 256);
   s->h = align_up((size_t)s->op * s->BH * s->NT * kKD * kVD, 256);
   s->dh = s->h;
   s->dbg_fwd = s->dbg_bwd = 0;
@@ -63,8 +63,8 @@ int fill_params(const KdnScanArgs* a, const Sizes& s, ScanParams* p) {
   p->o = a->o;
   p->ST = a->final_state;
   char* sv = static_cast<char*>(a->saved);
-  p->Tsave = reinterpret_cast<float*>(sv);
-  p->Qsave = reinterpret_cast<float*>(sv + s.tq);
+  p->Tsave = sv;
+  p->Qsave = sv + s.tq;
   p->h = sv + 2 * s.tq;
   p->dO = a->dO;
   p->dST = a->d_final_state;

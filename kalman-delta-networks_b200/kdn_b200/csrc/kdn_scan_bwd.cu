@@ -29,58 +29,47 @@ template <class CF>
 struct StateLayout {
   static constexpr size_t sz = sizeof(typename CF::OpT);
   static constexpr int C = CF::C;
-  static constexpr size_t dOst_bytes = (size_t)C * kBV * (CF::ISO ? 2 : 4);
   static constexpr size_t q = 0;
   static constexpr size_t k = q + A128((size_t)C * kKD * 2);
   static constexpr size_t g = k + A128((size_t)C * kKD * 2);
   static constexpr size_t kap = g + A128((size_t)C * kKD * 4);
-  static constexpr size_t Tst = kap + A128(CF::ISO ? (size_t)C * 4 : (size_t)C * kKD * 4);
-  static constexpr size_t Qst = Tst + A128((size_t)C * C * 4);
-  static constexpr size_t dOst = Qst + A128((size_t)C * C * 4);
-  static constexpr size_t raw_end = dOst + A128(dOst_bytes);
-  static constexpr size_t DS = 0;  // aliases the raw inputs after prep
-  static constexpr size_t dO = cmax(raw_end, A128((size_t)kKD * CF::LDV * sz));
-  static constexpr size_t Kr = dO + A128((size_t)C * CF::LDV * sz);
+  static constexpr size_t dOst = kap + A128(CF::ISO ? (size_t)C * 4 : (size_t)C * kKD * 4);  // diag fp32 dO
+  static constexpr size_t dO = dOst + A128(CF::ISO ? 16 : (size_t)C * kBV * 4);  // two buffers
+  static constexpr size_t Tb = dO + 2 * A128((size_t)C * CF::LDV * sz);          // two buffers
+  static constexpr size_t Qb = Tb + 2 * A128((size_t)C * CF::LDC * sz);          // two buffers
+  static constexpr size_t Kr = Qb + 2 * A128((size_t)C * CF::LDC * sz);
   static constexpr size_t Qr = Kr + A128((size_t)C * CF::LDK * sz);
   static constexpr size_t Kc = Qr + A128((size_t)C * CF::LDK * sz);
-  static constexpr size_t Tb = Kc + A128((size_t)C * CF::LDK * sz);
-  static constexpr size_t Qb = Tb + A128((size_t)C * CF::LDC * sz);
-  static constexpr size_t W = Qb + A128((size_t)C * CF::LDC * sz);
-  static constexpr size_t DD = W + A128((size_t)C * CF::LDK * sz);
+  static constexpr size_t W = Kc + A128((size_t)C * CF::LDK * sz);
+  static constexpr size_t DS = W + A128((size_t)C * CF::LDK * sz);
+  static constexpr size_t DD = DS + A128((size_t)kKD * CF::LDV * sz);
   static constexpr size_t small = DD + A128((size_t)C * CF::LDV * sz);
   static constexpr size_t bytes = small + A128(small_floats<CF>() * 4);
 };
 
-// Stage the fp32 T, Q of chunk cc (and the dO tile) with the raw inputs.
 template <class CF>
-__device__ __forceinline__ void load_saved_tq(float* Tst, float* Qst, const ScanParams& p, size_t cc) {
-  constexpr int C = CF::C;
-  copy_rows<!CF::F32>(Tst, C * 4, p.Tsave + cc * C * C, C * 4, C, C, C * 4);
-  copy_rows<!CF::F32>(Qst, C * 4, p.Qsave + cc * C * C, C * 4, C, C, C * 4);
-}
-
-template <class CF>
-__device__ __forceinline__ void stage_dO(void* dst, const ScanParams& p, int b, int h, int t0, int L, int v0) {
+__device__ __forceinline__ void stage_dO(void* dst, const ScanParams& p, int b, int h, int t0, int L, int v0,
+                                         int ld) {
   constexpr int C = CF::C;
   const size_t r0 = tok_row(p, b, h, t0) * kVD + v0;
   if constexpr (CF::ISO) {
-    copy_rows<!CF::F32>(dst, kBV * 2, static_cast<const bf16*>(p.dO) + r0, (size_t)p.H * kVD * 2, C, L, kBV * 2);
+    load_tile_op<CF>(static_cast<typename CF::OpT*>(dst), ld, static_cast<const bf16*>(p.dO) + r0,
+                     (size_t)p.H * kVD, C, L, kBV);
   } else {
     copy_rows<!CF::F32>(dst, kBV * 4, static_cast<const float*>(p.dO) + r0, (size_t)p.H * kVD * 4, C, L, kBV * 4);
   }
 }
 
-// dO tile as the OpT operand.  The diagonal variant's fp32 cotangent is
-// rounded to bf16 like the reference does before its backward kernels
-// (diag_kdn_chunk.py:3277).
+// The diagonal variant's fp32 cotangent as the OpT operand, rounded to bf16
+// like the reference does before its backward kernels (diag_kdn_chunk.py:3277).
 template <class CF>
-__device__ __forceinline__ typename CF::OpT dO_elem(const void* st, int i, int c) {
+__device__ __forceinline__ void convert_dO(typename CF::OpT* dst, const float* st) {
   using OpT = typename CF::OpT;
-  if constexpr (CF::ISO) {
-    return from_f<OpT>(__bfloat162float(static_cast<const bf16*>(st)[i * kBV + c]));
-  } else {
-    const float x = static_cast<const float*>(st)[i * kBV + c];
-    return from_f<OpT>(__bfloat162float(__float2bfloat16_rn(x)));
+  for (int e = threadIdx.x; e < CF::C * kBV / 2; e += blockDim.x) {
+    const int i = (2 * e) / kBV, c = 2 * e - i * kBV;
+    const float2 x = *reinterpret_cast<const float2*>(st + i * kBV + c);
+    const float a = __bfloat162float(__float2bfloat16_rn(x.x)), b = __bfloat162float(__float2bfloat16_rn(x.y));
+    st_pair(dst + i * CF::LDV + c, a, b);
   }
 }
 
@@ -106,13 +95,13 @@ __global__ void __launch_bounds__(256, 1) scan_bwd_state_kernel(ScanParams p) {
   ch.Qr = reinterpret_cast<OpT*>(base + Lo::Qr);
   ch.Kc = reinterpret_cast<OpT*>(base + Lo::Kc);
   bind_small(ch, reinterpret_cast<float*>(base + Lo::small));
-  float* Tst = reinterpret_cast<float*>(base + Lo::Tst);
-  float* Qst = reinterpret_cast<float*>(base + Lo::Qst);
-  void* dOst = base + Lo::dOst;
+  float* dOst = reinterpret_cast<float*>(base + Lo::dOst);
+  constexpr size_t dO_stride = A128((size_t)C * CF::LDV * sizeof(OpT));
+  constexpr size_t cc_stride = A128((size_t)C * CF::LDC * sizeof(OpT));
+  auto sdO_buf = [&](int i) { return reinterpret_cast<OpT*>(base + Lo::dO + i * dO_stride); };
+  auto sTb_buf = [&](int i) { return reinterpret_cast<OpT*>(base + Lo::Tb + i * cc_stride); };
+  auto sQb_buf = [&](int i) { return reinterpret_cast<OpT*>(base + Lo::Qb + i * cc_stride); };
   OpT* sDS = reinterpret_cast<OpT*>(base + Lo::DS);
-  OpT* sdO = reinterpret_cast<OpT*>(base + Lo::dO);
-  OpT* sTb = reinterpret_cast<OpT*>(base + Lo::Tb);
-  OpT* sQb = reinterpret_cast<OpT*>(base + Lo::Qb);
   OpT* sW = reinterpret_cast<OpT*>(base + Lo::W);
   OpT* sDD = reinterpret_cast<OpT*>(base + Lo::DD);
 
@@ -125,28 +114,29 @@ __global__ void __launch_bounds__(256, 1) scan_bwd_state_kernel(ScanParams p) {
     dS[0][nt][e] = p.dST ? p.dST[((size_t)bh * kKD + row) * kVD + v0 + col] : 0.f;
   });
 
-  auto issue_loads = [&](int c) {
+  auto issue_loads = [&](int c, int buf) {
     const int t0 = c * C, L = min(C, p.T - t0);
+    const size_t cc = (size_t)bh * p.NT + c;
     load_raw(ch, p, b, h, t0, L);
-    load_saved_tq<CF>(Tst, Qst, p, (size_t)bh * p.NT + c);
-    stage_dO<CF>(dOst, p, b, h, t0, L, v0);
+    load_cc<CF>(sTb_buf(buf), static_cast<const OpT*>(p.Tsave) + cc * C * C);
+    load_cc<CF>(sQb_buf(buf), static_cast<const OpT*>(p.Qsave) + cc * C * C);
+    stage_dO<CF>(CF::ISO ? static_cast<void*>(sdO_buf(buf)) : static_cast<void*>(dOst), p, b, h, t0, L, v0, CF::LDV);
     if constexpr (!CF::F32) cp_async_commit();
   };
-  issue_loads(p.NT - 1);
+  issue_loads(p.NT - 1, 0);
 
   for (int c = p.NT - 1; c >= 0; --c) {
-    const int t0 = c * C;
-    ch.L = min(C, p.T - t0);
+    const int buf = (p.NT - 1 - c) & 1;
+    OpT* sTb = sTb_buf(buf);
+    OpT* sQb = sQb_buf(buf);
+    OpT* sdO = sdO_buf(buf);
+    ch.L = min(C, p.T - c * C);
     if constexpr (!CF::F32) cp_async_wait_all();
     __syncthreads();
     prep_chunk(ch);
-    load_cc<CF>(sTb, Tst);
-    load_cc<CF>(sQb, Qst);
-    for (int e = threadIdx.x; e < C * kBV; e += blockDim.x) {
-      const int i = e / kBV, cc = e - i * kBV;
-      sdO[i * CF::LDV + cc] = dO_elem<CF>(dOst, i, cc);
-    }
+    if constexpr (!CF::ISO) convert_dO<CF>(sdO, dOst);
     __syncthreads();
+    if (c > 0) issue_loads(c - 1, buf ^ 1);
 
     // W0 = T Kr; fL-scaled adjoint operand; chunk-end adjoint to HBM
     const int I = warp / NJW;
@@ -157,10 +147,10 @@ __global__ void __launch_bounds__(256, 1) scan_bwd_state_kernel(ScanParams p) {
       store_acc(sW, CF::LDK, acc, 16 * I, (warp % NJW) * 8 * NTW);
     }
     OpT* dhdst = static_cast<OpT*>(p.dh) + ((size_t)bh * p.NT + c) * kKD * kVD;
-    for_acc<1, 8>(16 * warp, 0, [&](int, int nt, int e, int row, int col) {
-      const float x = dS[0][nt][e];
-      sDS[row * CF::LDV + col] = from_f<OpT>(ch.fL[row] * x);
-      dhdst[(size_t)row * kVD + v0 + col] = from_f<OpT>(x);
+    for_acc_pairs<1, 8>(dS, 16 * warp, 0, [&](int, int, int, int row, int col, float x0, float x1) {
+      const float f = ch.fL[row];
+      st_pair(sDS + row * CF::LDV + col, f * x0, f * x1);
+      st_pair(dhdst + (size_t)row * kVD + v0 + col, x0, x1);
     });
     __syncthreads();
 
@@ -172,12 +162,13 @@ __global__ void __launch_bounds__(256, 1) scan_bwd_state_kernel(ScanParams p) {
       zero_acc(a2);
       wgemm<1, NTU, false, false>(a1, sQb, CF::LDC, sdO, CF::LDV, 16 * Iu, nu, 16 * Iu, C);
       wgemm<1, NTU, true, false>(a2, ch.Kc, CF::LDK, sDS, CF::LDV, 16 * Iu, nu, 0, kKD);
-      for_acc<1, NTU>(16 * Iu, nu, [&](int, int nt, int e, int row, int col) {
-        sDD[row * CF::LDV + col] = from_f<OpT>(p.scale * a1[0][nt][e] + a2[0][nt][e]);
-      });
+#pragma unroll
+      for (int nt = 0; nt < NTU; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) a1[0][nt][e] = p.scale * a1[0][nt][e] + a2[0][nt][e];
+      store_acc(sDD, CF::LDV, a1, 16 * Iu, nu);
     }
     __syncthreads();
-    if (c > 0) issue_loads(c - 1);
 
     // dS <- Diag(2^g_L) dS + Diag(fr) (scale Qr^T dO - W0^T ddelta)
     {
@@ -205,14 +196,12 @@ template <class CF>
 struct ChunkLayout {
   static constexpr size_t sz = sizeof(typename CF::OpT);
   static constexpr int C = CF::C;
-  // raw inputs + staged T, Q
+  // raw inputs
   static constexpr size_t q = 0;
   static constexpr size_t k = q + A128((size_t)C * kKD * 2);
   static constexpr size_t g = k + A128((size_t)C * kKD * 2);
   static constexpr size_t kap = g + A128((size_t)C * kKD * 4);
-  static constexpr size_t Tst = kap + A128(CF::ISO ? (size_t)C * 4 : (size_t)C * kKD * 4);
-  static constexpr size_t Qst = Tst + A128((size_t)C * C * 4);
-  static constexpr size_t raw_end = Qst + A128((size_t)C * C * 4);
+  static constexpr size_t raw_end = kap + A128(CF::ISO ? (size_t)C * 4 : (size_t)C * kKD * 4);
   // value-half loop (aliases the raw inputs)
   static constexpr size_t v = 0;
   static constexpr size_t dO = v + A128((size_t)C * CF::LDV * sz);
@@ -228,7 +217,9 @@ struct ChunkLayout {
   static constexpr size_t X = dT + A128((size_t)C * CF::LDC * sz);
   static constexpr size_t dA = X + A128((size_t)C * CF::LDC * sz);
   static constexpr size_t dQ = dA + A128((size_t)C * CF::LDC * sz);
-  static constexpr size_t post_end = dQ + A128((size_t)C * CF::LDC * sz);
+  static constexpr size_t dAf = dQ + A128((size_t)C * CF::LDC * sz);  // fp32 copies for the exact path
+  static constexpr size_t dQf = dAf + A128((size_t)C * C * 4);
+  static constexpr size_t post_end = dQf + A128((size_t)C * C * 4);
   static constexpr size_t Kr = cmax(cmax(raw_end, loop_end), post_end);
   static constexpr size_t Qr = Kr + A128((size_t)C * CF::LDK * sz);
   static constexpr size_t Kc = Qr + A128((size_t)C * CF::LDK * sz);
@@ -270,8 +261,6 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_kernel(ScanParams p) {
   float* rbeta = cgl + kKD;
   float* rdotk = rbeta + C;
   float* rdotq = rdotk + C;
-  float* Tst = reinterpret_cast<float*>(base + Lo::Tst);
-  float* Qst = reinterpret_cast<float*>(base + Lo::Qst);
   OpT* sv = reinterpret_cast<OpT*>(base + Lo::v);
   OpT* sdO = reinterpret_cast<OpT*>(base + Lo::dO);
   OpT* sDel = reinterpret_cast<OpT*>(base + Lo::Del);
@@ -284,6 +273,8 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_kernel(ScanParams p) {
   OpT* sX = reinterpret_cast<OpT*>(base + Lo::X);
   OpT* sdA = reinterpret_cast<OpT*>(base + Lo::dA);
   OpT* sdQ = reinterpret_cast<OpT*>(base + Lo::dQ);
+  float* sdAf = reinterpret_cast<float*>(base + Lo::dAf);
+  float* sdQf = reinterpret_cast<float*>(base + Lo::dQf);
   OpT* sTb = reinterpret_cast<OpT*>(base + Lo::Tb);
   OpT* sQb = reinterpret_cast<OpT*>(base + Lo::Qb);
   OpT* sW = reinterpret_cast<OpT*>(base + Lo::W);
@@ -296,15 +287,14 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_kernel(ScanParams p) {
   ch.L = L;
 
   load_raw(ch, p, b, h, t0, L);
-  load_saved_tq<CF>(Tst, Qst, p, cc);
+  load_cc<CF>(sTb, static_cast<const OpT*>(p.Tsave) + cc * C * C);
+  load_cc<CF>(sQb, static_cast<const OpT*>(p.Qsave) + cc * C * C);
   if constexpr (!CF::F32) {
     cp_async_commit();
     cp_async_wait_all();
   }
   __syncthreads();
   prep_chunk(ch);
-  load_cc<CF>(sTb, Tst);
-  load_cc<CF>(sQb, Qst);
   for (int e = threadIdx.x; e < 2 * kKD + 3 * C; e += blockDim.x) cfl[e] = 0.f;
   __syncthreads();
 
@@ -354,12 +344,7 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_kernel(ScanParams p) {
       cp_async_wait_all();
     }
     __syncthreads();
-    if constexpr (!CF::ISO) {
-      for (int e = threadIdx.x; e < C * kBV; e += blockDim.x) {
-        const int i = e / kBV, cc2 = e - i * kBV;
-        sdO[i * CF::LDV + cc2] = dO_elem<CF>(dOst, i, cc2);
-      }
-    }
+    if constexpr (!CF::ISO) convert_dO<CF>(sdO, dOst);
     // S0' = fr S0, dS'' = fL dS, and cgl += sum_v S0' dS''  (4 threads per channel)
     {
       const int ch_ = threadIdx.x >> 2, part = threadIdx.x & 3;
@@ -456,11 +441,15 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_kernel(ScanParams p) {
       sX[i * CF::LDC + j] = from_f<OpT>(0.f);
       sdA[i * CF::LDC + j] = from_f<OpT>(0.f);
       sdQ[i * CF::LDC + j] = from_f<OpT>(0.f);
+      sdAf[e] = 0.f;
+      sdQf[e] = 0.f;
     }
   }
   if (own_tri) {
     for_acc<1, 2>(16 * TI, 16 * TJ, [&](int, int nt, int e, int row, int col) {
-      sdQ[row * CF::LDC + col] = from_f<OpT>(col <= row ? p.scale * aDQ[0][nt][e] : 0.f);
+      const float x = col <= row ? p.scale * aDQ[0][nt][e] : 0.f;
+      sdQ[row * CF::LDC + col] = from_f<OpT>(x);
+      sdQf[row * C + col] = x;
     });
   }
   __syncthreads();
@@ -489,7 +478,9 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_kernel(ScanParams p) {
     zero_acc(x);
     wgemm<1, 2, false, false>(x, sTb, CF::LDC, sX, CF::LDC, 16 * TI, 16 * TJ, 16 * TI, C);
     for_acc<1, 2>(16 * TI, 16 * TJ, [&](int, int nt, int e, int row, int col) {
-      sdA[row * CF::LDC + col] = from_f<OpT>(col < row ? -x[0][nt][e] : 0.f);
+      const float y = col < row ? -x[0][nt][e] : 0.f;
+      sdA[row * CF::LDC + col] = from_f<OpT>(y);
+      sdAf[row * C + col] = y;
     });
   }
   __syncthreads();
@@ -541,16 +532,16 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_kernel(ScanParams p) {
         }
         if (j <= row) {
           const float f = ex2(gi - gj);
-          const float dAij = j < row ? to_f(sdA[row * CF::LDC + j]) : 0.f;
-          const float dQij = to_f(sdQ[row * CF::LDC + j]);
+          const float dAij = j < row ? sdAf[row * C + j] : 0.f;
+          const float dQij = sdQf[row * C + j];
           dkh = fmaf(dAij * kapj, f, dkh);
           dqh = fmaf(dQij * kapj, f, dqh);
           dG = fmaf((dAij * kh + dQij * qh) * kapj, f, dG);
         }
         if (j >= row) {
           const float f = ex2(gj - gi);
-          const float dAji = j > row ? to_f(sdA[j * CF::LDC + row]) : 0.f;
-          const float dQji = to_f(sdQ[j * CF::LDC + row]);
+          const float dAji = j > row ? sdAf[j * C + row] : 0.f;
+          const float dQji = sdQf[j * C + row];
           const float w = (dAji * khj + dQji * qhj) * f;
           dkap += w;
           dG -= w * kap;

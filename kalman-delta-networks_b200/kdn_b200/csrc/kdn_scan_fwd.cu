@@ -16,17 +16,12 @@ template <class CF>
 struct FwdLayout {
   static constexpr size_t sz = sizeof(typename CF::OpT);
   static constexpr int C = CF::C;
+  // raw inputs of the next chunk land here while the current one finishes
   static constexpr size_t q = 0;
   static constexpr size_t k = q + A128((size_t)C * kKD * 2);
   static constexpr size_t g = k + A128((size_t)C * kKD * 2);
   static constexpr size_t kap = g + A128((size_t)C * kKD * 4);
-  static constexpr size_t raw_end = kap + A128(CF::ISO ? (size_t)C * 4 : (size_t)C * kKD * 4);
-  static constexpr size_t T = 0;
-  static constexpr size_t Tb = T + A128((size_t)C * CF::LDA * 4);
-  static constexpr size_t X = Tb + A128((size_t)C * CF::LDC * sz);
-  static constexpr size_t W = X + A128((size_t)(CF::NB > 1 ? CF::NB - 1 : 1) * 256 * 4);
-  static constexpr size_t alias_end = W + A128((size_t)C * CF::LDK * sz);
-  static constexpr size_t v = cmax(raw_end, alias_end);
+  static constexpr size_t v = kap + A128(CF::ISO ? (size_t)C * 4 : (size_t)C * kKD * 4);
   static constexpr size_t Kr = v + A128((size_t)C * CF::LDV * sz);
   static constexpr size_t Qr = Kr + A128((size_t)C * CF::LDK * sz);
   static constexpr size_t Kc = Qr + A128((size_t)C * CF::LDK * sz);
@@ -34,7 +29,11 @@ struct FwdLayout {
   static constexpr size_t S = As;  // aliases sA once the solve is done
   static constexpr size_t Del = S + A128((size_t)kKD * CF::LDV * sz);
   static constexpr size_t Qb = As + cmax(A128((size_t)C * CF::LDA * 4), Del - S + A128((size_t)C * CF::LDV * sz));
-  static constexpr size_t small = Qb + A128((size_t)C * CF::LDC * sz);
+  static constexpr size_t Tb = Qb + A128((size_t)C * CF::LDC * sz);
+  static constexpr size_t Ab = Tb + A128((size_t)C * CF::LDC * sz);
+  static constexpr size_t Xb = Ab + A128((size_t)C * CF::LDC * sz);
+  static constexpr size_t W = Xb + A128((size_t)C * CF::LDC * sz);
+  static constexpr size_t small = W + A128((size_t)C * CF::LDK * sz);
   static constexpr size_t bytes = small + A128(small_floats<CF>() * 4);
 };
 
@@ -68,9 +67,9 @@ __global__ void __launch_bounds__(256, 1) scan_fwd_kernel(ScanParams p) {
 
   Chunk<CF> ch;
   bind_fwd_chunk(ch, base);
-  float* sT = reinterpret_cast<float*>(base + Lo::T);
   OpT* sTb = reinterpret_cast<OpT*>(base + Lo::Tb);
-  float* sX = reinterpret_cast<float*>(base + Lo::X);
+  OpT* sAb = reinterpret_cast<OpT*>(base + Lo::Ab);
+  OpT* sXb = reinterpret_cast<OpT*>(base + Lo::Xb);
   OpT* sW = reinterpret_cast<OpT*>(base + Lo::W);
   OpT* sv = reinterpret_cast<OpT*>(base + Lo::v);
   float* sA = reinterpret_cast<float*>(base + Lo::As);
@@ -81,20 +80,28 @@ __global__ void __launch_bounds__(256, 1) scan_fwd_kernel(ScanParams p) {
   const int vt = blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
   const int warp = threadIdx.x >> 5;
   const int v0 = vt * kBV;
+  const bool save_tq = vt == 0 && p.Tsave;
 
   // state slice: rows 16*warp.., all kBV columns
   float S[1][8][4];
   for_acc<1, 8>(16 * warp, 0, [&](int, int nt, int e, int row, int col) {
     S[0][nt][e] = p.S0 ? p.S0[((size_t)bh * kKD + row) * kVD + v0 + col] : 0.f;
   });
+  zero_upper_blocks<CF>(sQb);
+  zero_upper_blocks<CF>(sTb);
 
-  auto issue_loads = [&](int c) {
-    const int t0 = c * C, L = min(C, p.T - t0);
-    load_raw(ch, p, b, h, t0, L);
-    load_tile_op<CF>(sv, CF::LDV, p.v + tok_row(p, b, h, t0) * kVD + v0, (size_t)p.H * kVD, C, L, kBV);
-    if constexpr (!CF::F32) cp_async_commit();
+  auto load_qkg = [&](int c) {
+    const int t0 = c * C;
+    load_raw(ch, p, b, h, t0, min(C, p.T - t0));
   };
-  issue_loads(0);
+  auto load_v = [&](int c) {
+    const int t0 = c * C;
+    load_tile_op<CF>(sv, CF::LDV, p.v + tok_row(p, b, h, t0) * kVD + v0, (size_t)p.H * kVD, C, min(C, p.T - t0),
+                     kBV);
+  };
+  load_qkg(0);
+  load_v(0);
+  if constexpr (!CF::F32) cp_async_commit();
 
   for (int c = 0; c < p.NT; ++c) {
     const int t0 = c * C;
@@ -104,9 +111,15 @@ __global__ void __launch_bounds__(256, 1) scan_fwd_kernel(ScanParams p) {
     prep_chunk(ch);
     __syncthreads();
     const size_t cc = (size_t)bh * p.NT + c;
-    const bool save_tq = vt == 0 && p.Tsave;
-    chunk_scores(ch, sA, sQb, save_tq ? p.Qsave + cc * C * C : nullptr);
-    chunk_solve<CF>(sA, sT, sTb, sX, save_tq ? p.Tsave + cc * C * C : nullptr);
+    chunk_scores(ch, sA, sAb, sQb);
+    // the raw inputs are consumed: fetch the next chunk's behind the rest of this one
+    if (c + 1 < p.NT) load_qkg(c + 1);
+    if constexpr (!CF::F32) cp_async_commit();
+    chunk_solve<CF>(sA, sAb, sTb, sXb);
+    if (save_tq) {
+      store_cc<CF>(static_cast<OpT*>(p.Tsave) + cc * C * C, sTb);
+      store_cc<CF>(static_cast<OpT*>(p.Qsave) + cc * C * C, sQb);
+    }
 
     // W0 = T Kr (C x 128), u = T v (C x 64), scaled state operand fr * S
     const int I = warp / NJW;
@@ -121,24 +134,27 @@ __global__ void __launch_bounds__(256, 1) scan_fwd_kernel(ScanParams p) {
     zero_acc(u);
     wgemm<1, NTU, true, false>(u, sTb, CF::LDC, sv, CF::LDV, 16 * Iu, nu, 0, 16 * (Iu + 1));
     OpT* hdst = p.h ? static_cast<OpT*>(p.h) + cc * kKD * kVD : nullptr;
-    for_acc<1, 8>(16 * warp, 0, [&](int, int nt, int e, int row, int col) {
-      const float x = S[0][nt][e];
-      sS[row * CF::LDV + col] = from_f<OpT>(ch.fr[row] * x);
-      if (hdst) hdst[(size_t)row * kVD + v0 + col] = from_f<OpT>(x);
+    for_acc_pairs<1, 8>(S, 16 * warp, 0, [&](int, int, int, int row, int col, float x0, float x1) {
+      const float f = ch.fr[row];
+      st_pair(sS + row * CF::LDV + col, f * x0, f * x1);
+      if (hdst) st_pair(hdst + (size_t)row * kVD + v0 + col, x0, x1);
     });
     __syncthreads();
+    if (c + 1 < p.NT) load_v(c + 1);
+    if constexpr (!CF::F32) cp_async_commit();
 
     // delta = u - W0 (fr S)
     {
       float acc[1][NTU][4];
       zero_acc(acc);
       wgemm<1, NTU, true, false>(acc, sW, CF::LDK, sS, CF::LDV, 16 * Iu, nu, 0, kKD);
-      for_acc<1, NTU>(16 * Iu, nu, [&](int, int nt, int e, int row, int col) {
-        sDel[row * CF::LDV + col] = from_f<OpT>(u[0][nt][e] - acc[0][nt][e]);
-      });
+#pragma unroll
+      for (int nt = 0; nt < NTU; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[0][nt][e] = u[0][nt][e] - acc[0][nt][e];
+      store_acc(sDel, CF::LDV, acc, 16 * Iu, nu);
     }
     __syncthreads();
-    if (c + 1 < p.NT) issue_loads(c + 1);
 
     // o = scale (Qr (fr S) + Q delta)
     {
@@ -146,14 +162,13 @@ __global__ void __launch_bounds__(256, 1) scan_fwd_kernel(ScanParams p) {
       zero_acc(acc);
       wgemm<1, NTU, true, false>(acc, ch.Qr, CF::LDK, sS, CF::LDV, 16 * Iu, nu, 0, kKD);
       wgemm<1, NTU, true, false>(acc, sQb, CF::LDC, sDel, CF::LDV, 16 * Iu, nu, 0, 16 * (Iu + 1));
-      for_acc<1, NTU>(16 * Iu, nu, [&](int, int nt, int e, int row, int col) {
+      for_acc_pairs<1, NTU>(acc, 16 * Iu, nu, [&](int, int, int, int row, int col, float x0, float x1) {
         if (row < ch.L) {
           const size_t off = tok_row(p, b, h, t0 + row) * kVD + v0 + col;
-          const float x = p.scale * acc[0][nt][e];
           if constexpr (CF::ISO) {
-            static_cast<bf16*>(p.o)[off] = __float2bfloat16_rn(x);
+            st_pair(static_cast<bf16*>(p.o) + off, p.scale * x0, p.scale * x1);
           } else {
-            static_cast<float*>(p.o)[off] = x;
+            st_pair(static_cast<float*>(p.o) + off, p.scale * x0, p.scale * x1);
           }
         }
       });

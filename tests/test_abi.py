@@ -49,9 +49,9 @@ def test_scan_size_queries(lib):
     a.variant, a.precision = N.KDN_ISO, N.KDN_PREC_BF16
     a.B, a.T, a.H, a.K, a.V = 4, 4096, 18, 128, 128
     saved = lib.kdn_scan_saved_bytes(ctypes.byref(a))
-    # T and Q per 64-chunk (fp32) + bf16 chunk-start states
+    # T and Q per 64-chunk + chunk-start states, all bf16
     nt = 4096 // 64
-    expect = 2 * (72 * nt * 64 * 64 * 4) + 72 * nt * 128 * 128 * 2
+    expect = 2 * (72 * nt * 64 * 64 * 2) + 72 * nt * 128 * 128 * 2
     assert saved == expect
     ws = lib.kdn_scan_workspace_bytes(ctypes.byref(a))
     assert ws == 72 * nt * 128 * 128 * 2  # chunk-end adjoints
