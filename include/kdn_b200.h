@@ -89,6 +89,24 @@ int kdn_diag_gain_fwd(const float* k, const float* alpha, const float* omega,
                       float* kappa, float* carry, float* p_final, int64_t B,
                       int64_t T, int64_t H, int64_t K, void* workspace,
                       size_t workspace_bytes, kdn_stream_t stream);
+/* Allocation-free variant of kdn_diag_gain_fwd (no counterpart in the
+ * reference).  For callers that must not allocate device memory at call
+ * time: code running while a CUDA stream is being captured into a graph (an
+ * allocation there breaks or invalidates the capture) and plugin hosts whose
+ * enqueue path forbids allocation.  It takes no workspace: the per-segment
+ * covariance maps live in a 16 MiB static device array of the library
+ * (B*H*ceil(T/64)*K <= 1048576, larger sizes return KDN_ERR_INVALID).  It
+ * calls no cudaMalloc or cudaFree.  Its first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress); make that first call before
+ * any stream capture.  All calls share the array, so calls that overlap on
+ * the GPU (different streams, no ordering) race; order them on one stream.
+ * Outputs and carry are as for kdn_diag_gain_fwd. */
+int kdn_diag_gain_fwd_noalloc(const float* k, const float* alpha,
+                              const float* omega, const float* r,
+                              const float* initial_precision, float* kappa,
+                              float* carry, float* p_final, int64_t B,
+                              int64_t T, int64_t H, int64_t K,
+                              kdn_stream_t stream);
 int kdn_diag_gain_bwd(const float* k, const float* alpha, const float* omega,
                       const float* r, const float* initial_precision,
                       const void* omega_raw, const void* r_raw,

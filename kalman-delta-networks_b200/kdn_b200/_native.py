@@ -73,6 +73,7 @@ _SIGNATURES = {
     "kdn_diag_gain_carry_elems": ([_I64, _I64, _I64, _I64], _I64),
     "kdn_diag_gain_workspace_bytes": ([_I64, _I64, _I64, _I64], _SZ),
     "kdn_diag_gain_fwd": ([_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _SZ, _P], ctypes.c_int),
+    "kdn_diag_gain_fwd_noalloc": ([_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P], ctypes.c_int),
     "kdn_diag_gain_bwd": (
         [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _SZ, _P],
         ctypes.c_int,

@@ -12,6 +12,8 @@
 // Diagonal (one thread per key channel, 64-token segments, per-token channel
 // reductions by warp transpose-reduce): diag_kdn_chunk.py:374-701 and the
 // oracle diag_kdn_naive.py:256-276.
+#include <mutex>
+
 #include "kdn_common.cuh"
 
 namespace kdn {
@@ -435,6 +437,39 @@ __global__ void __launch_bounds__(K) diag_gain_bwd_emit_kernel(
 }
 
 }  // namespace
+
+// ---------------------------------------------------------------------------
+// Scratch of kdn_diag_gain_fwd_noalloc: the per-segment covariance maps, in a
+// file-scope device array instead of caller workspace.  Every GPU that loads
+// the library holds these 16 MiB until the process exits.
+// ---------------------------------------------------------------------------
+constexpr int64_t kNoAllocMapEntries = 1 << 20;  // float4 entries = B*H*ceil(T/64)*K at most
+static __device__ __align__(256) float4 g_noalloc_maps[kNoAllocMapEntries];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float4* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of g_noalloc_maps on the current device.  In host code the
+// array's name is only a host-side stand-in; the real address comes from
+// cudaGetSymbolAddress, looked up once per device with that device current.
+int noalloc_maps(float4** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return check_launch("cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return set_error(KDN_ERR_INVALID, "kdn_diag_gain_fwd_noalloc: device %d", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* ptr = nullptr;
+    const cudaError_t rc = cudaGetSymbolAddress(&ptr, g_noalloc_maps);
+    if (rc != cudaSuccess || !ptr)
+      return set_error(KDN_ERR_CUDA, "kdn_diag_gain_fwd_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(rc));
+    g_noalloc_ptr[dev] = static_cast<float4*>(ptr);
+  }
+  *out = g_noalloc_ptr[dev];
+  return KDN_OK;
+}
+}  // namespace
 }  // namespace kdn
 
 using namespace kdn;
@@ -505,6 +540,40 @@ int kdn_diag_gain_fwd(const float* k, const float* alpha, const float* omega, co
     diag_gain_emit_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, carry, kappa, (int)T, (int)H, nseg);
   }
   return check_launch("diag_gain_fwd kernels");
+}
+
+int kdn_diag_gain_fwd_noalloc(const float* k, const float* alpha, const float* omega, const float* r,
+                              const float* init_prec, float* kappa, float* carry, float* p_final, int64_t B,
+                              int64_t T, int64_t H, int64_t K, kdn_stream_t stream) {
+  if (B <= 0 || H <= 0 || T <= 0 || !k || !alpha || !omega || !r || !init_prec || !kappa || !carry)
+    return set_error(KDN_ERR_INVALID, "kdn_diag_gain_fwd_noalloc: invalid arguments");
+  if (K != 64 && K != 128)
+    return set_error(KDN_ERR_INVALID, "kdn_diag_gain_fwd_noalloc: K must be 64 or 128, got %lld", (long long)K);
+  if (T > INT32_MAX || B * H > 65535 * 1024)
+    return set_error(KDN_ERR_INVALID, "kdn_diag_gain_fwd_noalloc: size too large");
+  const int64_t nseg = (T + kDiagSeg - 1) / kDiagSeg;
+  if (B * H * nseg * K > kNoAllocMapEntries)
+    return set_error(KDN_ERR_INVALID,
+                     "kdn_diag_gain_fwd_noalloc: B*H*ceil(T/64)*K = %lld exceeds the static scratch of %lld entries; "
+                     "use kdn_diag_gain_fwd with caller workspace",
+                     (long long)(B * H * nseg * K), (long long)kNoAllocMapEntries);
+  float4* maps = nullptr;
+  int rc = noalloc_maps(&maps);
+  if (rc != KDN_OK) return rc;
+  // Every map entry is written by diag_gain_map_kernel before the carry
+  // kernel reads it, so the scratch needs no clearing between calls.
+  cudaStream_t st = (cudaStream_t)stream;
+  dim3 grid((unsigned)nseg, (unsigned)(B * H));
+  if (K == 128) {
+    diag_gain_map_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, maps, (int)T, (int)H, (int)nseg);
+    diag_gain_carry_kernel<128><<<(unsigned)(B * H), 128, 0, st>>>(maps, init_prec, carry, p_final, (int)H, (int)nseg);
+    diag_gain_emit_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, carry, kappa, (int)T, (int)H, (int)nseg);
+  } else {
+    diag_gain_map_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, maps, (int)T, (int)H, (int)nseg);
+    diag_gain_carry_kernel<64><<<(unsigned)(B * H), 64, 0, st>>>(maps, init_prec, carry, p_final, (int)H, (int)nseg);
+    diag_gain_emit_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, carry, kappa, (int)T, (int)H, (int)nseg);
+  }
+  return check_launch("diag_gain_fwd_noalloc kernels");
 }
 
 int kdn_diag_gain_bwd(const float* k, const float* alpha, const float* omega, const float* r, const float* init_prec,
