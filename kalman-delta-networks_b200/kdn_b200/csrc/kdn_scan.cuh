@@ -32,6 +32,7 @@ constexpr int kKD = 128;  // key width
 constexpr int kVD = 128;  // value width
 constexpr int kBV = 64;   // value tile of the sequential kernels
 constexpr float kRngMax = 100.f;
+constexpr int kSeqThreads = 512;  // sequential kernels: 16 warps
 
 template <bool ISO_, int C_, class OpT_>
 struct Cfg {
@@ -200,21 +201,58 @@ __device__ __forceinline__ float rho_col(const Chunk<CF>& ch, int c) {
 // Row norms (iso), range check, per-channel factors and the three gated
 // operands.  Thread t handles channels 8*(t%16) .. +7 of rows t/16, t/16 +
 // blockDim/16, ...; the 16 threads of a row are one half-warp, so row norms
-// are half-warp shuffles.  The caller places the barrier that publishes the
-// results.
+// are half-warp shuffles.  The operands are built in the same pass with the
+// fast-path reference (the gate of the middle row, known up front) and built
+// again only when the range check sends the chunk to the exact path.  The
+// caller places the barrier that publishes the results.
+template <class CF>
+__device__ __forceinline__ void build_operands(Chunk<CF>& ch, int r, int c0, const float (&rr)[8],
+                                               const float (&rc)[8], float qs, float ks) {
+  float kr[8], qr[8], kc[8];
+  if (r < ch.L) {
+    float g8[8], k8[8], q8[8], kap[8];
+    ld8(g8, ch.g + r * kKD + c0);
+    ld8(k8, ch.k + r * kKD + c0);
+    ld8(q8, ch.q + r * kKD + c0);
+    float bs = 1.f;
+    if constexpr (CF::ISO) {
+      bs = ch.beta[r] * ks;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) kap[i] = k8[i];
+    } else {
+      ld8(kap, ch.kap + r * kKD + c0);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float er = ex2a(g8[i] - rr[i]);
+      const float ec = ex2a(rc[i] - g8[i]);
+      kr[i] = k8[i] * ks * er;
+      qr[i] = q8[i] * qs * er;
+      kc[i] = kap[i] * bs * ec;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) kr[i] = qr[i] = kc[i] = 0.f;
+  }
+  st8(ch.Kr + r * CF::LDK + c0, kr);
+  st8(ch.Qr + r * CF::LDK + c0, qr);
+  st8(ch.Kc + r * CF::LDK + c0, kc);
+}
+
 template <class CF>
 __device__ void prep_chunk(Chunk<CF>& ch) {
   constexpr int C = CF::C;
-  using OpT = typename CF::OpT;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   const int L = ch.L;
   ch.m = L >= C ? C / 2 : (((L - 1) / 2) & ~15);
   const int c0 = (threadIdx.x & 15) * 8;
   const int rstep = blockDim.x >> 4;
-  float gm[8];
+  float gm[8], gl[8];
   ld8(gm, ch.g + ch.m * kKD + c0);
+  ld8(gl, ch.g + (L - 1) * kKD + c0);
   float rng = 0.f;
   for (int r = threadIdx.x >> 4; r < C; r += rstep) {
+    float qs = 1.f, ks = 1.f;
     if constexpr (CF::ISO) {
       float q8[8], k8[8];
       ld8(q8, ch.q + r * kKD + c0);
@@ -230,9 +268,11 @@ __device__ void prep_chunk(Chunk<CF>& ch) {
         sq += __shfl_xor_sync(0xffffffffu, sq, o);
         sk += __shfl_xor_sync(0xffffffffu, sk, o);
       }
+      qs = rsqrtf(sq + 1e-6f);
+      ks = rsqrtf(sk + 1e-6f);
       if ((threadIdx.x & 15) == 0) {
-        ch.rq[r] = rsqrtf(sq + 1e-6f);
-        ch.rk[r] = rsqrtf(sk + 1e-6f);
+        ch.rq[r] = qs;
+        ch.rk[r] = ks;
       }
     }
     if (r < L) {
@@ -241,6 +281,7 @@ __device__ void prep_chunk(Chunk<CF>& ch) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) rng = fmaxf(rng, fabsf(g8[i] - gm[i]));
     }
+    build_operands(ch, r, c0, gm, gm, qs, ks);
   }
   rng = warp_max(rng);
   if (lane == 0) ch.red[warp] = rng;
@@ -248,8 +289,7 @@ __device__ void prep_chunk(Chunk<CF>& ch) {
   float tot = 0.f;
   for (int w = 0; w < nw; ++w) tot = fmaxf(tot, ch.red[w]);
   ch.fast = tot <= kRngMax;
-  float gl[8], rr[8], rc[8];
-  ld8(gl, ch.g + (L - 1) * kKD + c0);
+  float rr[8], rc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     rr[i] = ch.fast ? gm[i] : 0.f;
@@ -265,38 +305,11 @@ __device__ void prep_chunk(Chunk<CF>& ch) {
       ch.glast[c0 + i] = gl[i];
     }
   }
-  for (int r = threadIdx.x >> 4; r < C; r += rstep) {
-    float kr[8], qr[8], kc[8];
-    if (r < L) {
-      float g8[8], k8[8], q8[8], kap[8];
-      ld8(g8, ch.g + r * kKD + c0);
-      ld8(k8, ch.k + r * kKD + c0);
-      ld8(q8, ch.q + r * kKD + c0);
-      float ks = 1.f, qs = 1.f, bs = 1.f;
-      if constexpr (CF::ISO) {
-        ks = ch.rk[r];
-        qs = ch.rq[r];
-        bs = ch.beta[r] * ks;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) kap[i] = k8[i];
-      } else {
-        ld8(kap, ch.kap + r * kKD + c0);
-      }
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float er = ex2a(g8[i] - rr[i]);
-        const float ec = ex2a(rc[i] - g8[i]);
-        kr[i] = k8[i] * ks * er;
-        qr[i] = q8[i] * qs * er;
-        kc[i] = kap[i] * bs * ec;
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) kr[i] = qr[i] = kc[i] = 0.f;
+  if (!ch.fast) {
+    for (int r = threadIdx.x >> 4; r < C; r += rstep) {
+      const float qs = CF::ISO ? ch.rq[r] : 1.f, ks = CF::ISO ? ch.rk[r] : 1.f;
+      build_operands(ch, r, c0, rr, rc, qs, ks);
     }
-    st8(ch.Kr + r * CF::LDK + c0, kr);
-    st8(ch.Qr + r * CF::LDK + c0, qr);
-    st8(ch.Kc + r * CF::LDK + c0, kc);
   }
 }
 

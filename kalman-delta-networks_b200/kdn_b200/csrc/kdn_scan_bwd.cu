@@ -74,14 +74,15 @@ __device__ __forceinline__ void convert_dO(typename CF::OpT* dst, const float* s
 }
 
 template <class CF>
-__global__ void __launch_bounds__(256, 1) scan_bwd_state_kernel(ScanParams p) {
+__global__ void __launch_bounds__(kSeqThreads, 1) scan_bwd_state_kernel(ScanParams p) {
   using OpT = typename CF::OpT;
   using Lo = StateLayout<CF>;
   constexpr int C = CF::C;
-  constexpr int NTW = C / 8;
+  constexpr int NTW = C / 16;
   constexpr int NJW = kKD / (8 * NTW);
-  constexpr int NTU = C / 16;
+  constexpr int NTU = C / 32;
   constexpr int NJU = kBV / (8 * NTU);
+  static_assert((C / 16) * NJW == 16 && (C / 16) * NJU == 16, "16 warps");
   extern __shared__ __align__(128) char smem[];
   char* base = CF::F32 ? p.dbg + (size_t)(blockIdx.y * gridDim.x + blockIdx.x) * p.dbg_stride : smem;
 
@@ -109,8 +110,9 @@ __global__ void __launch_bounds__(256, 1) scan_bwd_state_kernel(ScanParams p) {
   const int warp = threadIdx.x >> 5;
   const int v0 = vt * kBV;
 
-  float dS[1][8][4];
-  for_acc<1, 8>(16 * warp, 0, [&](int, int nt, int e, int row, int col) {
+  const int sm0 = 16 * (warp >> 1), sn0 = 32 * (warp & 1);
+  float dS[1][4][4];
+  for_acc<1, 4>(sm0, sn0, [&](int, int nt, int e, int row, int col) {
     dS[0][nt][e] = p.dST ? p.dST[((size_t)bh * kKD + row) * kVD + v0 + col] : 0.f;
   });
 
@@ -147,7 +149,7 @@ __global__ void __launch_bounds__(256, 1) scan_bwd_state_kernel(ScanParams p) {
       store_acc(sW, CF::LDK, acc, 16 * I, (warp % NJW) * 8 * NTW);
     }
     OpT* dhdst = static_cast<OpT*>(p.dh) + ((size_t)bh * p.NT + c) * kKD * kVD;
-    for_acc_pairs<1, 8>(dS, 16 * warp, 0, [&](int, int, int, int row, int col, float x0, float x1) {
+    for_acc_pairs<1, 4>(dS, sm0, sn0, [&](int, int, int, int row, int col, float x0, float x1) {
       const float f = ch.fL[row];
       st_pair(sDS + row * CF::LDV + col, f * x0, f * x1);
       st_pair(dhdst + (size_t)row * kVD + v0 + col, x0, x1);
@@ -172,18 +174,18 @@ __global__ void __launch_bounds__(256, 1) scan_bwd_state_kernel(ScanParams p) {
 
     // dS <- Diag(2^g_L) dS + Diag(fr) (scale Qr^T dO - W0^T ddelta)
     {
-      float a1[1][8][4], a2[1][8][4];
+      float a1[1][4][4], a2[1][4][4];
       zero_acc(a1);
       zero_acc(a2);
-      wgemm<1, 8, false, false>(a1, ch.Qr, CF::LDK, sdO, CF::LDV, 16 * warp, 0, 0, C);
-      wgemm<1, 8, false, false>(a2, sW, CF::LDK, sDD, CF::LDV, 16 * warp, 0, 0, C);
-      for_acc<1, 8>(16 * warp, 0, [&](int, int nt, int e, int row, int) {
+      wgemm<1, 4, false, false>(a1, ch.Qr, CF::LDK, sdO, CF::LDV, sm0, sn0, 0, C);
+      wgemm<1, 4, false, false>(a2, sW, CF::LDK, sDD, CF::LDV, sm0, sn0, 0, C);
+      for_acc<1, 4>(sm0, sn0, [&](int, int nt, int e, int row, int) {
         dS[0][nt][e] = ch.gL[row] * dS[0][nt][e] + ch.fr[row] * (p.scale * a1[0][nt][e] - a2[0][nt][e]);
       });
     }
   }
   if (p.dS0) {
-    for_acc<1, 8>(16 * warp, 0, [&](int, int nt, int e, int row, int col) {
+    for_acc<1, 4>(sm0, sn0, [&](int, int nt, int e, int row, int col) {
       p.dS0[((size_t)bh * kKD + row) * kVD + v0 + col] = dS[0][nt][e];
     });
   }
@@ -211,16 +213,15 @@ struct ChunkLayout {
   static constexpr size_t dS = S0 + A128((size_t)kKD * CF::LDV * sz);
   static constexpr size_t dOst = dS + A128((size_t)kKD * CF::LDV * sz);  // diag fp32 dO staging
   static constexpr size_t loop_end = dOst + A128(CF::ISO ? 16 : (size_t)C * kBV * 4);
-  // after the loop (aliases again)
-  static constexpr size_t dW = 0;
+  // after the loop (aliases the loop buffers): the raw inputs are fetched
+  // again into [0, raw_end) for the final gate mapping, next to these
+  static constexpr size_t dW = raw_end;
   static constexpr size_t dT = dW + A128((size_t)C * CF::LDK * sz);
   static constexpr size_t X = dT + A128((size_t)C * CF::LDC * sz);
   static constexpr size_t dA = X + A128((size_t)C * CF::LDC * sz);
   static constexpr size_t dQ = dA + A128((size_t)C * CF::LDC * sz);
-  static constexpr size_t dAf = dQ + A128((size_t)C * CF::LDC * sz);  // fp32 copies for the exact path
-  static constexpr size_t dQf = dAf + A128((size_t)C * C * 4);
-  static constexpr size_t post_end = dQf + A128((size_t)C * C * 4);
-  static constexpr size_t Kr = cmax(cmax(raw_end, loop_end), post_end);
+  static constexpr size_t post_end = dQ + A128((size_t)C * CF::LDC * sz);
+  static constexpr size_t Kr = cmax(loop_end, post_end);
   static constexpr size_t Qr = Kr + A128((size_t)C * CF::LDK * sz);
   static constexpr size_t Kc = Qr + A128((size_t)C * CF::LDK * sz);
   static constexpr size_t Tb = Kc + A128((size_t)C * CF::LDK * sz);
@@ -273,8 +274,6 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_kernel(ScanParams p) {
   OpT* sX = reinterpret_cast<OpT*>(base + Lo::X);
   OpT* sdA = reinterpret_cast<OpT*>(base + Lo::dA);
   OpT* sdQ = reinterpret_cast<OpT*>(base + Lo::dQ);
-  float* sdAf = reinterpret_cast<float*>(base + Lo::dAf);
-  float* sdQf = reinterpret_cast<float*>(base + Lo::dQf);
   OpT* sTb = reinterpret_cast<OpT*>(base + Lo::Tb);
   OpT* sQb = reinterpret_cast<OpT*>(base + Lo::Qb);
   OpT* sW = reinterpret_cast<OpT*>(base + Lo::W);
@@ -345,23 +344,26 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_kernel(ScanParams p) {
     }
     __syncthreads();
     if constexpr (!CF::ISO) convert_dO<CF>(sdO, dOst);
-    // S0' = fr S0, dS'' = fL dS, and cgl += sum_v S0' dS''  (4 threads per channel)
-    {
-      const int ch_ = threadIdx.x >> 2, part = threadIdx.x & 3;
+    // S0' = fr S0, dS'' = fL dS, and cgl += sum_v S0' dS''  (8 threads per state row)
+    for (int grp = threadIdx.x; grp < kKD * (kBV / 8); grp += blockDim.x) {
+      const int row = grp >> 3, c8 = (grp & 7) * 8;
+      float s0[8], ds[8];
+      ld8(s0, sS0 + row * CF::LDV + c8);
+      ld8(ds, sdS + row * CF::LDV + c8);
+      const float fr = ch.fr[row], fl = ch.fL[row];
       float acc = 0.f;
-      if (ch_ < kKD) {
-        const float fr = ch.fr[ch_], fl = ch.fL[ch_];
-        for (int vv = part * (kBV / 4); vv < (part + 1) * (kBV / 4); ++vv) {
-          const float s0 = fr * to_f(sS0[ch_ * CF::LDV + vv]);
-          const float ds = fl * to_f(sdS[ch_ * CF::LDV + vv]);
-          sS0[ch_ * CF::LDV + vv] = from_f<OpT>(s0);
-          sdS[ch_ * CF::LDV + vv] = from_f<OpT>(ds);
-          acc = fmaf(s0, ds, acc);
-        }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        s0[i] *= fr;
+        ds[i] *= fl;
+        acc = fmaf(s0[i], ds[i], acc);
       }
+      st8(sS0 + row * CF::LDV + c8, s0);
+      st8(sdS + row * CF::LDV + c8, ds);
       acc += __shfl_xor_sync(0xffffffffu, acc, 1);
       acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-      if (ch_ < kKD && part == 0) cgl[ch_] += acc;
+      acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+      if ((grp & 7) == 0) cgl[row] += acc;
     }
     __syncthreads();
 
@@ -390,8 +392,8 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_kernel(ScanParams p) {
       float a[1][NTV][4];
       zero_acc(a);
       wgemm<1, NTV, false, false>(a, sTb, CF::LDC, sDD, CF::LDV, 16 * Iv, nv, 16 * Iv, C);
-      for_acc<1, NTV>(16 * Iv, nv, [&](int, int nt, int e, int row, int col) {
-        if (row < L) p.dv[tok_row(p, b, h, t0 + row) * kVD + v0 + col] = __float2bfloat16_rn(a[0][nt][e]);
+      for_acc_pairs<1, NTV>(a, 16 * Iv, nv, [&](int, int, int, int row, int col, float x0, float x1) {
+        if (row < L) st_pair(p.dv + tok_row(p, b, h, t0 + row) * kVD + v0 + col, x0, x1);
       });
     }
     // value-contracted accumulations
@@ -404,6 +406,10 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_kernel(ScanParams p) {
     }
     __syncthreads();
   }
+
+  // the raw inputs again, for the final gate mapping (overlaps the post-loop products)
+  load_raw(ch, p, b, h, t0, L);
+  if constexpr (!CF::F32) cp_async_commit();
 
   // cfl[c] = sum_j Kc_jc (delta dS''^T)_jc: the fL cotangent of the last row
   {
@@ -441,15 +447,11 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_kernel(ScanParams p) {
       sX[i * CF::LDC + j] = from_f<OpT>(0.f);
       sdA[i * CF::LDC + j] = from_f<OpT>(0.f);
       sdQ[i * CF::LDC + j] = from_f<OpT>(0.f);
-      sdAf[e] = 0.f;
-      sdQf[e] = 0.f;
     }
   }
   if (own_tri) {
     for_acc<1, 2>(16 * TI, 16 * TJ, [&](int, int nt, int e, int row, int col) {
-      const float x = col <= row ? p.scale * aDQ[0][nt][e] : 0.f;
-      sdQ[row * CF::LDC + col] = from_f<OpT>(x);
-      sdQf[row * C + col] = x;
+      sdQ[row * CF::LDC + col] = from_f<OpT>(col <= row ? p.scale * aDQ[0][nt][e] : 0.f);
     });
   }
   __syncthreads();
@@ -478,11 +480,11 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_kernel(ScanParams p) {
     zero_acc(x);
     wgemm<1, 2, false, false>(x, sTb, CF::LDC, sX, CF::LDC, 16 * TI, 16 * TJ, 16 * TI, C);
     for_acc<1, 2>(16 * TI, 16 * TJ, [&](int, int nt, int e, int row, int col) {
-      const float y = col < row ? -x[0][nt][e] : 0.f;
-      sdA[row * CF::LDC + col] = from_f<OpT>(y);
-      sdAf[row * C + col] = y;
+      sdA[row * CF::LDC + col] = from_f<OpT>(col < row ? -x[0][nt][e] : 0.f);
     });
   }
+  __syncthreads();
+  if constexpr (!CF::F32) cp_async_wait_all();
   __syncthreads();
   if (ch.fast) {
     wgemm<1, NTK, true, false>(aKr, sdA, CF::LDC, ch.Kc, CF::LDK, 16 * I, n0, 0, 16 * (I + 1));
@@ -491,86 +493,101 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_kernel(ScanParams p) {
     wgemm<1, NTK, false, false>(aKc, sdQ, CF::LDC, ch.Qr, CF::LDK, 16 * I, n0, 16 * I, C);
   }
 
-  // map back through the gate factors
-  float aG[1][NTK][4];
-  float rsum[2] = {0.f, 0.f};  // iso: dbeta partials of rows g, g+8
-  for_acc<1, NTK>(16 * I, n0, [&](int, int nt, int e, int row, int col) {
-    aG[0][nt][e] = 0.f;
-    if (row >= L) return;
-    const size_t rowg = tok_row(p, b, h, t0 + row);
-    const float gi = p.g[rowg * kKD + col];
-    const float rr = ch.fast ? ch.gmid[col] : 0.f;
-    const float rc = ch.fast ? ch.gmid[col] : ch.glast[col];
-    const float er = ex2(gi - rr), ec = ex2(rc - gi);
-    float kh, qh, kap;
-    if constexpr (CF::ISO) {
-      kh = ch.rk[row] * __bfloat162float(p.k[rowg * kKD + col]);
-      qh = ch.rq[row] * __bfloat162float(p.q[rowg * kKD + col]);
-      kap = p.beta[rowg] * kh;
-    } else {
-      kh = __bfloat162float(p.k[rowg * kKD + col]);
-      qh = __bfloat162float(p.q[rowg * kKD + col]);
-      kap = p.kappa[rowg * kKD + col];
-    }
-    float dkh = aKr[0][nt][e] * er, dqh = aQr[0][nt][e] * er, dkap = aKc[0][nt][e] * ec;
-    float dG = aKr[0][nt][e] * kh * er + aQr[0][nt][e] * qh * er - aKc[0][nt][e] * kap * ec;
-    if (row == L - 1) dG += cfl[col] + cgl[col] * ch.gL[col] / (ch.fr[col] * ch.fL[col]);
-    if (!ch.fast) {
-      // exact gate factors for the score terms
-      for (int j = 0; j < L; ++j) {
-        const size_t rowj = tok_row(p, b, h, t0 + j);
-        const float gj = p.g[rowj * kKD + col];
-        float khj, qhj, kapj;
-        if constexpr (CF::ISO) {
-          khj = ch.rk[j] * __bfloat162float(p.k[rowj * kKD + col]);
-          qhj = ch.rq[j] * __bfloat162float(p.q[rowj * kKD + col]);
-          kapj = p.beta[rowj] * khj;
-        } else {
-          khj = __bfloat162float(p.k[rowj * kKD + col]);
-          qhj = __bfloat162float(p.q[rowj * kKD + col]);
-          kapj = p.kappa[rowj * kKD + col];
+  // map back through the gate factors (two adjacent channels per step)
+  const int lane4 = lane & 3, gq = lane >> 2;
+  float rsum[2] = {0.f, 0.f};  // iso: dbeta partials of rows gq, gq+8
+#pragma unroll
+  for (int nt = 0; nt < NTK; ++nt)
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int row = 16 * I + gq + 8 * hh, col = n0 + nt * 8 + 2 * lane4;
+      if (row >= L) continue;
+      const float2 g2 = *reinterpret_cast<const float2*>(ch.g + row * kKD + col);
+      const float2 k2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(ch.k + row * kKD + col));
+      const float2 q2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(ch.q + row * kKD + col));
+      float kh[2] = {k2.x, k2.y}, qh[2] = {q2.x, q2.y}, gi[2] = {g2.x, g2.y}, kap[2];
+      if constexpr (CF::ISO) {
+        const float rk = ch.rk[row], rq = ch.rq[row], be = ch.beta[row];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          kh[u] *= rk;
+          qh[u] *= rq;
+          kap[u] = be * kh[u];
         }
-        if (j <= row) {
-          const float f = ex2(gi - gj);
-          const float dAij = j < row ? sdAf[row * C + j] : 0.f;
-          const float dQij = sdQf[row * C + j];
-          dkh = fmaf(dAij * kapj, f, dkh);
-          dqh = fmaf(dQij * kapj, f, dqh);
-          dG = fmaf((dAij * kh + dQij * qh) * kapj, f, dG);
-        }
-        if (j >= row) {
-          const float f = ex2(gj - gi);
-          const float dAji = j > row ? sdAf[j * C + row] : 0.f;
-          const float dQji = sdQf[j * C + row];
-          const float w = (dAji * khj + dQji * qhj) * f;
-          dkap += w;
-          dG -= w * kap;
+      } else {
+        const float2 c2 = *reinterpret_cast<const float2*>(ch.kap + row * kKD + col);
+        kap[0] = c2.x;
+        kap[1] = c2.y;
+      }
+      float dkh[2], dqh[2], dkap[2], dG[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int cu = col + u;
+        const float rr = ch.fast ? ch.gmid[cu] : 0.f;
+        const float rc = ch.fast ? ch.gmid[cu] : ch.glast[cu];
+        const float er = ex2a(gi[u] - rr), ec = ex2a(rc - gi[u]);
+        const float xk = aKr[0][nt][2 * hh + u], xq = aQr[0][nt][2 * hh + u], xc = aKc[0][nt][2 * hh + u];
+        dkh[u] = xk * er;
+        dqh[u] = xq * er;
+        dkap[u] = xc * ec;
+        dG[u] = xk * kh[u] * er + xq * qh[u] * er - xc * kap[u] * ec;
+        if (row == L - 1) dG[u] += cfl[cu] + cgl[cu] * ch.gL[cu] / (ch.fr[cu] * ch.fL[cu]);
+        if (!ch.fast) {
+          // exact gate factors for the score terms
+          for (int j = 0; j < L; ++j) {
+            const float gj = ch.g[j * kKD + cu];
+            const float khj = khat_at(ch, j, cu), qhj = qhat_at(ch, j, cu), kapj = kappa_at(ch, j, cu);
+            if (j <= row) {
+              const float f = ex2(gi[u] - gj);
+              const float dAij = j < row ? to_f(sdA[row * CF::LDC + j]) : 0.f;
+              const float dQij = to_f(sdQ[row * CF::LDC + j]);
+              dkh[u] = fmaf(dAij * kapj, f, dkh[u]);
+              dqh[u] = fmaf(dQij * kapj, f, dqh[u]);
+              dG[u] = fmaf((dAij * kh[u] + dQij * qh[u]) * kapj, f, dG[u]);
+            }
+            if (j >= row) {
+              const float f = ex2(gj - gi[u]);
+              const float dAji = j > row ? to_f(sdA[j * CF::LDC + row]) : 0.f;
+              const float dQji = to_f(sdQ[j * CF::LDC + row]);
+              const float w = (dAji * khj + dQji * qhj) * f;
+              dkap[u] += w;
+              dG[u] -= w * kap[u];
+            }
+          }
         }
       }
+      const size_t off = tok_row(p, b, h, t0 + row) * kKD + col;
+      st_pair(p.dg + off, dG[0], dG[1]);
+      if constexpr (CF::ISO) {
+        const float be = ch.beta[row];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          rsum[hh] += dkap[u] * kh[u];  // dbeta_i = sum_c dkappa_ic k_hat_ic
+          dkh[u] += be * dkap[u];       // kappa = beta k_hat
+        }
+      } else {
+        st_pair(p.dkappa + off, dkap[0], dkap[1]);
+      }
+      aKr[0][nt][2 * hh] = dkh[0];
+      aKr[0][nt][2 * hh + 1] = dkh[1];
+      aQr[0][nt][2 * hh] = dqh[0];
+      aQr[0][nt][2 * hh + 1] = dqh[1];
     }
-    aG[0][nt][e] = dG;
-    if constexpr (CF::ISO) {
-      rsum[e >> 1] += dkap * kh;                 // dbeta_i = sum_c dkappa_ic k_hat_ic
-      dkh += p.beta[rowg] * dkap;                // kappa = beta k_hat
-    } else {
-      p.dkappa[rowg * kKD + col] = dkap;
-    }
-    aKr[0][nt][e] = dkh;
-    aQr[0][nt][e] = dqh;
-    p.dg[rowg * kKD + col] = dG;
-  });
 
   if constexpr (CF::ISO) {
-    // row reductions: dbeta, <dk_hat, k_hat>, <dq_hat, q_hat>
+    // row reductions: dbeta, <dk_hat, k_hat>, <dq_hat, q_hat>, then the L2-norm VJP
     float dk_dot[2] = {0.f, 0.f}, dq_dot[2] = {0.f, 0.f};
-    for_acc<1, NTK>(16 * I, n0, [&](int, int nt, int e, int row, int col) {
-      if (row >= L) return;
-      const size_t rowg = tok_row(p, b, h, t0 + row);
-      const float kh = ch.rk[row] * __bfloat162float(p.k[rowg * kKD + col]);
-      const float qh = ch.rq[row] * __bfloat162float(p.q[rowg * kKD + col]);
-      dk_dot[e >> 1] += aKr[0][nt][e] * kh;
-      dq_dot[e >> 1] += aQr[0][nt][e] * qh;
-    });
+#pragma unroll
+    for (int nt = 0; nt < NTK; ++nt)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int row = 16 * I + gq + 8 * hh, col = n0 + nt * 8 + 2 * lane4;
+        if (row >= L) continue;
+        const float2 k2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(ch.k + row * kKD + col));
+        const float2 q2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(ch.q + row * kKD + col));
+        dk_dot[hh] += (aKr[0][nt][2 * hh] * k2.x + aKr[0][nt][2 * hh + 1] * k2.y) * ch.rk[row];
+        dq_dot[hh] += (aQr[0][nt][2 * hh] * q2.x + aQr[0][nt][2 * hh + 1] * q2.y) * ch.rq[row];
+      }
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       float x0 = rsum[j], x1 = dk_dot[j], x2 = dq_dot[j];
@@ -580,32 +597,42 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_kernel(ScanParams p) {
         x1 += __shfl_xor_sync(0xffffffffu, x1, o);
         x2 += __shfl_xor_sync(0xffffffffu, x2, o);
       }
-      if ((lane & 3) == 0) {
-        const int row = 16 * I + (lane >> 2) + 8 * j;
+      if (lane4 == 0) {
+        const int row = 16 * I + gq + 8 * j;
         atomicAdd(&rbeta[row], x0);
         atomicAdd(&rdotk[row], x1);
         atomicAdd(&rdotq[row], x2);
       }
     }
     __syncthreads();
-    for_acc<1, NTK>(16 * I, n0, [&](int, int nt, int e, int row, int col) {
-      if (row >= L) return;
-      const size_t rowg = tok_row(p, b, h, t0 + row);
-      const float kh = ch.rk[row] * __bfloat162float(p.k[rowg * kKD + col]);
-      const float qh = ch.rq[row] * __bfloat162float(p.q[rowg * kKD + col]);
-      p.dk[rowg * kKD + col] = __float2bfloat16_rn(ch.rk[row] * (aKr[0][nt][e] - kh * rdotk[row]));
-      p.dq[rowg * kKD + col] = __float2bfloat16_rn(ch.rq[row] * (aQr[0][nt][e] - qh * rdotq[row]));
-    });
+#pragma unroll
+    for (int nt = 0; nt < NTK; ++nt)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int row = 16 * I + gq + 8 * hh, col = n0 + nt * 8 + 2 * lane4;
+        if (row >= L) continue;
+        const float2 k2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(ch.k + row * kKD + col));
+        const float2 q2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(ch.q + row * kKD + col));
+        const float rk = ch.rk[row], rq = ch.rq[row];
+        const size_t off = tok_row(p, b, h, t0 + row) * kKD + col;
+        st_pair(p.dk + off, rk * (aKr[0][nt][2 * hh] - k2.x * rk * rdotk[row]),
+                rk * (aKr[0][nt][2 * hh + 1] - k2.y * rk * rdotk[row]));
+        st_pair(p.dq + off, rq * (aQr[0][nt][2 * hh] - q2.x * rq * rdotq[row]),
+                rq * (aQr[0][nt][2 * hh + 1] - q2.y * rq * rdotq[row]));
+      }
     for (int i = threadIdx.x; i < L; i += blockDim.x) p.dbeta[tok_row(p, b, h, t0 + i)] = rbeta[i];
   } else {
-    for_acc<1, NTK>(16 * I, n0, [&](int, int nt, int e, int row, int col) {
-      if (row >= L) return;
-      const size_t rowg = tok_row(p, b, h, t0 + row);
-      p.dk[rowg * kKD + col] = __float2bfloat16_rn(aKr[0][nt][e]);
-      p.dq[rowg * kKD + col] = __float2bfloat16_rn(aQr[0][nt][e]);
-    });
+#pragma unroll
+    for (int nt = 0; nt < NTK; ++nt)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int row = 16 * I + gq + 8 * hh, col = n0 + nt * 8 + 2 * lane4;
+        if (row >= L) continue;
+        const size_t off = tok_row(p, b, h, t0 + row) * kKD + col;
+        st_pair(p.dk + off, aKr[0][nt][2 * hh], aKr[0][nt][2 * hh + 1]);
+        st_pair(p.dq + off, aQr[0][nt][2 * hh], aQr[0][nt][2 * hh + 1]);
+      }
   }
-  (void)aG;
 }
 
 // ---------------------------------------------------------------------------
@@ -632,7 +659,7 @@ int launch_bwd(const ScanParams& p, cudaStream_t st) {
       return check_launch("cudaFuncSetAttribute(scan_bwd_chunk_kernel)");
     configured = true;
   }
-  scan_bwd_state_kernel<CF><<<dim3(kVD / kBV, p.B * p.H), 256, s1, st>>>(p);
+  scan_bwd_state_kernel<CF><<<dim3(kVD / kBV, p.B * p.H), kSeqThreads, s1, st>>>(p);
   int rc = check_launch("scan_bwd_state_kernel");
   if (rc != KDN_OK) return rc;
   scan_bwd_chunk_kernel<CF><<<dim3(p.NT, p.B * p.H), 512, s2, st>>>(p);

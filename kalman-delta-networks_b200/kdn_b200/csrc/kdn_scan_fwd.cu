@@ -53,15 +53,15 @@ __device__ __forceinline__ void bind_fwd_chunk(Chunk<CF>& ch, char* base) {
 }
 
 template <class CF>
-__global__ void __launch_bounds__(256, 1) scan_fwd_kernel(ScanParams p) {
+__global__ void __launch_bounds__(kSeqThreads, 1) scan_fwd_kernel(ScanParams p) {
   using OpT = typename CF::OpT;
   using Lo = FwdLayout<CF>;
   constexpr int C = CF::C;
-  constexpr int NTW = C / 8;            // n-tiles per warp job of W0 = T Kr (C x 128)
+  constexpr int NTW = C / 16;           // n-tiles per warp job of W0 = T Kr (C x 128)
   constexpr int NJW = kKD / (8 * NTW);  // column jobs per row block
-  constexpr int NTU = C / 16;           // n-tiles per warp job of the C x 64 products
+  constexpr int NTU = C / 32;           // n-tiles per warp job of the C x 64 products
   constexpr int NJU = kBV / (8 * NTU);
-  static_assert((C / 16) * NJW == 8 && (C / 16) * NJU == 8, "8 warps");
+  static_assert((C / 16) * NJW == 16 && (C / 16) * NJU == 16, "16 warps");
   extern __shared__ __align__(128) char smem[];
   char* base = CF::F32 ? p.dbg + (size_t)(blockIdx.y * gridDim.x + blockIdx.x) * p.dbg_stride : smem;
 
@@ -82,9 +82,10 @@ __global__ void __launch_bounds__(256, 1) scan_fwd_kernel(ScanParams p) {
   const int v0 = vt * kBV;
   const bool save_tq = vt == 0 && p.Tsave;
 
-  // state slice: rows 16*warp.., all kBV columns
-  float S[1][8][4];
-  for_acc<1, 8>(16 * warp, 0, [&](int, int nt, int e, int row, int col) {
+  // state slice: 16 rows x 32 columns per warp
+  const int sm0 = 16 * (warp >> 1), sn0 = 32 * (warp & 1);
+  float S[1][4][4];
+  for_acc<1, 4>(sm0, sn0, [&](int, int nt, int e, int row, int col) {
     S[0][nt][e] = p.S0 ? p.S0[((size_t)bh * kKD + row) * kVD + v0 + col] : 0.f;
   });
   zero_upper_blocks<CF>(sQb);
@@ -134,7 +135,7 @@ __global__ void __launch_bounds__(256, 1) scan_fwd_kernel(ScanParams p) {
     zero_acc(u);
     wgemm<1, NTU, true, false>(u, sTb, CF::LDC, sv, CF::LDV, 16 * Iu, nu, 0, 16 * (Iu + 1));
     OpT* hdst = p.h ? static_cast<OpT*>(p.h) + cc * kKD * kVD : nullptr;
-    for_acc_pairs<1, 8>(S, 16 * warp, 0, [&](int, int, int, int row, int col, float x0, float x1) {
+    for_acc_pairs<1, 4>(S, sm0, sn0, [&](int, int, int, int row, int col, float x0, float x1) {
       const float f = ch.fr[row];
       st_pair(sS + row * CF::LDV + col, f * x0, f * x1);
       if (hdst) st_pair(hdst + (size_t)row * kVD + v0 + col, x0, x1);
@@ -175,16 +176,16 @@ __global__ void __launch_bounds__(256, 1) scan_fwd_kernel(ScanParams p) {
     }
     // S = Diag(2^g_L) S + Diag(fL) Kc^T delta
     {
-      float acc[1][8][4];
+      float acc[1][4][4];
       zero_acc(acc);
-      wgemm<1, 8, false, false>(acc, ch.Kc, CF::LDK, sDel, CF::LDV, 16 * warp, 0, 0, C);
-      for_acc<1, 8>(16 * warp, 0, [&](int, int nt, int e, int row, int) {
+      wgemm<1, 4, false, false>(acc, ch.Kc, CF::LDK, sDel, CF::LDV, sm0, sn0, 0, C);
+      for_acc<1, 4>(sm0, sn0, [&](int, int nt, int e, int row, int) {
         S[0][nt][e] = ch.gL[row] * S[0][nt][e] + ch.fL[row] * acc[0][nt][e];
       });
     }
   }
   if (p.ST) {
-    for_acc<1, 8>(16 * warp, 0, [&](int, int nt, int e, int row, int col) {
+    for_acc<1, 4>(sm0, sn0, [&](int, int nt, int e, int row, int col) {
       p.ST[((size_t)bh * kKD + row) * kVD + v0 + col] = S[0][nt][e];
     });
   }
@@ -209,7 +210,7 @@ int launch_fwd(const ScanParams& p, cudaStream_t st) {
     configured = true;
   }
   dim3 grid(kVD / kBV, p.B * p.H);
-  scan_fwd_kernel<CF><<<grid, 256, smem, st>>>(p);
+  scan_fwd_kernel<CF><<<grid, kSeqThreads, smem, st>>>(p);
   return check_launch("scan_fwd_kernel");
 }
 
