@@ -189,7 +189,7 @@ def per_op_times(variant, x, device, reps=5):
     else:
         from kdn_b200.diag_kdn_chunk import _gain_forward
 
-        kappa, carry = _gain_forward(x["k_gain"], x["alpha"], x["omega"], x["r"], x["prec"])
+        kappa, carry, _ = _gain_forward(x["k_gain"], x["alpha"], x["omega"], x["r"], x["prec"])
         out["gain_fwd_ms"] = time_region(
             lambda: _gain_forward(x["k_gain"], x["alpha"], x["omega"], x["r"], x["prec"]), reps, device)
         args = (N.KDN_DIAG, x["q"], x["k"], x["v"], x["g_cumsum"], kappa, D ** -0.5)

@@ -53,19 +53,26 @@ const char* kdn_last_error(void);
  * entering each token) is written by the forward when non-null and is required
  * by the backward.  p_final (fp32 [B,H], nullable) receives p_{T-1}.
  * d_initial_precision is overwritten (not accumulated).
+ * Continuation (sequence parallelism): initial_cov (fp32 [B,H], nullable)
+ * replaces p_{-1} = 1/initial_precision; the backward then takes the
+ * cotangent of p_{T-1} in d_final_cov (nullable = 0), writes dL/dp_{-1} to
+ * d_initial_cov (nullable) and gives initial_precision no gradient.
  * ------------------------------------------------------------------------ */
 size_t kdn_iso_gain_workspace_bytes(int64_t B, int64_t T, int64_t H);
 int kdn_iso_gain_fwd(const float* a, const float* omega, const float* r,
-                     const float* initial_precision, float* gain, float* p_prev,
-                     float* p_final, int64_t B, int64_t T, int64_t H,
-                     float posterior_scale, void* workspace,
-                     size_t workspace_bytes, kdn_stream_t stream);
+                     const float* initial_precision, const float* initial_cov,
+                     float* gain, float* p_prev, float* p_final, int64_t B,
+                     int64_t T, int64_t H, float posterior_scale,
+                     void* workspace, size_t workspace_bytes,
+                     kdn_stream_t stream);
 int kdn_iso_gain_bwd(const float* a, const float* omega, const float* r,
-                     const float* initial_precision, const float* dgain,
-                     const float* p_prev, float* da, float* domega, float* dr,
-                     float* d_initial_precision, int64_t B, int64_t T, int64_t H,
-                     float posterior_scale, void* workspace,
-                     size_t workspace_bytes, kdn_stream_t stream);
+                     const float* initial_precision, const float* initial_cov,
+                     const float* dgain, const float* p_prev,
+                     const float* d_final_cov, float* da, float* domega,
+                     float* dr, float* d_initial_precision, float* d_initial_cov,
+                     int64_t B, int64_t T, int64_t H, float posterior_scale,
+                     void* workspace, size_t workspace_bytes,
+                     kdn_stream_t stream);
 
 /* ------------------------------------------------------------------------ *
  * Diagonal gain scan.  Replaces _diag_kdn_gain (diag_kdn_chunk.py:2737) ->
@@ -81,14 +88,19 @@ int kdn_iso_gain_bwd(const float* a, const float* omega, const float* r,
  * backward.  p_final (fp32 [B,H,K], nullable) receives the final covariance.
  * The backward fuses the softplus VJPs: domega_raw = dL/domega *
  * sigmoid(omega_raw), dr_raw = dL/dr * sigmoid(r_raw).  K must be 64 or 128.
+ * Continuation: initial_cov (fp32 [B,H,K], nullable) replaces
+ * p_{-1} = 1/initial_precision; d_final_cov / d_initial_cov (fp32 [B,H,K],
+ * nullable) carry the covariance cotangent in and out, and
+ * initial_precision then receives no gradient.
  * ------------------------------------------------------------------------ */
 int64_t kdn_diag_gain_carry_elems(int64_t B, int64_t T, int64_t H, int64_t K);
 size_t kdn_diag_gain_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t K);
 int kdn_diag_gain_fwd(const float* k, const float* alpha, const float* omega,
                       const float* r, const float* initial_precision,
-                      float* kappa, float* carry, float* p_final, int64_t B,
-                      int64_t T, int64_t H, int64_t K, void* workspace,
-                      size_t workspace_bytes, kdn_stream_t stream);
+                      const float* initial_cov, float* kappa, float* carry,
+                      float* p_final, int64_t B, int64_t T, int64_t H, int64_t K,
+                      void* workspace, size_t workspace_bytes,
+                      kdn_stream_t stream);
 /* Allocation-free variant of kdn_diag_gain_fwd (no counterpart in the
  * reference).  For callers that must not allocate device memory at call
  * time: code running while a CUDA stream is being captured into a graph (an
@@ -100,7 +112,7 @@ int kdn_diag_gain_fwd(const float* k, const float* alpha, const float* omega,
  * array's device address (cudaGetSymbolAddress); make that first call before
  * any stream capture.  All calls share the array, so calls that overlap on
  * the GPU (different streams, no ordering) race; order them on one stream.
- * Outputs and carry are as for kdn_diag_gain_fwd. */
+ * Outputs and carry are as for kdn_diag_gain_fwd (no initial_cov). */
 int kdn_diag_gain_fwd_noalloc(const float* k, const float* alpha,
                               const float* omega, const float* r,
                               const float* initial_precision, float* kappa,
@@ -109,12 +121,14 @@ int kdn_diag_gain_fwd_noalloc(const float* k, const float* alpha,
                               kdn_stream_t stream);
 int kdn_diag_gain_bwd(const float* k, const float* alpha, const float* omega,
                       const float* r, const float* initial_precision,
-                      const void* omega_raw, const void* r_raw,
-                      const float* dkappa, const float* carry, float* dk,
+                      const float* initial_cov, const void* omega_raw,
+                      const void* r_raw, const float* dkappa,
+                      const float* carry, const float* d_final_cov, float* dk,
                       float* dalpha, void* domega_raw, void* dr_raw,
-                      float* d_initial_precision, int64_t B, int64_t T,
-                      int64_t H, int64_t K, void* workspace,
-                      size_t workspace_bytes, kdn_stream_t stream);
+                      float* d_initial_precision, float* d_initial_cov,
+                      int64_t B, int64_t T, int64_t H, int64_t K,
+                      void* workspace, size_t workspace_bytes,
+                      kdn_stream_t stream);
 
 /* ------------------------------------------------------------------------ *
  * Chunked memory scan (both variants).

@@ -68,14 +68,17 @@ _SIGNATURES = {
     "kdn_version": ([], ctypes.c_int),
     "kdn_last_error": ([], ctypes.c_char_p),
     "kdn_iso_gain_workspace_bytes": ([_I64, _I64, _I64], _SZ),
-    "kdn_iso_gain_fwd": ([_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _F, _P, _SZ, _P], ctypes.c_int),
-    "kdn_iso_gain_bwd": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _F, _P, _SZ, _P], ctypes.c_int),
+    "kdn_iso_gain_fwd": ([_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _F, _P, _SZ, _P], ctypes.c_int),
+    "kdn_iso_gain_bwd": (
+        [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _F, _P, _SZ, _P],
+        ctypes.c_int,
+    ),
     "kdn_diag_gain_carry_elems": ([_I64, _I64, _I64, _I64], _I64),
     "kdn_diag_gain_workspace_bytes": ([_I64, _I64, _I64, _I64], _SZ),
-    "kdn_diag_gain_fwd": ([_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _SZ, _P], ctypes.c_int),
+    "kdn_diag_gain_fwd": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _SZ, _P], ctypes.c_int),
     "kdn_diag_gain_fwd_noalloc": ([_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P], ctypes.c_int),
     "kdn_diag_gain_bwd": (
-        [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _SZ, _P],
+        [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _SZ, _P],
         ctypes.c_int,
     ),
     "kdn_scan_saved_bytes": ([ctypes.POINTER(KdnScanArgs)], _SZ),

@@ -104,6 +104,7 @@ __global__ void __launch_bounds__(kIsoThreads) iso_gain_fwd_kernel(const float* 
                                                                    const float* __restrict__ omega,
                                                                    const float* __restrict__ r,
                                                                    const float* __restrict__ init_prec,
+                                                                   const float* __restrict__ init_cov,
                                                                    float* __restrict__ gain, float* __restrict__ p_prev,
                                                                    float* __restrict__ p_final, int T, int H, float s) {
   const int bh = blockIdx.x, b = bh / H, h = bh - b * H;
@@ -117,7 +118,7 @@ __global__ void __launch_bounds__(kIsoThreads) iso_gain_fwd_kernel(const float* 
     m = mob_mul(Mob{rt * at, rt * wt, s * at, rt + s * wt}, m);
   }
   const Mob pre = block_exclusive_mob(m);
-  const float p0 = 1.f / init_prec[h];
+  const float p0 = init_cov ? init_cov[bh] : 1.f / init_prec[h];
   float p = mob_apply(pre, p0);
   for (int t = t0; t < t1; ++t) {
     const size_t off = base + (size_t)t * H;
@@ -137,6 +138,7 @@ __global__ void __launch_bounds__(kIsoThreads) iso_gain_fwd_kernel(const float* 
 __global__ void __launch_bounds__(kIsoThreads) iso_gain_bwd_kernel(
     const float* __restrict__ a, const float* __restrict__ omega, const float* __restrict__ r,
     const float* __restrict__ init_prec, const float* __restrict__ dgain, const float* __restrict__ p_prev,
+    const float* __restrict__ d_final_cov, const bool has_init_cov, float* __restrict__ d_init_cov,
     float* __restrict__ da, float* __restrict__ domega, float* __restrict__ dr, float* __restrict__ dinit, int T,
     int H, float s) {
   const int bh = blockIdx.x, b = bh / H, h = bh - b * H;
@@ -155,7 +157,8 @@ __global__ void __launch_bounds__(kIsoThreads) iso_gain_bwd_kernel(
     f = aff_after(Aff{at * pr * pr, at * dbt * rt * gi * gi}, f);
   }
   const Aff suf = block_exclusive_suffix_aff(f);
-  float lam = suf.B;
+  // lambda after the last token: the cotangent of the final covariance (0 without one)
+  float lam = suf.A * (d_final_cov ? d_final_cov[bh] : 0.f) + suf.B;
   for (int t = t1 - 1; t >= t0; --t) {
     const size_t off = base + (size_t)t * H;
     const float at = a[off], wt = omega[off], rt = r[off], dbt = dgain[off], pp = p_prev[off];
@@ -177,8 +180,11 @@ __global__ void __launch_bounds__(kIsoThreads) iso_gain_bwd_kernel(
     lam = at * zbar;
   }
   if (threadIdx.x == 0) {
-    const float ip = init_prec[h];
-    atomicAdd(dinit + h, -lam / (ip * ip));
+    if (d_init_cov) d_init_cov[bh] = lam;  // d L / d p_{-1}
+    if (!has_init_cov) {
+      const float ip = init_prec[h];
+      atomicAdd(dinit + h, -lam / (ip * ip));
+    }
   }
 }
 
@@ -236,10 +242,11 @@ __global__ void __launch_bounds__(K) diag_gain_map_kernel(const float* __restric
 template <int K>
 __global__ void __launch_bounds__(K) diag_gain_carry_kernel(const float4* __restrict__ maps,
                                                             const float* __restrict__ init_prec,
+                                                            const float* __restrict__ init_cov,
                                                             float* __restrict__ carry, float* __restrict__ p_final,
                                                             int H, int nseg) {
   const int bh = blockIdx.x, h = bh % H, c = threadIdx.x;
-  float p = 1.f / init_prec[h];
+  float p = init_cov ? init_cov[(size_t)bh * K + c] : 1.f / init_prec[h];
   for (int s = 0; s < nseg; ++s) {
     carry[((size_t)bh * nseg + s) * K + c] = p;
     const float4 m = maps[((size_t)bh * nseg + s) * K + c];
@@ -348,9 +355,10 @@ __global__ void __launch_bounds__(K) diag_gain_bwd_map_kernel(
 
 template <int K>
 __global__ void __launch_bounds__(K) diag_gain_bwd_carry_kernel(const float2* __restrict__ maps,
+                                                                const float* __restrict__ d_final_cov,
                                                                 float* __restrict__ lam_carry, int nseg) {
   const int bh = blockIdx.x, c = threadIdx.x;
-  float lam = 0.f;
+  float lam = d_final_cov ? d_final_cov[(size_t)bh * K + c] : 0.f;
   for (int s = nseg - 1; s >= 0; --s) {
     lam_carry[((size_t)bh * nseg + s) * K + c] = lam;
     const float2 m = maps[((size_t)bh * nseg + s) * K + c];
@@ -367,7 +375,7 @@ __global__ void __launch_bounds__(K) diag_gain_bwd_emit_kernel(
     const bf16* __restrict__ r_raw, const float* __restrict__ dkappa, const float* __restrict__ carry,
     const float* __restrict__ lam_carry, const float2* __restrict__ dg_tok, float* __restrict__ dk_out,
     float* __restrict__ dalpha, bf16* __restrict__ domega_raw, bf16* __restrict__ dr_raw,
-    float* __restrict__ dinit, int T, int H, int nseg) {
+    float* __restrict__ dinit, float* __restrict__ d_init_cov, int T, int H, int nseg) {
   __shared__ float red[K];
   __shared__ float tok[32];
   __shared__ float pprev_s[kDiagSeg][K];
@@ -427,6 +435,7 @@ __global__ void __launch_bounds__(K) diag_gain_bwd_emit_kernel(
     }
     __syncthreads();
   }
+  if (seg == 0 && d_init_cov) d_init_cov[(size_t)bh * K + c] = lam;  // d L / d p_{-1}
   if (seg == 0 && dinit) {
     // p_{-1} = 1/mu, so d mu = -sum_c lambda_{-1,c} p_{-1,c}^2
     const float p0 = pprev_s[0][c];
@@ -478,19 +487,20 @@ extern "C" {
 
 size_t kdn_iso_gain_workspace_bytes(int64_t, int64_t, int64_t) { return 0; }
 
-int kdn_iso_gain_fwd(const float* a, const float* omega, const float* r, const float* init_prec, float* gain,
-                     float* p_prev, float* p_final, int64_t B, int64_t T, int64_t H, float s, void*, size_t,
-                     kdn_stream_t stream) {
+int kdn_iso_gain_fwd(const float* a, const float* omega, const float* r, const float* init_prec,
+                     const float* init_cov, float* gain, float* p_prev, float* p_final, int64_t B, int64_t T,
+                     int64_t H, float s, void*, size_t, kdn_stream_t stream) {
   if (B <= 0 || H <= 0 || T < 0 || !a || !omega || !r || !init_prec || !gain)
     return set_error(KDN_ERR_INVALID, "kdn_iso_gain_fwd: invalid arguments");
   if (T > INT32_MAX || B * H > INT32_MAX) return set_error(KDN_ERR_INVALID, "kdn_iso_gain_fwd: size too large");
-  iso_gain_fwd_kernel<<<(unsigned)(B * H), kIsoThreads, 0, (cudaStream_t)stream>>>(a, omega, r, init_prec, gain,
-                                                                                   p_prev, p_final, (int)T, (int)H, s);
+  iso_gain_fwd_kernel<<<(unsigned)(B * H), kIsoThreads, 0, (cudaStream_t)stream>>>(
+      a, omega, r, init_prec, init_cov, gain, p_prev, p_final, (int)T, (int)H, s);
   return check_launch("iso_gain_fwd_kernel");
 }
 
-int kdn_iso_gain_bwd(const float* a, const float* omega, const float* r, const float* init_prec, const float* dgain,
-                     const float* p_prev, float* da, float* domega, float* dr, float* dinit, int64_t B, int64_t T,
+int kdn_iso_gain_bwd(const float* a, const float* omega, const float* r, const float* init_prec,
+                     const float* init_cov, const float* dgain, const float* p_prev, const float* d_final_cov,
+                     float* da, float* domega, float* dr, float* dinit, float* d_init_cov, int64_t B, int64_t T,
                      int64_t H, float s, void*, size_t, kdn_stream_t stream) {
   if (B <= 0 || H <= 0 || T < 0 || !a || !omega || !r || !init_prec || !dgain || !da || !domega || !dr || !dinit ||
       (T > 0 && !p_prev))
@@ -498,9 +508,9 @@ int kdn_iso_gain_bwd(const float* a, const float* omega, const float* r, const f
   if (T > INT32_MAX || B * H > INT32_MAX) return set_error(KDN_ERR_INVALID, "kdn_iso_gain_bwd: size too large");
   cudaStream_t st = (cudaStream_t)stream;
   if (cudaMemsetAsync(dinit, 0, sizeof(float) * H, st) != cudaSuccess) return check_launch("memset d_initial_precision");
-  if (T == 0) return KDN_OK;
-  iso_gain_bwd_kernel<<<(unsigned)(B * H), kIsoThreads, 0, st>>>(a, omega, r, init_prec, dgain, p_prev, da, domega,
-                                                                 dr, dinit, (int)T, (int)H, s);
+  iso_gain_bwd_kernel<<<(unsigned)(B * H), kIsoThreads, 0, st>>>(a, omega, r, init_prec, dgain, p_prev, d_final_cov,
+                                                                 init_cov != nullptr, d_init_cov, da, domega, dr,
+                                                                 dinit, (int)T, (int)H, s);
   return check_launch("iso_gain_bwd_kernel");
 }
 
@@ -518,8 +528,8 @@ size_t kdn_diag_gain_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t K)
 }
 
 int kdn_diag_gain_fwd(const float* k, const float* alpha, const float* omega, const float* r, const float* init_prec,
-                      float* kappa, float* carry, float* p_final, int64_t B, int64_t T, int64_t H, int64_t K,
-                      void* ws, size_t ws_bytes, kdn_stream_t stream) {
+                      const float* init_cov, float* kappa, float* carry, float* p_final, int64_t B, int64_t T,
+                      int64_t H, int64_t K, void* ws, size_t ws_bytes, kdn_stream_t stream) {
   if (B <= 0 || H <= 0 || T <= 0 || !k || !alpha || !omega || !r || !init_prec || !kappa || !carry)
     return set_error(KDN_ERR_INVALID, "kdn_diag_gain_fwd: invalid arguments");
   if (K != 64 && K != 128) return set_error(KDN_ERR_INVALID, "kdn_diag_gain_fwd: K must be 64 or 128, got %lld", (long long)K);
@@ -532,11 +542,13 @@ int kdn_diag_gain_fwd(const float* k, const float* alpha, const float* omega, co
   dim3 grid(nseg, (unsigned)(B * H));
   if (K == 128) {
     diag_gain_map_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, maps, (int)T, (int)H, nseg);
-    diag_gain_carry_kernel<128><<<(unsigned)(B * H), 128, 0, st>>>(maps, init_prec, carry, p_final, (int)H, nseg);
+    diag_gain_carry_kernel<128><<<(unsigned)(B * H), 128, 0, st>>>(maps, init_prec, init_cov, carry, p_final, (int)H,
+                                                                   nseg);
     diag_gain_emit_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, carry, kappa, (int)T, (int)H, nseg);
   } else {
     diag_gain_map_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, maps, (int)T, (int)H, nseg);
-    diag_gain_carry_kernel<64><<<(unsigned)(B * H), 64, 0, st>>>(maps, init_prec, carry, p_final, (int)H, nseg);
+    diag_gain_carry_kernel<64><<<(unsigned)(B * H), 64, 0, st>>>(maps, init_prec, init_cov, carry, p_final, (int)H,
+                                                                 nseg);
     diag_gain_emit_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, carry, kappa, (int)T, (int)H, nseg);
   }
   return check_launch("diag_gain_fwd kernels");
@@ -566,20 +578,23 @@ int kdn_diag_gain_fwd_noalloc(const float* k, const float* alpha, const float* o
   dim3 grid((unsigned)nseg, (unsigned)(B * H));
   if (K == 128) {
     diag_gain_map_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, maps, (int)T, (int)H, (int)nseg);
-    diag_gain_carry_kernel<128><<<(unsigned)(B * H), 128, 0, st>>>(maps, init_prec, carry, p_final, (int)H, (int)nseg);
+    diag_gain_carry_kernel<128><<<(unsigned)(B * H), 128, 0, st>>>(maps, init_prec, nullptr, carry, p_final, (int)H,
+                                                                   (int)nseg);
     diag_gain_emit_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, carry, kappa, (int)T, (int)H, (int)nseg);
   } else {
     diag_gain_map_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, maps, (int)T, (int)H, (int)nseg);
-    diag_gain_carry_kernel<64><<<(unsigned)(B * H), 64, 0, st>>>(maps, init_prec, carry, p_final, (int)H, (int)nseg);
+    diag_gain_carry_kernel<64><<<(unsigned)(B * H), 64, 0, st>>>(maps, init_prec, nullptr, carry, p_final, (int)H,
+                                                                 (int)nseg);
     diag_gain_emit_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, carry, kappa, (int)T, (int)H, (int)nseg);
   }
   return check_launch("diag_gain_fwd_noalloc kernels");
 }
 
 int kdn_diag_gain_bwd(const float* k, const float* alpha, const float* omega, const float* r, const float* init_prec,
-                      const void* omega_raw, const void* r_raw, const float* dkappa, const float* carry, float* dk,
-                      float* dalpha, void* domega_raw, void* dr_raw, float* dinit, int64_t B, int64_t T, int64_t H,
-                      int64_t K, void* ws, size_t ws_bytes, kdn_stream_t stream) {
+                      const float* init_cov, const void* omega_raw, const void* r_raw, const float* dkappa,
+                      const float* carry, const float* d_final_cov, float* dk, float* dalpha, void* domega_raw,
+                      void* dr_raw, float* dinit, float* d_init_cov, int64_t B, int64_t T, int64_t H, int64_t K,
+                      void* ws, size_t ws_bytes, kdn_stream_t stream) {
   if (B <= 0 || H <= 0 || T <= 0 || !k || !alpha || !omega || !r || !init_prec || !omega_raw || !r_raw || !dkappa ||
       !carry || !dk || !dalpha || !domega_raw || !dr_raw)
     return set_error(KDN_ERR_INVALID, "kdn_diag_gain_bwd: invalid arguments");
@@ -597,23 +612,26 @@ int kdn_diag_gain_bwd(const float* k, const float* alpha, const float* omega, co
   float2* dg_tok = reinterpret_cast<float2*>(w);
   if (dinit && cudaMemsetAsync(dinit, 0, sizeof(float) * H, st) != cudaSuccess)
     return check_launch("memset d_initial_precision");
+  float* dmu = init_cov ? nullptr : dinit;  // with a carried-in covariance the prior gets no gradient here
   dim3 grid(nseg, (unsigned)(B * H));
   const bf16* wr = static_cast<const bf16*>(omega_raw);
   const bf16* rr = static_cast<const bf16*>(r_raw);
   if (K == 128) {
     diag_gain_bwd_map_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, dkappa, carry, maps, dg_tok, (int)T,
                                                         (int)H, nseg);
-    diag_gain_bwd_carry_kernel<128><<<(unsigned)(B * H), 128, 0, st>>>(maps, lam, nseg);
+    diag_gain_bwd_carry_kernel<128><<<(unsigned)(B * H), 128, 0, st>>>(maps, d_final_cov, lam, nseg);
     diag_gain_bwd_emit_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, init_prec, wr, rr, dkappa, carry, lam,
                                                          dg_tok, dk, dalpha, static_cast<bf16*>(domega_raw),
-                                                         static_cast<bf16*>(dr_raw), dinit, (int)T, (int)H, nseg);
+                                                         static_cast<bf16*>(dr_raw), dmu, d_init_cov, (int)T, (int)H,
+                                                         nseg);
   } else {
     diag_gain_bwd_map_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, dkappa, carry, maps, dg_tok, (int)T, (int)H,
                                                       nseg);
-    diag_gain_bwd_carry_kernel<64><<<(unsigned)(B * H), 64, 0, st>>>(maps, lam, nseg);
+    diag_gain_bwd_carry_kernel<64><<<(unsigned)(B * H), 64, 0, st>>>(maps, d_final_cov, lam, nseg);
     diag_gain_bwd_emit_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, init_prec, wr, rr, dkappa, carry, lam,
                                                        dg_tok, dk, dalpha, static_cast<bf16*>(domega_raw),
-                                                       static_cast<bf16*>(dr_raw), dinit, (int)T, (int)H, nseg);
+                                                       static_cast<bf16*>(dr_raw), dmu, d_init_cov, (int)T, (int)H,
+                                                       nseg);
   }
   return check_launch("diag_gain_bwd kernels");
 }

@@ -20,24 +20,29 @@ _VECTOR_DTYPE = torch.bfloat16
 _STATE_DTYPE = torch.float32
 
 
-def _gain_forward(k, alpha, omega, r, initial_precision):
+def _gain_forward(k, alpha, omega, r, initial_precision, initial_cov=None, want_final=False):
+    """Forward per-channel covariance scan; optional carried-in covariance
+    [B,H,K] and final covariance out (sequence parallelism)."""
     B, T, H, K = k.shape
     N.require_cuda(k)
     lib = N.load_library()
     kappa = torch.empty_like(k, dtype=_STATE_DTYPE)
     carry = torch.empty(lib.kdn_diag_gain_carry_elems(B, T, H, K), dtype=torch.float32, device=k.device)
+    p_final = torch.empty((B, H, K), dtype=torch.float32, device=k.device) if want_final else None
     ws = N.byte_buffer(lib.kdn_diag_gain_workspace_bytes(B, T, H, K), k.device)
     N.check(
         lib.kdn_diag_gain_fwd(
             k.data_ptr(), alpha.data_ptr(), omega.data_ptr(), r.data_ptr(), initial_precision.data_ptr(),
-            kappa.data_ptr(), carry.data_ptr(), None, B, T, H, K, ws.data_ptr(), ws.numel(), N.stream_of(k),
+            N.ptr(initial_cov), kappa.data_ptr(), carry.data_ptr(), N.ptr(p_final), B, T, H, K, ws.data_ptr(),
+            ws.numel(), N.stream_of(k),
         ),
         "kdn_diag_gain_fwd",
     )
-    return kappa, carry
+    return kappa, carry, p_final
 
 
-def _gain_backward(k, alpha, omega, r, initial_precision, omega_raw, r_raw, dkappa, carry, need_initial):
+def _gain_backward(k, alpha, omega, r, initial_precision, omega_raw, r_raw, dkappa, carry, need_initial,
+                   initial_cov=None, d_final_cov=None, want_d_initial=False):
     B, T, H, K = k.shape
     lib = N.load_library()
     dkappa = torch.zeros_like(k) if dkappa is None else dkappa.float().contiguous()
@@ -46,23 +51,25 @@ def _gain_backward(k, alpha, omega, r, initial_precision, omega_raw, r_raw, dkap
     domega_raw = torch.empty_like(omega_raw)
     dr_raw = torch.empty_like(r_raw)
     dinit = torch.empty((H,), dtype=_STATE_DTYPE, device=k.device) if need_initial else None
+    dic = torch.empty((B, H, K), dtype=_STATE_DTYPE, device=k.device) if want_d_initial else None
+    dfc = None if d_final_cov is None else d_final_cov.float().contiguous()
     ws = N.byte_buffer(lib.kdn_diag_gain_workspace_bytes(B, T, H, K), k.device)
     N.check(
         lib.kdn_diag_gain_bwd(
             k.data_ptr(), alpha.data_ptr(), omega.data_ptr(), r.data_ptr(), initial_precision.data_ptr(),
-            omega_raw.data_ptr(), r_raw.data_ptr(), dkappa.data_ptr(), carry.data_ptr(), dk.data_ptr(),
-            dalpha.data_ptr(), domega_raw.data_ptr(), dr_raw.data_ptr(), N.ptr(dinit), B, T, H, K,
-            ws.data_ptr(), ws.numel(), N.stream_of(k),
+            N.ptr(initial_cov), omega_raw.data_ptr(), r_raw.data_ptr(), dkappa.data_ptr(), carry.data_ptr(),
+            N.ptr(dfc), dk.data_ptr(), dalpha.data_ptr(), domega_raw.data_ptr(), dr_raw.data_ptr(), N.ptr(dinit),
+            N.ptr(dic), B, T, H, K, ws.data_ptr(), ws.numel(), N.stream_of(k),
         ),
         "kdn_diag_gain_bwd",
     )
-    return dk, dalpha, domega_raw, dr_raw, dinit
+    return dk, dalpha, domega_raw, dr_raw, dinit, dic
 
 
 class _DiagKdnGainFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, k, alpha, omega, r, initial_precision, omega_raw, r_raw):
-        kappa, carry = _gain_forward(k, alpha, omega, r, initial_precision)
+        kappa, carry, _ = _gain_forward(k, alpha, omega, r, initial_precision)
         ctx.save_for_backward(k, alpha, omega, r, initial_precision, omega_raw, r_raw, carry)
         ctx.set_materialize_grads(False)
         return kappa
@@ -72,7 +79,7 @@ class _DiagKdnGainFunction(torch.autograd.Function):
     def backward(ctx, dkappa):
         k, alpha, omega, r, initial_precision, omega_raw, r_raw, carry = ctx.saved_tensors
         needs = ctx.needs_input_grad
-        dk, dalpha, domega_raw, dr_raw, dinit = _gain_backward(
+        dk, dalpha, domega_raw, dr_raw, dinit, _ = _gain_backward(
             k, alpha, omega, r, initial_precision, omega_raw, r_raw, dkappa, carry, need_initial=needs[4]
         )
         return (

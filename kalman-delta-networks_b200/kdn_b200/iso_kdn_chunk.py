@@ -32,46 +32,54 @@ def _require_same_cuda_device(a: torch.Tensor, *named_tensors: tuple[str, torch.
     return device
 
 
-def _iso_gain_forward(a, omega, r, initial_precision, *, out_dtype, save_state, posterior_scale):
+def _iso_gain_forward(a, omega, r, initial_precision, *, out_dtype, save_state, posterior_scale,
+                      initial_cov=None, want_final=False):
+    """Forward scalar covariance scan; optional carried-in covariance [B,H] and
+    final covariance out (sequence parallelism)."""
     B, T, H = a.shape
     N.require_cuda(a)
     lib = N.load_library()
     a32, w32, r32, p32 = (x.float().contiguous() for x in (a, omega, r, initial_precision))
+    c32 = None if initial_cov is None else initial_cov.float().contiguous()
     gain = torch.empty((B, T, H), dtype=torch.float32, device=a.device)
     p_prev = torch.empty((B, T, H), dtype=torch.float32, device=a.device) if save_state else None
+    p_final = torch.empty((B, H), dtype=torch.float32, device=a.device) if want_final else None
     N.check(
         lib.kdn_iso_gain_fwd(
-            a32.data_ptr(), w32.data_ptr(), r32.data_ptr(), p32.data_ptr(), gain.data_ptr(), N.ptr(p_prev), None,
-            B, T, H, float(posterior_scale), None, 0, N.stream_of(a),
+            a32.data_ptr(), w32.data_ptr(), r32.data_ptr(), p32.data_ptr(), N.ptr(c32), gain.data_ptr(),
+            N.ptr(p_prev), N.ptr(p_final), B, T, H, float(posterior_scale), None, 0, N.stream_of(a),
         ),
         "kdn_iso_gain_fwd",
     )
-    return gain.to(out_dtype), p_prev
+    return gain.to(out_dtype), p_prev, p_final
 
 
-def _iso_gain_backward(a, omega, r, initial_precision, dgain, p_prev, *, posterior_scale):
+def _iso_gain_backward(a, omega, r, initial_precision, dgain, p_prev, *, posterior_scale, initial_cov=None,
+                       d_final_cov=None, want_d_initial=False):
     B, T, H = a.shape
     lib = N.load_library()
     a32, w32, r32, p32, d32 = (x.float().contiguous() for x in (a, omega, r, initial_precision, dgain))
+    dfc = None if d_final_cov is None else d_final_cov.float().contiguous()
     da = torch.empty((B, T, H), dtype=torch.float32, device=a.device)
     domega = torch.empty_like(da)
     dr = torch.empty_like(da)
     dinit = torch.empty((H,), dtype=torch.float32, device=a.device)
+    dic = torch.empty((B, H), dtype=torch.float32, device=a.device) if want_d_initial else None
     N.check(
         lib.kdn_iso_gain_bwd(
-            a32.data_ptr(), w32.data_ptr(), r32.data_ptr(), p32.data_ptr(), d32.data_ptr(), p_prev.data_ptr(),
-            da.data_ptr(), domega.data_ptr(), dr.data_ptr(), dinit.data_ptr(), B, T, H, float(posterior_scale),
-            None, 0, N.stream_of(a),
+            a32.data_ptr(), w32.data_ptr(), r32.data_ptr(), p32.data_ptr(), N.ptr(initial_cov), d32.data_ptr(),
+            p_prev.data_ptr(), N.ptr(dfc), da.data_ptr(), domega.data_ptr(), dr.data_ptr(), dinit.data_ptr(),
+            N.ptr(dic), B, T, H, float(posterior_scale), None, 0, N.stream_of(a),
         ),
         "kdn_iso_gain_bwd",
     )
-    return da.to(a.dtype), domega.to(omega.dtype), dr.to(r.dtype), dinit.to(initial_precision.dtype)
+    return da.to(a.dtype), domega.to(omega.dtype), dr.to(r.dtype), dinit.to(initial_precision.dtype), dic
 
 
 class _IsoKDNGainFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, a, omega, r, initial_precision, out_dtype, posterior_scale, needs_backward):
-        gain, p_prev = _iso_gain_forward(
+        gain, p_prev, _ = _iso_gain_forward(
             a, omega, r, initial_precision, out_dtype=out_dtype, save_state=needs_backward,
             posterior_scale=posterior_scale,
         )
@@ -88,7 +96,7 @@ class _IsoKDNGainFunction(torch.autograd.Function):
         if not ctx.has_saved_state:
             raise RuntimeError("Isotropic KDN gain backward called after a no-save forward")
         a, omega, r, initial_precision, p_prev = ctx.saved_tensors
-        da, domega, dr, dinit = _iso_gain_backward(
+        da, domega, dr, dinit, _ = _iso_gain_backward(
             a, omega, r, initial_precision, dgain, p_prev, posterior_scale=ctx.posterior_scale
         )
         needs = ctx.needs_input_grad

@@ -66,9 +66,9 @@ def test_invalid_arguments_are_rejected_without_launch(lib):
     rc = lib.kdn_scan_fwd(ctypes.byref(a), None)
     assert rc == -1
     assert b"K and V must be 128" in lib.kdn_last_error()
-    rc = lib.kdn_iso_gain_fwd(None, None, None, None, None, None, None, 1, 1, 1, 1.0, None, 0, None)
+    rc = lib.kdn_iso_gain_fwd(None, None, None, None, None, None, None, None, 1, 1, 1, 1.0, None, 0, None)
     assert rc == -1
-    rc = lib.kdn_diag_gain_fwd(None, None, None, None, None, None, None, None, 1, 8, 1, 96, None, 0, None)
+    rc = lib.kdn_diag_gain_fwd(None, None, None, None, None, None, None, None, None, 1, 8, 1, 96, None, 0, None)
     assert rc == -1
 
 

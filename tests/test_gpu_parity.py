@@ -170,3 +170,99 @@ def test_diag_scan(precision, B, T, H, decay):
     o, grads = run_diag(d, d["dO"], kappa, scale)
     tol, ftol = TOL[precision]
     check(o, grads, ref, ("q", "k", "kappa", "v", "g_cumsum"), tol, ftol)
+
+
+# ----------------------------------------------------------------------------- continuation (sequence parallelism)
+
+
+def _iso_full_reference(d, prec):
+    names = ("q", "k", "v", "g_cumsum", "a", "omega", "r")
+    L = {n: d[n].double().clone().requires_grad_(True) for n in names}
+    P = prec.double().clone().requires_grad_(True)
+    beta, _, _ = oracle.iso_gain(L["a"], L["omega"], L["r"], P, 1.0)
+    qh, kh = oracle.l2norm(L["q"]), oracle.l2norm(L["k"])
+    alpha = oracle.alpha_from_g_cumsum(L["g_cumsum"] * oracle.LN2, 64)
+    S0 = torch.zeros(qh.shape[0], qh.shape[2], 128, 128, dtype=torch.float64)
+    o, _ = oracle.memory_recurrence(qh, kh, L["v"], alpha, beta[..., None] * kh, S0, 128 ** -0.5)
+    (o * d["dO"].double()).sum().backward()
+    ref = {"o": o.detach(), "dprec": P.grad}
+    ref.update({"d" + n: L[n].grad for n in names})
+    return ref
+
+
+@pytest.mark.parametrize("precision", ["fp32", "bf16"], indirect=True)
+def test_iso_segments_with_carried_state(precision):
+    """Three segments chained through (S, p) reproduce one full-sequence call."""
+    from kdn_b200.sequence_parallel import iso_segment
+
+    d = oracle.make_iso_inputs(1, 256, 2, seed=21)
+    prec = torch.tensor([1.0, 0.7])
+    ref = _iso_full_reference(d, prec)
+    names = ("q", "k", "v", "g_cumsum", "a", "omega", "r")
+    L = {n: d[n].to(DEV).requires_grad_(True) for n in names}
+    P = prec.to(DEV).requires_grad_(True)
+    outs, S, p = [], None, None
+    for s0, s1 in ((0, 128), (128, 192), (192, 256)):
+        seg = [L[n][:, s0:s1] for n in names]
+        o, S, p = iso_segment(*seg, P, S, p, head_dim=128)
+        outs.append(o)
+    o = torch.cat(outs, 1)
+    o.backward(d["dO"].to(DEV))
+    grads = {n: L[n].grad for n in names}
+    grads["prec"] = P.grad
+    tol, ftol = TOL[precision]
+    check(o, grads, ref, names + ("prec",), tol, ftol)
+
+
+@pytest.mark.parametrize("precision", ["fp32", "bf16"], indirect=True)
+def test_diag_segments_with_carried_state(precision):
+    from kdn_b200.sequence_parallel import diag_segment
+
+    d = oracle.make_diag_inputs(1, 160, 2, seed=22)
+    d["dO"] = d["dO"].bfloat16().float()
+    prec = torch.tensor([1.0, 0.6])
+    names = ("q", "k", "v", "g_cumsum", "k_gain")
+    # reference: the full-sequence oracle (gain with alpha from g, then the memory scan)
+    Lr = {n: d[n].double().clone().requires_grad_(True) for n in names}
+    Pr = prec.double().clone().requires_grad_(True)
+    alpha_r = oracle.alpha_from_g_cumsum(Lr["g_cumsum"] * oracle.LN2, 32)
+    kappa_r, _ = oracle.diag_gain(Lr["k_gain"], alpha_r, d["omega"].double(), d["r"].double(), Pr)
+    S0 = torch.zeros(1, 2, 128, 128, dtype=torch.float64)
+    o_r, _ = oracle.memory_recurrence(Lr["q"], Lr["k"], Lr["v"], alpha_r, kappa_r, S0, 128 ** -0.5)
+    (o_r * d["dO"].double()).sum().backward()
+    ref = {"o": o_r.detach(), "dprec": Pr.grad, **{"d" + n: Lr[n].grad for n in names}}
+    # ours: the gain takes alpha from the same g so both paths share it
+    L = {n: d[n].to(DEV).requires_grad_(True) for n in names}
+    P = prec.to(DEV).requires_grad_(True)
+    alpha = oracle.alpha_from_g_cumsum(d["g_cumsum"].double() * oracle.LN2, 32).float().to(DEV)
+    omega, r, wr, rr = (d[n].to(DEV) for n in ("omega", "r", "omega_raw", "r_raw"))
+    outs, S, p = [], None, None
+    for s0, s1 in ((0, 64), (64, 96), (96, 160)):
+        o, S, p = diag_segment(L["q"][:, s0:s1], L["k"][:, s0:s1], L["v"][:, s0:s1], L["g_cumsum"][:, s0:s1],
+                               L["k_gain"][:, s0:s1].contiguous(), alpha[:, s0:s1].contiguous(),
+                               omega[:, s0:s1].contiguous(), r[:, s0:s1].contiguous(), P,
+                               wr[:, s0:s1].contiguous(), rr[:, s0:s1].contiguous(), S, p)
+        outs.append(o)
+    o = torch.cat(outs, 1)
+    o.backward(d["dO"].to(DEV))
+    grads = {n: L[n].grad for n in names}
+    grads["prec"] = P.grad
+    tol, ftol = TOL[precision]
+    # the memory scan's gate cotangent has no reference here (alpha enters the gain separately)
+    check(o, grads, ref, ("q", "k", "v", "k_gain", "prec"), tol, ftol)
+
+
+def test_sp_nccl_two_gpus(tmp_path):
+    """Sequence parallelism over NCCL between two GPUs (skipped on one GPU)."""
+    import subprocess
+    import sys
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    here = os.path.dirname(os.path.abspath(__file__))
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", "--master-port=29533", os.path.join(here, "sp_nccl_worker.py"), str(tmp_path)]
+    res = subprocess.run(cmd, capture_output=True, text=True, timeout=600,
+                         env={**os.environ, "NCCL_NVLS_ENABLE": "0"})
+    assert res.returncode == 0, res.stdout[-2000:] + res.stderr[-4000:]
+    assert "sp nccl ok" in res.stdout

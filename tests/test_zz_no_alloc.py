@@ -27,12 +27,13 @@ def _call(lib, fn, args, B, T, H, K, workspace):
     carry = torch.empty(lib.kdn_diag_gain_carry_elems(B, T, H, K), device="cuda")
     p_final = torch.empty(B, H, K, device="cuda")
     stream = torch.cuda.current_stream().cuda_stream
-    ptrs = [t.data_ptr() for t in (k, alpha, omega, r, prec, kappa, carry, p_final)]
+    outs = [t.data_ptr() for t in (kappa, carry, p_final)]
+    ins = [t.data_ptr() for t in (k, alpha, omega, r, prec)]
     if workspace:
         ws = torch.empty(lib.kdn_diag_gain_workspace_bytes(B, T, H, K), dtype=torch.uint8, device="cuda")
-        rc = fn(*ptrs, B, T, H, K, ws.data_ptr(), ws.numel(), stream)
+        rc = fn(*ins, None, *outs, B, T, H, K, ws.data_ptr(), ws.numel(), stream)
     else:
-        rc = fn(*ptrs, B, T, H, K, stream)
+        rc = fn(*ins, *outs, B, T, H, K, stream)
     assert rc == 0, lib.kdn_last_error()
     torch.cuda.synchronize()
     return kappa, carry, p_final
