@@ -187,6 +187,8 @@ def _iso_full_reference(d, prec):
     (o * d["dO"].double()).sum().backward()
     ref = {"o": o.detach(), "dprec": P.grad}
     ref.update({"d" + n: L[n].grad for n in names})
+    # the operator's gate cotangent is taken in natural-log coordinates, G = ln2 * g
+    ref["dg"] = ref.pop("dg_cumsum") / oracle.LN2
     return ref
 
 
