@@ -61,10 +61,10 @@ struct ScanParams {
   const float* S0;
   void* o;
   float* ST;
-  void* Tsave;  // [BH][NT][C][C] OpT, the triangular solve of each chunk
-  void* Qsave;  // [BH][NT][C][C] OpT, the query-key scores of each chunk
-  void* h;       // [BH][NT][KD][VD] OpT, chunk-start states
-  void* dh;      // [BH][NT][KD][VD] OpT, chunk-end state adjoints
+  void* rec;  // [BH][NT] chunk records (Rec<CF>): Qr, Kc, W0, T, Q, gate factors
+  void* h;    // [BH][NT][KD/BV][KD][LDV] OpT, chunk-start states scaled by fr
+  void* dh;   // [BH][NT][KD/BV][KD][LDV] OpT, chunk-end state adjoints scaled by fL
+  int* status;  // bounded waits that gave up set this word to 1
   const void* dO;
   const float* dST;
   float* dS0;
@@ -80,16 +80,46 @@ struct ScanParams {
   float scale;
 };
 
-// Per-chunk views of the staging buffers.
+__host__ __device__ constexpr size_t A128(size_t x) { return align_up(x, 128); }
+__host__ __device__ constexpr size_t cmax(size_t a, size_t b) { return a > b ? a : b; }
+
+// Per-chunk record: written once by the chunk-parallel pass, read by the
+// sequential passes (and T, Q by the chunk-parallel backward).  Rows are
+// padded exactly like the shared-memory operands, so each block (or the
+// whole record) moves with one bulk copy.
+//   Qr, Kc, W0 = T Kr  [C][LDK] OpT;  T, Q [C][LDC] OpT;  fr, fL, 2^g_L [3][KD] fp32
+template <class CF>
+struct Rec {
+  static constexpr size_t sz = sizeof(typename CF::OpT);
+  static constexpr int C = CF::C;
+  static constexpr size_t Qr = 0;
+  static constexpr size_t Kc = Qr + (size_t)C * CF::LDK * sz;
+  static constexpr size_t W0 = Kc + (size_t)C * CF::LDK * sz;
+  static constexpr size_t T = W0 + (size_t)C * CF::LDK * sz;
+  static constexpr size_t Q = T + (size_t)C * CF::LDC * sz;
+  static constexpr size_t F = Q + (size_t)C * CF::LDC * sz;
+  static constexpr size_t bytes = A128(F + 3 * kKD * 4);
+  static_assert(Kc % 128 == 0 && T % 128 == 0 && F % 128 == 0, "16-byte aligned blocks");
+};
+
+// One value tile of a chunk's state (h, dh): [KD][LDV] OpT.
+template <class CF>
+__host__ __device__ constexpr size_t state_block_bytes() {
+  return A128((size_t)kKD * CF::LDV * sizeof(typename CF::OpT));
+}
+
+// Per-chunk views of the raw inputs (rows in shared memory or straight in
+// HBM), the per-row / per-channel scalars and the gated operands.
 template <class CF>
 struct Chunk {
   using OpT = typename CF::OpT;
-  // raw inputs
-  bf16* q;
-  bf16* k;
-  float* g;
-  float* kap;   // diag
-  float* beta;  // iso, [C]
+  // raw inputs: row i of q, k, g (and kappa) at ptr + i * ldr; beta at beta[i * ldb]
+  const bf16* q;
+  const bf16* k;
+  const float* g;
+  const float* kap;   // diag
+  const float* beta;  // iso
+  int ldr, ldb;
   // per-row / per-channel scalars
   float* rq;  // iso rstd of q rows
   float* rk;  // iso rstd of k rows
@@ -108,11 +138,8 @@ struct Chunk {
   bool fast;
 };
 
-__host__ __device__ constexpr size_t A128(size_t x) { return align_up(x, 128); }
-__host__ __device__ constexpr size_t cmax(size_t a, size_t b) { return a > b ? a : b; }
-
 // Per-row / per-channel scalars of a chunk: rq, rk [C]; fr, fL, gL, gmid,
-// glast [KD]; red [32].
+// glast [KD]; red [32].  fr, fL, gL are contiguous (the record's F block).
 template <class CF>
 __host__ __device__ constexpr size_t small_floats() {
   return 2 * CF::C + 5 * kKD + 32;
@@ -147,88 +174,114 @@ __device__ __forceinline__ size_t tok_row(const ScanParams& p, int b, int h, int
   return ((size_t)b * p.T + t) * p.H + h;
 }
 
-// Issue the loads of a chunk's q, k, g (and kappa or beta) rows.
+// Stage a chunk's q, k, g (and kappa or beta) rows in shared memory (cp.async,
+// rows >= L zero-filled) and point the chunk view at them.
 template <class CF>
-__device__ __forceinline__ void load_raw(const Chunk<CF>& ch, const ScanParams& p, int b, int h, int t0, int L) {
+__device__ __forceinline__ void load_raw(Chunk<CF>& ch, bf16* sq, bf16* sk, float* sg, float* skap,
+                                         const ScanParams& p, int b, int h, int t0, int L) {
   constexpr bool SM = !CF::F32;
   const size_t r0 = tok_row(p, b, h, t0);
   const size_t rs = (size_t)p.H;
-  copy_rows<SM>(ch.q, kKD * 2, p.q + r0 * kKD, rs * kKD * 2, CF::C, L, kKD * 2);
-  copy_rows<SM>(ch.k, kKD * 2, p.k + r0 * kKD, rs * kKD * 2, CF::C, L, kKD * 2);
-  copy_rows<SM>(ch.g, kKD * 4, p.g + r0 * kKD, rs * kKD * 4, CF::C, L, kKD * 4);
+  copy_rows<SM>(sq, kKD * 2, p.q + r0 * kKD, rs * kKD * 2, CF::C, L, kKD * 2);
+  copy_rows<SM>(sk, kKD * 2, p.k + r0 * kKD, rs * kKD * 2, CF::C, L, kKD * 2);
+  copy_rows<SM>(sg, kKD * 4, p.g + r0 * kKD, rs * kKD * 4, CF::C, L, kKD * 4);
   if constexpr (CF::ISO) {
-    for (int i = threadIdx.x; i < CF::C; i += blockDim.x) ch.beta[i] = i < L ? p.beta[r0 + (size_t)i * rs] : 0.f;
+    for (int i = threadIdx.x; i < CF::C; i += blockDim.x) skap[i] = i < L ? p.beta[r0 + (size_t)i * rs] : 0.f;
   } else {
-    copy_rows<SM>(ch.kap, kKD * 4, p.kappa + r0 * kKD, rs * kKD * 4, CF::C, L, kKD * 4);
+    copy_rows<SM>(skap, kKD * 4, p.kappa + r0 * kKD, rs * kKD * 4, CF::C, L, kKD * 4);
   }
+  ch.q = sq;
+  ch.k = sk;
+  ch.g = sg;
+  ch.kap = CF::ISO ? nullptr : skap;
+  ch.beta = CF::ISO ? skap : nullptr;
+  ch.ldr = kKD;
+  ch.ldb = 1;
+}
+
+// Point the chunk view at the rows in HBM.
+template <class CF>
+__device__ __forceinline__ void bind_raw_global(Chunk<CF>& ch, const ScanParams& p, int b, int h, int t0) {
+  const size_t r0 = tok_row(p, b, h, t0);
+  ch.q = p.q + r0 * kKD;
+  ch.k = p.k + r0 * kKD;
+  ch.g = p.g + r0 * kKD;
+  ch.kap = CF::ISO ? nullptr : p.kappa + r0 * kKD;
+  ch.beta = CF::ISO ? p.beta + r0 : nullptr;
+  ch.ldr = p.H * kKD;
+  ch.ldb = p.H;
 }
 
 template <class CF>
 __device__ __forceinline__ float kappa_at(const Chunk<CF>& ch, int i, int c) {
   if constexpr (CF::ISO) {
-    return ch.beta[i] * ch.rk[i] * to_f(ch.k[i * kKD + c]);
+    return ch.beta[(size_t)i * ch.ldb] * ch.rk[i] * to_f(ch.k[(size_t)i * ch.ldr + c]);
   } else {
-    return ch.kap[i * kKD + c];
+    return ch.kap[(size_t)i * ch.ldr + c];
   }
 }
 template <class CF>
 __device__ __forceinline__ float khat_at(const Chunk<CF>& ch, int i, int c) {
   if constexpr (CF::ISO) {
-    return ch.rk[i] * to_f(ch.k[i * kKD + c]);
+    return ch.rk[i] * to_f(ch.k[(size_t)i * ch.ldr + c]);
   } else {
-    return to_f(ch.k[i * kKD + c]);
+    return to_f(ch.k[(size_t)i * ch.ldr + c]);
   }
 }
 template <class CF>
 __device__ __forceinline__ float qhat_at(const Chunk<CF>& ch, int i, int c) {
   if constexpr (CF::ISO) {
-    return ch.rq[i] * to_f(ch.q[i * kKD + c]);
+    return ch.rq[i] * to_f(ch.q[(size_t)i * ch.ldr + c]);
   } else {
-    return to_f(ch.q[i * kKD + c]);
+    return to_f(ch.q[(size_t)i * ch.ldr + c]);
   }
 }
 
-// Gate references of a chunk: rho for the rows (Kr, Qr) and for the columns (Kc).
+// One row's raw values for the 8 channels a thread handles.
 template <class CF>
-__device__ __forceinline__ float rho_row(const Chunk<CF>& ch, int c) {
-  return ch.fast ? ch.g[ch.m * kKD + c] : 0.f;
-}
-template <class CF>
-__device__ __forceinline__ float rho_col(const Chunk<CF>& ch, int c) {
-  return ch.g[(ch.fast ? ch.m : ch.L - 1) * kKD + c];
-}
+struct RawRow {
+  float g[8], k[8], q[8], kap[CF::ISO ? 1 : 8];
+  float beta;
+};
 
-// Row norms (iso), range check, per-channel factors and the three gated
-// operands.  Thread t handles channels 8*(t%16) .. +7 of rows t/16, t/16 +
-// blockDim/16, ...; the 16 threads of a row are one half-warp, so row norms
-// are half-warp shuffles.  The operands are built in the same pass with the
-// fast-path reference (the gate of the middle row, known up front) and built
-// again only when the range check sends the chunk to the exact path.  The
-// caller places the barrier that publishes the results.
 template <class CF>
-__device__ __forceinline__ void build_operands(Chunk<CF>& ch, int r, int c0, const float (&rr)[8],
-                                               const float (&rc)[8], float qs, float ks) {
-  float kr[8], qr[8], kc[8];
+__device__ __forceinline__ void load_row(RawRow<CF>& x, const Chunk<CF>& ch, int r, int c0) {
   if (r < ch.L) {
-    float g8[8], k8[8], q8[8], kap[8];
-    ld8(g8, ch.g + r * kKD + c0);
-    ld8(k8, ch.k + r * kKD + c0);
-    ld8(q8, ch.q + r * kKD + c0);
-    float bs = 1.f;
+    const size_t o = (size_t)r * ch.ldr + c0;
+    ld8(x.g, ch.g + o);
+    ld8(x.k, ch.k + o);
+    ld8(x.q, ch.q + o);
     if constexpr (CF::ISO) {
-      bs = ch.beta[r] * ks;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) kap[i] = k8[i];
+      x.beta = ch.beta[(size_t)r * ch.ldb];
     } else {
-      ld8(kap, ch.kap + r * kKD + c0);
+      ld8(x.kap, ch.kap + o);
+      x.beta = 1.f;
     }
+  } else {
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const float er = ex2a(g8[i] - rr[i]);
-      const float ec = ex2a(rc[i] - g8[i]);
-      kr[i] = k8[i] * ks * er;
-      qr[i] = q8[i] * qs * er;
-      kc[i] = kap[i] * bs * ec;
+      x.g[i] = x.k[i] = x.q[i] = 0.f;
+      if constexpr (!CF::ISO) x.kap[i] = 0.f;
+    }
+    x.beta = 0.f;
+  }
+}
+
+// Gated operands of one row: Kr = k_hat 2^(g - rr), Qr = q_hat 2^(g - rr),
+// Kc = kappa 2^(rc - g); zero rows past the chunk's end.
+template <class CF>
+__device__ __forceinline__ void build_operands(const Chunk<CF>& ch, int r, int c0, const RawRow<CF>& x,
+                                               const float (&rr)[8], const float (&rc)[8], float qs, float ks) {
+  float kr[8], qr[8], kc[8];
+  if (r < ch.L) {
+    const float bs = CF::ISO ? x.beta * ks : 1.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float er = ex2a(x.g[i] - rr[i]);
+      const float ec = ex2a(rc[i] - x.g[i]);
+      kr[i] = x.k[i] * ks * er;
+      qr[i] = x.q[i] * qs * er;
+      kc[i] = (CF::ISO ? x.k[i] : x.kap[i]) * bs * ec;
     }
   } else {
 #pragma unroll
@@ -239,55 +292,68 @@ __device__ __forceinline__ void build_operands(Chunk<CF>& ch, int r, int c0, con
   st8(ch.Kc + r * CF::LDK + c0, kc);
 }
 
-template <class CF>
+// Row norms (iso), range check, per-channel factors and the three gated
+// operands, for a block of NTH threads.  Thread t handles channels
+// 8*(t%16) .. +7 of rows t/16, t/16 + NTH/16, ...; the 16 threads of a row
+// are one half-warp, so row norms are half-warp shuffles.  Rows are loaded
+// two at a time ahead of their arithmetic (they may come straight from HBM).
+// The operands are built with the fast-path reference (the gate of the
+// middle row, known up front) and built again only when the range check
+// sends the chunk to the exact path.  Contains one barrier; the caller
+// places the barrier that publishes the results.
+template <class CF, int NTH>
 __device__ void prep_chunk(Chunk<CF>& ch) {
-  constexpr int C = CF::C;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  constexpr int C = CF::C, RSTEP = NTH / 16, RPT = C / RSTEP, BATCH = RPT >= 2 ? 2 : 1;
+  static_assert(NTH % 32 == 0 && C % RSTEP == 0 && RPT % BATCH == 0, "rows per thread");
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int L = ch.L;
   ch.m = L >= C ? C / 2 : (((L - 1) / 2) & ~15);
-  const int c0 = (threadIdx.x & 15) * 8;
-  const int rstep = blockDim.x >> 4;
+  const int c0 = (threadIdx.x & 15) * 8, rt = threadIdx.x >> 4;
   float gm[8], gl[8];
-  ld8(gm, ch.g + ch.m * kKD + c0);
-  ld8(gl, ch.g + (L - 1) * kKD + c0);
+  ld8(gm, ch.g + (size_t)ch.m * ch.ldr + c0);
+  ld8(gl, ch.g + (size_t)(L - 1) * ch.ldr + c0);
   float rng = 0.f;
-  for (int r = threadIdx.x >> 4; r < C; r += rstep) {
-    float qs = 1.f, ks = 1.f;
-    if constexpr (CF::ISO) {
-      float q8[8], k8[8];
-      ld8(q8, ch.q + r * kKD + c0);
-      ld8(k8, ch.k + r * kKD + c0);
-      float sq = 0.f, sk = 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        sq = fmaf(q8[i], q8[i], sq);
-        sk = fmaf(k8[i], k8[i], sk);
-      }
+  for (int j0 = 0; j0 < RPT; j0 += BATCH) {
+    RawRow<CF> x[BATCH];
 #pragma unroll
-      for (int o = 1; o < 16; o <<= 1) {
-        sq += __shfl_xor_sync(0xffffffffu, sq, o);
-        sk += __shfl_xor_sync(0xffffffffu, sk, o);
+    for (int j = 0; j < BATCH; ++j) load_row(x[j], ch, rt + (j0 + j) * RSTEP, c0);
+#pragma unroll
+    for (int j = 0; j < BATCH; ++j) {
+      const int r = rt + (j0 + j) * RSTEP;
+      float qs = 1.f, ks = 1.f;
+      if constexpr (CF::ISO) {
+        float sq = 0.f, sk = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          sq = fmaf(x[j].q[i], x[j].q[i], sq);
+          sk = fmaf(x[j].k[i], x[j].k[i], sk);
+        }
+#pragma unroll
+        for (int o = 1; o < 16; o <<= 1) {
+          sq += __shfl_xor_sync(0xffffffffu, sq, o);
+          sk += __shfl_xor_sync(0xffffffffu, sk, o);
+        }
+        qs = rsqrtf(sq + 1e-6f);
+        ks = rsqrtf(sk + 1e-6f);
+        if ((threadIdx.x & 15) == 0) {
+          ch.rq[r] = qs;
+          ch.rk[r] = ks;
+        }
       }
-      qs = rsqrtf(sq + 1e-6f);
-      ks = rsqrtf(sk + 1e-6f);
-      if ((threadIdx.x & 15) == 0) {
-        ch.rq[r] = qs;
-        ch.rk[r] = ks;
+      if (r < L) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) rng = fmaxf(rng, fabsf(x[j].g[i] - gm[i]));
       }
+      build_operands(ch, r, c0, x[j], gm, gm, qs, ks);
     }
-    if (r < L) {
-      float g8[8];
-      ld8(g8, ch.g + r * kKD + c0);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) rng = fmaxf(rng, fabsf(g8[i] - gm[i]));
-    }
-    build_operands(ch, r, c0, gm, gm, qs, ks);
   }
   rng = warp_max(rng);
   if (lane == 0) ch.red[warp] = rng;
   __syncthreads();
   float tot = 0.f;
-  for (int w = 0; w < nw; ++w) tot = fmaxf(tot, ch.red[w]);
+#pragma unroll
+  for (int w = 0; w < NTH / 32; ++w) tot = fmaxf(tot, ch.red[w]);
   ch.fast = tot <= kRngMax;
   float rr[8], rc[8];
 #pragma unroll
@@ -306,9 +372,13 @@ __device__ void prep_chunk(Chunk<CF>& ch) {
     }
   }
   if (!ch.fast) {
-    for (int r = threadIdx.x >> 4; r < C; r += rstep) {
+#pragma unroll 1
+    for (int j = 0; j < RPT; ++j) {
+      const int r = rt + j * RSTEP;
+      RawRow<CF> x;
+      load_row(x, ch, r, c0);
       const float qs = CF::ISO ? ch.rq[r] : 1.f, ks = CF::ISO ? ch.rk[r] : 1.f;
-      build_operands(ch, r, c0, rr, rc, qs, ks);
+      build_operands(ch, r, c0, x, rr, rc, qs, ks);
     }
   }
 }
@@ -359,7 +429,7 @@ __device__ void chunk_scores(const Chunk<CF>& ch, float* sA, typename CF::OpT* s
       float a = 0.f, qq = 0.f;
       if (j <= i && i < ch.L) {
         for (int c = 0; c < kKD; ++c) {
-          const float f = kappa_at(ch, j, c) * ex2(ch.g[i * kKD + c] - ch.g[j * kKD + c]);
+          const float f = kappa_at(ch, j, c) * ex2(ch.g[(size_t)i * ch.ldr + c] - ch.g[(size_t)j * ch.ldr + c]);
           a = fmaf(khat_at(ch, i, c), f, a);
           qq = fmaf(qhat_at(ch, i, c), f, qq);
         }
@@ -457,21 +527,20 @@ __device__ void chunk_solve(const float* sA, const typename CF::OpT* sAb, typena
   static_assert(NB == 2 || NB == 4, "chunk of 32 or 64 tokens");
 }
 
-// Copy a C x C OpT matrix between a padded shared buffer and an unpadded
-// global one (saved T and Q).  Async (cp.async) towards shared memory.
+// Contiguous copy of `bytes` (a multiple of 16) by the whole block:
+// cp.async towards shared memory, or plain 16-byte copies in the fp32 debug
+// precision (where both sides are global memory).
 template <class CF>
-__device__ __forceinline__ void store_cc(typename CF::OpT* dst, const typename CF::OpT* src) {
-  constexpr int C = CF::C, VEC = 16 / sizeof(typename CF::OpT), PER = C / VEC;
-  for (int e = threadIdx.x; e < C * PER; e += blockDim.x) {
-    const int i = e / PER, c = (e - i * PER) * VEC;
-    *reinterpret_cast<uint4*>(dst + i * C + c) = *reinterpret_cast<const uint4*>(src + i * CF::LDC + c);
+__device__ __forceinline__ void copy_block(void* dst, const void* src, size_t bytes) {
+  char* d = static_cast<char*>(dst);
+  const char* s = static_cast<const char*>(src);
+  for (size_t o = (size_t)threadIdx.x * 16; o < bytes; o += (size_t)blockDim.x * 16) {
+    if constexpr (CF::F32) {
+      *reinterpret_cast<int4*>(d + o) = *reinterpret_cast<const int4*>(s + o);
+    } else {
+      cp_async16(d + o, s + o);
+    }
   }
-}
-template <class CF>
-__device__ __forceinline__ void load_cc(typename CF::OpT* dst, const typename CF::OpT* src) {
-  constexpr int C = CF::C;
-  copy_rows<!CF::F32>(dst, CF::LDC * sizeof(typename CF::OpT), src, C * sizeof(typename CF::OpT), C, C,
-                      C * sizeof(typename CF::OpT));
 }
 
 }  // namespace kdn

@@ -8,6 +8,7 @@ namespace kdn {
 
 template <class CF> int launch_fwd(const ScanParams&, cudaStream_t);
 template <class CF> int launch_bwd(const ScanParams&, cudaStream_t);
+template <class CF> size_t prep_dbg_bytes();
 template <class CF> size_t fwd_dbg_bytes();
 template <class CF> size_t state_bytes();
 template <class CF> size_t chunk_bytes();
@@ -19,39 +20,59 @@ using DiagF = Cfg<false, 32, float>;
 
 namespace {
 
+// saved     = [status word | chunk records | chunk-start states h]
+// workspace = [status word | chunk-end adjoints dh | fp32-precision scratch]
+constexpr size_t kHeader = 256;
+constexpr int kVT = kVD / kBV;
+
 struct Sizes {
-  int64_t C, NT, BH, op;  // chunk, chunks, streams, bytes per state element
-  size_t tq, h, dh, dbg_fwd, dbg_bwd;
+  int64_t C, NT, BH;
+  size_t rec, h, dh;
+  size_t fwd_stride, bwd_stride;  // per-CTA scratch of the fp32 precision
+  size_t dbg_fwd, dbg_bwd;
 };
+
+template <class CF>
+void layout_sizes(Sizes* s) {
+  s->rec = align_up(Rec<CF>::bytes * s->BH * s->NT, 256);
+  s->h = align_up(state_block_bytes<CF>() * kVT * s->BH * s->NT, 256);
+  s->dh = s->h;
+}
 
 bool sizes_of(const KdnScanArgs* a, Sizes* s) {
   if (!a || (a->variant != KDN_ISO && a->variant != KDN_DIAG) ||
       (a->precision != KDN_PREC_BF16 && a->precision != KDN_PREC_FP32))
     return false;
   if (a->B <= 0 || a->T <= 0 || a->H <= 0 || a->K != kKD || a->V != kVD) return false;
-  s->C = a->variant == KDN_ISO ? 64 : 32;
+  const bool iso = a->variant == KDN_ISO, f32 = a->precision == KDN_PREC_FP32;
+  s->C = iso ? 64 : 32;
   s->NT = (a->T + s->C - 1) / s->C;
   s->BH = a->B * a->H;
-  s->op = a->precision == KDN_PREC_FP32 ? 4 : 2;
-  s->tq = align_up((size_t)s->op * s->BH * s->NT * s->C * s->C, 256);
-  s->h = align_up((size_t)s->op * s->BH * s->NT * kKD * kVD, 256);
-  s->dh = s->h;
-  s->dbg_fwd = s->dbg_bwd = 0;
-  if (a->precision == KDN_PREC_FP32) {
-    const bool iso = a->variant == KDN_ISO;
+  if (iso) {
+    f32 ? layout_sizes<IsoF>(s) : layout_sizes<IsoB>(s);
+  } else {
+    f32 ? layout_sizes<DiagF>(s) : layout_sizes<DiagB>(s);
+  }
+  s->fwd_stride = s->bwd_stride = s->dbg_fwd = s->dbg_bwd = 0;
+  if (f32) {
+    const size_t pr = iso ? prep_dbg_bytes<IsoF>() : prep_dbg_bytes<DiagF>();
     const size_t f = iso ? fwd_dbg_bytes<IsoF>() : fwd_dbg_bytes<DiagF>();
     const size_t st = iso ? state_bytes<IsoF>() : state_bytes<DiagF>();
     const size_t ck = iso ? chunk_bytes<IsoF>() : chunk_bytes<DiagF>();
-    s->dbg_fwd = align_up(f * 2 * s->BH, 256);
-    // both backward kernels index per-CTA slices with one stride
-    s->dbg_bwd = align_up((st > ck ? st : ck) * (size_t)(s->NT > 2 ? s->NT : 2) * s->BH, 256);
+    // the two kernels of each direction index per-CTA slices with one stride
+    const size_t ctas = (size_t)(s->NT > kVT ? s->NT : kVT) * s->BH;
+    s->fwd_stride = pr > f ? pr : f;
+    s->bwd_stride = st > ck ? st : ck;
+    s->dbg_fwd = align_up(s->fwd_stride * ctas, 256);
+    s->dbg_bwd = align_up(s->bwd_stride * ctas, 256);
   }
   return true;
 }
 
 int fill_params(const KdnScanArgs* a, const Sizes& s, ScanParams* p) {
   if (!(isfinite(a->scale))) return set_error(KDN_ERR_INVALID, "kdn_scan: scale must be finite");
-  if (a->T > (1ll << 30) || s.BH > 65535) return set_error(KDN_ERR_INVALID, "kdn_scan: size too large");
+  if (a->T > (1ll << 30) || s.BH > 65535 || s.NT > 2147483647ll / 64)
+    return set_error(KDN_ERR_INVALID, "kdn_scan: size too large");
   *p = ScanParams{};
   p->q = static_cast<const bf16*>(a->q);
   p->k = static_cast<const bf16*>(a->k);
@@ -63,9 +84,9 @@ int fill_params(const KdnScanArgs* a, const Sizes& s, ScanParams* p) {
   p->o = a->o;
   p->ST = a->final_state;
   char* sv = static_cast<char*>(a->saved);
-  p->Tsave = sv;
-  p->Qsave = sv + s.tq;
-  p->h = sv + 2 * s.tq;
+  p->status = reinterpret_cast<int*>(sv);
+  p->rec = sv + kHeader;
+  p->h = sv + kHeader + s.rec;
   p->dO = a->dO;
   p->dST = a->d_final_state;
   p->dS0 = a->d_initial_state;
@@ -93,13 +114,13 @@ extern "C" {
 size_t kdn_scan_saved_bytes(const KdnScanArgs* a) {
   Sizes s;
   if (!sizes_of(a, &s)) return 0;
-  return 2 * s.tq + s.h;
+  return kHeader + s.rec + s.h;
 }
 
 size_t kdn_scan_workspace_bytes(const KdnScanArgs* a) {
   Sizes s;
   if (!sizes_of(a, &s)) return 0;
-  const size_t bwd = s.dh + s.dbg_bwd;
+  const size_t bwd = kHeader + s.dh + s.dbg_bwd;
   return bwd > s.dbg_fwd ? bwd : s.dbg_fwd;
 }
 
@@ -115,13 +136,13 @@ int kdn_scan_fwd(const KdnScanArgs* a, kdn_stream_t stream) {
   ScanParams p;
   int rc = fill_params(a, s, &p);
   if (rc != KDN_OK) return rc;
+  const cudaStream_t st = (cudaStream_t)stream;
+  if (cudaMemsetAsync(p.status, 0, sizeof(int), st) != cudaSuccess) return check_launch("kdn_scan_fwd: status reset");
   p.dbg = static_cast<char*>(a->workspace);
+  p.dbg_stride = s.fwd_stride;
   const bool iso = a->variant == KDN_ISO;
-  if (a->precision == KDN_PREC_FP32) {
-    p.dbg_stride = iso ? fwd_dbg_bytes<IsoF>() : fwd_dbg_bytes<DiagF>();
-    return iso ? launch_fwd<IsoF>(p, (cudaStream_t)stream) : launch_fwd<DiagF>(p, (cudaStream_t)stream);
-  }
-  return iso ? launch_fwd<IsoB>(p, (cudaStream_t)stream) : launch_fwd<DiagB>(p, (cudaStream_t)stream);
+  if (a->precision == KDN_PREC_FP32) return iso ? launch_fwd<IsoF>(p, st) : launch_fwd<DiagF>(p, st);
+  return iso ? launch_fwd<IsoB>(p, st) : launch_fwd<DiagB>(p, st);
 }
 
 int kdn_scan_bwd(const KdnScanArgs* a, kdn_stream_t stream) {
@@ -132,21 +153,20 @@ int kdn_scan_bwd(const KdnScanArgs* a, kdn_stream_t stream) {
   if (!a->q || !a->k || !a->v || !a->g || !a->saved || !a->dO || !a->dq || !a->dk || !a->dv || !a->dg ||
       (iso ? (!a->beta || !a->dbeta) : (!a->kappa || !a->dkappa)))
     return set_error(KDN_ERR_INVALID, "kdn_scan_bwd: null input/output pointer");
-  if (!a->workspace || a->workspace_bytes < s.dh + s.dbg_bwd)
+  if (!a->workspace || a->workspace_bytes < kHeader + s.dh + s.dbg_bwd)
     return set_error(KDN_ERR_WORKSPACE, "kdn_scan_bwd: workspace too small");
   ScanParams p;
   int rc = fill_params(a, s, &p);
   if (rc != KDN_OK) return rc;
-  p.dh = a->workspace;
-  p.dbg = static_cast<char*>(a->workspace) + s.dh;
-  if (a->precision == KDN_PREC_FP32) {
-    // both backward kernels use the same per-CTA stride bound
-    const size_t st = iso ? state_bytes<IsoF>() : state_bytes<DiagF>();
-    const size_t ck = iso ? chunk_bytes<IsoF>() : chunk_bytes<DiagF>();
-    p.dbg_stride = st > ck ? st : ck;
-    return iso ? launch_bwd<IsoF>(p, (cudaStream_t)stream) : launch_bwd<DiagF>(p, (cudaStream_t)stream);
-  }
-  return iso ? launch_bwd<IsoB>(p, (cudaStream_t)stream) : launch_bwd<DiagB>(p, (cudaStream_t)stream);
+  char* ws = static_cast<char*>(a->workspace);
+  p.status = reinterpret_cast<int*>(ws);
+  p.dh = ws + kHeader;
+  p.dbg = ws + kHeader + s.dh;
+  p.dbg_stride = s.bwd_stride;
+  const cudaStream_t st = (cudaStream_t)stream;
+  if (cudaMemsetAsync(p.status, 0, sizeof(int), st) != cudaSuccess) return check_launch("kdn_scan_bwd: status reset");
+  if (a->precision == KDN_PREC_FP32) return iso ? launch_bwd<IsoF>(p, st) : launch_bwd<DiagF>(p, st);
+  return iso ? launch_bwd<IsoB>(p, st) : launch_bwd<DiagB>(p, st);
 }
 
 }  // extern "C"

@@ -1,12 +1,15 @@
 // Backward of the chunked KDN memory scan.
 //
 // 1. scan_bwd_state_kernel (one CTA per (value tile, b*h), chunks in reverse):
-//    carries the state adjoint dS in registers,
+//    carries the state adjoint dS in registers; a producer warp streams the
+//    chunk records of the forward's first pass and the dO rows through a
+//    ring of bulk-copy stages,
 //        ddelta  = scale Q^T dO + Kc (fL*dS)
 //        dS_prev = Diag(2^g_L) dS + Diag(fr) (scale Qr^T dO - W0^T ddelta)
-//    and stores the chunk-end adjoint of every chunk (bf16) for step 2.
+//    and stores every chunk's fL-scaled chunk-end adjoint (bf16) for step 2.
 // 2. scan_bwd_chunk_kernel (one CTA per (chunk, b*h), all chunks in parallel):
-//    with the saved chunk-start state S0 and the chunk-end adjoint dS it
+//    with the saved chunk-start state S0' = fr S0 and chunk-end adjoint
+//    dS'' = fL dS it
 //    rebuilds delta and ddelta and forms every input gradient of the chunk:
 //        dQ = scale dO delta^T,  dT = ddelta v^T + dW0 Kr^T,
 //        dA = -T^T dT T^T,  dv = T^T ddelta,  dW0 = -ddelta (fr S0)^T,
@@ -25,46 +28,205 @@ namespace kdn {
 // ---------------------------------------------------------------------------
 // 1. reverse state-adjoint sweep
 // ---------------------------------------------------------------------------
+// Stage: the chunk record, then dO [C][LDV] OpT (iso) or fp32 [C][BV]
+// staging (diag, rounded to bf16 into the dOb buffer).
 template <class CF>
 struct StateLayout {
   static constexpr size_t sz = sizeof(typename CF::OpT);
   static constexpr int C = CF::C;
-  static constexpr size_t q = 0;
-  static constexpr size_t k = q + A128((size_t)C * kKD * 2);
-  static constexpr size_t g = k + A128((size_t)C * kKD * 2);
-  static constexpr size_t kap = g + A128((size_t)C * kKD * 4);
-  static constexpr size_t dOst = kap + A128(CF::ISO ? (size_t)C * 4 : (size_t)C * kKD * 4);  // diag fp32 dO
-  static constexpr size_t dO = dOst + A128(CF::ISO ? 16 : (size_t)C * kBV * 4);  // two buffers
-  static constexpr size_t Tb = dO + 2 * A128((size_t)C * CF::LDV * sz);          // two buffers
-  static constexpr size_t Qb = Tb + 2 * A128((size_t)C * CF::LDC * sz);          // two buffers
-  static constexpr size_t Kr = Qb + 2 * A128((size_t)C * CF::LDC * sz);
-  static constexpr size_t Qr = Kr + A128((size_t)C * CF::LDK * sz);
-  static constexpr size_t Kc = Qr + A128((size_t)C * CF::LDK * sz);
-  static constexpr size_t W = Kc + A128((size_t)C * CF::LDK * sz);
-  static constexpr size_t DS = W + A128((size_t)C * CF::LDK * sz);
-  static constexpr size_t DD = DS + A128((size_t)kKD * CF::LDV * sz);
-  static constexpr size_t small = DD + A128((size_t)C * CF::LDV * sz);
-  static constexpr size_t bytes = small + A128(small_floats<CF>() * 4);
+  static constexpr int NS = CF::F32 ? 1 : (CF::ISO ? 2 : 4);
+  static constexpr bool STAGE_F32 = !CF::ISO;  // diag cotangent arrives as fp32
+  static constexpr size_t dO = Rec<CF>::bytes;
+  static constexpr size_t stage = A128(dO + (STAGE_F32 ? (size_t)C * kBV * 4 : (size_t)C * CF::LDV * sz));
+  static constexpr size_t dOb = NS * stage;  // diag: the rounded operand
+  static constexpr size_t DS = dOb + A128(STAGE_F32 ? (size_t)C * CF::LDV * sz : 16);  // two [KD][LDV] buffers
+  static constexpr size_t DD = DS + 2 * state_block_bytes<CF>();
+  static constexpr size_t bar = DD + A128((size_t)C * CF::LDV * sz);
+  static constexpr size_t bytes = bar + 128;
 };
 
 template <class CF>
-__device__ __forceinline__ void stage_dO(void* dst, const ScanParams& p, int b, int h, int t0, int L, int v0,
-                                         int ld) {
-  constexpr int C = CF::C;
-  const size_t r0 = tok_row(p, b, h, t0) * kVD + v0;
-  if constexpr (CF::ISO) {
-    load_tile_op<CF>(static_cast<typename CF::OpT*>(dst), ld, static_cast<const bf16*>(p.dO) + r0,
-                     (size_t)p.H * kVD, C, L, kBV);
-  } else {
-    copy_rows<!CF::F32>(dst, kBV * 4, static_cast<const float*>(p.dO) + r0, (size_t)p.H * kVD * 4, C, L, kBV * 4);
+__global__ void __launch_bounds__(kSeqThreads + 32, 1) scan_bwd_state_kernel(ScanParams p) {
+  using OpT = typename CF::OpT;
+  using Lo = StateLayout<CF>;
+  using R = Rec<CF>;
+  constexpr int C = CF::C, NS = Lo::NS;
+  constexpr int NTU = C / 32;
+  constexpr int NJU = kBV / (8 * NTU);
+  static_assert((C / 16) * NJU == 16, "16 warps");
+  extern __shared__ __align__(128) char smem[];
+  char* base = CF::F32 ? p.dbg + (size_t)(blockIdx.y * gridDim.x + blockIdx.x) * p.dbg_stride : smem;
+
+  const int vt = blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int v0 = vt * kBV;
+  const char* recs = static_cast<const char*>(p.rec) + (size_t)bh * p.NT * R::bytes;
+  char* dhout = static_cast<char*>(p.dh) + ((size_t)bh * p.NT * (kVD / kBV) + vt) * state_block_bytes<CF>();
+  constexpr size_t h_stride = (kVD / kBV) * state_block_bytes<CF>();
+  uint64_t* full = reinterpret_cast<uint64_t*>(base + Lo::bar);
+  uint64_t* empty = full + NS;
+  OpT* sDD = reinterpret_cast<OpT*>(base + Lo::DD);
+  constexpr unsigned dO_row = Lo::STAGE_F32 ? kBV * 4 : kBV * 2;
+  constexpr size_t dO_pitch = Lo::STAGE_F32 ? (size_t)kBV * 4 : (size_t)CF::LDV * Lo::sz;
+
+  // the it-th chunk from the end into stage it % NS (producer warp)
+  auto issue = [&](int it) {
+    const int c = p.NT - 1 - it;
+    char* st = base + (it % NS) * Lo::stage;
+    const int t0 = c * C, L = min(C, p.T - t0);
+    if (lane == 0) {
+      mbar_expect_tx(&full[it % NS], (unsigned)(R::bytes + (size_t)L * dO_row));
+      bulk_g2s(st, recs + (size_t)c * R::bytes, (unsigned)R::bytes, &full[it % NS]);
+    }
+    __syncwarp();
+    const char* src = static_cast<const char*>(p.dO) + (Lo::STAGE_F32 ? 4 : 2) * (size_t)v0;
+    const size_t row_bytes = (Lo::STAGE_F32 ? 4 : 2) * (size_t)kVD;
+    for (int r = lane; r < L; r += 32)
+      bulk_g2s(st + Lo::dO + r * dO_pitch, src + tok_row(p, b, h, t0 + r) * row_bytes, dO_row, &full[it % NS]);
+  };
+  auto load_sync = [&](int it) {
+    const int c = p.NT - 1 - it;
+    const int t0 = c * C, L = min(C, p.T - t0);
+    copy_block<CF>(base, recs + (size_t)c * R::bytes, R::bytes);
+    const size_t r0 = tok_row(p, b, h, t0) * kVD + v0;
+    if constexpr (CF::ISO) {
+      load_tile_op<CF>(reinterpret_cast<OpT*>(base + Lo::dO), CF::LDV, static_cast<const bf16*>(p.dO) + r0,
+                       (size_t)p.H * kVD, C, L, kBV);
+    } else {
+      copy_rows<false>(base + Lo::dO, kBV * 4, static_cast<const float*>(p.dO) + r0, (size_t)p.H * kVD * 4, C, L,
+                       kBV * 4);
+    }
+  };
+
+  if constexpr (!CF::F32) {
+    if (threadIdx.x == 0) {
+      for (int s = 0; s < NS; ++s) {
+        mbar_init(&full[s], 1);
+        mbar_init(&empty[s], kSeqThreads / 32);
+      }
+      fence_mbar_init();
+    }
+    __syncthreads();
+    if (warp == kSeqThreads / 32) {
+      for (int it = 0; it < p.NT; ++it) {
+        if (it >= NS) mbar_wait(&empty[it % NS], (it / NS - 1) & 1, p.status);
+        issue(it);
+      }
+      return;
+    }
   }
+
+  const int sm0 = 16 * (warp >> 1), sn0 = 32 * (warp & 1);
+  float dS[1][4][4];
+  for_acc<1, 4>(sm0, sn0, [&](int, int nt, int e, int row, int col) {
+    dS[0][nt][e] = p.dST ? p.dST[((size_t)bh * kKD + row) * kVD + v0 + col] : 0.f;
+  });
+  const int Iu = warp / NJU, nu = (warp % NJU) * 8 * NTU;
+
+  for (int it = 0; it < p.NT; ++it) {
+    const int c = p.NT - 1 - it;
+    const int L = min(C, p.T - c * C);
+    char* st = base + (it % NS) * Lo::stage;
+    const OpT* sQr = reinterpret_cast<const OpT*>(st + R::Qr);
+    const OpT* sKc = reinterpret_cast<const OpT*>(st + R::Kc);
+    const OpT* sW0 = reinterpret_cast<const OpT*>(st + R::W0);
+    const OpT* sQ = reinterpret_cast<const OpT*>(st + R::Q);
+    const float* fr = reinterpret_cast<const float*>(st + R::F);
+    const float* fL = fr + kKD;
+    const float* gL = fL + kKD;
+    OpT* sdO = reinterpret_cast<OpT*>(Lo::STAGE_F32 ? base + Lo::dOb : st + Lo::dO);
+    OpT* sDS = reinterpret_cast<OpT*>(base + Lo::DS + (it & 1) * state_block_bytes<CF>());
+
+    if constexpr (CF::F32) {
+      __syncthreads();
+      load_sync(it);
+      __syncthreads();
+    } else {
+      mbar_wait(&full[it % NS], (it / NS) & 1, p.status);
+      if constexpr (CF::ISO) {
+        for (int e = threadIdx.x; e < (C - L) * (kBV / 8); e += kSeqThreads)
+          *reinterpret_cast<int4*>(sdO + (L + e / (kBV / 8)) * CF::LDV + (e % (kBV / 8)) * 8) =
+              make_int4(0, 0, 0, 0);
+      }
+    }
+    if constexpr (Lo::STAGE_F32) {
+      // the reference rounds the fp32 cotangent to bf16 first (diag_kdn_chunk.py:3277)
+      const float* stg = reinterpret_cast<const float*>(st + Lo::dO);
+      for (int e = threadIdx.x; e < C * kBV / 2; e += kSeqThreads) {
+        const int i = (2 * e) / kBV, cc = 2 * e - i * kBV;
+        float2 x = make_float2(0.f, 0.f);
+        if (i < L) x = *reinterpret_cast<const float2*>(stg + i * kBV + cc);
+        st_pair(sdO + i * CF::LDV + cc, __bfloat162float(__float2bfloat16_rn(x.x)),
+                __bfloat162float(__float2bfloat16_rn(x.y)));
+      }
+    }
+    // dS'' = fL dS: the product operand and the saved chunk-end adjoint
+    for_acc_pairs<1, 4>(dS, sm0, sn0, [&](int, int, int, int row, int col, float x0, float x1) {
+      const float f = fL[row];
+      st_pair(sDS + row * CF::LDV + col, f * x0, f * x1);
+    });
+    if constexpr (!CF::F32) fence_async_shared();
+    bar_sync(1, kSeqThreads);
+    if constexpr (CF::F32) {
+      copy_block<CF>(dhout + c * h_stride, sDS, state_block_bytes<CF>());
+    } else {
+      if (threadIdx.x == 32) {
+        bulk_s2g(dhout + c * h_stride, sDS, (unsigned)state_block_bytes<CF>());
+        bulk_commit();
+      }
+    }
+
+    // Qr^T dO (independent of the carried adjoint)
+    float a1[1][4][4];
+    zero_acc(a1);
+    wgemm<1, 4, false, false>(a1, sQr, CF::LDK, sdO, CF::LDV, sm0, sn0, 0, C);
+    // ddelta = scale Q^T dO + Kc dS''
+    {
+      float u[1][NTU][4], a[1][NTU][4];
+      zero_acc(u);
+      zero_acc(a);
+      wgemm<1, NTU, false, false>(u, sQ, CF::LDC, sdO, CF::LDV, 16 * Iu, nu, 16 * Iu, C);
+      wgemm<1, NTU, true, false>(a, sKc, CF::LDK, sDS, CF::LDV, 16 * Iu, nu, 0, kKD);
+#pragma unroll
+      for (int nt = 0; nt < NTU; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) u[0][nt][e] = p.scale * u[0][nt][e] + a[0][nt][e];
+      store_acc(sDD, CF::LDV, u, 16 * Iu, nu);
+    }
+    if constexpr (!CF::F32)
+      if (threadIdx.x == 32) bulk_wait_read<1>();
+    bar_sync(1, kSeqThreads);
+
+    // dS <- Diag(2^g_L) dS + Diag(fr) (scale Qr^T dO - W0^T ddelta)
+    {
+      float a2[1][4][4];
+      zero_acc(a2);
+      wgemm<1, 4, false, false>(a2, sW0, CF::LDK, sDD, CF::LDV, sm0, sn0, 0, C);
+      for_acc<1, 4>(sm0, sn0, [&](int, int nt, int e, int row, int) {
+        dS[0][nt][e] = gL[row] * dS[0][nt][e] + fr[row] * (p.scale * a1[0][nt][e] - a2[0][nt][e]);
+      });
+    }
+    if constexpr (!CF::F32) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[it % NS]);
+    }
+  }
+  if (p.dS0) {
+    for_acc<1, 4>(sm0, sn0, [&](int, int nt, int e, int row, int col) {
+      p.dS0[((size_t)bh * kKD + row) * kVD + v0 + col] = dS[0][nt][e];
+    });
+  }
+  if constexpr (!CF::F32)
+    if (threadIdx.x == 32) bulk_wait_all();
 }
 
+// ---------------------------------------------------------------------------
+// 2. chunk-parallel gradients
+// ---------------------------------------------------------------------------
 // The diagonal variant's fp32 cotangent as the OpT operand, rounded to bf16
 // like the reference does before its backward kernels (diag_kdn_chunk.py:3277).
 template <class CF>
 __device__ __forceinline__ void convert_dO(typename CF::OpT* dst, const float* st) {
-  using OpT = typename CF::OpT;
   for (int e = threadIdx.x; e < CF::C * kBV / 2; e += blockDim.x) {
     const int i = (2 * e) / kBV, c = 2 * e - i * kBV;
     const float2 x = *reinterpret_cast<const float2*>(st + i * kBV + c);
@@ -73,127 +235,6 @@ __device__ __forceinline__ void convert_dO(typename CF::OpT* dst, const float* s
   }
 }
 
-template <class CF>
-__global__ void __launch_bounds__(kSeqThreads, 1) scan_bwd_state_kernel(ScanParams p) {
-  using OpT = typename CF::OpT;
-  using Lo = StateLayout<CF>;
-  constexpr int C = CF::C;
-  constexpr int NTW = C / 16;
-  constexpr int NJW = kKD / (8 * NTW);
-  constexpr int NTU = C / 32;
-  constexpr int NJU = kBV / (8 * NTU);
-  static_assert((C / 16) * NJW == 16 && (C / 16) * NJU == 16, "16 warps");
-  extern __shared__ __align__(128) char smem[];
-  char* base = CF::F32 ? p.dbg + (size_t)(blockIdx.y * gridDim.x + blockIdx.x) * p.dbg_stride : smem;
-
-  Chunk<CF> ch;
-  ch.q = reinterpret_cast<bf16*>(base + Lo::q);
-  ch.k = reinterpret_cast<bf16*>(base + Lo::k);
-  ch.g = reinterpret_cast<float*>(base + Lo::g);
-  ch.kap = reinterpret_cast<float*>(base + Lo::kap);
-  ch.beta = ch.kap;
-  ch.Kr = reinterpret_cast<OpT*>(base + Lo::Kr);
-  ch.Qr = reinterpret_cast<OpT*>(base + Lo::Qr);
-  ch.Kc = reinterpret_cast<OpT*>(base + Lo::Kc);
-  bind_small(ch, reinterpret_cast<float*>(base + Lo::small));
-  float* dOst = reinterpret_cast<float*>(base + Lo::dOst);
-  constexpr size_t dO_stride = A128((size_t)C * CF::LDV * sizeof(OpT));
-  constexpr size_t cc_stride = A128((size_t)C * CF::LDC * sizeof(OpT));
-  auto sdO_buf = [&](int i) { return reinterpret_cast<OpT*>(base + Lo::dO + i * dO_stride); };
-  auto sTb_buf = [&](int i) { return reinterpret_cast<OpT*>(base + Lo::Tb + i * cc_stride); };
-  auto sQb_buf = [&](int i) { return reinterpret_cast<OpT*>(base + Lo::Qb + i * cc_stride); };
-  OpT* sDS = reinterpret_cast<OpT*>(base + Lo::DS);
-  OpT* sW = reinterpret_cast<OpT*>(base + Lo::W);
-  OpT* sDD = reinterpret_cast<OpT*>(base + Lo::DD);
-
-  const int vt = blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
-  const int warp = threadIdx.x >> 5;
-  const int v0 = vt * kBV;
-
-  const int sm0 = 16 * (warp >> 1), sn0 = 32 * (warp & 1);
-  float dS[1][4][4];
-  for_acc<1, 4>(sm0, sn0, [&](int, int nt, int e, int row, int col) {
-    dS[0][nt][e] = p.dST ? p.dST[((size_t)bh * kKD + row) * kVD + v0 + col] : 0.f;
-  });
-
-  auto issue_loads = [&](int c, int buf) {
-    const int t0 = c * C, L = min(C, p.T - t0);
-    const size_t cc = (size_t)bh * p.NT + c;
-    load_raw(ch, p, b, h, t0, L);
-    load_cc<CF>(sTb_buf(buf), static_cast<const OpT*>(p.Tsave) + cc * C * C);
-    load_cc<CF>(sQb_buf(buf), static_cast<const OpT*>(p.Qsave) + cc * C * C);
-    stage_dO<CF>(CF::ISO ? static_cast<void*>(sdO_buf(buf)) : static_cast<void*>(dOst), p, b, h, t0, L, v0, CF::LDV);
-    if constexpr (!CF::F32) cp_async_commit();
-  };
-  issue_loads(p.NT - 1, 0);
-
-  for (int c = p.NT - 1; c >= 0; --c) {
-    const int buf = (p.NT - 1 - c) & 1;
-    OpT* sTb = sTb_buf(buf);
-    OpT* sQb = sQb_buf(buf);
-    OpT* sdO = sdO_buf(buf);
-    ch.L = min(C, p.T - c * C);
-    if constexpr (!CF::F32) cp_async_wait_all();
-    __syncthreads();
-    prep_chunk(ch);
-    if constexpr (!CF::ISO) convert_dO<CF>(sdO, dOst);
-    __syncthreads();
-    if (c > 0) issue_loads(c - 1, buf ^ 1);
-
-    // W0 = T Kr; fL-scaled adjoint operand; chunk-end adjoint to HBM
-    const int I = warp / NJW;
-    {
-      float acc[1][NTW][4];
-      zero_acc(acc);
-      wgemm<1, NTW, true, false>(acc, sTb, CF::LDC, ch.Kr, CF::LDK, 16 * I, (warp % NJW) * 8 * NTW, 0, 16 * (I + 1));
-      store_acc(sW, CF::LDK, acc, 16 * I, (warp % NJW) * 8 * NTW);
-    }
-    OpT* dhdst = static_cast<OpT*>(p.dh) + ((size_t)bh * p.NT + c) * kKD * kVD;
-    for_acc_pairs<1, 4>(dS, sm0, sn0, [&](int, int, int, int row, int col, float x0, float x1) {
-      const float f = ch.fL[row];
-      st_pair(sDS + row * CF::LDV + col, f * x0, f * x1);
-      st_pair(dhdst + (size_t)row * kVD + v0 + col, x0, x1);
-    });
-    __syncthreads();
-
-    // ddelta = scale Q^T dO + Kc (fL dS)
-    const int Iu = warp / NJU, nu = (warp % NJU) * 8 * NTU;
-    {
-      float a1[1][NTU][4], a2[1][NTU][4];
-      zero_acc(a1);
-      zero_acc(a2);
-      wgemm<1, NTU, false, false>(a1, sQb, CF::LDC, sdO, CF::LDV, 16 * Iu, nu, 16 * Iu, C);
-      wgemm<1, NTU, true, false>(a2, ch.Kc, CF::LDK, sDS, CF::LDV, 16 * Iu, nu, 0, kKD);
-#pragma unroll
-      for (int nt = 0; nt < NTU; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) a1[0][nt][e] = p.scale * a1[0][nt][e] + a2[0][nt][e];
-      store_acc(sDD, CF::LDV, a1, 16 * Iu, nu);
-    }
-    __syncthreads();
-
-    // dS <- Diag(2^g_L) dS + Diag(fr) (scale Qr^T dO - W0^T ddelta)
-    {
-      float a1[1][4][4], a2[1][4][4];
-      zero_acc(a1);
-      zero_acc(a2);
-      wgemm<1, 4, false, false>(a1, ch.Qr, CF::LDK, sdO, CF::LDV, sm0, sn0, 0, C);
-      wgemm<1, 4, false, false>(a2, sW, CF::LDK, sDD, CF::LDV, sm0, sn0, 0, C);
-      for_acc<1, 4>(sm0, sn0, [&](int, int nt, int e, int row, int) {
-        dS[0][nt][e] = ch.gL[row] * dS[0][nt][e] + ch.fr[row] * (p.scale * a1[0][nt][e] - a2[0][nt][e]);
-      });
-    }
-  }
-  if (p.dS0) {
-    for_acc<1, 4>(sm0, sn0, [&](int, int nt, int e, int row, int col) {
-      p.dS0[((size_t)bh * kKD + row) * kVD + v0 + col] = dS[0][nt][e];
-    });
-  }
-}
-
-// ---------------------------------------------------------------------------
-// 2. chunk-parallel gradients
-// ---------------------------------------------------------------------------
 template <class CF>
 struct ChunkLayout {
   static constexpr size_t sz = sizeof(typename CF::OpT);
@@ -247,11 +288,10 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_kernel(ScanParams p) {
   char* base = CF::F32 ? p.dbg + (size_t)(blockIdx.y * gridDim.x + blockIdx.x) * p.dbg_stride : smem;
 
   Chunk<CF> ch;
-  ch.q = reinterpret_cast<bf16*>(base + Lo::q);
-  ch.k = reinterpret_cast<bf16*>(base + Lo::k);
-  ch.g = reinterpret_cast<float*>(base + Lo::g);
-  ch.kap = reinterpret_cast<float*>(base + Lo::kap);
-  ch.beta = ch.kap;
+  bf16* rq_ = reinterpret_cast<bf16*>(base + Lo::q);
+  bf16* rk_ = reinterpret_cast<bf16*>(base + Lo::k);
+  float* rg_ = reinterpret_cast<float*>(base + Lo::g);
+  float* rkap_ = reinterpret_cast<float*>(base + Lo::kap);
   ch.Kr = reinterpret_cast<OpT*>(base + Lo::Kr);
   ch.Qr = reinterpret_cast<OpT*>(base + Lo::Qr);
   ch.Kc = reinterpret_cast<OpT*>(base + Lo::Kc);
@@ -285,15 +325,16 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_kernel(ScanParams p) {
   const size_t cc = (size_t)bh * p.NT + c;
   ch.L = L;
 
-  load_raw(ch, p, b, h, t0, L);
-  load_cc<CF>(sTb, static_cast<const OpT*>(p.Tsave) + cc * C * C);
-  load_cc<CF>(sQb, static_cast<const OpT*>(p.Qsave) + cc * C * C);
+  load_raw(ch, rq_, rk_, rg_, rkap_, p, b, h, t0, L);
+  const char* rec = static_cast<const char*>(p.rec) + cc * Rec<CF>::bytes;
+  copy_block<CF>(sTb, rec + Rec<CF>::T, Rec<CF>::Q - Rec<CF>::T);
+  copy_block<CF>(sQb, rec + Rec<CF>::Q, Rec<CF>::F - Rec<CF>::Q);
   if constexpr (!CF::F32) {
     cp_async_commit();
     cp_async_wait_all();
   }
   __syncthreads();
-  prep_chunk(ch);
+  prep_chunk<CF, 512>(ch);
   for (int e = threadIdx.x; e < 2 * kKD + 3 * C; e += blockDim.x) cfl[e] = 0.f;
   __syncthreads();
 
@@ -323,8 +364,8 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_kernel(ScanParams p) {
   zero_acc(aDQ);
   zero_acc(aDT);
   const int Iv = warp / NJV, nv = (warp % NJV) * 8 * NTV;
-  const OpT* hsrc = static_cast<const OpT*>(p.h) + cc * kKD * kVD;
-  const OpT* dhsrc = static_cast<const OpT*>(p.dh) + cc * kKD * kVD;
+  const char* hsrc = static_cast<const char*>(p.h) + cc * (kVD / kBV) * state_block_bytes<CF>();
+  const char* dhsrc = static_cast<const char*>(p.dh) + cc * (kVD / kBV) * state_block_bytes<CF>();
 
   for (int vh = 0; vh < kVD / kBV; ++vh) {
     const int v0 = vh * kBV;
@@ -336,30 +377,23 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_kernel(ScanParams p) {
       copy_rows<!CF::F32>(dOst, kBV * 4, static_cast<const float*>(p.dO) + r0 * kVD + v0, (size_t)p.H * kVD * 4, C, L,
                           kBV * 4);
     }
-    copy_rows<!CF::F32>(sS0, CF::LDV * sizeof(OpT), hsrc + v0, kVD * sizeof(OpT), kKD, kKD, kBV * sizeof(OpT));
-    copy_rows<!CF::F32>(sdS, CF::LDV * sizeof(OpT), dhsrc + v0, kVD * sizeof(OpT), kKD, kKD, kBV * sizeof(OpT));
+    copy_block<CF>(sS0, hsrc + vh * state_block_bytes<CF>(), state_block_bytes<CF>());
+    copy_block<CF>(sdS, dhsrc + vh * state_block_bytes<CF>(), state_block_bytes<CF>());
     if constexpr (!CF::F32) {
       cp_async_commit();
       cp_async_wait_all();
     }
     __syncthreads();
     if constexpr (!CF::ISO) convert_dO<CF>(sdO, dOst);
-    // S0' = fr S0, dS'' = fL dS, and cgl += sum_v S0' dS''  (8 threads per state row)
+    // cgl += sum_v S0' dS''  (8 threads per state row)
     for (int grp = threadIdx.x; grp < kKD * (kBV / 8); grp += blockDim.x) {
       const int row = grp >> 3, c8 = (grp & 7) * 8;
       float s0[8], ds[8];
       ld8(s0, sS0 + row * CF::LDV + c8);
       ld8(ds, sdS + row * CF::LDV + c8);
-      const float fr = ch.fr[row], fl = ch.fL[row];
       float acc = 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        s0[i] *= fr;
-        ds[i] *= fl;
-        acc = fmaf(s0[i], ds[i], acc);
-      }
-      st8(sS0 + row * CF::LDV + c8, s0);
-      st8(sdS + row * CF::LDV + c8, ds);
+      for (int i = 0; i < 8; ++i) acc = fmaf(s0[i], ds[i], acc);
       acc += __shfl_xor_sync(0xffffffffu, acc, 1);
       acc += __shfl_xor_sync(0xffffffffu, acc, 2);
       acc += __shfl_xor_sync(0xffffffffu, acc, 4);
@@ -408,7 +442,7 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_kernel(ScanParams p) {
   }
 
   // the raw inputs again, for the final gate mapping (overlaps the post-loop products)
-  load_raw(ch, p, b, h, t0, L);
+  load_raw(ch, rq_, rk_, rg_, rkap_, p, b, h, t0, L);
   if constexpr (!CF::F32) cp_async_commit();
 
   // cfl[c] = sum_j Kc_jc (delta dS''^T)_jc: the fL cotangent of the last row
@@ -659,7 +693,7 @@ int launch_bwd(const ScanParams& p, cudaStream_t st) {
       return check_launch("cudaFuncSetAttribute(scan_bwd_chunk_kernel)");
     configured = true;
   }
-  scan_bwd_state_kernel<CF><<<dim3(kVD / kBV, p.B * p.H), kSeqThreads, s1, st>>>(p);
+  scan_bwd_state_kernel<CF><<<dim3(kVD / kBV, p.B * p.H), CF::F32 ? kSeqThreads : kSeqThreads + 32, s1, st>>>(p);
   int rc = check_launch("scan_bwd_state_kernel");
   if (rc != KDN_OK) return rc;
   scan_bwd_chunk_kernel<CF><<<dim3(p.NT, p.B * p.H), 512, s2, st>>>(p);

@@ -1,0 +1,131 @@
+// Chunk-parallel first pass of the chunked KDN memory scan: everything a
+// chunk needs that does not depend on the running state.  One CTA per
+// (chunk, b*h), two CTAs per SM; the raw rows come straight from HBM.
+//   q, k, g, kappa|beta -> gated operands Kr, Qr, Kc (reference rho, exact
+//   path for wide gate ranges) -> A = Kr Kc^T, Q = Qr Kc^T (tensor cores)
+//   -> T = (I + A)^-1 -> W0 = T Kr
+// and writes the chunk record (Qr, Kc, W0, T, Q, fr, fL, 2^g_L) with bulk
+// copies from shared memory.  The sequential forward and reverse passes then
+// only carry the state.  Replaces the intra-chunk half of
+// _chunk_kda_fwd_precum (lit_gpt/kdn_ops/iso_kdn_chunk.py:2037-2086, the
+// scaled-dot-kkt / solve-tril / recompute-w-u stages of the FLA pipeline it
+// calls) and of _diag_kdn_memory_forward (diag_kdn_chunk.py:3224-3245).
+#include "kdn_scan.cuh"
+
+namespace kdn {
+
+constexpr int kPrepThreads = 256;
+
+template <class CF>
+struct PrepLayout {
+  static constexpr size_t sz = sizeof(typename CF::OpT);
+  static constexpr int C = CF::C;
+  static constexpr size_t Kr = 0;  // holds W0 = T Kr at the end
+  static constexpr size_t Qr = Kr + A128((size_t)C * CF::LDK * sz);
+  static constexpr size_t Kc = Qr + A128((size_t)C * CF::LDK * sz);
+  static constexpr size_t Tb = Kc + A128((size_t)C * CF::LDK * sz);
+  static constexpr size_t Qb = Tb + A128((size_t)C * CF::LDC * sz);
+  static constexpr size_t Xb = Qb + A128((size_t)C * CF::LDC * sz);
+  static constexpr size_t Ab = Xb + A128((size_t)C * CF::LDC * sz);
+  static constexpr size_t As = Ab + A128((size_t)C * CF::LDC * sz);
+  static constexpr size_t small = As + A128((size_t)C * CF::LDA * 4);
+  static constexpr size_t bytes = small + A128(small_floats<CF>() * 4);
+};
+
+template <class CF>
+__global__ void __launch_bounds__(kPrepThreads, 2) scan_prep_kernel(ScanParams p) {
+  using OpT = typename CF::OpT;
+  using Lo = PrepLayout<CF>;
+  using R = Rec<CF>;
+  constexpr int C = CF::C;
+  constexpr int NJ = (kPrepThreads / 32) / (C / 16);  // warps per 16-row block of W0
+  constexpr int NTW = kKD / (8 * NJ);
+  extern __shared__ __align__(128) char smem[];
+  char* base = CF::F32 ? p.dbg + (size_t)(blockIdx.y * gridDim.x + blockIdx.x) * p.dbg_stride : smem;
+
+  const int c = blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
+  const int warp = threadIdx.x >> 5;
+  const int t0 = c * C;
+  const size_t cc = (size_t)bh * p.NT + c;
+
+  Chunk<CF> ch;
+  bind_raw_global(ch, p, b, h, t0);
+  ch.L = min(C, p.T - t0);
+  float* small = reinterpret_cast<float*>(base + Lo::small);
+  bind_small(ch, small);
+  ch.Kr = reinterpret_cast<OpT*>(base + Lo::Kr);
+  ch.Qr = reinterpret_cast<OpT*>(base + Lo::Qr);
+  ch.Kc = reinterpret_cast<OpT*>(base + Lo::Kc);
+  OpT* sTb = reinterpret_cast<OpT*>(base + Lo::Tb);
+  OpT* sQb = reinterpret_cast<OpT*>(base + Lo::Qb);
+  OpT* sXb = reinterpret_cast<OpT*>(base + Lo::Xb);
+  OpT* sAb = reinterpret_cast<OpT*>(base + Lo::Ab);
+  float* sA = reinterpret_cast<float*>(base + Lo::As);
+
+  zero_upper_blocks<CF>(sQb);
+  zero_upper_blocks<CF>(sTb);
+  prep_chunk<CF, kPrepThreads>(ch);
+  __syncthreads();
+  chunk_scores(ch, sA, sAb, sQb);
+  chunk_solve<CF>(sA, sAb, sTb, sXb);
+
+  // W0 = T Kr, written over Kr once every warp has read it
+  {
+    const int I = warp / NJ, n0 = (warp % NJ) * 8 * NTW;
+    float acc[1][NTW][4];
+    zero_acc(acc);
+    wgemm<1, NTW, true, false>(acc, sTb, CF::LDC, ch.Kr, CF::LDK, 16 * I, n0, 0, 16 * (I + 1));
+    __syncthreads();
+    store_acc(ch.Kr, CF::LDK, acc, 16 * I, n0);
+  }
+
+  char* rec = static_cast<char*>(p.rec) + cc * R::bytes;
+  const char* src[6] = {base + Lo::Qr, base + Lo::Kc, base + Lo::Kr, base + Lo::Tb, base + Lo::Qb,
+                        reinterpret_cast<const char*>(ch.fr)};
+  const size_t dst[6] = {R::Qr, R::Kc, R::W0, R::T, R::Q, R::F};
+  const size_t len[6] = {R::Kc - R::Qr, R::W0 - R::Kc, R::T - R::W0, R::Q - R::T, R::F - R::Q, 3 * kKD * 4};
+  if constexpr (CF::F32) {
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 6; ++i)
+      for (size_t o = (size_t)threadIdx.x * 16; o < len[i]; o += (size_t)blockDim.x * 16)
+        *reinterpret_cast<int4*>(rec + dst[i] + o) = *reinterpret_cast<const int4*>(src[i] + o);
+  } else {
+    fence_async_shared();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+#pragma unroll
+      for (int i = 0; i < 6; ++i) bulk_s2g(rec + dst[i], src[i], (unsigned)len[i]);
+      bulk_commit();
+      bulk_wait_all();
+    }
+  }
+}
+
+template <class CF>
+size_t prep_dbg_bytes() {
+  return CF::F32 ? PrepLayout<CF>::bytes : 0;
+}
+
+template <class CF>
+int launch_prep(const ScanParams& p, cudaStream_t st) {
+  const size_t smem = CF::F32 ? 0 : PrepLayout<CF>::bytes;
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(scan_prep_kernel<CF>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
+      return check_launch("cudaFuncSetAttribute(scan_prep_kernel)");
+    configured = true;
+  }
+  scan_prep_kernel<CF><<<dim3(p.NT, p.B * p.H), kPrepThreads, smem, st>>>(p);
+  return check_launch("scan_prep_kernel");
+}
+
+template int launch_prep<Cfg<true, 64, bf16>>(const ScanParams&, cudaStream_t);
+template int launch_prep<Cfg<true, 64, float>>(const ScanParams&, cudaStream_t);
+template int launch_prep<Cfg<false, 32, bf16>>(const ScanParams&, cudaStream_t);
+template int launch_prep<Cfg<false, 32, float>>(const ScanParams&, cudaStream_t);
+template size_t prep_dbg_bytes<Cfg<true, 64, float>>();
+template size_t prep_dbg_bytes<Cfg<false, 32, float>>();
+
+}  // namespace kdn
