@@ -329,6 +329,11 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::); }
+// All but the newest N committed cp.async groups have landed.
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
 
 // Copy `rows` rows of `row_bytes` (multiple of 16) from a strided global
 // source into a padded destination.  Rows >= valid are zero-filled.  `smem`

@@ -239,38 +239,49 @@ template <class CF>
 struct ChunkLayout {
   static constexpr size_t sz = sizeof(typename CF::OpT);
   static constexpr int C = CF::C;
-  // raw inputs
+  static constexpr int LDO = kKD + 8;  // fp32 gradient pitch: conflict-free pair stores
+  // raw inputs (fetched a second time after the value loop, for the gate mapping)
   static constexpr size_t q = 0;
   static constexpr size_t k = q + A128((size_t)C * kKD * 2);
   static constexpr size_t g = k + A128((size_t)C * kKD * 2);
   static constexpr size_t kap = g + A128((size_t)C * kKD * 4);
   static constexpr size_t raw_end = kap + A128(CF::ISO ? (size_t)C * 4 : (size_t)C * kKD * 4);
-  // value-half loop (aliases the raw inputs)
-  static constexpr size_t v = 0;
-  static constexpr size_t dO = v + A128((size_t)C * CF::LDV * sz);
-  static constexpr size_t Del = dO + A128((size_t)C * CF::LDV * sz);
+  // one value half: v, dO [C][LDV]; S0', dS'' [KD][LDV]; diag fp32 dO staging
+  static constexpr size_t hv = 0;
+  static constexpr size_t hdO = hv + A128((size_t)C * CF::LDV * sz);
+  static constexpr size_t hS0 = hdO + A128((size_t)C * CF::LDV * sz);
+  static constexpr size_t hdS = hS0 + state_block_bytes<CF>();
+  static constexpr size_t hdOst = hdS + state_block_bytes<CF>();
+  static constexpr size_t half_bytes = hdOst + A128(CF::ISO ? 16 : (size_t)C * kBV * 4);
+  // region 1: the raw inputs, or the second value half next to delta and ddelta
+  static constexpr size_t setA = 0;
+  static constexpr size_t Del = setA + half_bytes;
   static constexpr size_t DD = Del + A128((size_t)C * CF::LDV * sz);
-  static constexpr size_t S0 = DD + A128((size_t)C * CF::LDV * sz);
-  static constexpr size_t dS = S0 + A128((size_t)kKD * CF::LDV * sz);
-  static constexpr size_t dOst = dS + A128((size_t)kKD * CF::LDV * sz);  // diag fp32 dO staging
-  static constexpr size_t loop_end = dOst + A128(CF::ISO ? 16 : (size_t)C * kBV * 4);
-  // after the loop (aliases the loop buffers): the raw inputs are fetched
-  // again into [0, raw_end) for the final gate mapping, next to these
-  static constexpr size_t dW = raw_end;
+  static constexpr size_t r1_end = cmax(raw_end, DD + A128((size_t)C * CF::LDV * sz));
+  // region 2: the first value half, or after the loop the post-loop buffers
+  // (dA and dQ first: the exact path of the gate mapping still reads them)
+  static constexpr size_t setB = r1_end;
+  static constexpr size_t dA = r1_end;
+  static constexpr size_t dQ = dA + A128((size_t)C * CF::LDC * sz);
+  static constexpr size_t dW = dQ + A128((size_t)C * CF::LDC * sz);
   static constexpr size_t dT = dW + A128((size_t)C * CF::LDK * sz);
   static constexpr size_t X = dT + A128((size_t)C * CF::LDC * sz);
-  static constexpr size_t dA = X + A128((size_t)C * CF::LDC * sz);
-  static constexpr size_t dQ = dA + A128((size_t)C * CF::LDC * sz);
-  static constexpr size_t post_end = dQ + A128((size_t)C * CF::LDC * sz);
-  static constexpr size_t Kr = cmax(loop_end, post_end);
+  static constexpr size_t r2_end = cmax(setB + half_bytes, X + A128((size_t)C * CF::LDC * sz));
+  static constexpr size_t Kr = r2_end;
   static constexpr size_t Qr = Kr + A128((size_t)C * CF::LDK * sz);
   static constexpr size_t Kc = Qr + A128((size_t)C * CF::LDK * sz);
   static constexpr size_t Tb = Kc + A128((size_t)C * CF::LDK * sz);
   static constexpr size_t Qb = Tb + A128((size_t)C * CF::LDC * sz);
   static constexpr size_t W = Qb + A128((size_t)C * CF::LDC * sz);
   static constexpr size_t small = W + A128((size_t)C * CF::LDK * sz);
-  // small: chunk scalars, cfl[KD], cgl[KD], rows: dbeta, dotk, dotq [C]
-  static constexpr size_t bytes = small + A128((small_floats<CF>() + 2 * kKD + 3 * C) * 4);
+  // small: chunk scalars, cfl[KD], cgl[KD]
+  static constexpr size_t bytes = small + A128((small_floats<CF>() + 2 * kKD) * 4);
+  // fp32 gradient operands of the gate mapping (over dW .. W, dead by then)
+  static constexpr size_t xk = dW;  // dKr [C][LDO]
+  static constexpr size_t xq = xk + A128((size_t)C * LDO * 4);
+  static constexpr size_t xc = xq + A128((size_t)C * LDO * 4);
+  static constexpr size_t x_end = xc + A128((size_t)C * LDO * 4);
+  static_assert(x_end <= small, "gradient operands fit in the dead operand buffers");
 };
 
 template <class CF>
@@ -299,16 +310,8 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_kernel(ScanParams p) {
   bind_small(ch, small);
   float* cfl = small + small_floats<CF>();
   float* cgl = cfl + kKD;
-  float* rbeta = cgl + kKD;
-  float* rdotk = rbeta + C;
-  float* rdotq = rdotk + C;
-  OpT* sv = reinterpret_cast<OpT*>(base + Lo::v);
-  OpT* sdO = reinterpret_cast<OpT*>(base + Lo::dO);
   OpT* sDel = reinterpret_cast<OpT*>(base + Lo::Del);
   OpT* sDD = reinterpret_cast<OpT*>(base + Lo::DD);
-  OpT* sS0 = reinterpret_cast<OpT*>(base + Lo::S0);
-  OpT* sdS = reinterpret_cast<OpT*>(base + Lo::dS);
-  float* dOst = reinterpret_cast<float*>(base + Lo::dOst);
   OpT* sdW = reinterpret_cast<OpT*>(base + Lo::dW);
   OpT* sdT = reinterpret_cast<OpT*>(base + Lo::dT);
   OpT* sX = reinterpret_cast<OpT*>(base + Lo::X);
@@ -325,18 +328,43 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_kernel(ScanParams p) {
   const size_t cc = (size_t)bh * p.NT + c;
   ch.L = L;
 
+  const char* hsrc = static_cast<const char*>(p.h) + cc * (kVD / kBV) * state_block_bytes<CF>();
+  const char* dhsrc = static_cast<const char*>(p.dh) + cc * (kVD / kBV) * state_block_bytes<CF>();
+  // value half vh: the first in region 2, the second over the consumed raw inputs
+  auto half_base = [&](int vh) { return base + (vh == 0 ? Lo::setB : Lo::setA); };
+  auto issue_half = [&](int vh) {
+    char* hb = half_base(vh);
+    const int v0 = vh * kBV;
+    const size_t r0 = tok_row(p, b, h, t0);
+    load_tile_op<CF>(reinterpret_cast<OpT*>(hb + Lo::hv), CF::LDV, p.v + r0 * kVD + v0, (size_t)p.H * kVD, C, L,
+                     kBV);
+    if constexpr (CF::ISO) {
+      load_tile_op<CF>(reinterpret_cast<OpT*>(hb + Lo::hdO), CF::LDV, static_cast<const bf16*>(p.dO) + r0 * kVD + v0,
+                       (size_t)p.H * kVD, C, L, kBV);
+    } else {
+      copy_rows<!CF::F32>(hb + Lo::hdOst, kBV * 4, static_cast<const float*>(p.dO) + r0 * kVD + v0,
+                          (size_t)p.H * kVD * 4, C, L, kBV * 4);
+    }
+    copy_block<CF>(hb + Lo::hS0, hsrc + vh * state_block_bytes<CF>(), state_block_bytes<CF>());
+    copy_block<CF>(hb + Lo::hdS, dhsrc + vh * state_block_bytes<CF>(), state_block_bytes<CF>());
+  };
+
   load_raw(ch, rq_, rk_, rg_, rkap_, p, b, h, t0, L);
   const char* rec = static_cast<const char*>(p.rec) + cc * Rec<CF>::bytes;
   copy_block<CF>(sTb, rec + Rec<CF>::T, Rec<CF>::Q - Rec<CF>::T);
   copy_block<CF>(sQb, rec + Rec<CF>::Q, Rec<CF>::F - Rec<CF>::Q);
+  if constexpr (!CF::F32) cp_async_commit();
+  issue_half(0);
   if constexpr (!CF::F32) {
     cp_async_commit();
-    cp_async_wait_all();
+    cp_async_wait_group<1>();  // raw inputs, T and Q
   }
   __syncthreads();
   prep_chunk<CF, 512>(ch);
-  for (int e = threadIdx.x; e < 2 * kKD + 3 * C; e += blockDim.x) cfl[e] = 0.f;
+  for (int e = threadIdx.x; e < 2 * kKD; e += blockDim.x) cfl[e] = 0.f;
   __syncthreads();
+  issue_half(1);  // the raw inputs are consumed
+  if constexpr (!CF::F32) cp_async_commit();
 
   // W0 = T Kr
   const int I = warp / NJK, n0 = (warp % NJK) * 8 * NTK;
@@ -364,24 +392,21 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_kernel(ScanParams p) {
   zero_acc(aDQ);
   zero_acc(aDT);
   const int Iv = warp / NJV, nv = (warp % NJV) * 8 * NTV;
-  const char* hsrc = static_cast<const char*>(p.h) + cc * (kVD / kBV) * state_block_bytes<CF>();
-  const char* dhsrc = static_cast<const char*>(p.dh) + cc * (kVD / kBV) * state_block_bytes<CF>();
 
   for (int vh = 0; vh < kVD / kBV; ++vh) {
     const int v0 = vh * kBV;
-    const size_t r0 = tok_row(p, b, h, t0);
-    load_tile_op<CF>(sv, CF::LDV, p.v + r0 * kVD + v0, (size_t)p.H * kVD, C, L, kBV);
-    if constexpr (CF::ISO) {
-      load_tile_op<CF>(sdO, CF::LDV, static_cast<const bf16*>(p.dO) + r0 * kVD + v0, (size_t)p.H * kVD, C, L, kBV);
-    } else {
-      copy_rows<!CF::F32>(dOst, kBV * 4, static_cast<const float*>(p.dO) + r0 * kVD + v0, (size_t)p.H * kVD * 4, C, L,
-                          kBV * 4);
-    }
-    copy_block<CF>(sS0, hsrc + vh * state_block_bytes<CF>(), state_block_bytes<CF>());
-    copy_block<CF>(sdS, dhsrc + vh * state_block_bytes<CF>(), state_block_bytes<CF>());
+    char* hb = half_base(vh);
+    OpT* sv = reinterpret_cast<OpT*>(hb + Lo::hv);
+    OpT* sdO = reinterpret_cast<OpT*>(hb + Lo::hdO);
+    OpT* sS0 = reinterpret_cast<OpT*>(hb + Lo::hS0);
+    OpT* sdS = reinterpret_cast<OpT*>(hb + Lo::hdS);
+    float* dOst = reinterpret_cast<float*>(hb + Lo::hdOst);
     if constexpr (!CF::F32) {
-      cp_async_commit();
-      cp_async_wait_all();
+      if (vh == 0) {
+        cp_async_wait_group<1>();
+      } else {
+        cp_async_wait_all();
+      }
     }
     __syncthreads();
     if constexpr (!CF::ISO) convert_dO<CF>(sdO, dOst);
@@ -527,145 +552,141 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_kernel(ScanParams p) {
     wgemm<1, NTK, false, false>(aKc, sdQ, CF::LDC, ch.Qr, CF::LDK, 16 * I, n0, 16 * I, C);
   }
 
-  // map back through the gate factors (two adjacent channels per step)
-  const int lane4 = lane & 3, gq = lane >> 2;
-  float rsum[2] = {0.f, 0.f};  // iso: dbeta partials of rows gq, gq+8
+  // dKr, dQr, dKc to shared memory (fp32, over the operand buffers, which every
+  // warp must be done with); one elementwise pass then maps them back through
+  // the gate factors, half a warp per row and 8 channels per thread, so row
+  // sums are half-warp shuffles and every store is a whole 16-byte granule.
+  __syncthreads();
+  constexpr int LDO = Lo::LDO;
+  float* sXk = reinterpret_cast<float*>(base + Lo::xk);
+  float* sXq = reinterpret_cast<float*>(base + Lo::xq);
+  float* sXc = reinterpret_cast<float*>(base + Lo::xc);
+  store_acc(sXk, LDO, aKr, 16 * I, n0);
+  store_acc(sXq, LDO, aQr, 16 * I, n0);
+  store_acc(sXc, LDO, aKc, 16 * I, n0);
+  __syncthreads();
+
+  const int c0 = (threadIdx.x & 15) * 8;
+#pragma unroll 1
+  for (int row = threadIdx.x >> 4; row < C; row += 512 / 16) {
+    const bool active = row < L;
+    const int r = active ? row : L - 1;  // inactive rows compute on a valid row and store nothing
+    float g8[8], k8[8], q8[8], dkh[8], dqh[8], dkap[8], dG[8];
+    ld8(g8, ch.g + r * kKD + c0);
+    ld8(k8, ch.k + r * kKD + c0);
+    ld8(q8, ch.q + r * kKD + c0);
+    ld8(dkh, sXk + r * LDO + c0);
+    ld8(dqh, sXq + r * LDO + c0);
+    ld8(dkap, sXc + r * LDO + c0);
+    float be = 1.f, rk = 1.f, rq = 1.f;
+    if constexpr (CF::ISO) {
+      be = ch.beta[r];
+      rk = ch.rk[r];
+      rq = ch.rq[r];
 #pragma unroll
-  for (int nt = 0; nt < NTK; ++nt)
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      const int row = 16 * I + gq + 8 * hh, col = n0 + nt * 8 + 2 * lane4;
-      if (row >= L) continue;
-      const float2 g2 = *reinterpret_cast<const float2*>(ch.g + row * kKD + col);
-      const float2 k2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(ch.k + row * kKD + col));
-      const float2 q2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(ch.q + row * kKD + col));
-      float kh[2] = {k2.x, k2.y}, qh[2] = {q2.x, q2.y}, gi[2] = {g2.x, g2.y}, kap[2];
-      if constexpr (CF::ISO) {
-        const float rk = ch.rk[row], rq = ch.rq[row], be = ch.beta[row];
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          kh[u] *= rk;
-          qh[u] *= rq;
-          kap[u] = be * kh[u];
-        }
-      } else {
-        const float2 c2 = *reinterpret_cast<const float2*>(ch.kap + row * kKD + col);
-        kap[0] = c2.x;
-        kap[1] = c2.y;
+      for (int i = 0; i < 8; ++i) {
+        k8[i] *= rk;  // k_hat, q_hat
+        q8[i] *= rq;
       }
-      float dkh[2], dqh[2], dkap[2], dG[2];
+    }
+    float kap8[8];
+    if constexpr (CF::ISO) {
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int cu = col + u;
-        const float rr = ch.fast ? ch.gmid[cu] : 0.f;
-        const float rc = ch.fast ? ch.gmid[cu] : ch.glast[cu];
-        const float er = ex2a(gi[u] - rr), ec = ex2a(rc - gi[u]);
-        const float xk = aKr[0][nt][2 * hh + u], xq = aQr[0][nt][2 * hh + u], xc = aKc[0][nt][2 * hh + u];
-        dkh[u] = xk * er;
-        dqh[u] = xq * er;
-        dkap[u] = xc * ec;
-        dG[u] = xk * kh[u] * er + xq * qh[u] * er - xc * kap[u] * ec;
-        if (row == L - 1) dG[u] += cfl[cu] + cgl[cu] * ch.gL[cu] / (ch.fr[cu] * ch.fL[cu]);
-        if (!ch.fast) {
-          // exact gate factors for the score terms
-          for (int j = 0; j < L; ++j) {
-            const float gj = ch.g[j * kKD + cu];
-            const float khj = khat_at(ch, j, cu), qhj = qhat_at(ch, j, cu), kapj = kappa_at(ch, j, cu);
-            if (j <= row) {
-              const float f = ex2(gi[u] - gj);
-              const float dAij = j < row ? to_f(sdA[row * CF::LDC + j]) : 0.f;
-              const float dQij = to_f(sdQ[row * CF::LDC + j]);
-              dkh[u] = fmaf(dAij * kapj, f, dkh[u]);
-              dqh[u] = fmaf(dQij * kapj, f, dqh[u]);
-              dG[u] = fmaf((dAij * kh[u] + dQij * qh[u]) * kapj, f, dG[u]);
-            }
-            if (j >= row) {
-              const float f = ex2(gj - gi[u]);
-              const float dAji = j > row ? to_f(sdA[j * CF::LDC + row]) : 0.f;
-              const float dQji = to_f(sdQ[j * CF::LDC + row]);
-              const float w = (dAji * khj + dQji * qhj) * f;
-              dkap[u] += w;
-              dG[u] -= w * kap[u];
-            }
+      for (int i = 0; i < 8; ++i) kap8[i] = be * k8[i];
+    } else {
+      ld8(kap8, ch.kap + r * kKD + c0);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int cu = c0 + i;
+      const float rr = ch.fast ? ch.gmid[cu] : 0.f;
+      const float rc = ch.fast ? ch.gmid[cu] : ch.glast[cu];
+      const float er = ex2a(g8[i] - rr), ec = ex2a(rc - g8[i]);
+      const float xk = dkh[i], xq = dqh[i], xc = dkap[i];
+      dkh[i] = xk * er;
+      dqh[i] = xq * er;
+      dkap[i] = xc * ec;
+      dG[i] = xk * k8[i] * er + xq * q8[i] * er - xc * kap8[i] * ec;
+      if (r == L - 1) dG[i] += cfl[cu] + cgl[cu] * ch.gL[cu] / (ch.fr[cu] * ch.fL[cu]);
+    }
+    if (!ch.fast) {
+      // exact gate factors for the score terms
+#pragma unroll 1
+      for (int j = 0; j < L; ++j) {
+        float gj[8], kj[8], qj[8], cj[8];
+        ld8(gj, ch.g + j * kKD + c0);
+        ld8(kj, ch.k + j * kKD + c0);
+        ld8(qj, ch.q + j * kKD + c0);
+        if constexpr (CF::ISO) {
+          const float rkj = ch.rk[j], rqj = ch.rq[j], bj = ch.beta[j];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            kj[i] *= rkj;
+            qj[i] *= rqj;
+            cj[i] = bj * kj[i];
+          }
+        } else {
+          ld8(cj, ch.kap + j * kKD + c0);
+        }
+        const float dAij = j < r ? to_f(sdA[r * CF::LDC + j]) : 0.f;
+        const float dQij = j <= r ? to_f(sdQ[r * CF::LDC + j]) : 0.f;
+        const float dAji = j > r ? to_f(sdA[j * CF::LDC + r]) : 0.f;
+        const float dQji = j >= r ? to_f(sdQ[j * CF::LDC + r]) : 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          if (j <= r) {
+            const float f = ex2(g8[i] - gj[i]);
+            dkh[i] = fmaf(dAij * cj[i], f, dkh[i]);
+            dqh[i] = fmaf(dQij * cj[i], f, dqh[i]);
+            dG[i] = fmaf((dAij * k8[i] + dQij * q8[i]) * cj[i], f, dG[i]);
+          }
+          if (j >= r) {
+            const float f = ex2(gj[i] - g8[i]);
+            const float w = (dAji * kj[i] + dQji * qj[i]) * f;
+            dkap[i] += w;
+            dG[i] -= w * kap8[i];
           }
         }
       }
-      const size_t off = tok_row(p, b, h, t0 + row) * kKD + col;
-      st_pair(p.dg + off, dG[0], dG[1]);
-      if constexpr (CF::ISO) {
-        const float be = ch.beta[row];
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          rsum[hh] += dkap[u] * kh[u];  // dbeta_i = sum_c dkappa_ic k_hat_ic
-          dkh[u] += be * dkap[u];       // kappa = beta k_hat
-        }
-      } else {
-        st_pair(p.dkappa + off, dkap[0], dkap[1]);
-      }
-      aKr[0][nt][2 * hh] = dkh[0];
-      aKr[0][nt][2 * hh + 1] = dkh[1];
-      aQr[0][nt][2 * hh] = dqh[0];
-      aQr[0][nt][2 * hh + 1] = dqh[1];
     }
-
-  if constexpr (CF::ISO) {
-    // row reductions: dbeta, <dk_hat, k_hat>, <dq_hat, q_hat>, then the L2-norm VJP
-    float dk_dot[2] = {0.f, 0.f}, dq_dot[2] = {0.f, 0.f};
+    const size_t off = tok_row(p, b, h, t0 + r) * kKD + c0;
+    if (active) st8(p.dg + off, dG);
+    if constexpr (CF::ISO) {
+      // kappa = beta k_hat: dbeta = <dkappa, k_hat>; then the L2-norm VJPs
+      float db = 0.f, dk_dot = 0.f, dq_dot = 0.f;
 #pragma unroll
-    for (int nt = 0; nt < NTK; ++nt)
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int row = 16 * I + gq + 8 * hh, col = n0 + nt * 8 + 2 * lane4;
-        if (row >= L) continue;
-        const float2 k2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(ch.k + row * kKD + col));
-        const float2 q2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(ch.q + row * kKD + col));
-        dk_dot[hh] += (aKr[0][nt][2 * hh] * k2.x + aKr[0][nt][2 * hh + 1] * k2.y) * ch.rk[row];
-        dq_dot[hh] += (aQr[0][nt][2 * hh] * q2.x + aQr[0][nt][2 * hh + 1] * q2.y) * ch.rq[row];
+      for (int i = 0; i < 8; ++i) {
+        db = fmaf(dkap[i], k8[i], db);
+        dkh[i] = fmaf(be, dkap[i], dkh[i]);
       }
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      float x0 = rsum[j], x1 = dk_dot[j], x2 = dq_dot[j];
-#pragma unroll
-      for (int o = 1; o < 4; o <<= 1) {
-        x0 += __shfl_xor_sync(0xffffffffu, x0, o);
-        x1 += __shfl_xor_sync(0xffffffffu, x1, o);
-        x2 += __shfl_xor_sync(0xffffffffu, x2, o);
+      for (int i = 0; i < 8; ++i) {
+        dk_dot = fmaf(dkh[i], k8[i], dk_dot);
+        dq_dot = fmaf(dqh[i], q8[i], dq_dot);
       }
-      if (lane4 == 0) {
-        const int row = 16 * I + gq + 8 * j;
-        atomicAdd(&rbeta[row], x0);
-        atomicAdd(&rdotk[row], x1);
-        atomicAdd(&rdotq[row], x2);
+#pragma unroll
+      for (int o = 1; o < 16; o <<= 1) {
+        db += __shfl_xor_sync(0xffffffffu, db, o);
+        dk_dot += __shfl_xor_sync(0xffffffffu, dk_dot, o);
+        dq_dot += __shfl_xor_sync(0xffffffffu, dq_dot, o);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        dkh[i] = rk * (dkh[i] - k8[i] * dk_dot);
+        dqh[i] = rq * (dqh[i] - q8[i] * dq_dot);
+      }
+      if (active) {
+        st8(p.dk + off, dkh);
+        st8(p.dq + off, dqh);
+        if (c0 == 0) p.dbeta[tok_row(p, b, h, t0 + r)] = db;
+      }
+    } else {
+      if (active) {
+        st8(p.dkappa + off, dkap);
+        st8(p.dk + off, dkh);
+        st8(p.dq + off, dqh);
       }
     }
-    __syncthreads();
-#pragma unroll
-    for (int nt = 0; nt < NTK; ++nt)
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int row = 16 * I + gq + 8 * hh, col = n0 + nt * 8 + 2 * lane4;
-        if (row >= L) continue;
-        const float2 k2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(ch.k + row * kKD + col));
-        const float2 q2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(ch.q + row * kKD + col));
-        const float rk = ch.rk[row], rq = ch.rq[row];
-        const size_t off = tok_row(p, b, h, t0 + row) * kKD + col;
-        st_pair(p.dk + off, rk * (aKr[0][nt][2 * hh] - k2.x * rk * rdotk[row]),
-                rk * (aKr[0][nt][2 * hh + 1] - k2.y * rk * rdotk[row]));
-        st_pair(p.dq + off, rq * (aQr[0][nt][2 * hh] - q2.x * rq * rdotq[row]),
-                rq * (aQr[0][nt][2 * hh + 1] - q2.y * rq * rdotq[row]));
-      }
-    for (int i = threadIdx.x; i < L; i += blockDim.x) p.dbeta[tok_row(p, b, h, t0 + i)] = rbeta[i];
-  } else {
-#pragma unroll
-    for (int nt = 0; nt < NTK; ++nt)
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int row = 16 * I + gq + 8 * hh, col = n0 + nt * 8 + 2 * lane4;
-        if (row >= L) continue;
-        const size_t off = tok_row(p, b, h, t0 + row) * kKD + col;
-        st_pair(p.dk + off, aKr[0][nt][2 * hh], aKr[0][nt][2 * hh + 1]);
-        st_pair(p.dq + off, aQr[0][nt][2 * hh], aQr[0][nt][2 * hh + 1]);
-      }
   }
 }
 
