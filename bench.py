@@ -158,7 +158,7 @@ def step_diag(x):
 
 GRAD_NAMES = {"iso": ("q", "k", "v", "g_cumsum", "a", "omega", "r"),
               "diag": ("q", "k", "v", "g_cumsum", "k_gain", "alpha", "omega_raw", "r_raw")}
-LAUNCHES_PER_STEP = {"iso": 5, "diag": 9}  # gain fwd 1|3, scan fwd 1, scan bwd 2, gain bwd 1|3
+LAUNCHES_PER_STEP = {"iso": 6, "diag": 10}  # gain fwd 1|3, scan fwd 2, scan bwd 2, gain bwd 1|3
 
 
 def time_region(fn, steps, device):
@@ -172,31 +172,52 @@ def time_region(fn, steps, device):
     return start.elapsed_time(stop) / steps
 
 
-def per_op_times(variant, x, device, reps=5):
-    """Average device time of each public op call, forward and backward."""
-    from kdn_b200 import _scan
-    from kdn_b200 import _native as N
+def per_op_times(variant, x, device, reps=10):
+    """Device time of the scan's two C-ABI calls, kdn_scan_fwd (chunk-record
+    pass + sequential pass) and kdn_scan_bwd (reverse state sweep +
+    chunk-parallel gradients), with every buffer allocated up front: CUDA
+    events on the stream the kernels are launched on."""
+    import ctypes
 
-    out = {}
+    from kdn_b200 import _native as N
+    from kdn_b200 import _scan
+
+    lib = N.load_library()
     if variant == "iso":
         from kdn_b200.iso_kdn_chunk import iso_kdn_gain
 
-        beta = iso_kdn_gain(x["a"], x["omega"], x["r"], x["prec"], head_dim=D)
-        args = (N.KDN_ISO, x["q"], x["k"], x["v"], x["g_cumsum"], beta, D ** -0.5)
-        o, _, saved = _scan.scan_forward(*args)
-        out["scan_fwd_ms"] = time_region(lambda: _scan.scan_forward(*args), reps, device)
-        out["scan_bwd_ms"] = time_region(lambda: _scan.scan_backward(*args, saved, x["dO"]), reps, device)
+        gate = iso_kdn_gain(x["a"], x["omega"], x["r"], x["prec"], head_dim=D).detach()
+        kind = N.KDN_ISO
     else:
         from kdn_b200.diag_kdn_chunk import _gain_forward
 
-        kappa, carry, _ = _gain_forward(x["k_gain"], x["alpha"], x["omega"], x["r"], x["prec"])
-        out["gain_fwd_ms"] = time_region(
-            lambda: _gain_forward(x["k_gain"], x["alpha"], x["omega"], x["r"], x["prec"]), reps, device)
-        args = (N.KDN_DIAG, x["q"], x["k"], x["v"], x["g_cumsum"], kappa, D ** -0.5)
-        o, _, saved = _scan.scan_forward(*args)
-        out["scan_fwd_ms"] = time_region(lambda: _scan.scan_forward(*args), reps, device)
-        out["scan_bwd_ms"] = time_region(lambda: _scan.scan_backward(*args, saved, x["dO"]), reps, device)
-    return out
+        gate = _gain_forward(x["k_gain"], x["alpha"], x["omega"], x["r"], x["prec"])[0]
+        kind = N.KDN_DIAG
+    q, k, v, g, dO = x["q"], x["k"], x["v"], x["g_cumsum"], x["dO"]
+    a = _scan._args(kind, N.precision(), q, v, D ** -0.5)
+    saved = N.byte_buffer(lib.kdn_scan_saved_bytes(ctypes.byref(a)), device)
+    ws = N.byte_buffer(lib.kdn_scan_workspace_bytes(ctypes.byref(a)), device)
+    o = torch.empty(v.shape, dtype=torch.bfloat16 if kind == N.KDN_ISO else torch.float32, device=device)
+    dq, dk, dv, dg, dgate = (torch.empty_like(t) for t in (q, k, v, g, gate))
+    a.q, a.k, a.v, a.g = q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr()
+    if kind == N.KDN_ISO:
+        a.beta, a.dbeta = gate.data_ptr(), dgate.data_ptr()
+    else:
+        a.kappa, a.dkappa = gate.data_ptr(), dgate.data_ptr()
+    a.o, a.saved, a.dO = o.data_ptr(), saved.data_ptr(), dO.data_ptr()
+    a.dq, a.dk, a.dv, a.dg = dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dg.data_ptr()
+    a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+    stream = N.stream_of(q)
+
+    def fwd():
+        N.check(lib.kdn_scan_fwd(ctypes.byref(a), stream), "kdn_scan_fwd")
+
+    def bwd():
+        N.check(lib.kdn_scan_bwd(ctypes.byref(a), stream), "kdn_scan_bwd")
+
+    fwd()
+    bwd()
+    return {"scan_fwd_ms": time_region(fwd, reps, device), "scan_bwd_ms": time_region(bwd, reps, device)}
 
 
 # ----------------------------------------------------------------------------- CPU baseline
@@ -247,7 +268,9 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--batch", type=int, default=B, help="sequences per GPU (profiling runs use smaller cases)")
     args = ap.parse_args()
+    globals()["B"] = args.batch
     warmup = max(args.warmup, 3)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -360,8 +383,8 @@ def main():
         "metric": METRIC, "value": value, "unit": "Mtok/s", "n_gpus": world, "steps": args.steps, "warmup": warmup,
         "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"{args.variant}_kdn gain+scan fwd+bwd B4 T4096 H18 d128 (config 1)" if args.variant == "iso"
-                   else "diag_kdn gain+scan fwd+bwd B4 T4096 H18 d128 (config 2)",
+        "config": {"workload": f"iso_kdn gain+scan fwd+bwd B{B} T{T} H{H} d{D} (config 1)" if args.variant == "iso"
+                   else f"diag_kdn gain+scan fwd+bwd B{B} T{T} H{H} d{D} (config 2)",
                    "global_batch": B * world, "seq_len": T, "heads": H, "head_dim": D,
                    "parallelism": f"batch-sharded x{world}", "l2": "inputs > L2 (no flush)"},
         "gpu_launches": LAUNCHES_PER_STEP[args.variant] * args.steps,

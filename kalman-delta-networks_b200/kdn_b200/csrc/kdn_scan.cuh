@@ -102,10 +102,41 @@ struct Rec {
   static_assert(Kc % 128 == 0 && T % 128 == 0 && F % 128 == 0, "16-byte aligned blocks");
 };
 
-// One value tile of a chunk's state (h, dh): [KD][LDV] OpT.
+// Tensor-core record (bf16 precision): tiles in the swizzled layout of
+// kdn_tc.cuh, with the chunk's scale factors folded in so that the
+// sequential passes carry the unscaled state:
+//   T, Qq = scale Q, Qt = scale Q^T               [C][64] (columns >= C unused)
+//   Qs = scale fr Qr,  Kf = fL Kc,  Wf = fr W0   [2][C][64] (64 keys per block)
+//   fr, fL, 2^g_L                                  [3][KD] fp32
+// The forward reads [0, fwd_end), the reverse sweep [bwd_begin, bytes).
+template <class CF>
+struct RecTc {
+  static constexpr int C = CF::C;
+  static constexpr size_t T = 0;
+  static constexpr size_t Qq = T + (size_t)C * 128;
+  static constexpr size_t Qs = Qq + (size_t)C * 128;
+  static constexpr size_t Kf = Qs + (size_t)C * 256;
+  static constexpr size_t Wf = Kf + (size_t)C * 256;
+  static constexpr size_t F = Wf + (size_t)C * 256;
+  static constexpr size_t Qt = F + align_up(3 * kKD * 4, 1024);
+  static constexpr size_t bytes = Qt + (size_t)C * 128;
+  static constexpr size_t fwd_end = Qt;
+  static constexpr size_t bwd_begin = Qs;
+  static_assert(bytes % 1024 == 0 && Qs % 1024 == 0, "1024-byte aligned tiles");
+};
+template <class CF>
+using RecOf = typename std::conditional<CF::F32, Rec<CF>, RecTc<CF>>::type;
+
+// One value tile of a chunk's state in shared memory (padded): [KD][LDV] OpT.
 template <class CF>
 __host__ __device__ constexpr size_t state_block_bytes() {
   return A128((size_t)kKD * CF::LDV * sizeof(typename CF::OpT));
+}
+// ... and in HBM (h, dh): the padded tile (fp32 precision, states scaled by
+// fr / fL) or the swizzled bf16 tile [KD][64] of the unscaled state.
+template <class CF>
+__host__ __device__ constexpr size_t hblock_bytes() {
+  return CF::F32 ? state_block_bytes<CF>() : (size_t)kKD * 64 * 2;
 }
 
 // Per-chunk views of the raw inputs (rows in shared memory or straight in

@@ -34,8 +34,8 @@ struct Sizes {
 
 template <class CF>
 void layout_sizes(Sizes* s) {
-  s->rec = align_up(Rec<CF>::bytes * s->BH * s->NT, 256);
-  s->h = align_up(state_block_bytes<CF>() * kVT * s->BH * s->NT, 256);
+  s->rec = align_up(RecOf<CF>::bytes * s->BH * s->NT, 256);
+  s->h = align_up(hblock_bytes<CF>() * kVT * s->BH * s->NT, 256);
   s->dh = s->h;
 }
 

@@ -22,6 +22,8 @@
 // Replaces _chunk_kda_bwd_precum (iso_kdn_chunk.py:2089-2187) and
 // _DiagKdnMemoryFunction.backward (diag_kdn_chunk.py:3258-3312).
 #include "kdn_scan.cuh"
+#include "kdn_tc.cuh"
+#include "kdn_tma.cuh"
 
 namespace kdn {
 
@@ -220,6 +222,185 @@ __global__ void __launch_bounds__(kSeqThreads + 32, 1) scan_bwd_state_kernel(Sca
     if (threadIdx.x == 32) bulk_wait_all();
 }
 
+// Tensor-core reverse sweep (bf16 precision): one CTA per (b, h) stream with
+// the 128 x 128 fp32 adjoint in TMEM; same roles as the tensor-core forward
+// (8 data warps, one MMA thread, one producer warp).  Per chunk, with the
+// record's folded factors (Qs = scale fr Qr, Kf = fL Kc, Wf = fr W0,
+// Qq = scale Q):
+//   dS -> bf16 operand (saved as dh);  dS <- 2^g_L dS           (TMEM ld / st)
+//   ddelta^T = dO^T Qq + dS^T Kf^T, Qq read as its transpose Qt (MMA, M = 128 values)
+//   dS += Qs^T dO - Wf^T ddelta                                  (MMA, M = 128 keys)
+template <class CF>
+struct StateTcLayout {
+  static constexpr int C = CF::C;
+  static constexpr int NS = CF::ISO ? 2 : 3;
+  static constexpr bool DF32 = !CF::ISO;  // the diagonal variant's cotangent arrives as fp32 rows
+  using R = RecTc<CF>;
+  static constexpr size_t rec = R::bytes - R::bwd_begin;  // the record from Qs on
+  static constexpr size_t dO = rec;  // iso: [2][C][64] bf16 swizzled; diag: [C][128] fp32
+  static constexpr size_t stage = align_up(dO + (size_t)C * (DF32 ? 512 : 256), 1024);
+  static constexpr size_t dOb = NS * stage;  // diag: the bf16-rounded operand [2][C][64]
+  static constexpr size_t DS = dOb + (DF32 ? align_up((size_t)C * 256, 1024) : 0);  // [2][KD][64] (also dh)
+  static constexpr size_t DD = DS + (size_t)kKD * 256;                               // ddelta [2][C][64]
+  static constexpr size_t bar = DD + align_up((size_t)C * 256, 1024);
+  static constexpr size_t bytes = bar + 128 + 1024;
+};
+
+template <class CF>
+__global__ void __launch_bounds__(kTcThreads, 1) scan_bwd_state_tc_kernel(ScanParams p,
+                                                                          const __grid_constant__ TcMaps maps) {
+  using Lo = StateTcLayout<CF>;
+  using R = RecTc<CF>;
+  constexpr int C = CF::C, NS = Lo::NS, HC = C / 2;
+  constexpr uint32_t TS = 0, TD = kKD;  // TMEM columns: adjoint, ddelta^T
+  constexpr int NTH = kTcWarps * 32;
+  extern __shared__ __align__(1024) char smem_raw[];
+  char* base = align1024(smem_raw);
+
+  const int bh = blockIdx.x, b = bh / p.H, h = bh - b * p.H;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const char* recs = static_cast<const char*>(p.rec) + (size_t)bh * p.NT * R::bytes;
+  char* dhout = static_cast<char*>(p.dh) + (size_t)bh * p.NT * 2 * hblock_bytes<CF>();
+  uint64_t* full = reinterpret_cast<uint64_t*>(base + Lo::bar);
+  uint64_t* empty = full + NS;
+  uint64_t* mmab = empty + NS;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(mmab + 1);
+  char* sDS = base + Lo::DS;
+  char* sDD = base + Lo::DD;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(mmab, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tc::alloc(tslot, 256);
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem = *tslot;
+
+  if (warp == kTcWarps) {
+    for (int it = 0; it < p.NT; ++it) {
+      const int s = it % NS, c = p.NT - 1 - it;
+      if (it >= NS) mbar_wait(&empty[s], (it / NS - 1) & 1, p.status);
+      if (lane == 0) {
+        char* st = base + s * Lo::stage;
+        mbar_expect_tx(&full[s], (unsigned)(Lo::rec + (size_t)C * (Lo::DF32 ? 512 : 256)));
+        bulk_g2s(st, recs + (size_t)c * R::bytes + R::bwd_begin, (unsigned)Lo::rec, &full[s]);
+        tma_load_4d(st + Lo::dO, &maps.in, 0, h, c * C, b, &full[s]);
+        if constexpr (!Lo::DF32) tma_load_4d(st + Lo::dO + C * 128, &maps.in, 64, h, c * C, b, &full[s]);
+      }
+      __syncwarp();
+    }
+    return;
+  }
+
+  const int q = warp & 3, hf = warp >> 2;
+  const int row = 32 * q + lane;
+  const uint32_t tl = tmem + ((uint32_t)(32 * q) << 16);
+  for (int j = 0; j < 64; j += 16) {
+    float x[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) x[i] = p.dST ? p.dST[((size_t)bh * kKD + row) * kVD + 64 * hf + j + i] : 0.f;
+    tc::st16(tl + TS + 64 * hf + j, x);
+  }
+  tc::wait_st();
+  uint32_t mph = 0;
+
+  for (int it = 0; it < p.NT; ++it) {
+    const int s = it % NS, c = p.NT - 1 - it;
+    char* st = base + s * Lo::stage;
+    char* sdO = Lo::DF32 ? base + Lo::dOb : st + Lo::dO;
+    mbar_wait(&full[s], (it / NS) & 1, p.status);
+    if constexpr (Lo::DF32) {
+      // the reference rounds the fp32 cotangent to bf16 first (diag_kdn_chunk.py:3277)
+      const float* src = reinterpret_cast<const float*>(st + Lo::dO);
+      for (int e = threadIdx.x; e < C * 16; e += NTH) {
+        const int r = e >> 4, g = e & 15;
+        float x[8];
+        ld8(x, src + r * kVD + 8 * g);
+        st8(reinterpret_cast<bf16*>(sdO + tc::sw_off(r, 8 * g, C)), x);
+      }
+    }
+    {
+      // adjoint operand (and dh), then dS <- 2^g_L dS
+      const float gl = reinterpret_cast<const float*>(st + (R::F - R::bwd_begin))[2 * kKD + row];
+#pragma unroll 1
+      for (int j = 0; j < 64; j += 16) {
+        float x[16];
+        tc::ld16(tl + TS + 64 * hf + j, x);
+        tc::st_row16(sDS, kKD, row, 64 * hf + j, x, 1.f);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) x[i] *= gl;
+        tc::st16(tl + TS + 64 * hf + j, x);
+      }
+      tc::wait_st();
+    }
+    fence_async_shared();
+    tc::fence_before();
+    bar_sync(1, NTH);
+    if (threadIdx.x == 32) {
+      bulk_s2g(dhout + (size_t)c * 2 * hblock_bytes<CF>(), sDS, (unsigned)(2 * hblock_bytes<CF>()));
+      bulk_commit();
+    }
+    if (threadIdx.x == 0) {
+      tc::fence_after();
+      constexpr uint32_t id2 = tc::idesc(128, C, true, false);
+      for (int ks = 0; ks < C / 16; ++ks)
+        tc::mma(tmem + TD, tc::desc_mn(sdO, C, ks), tc::desc_k(st + (R::Qt - R::bwd_begin), C, ks), id2, ks > 0);
+      for (int ks = 0; ks < kKD / 16; ++ks)
+        tc::mma(tmem + TD, tc::desc_mn(sDS, kKD, ks), tc::desc_k(st + (R::Kf - R::bwd_begin), C, ks), id2, true);
+      tc::commit(mmab);
+    }
+    mbar_wait(mmab, mph, p.status);
+    mph ^= 1;
+    tc::fence_after();
+#pragma unroll 1
+    for (int j = 0; j < HC; j += 16) {
+      float x[16];
+      tc::ld16(tl + TD + HC * hf + j, x);
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        *reinterpret_cast<bf16*>(sDD + tc::sw_off(HC * hf + j + i, row, C)) = __float2bfloat16_rn(x[i]);
+    }
+    if (threadIdx.x == 32) bulk_wait_read<0>();  // dh has left the adjoint operand (rewritten next chunk)
+    fence_async_shared();
+    tc::fence_before();
+    bar_sync(1, NTH);
+    if (threadIdx.x == 0) {
+      tc::fence_after();
+      constexpr uint32_t ids = tc::idesc(128, 128, true, true), idn = tc::idesc(128, 128, true, true, true);
+      for (int ks = 0; ks < C / 16; ++ks)
+        tc::mma(tmem + TS, tc::desc_mn(st + (R::Qs - R::bwd_begin), C, ks), tc::desc_mn(sdO, C, ks), ids, true);
+      for (int ks = 0; ks < C / 16; ++ks)
+        tc::mma(tmem + TS, tc::desc_mn(st + (R::Wf - R::bwd_begin), C, ks), tc::desc_mn(sDD, C, ks), idn, true);
+      tc::commit(&empty[s]);
+      tc::commit(mmab);
+    }
+    mbar_wait(mmab, mph, p.status);
+    mph ^= 1;
+    tc::fence_after();
+  }
+  if (p.dS0) {
+    for (int j = 0; j < 64; j += 16) {
+      float x[16];
+      tc::ld16(tl + TS + 64 * hf + j, x);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) p.dS0[((size_t)bh * kKD + row) * kVD + 64 * hf + j + i] = x[i];
+    }
+  }
+  if (threadIdx.x == 32) bulk_wait_all();
+  tc::fence_before();
+  bar_sync(1, NTH);
+  if (warp == 0) {
+    tc::fence_after();
+    tc::dealloc(tmem, 256);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // 2. chunk-parallel gradients
 // ---------------------------------------------------------------------------
@@ -328,8 +509,8 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_kernel(ScanParams p) {
   const size_t cc = (size_t)bh * p.NT + c;
   ch.L = L;
 
-  const char* hsrc = static_cast<const char*>(p.h) + cc * (kVD / kBV) * state_block_bytes<CF>();
-  const char* dhsrc = static_cast<const char*>(p.dh) + cc * (kVD / kBV) * state_block_bytes<CF>();
+  const char* hsrc = static_cast<const char*>(p.h) + cc * (kVD / kBV) * hblock_bytes<CF>();
+  const char* dhsrc = static_cast<const char*>(p.dh) + cc * (kVD / kBV) * hblock_bytes<CF>();
   // value half vh: the first in region 2, the second over the consumed raw inputs
   auto half_base = [&](int vh) { return base + (vh == 0 ? Lo::setB : Lo::setA); };
   auto issue_half = [&](int vh) {
@@ -345,14 +526,32 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_kernel(ScanParams p) {
       copy_rows<!CF::F32>(hb + Lo::hdOst, kBV * 4, static_cast<const float*>(p.dO) + r0 * kVD + v0,
                           (size_t)p.H * kVD * 4, C, L, kBV * 4);
     }
-    copy_block<CF>(hb + Lo::hS0, hsrc + vh * state_block_bytes<CF>(), state_block_bytes<CF>());
-    copy_block<CF>(hb + Lo::hdS, dhsrc + vh * state_block_bytes<CF>(), state_block_bytes<CF>());
+    if constexpr (CF::F32) {
+      copy_block<CF>(hb + Lo::hS0, hsrc + vh * hblock_bytes<CF>(), hblock_bytes<CF>());
+      copy_block<CF>(hb + Lo::hdS, dhsrc + vh * hblock_bytes<CF>(), hblock_bytes<CF>());
+    } else {
+      // swizzled [KD][64] state tiles into the padded operand rows
+      for (int e = threadIdx.x; e < 2 * kKD * 8; e += blockDim.x) {
+        const int m = e / (kKD * 8), r = (e >> 3) % kKD, g = e & 7;
+        cp_async16(reinterpret_cast<OpT*>(hb + (m == 0 ? Lo::hS0 : Lo::hdS)) + r * CF::LDV + 8 * g,
+                   (m == 0 ? hsrc : dhsrc) + vh * hblock_bytes<CF>() + tc::sw_off(r, 8 * g, kKD));
+      }
+    }
   };
 
   load_raw(ch, rq_, rk_, rg_, rkap_, p, b, h, t0, L);
-  const char* rec = static_cast<const char*>(p.rec) + cc * Rec<CF>::bytes;
-  copy_block<CF>(sTb, rec + Rec<CF>::T, Rec<CF>::Q - Rec<CF>::T);
-  copy_block<CF>(sQb, rec + Rec<CF>::Q, Rec<CF>::F - Rec<CF>::Q);
+  const char* rec = static_cast<const char*>(p.rec) + cc * RecOf<CF>::bytes;
+  if constexpr (CF::F32) {
+    copy_block<CF>(sTb, rec + Rec<CF>::T, Rec<CF>::Q - Rec<CF>::T);
+    copy_block<CF>(sQb, rec + Rec<CF>::Q, Rec<CF>::F - Rec<CF>::Q);
+  } else {
+    // swizzled T and scale*Q into the padded operand rows
+    for (int e = threadIdx.x; e < 2 * C * (C / 8); e += blockDim.x) {
+      const int m = e / (C * (C / 8)), r = (e / (C / 8)) % C, g = e % (C / 8);
+      cp_async16((m == 0 ? sTb : sQb) + r * CF::LDC + 8 * g,
+                 rec + (m == 0 ? RecTc<CF>::T : RecTc<CF>::Qq) + tc::sw_off(r, 8 * g, C));
+    }
+  }
   if constexpr (!CF::F32) cp_async_commit();
   issue_half(0);
   if constexpr (!CF::F32) {
@@ -392,6 +591,7 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_kernel(ScanParams p) {
   zero_acc(aDQ);
   zero_acc(aDT);
   const int Iv = warp / NJV, nv = (warp % NJV) * 8 * NTV;
+  const float qscale = CF::F32 ? p.scale : 1.f;  // the bf16 record holds scale * Q
 
   for (int vh = 0; vh < kVD / kBV; ++vh) {
     const int v0 = vh * kBV;
@@ -410,12 +610,23 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_kernel(ScanParams p) {
     }
     __syncthreads();
     if constexpr (!CF::ISO) convert_dO<CF>(sdO, dOst);
-    // cgl += sum_v S0' dS''  (8 threads per state row)
+    // S0' = fr S0, dS'' = fL dS (the bf16 precision saves unscaled states),
+    // and cgl += sum_v S0' dS''  (8 threads per state row)
     for (int grp = threadIdx.x; grp < kKD * (kBV / 8); grp += blockDim.x) {
       const int row = grp >> 3, c8 = (grp & 7) * 8;
       float s0[8], ds[8];
       ld8(s0, sS0 + row * CF::LDV + c8);
       ld8(ds, sdS + row * CF::LDV + c8);
+      if constexpr (!CF::F32) {
+        const float fr = ch.fr[row], fl = ch.fL[row];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          s0[i] *= fr;
+          ds[i] *= fl;
+        }
+        st8(sS0 + row * CF::LDV + c8, s0);
+        st8(sdS + row * CF::LDV + c8, ds);
+      }
       float acc = 0.f;
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc = fmaf(s0[i], ds[i], acc);
@@ -441,7 +652,7 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_kernel(ScanParams p) {
       wgemm<1, NTV, false, false>(u, sQb, CF::LDC, sdO, CF::LDV, 16 * Iv, nv, 16 * Iv, C);
       wgemm<1, NTV, true, false>(a, ch.Kc, CF::LDK, sdS, CF::LDV, 16 * Iv, nv, 0, kKD);
       for_acc<1, NTV>(16 * Iv, nv, [&](int, int nt, int e, int row, int col) {
-        sDD[row * CF::LDV + col] = from_f<OpT>(p.scale * u[0][nt][e] + a[0][nt][e]);
+        sDD[row * CF::LDV + col] = from_f<OpT>(qscale * u[0][nt][e] + a[0][nt][e]);
       });
     }
     __syncthreads();
@@ -702,19 +913,29 @@ size_t chunk_bytes() {
 
 template <class CF>
 int launch_bwd(const ScanParams& p, cudaStream_t st) {
-  const size_t s1 = CF::F32 ? 0 : StateLayout<CF>::bytes;
   const size_t s2 = CF::F32 ? 0 : ChunkLayout<CF>::bytes;
   static bool configured = false;
   if (!configured) {
-    if (cudaFuncSetAttribute(scan_bwd_state_kernel<CF>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s1) !=
-        cudaSuccess)
-      return check_launch("cudaFuncSetAttribute(scan_bwd_state_kernel)");
     if (cudaFuncSetAttribute(scan_bwd_chunk_kernel<CF>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s2) !=
         cudaSuccess)
       return check_launch("cudaFuncSetAttribute(scan_bwd_chunk_kernel)");
+    if constexpr (!CF::F32) {
+      if (cudaFuncSetAttribute(scan_bwd_state_tc_kernel<CF>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)StateTcLayout<CF>::bytes) != cudaSuccess)
+        return check_launch("cudaFuncSetAttribute(scan_bwd_state_tc_kernel)");
+    }
     configured = true;
   }
-  scan_bwd_state_kernel<CF><<<dim3(kVD / kBV, p.B * p.H), CF::F32 ? kSeqThreads : kSeqThreads + 32, s1, st>>>(p);
+  if constexpr (CF::F32) {
+    scan_bwd_state_kernel<CF><<<dim3(kVD / kBV, p.B * p.H), kSeqThreads, 0, st>>>(p);
+  } else {
+    TcMaps maps;
+    int rc = CF::ISO ? encode_bthd(&maps.in, p.dO, true, p.B, p.T, p.H, kVD, 64, CF::C, true)
+                     : encode_bthd(&maps.in, p.dO, false, p.B, p.T, p.H, kVD, kVD, CF::C, false);
+    if (rc != KDN_OK) return rc;
+    maps.out = maps.in;
+    scan_bwd_state_tc_kernel<CF><<<p.B * p.H, kTcThreads, StateTcLayout<CF>::bytes, st>>>(p, maps);
+  }
   int rc = check_launch("scan_bwd_state_kernel");
   if (rc != KDN_OK) return rc;
   scan_bwd_chunk_kernel<CF><<<dim3(p.NT, p.B * p.H), 512, s2, st>>>(p);

@@ -14,6 +14,8 @@
 // and the output stage) and of _diag_kdn_memory_forward
 // (diag_kdn_chunk.py:3224-3245).
 #include "kdn_scan.cuh"
+#include "kdn_tc.cuh"
+#include "kdn_tma.cuh"
 
 namespace kdn {
 
@@ -197,6 +199,199 @@ __global__ void __launch_bounds__(kSeqThreads + 32, 1) scan_fwd_kernel(ScanParam
     if (threadIdx.x == 32) bulk_wait_all();
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core sequential pass (bf16 precision): one CTA per (b, h) stream
+// carries the whole 128 x 128 fp32 state in TMEM.  Warps 0-7 move data
+// between TMEM and shared memory, thread 0 issues the MMAs, warp 8 streams
+// the chunk records (bulk copy) and value rows (TMA, 128-byte swizzle) into
+// NS stages.  Per chunk, with the record's folded factors
+// (Qs = scale fr Qr, Kf = fL Kc, Wf = fr W0, Qq = scale Q):
+//   S -> bf16 operand (saved as h);  S <- 2^g_L S            (TMEM ld / st)
+//   delta^T = v^T T^T - S^T Wf^T                               (MMA, M = 128 values)
+//   o^T = S^T Qs^T + delta^T Qq^T;  S += Kf^T delta            (MMA)
+//   o -> shared memory -> one TMA store of the chunk's rows
+// ---------------------------------------------------------------------------
+template <class CF>
+struct FwdTcLayout {
+  static constexpr int C = CF::C;
+  static constexpr int NS = CF::ISO ? 2 : 3;
+  using R = RecTc<CF>;
+  static constexpr size_t v = R::fwd_end;  // [2][C][64] bf16, swizzled by the TMA engine
+  static constexpr size_t stage = align_up(v + (size_t)C * 256, 1024);
+  static constexpr size_t S = NS * stage;                 // state operand [2][KD][64] bf16 (also h)
+  static constexpr size_t Del = S + (size_t)kKD * 256;    // delta [2][C][64] bf16, then the output rows
+  static constexpr size_t O_bytes = (size_t)C * kVD * (CF::ISO ? 2 : 4);
+  static constexpr size_t bar = Del + align_up(cmax((size_t)C * 256, O_bytes), 1024);
+  static constexpr size_t bytes = bar + 128 + 1024;       // barriers and TMEM slot; alignment slack
+};
+
+template <class CF>
+__global__ void __launch_bounds__(kTcThreads, 1) scan_fwd_tc_kernel(ScanParams p, const __grid_constant__ TcMaps maps) {
+  using Lo = FwdTcLayout<CF>;
+  using R = RecTc<CF>;
+  using OutT = typename std::conditional<CF::ISO, bf16, float>::type;
+  constexpr int C = CF::C, NS = Lo::NS, HC = C / 2;
+  constexpr uint32_t TS = 0, TD = kKD, TO = kKD + C;  // TMEM columns: state, delta^T, o^T
+  constexpr int NTH = kTcWarps * 32;
+  extern __shared__ __align__(1024) char smem_raw[];
+  char* base = align1024(smem_raw);
+
+  const int bh = blockIdx.x, b = bh / p.H, h = bh - b * p.H;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const char* recs = static_cast<const char*>(p.rec) + (size_t)bh * p.NT * R::bytes;
+  char* hout = static_cast<char*>(p.h) + (size_t)bh * p.NT * 2 * hblock_bytes<CF>();
+  uint64_t* full = reinterpret_cast<uint64_t*>(base + Lo::bar);
+  uint64_t* empty = full + NS;
+  uint64_t* mmab = empty + NS;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(mmab + 1);
+  char* sS = base + Lo::S;
+  char* sDel = base + Lo::Del;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(mmab, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tc::alloc(tslot, 256);
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem = *tslot;
+
+  if (warp == kTcWarps) {
+    // producer: refill a stage once the MMAs of its previous chunk completed
+    for (int c = 0; c < p.NT; ++c) {
+      const int s = c % NS;
+      if (c >= NS) mbar_wait(&empty[s], (c / NS - 1) & 1, p.status);
+      if (lane == 0) {
+        char* st = base + s * Lo::stage;
+        mbar_expect_tx(&full[s], (unsigned)(R::fwd_end + (size_t)C * 256));
+        bulk_g2s(st, recs + (size_t)c * R::bytes, (unsigned)R::fwd_end, &full[s]);
+        tma_load_4d(st + Lo::v, &maps.in, 0, h, c * C, b, &full[s]);
+        tma_load_4d(st + Lo::v + C * 128, &maps.in, 64, h, c * C, b, &full[s]);
+      }
+      __syncwarp();
+    }
+    return;
+  }
+
+  // compute warps: warp w reads TMEM lanes 32(w%4).., column half w/4
+  const int q = warp & 3, hf = warp >> 2;
+  const int row = 32 * q + lane;  // key (state) or value channel (delta^T, o^T)
+  const uint32_t tl = tmem + ((uint32_t)(32 * q) << 16);
+  for (int j = 0; j < 64; j += 16) {
+    float x[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) x[i] = p.S0 ? p.S0[((size_t)bh * kKD + row) * kVD + 64 * hf + j + i] : 0.f;
+    tc::st16(tl + TS + 64 * hf + j, x);
+  }
+  tc::wait_st();
+  uint32_t mph = 0;
+
+  for (int c = 0; c < p.NT; ++c) {
+    const int s = c % NS, t0 = c * C;
+    char* st = base + s * Lo::stage;
+    mbar_wait(&full[s], (c / NS) & 1, p.status);
+    {
+      // state operand (and h), then S <- 2^g_L S
+      const float gl = reinterpret_cast<const float*>(st + R::F)[2 * kKD + row];
+#pragma unroll 1
+      for (int j = 0; j < 64; j += 16) {
+        float x[16];
+        tc::ld16(tl + TS + 64 * hf + j, x);
+        tc::st_row16(sS, kKD, row, 64 * hf + j, x, 1.f);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) x[i] *= gl;
+        tc::st16(tl + TS + 64 * hf + j, x);
+      }
+      tc::wait_st();
+    }
+    if (threadIdx.x == 0) bulk_wait_read<0>();  // the previous output tile has left shared memory
+    fence_async_shared();
+    tc::fence_before();
+    bar_sync(1, NTH);
+    if (threadIdx.x == 32) {
+      bulk_s2g(hout + (size_t)c * 2 * hblock_bytes<CF>(), sS, (unsigned)(2 * hblock_bytes<CF>()));
+      bulk_commit();
+    }
+    if (threadIdx.x == 0) {
+      tc::fence_after();
+      constexpr uint32_t id = tc::idesc(128, C, true, false), idn = tc::idesc(128, C, true, false, true);
+      for (int ks = 0; ks < C / 16; ++ks)
+        tc::mma(tmem + TD, tc::desc_mn(st + Lo::v, C, ks), tc::desc_k(st + R::T, C, ks), id, ks > 0);
+      for (int ks = 0; ks < kKD / 16; ++ks)
+        tc::mma(tmem + TD, tc::desc_mn(sS, kKD, ks), tc::desc_k(st + R::Wf, C, ks), idn, true);
+      tc::commit(mmab);
+    }
+    mbar_wait(mmab, mph, p.status);
+    mph ^= 1;
+    tc::fence_after();
+    // delta (lane = value channel) -> bf16 operand tile [2][C][64]
+#pragma unroll 1
+    for (int j = 0; j < HC; j += 16) {
+      float x[16];
+      tc::ld16(tl + TD + HC * hf + j, x);
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        *reinterpret_cast<bf16*>(sDel + tc::sw_off(HC * hf + j + i, row, C)) = __float2bfloat16_rn(x[i]);
+    }
+    if (threadIdx.x == 32) bulk_wait_read<0>();  // h has left the state operand (rewritten next chunk)
+    fence_async_shared();
+    tc::fence_before();
+    bar_sync(1, NTH);
+    if (threadIdx.x == 0) {
+      tc::fence_after();
+      constexpr uint32_t ido = tc::idesc(128, C, true, false), ids = tc::idesc(128, 128, true, true);
+      for (int ks = 0; ks < kKD / 16; ++ks)
+        tc::mma(tmem + TO, tc::desc_mn(sS, kKD, ks), tc::desc_k(st + R::Qs, C, ks), ido, ks > 0);
+      for (int ks = 0; ks < C / 16; ++ks)
+        tc::mma(tmem + TO, tc::desc_mn(sDel, C, ks), tc::desc_k(st + R::Qq, C, ks), ido, true);
+      for (int ks = 0; ks < C / 16; ++ks)
+        tc::mma(tmem + TS, tc::desc_mn(st + R::Kf, C, ks), tc::desc_mn(sDel, C, ks), ids, true);
+      tc::commit(&empty[s]);
+      tc::commit(mmab);
+    }
+    mbar_wait(mmab, mph, p.status);
+    mph ^= 1;
+    tc::fence_after();
+    // output rows (lane = value channel) over the delta tile, then one TMA store
+    {
+      OutT* sO = reinterpret_cast<OutT*>(sDel);
+#pragma unroll 1
+      for (int j = 0; j < HC; j += 16) {
+        float x[16];
+        tc::ld16(tl + TO + HC * hf + j, x);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) sO[(HC * hf + j + i) * kVD + row] = from_f<OutT>(x[i]);
+      }
+    }
+    fence_async_shared();
+    bar_sync(1, NTH);
+    if (threadIdx.x == 0) {
+      tc::tma_store_4d(&maps.out, sDel, 0, h, t0, b);
+      bulk_commit();
+    }
+  }
+  if (p.ST) {
+    for (int j = 0; j < 64; j += 16) {
+      float x[16];
+      tc::ld16(tl + TS + 64 * hf + j, x);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) p.ST[((size_t)bh * kKD + row) * kVD + 64 * hf + j + i] = x[i];
+    }
+  }
+  if (threadIdx.x == 0 || threadIdx.x == 32) bulk_wait_all();
+  tc::fence_before();
+  bar_sync(1, NTH);
+  if (warp == 0) {
+    tc::fence_after();
+    tc::dealloc(tmem, 256);
+  }
+}
+
 template <class CF>
 size_t fwd_dbg_bytes() {
   return CF::F32 ? FwdLayout<CF>::bytes : 0;
@@ -208,16 +403,32 @@ template <class CF>
 int launch_fwd(const ScanParams& p, cudaStream_t st) {
   int rc = launch_prep<CF>(p, st);
   if (rc != KDN_OK) return rc;
-  const size_t smem = CF::F32 ? 0 : FwdLayout<CF>::bytes;
   static bool configured = false;
-  if (!configured) {
-    if (cudaFuncSetAttribute(scan_fwd_kernel<CF>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-      return check_launch("cudaFuncSetAttribute(scan_fwd_kernel)");
-    configured = true;
+  if constexpr (CF::F32) {
+    if (!configured) {
+      if (cudaFuncSetAttribute(scan_fwd_kernel<CF>, cudaFuncAttributeMaxDynamicSharedMemorySize, 0) != cudaSuccess)
+        return check_launch("cudaFuncSetAttribute(scan_fwd_kernel)");
+      configured = true;
+    }
+    dim3 grid(kVD / kBV, p.B * p.H);
+    scan_fwd_kernel<CF><<<grid, kSeqThreads, 0, st>>>(p);
+    return check_launch("scan_fwd_kernel");
+  } else {
+    const size_t smem = FwdTcLayout<CF>::bytes;
+    if (!configured) {
+      if (cudaFuncSetAttribute(scan_fwd_tc_kernel<CF>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+          cudaSuccess)
+        return check_launch("cudaFuncSetAttribute(scan_fwd_tc_kernel)");
+      configured = true;
+    }
+    TcMaps maps;
+    rc = encode_bthd(&maps.in, p.v, true, p.B, p.T, p.H, kVD, 64, CF::C, true);
+    if (rc != KDN_OK) return rc;
+    rc = encode_bthd(&maps.out, p.o, CF::ISO, p.B, p.T, p.H, kVD, kVD, CF::C, false);
+    if (rc != KDN_OK) return rc;
+    scan_fwd_tc_kernel<CF><<<p.B * p.H, kTcThreads, smem, st>>>(p, maps);
+    return check_launch("scan_fwd_tc_kernel");
   }
-  dim3 grid(kVD / kBV, p.B * p.H);
-  scan_fwd_kernel<CF><<<grid, CF::F32 ? kSeqThreads : kSeqThreads + 32, smem, st>>>(p);
-  return check_launch("scan_fwd_kernel");
 }
 
 template int launch_fwd<Cfg<true, 64, bf16>>(const ScanParams&, cudaStream_t);

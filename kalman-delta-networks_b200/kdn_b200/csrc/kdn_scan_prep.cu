@@ -4,13 +4,15 @@
 //   q, k, g, kappa|beta -> gated operands Kr, Qr, Kc (reference rho, exact
 //   path for wide gate ranges) -> A = Kr Kc^T, Q = Qr Kc^T (tensor cores)
 //   -> T = (I + A)^-1 -> W0 = T Kr
-// and writes the chunk record (Qr, Kc, W0, T, Q, fr, fL, 2^g_L) with bulk
-// copies from shared memory.  The sequential forward and reverse passes then
+// and writes the chunk record: (Qr, Kc, W0, T, Q, fr, fL, 2^g_L) as padded
+// rows in the fp32 precision, or the swizzled tensor-core tiles with the
+// scale factors folded in (RecTc) in the bf16 precision.  The sequential forward and reverse passes then
 // only carry the state.  Replaces the intra-chunk half of
 // _chunk_kda_fwd_precum (lit_gpt/kdn_ops/iso_kdn_chunk.py:2037-2086, the
 // scaled-dot-kkt / solve-tril / recompute-w-u stages of the FLA pipeline it
 // calls) and of _diag_kdn_memory_forward (diag_kdn_chunk.py:3224-3245).
 #include "kdn_scan.cuh"
+#include "kdn_tc.cuh"
 
 namespace kdn {
 
@@ -79,26 +81,69 @@ __global__ void __launch_bounds__(kPrepThreads, 2) scan_prep_kernel(ScanParams p
     store_acc(ch.Kr, CF::LDK, acc, 16 * I, n0);
   }
 
-  char* rec = static_cast<char*>(p.rec) + cc * R::bytes;
-  const char* src[6] = {base + Lo::Qr, base + Lo::Kc, base + Lo::Kr, base + Lo::Tb, base + Lo::Qb,
-                        reinterpret_cast<const char*>(ch.fr)};
-  const size_t dst[6] = {R::Qr, R::Kc, R::W0, R::T, R::Q, R::F};
-  const size_t len[6] = {R::Kc - R::Qr, R::W0 - R::Kc, R::T - R::W0, R::Q - R::T, R::F - R::Q, 3 * kKD * 4};
   if constexpr (CF::F32) {
+    // padded record, blocks as they lie in shared memory
+    char* rec = static_cast<char*>(p.rec) + cc * R::bytes;
+    const char* src[6] = {base + Lo::Qr, base + Lo::Kc, base + Lo::Kr, base + Lo::Tb, base + Lo::Qb,
+                          reinterpret_cast<const char*>(ch.fr)};
+    const size_t dst[6] = {R::Qr, R::Kc, R::W0, R::T, R::Q, R::F};
+    const size_t len[6] = {R::Kc - R::Qr, R::W0 - R::Kc, R::T - R::W0, R::Q - R::T, R::F - R::Q, 3 * kKD * 4};
     __syncthreads();
 #pragma unroll
     for (int i = 0; i < 6; ++i)
       for (size_t o = (size_t)threadIdx.x * 16; o < len[i]; o += (size_t)blockDim.x * 16)
         *reinterpret_cast<int4*>(rec + dst[i] + o) = *reinterpret_cast<const int4*>(src[i] + o);
   } else {
-    fence_async_shared();
+    // swizzled tensor-core record with the scale factors folded in
+    using RT = RecTc<CF>;
+    char* rec = static_cast<char*>(p.rec) + cc * RT::bytes;
     __syncthreads();
-    if (threadIdx.x == 0) {
+    // Qs = scale fr Qr, Kf = fL Kc, Wf = fr W0: thread t owns keys 8(t%16)..+7
+    {
+      const int g = threadIdx.x & 15;
+#pragma unroll 1
+      for (int m = 0; m < 3; ++m) {
+        const OpT* src = m == 0 ? ch.Qr : (m == 1 ? ch.Kc : ch.Kr);
+        const float* fac = m == 1 ? ch.fL : ch.fr;
+        const float mul = m == 0 ? p.scale : 1.f;
+        float f[8];
 #pragma unroll
-      for (int i = 0; i < 6; ++i) bulk_s2g(rec + dst[i], src[i], (unsigned)len[i]);
-      bulk_commit();
-      bulk_wait_all();
+        for (int i = 0; i < 8; ++i) f[i] = mul * fac[8 * g + i];
+        char* dst = rec + (m == 0 ? RT::Qs : (m == 1 ? RT::Kf : RT::Wf));
+        for (int r = threadIdx.x >> 4; r < C; r += kPrepThreads / 16) {
+          float x[8];
+          ld8(x, src + r * CF::LDK + 8 * g);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) x[i] *= f[i];
+          st8(reinterpret_cast<bf16*>(dst + tc::sw_off(r, 8 * g, C)), x);
+        }
+      }
     }
+    // T, Qq = scale Q, Qt = scale Q^T: thread t owns columns 8(t%8)..+7 (columns >= C zero)
+    {
+      const int g = threadIdx.x & 7;
+#pragma unroll 1
+      for (int m = 0; m < 3; ++m) {
+        char* dst = rec + (m == 0 ? RT::T : (m == 1 ? RT::Qq : RT::Qt));
+        const float mul = m == 0 ? 1.f : p.scale;
+        for (int r = threadIdx.x >> 3; r < C; r += kPrepThreads / 8) {
+          float x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          if (8 * g < C) {
+            if (m < 2) {
+              ld8(x, (m == 0 ? sTb : sQb) + r * CF::LDC + 8 * g);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 8; ++i) x[i] = to_f(sQb[(8 * g + i) * CF::LDC + r]);
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) x[i] *= mul;
+          }
+          st8(reinterpret_cast<bf16*>(dst + tc::sw_off(r, 8 * g, C)), x);
+        }
+      }
+    }
+    for (int e = threadIdx.x; e < 3 * kKD / 4; e += blockDim.x)
+      reinterpret_cast<float4*>(rec + RT::F)[e] = reinterpret_cast<const float4*>(ch.fr)[e];
   }
 }
 
