@@ -105,7 +105,7 @@ struct Rec {
 // Tensor-core record (bf16 precision): tiles in the swizzled layout of
 // kdn_tc.cuh, with the chunk's scale factors folded in so that the
 // sequential passes carry the unscaled state:
-//   T, Qq = scale Q, Qt = scale Q^T               [C][64] (columns >= C unused)
+//   T, Qq = scale Q, Qt = scale Q^T, Tt = T^T     [C][64] (columns >= C unused)
 //   Qs = scale fr Qr,  Kf = fL Kc,  Wf = fr W0   [2][C][64] (64 keys per block)
 //   fr, fL, 2^g_L                                  [3][KD] fp32
 // The forward reads [0, fwd_end), the reverse sweep [bwd_begin, bytes).
@@ -119,7 +119,8 @@ struct RecTc {
   static constexpr size_t Wf = Kf + (size_t)C * 256;
   static constexpr size_t F = Wf + (size_t)C * 256;
   static constexpr size_t Qt = F + align_up(3 * kKD * 4, 1024);
-  static constexpr size_t bytes = Qt + (size_t)C * 128;
+  static constexpr size_t Tt = Qt + (size_t)C * 128;
+  static constexpr size_t bytes = Tt + (size_t)C * 128;
   static constexpr size_t fwd_end = Qt;
   static constexpr size_t bwd_begin = Qs;
   static_assert(bytes % 1024 == 0 && Qs % 1024 == 0, "1024-byte aligned tiles");
@@ -299,8 +300,9 @@ __device__ __forceinline__ void load_row(RawRow<CF>& x, const Chunk<CF>& ch, int
 }
 
 // Gated operands of one row: Kr = k_hat 2^(g - rr), Qr = q_hat 2^(g - rr),
-// Kc = kappa 2^(rc - g); zero rows past the chunk's end.
-template <class CF>
+// Kc = kappa 2^(rc - g); zero rows past the chunk's end.  SW: the operand
+// buffers are 64-row swizzled tensor-core tiles instead of padded rows.
+template <class CF, bool SW = false>
 __device__ __forceinline__ void build_operands(const Chunk<CF>& ch, int r, int c0, const RawRow<CF>& x,
                                                const float (&rr)[8], const float (&rc)[8], float qs, float ks) {
   float kr[8], qr[8], kc[8];
@@ -318,9 +320,17 @@ __device__ __forceinline__ void build_operands(const Chunk<CF>& ch, int r, int c
 #pragma unroll
     for (int i = 0; i < 8; ++i) kr[i] = qr[i] = kc[i] = 0.f;
   }
-  st8(ch.Kr + r * CF::LDK + c0, kr);
-  st8(ch.Qr + r * CF::LDK + c0, qr);
-  st8(ch.Kc + r * CF::LDK + c0, kc);
+  if constexpr (SW) {
+    // byte offset of (r, c0) in a [2][64][64] swizzled tile
+    const uint32_t o = (uint32_t)((c0 >> 6) * 64 * 128 + r * 128 + ((((c0 & 63) >> 3) ^ (r & 7)) << 4));
+    st8(reinterpret_cast<typename CF::OpT*>(reinterpret_cast<char*>(ch.Kr) + o), kr);
+    st8(reinterpret_cast<typename CF::OpT*>(reinterpret_cast<char*>(ch.Qr) + o), qr);
+    st8(reinterpret_cast<typename CF::OpT*>(reinterpret_cast<char*>(ch.Kc) + o), kc);
+  } else {
+    st8(ch.Kr + r * CF::LDK + c0, kr);
+    st8(ch.Qr + r * CF::LDK + c0, qr);
+    st8(ch.Kc + r * CF::LDK + c0, kc);
+  }
 }
 
 // Row norms (iso), range check, per-channel factors and the three gated
@@ -332,7 +342,7 @@ __device__ __forceinline__ void build_operands(const Chunk<CF>& ch, int r, int c
 // middle row, known up front) and built again only when the range check
 // sends the chunk to the exact path.  Contains one barrier; the caller
 // places the barrier that publishes the results.
-template <class CF, int NTH>
+template <class CF, int NTH, bool SW = false>
 __device__ void prep_chunk(Chunk<CF>& ch) {
   constexpr int C = CF::C, RSTEP = NTH / 16, RPT = C / RSTEP, BATCH = RPT >= 2 ? 2 : 1;
   static_assert(NTH % 32 == 0 && C % RSTEP == 0 && RPT % BATCH == 0, "rows per thread");
@@ -376,7 +386,7 @@ __device__ void prep_chunk(Chunk<CF>& ch) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) rng = fmaxf(rng, fabsf(x[j].g[i] - gm[i]));
       }
-      build_operands(ch, r, c0, x[j], gm, gm, qs, ks);
+      build_operands<CF, SW>(ch, r, c0, x[j], gm, gm, qs, ks);
     }
   }
   rng = warp_max(rng);
@@ -409,7 +419,7 @@ __device__ void prep_chunk(Chunk<CF>& ch) {
       RawRow<CF> x;
       load_row(x, ch, r, c0);
       const float qs = CF::ISO ? ch.rq[r] : 1.f, ks = CF::ISO ? ch.rk[r] : 1.f;
-      build_operands(ch, r, c0, x, rr, rc, qs, ks);
+      build_operands<CF, SW>(ch, r, c0, x, rr, rc, qs, ks);
     }
   }
 }

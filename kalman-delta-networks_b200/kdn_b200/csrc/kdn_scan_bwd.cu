@@ -911,6 +911,8 @@ size_t chunk_bytes() {
   return ChunkLayout<CF>::bytes;
 }
 
+template <class CF> int launch_bwd_chunk_tc(const ScanParams&, cudaStream_t);
+
 template <class CF>
 int launch_bwd(const ScanParams& p, cudaStream_t st) {
   const size_t s2 = CF::F32 ? 0 : ChunkLayout<CF>::bytes;
@@ -938,6 +940,7 @@ int launch_bwd(const ScanParams& p, cudaStream_t st) {
   }
   int rc = check_launch("scan_bwd_state_kernel");
   if (rc != KDN_OK) return rc;
+  if constexpr (CF::ISO && !CF::F32) return launch_bwd_chunk_tc<CF>(p, st);
   scan_bwd_chunk_kernel<CF><<<dim3(p.NT, p.B * p.H), 512, s2, st>>>(p);
   return check_launch("scan_bwd_chunk_kernel");
 }

@@ -1,0 +1,511 @@
+// Chunk-parallel gradients of the isotropic scan on tcgen05 tensor cores
+// (bf16 precision).  One CTA (16 warps) per (chunk, b*h).  All operands are
+// 128-byte-swizzled bf16 tiles in shared memory (kdn_tc.cuh): the chunk
+// record blocks and the saved states arrive by bulk copies, v and dO by TMA,
+// the gated operands Kr, Qr, Kc are built from the raw rows in HBM.  Thread 0
+// issues six groups of MMAs into tensor memory (512 columns):
+//   A  delta^T  = v^T T^T - S0^T Wf^T,  ddelta^T = dO^T Qq + dS^T Kf^T
+//   B  dv = T^T ddelta,  (S0' dO^T, S0' ddelta^T, dS'' delta^T)  [K x C],
+//      dO delta^T, ddelta v^T  [C x C]
+//   C  dKr^T = dW^T ... (T^T dW)^T,  dT += dW Kr^T
+//   D  X = dT T^T      E  dA = -T^T X
+//   F  the score terms dA Kc, dQ Kc, dA^T Kr, dQ^T Qr (fast path)
+// and the warps turn accumulators into the next operand tiles in between
+// (S0' = fr S0, dS'' = fL dS, masks, signs).  The key-side accumulators are
+// kept transposed (lane = key), so the final gate mapping has one key per
+// lane and every store of a token row is contiguous.  Same mathematics as
+// scan_bwd_chunk_kernel (kdn_scan_bwd.cu); replaces _chunk_kda_bwd_precum
+// (lit_gpt/kdn_ops/iso_kdn_chunk.py:2089-2187) on the fixed-length path.
+#include "kdn_scan.cuh"
+#include "kdn_tc.cuh"
+#include "kdn_tma.cuh"
+
+namespace kdn {
+
+struct alignas(64) ChunkMaps {
+  CUtensorMap v, dO, dv;
+};
+
+template <class CF>
+struct ChunkTcLayout {
+  static_assert(CF::ISO && CF::C == 64 && !CF::F32, "isotropic bf16 chunks of 64");
+  static constexpr int C = 64;
+  // whole kernel
+  static constexpr size_t Kr = 0, Qr = 16384, Kc = 32768, T = 49152, Tt = 57344;
+  // Qt | Kf Wf (record), then delta | ddelta
+  static constexpr size_t G = 65536;
+  static constexpr size_t Qt = G, Kf = G + 8192, Wf = G + 8192 + 16384;
+  static constexpr size_t Del = G, DDel = G + 16384;
+  // v | dO, then the dv rows
+  static constexpr size_t V = G + 40960;
+  static constexpr size_t vv = V, dO = V + 16384, dvst = V;
+  // S0 | dS (saved states), then dW dQ dQu dT X dA
+  static constexpr size_t A = V + 32768;
+  static constexpr size_t S0 = A, dS = A + 32768;
+  static constexpr size_t dW = A, dQ = A + 16384, dQu = A + 24576, dT = A + 32768, X = A + 40960, dA = A + 49152;
+  // chunk scalars; cfl, cgl [KD]; token sums dbeta, <dk_hat,k_hat>, <dq_hat,q_hat> [C]
+  static constexpr size_t small = A + 65536;
+  static constexpr size_t bar = small + align_up((small_floats<CF>() + 2 * kKD + 3 * C) * 4, 128);
+  static constexpr size_t bytes = bar + 64 + 1024;
+  static constexpr unsigned load_bytes = 3 * C * 128 + 2 * C * 256 + 2 * 32768 + 2 * C * 256;
+};
+
+// Exact-path score terms of one (token r, key) element: the sum over the
+// chunk's other tokens j of dA, dQ times the gate factor 2^(g_r - g_j) (j <= r)
+// or 2^(g_j - g_r) (j >= r), each <= 1 (see scan_bwd_chunk_kernel).
+struct ExactTerms {
+  float dkh, dqh, dkap, dG;
+};
+__device__ __noinline__ ExactTerms exact_terms(const float* g, const bf16* k, const bf16* qv, const float* beta,
+                                              const float* rk, const float* rq, int ldr, int ldb, const char* sdA,
+                                              const char* sdQ, int r, int key, int L, float gi, float k1, float q1,
+                                              float kap) {
+  ExactTerms t{0.f, 0.f, 0.f, 0.f};
+  for (int j = 0; j < L; ++j) {
+    const size_t oj = (size_t)j * ldr + key;
+    const float gj = g[oj];
+    const float khj = rk[j] * __bfloat162float(k[oj]), qhj = rq[j] * __bfloat162float(qv[oj]);
+    const float kapj = beta[(size_t)j * ldb] * khj;
+    if (j <= r) {
+      const float f = exp2f(gi - gj);
+      const float dAij = j < r ? __bfloat162float(*reinterpret_cast<const bf16*>(sdA + tc::sw_off(r, j, 64))) : 0.f;
+      const float dQij = __bfloat162float(*reinterpret_cast<const bf16*>(sdQ + tc::sw_off(r, j, 64)));
+      t.dkh = fmaf(dAij * kapj, f, t.dkh);
+      t.dqh = fmaf(dQij * kapj, f, t.dqh);
+      t.dG = fmaf((dAij * k1 + dQij * q1) * kapj, f, t.dG);
+    }
+    if (j >= r) {
+      const float f = exp2f(gj - gi);
+      const float dAji = j > r ? __bfloat162float(*reinterpret_cast<const bf16*>(sdA + tc::sw_off(j, r, 64))) : 0.f;
+      const float dQji = __bfloat162float(*reinterpret_cast<const bf16*>(sdQ + tc::sw_off(j, r, 64)));
+      const float w = (dAji * khj + dQji * qhj) * f;
+      t.dkap += w;
+      t.dG -= w * kap;
+    }
+  }
+  return t;
+}
+
+template <class CF>
+__global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p, const __grid_constant__ ChunkMaps maps) {
+  using Lo = ChunkTcLayout<CF>;
+  using RT = RecTc<CF>;
+  using OpT = typename CF::OpT;
+  constexpr int C = Lo::C;
+  // TMEM columns
+  constexpr uint32_t TDEL = 0, TDD = 64, TQR = 128, TW = 192, TKC = 256, TDQ = 320, TDT = 384, TKR = 448;
+  constexpr uint32_t TDV = 0, TX = 0, TDA = 64;
+  extern __shared__ __align__(1024) char smem_raw[];
+  char* base = align1024(smem_raw);
+
+  const int c = blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q = warp & 3, cg = warp >> 2;  // TMEM lane quadrant, column group
+  const int t0 = c * C, L = min(C, p.T - t0);
+  const size_t cc = (size_t)bh * p.NT + c;
+  uint64_t* ldbar = reinterpret_cast<uint64_t*>(base + Lo::bar);
+  uint64_t* mmab = ldbar + 1;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(mmab + 1);
+  float* small = reinterpret_cast<float*>(base + Lo::small);
+  float* cfl = small + small_floats<CF>();
+  float* cgl = cfl + kKD;
+  float* tsum = cgl + kKD;  // [3][C]
+
+  Chunk<CF> ch;
+  bind_raw_global(ch, p, b, h, t0);
+  ch.L = L;
+  bind_small(ch, small);
+  ch.Kr = reinterpret_cast<OpT*>(base + Lo::Kr);
+  ch.Qr = reinterpret_cast<OpT*>(base + Lo::Qr);
+  ch.Kc = reinterpret_cast<OpT*>(base + Lo::Kc);
+  auto bf = [&](size_t off) { return reinterpret_cast<bf16*>(base + off); };
+  auto at = [&](size_t tile, int row, int col, int rows) { return reinterpret_cast<bf16*>(base + tile + tc::sw_off(row, col, rows)); };
+
+  if (threadIdx.x == 0) {
+    mbar_init(ldbar, 1);
+    mbar_init(mmab, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tc::alloc(tslot, 512);
+  for (int e = threadIdx.x; e < 2 * kKD + 3 * C; e += 512) cfl[e] = 0.f;
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem = *tslot;
+  const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16);  // this warp's lane quadrant
+
+  if (threadIdx.x == 0) {
+    const char* rec = static_cast<const char*>(p.rec) + cc * RT::bytes;
+    const char* hs = static_cast<const char*>(p.h) + cc * 2 * hblock_bytes<CF>();
+    const char* dhs = static_cast<const char*>(p.dh) + cc * 2 * hblock_bytes<CF>();
+    mbar_expect_tx(ldbar, Lo::load_bytes);
+    bulk_g2s(base + Lo::T, rec + RT::T, C * 128, ldbar);
+    bulk_g2s(base + Lo::Qt, rec + RT::Qt, C * 128, ldbar);
+    bulk_g2s(base + Lo::Tt, rec + RT::Tt, C * 128, ldbar);
+    bulk_g2s(base + Lo::Kf, rec + RT::Kf, 2 * C * 256, ldbar);  // Kf, Wf
+    bulk_g2s(base + Lo::S0, hs, 32768, ldbar);
+    bulk_g2s(base + Lo::dS, dhs, 32768, ldbar);
+    tma_load_4d(base + Lo::vv, &maps.v, 0, h, t0, b, ldbar);
+    tma_load_4d(base + Lo::vv + C * 128, &maps.v, 64, h, t0, b, ldbar);
+    tma_load_4d(base + Lo::dO, &maps.dO, 0, h, t0, b, ldbar);
+    tma_load_4d(base + Lo::dO + C * 128, &maps.dO, 64, h, t0, b, ldbar);
+  }
+  // gated operands from the raw rows while the copies fly
+  prep_chunk<CF, 512, true>(ch);
+  mbar_wait(ldbar, 0, p.status);
+  fence_async_shared();
+  tc::fence_before();
+  __syncthreads();
+
+  uint32_t mph = 0;
+  auto mma_wait = [&]() {
+    mbar_wait(mmab, mph, p.status);
+    mph ^= 1;
+    tc::fence_after();
+  };
+  auto publish = [&]() {
+    fence_async_shared();
+    tc::fence_before();
+    __syncthreads();
+  };
+
+  // ---- A: delta^T, ddelta^T (lane = value channel)
+  if (threadIdx.x == 0) {
+    tc::fence_after();
+    constexpr uint32_t id = tc::idesc(128, C, true, false), idn = tc::idesc(128, C, true, false, true);
+    // the two accumulators alternate so consecutive MMAs are independent
+    for (int ks = 0; ks < C / 16; ++ks) {
+      tc::mma(tmem + TDEL, tc::desc_mn(base + Lo::vv, C, ks), tc::desc_k(base + Lo::T, C, ks), id, ks > 0);
+      tc::mma(tmem + TDD, tc::desc_mn(base + Lo::dO, C, ks), tc::desc_k(base + Lo::Qt, C, ks), id, ks > 0);
+    }
+    for (int ks = 0; ks < kKD / 16; ++ks) {
+      tc::mma(tmem + TDEL, tc::desc_mn(base + Lo::S0, kKD, ks), tc::desc_k(base + Lo::Wf, C, ks), idn, true);
+      tc::mma(tmem + TDD, tc::desc_mn(base + Lo::dS, kKD, ks), tc::desc_k(base + Lo::Kf, C, ks), id, true);
+    }
+    tc::commit(mmab);
+  }
+  mma_wait();
+  {
+    const int v = 32 * q + lane;
+    float x[16];
+    tc::ld16(tq + TDEL + 16 * cg, x);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) *at(Lo::Del, 16 * cg + i, v, C) = __float2bfloat16_rn(x[i]);
+    tc::ld16(tq + TDD + 16 * cg, x);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) *at(Lo::DDel, 16 * cg + i, v, C) = __float2bfloat16_rn(x[i]);
+  }
+  // S0' = fr S0, dS'' = fL dS in place, cgl = sum_v S0' dS''  (a half-warp per key row)
+  for (int e = threadIdx.x; e < kKD * 16; e += 512) {
+    const int r = e >> 4, g = e & 15;
+    bf16* s0 = at(Lo::S0, r, 8 * g, kKD);
+    bf16* ds = at(Lo::dS, r, 8 * g, kKD);
+    float a[8], d[8];
+    ld8(a, s0);
+    ld8(d, ds);
+    const float fr = ch.fr[r], fl = ch.fL[r];
+    float acc = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      a[i] *= fr;
+      d[i] *= fl;
+      acc = fmaf(a[i], d[i], acc);
+    }
+    st8(s0, a);
+    st8(ds, d);
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (g == 0) cgl[r] = acc;
+  }
+  publish();
+
+  // ---- B
+  if (threadIdx.x == 0) {
+    tc::fence_after();
+    constexpr uint32_t id_dv = tc::idesc(64, 128, true, true);
+    for (int ks = 0; ks < C / 16; ++ks)
+      tc::mma(tmem + TDV, tc::desc_mn(base + Lo::T, C, ks), tc::desc_mn(base + Lo::DDel, C, ks), id_dv, ks > 0);
+    constexpr uint32_t id_kc = tc::idesc(128, C, false, false);
+    constexpr uint32_t id_cc = tc::idesc(64, C, false, false);
+    for (int ks = 0; ks < kVD / 16; ++ks) {
+      tc::mma(tmem + TQR, tc::desc_k(base + Lo::S0, kKD, ks), tc::desc_k(base + Lo::dO, C, ks), id_kc, ks > 0);
+      tc::mma(tmem + TW, tc::desc_k(base + Lo::S0, kKD, ks), tc::desc_k(base + Lo::DDel, C, ks), id_kc, ks > 0);
+      tc::mma(tmem + TKC, tc::desc_k(base + Lo::dS, kKD, ks), tc::desc_k(base + Lo::Del, C, ks), id_kc, ks > 0);
+      tc::mma(tmem + TDQ, tc::desc_k(base + Lo::dO, C, ks), tc::desc_k(base + Lo::Del, C, ks), id_cc, ks > 0);
+      tc::mma(tmem + TDT, tc::desc_k(base + Lo::DDel, C, ks), tc::desc_k(base + Lo::vv, C, ks), id_cc, ks > 0);
+    }
+    tc::commit(mmab);
+  }
+  mma_wait();
+  {
+    // dv rows (M = 64 accumulator: row m in lane (m % 16) + 32 (m / 16))
+    bf16* dvst = bf(Lo::dvst);
+    const int m = 16 * q + (lane & 15);
+#pragma unroll
+    for (int j = 0; j < 32; j += 16) {
+      float x[16];
+      tc::ld16(tq + TDV + 32 * cg + j, x);
+      if (lane < 16) {
+        float y[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] = x[i];
+        st8(dvst + m * kVD + 32 * cg + j, y);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] = x[8 + i];
+        st8(dvst + m * kVD + 32 * cg + j + 8, y);
+      }
+    }
+    // dW = -(S0' ddelta^T)^T  (lane = key)
+    const int key = 32 * q + lane;
+    float x[16];
+    tc::ld16(tq + TW + 16 * cg, x);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) *at(Lo::dW, 16 * cg + i, key, C) = __float2bfloat16_rn(-x[i]);
+    // cfl[key] = sum_j Kc[j][key] (delta dS''^T)[j][key]
+    tc::ld16(tq + TKC + 16 * cg, x);
+    float part = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) part = fmaf(to_f(*at(Lo::Kc, 16 * cg + i, key, C)), x[i], part);
+    atomicAdd(&cfl[key], part);
+    // dQ = scale * lower(dO delta^T) and its unscaled copy
+    tc::ld16(tq + TDQ + 16 * cg, x);
+    if (lane < 16) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int j = 16 * cg + i;
+        const float d = j <= m ? x[i] : 0.f;
+        *at(Lo::dQu, m, j, C) = __float2bfloat16_rn(d);
+        *at(Lo::dQ, m, j, C) = __float2bfloat16_rn(p.scale * d);
+      }
+    }
+  }
+  publish();
+  if (threadIdx.x == 0) {
+    tc::tma_store_4d(&maps.dv, base + Lo::dvst, 0, h, t0, b);
+    bulk_commit();
+  }
+
+  // ---- C: dKr^T = dW^T Tt^T, dT += dW Kr^T
+  if (threadIdx.x == 0) {
+    tc::fence_after();
+    constexpr uint32_t id_kr = tc::idesc(128, C, true, false);
+    for (int ks = 0; ks < C / 16; ++ks)
+      tc::mma(tmem + TKR, tc::desc_mn(base + Lo::dW, C, ks), tc::desc_k(base + Lo::Tt, C, ks), id_kr, ks > 0);
+    constexpr uint32_t id_cc = tc::idesc(64, C, false, false);
+    for (int ks = 0; ks < kKD / 16; ++ks)
+      tc::mma(tmem + TDT, tc::desc_k(base + Lo::dW, C, ks), tc::desc_k(base + Lo::Kr, C, ks), id_cc, true);
+    tc::commit(mmab);
+  }
+  mma_wait();
+  auto cc_tile = [&](uint32_t col, size_t tile, float sign, bool strict) {
+    // M = 64 accumulator -> masked (j < i, or j <= i) bf16 tile
+    float x[16];
+    tc::ld16(tq + col + 16 * cg, x);
+    if (lane < 16) {
+      const int m = 16 * q + lane;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int j = 16 * cg + i;
+        *at(tile, m, j, C) = __float2bfloat16_rn((strict ? j < m : j <= m) ? sign * x[i] : 0.f);
+      }
+    }
+  };
+  cc_tile(TDT, Lo::dT, 1.f, true);
+  publish();
+  // ---- D: X = dT T^T
+  if (threadIdx.x == 0) {
+    tc::fence_after();
+    constexpr uint32_t id_cc = tc::idesc(64, C, false, false);
+    for (int ks = 0; ks < C / 16; ++ks)
+      tc::mma(tmem + TX, tc::desc_k(base + Lo::dT, C, ks), tc::desc_k(base + Lo::T, C, ks), id_cc, ks > 0);
+    tc::commit(mmab);
+  }
+  mma_wait();
+  cc_tile(TX, Lo::X, 1.f, true);
+  publish();
+  // ---- E: dA = -T^T X (strictly lower)
+  if (threadIdx.x == 0) {
+    tc::fence_after();
+    constexpr uint32_t id_cc = tc::idesc(64, C, true, true);
+    for (int ks = 0; ks < C / 16; ++ks)
+      tc::mma(tmem + TDA, tc::desc_mn(base + Lo::T, C, ks), tc::desc_mn(base + Lo::X, C, ks), id_cc, ks > 0);
+    tc::commit(mmab);
+  }
+  mma_wait();
+  cc_tile(TDA, Lo::dA, -1.f, true);
+  publish();
+  // ---- F: score terms (the exact path adds them elementwise below)
+  if (ch.fast) {
+    if (threadIdx.x == 0) {
+      tc::fence_after();
+      constexpr uint32_t id_t = tc::idesc(128, C, true, false), id_n = tc::idesc(128, C, true, true);
+      for (int ks = 0; ks < C / 16; ++ks) {
+        tc::mma(tmem + TKR, tc::desc_mn(base + Lo::Kc, C, ks), tc::desc_k(base + Lo::dA, C, ks), id_t, true);
+        tc::mma(tmem + TQR, tc::desc_mn(base + Lo::Kc, C, ks), tc::desc_k(base + Lo::dQu, C, ks), id_t, true);
+        tc::mma(tmem + TKC, tc::desc_mn(base + Lo::Kr, C, ks), tc::desc_mn(base + Lo::dA, C, ks), id_n, true);
+      }
+      for (int ks = 0; ks < C / 16; ++ks)
+        tc::mma(tmem + TKC, tc::desc_mn(base + Lo::Qr, C, ks), tc::desc_mn(base + Lo::dQ, C, ks), id_n, true);
+      tc::commit(mmab);
+    }
+    mma_wait();
+  }
+
+  // ---- gate mapping: lane = key, 16 tokens per thread
+  const int key = 32 * q + lane;
+  float xk[16], xq[16], xc[16];
+  tc::ld16(tq + TKR + 16 * cg, xk);
+  tc::ld16(tq + TQR + 16 * cg, xq);
+  tc::ld16(tq + TKC + 16 * cg, xc);
+  const float rr = ch.fast ? ch.gmid[key] : 0.f;
+  const float rc = ch.fast ? ch.gmid[key] : ch.glast[key];
+  const float last = cfl[key] + cgl[key] * ch.gL[key] / (ch.fr[key] * ch.fL[key]);
+  float* part = reinterpret_cast<float*>(base + Lo::X);  // [4 quadrants][3][C] partial token sums
+  // exact-path terms of 8 tokens per thread, [8][4][512] fp32 over the operand
+  // tiles Kr .. Tt (dead once the score MMAs are skipped)
+  float* xs = reinterpret_cast<float*>(base + Lo::Kr);
+  static_assert(Lo::Tt + 8192 >= 8 * 4 * 512 * 4, "exact-path scratch");
+  float kh[16], qh[16];
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    if (!ch.fast) {
+#pragma unroll 1
+      for (int i = 0; i < 8; ++i) {
+        const int tok = 16 * cg + 8 * half + i;
+        const int r = tok < L ? tok : L - 1;
+        const size_t off = (size_t)r * ch.ldr + key;
+        const float gi = ch.g[off];
+        const float k1 = ch.rk[r] * to_f(ch.k[off]), q1 = ch.rq[r] * to_f(ch.q[off]);
+        const float kap = ch.beta[(size_t)r * ch.ldb] * k1;
+        const ExactTerms t = exact_terms(ch.g, ch.k, ch.q, ch.beta, ch.rk, ch.rq, ch.ldr, ch.ldb, base + Lo::dA,
+                                         base + Lo::dQ, r, key, L, gi, k1, q1, kap);
+        xs[(i * 4 + 0) * 512 + threadIdx.x] = t.dkh;
+        xs[(i * 4 + 1) * 512 + threadIdx.x] = t.dqh;
+        xs[(i * 4 + 2) * 512 + threadIdx.x] = t.dkap;
+        xs[(i * 4 + 3) * 512 + threadIdx.x] = t.dG;
+      }
+    }
+    // raw rows of 8 tokens first (no store in between), then the arithmetic
+    float gv[8], kv[8], qv[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int tok = 16 * cg + 8 * half + i;
+      const size_t off = (size_t)(tok < L ? tok : L - 1) * ch.ldr + key;
+      gv[i] = ch.g[off];
+      kv[i] = to_f(ch.k[off]);
+      qv[i] = to_f(ch.q[off]);
+    }
+    float dgv[8], db[8], dkd[8], dqd[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int ii = 8 * half + i;
+      const int tok = 16 * cg + ii;
+      const int r = tok < L ? tok : L - 1;
+      const float rk = ch.rk[r], rq = ch.rq[r], be = ch.beta[(size_t)r * ch.ldb];
+      const float gi = gv[i], k1 = rk * kv[i], q1 = rq * qv[i], kap = be * k1;
+      const float er = ex2a(gi - rr), ec = ex2a(rc - gi);
+      const float dKr = xk[ii], dQr = p.scale * xq[ii], dKc = xc[ii];
+      float dkh = dKr * er, dqh = dQr * er, dkap = dKc * ec;
+      float dG = dKr * k1 * er + dQr * q1 * er - dKc * kap * ec;
+      if (r == L - 1) dG += last;
+      if (!ch.fast) {
+        dkh += xs[(i * 4 + 0) * 512 + threadIdx.x];
+        dqh += xs[(i * 4 + 1) * 512 + threadIdx.x];
+        dkap += xs[(i * 4 + 2) * 512 + threadIdx.x];
+        dG += xs[(i * 4 + 3) * 512 + threadIdx.x];
+      }
+      dgv[i] = dG;
+      db[i] = dkap * k1;          // dbeta = <dkappa, k_hat>
+      dkh = fmaf(be, dkap, dkh);  // kappa = beta k_hat
+      dkd[i] = dkh * k1;
+      dqd[i] = dqh * q1;
+      xk[ii] = dkh;
+      xq[ii] = dqh;
+      kh[ii] = k1;
+      qh[ii] = q1;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int tok = 16 * cg + 8 * half + i;
+      if (tok < L) p.dg[tok_row(p, b, h, t0 + tok) * kKD + key] = dgv[i];
+    }
+    // token sums over this warp's 32 keys
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float a = db[i], d = dkd[i], e = dqd[i];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        a += __shfl_xor_sync(0xffffffffu, a, o);
+        d += __shfl_xor_sync(0xffffffffu, d, o);
+        e += __shfl_xor_sync(0xffffffffu, e, o);
+      }
+      if (lane == 0) {
+        const int tok = 16 * cg + 8 * half + i;
+        part[(q * 3 + 0) * C + tok] = a;
+        part[(q * 3 + 1) * C + tok] = d;
+        part[(q * 3 + 2) * C + tok] = e;
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < 3 * C) {
+    const int sidx = threadIdx.x / C, tok = threadIdx.x % C;
+    float t = 0.f;
+#pragma unroll
+    for (int qq = 0; qq < 4; ++qq) t += part[(qq * 3 + sidx) * C + tok];
+    tsum[threadIdx.x] = t;
+  }
+  __syncthreads();
+  {
+    float rkv[16], rqv[16], dkdot[16], dqdot[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int tok = 16 * cg + i;
+      rkv[i] = ch.rk[tok];
+      rqv[i] = ch.rq[tok];
+      dkdot[i] = tsum[C + tok];
+      dqdot[i] = tsum[2 * C + tok];
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int tok = 16 * cg + i;
+      if (tok < L) {
+        const size_t off = tok_row(p, b, h, t0 + tok) * kKD + key;
+        p.dk[off] = __float2bfloat16_rn(rkv[i] * (xk[i] - kh[i] * dkdot[i]));
+        p.dq[off] = __float2bfloat16_rn(rqv[i] * (xq[i] - qh[i] * dqdot[i]));
+      }
+    }
+  }
+  if (threadIdx.x < L) p.dbeta[tok_row(p, b, h, t0 + threadIdx.x)] = tsum[threadIdx.x];
+
+  if (threadIdx.x == 0) bulk_wait_all();
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::fence_after();
+    tc::dealloc(tmem, 512);
+  }
+}
+
+template <class CF>
+int launch_bwd_chunk_tc(const ScanParams& p, cudaStream_t st) {
+  const size_t smem = ChunkTcLayout<CF>::bytes;
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(scan_bwd_chunk_tc_kernel<CF>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
+      return check_launch("cudaFuncSetAttribute(scan_bwd_chunk_tc_kernel)");
+    configured = true;
+  }
+  ChunkMaps maps;
+  int rc = encode_bthd(&maps.v, p.v, true, p.B, p.T, p.H, kVD, 64, CF::C, true);
+  if (rc == KDN_OK) rc = encode_bthd(&maps.dO, p.dO, true, p.B, p.T, p.H, kVD, 64, CF::C, true);
+  if (rc == KDN_OK) rc = encode_bthd(&maps.dv, p.dv, true, p.B, p.T, p.H, kVD, kVD, CF::C, false);
+  if (rc != KDN_OK) return rc;
+  scan_bwd_chunk_tc_kernel<CF><<<dim3(p.NT, p.B * p.H), 512, smem, st>>>(p, maps);
+  return check_launch("scan_bwd_chunk_tc_kernel");
+}
+
+template int launch_bwd_chunk_tc<Cfg<true, 64, bf16>>(const ScanParams&, cudaStream_t);
+
+}  // namespace kdn

@@ -119,21 +119,22 @@ __global__ void __launch_bounds__(kPrepThreads, 2) scan_prep_kernel(ScanParams p
         }
       }
     }
-    // T, Qq = scale Q, Qt = scale Q^T: thread t owns columns 8(t%8)..+7 (columns >= C zero)
+    // T, Qq = scale Q, Qt = scale Q^T, Tt = T^T: thread t owns columns 8(t%8)..+7 (columns >= C zero)
     {
       const int g = threadIdx.x & 7;
 #pragma unroll 1
-      for (int m = 0; m < 3; ++m) {
-        char* dst = rec + (m == 0 ? RT::T : (m == 1 ? RT::Qq : RT::Qt));
-        const float mul = m == 0 ? 1.f : p.scale;
+      for (int m = 0; m < 4; ++m) {
+        char* dst = rec + (m == 0 ? RT::T : (m == 1 ? RT::Qq : (m == 2 ? RT::Qt : RT::Tt)));
+        const float mul = (m == 1 || m == 2) ? p.scale : 1.f;
         for (int r = threadIdx.x >> 3; r < C; r += kPrepThreads / 8) {
           float x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
           if (8 * g < C) {
             if (m < 2) {
               ld8(x, (m == 0 ? sTb : sQb) + r * CF::LDC + 8 * g);
             } else {
+              const OpT* src = m == 2 ? sQb : sTb;
 #pragma unroll
-              for (int i = 0; i < 8; ++i) x[i] = to_f(sQb[(8 * g + i) * CF::LDC + r]);
+              for (int i = 0; i < 8; ++i) x[i] = to_f(src[(8 * g + i) * CF::LDC + r]);
             }
 #pragma unroll
             for (int i = 0; i < 8; ++i) x[i] *= mul;
