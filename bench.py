@@ -9,7 +9,9 @@ than L2 (about 0.5 GB per step), so no explicit L2 flush is needed.
     python bench.py [--gpus N] [--steps K] [--warmup W] [--variant iso|diag] [--impl ours|reference]
 
 Under torchrun each rank runs its own batch of B=4 sequences (weak scaling,
-no collective on the data path); timing is max over ranks.
+no collective on the data path); timing is max over ranks.  The timed step
+is captured once in a CUDA graph and replayed (``--eager`` times eager steps
+instead; the JSON line carries both).
 """
 from __future__ import annotations
 
@@ -35,6 +37,10 @@ B, T, H, D = 4, 4096, 18, 128
 ISO_BYTES_PER_TH = {"scan_fwd": 1540, "scan_bwd": 2824, "gain": 48}
 DIAG_BYTES_PER_TH = {"scan_fwd": 2304, "scan_bwd": 4096, "gain_fwd": 2052, "gain_bwd": 3592}
 FLOPS_PER_TH = 540_672  # 3 * 2 * (3 d^2 + 5 C d), C = 64
+# DRAM bytes (read + write) per token-head of one kdn_scan_bwd call (reverse
+# sweep + chunk kernel): ncu dram__bytes_read.sum + dram__bytes_write.sum of
+# the two kernels at B=1 T=4096 H=18, divided by its 73,728 token-heads
+SCAN_BWD_TRAFFIC_PER_TH = {"iso": 5836, "diag": None}
 
 
 def load_peaks():
@@ -161,6 +167,23 @@ GRAD_NAMES = {"iso": ("q", "k", "v", "g_cumsum", "a", "omega", "r"),
 LAUNCHES_PER_STEP = {"iso": 6, "diag": 10}  # gain fwd 1|3, scan fwd 2, scan bwd 2, gain bwd 1|3
 
 
+def capture_step(step, x, device):
+    """One step (forward + backward through the public operators) captured in
+    a CUDA graph on a side stream, after two warm-up steps on that stream."""
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            step(x)
+    torch.cuda.current_stream(device).wait_stream(side)
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step(x)
+    torch.cuda.synchronize(device)
+    return graph
+
+
 def time_region(fn, steps, device):
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize(device)
@@ -268,6 +291,7 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--eager", action="store_true", help="time eager steps instead of a replayed CUDA graph")
     ap.add_argument("--batch", type=int, default=B, help="sequences per GPU (profiling runs use smaller cases)")
     args = ap.parse_args()
     globals()["B"] = args.batch
@@ -318,13 +342,28 @@ def main():
         if dist is not None:
             dist.barrier()
 
+    # eager steps: every step pays the Python / autograd dispatch of the public operators
+    barrier()
+    eager_ms = time_region(lambda: step(x), args.steps, device)
+    # the same step captured once in a CUDA graph and replayed, as a training
+    # loop with graphs runs it: identical kernels and inputs, no host dispatch
+    graph, timing = None, "eager"
+    if not args.eager:
+        try:
+            graph = capture_step(step, x, device)
+            timing = "cuda_graph"
+        except Exception as e:  # the eager number stands if capture is unavailable
+            print(f"bench: CUDA graph capture failed ({type(e).__name__}: {e}); timing eager steps", file=sys.stderr)
+    run = graph.replay if graph is not None else (lambda: step(x))
+    for _ in range(warmup):
+        run()
     barrier()
     torch.cuda.synchronize(device)
     with ClockSampler(local) as clk:
         start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record()
         for _ in range(args.steps):
-            step(x)
+            run()
         stop.record()
         torch.cuda.synchronize(device)
     barrier()
@@ -374,14 +413,16 @@ def main():
     roofline = {
         "kernel": "kdn_scan_bwd (scan_bwd_state + scan_bwd_chunk)",
         "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-        "peak_kind": peak_kind, "traffic": None,
+        "peak_kind": peak_kind,
+        "traffic": SCAN_BWD_TRAFFIC_PER_TH.get(args.variant) and SCAN_BWD_TRAFFIC_PER_TH[args.variant] * th,
         "step_frac": (step_bytes / (ms * 1e-3) / 1e9) / hbm,
         "op_ms": ops,
     }
 
     out = {
         "metric": METRIC, "value": value, "unit": "Mtok/s", "n_gpus": world, "steps": args.steps, "warmup": warmup,
-        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "ms_per_step": ms, "timing": timing, "eager_ms_per_step": eager_ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic",
         "config": {"workload": f"iso_kdn gain+scan fwd+bwd B{B} T{T} H{H} d{D} (config 1)" if args.variant == "iso"
                    else f"diag_kdn gain+scan fwd+bwd B{B} T{T} H{H} d{D} (config 2)",
