@@ -29,6 +29,10 @@ for _p in (ROOT, os.path.join(ROOT, "kalman-delta-networks_b200")):
     if _p not in sys.path:
         sys.path.insert(0, _p)
 
+if "--varlen" in sys.argv:
+    # the packed step allocates ~15 GB on several streams; per-stream caches fragment without this
+    os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
+
 import torch  # noqa: E402
 
 METRIC = "KDN scan fwd+bwd Mtok/s/GPU (B4,T4096,H18,d128 bf16), % of roofline"
@@ -136,6 +140,50 @@ def make_diag(device, seed):
     x["prec"] = torch.ones(H, device=device)
     x["dO"] = torch.randn(B, T, H, D, generator=g, device=device)
     return x
+
+
+VARLEN_T = 131072  # config 4: sequences of lengths ~ U[256, 8192] packed to 131,072 tokens
+
+
+def varlen_lengths(seed, total=VARLEN_T, lo=256, hi=8192):
+    gen = torch.Generator().manual_seed(seed)
+    lens = []
+    while sum(lens) < total:
+        lens.append(int(torch.randint(lo, hi + 1, (1,), generator=gen)))
+    lens[-1] -= sum(lens) - total
+    return lens
+
+
+def make_diag_varlen(device, seed):
+    """Config 4's packed batch: make_diag at B = 1, T = 131,072, with the
+    gate prefix restarting every 32 tokens from each sequence's first token."""
+    x = make_diag(device, seed)
+    lens = varlen_lengths(seed)
+    cu = [0]
+    for n in lens:
+        cu.append(cu[-1] + n)
+    log_alpha = torch.log(x["alpha"])
+    g = torch.empty_like(log_alpha)
+    for a, b in zip(cu, cu[1:]):
+        n = b - a
+        pad = (-n) % 32
+        la = torch.nn.functional.pad(log_alpha[:, a:b], (0, 0, 0, 0, 0, pad))
+        g[:, a:b] = (la.view(1, (n + pad) // 32, 32, H, D).cumsum(2) * 1.4426950408889634).view(1, n + pad, H, D)[:, :n]
+    x["g_cumsum"] = g.contiguous()
+    x["cu"] = cu
+    return x
+
+
+def step_diag_varlen(x):
+    from kdn_b200 import varlen
+
+    L = leafify(x, ("q", "k", "v", "g_cumsum", "k_gain", "alpha", "prec", "omega_raw", "r_raw"))
+    kappa = varlen.diag_kdn_gain_varlen(L["k_gain"], L["alpha"], L["omega"], L["r"], L["prec"], L["omega_raw"],
+                                        L["r_raw"], x["cu"])
+    o = varlen.chunk_kalman_varlen(L["q"], L["k"], kappa, L["v"], L["g_cumsum"], float(D ** -0.5), x["cu"])
+    o.backward(x["dO"])
+    varlen.join(x["dO"].device)
+    return L
 
 
 def leafify(x, names):
@@ -292,9 +340,15 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--eager", action="store_true", help="time eager steps instead of a replayed CUDA graph")
+    ap.add_argument("--varlen", action="store_true",
+                    help="config 4 packed batch: diag, B=1, T=131072 of sequences ~U[256, 8192] (cu_seqlens)")
     ap.add_argument("--batch", type=int, default=B, help="sequences per GPU (profiling runs use smaller cases)")
     args = ap.parse_args()
     globals()["B"] = args.batch
+    if args.varlen:
+        args.variant = "diag"
+        globals()["B"], globals()["T"] = 1, VARLEN_T
+        args.eager = True  # autograd runs the sequences' backward on several streams: timed eagerly
     warmup = max(args.warmup, 3)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -332,8 +386,11 @@ def main():
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
 
-    x = (make_iso if args.variant == "iso" else make_diag)(device, seed=1234 + rank)
-    step = step_iso if args.variant == "iso" else step_diag
+    if args.varlen:
+        x, step = make_diag_varlen(device, seed=1234 + rank), step_diag_varlen
+    else:
+        x = (make_iso if args.variant == "iso" else make_diag)(device, seed=1234 + rank)
+        step = step_iso if args.variant == "iso" else step_diag
     for _ in range(warmup):
         step(x)
     torch.cuda.synchronize(device)
@@ -382,13 +439,13 @@ def main():
     e2e = None
     if not args.no_e2e:
         names = GRAD_NAMES[args.variant]
-        host = {n: v.detach().cpu().pin_memory() for n, v in x.items()}
+        host = {n: (v.detach().cpu().pin_memory() if isinstance(v, torch.Tensor) else v) for n, v in x.items()}
         grads_host = {n: torch.empty(x[n].shape, dtype=x[n].dtype).pin_memory() for n in names}
-        h2d = sum(v.numel() * v.element_size() for v in host.values())
+        h2d = sum(v.numel() * v.element_size() for v in host.values() if isinstance(v, torch.Tensor))
         d2h = sum(v.numel() * v.element_size() for v in grads_host.values())
 
         def e2e_step():
-            xd = {n: v.to(device, non_blocking=True) for n, v in host.items()}
+            xd = {n: (v.to(device, non_blocking=True) if isinstance(v, torch.Tensor) else v) for n, v in host.items()}
             L = step(xd)
             for n in names:
                 grads_host[n].copy_(L[n].grad, non_blocking=True)
@@ -404,36 +461,45 @@ def main():
         e2e = {"value": tokens / (e2e_ms * 1e-3) / 1e6, "unit": "Mtok/s", "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms}
 
-    ops = per_op_times(args.variant, x, device)
     per_th = ISO_BYTES_PER_TH if args.variant == "iso" else DIAG_BYTES_PER_TH
-    # dominant kernel call: the scan backward (reverse state sweep + chunk-parallel gradients)
-    bwd_bytes = per_th["scan_bwd"] * th
-    achieved = bwd_bytes / (ops["scan_bwd_ms"] * 1e-3) / 1e9
     step_bytes = sum(per_th.values()) * th
-    roofline = {
-        "kernel": "kdn_scan_bwd (scan_bwd_state + scan_bwd_chunk)",
-        "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-        "peak_kind": peak_kind,
-        "traffic": SCAN_BWD_TRAFFIC_PER_TH.get(args.variant) and SCAN_BWD_TRAFFIC_PER_TH[args.variant] * th,
-        "step_frac": (step_bytes / (ms * 1e-3) / 1e9) / hbm,
-        "op_ms": ops,
-    }
+    if args.varlen:
+        # packed sequences run as per-sequence calls on several streams: the whole step is the unit
+        achieved = step_bytes / (ms * 1e-3) / 1e9
+        roofline = {"kernel": "whole varlen step (gain + scan, fwd + bwd, all sequences)", "bound": "hbm",
+                    "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                    "peak_kind": peak_kind, "traffic": None, "step_frac": achieved / hbm}
+    else:
+        ops = per_op_times(args.variant, x, device)
+        # dominant kernel call: the scan backward (reverse state sweep + chunk-parallel gradients)
+        bwd_bytes = per_th["scan_bwd"] * th
+        achieved = bwd_bytes / (ops["scan_bwd_ms"] * 1e-3) / 1e9
+        roofline = {
+            "kernel": "kdn_scan_bwd (scan_bwd_state + scan_bwd_chunk)",
+            "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+            "peak_kind": peak_kind,
+            "traffic": SCAN_BWD_TRAFFIC_PER_TH.get(args.variant) and SCAN_BWD_TRAFFIC_PER_TH[args.variant] * th,
+            "step_frac": (step_bytes / (ms * 1e-3) / 1e9) / hbm,
+            "op_ms": ops,
+        }
 
     out = {
         "metric": METRIC, "value": value, "unit": "Mtok/s", "n_gpus": world, "steps": args.steps, "warmup": warmup,
         "ms_per_step": ms, "timing": timing, "eager_ms_per_step": eager_ms,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"iso_kdn gain+scan fwd+bwd B{B} T{T} H{H} d{D} (config 1)" if args.variant == "iso"
+        "config": {"workload": (f"diag_kdn gain+scan fwd+bwd, {len(x['cu']) - 1} packed sequences ~U[256,8192], "
+                                f"T{T} H{H} d{D} (config 4 varlen)") if args.varlen
+                   else f"iso_kdn gain+scan fwd+bwd B{B} T{T} H{H} d{D} (config 1)" if args.variant == "iso"
                    else f"diag_kdn gain+scan fwd+bwd B{B} T{T} H{H} d{D} (config 2)",
                    "global_batch": B * world, "seq_len": T, "heads": H, "head_dim": D,
                    "parallelism": f"batch-sharded x{world}", "l2": "inputs > L2 (no flush)"},
-        "gpu_launches": LAUNCHES_PER_STEP[args.variant] * args.steps,
+        "gpu_launches": LAUNCHES_PER_STEP[args.variant] * args.steps * (len(x["cu"]) - 1 if args.varlen else 1),
         "e2e": e2e,
         "roofline": roofline,
         "clocks": clk.summary(),
     }
-    if rank == 0 and world == 1 and not args.no_cpu:
+    if rank == 0 and world == 1 and not args.no_cpu and not args.varlen:
         out["cpu_baseline"] = cpu_baseline(args.variant)
     if rank == 0:
         print(json.dumps(out))

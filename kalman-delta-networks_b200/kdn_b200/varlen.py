@@ -35,6 +35,17 @@ def _streams(device: torch.device, n: int) -> list[torch.cuda.Stream]:
     return pool[:n]
 
 
+def join(device=None) -> None:
+    """Make the current stream wait for every pool stream of ``device``: call
+    after ``backward`` when the next work (or a CUDA graph capture) must see
+    all per-sequence gradients on the current stream."""
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    cur = torch.cuda.current_stream(device)
+    for s in _POOL.get(key, []):
+        cur.wait_stream(s)
+
+
 def offsets(cu_seqlens) -> list[int]:
     """Host list of the token offsets; validates monotonicity."""
     cu = cu_seqlens.tolist() if isinstance(cu_seqlens, torch.Tensor) else list(cu_seqlens)
@@ -44,7 +55,7 @@ def offsets(cu_seqlens) -> list[int]:
     return cu
 
 
-def map_sequences(fn: Callable, tensors: Sequence, cu_seqlens, *, streams: int = 8):
+def map_sequences(fn: Callable, tensors: Sequence, cu_seqlens, *, streams: int = 4):
     """Apply ``fn(*slices)`` to every sequence (slices along dim 1 of the
     [1, T, ...] tensors; other arguments pass through) on a pool of streams and
     concatenate each output along dim 1."""
@@ -76,7 +87,7 @@ def map_sequences(fn: Callable, tensors: Sequence, cu_seqlens, *, streams: int =
     return torch.cat(outs, dim=1)
 
 
-def chunk_kalman_varlen(q_memory, k_memory, kappa, v, g_cumsum, scale: float, cu_seqlens, *, streams: int = 8):
+def chunk_kalman_varlen(q_memory, k_memory, kappa, v, g_cumsum, scale: float, cu_seqlens, *, streams: int = 4):
     """``chunk_kalman`` over a packed batch (fp32 output [1, T, H, V])."""
     def one(q, k, kap, vv, g):
         return diag_kdn_chunk.chunk_kalman(q.contiguous(), k.contiguous(), kap.contiguous(), vv.contiguous(),
@@ -86,7 +97,7 @@ def chunk_kalman_varlen(q_memory, k_memory, kappa, v, g_cumsum, scale: float, cu
 
 
 def diag_kdn_gain_varlen(k_gain, alpha, omega, r, initial_precision, omega_raw, r_raw, cu_seqlens, *,
-                         streams: int = 8):
+                         streams: int = 4):
     """``_diag_kdn_gain`` over a packed batch: the covariance restarts at every sequence."""
     def one(kg, a, w, rr, wr, rrr):
         return diag_kdn_chunk._diag_kdn_gain(kg.contiguous(), a.contiguous(), w.contiguous(), rr.contiguous(),
@@ -96,7 +107,7 @@ def diag_kdn_gain_varlen(k_gain, alpha, omega, r, initial_precision, omega_raw, 
 
 
 def chunk_kda_precumsum_varlen(q, k, v, g_cumsum, beta, scale: float | None = None, *, cu_seqlens,
-                               streams: int = 8):
+                               streams: int = 4):
     """``_chunk_kda_precumsum_paired`` over a packed batch."""
     def one(qq, kk, vv, g, b):
         return iso_kdn_chunk._chunk_kda_precumsum_paired(qq.contiguous(), kk.contiguous(), vv.contiguous(),
@@ -106,7 +117,7 @@ def chunk_kda_precumsum_varlen(q, k, v, g_cumsum, beta, scale: float | None = No
 
 
 def iso_kdn_gain_varlen(a, omega, r, initial_precision, *, head_dim: int, cu_seqlens, out_dtype=None,
-                        info_scale=None, streams: int = 8):
+                        info_scale=None, streams: int = 4):
     """``iso_kdn_gain`` over a packed batch: the covariance restarts at every sequence."""
     def one(aa, w, rr):
         return iso_kdn_chunk.iso_kdn_gain(aa.contiguous(), w.contiguous(), rr.contiguous(), initial_precision,
@@ -116,4 +127,4 @@ def iso_kdn_gain_varlen(a, omega, r, initial_precision, *, head_dim: int, cu_seq
 
 
 __all__ = ("chunk_kalman_varlen", "diag_kdn_gain_varlen", "chunk_kda_precumsum_varlen", "iso_kdn_gain_varlen",
-           "map_sequences", "offsets")
+           "map_sequences", "offsets", "join")
