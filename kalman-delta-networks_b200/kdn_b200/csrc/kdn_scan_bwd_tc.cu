@@ -23,7 +23,8 @@
 namespace kdn {
 
 struct alignas(64) ChunkMaps {
-  CUtensorMap v, dO, dv;
+  CUtensorMap v, dO, dv;  // value rows (128-byte swizzle), dv rows (plain)
+  CUtensorMap g, k, q;    // the chunk's raw rows again, plain, for the gate mapping
 };
 
 template <class CF>
@@ -36,9 +37,10 @@ struct ChunkTcLayout {
   static constexpr size_t G = 65536;
   static constexpr size_t Qt = G, Kf = G + 8192, Wf = G + 8192 + 16384;
   static constexpr size_t Del = G, DDel = G + 16384;
-  // v | dO, then the dv rows
+  // v | dO, then the dv rows, then the raw k | q rows of the gate mapping
   static constexpr size_t V = G + 40960;
-  static constexpr size_t vv = V, dO = V + 16384, dvst = V;
+  static constexpr size_t vv = V, dO = V + 16384, dvst = V, rk = V, rq = V + 16384;
+  static constexpr size_t rg = G;  // raw g rows [C][KD] fp32 over delta | ddelta
   // S0 | dS (saved states), then dW dQ dQu dT X dA
   static constexpr size_t A = V + 32768;
   static constexpr size_t S0 = A, dS = A + 32768;
@@ -105,7 +107,8 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
   const size_t cc = (size_t)bh * p.NT + c;
   uint64_t* ldbar = reinterpret_cast<uint64_t*>(base + Lo::bar);
   uint64_t* mmab = ldbar + 1;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(mmab + 1);
+  uint64_t* rawbar = ldbar + 2;  // the raw rows of the gate mapping
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(ldbar + 3);
   float* small = reinterpret_cast<float*>(base + Lo::small);
   float* cfl = small + small_floats<CF>();
   float* cgl = cfl + kKD;
@@ -124,6 +127,7 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
   if (threadIdx.x == 0) {
     mbar_init(ldbar, 1);
     mbar_init(mmab, 1);
+    mbar_init(rawbar, 1);
     fence_mbar_init();
   }
   if (warp == 0) tc::alloc(tslot, 512);
@@ -295,6 +299,9 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
     for (int ks = 0; ks < kKD / 16; ++ks)
       tc::mma(tmem + TDT, tc::desc_k(base + Lo::dW, C, ks), tc::desc_k(base + Lo::Kr, C, ks), id_cc, true);
     tc::commit(mmab);
+    // the delta tiles are dead: the raw g rows of the gate mapping come back meanwhile
+    mbar_expect_tx(rawbar, C * kKD * 8);
+    tma_load_4d(base + Lo::rg, &maps.g, 0, h, t0, b, rawbar);
   }
   mma_wait();
   auto cc_tile = [&](uint32_t col, size_t tile, float sign, bool strict) {
@@ -319,6 +326,10 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
     for (int ks = 0; ks < C / 16; ++ks)
       tc::mma(tmem + TX, tc::desc_k(base + Lo::dT, C, ks), tc::desc_k(base + Lo::T, C, ks), id_cc, ks > 0);
     tc::commit(mmab);
+    // ... and the raw k, q rows over the value tiles once the dv rows have left
+    bulk_wait_read<0>();
+    tma_load_4d(base + Lo::rk, &maps.k, 0, h, t0, b, rawbar);
+    tma_load_4d(base + Lo::rq, &maps.q, 0, h, t0, b, rawbar);
   }
   mma_wait();
   cc_tile(TX, Lo::X, 1.f, true);
@@ -352,6 +363,7 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
   }
 
   // ---- gate mapping: lane = key, 16 tokens per thread
+  mbar_wait(rawbar, 0, p.status);
   const int key = 32 * q + lane;
   float xk[16], xq[16], xc[16];
   tc::ld16(tq + TKR + 16 * cg, xk);
@@ -385,15 +397,15 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
         xs[(i * 4 + 3) * 512 + threadIdx.x] = t.dG;
       }
     }
-    // raw rows of 8 tokens first (no store in between), then the arithmetic
+    // raw rows of 8 tokens (shared memory), then the arithmetic
     float gv[8], kv[8], qv[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int tok = 16 * cg + 8 * half + i;
-      const size_t off = (size_t)(tok < L ? tok : L - 1) * ch.ldr + key;
-      gv[i] = ch.g[off];
-      kv[i] = to_f(ch.k[off]);
-      qv[i] = to_f(ch.q[off]);
+      const int r = tok < L ? tok : L - 1;
+      gv[i] = reinterpret_cast<const float*>(base + Lo::rg)[r * kKD + key];
+      kv[i] = to_f(bf(Lo::rk)[r * kKD + key]);
+      qv[i] = to_f(bf(Lo::rq)[r * kKD + key]);
     }
     float dgv[8], db[8], dkd[8], dqd[8];
 #pragma unroll
@@ -501,6 +513,9 @@ int launch_bwd_chunk_tc(const ScanParams& p, cudaStream_t st) {
   int rc = encode_bthd(&maps.v, p.v, true, p.B, p.T, p.H, kVD, 64, CF::C, true);
   if (rc == KDN_OK) rc = encode_bthd(&maps.dO, p.dO, true, p.B, p.T, p.H, kVD, 64, CF::C, true);
   if (rc == KDN_OK) rc = encode_bthd(&maps.dv, p.dv, true, p.B, p.T, p.H, kVD, kVD, CF::C, false);
+  if (rc == KDN_OK) rc = encode_bthd(&maps.g, p.g, false, p.B, p.T, p.H, kKD, kKD, CF::C, false);
+  if (rc == KDN_OK) rc = encode_bthd(&maps.k, p.k, true, p.B, p.T, p.H, kKD, kKD, CF::C, false);
+  if (rc == KDN_OK) rc = encode_bthd(&maps.q, p.q, true, p.B, p.T, p.H, kKD, kKD, CF::C, false);
   if (rc != KDN_OK) return rc;
   scan_bwd_chunk_tc_kernel<CF><<<dim3(p.NT, p.B * p.H), 512, smem, st>>>(p, maps);
   return check_launch("scan_bwd_chunk_tc_kernel");
