@@ -270,19 +270,32 @@ __device__ __forceinline__ float qhat_at(const Chunk<CF>& ch, int i, int c) {
 }
 
 // One row's raw values for the 8 channels a thread handles.
+// k and q stay packed (8 bf16 in 16 bytes) until used, so that all of a
+// thread's rows can be in flight at once.
 template <class CF>
 struct RawRow {
-  float g[8], k[8], q[8], kap[CF::ISO ? 1 : 8];
+  float g[8], kap[CF::ISO ? 1 : 8];
+  uint4 kp, qp;
   float beta;
 };
+
+__device__ __forceinline__ void unpack8(float (&d)[8], const uint4& u) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    d[2 * i] = f.x;
+    d[2 * i + 1] = f.y;
+  }
+}
 
 template <class CF>
 __device__ __forceinline__ void load_row(RawRow<CF>& x, const Chunk<CF>& ch, int r, int c0) {
   if (r < ch.L) {
     const size_t o = (size_t)r * ch.ldr + c0;
     ld8(x.g, ch.g + o);
-    ld8(x.k, ch.k + o);
-    ld8(x.q, ch.q + o);
+    x.kp = *reinterpret_cast<const uint4*>(ch.k + o);
+    x.qp = *reinterpret_cast<const uint4*>(ch.q + o);
     if constexpr (CF::ISO) {
       x.beta = ch.beta[(size_t)r * ch.ldb];
     } else {
@@ -292,9 +305,10 @@ __device__ __forceinline__ void load_row(RawRow<CF>& x, const Chunk<CF>& ch, int
   } else {
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      x.g[i] = x.k[i] = x.q[i] = 0.f;
+      x.g[i] = 0.f;
       if constexpr (!CF::ISO) x.kap[i] = 0.f;
     }
+    x.kp = x.qp = make_uint4(0, 0, 0, 0);
     x.beta = 0.f;
   }
 }
@@ -308,13 +322,16 @@ __device__ __forceinline__ void build_operands(const Chunk<CF>& ch, int r, int c
   float kr[8], qr[8], kc[8];
   if (r < ch.L) {
     const float bs = CF::ISO ? x.beta * ks : 1.f;
+    float k8[8], q8[8];
+    unpack8(k8, x.kp);
+    unpack8(q8, x.qp);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const float er = ex2a(x.g[i] - rr[i]);
       const float ec = ex2a(rc[i] - x.g[i]);
-      kr[i] = x.k[i] * ks * er;
-      qr[i] = x.q[i] * qs * er;
-      kc[i] = (CF::ISO ? x.k[i] : x.kap[i]) * bs * ec;
+      kr[i] = k8[i] * ks * er;
+      qr[i] = q8[i] * qs * er;
+      kc[i] = (CF::ISO ? k8[i] : x.kap[i]) * bs * ec;
     }
   } else {
 #pragma unroll
@@ -336,15 +353,16 @@ __device__ __forceinline__ void build_operands(const Chunk<CF>& ch, int r, int c
 // Row norms (iso), range check, per-channel factors and the three gated
 // operands, for a block of NTH threads.  Thread t handles channels
 // 8*(t%16) .. +7 of rows t/16, t/16 + NTH/16, ...; the 16 threads of a row
-// are one half-warp, so row norms are half-warp shuffles.  Rows are loaded
-// two at a time ahead of their arithmetic (they may come straight from HBM).
+// are one half-warp, so row norms are half-warp shuffles.  All of a thread's
+// rows (up to 4) are loaded ahead of their arithmetic (they may come straight
+// from HBM).
 // The operands are built with the fast-path reference (the gate of the
 // middle row, known up front) and built again only when the range check
 // sends the chunk to the exact path.  Contains one barrier; the caller
 // places the barrier that publishes the results.
 template <class CF, int NTH, bool SW = false>
 __device__ void prep_chunk(Chunk<CF>& ch) {
-  constexpr int C = CF::C, RSTEP = NTH / 16, RPT = C / RSTEP, BATCH = RPT >= 2 ? 2 : 1;
+  constexpr int C = CF::C, RSTEP = NTH / 16, RPT = C / RSTEP, BATCH = RPT <= 4 ? RPT : 2;
   static_assert(NTH % 32 == 0 && C % RSTEP == 0 && RPT % BATCH == 0, "rows per thread");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int L = ch.L;
@@ -364,11 +382,13 @@ __device__ void prep_chunk(Chunk<CF>& ch) {
       const int r = rt + (j0 + j) * RSTEP;
       float qs = 1.f, ks = 1.f;
       if constexpr (CF::ISO) {
-        float sq = 0.f, sk = 0.f;
+        float sq = 0.f, sk = 0.f, k8[8], q8[8];
+        unpack8(k8, x[j].kp);
+        unpack8(q8, x[j].qp);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          sq = fmaf(x[j].q[i], x[j].q[i], sq);
-          sk = fmaf(x[j].k[i], x[j].k[i], sk);
+          sq = fmaf(q8[i], q8[i], sq);
+          sk = fmaf(k8[i], k8[i], sk);
         }
 #pragma unroll
         for (int o = 1; o < 16; o <<= 1) {

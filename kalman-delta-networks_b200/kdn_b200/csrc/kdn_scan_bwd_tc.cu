@@ -441,22 +441,28 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
       const int tok = 16 * cg + 8 * half + i;
       if (tok < L) p.dg[tok_row(p, b, h, t0 + tok) * kKD + key] = dgv[i];
     }
-    // token sums over this warp's 32 keys
+    // token sums over this warp's 32 keys: one transpose-reduce leaves the sum
+    // of value j in lane j (j = 8 * quantity + token)
+    {
+      float v32[32];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      float a = db[i], d = dkd[i], e = dqd[i];
+      for (int i = 0; i < 8; ++i) {
+        v32[i] = db[i];
+        v32[8 + i] = dkd[i];
+        v32[16 + i] = dqd[i];
+        v32[24 + i] = 0.f;
+      }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        a += __shfl_xor_sync(0xffffffffu, a, o);
-        d += __shfl_xor_sync(0xffffffffu, d, o);
-        e += __shfl_xor_sync(0xffffffffu, e, o);
+      for (int off = 16; off >= 1; off >>= 1) {
+        const bool upper = lane & off;
+#pragma unroll
+        for (int i = 0; i < off; ++i) {
+          const float send = upper ? v32[i] : v32[i + off];
+          const float keep = upper ? v32[i + off] : v32[i];
+          v32[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
       }
-      if (lane == 0) {
-        const int tok = 16 * cg + 8 * half + i;
-        part[(q * 3 + 0) * C + tok] = a;
-        part[(q * 3 + 1) * C + tok] = d;
-        part[(q * 3 + 2) * C + tok] = e;
-      }
+      if (lane < 24) part[(q * 3 + (lane >> 3)) * C + 16 * cg + 8 * half + (lane & 7)] = v32[0];
     }
   }
   __syncthreads();
