@@ -57,47 +57,63 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+    """SM clock and throttle reasons from one ``nvidia-smi -lms`` process.
+
+    The process starts before the warm-up replays, so its start-up (driver
+    queries, process creation) falls outside the timed region; ``summary``
+    keeps the samples taken from the first warm-up replay to the end of the
+    timed region, the same load throughout."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int):
-        self.index = index
-        self.samples = []
-        self._stop = threading.Event()
-        self._thread = threading.Thread(target=self._run, daemon=True)
+    def __init__(self, index: int, period_ms: int = 50):
+        self.index, self.period_ms = index, period_ms
+        self.samples = []  # (time.monotonic(), fields)
+        self._proc = None
+        self._thread = None
 
-    def _run(self):
-        while not self._stop.is_set():
-            try:
-                out = subprocess.run(
-                    ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits"],
-                    capture_output=True, text=True, timeout=5,
-                ).stdout.strip()
-                if out:
-                    self.samples.append([x.strip() for x in out.split(",")])
-            except Exception:
-                pass
-            self._stop.wait(0.2)
-
-    def __enter__(self):
+    def start(self):
+        try:
+            self._proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", str(self.period_ms)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            return self
+        self._thread = threading.Thread(target=self._read, daemon=True)
         self._thread.start()
+        deadline = time.monotonic() + 5.0  # first sample: the process is up
+        while not self.samples and self._proc.poll() is None and time.monotonic() < deadline:
+            time.sleep(0.02)
         return self
 
-    def __exit__(self, *exc):
-        self._stop.set()
-        self._thread.join(timeout=10)
+    def _read(self):
+        for line in self._proc.stdout:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) == 6:
+                self.samples.append((time.monotonic(), f))
 
-    def summary(self):
-        if not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
-        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+    def stop(self):
+        if self._proc is not None and self._proc.poll() is None:
+            self._proc.terminate()
+            try:
+                self._proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self._proc.kill()
+        if self._thread is not None:
+            self._thread.join(timeout=5)
+
+    def summary(self, t0: float, t1: float):
+        rows = [f for t, f in self.samples if t0 <= t <= t1 + self.period_ms / 1000.0]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(s[0]) for s in rows if s[0].replace(".", "").isdigit()]
+        mx = [float(s[1]) for s in rows if s[1].replace(".", "").isdigit()]
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        reasons = sorted({names[i] for s in self.samples for i in range(4) if s[2 + i].lower() == "active"})
+        reasons = sorted({names[i] for s in rows for i in range(4) if s[2 + i].lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.samples)}
+                "reasons": reasons, "samples": len(rows), "window": "warm-up replays + timed steps"}
 
 
 # ----------------------------------------------------------------------------- inputs
@@ -412,17 +428,20 @@ def main():
         except Exception as e:  # the eager number stands if capture is unavailable
             print(f"bench: CUDA graph capture failed ({type(e).__name__}: {e}); timing eager steps", file=sys.stderr)
     run = graph.replay if graph is not None else (lambda: step(x))
+    clk = ClockSampler(local).start()
+    t_load = time.monotonic()
     for _ in range(warmup):
         run()
     barrier()
     torch.cuda.synchronize(device)
-    with ClockSampler(local) as clk:
-        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        start.record()
-        for _ in range(args.steps):
-            run()
-        stop.record()
-        torch.cuda.synchronize(device)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        run()
+    stop.record()
+    torch.cuda.synchronize(device)
+    clocks = clk.summary(t_load, time.monotonic())
+    clk.stop()
     barrier()
     ms = start.elapsed_time(stop) / args.steps
     if dist is not None:
@@ -497,7 +516,7 @@ def main():
         "gpu_launches": LAUNCHES_PER_STEP[args.variant] * args.steps * (len(x["cu"]) - 1 if args.varlen else 1),
         "e2e": e2e,
         "roofline": roofline,
-        "clocks": clk.summary(),
+        "clocks": clocks,
     }
     if rank == 0 and world == 1 and not args.no_cpu and not args.varlen:
         out["cpu_baseline"] = cpu_baseline(args.variant)
