@@ -19,7 +19,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -57,62 +56,80 @@ def load_peaks():
 
 
 class ClockSampler:
-    """SM clock and throttle reasons from one ``nvidia-smi -lms`` process.
+    """SM clock and throttle reasons read through NVML (in-process, no child
+    process) every ``period_ms`` by a background thread.
 
-    The process starts before the warm-up replays, so its start-up (driver
-    queries, process creation) falls outside the timed region; ``summary``
-    keeps the samples taken from the first warm-up replay to the end of the
-    timed region, the same load throughout."""
+    ``start`` runs before the warm-up replays; ``summary`` keeps the samples
+    taken from the first warm-up replay to the end of the timed region, one
+    load throughout.  Reading clocks changes no GPU setting."""
 
-    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown", 0x8),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap", 0x4))
 
-    def __init__(self, index: int, period_ms: int = 50):
-        self.index, self.period_ms = index, period_ms
-        self.samples = []  # (time.monotonic(), fields)
-        self._proc = None
+    def __init__(self, device: torch.device, period_ms: int = 10):
+        self.device, self.period = device, period_ms / 1000.0
+        self.samples = []  # (time.monotonic(), sm MHz, max sm MHz, reason bits)
+        self._stop = threading.Event()
         self._thread = None
+        self._nvml = None
+
+    def _handle(self, nvml):
+        props = torch.cuda.get_device_properties(self.device)
+        bus = getattr(props, "pci_bus_id", None)
+        if bus is not None:
+            pci = f"{getattr(props, 'pci_domain_id', 0):08x}:{bus:02x}:{getattr(props, 'pci_device_id', 0):02x}.0"
+            try:
+                return nvml.nvmlDeviceGetHandleByPciBusId(pci)
+            except nvml.NVMLError:
+                pass
+        return nvml.nvmlDeviceGetHandleByIndex(self.device.index or 0)
 
     def start(self):
         try:
-            self._proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", str(self.period_ms)],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
+            import pynvml as nvml
+
+            nvml.nvmlInit()
+            self._nvml = nvml
+            handle = self._handle(nvml)
+            mx = nvml.nvmlDeviceGetMaxClockInfo(handle, nvml.NVML_CLOCK_SM)
+        except Exception:
             return self
-        self._thread = threading.Thread(target=self._read, daemon=True)
+        get_reasons = getattr(nvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nvml.nvmlDeviceGetCurrentClocksThrottleReasons
+
+        def run():
+            while not self._stop.is_set():
+                try:
+                    sm = nvml.nvmlDeviceGetClockInfo(handle, nvml.NVML_CLOCK_SM)
+                    self.samples.append((time.monotonic(), sm, mx, get_reasons(handle)))
+                except Exception:
+                    pass
+                self._stop.wait(self.period)
+
+        self._thread = threading.Thread(target=run, daemon=True)
         self._thread.start()
-        deadline = time.monotonic() + 5.0  # first sample: the process is up
-        while not self.samples and self._proc.poll() is None and time.monotonic() < deadline:
-            time.sleep(0.02)
         return self
 
-    def _read(self):
-        for line in self._proc.stdout:
-            f = [x.strip() for x in line.split(",")]
-            if len(f) == 6:
-                self.samples.append((time.monotonic(), f))
-
     def stop(self):
-        if self._proc is not None and self._proc.poll() is None:
-            self._proc.terminate()
-            try:
-                self._proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self._proc.kill()
+        self._stop.set()
         if self._thread is not None:
             self._thread.join(timeout=5)
+        if self._nvml is not None:
+            try:
+                self._nvml.nvmlShutdown()
+            except Exception:
+                pass
 
     def summary(self, t0: float, t1: float):
-        rows = [f for t, f in self.samples if t0 <= t <= t1 + self.period_ms / 1000.0]
+        rows = [r for r in self.samples if t0 <= r[0] <= t1]
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
-        sm = [float(s[0]) for s in rows if s[0].replace(".", "").isdigit()]
-        mx = [float(s[1]) for s in rows if s[1].replace(".", "").isdigit()]
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        reasons = sorted({names[i] for s in rows for i in range(4) if s[2 + i].lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+        nvml = self._nvml
+        reasons = sorted({name for r in rows for name, attr, bit in self.REASONS
+                          if r[3] & getattr(nvml, attr, bit)})
+        return {"sm_mhz": statistics.median(r[1] for r in rows), "sm_max_mhz": max(r[2] for r in rows),
                 "reasons": reasons, "samples": len(rows), "window": "warm-up replays + timed steps"}
 
 
@@ -428,7 +445,7 @@ def main():
         except Exception as e:  # the eager number stands if capture is unavailable
             print(f"bench: CUDA graph capture failed ({type(e).__name__}: {e}); timing eager steps", file=sys.stderr)
     run = graph.replay if graph is not None else (lambda: step(x))
-    clk = ClockSampler(local).start()
+    clk = ClockSampler(device).start()
     t_load = time.monotonic()
     for _ in range(warmup):
         run()

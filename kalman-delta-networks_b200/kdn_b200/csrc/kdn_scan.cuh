@@ -77,6 +77,10 @@ struct ScanParams {
   char* dbg;  // fp32 precision: per-CTA global scratch standing in for shared memory
   size_t dbg_stride;
   int B, T, H, NT;
+  // the launch covers chunks [c_lo, c_hi) of every stream (the C ABI passes
+  // the whole sequence; a sequential pass over a sub-range starts from S0 /
+  // dST and ends in ST / dS0 at the range's ends)
+  int c_lo, c_hi;
   float scale;
 };
 
@@ -161,6 +165,7 @@ struct Chunk {
   float* gmid;   // gate at the reference row, per channel
   float* glast;  // gate at the last valid row, per channel
   float* red;    // [32] scratch
+  float* rb;     // iso beta of the rows (0 past the chunk's end)
   // operands
   OpT* Kr;
   OpT* Qr;
@@ -174,7 +179,7 @@ struct Chunk {
 // glast [KD]; red [32].  fr, fL, gL are contiguous (the record's F block).
 template <class CF>
 __host__ __device__ constexpr size_t small_floats() {
-  return 2 * CF::C + 5 * kKD + 32;
+  return 3 * CF::C + 5 * kKD + 32;
 }
 template <class CF>
 __device__ __forceinline__ void bind_small(Chunk<CF>& ch, float* small) {
@@ -186,6 +191,7 @@ __device__ __forceinline__ void bind_small(Chunk<CF>& ch, float* small) {
   ch.gmid = ch.gL + kKD;
   ch.glast = ch.gmid + kKD;
   ch.red = ch.glast + kKD;
+  ch.rb = ch.red + 32;
 }
 
 // Load rows x cols bf16 (row stride src_ld elements) into an OpT buffer.
@@ -400,6 +406,7 @@ __device__ void prep_chunk(Chunk<CF>& ch) {
         if ((threadIdx.x & 15) == 0) {
           ch.rq[r] = qs;
           ch.rk[r] = ks;
+          ch.rb[r] = x[j].beta;
         }
       }
       if (r < L) {

@@ -100,6 +100,8 @@ int fill_params(const KdnScanArgs* a, const Sizes& s, ScanParams* p) {
   p->T = (int)a->T;
   p->H = (int)a->H;
   p->NT = (int)s.NT;
+  p->c_lo = 0;
+  p->c_hi = (int)s.NT;
   p->scale = a->scale;
   return KDN_OK;
 }

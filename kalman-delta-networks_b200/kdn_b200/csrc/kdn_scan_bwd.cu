@@ -283,8 +283,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_bwd_state_tc_kernel(ScanPa
   const uint32_t tmem = *tslot;
 
   if (warp == kTcWarps) {
-    for (int it = 0; it < p.NT; ++it) {
-      const int s = it % NS, c = p.NT - 1 - it;
+    for (int it = 0; it < p.c_hi - p.c_lo; ++it) {
+      const int s = it % NS, c = p.c_hi - 1 - it;
       if (it >= NS) mbar_wait(&empty[s], (it / NS - 1) & 1, p.status);
       if (lane == 0) {
         char* st = base + s * Lo::stage;
@@ -310,8 +310,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_bwd_state_tc_kernel(ScanPa
   tc::wait_st();
   uint32_t mph = 0;
 
-  for (int it = 0; it < p.NT; ++it) {
-    const int s = it % NS, c = p.NT - 1 - it;
+  for (int it = 0; it < p.c_hi - p.c_lo; ++it) {
+    const int s = it % NS, c = p.c_hi - 1 - it;
     char* st = base + s * Lo::stage;
     char* sdO = Lo::DF32 ? base + Lo::dOb : st + Lo::dO;
     mbar_wait(&full[s], (it / NS) & 1, p.status);
@@ -502,7 +502,7 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_kernel(ScanParams p) {
   OpT* sQb = reinterpret_cast<OpT*>(base + Lo::Qb);
   OpT* sW = reinterpret_cast<OpT*>(base + Lo::W);
 
-  const int c = blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
+  const int c = p.c_lo + blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t0 = c * C;
   const int L = min(C, p.T - t0);
@@ -913,14 +913,12 @@ size_t chunk_bytes() {
 
 template <class CF> int launch_bwd_chunk_tc(const ScanParams&, cudaStream_t);
 
+// The reverse state sweep over chunks [p.c_lo, p.c_hi) (the whole sequence
+// for the fp32 precision).
 template <class CF>
-int launch_bwd(const ScanParams& p, cudaStream_t st) {
-  const size_t s2 = CF::F32 ? 0 : ChunkLayout<CF>::bytes;
+int launch_bwd_state(const ScanParams& p, cudaStream_t st) {
   static bool configured = false;
   if (!configured) {
-    if (cudaFuncSetAttribute(scan_bwd_chunk_kernel<CF>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s2) !=
-        cudaSuccess)
-      return check_launch("cudaFuncSetAttribute(scan_bwd_chunk_kernel)");
     if constexpr (!CF::F32) {
       if (cudaFuncSetAttribute(scan_bwd_state_tc_kernel<CF>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)StateTcLayout<CF>::bytes) != cudaSuccess)
@@ -938,11 +936,33 @@ int launch_bwd(const ScanParams& p, cudaStream_t st) {
     maps.out = maps.in;
     scan_bwd_state_tc_kernel<CF><<<p.B * p.H, kTcThreads, StateTcLayout<CF>::bytes, st>>>(p, maps);
   }
-  int rc = check_launch("scan_bwd_state_kernel");
+  return check_launch("scan_bwd_state_kernel");
+}
+
+// The chunk-parallel gradients of chunks [p.c_lo, p.c_hi).
+template <class CF>
+int launch_bwd_chunk(const ScanParams& p, cudaStream_t st) {
+  if constexpr (CF::ISO && !CF::F32) {
+    return launch_bwd_chunk_tc<CF>(p, st);
+  } else {
+    const size_t s2 = CF::F32 ? 0 : ChunkLayout<CF>::bytes;
+    static bool configured = false;
+    if (!configured) {
+      if (cudaFuncSetAttribute(scan_bwd_chunk_kernel<CF>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s2) !=
+          cudaSuccess)
+        return check_launch("cudaFuncSetAttribute(scan_bwd_chunk_kernel)");
+      configured = true;
+    }
+    scan_bwd_chunk_kernel<CF><<<dim3(p.c_hi - p.c_lo, p.B * p.H), 512, s2, st>>>(p);
+    return check_launch("scan_bwd_chunk_kernel");
+  }
+}
+
+template <class CF>
+int launch_bwd(const ScanParams& p, cudaStream_t st) {
+  int rc = launch_bwd_state<CF>(p, st);
   if (rc != KDN_OK) return rc;
-  if constexpr (CF::ISO && !CF::F32) return launch_bwd_chunk_tc<CF>(p, st);
-  scan_bwd_chunk_kernel<CF><<<dim3(p.NT, p.B * p.H), 512, s2, st>>>(p);
-  return check_launch("scan_bwd_chunk_kernel");
+  return launch_bwd_chunk<CF>(p, st);
 }
 
 template int launch_bwd<Cfg<true, 64, bf16>>(const ScanParams&, cudaStream_t);

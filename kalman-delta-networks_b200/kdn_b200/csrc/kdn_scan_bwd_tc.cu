@@ -100,7 +100,7 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
   extern __shared__ __align__(1024) char smem_raw[];
   char* base = align1024(smem_raw);
 
-  const int c = blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
+  const int c = p.c_lo + blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q = warp & 3, cg = warp >> 2;  // TMEM lane quadrant, column group
   const int t0 = c * C, L = min(C, p.T - t0);
@@ -138,6 +138,10 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
   const uint32_t tmem = *tslot;
   const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16);  // this warp's lane quadrant
 
+  // gated operands from the raw rows first: issuing the bulk copies blocks the
+  // issuing thread for about as long as they take to land, and the raw-row
+  // loads would compete with them
+  prep_chunk<CF, 512, true>(ch);
   if (threadIdx.x == 0) {
     const char* rec = static_cast<const char*>(p.rec) + cc * RT::bytes;
     const char* hs = static_cast<const char*>(p.h) + cc * 2 * hblock_bytes<CF>();
@@ -154,8 +158,6 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
     tma_load_4d(base + Lo::dO, &maps.dO, 0, h, t0, b, ldbar);
     tma_load_4d(base + Lo::dO + C * 128, &maps.dO, 64, h, t0, b, ldbar);
   }
-  // gated operands from the raw rows while the copies fly
-  prep_chunk<CF, 512, true>(ch);
   mbar_wait(ldbar, 0, p.status);
   fence_async_shared();
   tc::fence_before();
@@ -413,7 +415,7 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
       const int ii = 8 * half + i;
       const int tok = 16 * cg + ii;
       const int r = tok < L ? tok : L - 1;
-      const float rk = ch.rk[r], rq = ch.rq[r], be = ch.beta[(size_t)r * ch.ldb];
+      const float rk = ch.rk[r], rq = ch.rq[r], be = ch.rb[r];
       const float gi = gv[i], k1 = rk * kv[i], q1 = rq * qv[i], kap = be * k1;
       const float er = ex2a(gi - rr), ec = ex2a(rc - gi);
       const float dKr = xk[ii], dQr = p.scale * xq[ii], dKc = xc[ii];
@@ -523,7 +525,7 @@ int launch_bwd_chunk_tc(const ScanParams& p, cudaStream_t st) {
   if (rc == KDN_OK) rc = encode_bthd(&maps.k, p.k, true, p.B, p.T, p.H, kKD, kKD, CF::C, false);
   if (rc == KDN_OK) rc = encode_bthd(&maps.q, p.q, true, p.B, p.T, p.H, kKD, kKD, CF::C, false);
   if (rc != KDN_OK) return rc;
-  scan_bwd_chunk_tc_kernel<CF><<<dim3(p.NT, p.B * p.H), 512, smem, st>>>(p, maps);
+  scan_bwd_chunk_tc_kernel<CF><<<dim3(p.c_hi - p.c_lo, p.B * p.H), 512, smem, st>>>(p, maps);
   return check_launch("scan_bwd_chunk_tc_kernel");
 }
 

@@ -263,9 +263,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_fwd_tc_kernel(ScanParams p
 
   if (warp == kTcWarps) {
     // producer: refill a stage once the MMAs of its previous chunk completed
-    for (int c = 0; c < p.NT; ++c) {
-      const int s = c % NS;
-      if (c >= NS) mbar_wait(&empty[s], (c / NS - 1) & 1, p.status);
+    for (int c = p.c_lo; c < p.c_hi; ++c) {
+      const int it = c - p.c_lo, s = it % NS;
+      if (it >= NS) mbar_wait(&empty[s], (it / NS - 1) & 1, p.status);
       if (lane == 0) {
         char* st = base + s * Lo::stage;
         mbar_expect_tx(&full[s], (unsigned)(R::fwd_end + (size_t)C * 256));
@@ -291,10 +291,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_fwd_tc_kernel(ScanParams p
   tc::wait_st();
   uint32_t mph = 0;
 
-  for (int c = 0; c < p.NT; ++c) {
-    const int s = c % NS, t0 = c * C;
+  for (int c = p.c_lo; c < p.c_hi; ++c) {
+    const int it = c - p.c_lo, s = it % NS, t0 = c * C;
     char* st = base + s * Lo::stage;
-    mbar_wait(&full[s], (c / NS) & 1, p.status);
+    mbar_wait(&full[s], (it / NS) & 1, p.status);
     {
       // state operand (and h), then S <- 2^g_L S
       const float gl = reinterpret_cast<const float*>(st + R::F)[2 * kKD + row];
@@ -399,10 +399,11 @@ size_t fwd_dbg_bytes() {
 
 template <class CF> int launch_prep(const ScanParams&, cudaStream_t);
 
+// The sequential forward pass over chunks [p.c_lo, p.c_hi) (the whole
+// sequence for the fp32 precision).
 template <class CF>
-int launch_fwd(const ScanParams& p, cudaStream_t st) {
-  int rc = launch_prep<CF>(p, st);
-  if (rc != KDN_OK) return rc;
+int launch_fwd_seq(const ScanParams& p, cudaStream_t st) {
+  int rc = KDN_OK;
   static bool configured = false;
   if constexpr (CF::F32) {
     if (!configured) {
@@ -429,6 +430,13 @@ int launch_fwd(const ScanParams& p, cudaStream_t st) {
     scan_fwd_tc_kernel<CF><<<p.B * p.H, kTcThreads, smem, st>>>(p, maps);
     return check_launch("scan_fwd_tc_kernel");
   }
+}
+
+template <class CF>
+int launch_fwd(const ScanParams& p, cudaStream_t st) {
+  int rc = launch_prep<CF>(p, st);
+  if (rc != KDN_OK) return rc;
+  return launch_fwd_seq<CF>(p, st);
 }
 
 template int launch_fwd<Cfg<true, 64, bf16>>(const ScanParams&, cudaStream_t);

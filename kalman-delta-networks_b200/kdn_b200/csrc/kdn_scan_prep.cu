@@ -45,7 +45,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2) scan_prep_kernel(ScanParams p
   extern __shared__ __align__(128) char smem[];
   char* base = CF::F32 ? p.dbg + (size_t)(blockIdx.y * gridDim.x + blockIdx.x) * p.dbg_stride : smem;
 
-  const int c = blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
+  const int c = p.c_lo + blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
   const int warp = threadIdx.x >> 5;
   const int t0 = c * C;
   const size_t cc = (size_t)bh * p.NT + c;
@@ -163,7 +163,7 @@ int launch_prep(const ScanParams& p, cudaStream_t st) {
       return check_launch("cudaFuncSetAttribute(scan_prep_kernel)");
     configured = true;
   }
-  scan_prep_kernel<CF><<<dim3(p.NT, p.B * p.H), kPrepThreads, smem, st>>>(p);
+  scan_prep_kernel<CF><<<dim3(p.c_hi - p.c_lo, p.B * p.H), kPrepThreads, smem, st>>>(p);
   return check_launch("scan_prep_kernel");
 }
 

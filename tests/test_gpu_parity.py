@@ -172,6 +172,33 @@ def test_diag_scan(precision, B, T, H, decay):
     check(o, grads, ref, ("q", "k", "kappa", "v", "g_cumsum"), tol, ftol)
 
 
+# Longer sequences (17 to 66 chunks): the sequential passes' multi-stage
+# pipelines wrap around their stage rings several times.
+@pytest.mark.parametrize("precision", ["bf16"], indirect=True)
+@pytest.mark.parametrize("B,T,H", [(1, 1100, 2), (1, 2100, 1)])
+def test_iso_scan_long(precision, B, T, H):
+    d = oracle.make_iso_inputs(B, T, H, seed=T + 11)
+    ref = oracle.scan_grads("iso", {n: d[n] for n in ("q", "k", "v", "g_cumsum", "beta")}, d["dO"])
+    o, grads = run_iso(d, d["dO"])
+    tol, ftol = TOL[precision]
+    check(o, grads, ref, ("q", "k", "v", "g_cumsum", "beta"), tol, ftol)
+
+
+@pytest.mark.parametrize("precision", ["bf16"], indirect=True)
+@pytest.mark.parametrize("B,T,H", [(1, 600, 2), (1, 1050, 1)])
+def test_diag_scan_long(precision, B, T, H):
+    d = oracle.make_diag_inputs(B, T, H, seed=T + 13)
+    d["dO"] = d["dO"].bfloat16().float()
+    kappa = oracle.diag_gain(d["k_gain"].double(), d["alpha"].double(), d["omega"].double(), d["r"].double(),
+                             d["initial_precision"].double())[0].float()
+    scale = 128 ** -0.5
+    ref = oracle.scan_grads("diag", {"q": d["q"], "k": d["k"], "kappa": kappa, "v": d["v"], "g_cumsum": d["g_cumsum"]},
+                            d["dO"], scale=scale)
+    o, grads = run_diag(d, d["dO"], kappa, scale)
+    tol, ftol = TOL[precision]
+    check(o, grads, ref, ("q", "k", "kappa", "v", "g_cumsum"), tol, ftol)
+
+
 # ----------------------------------------------------------------------------- continuation (sequence parallelism)
 
 
@@ -192,19 +219,21 @@ def _iso_full_reference(d, prec):
     return ref
 
 
-@pytest.mark.parametrize("precision", ["fp32", "bf16"], indirect=True)
-def test_iso_segments_with_carried_state(precision):
-    """Three segments chained through (S, p) reproduce one full-sequence call."""
+@pytest.mark.parametrize("precision,T,cuts", [("fp32", 256, (128, 192)), ("bf16", 256, (128, 192)),
+                                               ("bf16", 2200, (64, 128))], indirect=["precision"])
+def test_iso_segments_with_carried_state(precision, T, cuts):
+    """Three segments chained through (S, p) reproduce one full-sequence call
+    (at T = 2200 the last segment is 33 chunks long)."""
     from kdn_b200.sequence_parallel import iso_segment
 
-    d = oracle.make_iso_inputs(1, 256, 2, seed=21)
+    d = oracle.make_iso_inputs(1, T, 2, seed=21)
     prec = torch.tensor([1.0, 0.7])
     ref = _iso_full_reference(d, prec)
     names = ("q", "k", "v", "g_cumsum", "a", "omega", "r")
     L = {n: d[n].to(DEV).requires_grad_(True) for n in names}
     P = prec.to(DEV).requires_grad_(True)
     outs, S, p = [], None, None
-    for s0, s1 in ((0, 128), (128, 192), (192, 256)):
+    for s0, s1 in zip((0,) + cuts, cuts + (T,)):
         seg = [L[n][:, s0:s1] for n in names]
         o, S, p = iso_segment(*seg, P, S, p, head_dim=128)
         outs.append(o)
