@@ -379,6 +379,13 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
   // tiles Kr .. Tt (dead once the score MMAs are skipped)
   float* xs = reinterpret_cast<float*>(base + Lo::Kr);
   static_assert(Lo::Tt + 8192 >= 8 * 4 * 512 * 4, "exact-path scratch");
+  // the same 64 KB once the mapping is done (on the fast path already during
+  // it): the dg, dk, dq rows [C][128], written lane = key and copied out with
+  // 16-byte stores
+  float* sdg = xs;
+  bf16* sdk = reinterpret_cast<bf16*>(base + Lo::Kr + C * kKD * 4);
+  bf16* sdq = sdk + C * kKD;
+  static_assert(Lo::Kr + C * kKD * 8 <= Lo::Tt + 8192, "output staging");
   float kh[16], qh[16];
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
@@ -438,10 +445,15 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
       kh[ii] = k1;
       qh[ii] = q1;
     }
+    if (ch.fast) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int tok = 16 * cg + 8 * half + i;
-      if (tok < L) p.dg[tok_row(p, b, h, t0 + tok) * kKD + key] = dgv[i];
+      for (int i = 0; i < 8; ++i) sdg[(16 * cg + 8 * half + i) * kKD + key] = dgv[i];
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int tok = 16 * cg + 8 * half + i;
+        if (tok < L) p.dg[tok_row(p, b, h, t0 + tok) * kKD + key] = dgv[i];
+      }
     }
     // token sums over this warp's 32 keys: one transpose-reduce leaves the sum
     // of value j in lane j (j = 8 * quantity + token)
@@ -489,14 +501,26 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
       const int tok = 16 * cg + i;
-      if (tok < L) {
-        const size_t off = tok_row(p, b, h, t0 + tok) * kKD + key;
-        p.dk[off] = __float2bfloat16_rn(rkv[i] * (xk[i] - kh[i] * dkdot[i]));
-        p.dq[off] = __float2bfloat16_rn(rqv[i] * (xq[i] - qh[i] * dqdot[i]));
-      }
+      sdk[tok * kKD + key] = __float2bfloat16_rn(rkv[i] * (xk[i] - kh[i] * dkdot[i]));
+      sdq[tok * kKD + key] = __float2bfloat16_rn(rqv[i] * (xq[i] - qh[i] * dqdot[i]));
     }
   }
   if (threadIdx.x < L) p.dbeta[tok_row(p, b, h, t0 + threadIdx.x)] = tsum[threadIdx.x];
+  __syncthreads();
+  // copy-out of the valid rows: 16 bytes per thread and store
+  for (int e = threadIdx.x; e < L * 16; e += 512) {
+    const int r = e >> 4, c8 = 8 * (e & 15);
+    const size_t off = tok_row(p, b, h, t0 + r) * kKD + c8;
+    *reinterpret_cast<uint4*>(p.dk + off) = *reinterpret_cast<const uint4*>(sdk + r * kKD + c8);
+    *reinterpret_cast<uint4*>(p.dq + off) = *reinterpret_cast<const uint4*>(sdq + r * kKD + c8);
+  }
+  if (ch.fast) {
+    for (int e = threadIdx.x; e < L * 32; e += 512) {
+      const int r = e >> 5, c4 = 4 * (e & 31);
+      *reinterpret_cast<float4*>(p.dg + tok_row(p, b, h, t0 + r) * kKD + c4) =
+          *reinterpret_cast<const float4*>(sdg + r * kKD + c4);
+    }
+  }
 
   if (threadIdx.x == 0) bulk_wait_all();
   tc::fence_before();
