@@ -285,6 +285,14 @@ struct RawRow {
   float beta;
 };
 
+__device__ __forceinline__ uint4 pack8(const float (&x)[8]) {
+  uint4 u;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
+  return u;
+}
+
 __device__ __forceinline__ void unpack8(float (&d)[8], const uint4& u) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll

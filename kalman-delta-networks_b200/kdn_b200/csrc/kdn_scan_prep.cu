@@ -31,7 +31,13 @@ struct PrepLayout {
   static constexpr size_t Ab = Xb + A128((size_t)C * CF::LDC * sz);
   static constexpr size_t As = Ab + A128((size_t)C * CF::LDC * sz);
   static constexpr size_t small = As + A128((size_t)C * CF::LDA * 4);
-  static constexpr size_t bytes = small + A128(small_floats<CF>() * 4);
+  static constexpr size_t base_bytes = small + A128(small_floats<CF>() * 4);
+  // bf16 record tiles T, Qq, Qt, Tt ([C][64] swizzled each), staged for the
+  // bulk stores over Xb .. As (dead after the solve) when they fit there
+  static constexpr size_t rec_tiles = 4 * (size_t)C * 128;
+  static constexpr bool alias = small - Xb >= rec_tiles;
+  static constexpr size_t St = alias ? Xb : base_bytes;
+  static constexpr size_t bytes = alias ? base_bytes : base_bytes + rec_tiles;
 };
 
 template <class CF>
@@ -94,57 +100,87 @@ __global__ void __launch_bounds__(kPrepThreads, 2) scan_prep_kernel(ScanParams p
       for (size_t o = (size_t)threadIdx.x * 16; o < len[i]; o += (size_t)blockDim.x * 16)
         *reinterpret_cast<int4*>(rec + dst[i] + o) = *reinterpret_cast<const int4*>(src[i] + o);
   } else {
-    // swizzled tensor-core record with the scale factors folded in
+    // swizzled tensor-core record with the scale factors folded in, assembled
+    // in shared memory and written by bulk stores (one thread issues them)
     using RT = RecTc<CF>;
     char* rec = static_cast<char*>(p.rec) + cc * RT::bytes;
+    char* st = base + Lo::St;
     __syncthreads();
-    // Qs = scale fr Qr, Kf = fL Kc, Wf = fr W0: thread t owns keys 8(t%16)..+7
+    // Qs = scale fr Qr, Kf = fL Kc, Wf = fr W0, each rewritten swizzled over its
+    // own padded tile (through registers): thread t owns keys 8(t%16)..+7 of
+    // rows t/16, t/16 + 16, ...
     {
-      const int g = threadIdx.x & 15;
-#pragma unroll 1
+      constexpr int RPT = C / (kPrepThreads / 16);
+      const int g = threadIdx.x & 15, r0 = threadIdx.x >> 4;
+      char* tiles[3] = {base + Lo::Qr, base + Lo::Kc, base + Lo::Kr};
+      uint4 v[3][RPT];
+#pragma unroll
       for (int m = 0; m < 3; ++m) {
-        const OpT* src = m == 0 ? ch.Qr : (m == 1 ? ch.Kc : ch.Kr);
         const float* fac = m == 1 ? ch.fL : ch.fr;
         const float mul = m == 0 ? p.scale : 1.f;
         float f[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) f[i] = mul * fac[8 * g + i];
-        char* dst = rec + (m == 0 ? RT::Qs : (m == 1 ? RT::Kf : RT::Wf));
-        for (int r = threadIdx.x >> 4; r < C; r += kPrepThreads / 16) {
+#pragma unroll
+        for (int j = 0; j < RPT; ++j) {
           float x[8];
-          ld8(x, src + r * CF::LDK + 8 * g);
+          ld8(x, reinterpret_cast<const OpT*>(tiles[m]) + (r0 + 16 * j) * CF::LDK + 8 * g);
 #pragma unroll
           for (int i = 0; i < 8; ++i) x[i] *= f[i];
-          st8(reinterpret_cast<bf16*>(dst + tc::sw_off(r, 8 * g, C)), x);
+          v[m][j] = pack8(x);
         }
       }
+      __syncthreads();
+#pragma unroll
+      for (int m = 0; m < 3; ++m)
+#pragma unroll
+        for (int j = 0; j < RPT; ++j)
+          *reinterpret_cast<uint4*>(tiles[m] + tc::sw_off(r0 + 16 * j, 8 * g, C)) = v[m][j];
     }
-    // T, Qq = scale Q, Qt = scale Q^T, Tt = T^T: thread t owns columns 8(t%8)..+7 (columns >= C zero)
+    // T, Qq = scale Q: thread t owns columns 8(t%8)..+7 of rows t/8, t/8 + 32, ...
+    // (columns >= C zero); Qt = scale Q^T, Tt = T^T: warp w owns output columns
+    // 8(w%8)..+7 and lane l output row l, l + 32, ..., so the column reads of
+    // the source are consecutive along a row (no bank conflicts)
     {
-      const int g = threadIdx.x & 7;
 #pragma unroll 1
       for (int m = 0; m < 4; ++m) {
-        char* dst = rec + (m == 0 ? RT::T : (m == 1 ? RT::Qq : (m == 2 ? RT::Qt : RT::Tt)));
+        char* dst = st + (size_t)m * C * 128;  // T, Qq, Qt, Tt: the record's order
         const float mul = (m == 1 || m == 2) ? p.scale : 1.f;
-        for (int r = threadIdx.x >> 3; r < C; r += kPrepThreads / 8) {
+        const OpT* src = (m == 0 || m == 3) ? sTb : sQb;
+        const bool tr = m >= 2;
+        const int g = tr ? (warp & 7) : (threadIdx.x & 7);
+        const int r0 = tr ? (threadIdx.x & 31) + 32 * (warp >> 3) : threadIdx.x >> 3;
+        const int rs = tr ? 32 * (kPrepThreads / 256) : kPrepThreads / 8;
+        for (int r = r0; r < C; r += rs) {
           float x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
           if (8 * g < C) {
-            if (m < 2) {
-              ld8(x, (m == 0 ? sTb : sQb) + r * CF::LDC + 8 * g);
+            if (!tr) {
+              ld8(x, src + r * CF::LDC + 8 * g);
             } else {
-              const OpT* src = m == 2 ? sQb : sTb;
 #pragma unroll
               for (int i = 0; i < 8; ++i) x[i] = to_f(src[(8 * g + i) * CF::LDC + r]);
             }
 #pragma unroll
             for (int i = 0; i < 8; ++i) x[i] *= mul;
           }
-          st8(reinterpret_cast<bf16*>(dst + tc::sw_off(r, 8 * g, C)), x);
+          *reinterpret_cast<uint4*>(dst + tc::sw_off(r, 8 * g, C)) = pack8(x);
         }
       }
     }
-    for (int e = threadIdx.x; e < 3 * kKD / 4; e += blockDim.x)
-      reinterpret_cast<float4*>(rec + RT::F)[e] = reinterpret_cast<const float4*>(ch.fr)[e];
+    fence_async_shared();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      static_assert(RT::Qq == RT::T + (size_t)C * 128 && RT::Tt == RT::Qt + (size_t)C * 128, "record tile order");
+      static_assert(RT::Kf == RT::Qs + (size_t)C * 256 && RT::Wf == RT::Kf + (size_t)C * 256, "record tile order");
+      bulk_s2g(rec + RT::T, st, 2 * C * 128);
+      bulk_s2g(rec + RT::Qt, st + 2 * C * 128, 2 * C * 128);
+      bulk_s2g(rec + RT::Qs, base + Lo::Qr, C * 256);
+      bulk_s2g(rec + RT::Kf, base + Lo::Kc, C * 256);
+      bulk_s2g(rec + RT::Wf, base + Lo::Kr, C * 256);
+      bulk_s2g(rec + RT::F, ch.fr, 3 * kKD * 4);
+      bulk_commit();
+      bulk_wait_read<0>();  // shared memory stays valid until the stores have read it
+    }
   }
 }
 
