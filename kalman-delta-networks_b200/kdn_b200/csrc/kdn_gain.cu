@@ -29,7 +29,7 @@ struct Mob {  // 2x2 Moebius map p -> (A p + B) / (C p + D)
 __device__ __forceinline__ Mob mob_mul(const Mob& x, const Mob& y) {  // x after y
   Mob z{x.A * y.A + x.B * y.C, x.A * y.B + x.B * y.D, x.C * y.A + x.D * y.C, x.C * y.B + x.D * y.D};
   float m = fmaxf(fmaxf(fabsf(z.A), fabsf(z.B)), fmaxf(fabsf(z.C), fabsf(z.D)));
-  float inv = 1.f / fmaxf(m, 1e-30f);
+  float inv = __fdividef(1.f, fmaxf(m, 1e-30f));
   return Mob{z.A * inv, z.B * inv, z.C * inv, z.D * inv};
 }
 __device__ __forceinline__ float mob_apply(const Mob& m, float p) { return (m.A * p + m.B) / (m.C * p + m.D); }
@@ -191,11 +191,13 @@ __global__ void __launch_bounds__(kIsoThreads) iso_gain_bwd_kernel(
 // ---------------------------------------------------------------------------
 // Diagonal gain
 // ---------------------------------------------------------------------------
-// After this, lane j holds the warp sum of v[j] over the 32 lanes.
-__device__ __forceinline__ float transpose_reduce32(float (&v)[32]) {
+// Lane l ends with the warp sum of v[l % N] (N = 8, 16 or 32): a butterfly
+// that halves the values exchanged at every step.
+template <int N>
+__device__ __forceinline__ float transpose_reduce(float (&v)[N]) {
   const int lane = threadIdx.x & 31;
 #pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) {
+  for (int off = N / 2; off >= 1; off >>= 1) {
     const bool upper = lane & off;
 #pragma unroll
     for (int i = 0; i < off; ++i) {
@@ -204,37 +206,81 @@ __device__ __forceinline__ float transpose_reduce32(float (&v)[32]) {
       v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
     }
   }
-  return v[0];
+  float s = v[0];
+#pragma unroll
+  for (int o = N; o < 32; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  return s;
 }
 
-// Sum of v[j] over all K threads of the block for each of the 32 tokens of a
-// group; result in red[j] (shared) after a barrier.
-template <int K>
-__device__ __forceinline__ void block_token_sums(float (&v)[32], float* red /* [K/32][32] */, float* out /*[32]*/) {
+// Sum of v[j] over all K threads of the block for each of N tokens; result in
+// out[j] (shared) after the second barrier.
+template <int K, int N>
+__device__ __forceinline__ void block_token_sums(float (&v)[N], float* red /* [K/32][N] */, float* out /* [N] */) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  red[warp * 32 + lane] = transpose_reduce32(v);
+  const float s = transpose_reduce<N>(v);
+  if (lane < N) red[warp * N + lane] = s;
   __syncthreads();
-  if (threadIdx.x < 32) {
+  if (threadIdx.x < N) {
     float acc = 0.f;
 #pragma unroll
-    for (int w = 0; w < K / 32; ++w) acc += red[w * 32 + threadIdx.x];
+    for (int w = 0; w < K / 32; ++w) acc += red[w * N + threadIdx.x];
     out[threadIdx.x] = acc;
   }
   __syncthreads();
 }
 
+// One channel's inputs for TT consecutive tokens of a segment.  The loads of a
+// tile do not depend on the running covariance, so each kernel issues the next
+// tile before it runs the current one: the memory latency overlaps the
+// sequential chain (one division per token).  Rows past the segment read as
+// neutral values and are skipped by the callers.
+template <int K, int TT, bool DK>
+struct GainTile {
+  float k[TT], a[TT], w[TT], r[TT], dk[DK ? TT : 1];
+  __device__ __forceinline__ void load(const float* __restrict__ kk, const float* __restrict__ al,
+                                       const float* __restrict__ om, const float* __restrict__ rr,
+                                       const float* __restrict__ dkap, size_t row0, int H, int n, int c) {
+#pragma unroll
+    for (int j = 0; j < TT; ++j) {
+      if (j < n) {
+        const size_t row = row0 + (size_t)j * H;
+        k[j] = kk[row * K + c];
+        a[j] = al[row * K + c];
+        w[j] = om[row * K + c];
+        r[j] = rr[row];
+        if constexpr (DK) dk[j] = dkap[row * K + c];
+      } else {
+        k[j] = 0.f;
+        a[j] = 1.f;
+        w[j] = 0.f;
+        r[j] = 1.f;
+        if constexpr (DK) dk[j] = 0.f;
+      }
+    }
+  }
+};
+
 template <int K>
 __global__ void __launch_bounds__(K) diag_gain_map_kernel(const float* __restrict__ k, const float* __restrict__ alpha,
                                                           const float* __restrict__ omega, const float* __restrict__ r,
                                                           float4* __restrict__ maps, int T, int H, int nseg) {
+  constexpr int TT = 4;
   const int seg = blockIdx.x, bh = blockIdx.y, b = bh / H, h = bh - b * H, c = threadIdx.x;
-  const int t0 = seg * kDiagSeg, t1 = min(t0 + kDiagSeg, T);
+  const int t0 = seg * kDiagSeg, n = min(kDiagSeg, T - t0);
+  const size_t row0 = ((size_t)b * T + t0) * H + h;
+  GainTile<K, TT, false> cu, nx;
+  nx.load(k, alpha, omega, r, nullptr, row0, H, n, c);
   Mob m{1.f, 0.f, 0.f, 1.f};
-  for (int t = t0; t < t1; ++t) {
-    const size_t row = ((size_t)b * T + t) * H + h;
-    const float kt = k[row * K + c], at = alpha[row * K + c], wt = omega[row * K + c], rt = r[row];
-    const float a2 = at * at, u = (float)K * kt * kt / rt;
-    m = mob_mul(Mob{a2, wt, u * a2, 1.f + u * wt}, m);
+  for (int ts = 0; ts < n; ts += TT) {
+    cu = nx;
+    if (ts + TT < n) nx.load(k, alpha, omega, r, nullptr, row0 + (size_t)(ts + TT) * H, H, n - ts - TT, c);
+#pragma unroll
+    for (int j = 0; j < TT; ++j) {
+      if (ts + j < n) {
+        const float a2 = cu.a[j] * cu.a[j], u = __fdividef((float)K * cu.k[j] * cu.k[j], cu.r[j]);
+        m = mob_mul(Mob{a2, cu.w[j], u * a2, 1.f + u * cu.w[j]}, m);
+      }
+    }
   }
   maps[((size_t)bh * nseg + seg) * K + c] = make_float4(m.A, m.B, m.C, m.D);
 }
@@ -261,39 +307,36 @@ __global__ void __launch_bounds__(K) diag_gain_emit_kernel(const float* __restri
                                                            const float* __restrict__ r,
                                                            const float* __restrict__ carry,
                                                            float* __restrict__ kappa, int T, int H, int nseg) {
-  __shared__ float red[K];
-  __shared__ float tok[32];
+  constexpr int TT = 8;
+  __shared__ float red[K / 32 * TT];
+  __shared__ float tok[TT];
   const int seg = blockIdx.x, bh = blockIdx.y, b = bh / H, h = bh - b * H, c = threadIdx.x;
-  const int t0 = seg * kDiagSeg, t1 = min(t0 + kDiagSeg, T);
+  const int t0 = seg * kDiagSeg, n = min(kDiagSeg, T - t0);
+  const size_t row0 = ((size_t)b * T + t0) * H + h;
+  GainTile<K, TT, false> cu, nx;
+  nx.load(k, alpha, omega, r, nullptr, row0, H, n, c);
   float p = carry[((size_t)bh * nseg + seg) * K + c];
-  for (int tg = t0; tg < t1; tg += 32) {
-    float num[32], pk2[32];
+  for (int ts = 0; ts < n; ts += TT) {
+    cu = nx;
+    if (ts + TT < n) nx.load(k, alpha, omega, r, nullptr, row0 + (size_t)(ts + TT) * H, H, n - ts - TT, c);
+    float num[TT], pk2[TT];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const int t = tg + j;
+    for (int j = 0; j < TT; ++j) {
       num[j] = 0.f;
       pk2[j] = 0.f;
-      if (t < t1) {
-        const size_t row = ((size_t)b * T + t) * H + h;
-        const float kt = k[row * K + c], at = alpha[row * K + c], wt = omega[row * K + c], rt = r[row];
-        const float ph = at * at * p + wt;
-        const float ksq = kt * kt;
-        num[j] = ph * kt;
+      if (ts + j < n) {
+        const float ph = cu.a[j] * cu.a[j] * p + cu.w[j];
+        const float ksq = cu.k[j] * cu.k[j];
+        num[j] = ph * cu.k[j];
         pk2[j] = ph * ksq;
-        const float u = (float)K * ksq / rt;
-        p = ph / (1.f + u * ph);
+        const float u = __fdividef((float)K * ksq, cu.r[j]);
+        p = __fdividef(ph, 1.f + u * ph);
       }
     }
-    block_token_sums<K>(pk2, red, tok);
+    block_token_sums<K, TT>(pk2, red, tok);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const int t = tg + j;
-      if (t < t1) {
-        const size_t row = ((size_t)b * T + t) * H + h;
-        kappa[row * K + c] = num[j] / (r[row] + tok[j]);
-      }
-    }
-    __syncthreads();
+    for (int j = 0; j < TT; ++j)
+      if (ts + j < n) kappa[(row0 + (size_t)(ts + j) * H) * K + c] = __fdividef(num[j], cu.r[j] + tok[j]);
   }
 }
 
@@ -305,50 +348,49 @@ __global__ void __launch_bounds__(K) diag_gain_bwd_map_kernel(
     const float* __restrict__ k, const float* __restrict__ alpha, const float* __restrict__ omega,
     const float* __restrict__ r, const float* __restrict__ dkappa, const float* __restrict__ carry,
     float2* __restrict__ maps, float2* __restrict__ dg_tok, int T, int H, int nseg) {
-  __shared__ float red[K];
-  __shared__ float tok_s1[32], tok_s2[32];
-  __shared__ float pprev_s[32][K];
+  constexpr int TT = 4;
+  __shared__ float red[K / 32 * 2 * TT];
+  __shared__ float tok[2 * TT];  // [sum p_hat k^2 | sum dkappa p_hat k] per token
   const int seg = blockIdx.x, bh = blockIdx.y, b = bh / H, h = bh - b * H, c = threadIdx.x;
-  const int t0 = seg * kDiagSeg, t1 = min(t0 + kDiagSeg, T);
+  const int t0 = seg * kDiagSeg, n = min(kDiagSeg, T - t0);
+  const size_t row0 = ((size_t)b * T + t0) * H + h;
+  const float Kf = (float)K;
+  GainTile<K, TT, true> cu, nx;
+  nx.load(k, alpha, omega, r, dkappa, row0, H, n, c);
   float p = carry[((size_t)bh * nseg + seg) * K + c];
   Aff comp{1.f, 0.f};
-  for (int tg = t0; tg < t1; tg += 32) {
-    float s1[32], s2[32];
+  for (int ts = 0; ts < n; ts += TT) {
+    cu = nx;
+    if (ts + TT < n) nx.load(k, alpha, omega, r, dkappa, row0 + (size_t)(ts + TT) * H, H, n - ts - TT, c);
+    float v[2 * TT], pp[TT];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const int t = tg + j;
-      s1[j] = 0.f;
-      s2[j] = 0.f;
-      if (t < t1) {
-        const size_t row = ((size_t)b * T + t) * H + h;
-        const float kt = k[row * K + c], at = alpha[row * K + c], wt = omega[row * K + c], rt = r[row];
-        const float dk = dkappa[row * K + c];
-        pprev_s[j][c] = p;
-        const float ph = at * at * p + wt;
-        s1[j] = ph * kt * kt;
-        s2[j] = dk * ph * kt;
-        const float u = (float)K * kt * kt / rt;
-        p = ph / (1.f + u * ph);
+    for (int j = 0; j < TT; ++j) {
+      pp[j] = p;
+      v[j] = 0.f;
+      v[TT + j] = 0.f;
+      if (ts + j < n) {
+        const float ph = cu.a[j] * cu.a[j] * p + cu.w[j];
+        v[j] = ph * cu.k[j] * cu.k[j];
+        v[TT + j] = cu.dk[j] * ph * cu.k[j];
+        const float u = __fdividef(Kf * cu.k[j] * cu.k[j], cu.r[j]);
+        p = __fdividef(ph, 1.f + u * ph);
       }
     }
-    block_token_sums<K>(s1, red, tok_s1);
-    block_token_sums<K>(s2, red, tok_s2);
-    for (int j = 0; j < 32; ++j) {
-      const int t = tg + j;
-      if (t >= t1) break;
-      const size_t row = ((size_t)b * T + t) * H + h;
-      const float kt = k[row * K + c], at = alpha[row * K + c], wt = omega[row * K + c], rt = r[row];
-      const float dk = dkappa[row * K + c];
-      const float D = rt + tok_s1[j];
-      const float G = tok_s2[j] / D;
-      if (c == 0) dg_tok[(size_t)bh * T + t] = make_float2(D, G);
-      const float a2 = at * at;
-      const float ph = a2 * pprev_s[j][c] + wt;
-      const float hh = 1.f + (float)K * kt * kt / rt * ph;
-      const float pbar_gain = dk * kt / D - kt * kt * G / D;
-      comp = aff_after(comp, Aff{a2 / (hh * hh), a2 * pbar_gain});
+    block_token_sums<K, 2 * TT>(v, red, tok);
+#pragma unroll
+    for (int j = 0; j < TT; ++j) {
+      if (ts + j < n) {
+        const float kt = cu.k[j], rt = cu.r[j];
+        const float D = rt + tok[j], iD = __fdividef(1.f, D);
+        const float G = tok[TT + j] * iD;
+        if (c == 0) dg_tok[(size_t)bh * T + t0 + ts + j] = make_float2(D, G);
+        const float a2 = cu.a[j] * cu.a[j];
+        const float ph = a2 * pp[j] + cu.w[j];
+        const float ihh = __fdividef(1.f, 1.f + __fdividef(Kf * kt * kt, rt) * ph);
+        const float pbar_gain = (cu.dk[j] * kt - kt * kt * G) * iD;
+        comp = aff_after(comp, Aff{a2 * ihh * ihh, a2 * pbar_gain});
+      }
     }
-    __syncthreads();
   }
   maps[((size_t)bh * nseg + seg) * K + c] = make_float2(comp.A, comp.B);
 }
@@ -366,7 +408,7 @@ __global__ void __launch_bounds__(K) diag_gain_bwd_carry_kernel(const float2* __
   }
 }
 
-__device__ __forceinline__ float sigmoidf_(float x) { return 1.f / (1.f + __expf(-x)); }
+__device__ __forceinline__ float sigmoidf_(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
 
 template <int K>
 __global__ void __launch_bounds__(K) diag_gain_bwd_emit_kernel(
@@ -376,64 +418,92 @@ __global__ void __launch_bounds__(K) diag_gain_bwd_emit_kernel(
     const float* __restrict__ lam_carry, const float2* __restrict__ dg_tok, float* __restrict__ dk_out,
     float* __restrict__ dalpha, bf16* __restrict__ domega_raw, bf16* __restrict__ dr_raw,
     float* __restrict__ dinit, float* __restrict__ d_init_cov, int T, int H, int nseg) {
-  __shared__ float red[K];
-  __shared__ float tok[32];
+  constexpr int TF = 4, TT = 4;
+  __shared__ float red[K / 32 * TT];
+  __shared__ float tok[TT];
   __shared__ float pprev_s[kDiagSeg][K];
   const int seg = blockIdx.x, bh = blockIdx.y, b = bh / H, h = bh - b * H, c = threadIdx.x;
-  const int t0 = seg * kDiagSeg, t1 = min(t0 + kDiagSeg, T);
+  const int t0 = seg * kDiagSeg, n = min(kDiagSeg, T - t0);
+  const size_t row0 = ((size_t)b * T + t0) * H + h;
   const float Kf = (float)K;
-  float p = carry[((size_t)bh * nseg + seg) * K + c];
-  for (int t = t0; t < t1; ++t) {
-    const size_t row = ((size_t)b * T + t) * H + h;
-    const float kt = k[row * K + c], at = alpha[row * K + c], wt = omega[row * K + c], rt = r[row];
-    pprev_s[t - t0][c] = p;
-    const float ph = at * at * p + wt;
-    p = ph / (1.f + Kf * kt * kt / rt * ph);
-  }
-  float lam = lam_carry[((size_t)bh * nseg + seg) * K + c];
-  const int ngroups = (t1 - t0 + 31) / 32;
-  for (int gi = ngroups - 1; gi >= 0; --gi) {
-    const int tg = t0 + gi * 32;
-    float ur[32];
+  // forward re-run of the covariance: p before every token of the segment
+  {
+    GainTile<K, TF, false> cu, nx;
+    nx.load(k, alpha, omega, r, nullptr, row0, H, n, c);
+    float p = carry[((size_t)bh * nseg + seg) * K + c];
+    for (int ts = 0; ts < n; ts += TF) {
+      cu = nx;
+      if (ts + TF < n) nx.load(k, alpha, omega, r, nullptr, row0 + (size_t)(ts + TF) * H, H, n - ts - TF, c);
 #pragma unroll
-    for (int jj = 31; jj >= 0; --jj) {
-      const int t = tg + jj;
+      for (int j = 0; j < TF; ++j) {
+        if (ts + j < n) {
+          pprev_s[ts + j][c] = p;
+          const float ph = cu.a[j] * cu.a[j] * p + cu.w[j];
+          p = __fdividef(ph, 1.f + __fdividef(Kf * cu.k[j] * cu.k[j], cu.r[j]) * ph);
+        }
+      }
+    }
+  }
+  // reverse adjoint over tiles of TT tokens, last tile first
+  struct Rev {
+    GainTile<K, TT, true> g;
+    float2 DG[TT];
+    float wr[TT];
+  };
+  auto load_rev = [&](Rev& x, int ts) {
+    const int m = min(TT, n - ts);
+    x.g.load(k, alpha, omega, r, dkappa, row0 + (size_t)ts * H, H, m, c);
+#pragma unroll
+    for (int j = 0; j < TT; ++j) {
+      if (j < m) {
+        const size_t row = row0 + (size_t)(ts + j) * H;
+        x.DG[j] = dg_tok[(size_t)bh * T + t0 + ts + j];
+        x.wr[j] = __bfloat162float(omega_raw[row * K + c]);
+      } else {
+        x.DG[j] = make_float2(1.f, 0.f);
+        x.wr[j] = 0.f;
+      }
+    }
+  };
+  float lam = lam_carry[((size_t)bh * nseg + seg) * K + c];
+  const int last = ((n - 1) / TT) * TT;
+  Rev cu, nx;
+  load_rev(nx, last);
+  for (int ts = last; ts >= 0; ts -= TT) {
+    cu = nx;
+    if (ts > 0) load_rev(nx, ts - TT);
+    float ur[TT];
+#pragma unroll
+    for (int jj = TT - 1; jj >= 0; --jj) {
       ur[jj] = 0.f;
-      if (t < t1) {
-        const size_t row = ((size_t)b * T + t) * H + h;
-        const float kt = k[row * K + c], at = alpha[row * K + c], wt = omega[row * K + c], rt = r[row];
-        const float dk = dkappa[row * K + c];
-        const float2 DG = dg_tok[(size_t)bh * T + t];
-        const float D = DG.x, G = DG.y;
-        const float pp = pprev_s[t - t0][c];
+      if (ts + jj < n) {
+        const size_t row = row0 + (size_t)(ts + jj) * H;
+        const float kt = cu.g.k[jj], at = cu.g.a[jj], wt = cu.g.w[jj], rt = cu.g.r[jj], dk = cu.g.dk[jj];
+        const float D = cu.DG[jj].x, G = cu.DG[jj].y, iD = __fdividef(1.f, D), ir = __fdividef(1.f, rt);
+        const float pp = pprev_s[ts + jj][c];
         const float a2 = at * at, ksq = kt * kt;
         const float ph = a2 * pp + wt;
-        const float u = Kf * ksq / rt;
-        const float hh = 1.f + u * ph;
-        const float pnext = ph / hh;
-        const float beta_c = ph / D;
-        const float pbar_gain = dk * kt / D - ksq * G / D;
-        const float kbar_gain = dk * beta_c - 2.f * ph * kt * G / D;
-        const float pbar_tot = pbar_gain + lam / (hh * hh);
+        const float u = Kf * ksq * ir;
+        const float ihh = __fdividef(1.f, 1.f + u * ph);
+        const float pnext = ph * ihh;
+        const float pbar_gain = (dk * kt - ksq * G) * iD;
+        const float kbar_gain = (dk * ph - 2.f * ph * kt * G) * iD;
+        const float pbar_tot = pbar_gain + lam * ihh * ihh;
         const float ubar = -lam * pnext * pnext;
-        dk_out[row * K + c] = kbar_gain + ubar * (2.f * Kf * kt / rt);
+        dk_out[row * K + c] = kbar_gain + ubar * (2.f * Kf * kt * ir);
         dalpha[row * K + c] = 2.f * at * pp * pbar_tot;
-        domega_raw[row * K + c] = __float2bfloat16_rn(pbar_tot * sigmoidf_(__bfloat162float(omega_raw[row * K + c])));
-        ur[jj] = ubar * (-Kf * ksq / (rt * rt));
+        domega_raw[row * K + c] = __float2bfloat16_rn(pbar_tot * sigmoidf_(cu.wr[jj]));
+        ur[jj] = -ubar * u * ir;
         lam = a2 * pbar_tot;
       }
     }
-    block_token_sums<K>(ur, red, tok);
-    if (c < 32) {
-      const int t = tg + c;
-      if (t < t1) {
-        const size_t row = ((size_t)b * T + t) * H + h;
-        const float2 DG = dg_tok[(size_t)bh * T + t];
-        const float drt = -DG.y / DG.x + tok[c];
-        dr_raw[row] = __float2bfloat16_rn(drt * sigmoidf_(__bfloat162float(r_raw[row])));
-      }
+    block_token_sums<K, TT>(ur, red, tok);
+    if (c < TT && ts + c < n) {
+      const size_t row = row0 + (size_t)(ts + c) * H;
+      const float2 DG = dg_tok[(size_t)bh * T + t0 + ts + c];
+      const float drt = tok[c] - __fdividef(DG.y, DG.x);
+      dr_raw[row] = __float2bfloat16_rn(drt * sigmoidf_(__bfloat162float(r_raw[row])));
     }
-    __syncthreads();
   }
   if (seg == 0 && d_init_cov) d_init_cov[(size_t)bh * K + c] = lam;  // d L / d p_{-1}
   if (seg == 0 && dinit) {
