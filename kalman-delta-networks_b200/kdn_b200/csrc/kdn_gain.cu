@@ -233,7 +233,9 @@ __device__ __forceinline__ void block_token_sums(float (&v)[N], float* red /* [K
 // tile do not depend on the running covariance, so each kernel issues the next
 // tile before it runs the current one: the memory latency overlaps the
 // sequential chain (one division per token).  Rows past the segment read as
-// neutral values and are skipped by the callers.
+// neutral values and are skipped by the callers.  Tile sizes (2 to 8 tokens)
+// were chosen by timing at B=4, T=4096, H=18, K=128: larger tiles cost
+// occupancy (registers) and lost more than the deeper prefetch gained.
 template <int K, int TT, bool DK>
 struct GainTile {
   float k[TT], a[TT], w[TT], r[TT], dk[DK ? TT : 1];
@@ -307,7 +309,7 @@ __global__ void __launch_bounds__(K) diag_gain_emit_kernel(const float* __restri
                                                            const float* __restrict__ r,
                                                            const float* __restrict__ carry,
                                                            float* __restrict__ kappa, int T, int H, int nseg) {
-  constexpr int TT = 8;
+  constexpr int TT = 4;
   __shared__ float red[K / 32 * TT];
   __shared__ float tok[TT];
   const int seg = blockIdx.x, bh = blockIdx.y, b = bh / H, h = bh - b * H, c = threadIdx.x;
@@ -348,7 +350,7 @@ __global__ void __launch_bounds__(K) diag_gain_bwd_map_kernel(
     const float* __restrict__ k, const float* __restrict__ alpha, const float* __restrict__ omega,
     const float* __restrict__ r, const float* __restrict__ dkappa, const float* __restrict__ carry,
     float2* __restrict__ maps, float2* __restrict__ dg_tok, int T, int H, int nseg) {
-  constexpr int TT = 4;
+  constexpr int TT = 2;
   __shared__ float red[K / 32 * 2 * TT];
   __shared__ float tok[2 * TT];  // [sum p_hat k^2 | sum dkappa p_hat k] per token
   const int seg = blockIdx.x, bh = blockIdx.y, b = bh / H, h = bh - b * H, c = threadIdx.x;
@@ -418,7 +420,7 @@ __global__ void __launch_bounds__(K) diag_gain_bwd_emit_kernel(
     const float* __restrict__ lam_carry, const float2* __restrict__ dg_tok, float* __restrict__ dk_out,
     float* __restrict__ dalpha, bf16* __restrict__ domega_raw, bf16* __restrict__ dr_raw,
     float* __restrict__ dinit, float* __restrict__ d_init_cov, int T, int H, int nseg) {
-  constexpr int TF = 4, TT = 4;
+  constexpr int TF = 8, TT = 8;
   __shared__ float red[K / 32 * TT];
   __shared__ float tok[TT];
   __shared__ float pprev_s[kDiagSeg][K];
