@@ -28,10 +28,6 @@ for _p in (ROOT, os.path.join(ROOT, "kalman-delta-networks_b200")):
     if _p not in sys.path:
         sys.path.insert(0, _p)
 
-if "--varlen" in sys.argv:
-    # the packed step allocates ~15 GB on several streams; per-stream caches fragment without this
-    os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
-
 import torch  # noqa: E402
 
 METRIC = "KDN scan fwd+bwd Mtok/s/GPU (B4,T4096,H18,d128 bf16), % of roofline"
@@ -207,6 +203,12 @@ def make_diag_varlen(device, seed):
     return x
 
 
+def varlen_buckets(cu, bucket=1024):
+    """Number of batched calls of a packed step (sequences grouped by length
+    rounded up to the varlen bucket)."""
+    return len({-(-(b - a) // bucket) for a, b in zip(cu, cu[1:])})
+
+
 def step_diag_varlen(x):
     from kdn_b200 import varlen
 
@@ -215,7 +217,6 @@ def step_diag_varlen(x):
                                         L["r_raw"], x["cu"])
     o = varlen.chunk_kalman_varlen(L["q"], L["k"], kappa, L["v"], L["g_cumsum"], float(D ** -0.5), x["cu"])
     o.backward(x["dO"])
-    varlen.join(x["dO"].device)
     return L
 
 
@@ -381,7 +382,6 @@ def main():
     if args.varlen:
         args.variant = "diag"
         globals()["B"], globals()["T"] = 1, VARLEN_T
-        args.eager = True  # autograd runs the sequences' backward on several streams: timed eagerly
     warmup = max(args.warmup, 3)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -500,7 +500,7 @@ def main():
     per_th = ISO_BYTES_PER_TH if args.variant == "iso" else DIAG_BYTES_PER_TH
     step_bytes = sum(per_th.values()) * th
     if args.varlen:
-        # packed sequences run as per-sequence calls on several streams: the whole step is the unit
+        # packed sequences run as batched calls, one per length bucket: the whole step is the unit
         achieved = step_bytes / (ms * 1e-3) / 1e9
         roofline = {"kernel": "whole varlen step (gain + scan, fwd + bwd, all sequences)", "bound": "hbm",
                     "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
@@ -530,7 +530,7 @@ def main():
                    else f"diag_kdn gain+scan fwd+bwd B{B} T{T} H{H} d{D} (config 2)",
                    "global_batch": B * world, "seq_len": T, "heads": H, "head_dim": D,
                    "parallelism": f"batch-sharded x{world}", "l2": "inputs > L2 (no flush)"},
-        "gpu_launches": LAUNCHES_PER_STEP[args.variant] * args.steps * (len(x["cu"]) - 1 if args.varlen else 1),
+        "gpu_launches": LAUNCHES_PER_STEP[args.variant] * args.steps * (varlen_buckets(x["cu"]) if args.varlen else 1),
         "e2e": e2e,
         "roofline": roofline,
         "clocks": clocks,

@@ -4,14 +4,26 @@ along T of a B = 1 batch, delimited by ``cu_seqlens`` (token offsets
 convention the reference's dense path builds on.
 
 Every sequence is an independent KDN stream: its memory state starts at
-zero, its covariance at 1 / initial_precision,
-and its gate prefix ``g_cumsum`` restarts every chunk (64 tokens isotropic,
-32 diagonal) counted from the sequence's own first token.  Each sequence
-therefore runs as its own B = 1 call of the fixed-length operators, which
-keeps the chunk boundaries and the mathematics identical; the calls are
-spread over a pool of CUDA streams so that the sequential passes of
-different sequences run at the same time.  Autograd runs each sequence's
-backward on the stream of its forward.  Outputs are concatenated along T.
+zero, its covariance at 1 / initial_precision, and its gate prefix
+``g_cumsum`` restarts every chunk (64 tokens isotropic, 32 diagonal) counted
+from the sequence's own first token.
+
+The sequences run as rows of fixed-length batched calls.  They are grouped by
+length rounded up to ``bucket`` tokens (a multiple of 64); each group is
+gathered into a ``[n_seq, L, ...]`` batch whose rows start at a sequence's
+first token, so chunk boundaries and gate prefixes are the sequence's own, and
+are padded after the sequence's end with neutral tokens: zero keys, values,
+queries and write gains, unit retention and observation noise, and a gate
+prefix held at the last real token's value until the chunk ends (0 in later
+chunks), so that no padding token decays or grows the state.  Padding follows
+every real token, so it changes no output of a real token and, its
+cotangents being zero, no gradient either.  Outputs are scattered back to the
+packed layout.  The padded call rounds the last partial chunk of a sequence
+like a full chunk (its reference gate row can differ), so results agree with
+a separate fixed-length call of the sequence to bf16 rounding, not bitwise.
+A call is a handful of kernels per group, all on the caller's stream (it can
+be captured in a CUDA graph once the first call has cached the gather
+indices).
 
 ``cu_seqlens`` may be a list, a CPU tensor or a CUDA tensor (read once on
 the host: a CUDA tensor costs a device synchronisation).
@@ -24,26 +36,7 @@ import torch
 
 from . import diag_kdn_chunk, iso_kdn_chunk
 
-_POOL: dict[int, list[torch.cuda.Stream]] = {}
-
-
-def _streams(device: torch.device, n: int) -> list[torch.cuda.Stream]:
-    key = device.index if device.index is not None else torch.cuda.current_device()
-    pool = _POOL.setdefault(key, [])
-    while len(pool) < n:
-        pool.append(torch.cuda.Stream(device))
-    return pool[:n]
-
-
-def join(device=None) -> None:
-    """Make the current stream wait for every pool stream of ``device``: call
-    after ``backward`` when the next work (or a CUDA graph capture) must see
-    all per-sequence gradients on the current stream."""
-    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
-    key = device.index if device.index is not None else torch.cuda.current_device()
-    cur = torch.cuda.current_stream(device)
-    for s in _POOL.get(key, []):
-        cur.wait_stream(s)
+_INDEX_CACHE: dict = {}
 
 
 def offsets(cu_seqlens) -> list[int]:
@@ -55,10 +48,88 @@ def offsets(cu_seqlens) -> list[int]:
     return cu
 
 
-def map_sequences(fn: Callable, tensors: Sequence, cu_seqlens, *, streams: int = 4):
-    """Apply ``fn(*slices)`` to every sequence (slices along dim 1 of the
-    [1, T, ...] tensors; other arguments pass through) on a pool of streams and
-    concatenate each output along dim 1."""
+def _plan(cu: list[int], bucket: int, chunk: int, device: torch.device):
+    """Groups of sequences by padded length and the device index tensors that
+    gather every group's padded rows in one pass (cached per offsets, bucket,
+    gate chunk and device).  Returns ``(shapes, src, valid, src_g, hold, out)``:
+    ``shapes`` lists ``(L, n_seq)`` per group; the gathered rows of all groups
+    are concatenated, row i reading packed token ``src[i]`` (``valid[i]``) or
+    padding; ``out[t]`` is the gathered row of packed token t."""
+    key = (tuple(cu), bucket, chunk, str(device))
+    plan = _INDEX_CACHE.get(key)
+    if plan is not None:
+        return plan
+    groups: dict[int, list[int]] = {}
+    for i in range(len(cu) - 1):
+        n = cu[i + 1] - cu[i]
+        groups.setdefault(-(-n // bucket) * bucket, []).append(i)
+    shapes, pos_l, start_l, len_l = [], [], [], []
+    for L, seqs in sorted(groups.items()):
+        shapes.append((L, len(seqs)))
+        pos_l.append(torch.arange(L).repeat(len(seqs)))  # position inside the padded row
+        start_l.append(torch.tensor([cu[i] for i in seqs]).repeat_interleave(L))
+        len_l.append(torch.tensor([cu[i + 1] - cu[i] for i in seqs]).repeat_interleave(L))
+    pos, start, length = torch.cat(pos_l), torch.cat(start_l), torch.cat(len_l)
+    valid = pos < length
+    src = torch.where(valid, start + pos, torch.zeros_like(pos))  # any in-range row where padded
+    # gate prefix: the last real token's value up to the end of its chunk
+    hold = pos < (length + chunk - 1) // chunk * chunk
+    src_g = start + torch.minimum(pos, length - 1)
+    out = torch.empty(cu[-1], dtype=torch.long)
+    out[(start + pos)[valid]] = torch.nonzero(valid).squeeze(1)
+    plan = (shapes, src.to(device), valid.to(device), src_g.to(device), hold.to(device), out.to(device))
+    _INDEX_CACHE[key] = plan
+    return plan
+
+
+class _Gather(torch.autograd.Function):
+    """rows[i] = x[src[i]] where keep[i], else ``fill``.  Every token is the
+    source of exactly one real row (``inv[t]``), so the gradient of x is a
+    gather as well (held padding copies of a gate row carry no cotangent)."""
+
+    @staticmethod
+    def forward(ctx, x, src, keep, fill, inv):
+        ctx.save_for_backward(inv)
+        rows = x.index_select(0, src)
+        mask = keep.view(-1, *([1] * (rows.dim() - 1)))
+        return torch.where(mask, rows, torch.full((), fill, dtype=x.dtype, device=x.device))
+
+    @staticmethod
+    def backward(ctx, g):
+        (inv,) = ctx.saved_tensors
+        return g.index_select(0, inv), None, None, None, None
+
+
+class _Scatter(torch.autograd.Function):
+    """out[t] = rows[inv[t]]: the real rows back in packed order; the gradient
+    of the rows is the gather of the packed gradient, zero on padding rows."""
+
+    @staticmethod
+    def forward(ctx, rows, inv, src, valid):
+        ctx.save_for_backward(src, valid)
+        return rows.index_select(0, inv)
+
+    @staticmethod
+    def backward(ctx, g):
+        src, valid = ctx.saved_tensors
+        d = g.index_select(0, src)
+        mask = valid.view(-1, *([1] * (d.dim() - 1)))
+        return torch.where(mask, d, torch.zeros((), dtype=d.dtype, device=d.device)), None, None, None
+
+
+def map_sequences(fn: Callable, tensors: Sequence, cu_seqlens, *, pad: Sequence = (), bucket: int = 1024,
+                  gate: int | None = None, chunk: int = 64):
+    """Apply ``fn(*batched)`` to the sequences of packed ``[1, total, ...]``
+    tensors (other arguments pass through unchanged) and return its output(s)
+    in the packed layout.  ``pad[i]`` is the fill value of ``tensors[i]`` after
+    a sequence's end (default 0); ``tensors[gate]``, a chunk-local gate prefix
+    restarting every ``chunk`` tokens, is held at its last real value to the
+    end of that chunk instead.  ``fn`` receives ``[n_seq, L, ...]`` batches and
+    must return tensors of the same leading shape.  Each packed tensor is
+    gathered once for all groups, and every gradient moves by a gather too
+    (no scatter-add)."""
+    if bucket <= 0 or bucket % 64:
+        raise ValueError("bucket must be a positive multiple of 64")
     cu = offsets(cu_seqlens)
     packed = [t for t in tensors if isinstance(t, torch.Tensor) and t.dim() >= 2]
     if not packed:
@@ -66,65 +137,65 @@ def map_sequences(fn: Callable, tensors: Sequence, cu_seqlens, *, streams: int =
     total = packed[0].shape[1]
     if cu[-1] != total or any(t.shape[0] != 1 or t.shape[1] != total for t in packed):
         raise ValueError(f"packed tensors must be [1, {cu[-1]}, ...] to match cu_seqlens")
-    device = packed[0].device
-    main = torch.cuda.current_stream(device)
-    pool = _streams(device, min(streams, len(cu) - 1))
-    for s in pool:
-        s.wait_stream(main)
+    shapes, src, valid, src_g, hold, out_rows = _plan(cu, bucket, chunk, packed[0].device)
+    sizes = [L * n for L, n in shapes]
+    fills = list(pad) + [0.0] * (len(tensors) - len(pad))
+    per_group = []  # per tensor: its [n, L, ...] batches, or the pass-through argument
+    for i, (t, fill) in enumerate(zip(tensors, fills)):
+        if isinstance(t, torch.Tensor) and t.dim() >= 2:
+            rows = _Gather.apply(t[0], src_g if i == gate else src, hold if i == gate else valid, fill, out_rows)
+            per_group.append([part.view(n, L, *t.shape[2:])
+                              for part, (L, n) in zip(torch.split(rows, sizes), shapes)])
+        else:
+            per_group.append([t] * len(shapes))
+    results, is_tuple = [], False
+    for gi in range(len(shapes)):
+        out = fn(*(arg[gi] for arg in per_group))
+        is_tuple = isinstance(out, tuple)
+        results.append(out if is_tuple else (out,))
     outs = []
-    for i in range(len(cu) - 1):
-        s = pool[i % len(pool)]
-        with torch.cuda.stream(s):
-            args = [t[:, cu[i]:cu[i + 1]] if isinstance(t, torch.Tensor) and t.dim() >= 2 else t for t in tensors]
-            outs.append(fn(*args))
-    for s in pool:
-        main.wait_stream(s)
-    for o in outs:  # made on side streams, read by the concatenation on the main one
-        for t in (o if isinstance(o, tuple) else (o,)):
-            t.record_stream(main)
-    if isinstance(outs[0], tuple):
-        return tuple(torch.cat([o[j] for o in outs], dim=1) for j in range(len(outs[0])))
-    return torch.cat(outs, dim=1)
+    for j in range(len(results[0])):
+        cat = torch.cat([res[j].reshape(-1, *res[j].shape[2:]) for res in results], 0)
+        outs.append(_Scatter.apply(cat, out_rows, src, valid).unsqueeze(0))
+    return tuple(outs) if is_tuple else outs[0]
 
 
-def chunk_kalman_varlen(q_memory, k_memory, kappa, v, g_cumsum, scale: float, cu_seqlens, *, streams: int = 4):
+def chunk_kalman_varlen(q_memory, k_memory, kappa, v, g_cumsum, scale: float, cu_seqlens, *, bucket: int = 1024):
     """``chunk_kalman`` over a packed batch (fp32 output [1, T, H, V])."""
     def one(q, k, kap, vv, g):
-        return diag_kdn_chunk.chunk_kalman(q.contiguous(), k.contiguous(), kap.contiguous(), vv.contiguous(),
-                                           g.contiguous(), scale)
+        return diag_kdn_chunk.chunk_kalman(q, k, kap, vv, g, scale)
 
-    return map_sequences(one, (q_memory, k_memory, kappa, v, g_cumsum), cu_seqlens, streams=streams)
+    return map_sequences(one, (q_memory, k_memory, kappa, v, g_cumsum), cu_seqlens, bucket=bucket, gate=4, chunk=32)
 
 
 def diag_kdn_gain_varlen(k_gain, alpha, omega, r, initial_precision, omega_raw, r_raw, cu_seqlens, *,
-                         streams: int = 4):
+                         bucket: int = 1024):
     """``_diag_kdn_gain`` over a packed batch: the covariance restarts at every sequence."""
     def one(kg, a, w, rr, wr, rrr):
-        return diag_kdn_chunk._diag_kdn_gain(kg.contiguous(), a.contiguous(), w.contiguous(), rr.contiguous(),
-                                            initial_precision, wr.contiguous(), rrr.contiguous())
+        return diag_kdn_chunk._diag_kdn_gain(kg, a, w, rr, initial_precision, wr, rrr)
 
-    return map_sequences(one, (k_gain, alpha, omega, r, omega_raw, r_raw), cu_seqlens, streams=streams)
+    return map_sequences(one, (k_gain, alpha, omega, r, omega_raw, r_raw), cu_seqlens,
+                         pad=(0.0, 1.0, 0.0, 1.0, 0.0, 0.0), bucket=bucket)
 
 
 def chunk_kda_precumsum_varlen(q, k, v, g_cumsum, beta, scale: float | None = None, *, cu_seqlens,
-                               streams: int = 4):
+                               bucket: int = 1024):
     """``_chunk_kda_precumsum_paired`` over a packed batch."""
     def one(qq, kk, vv, g, b):
-        return iso_kdn_chunk._chunk_kda_precumsum_paired(qq.contiguous(), kk.contiguous(), vv.contiguous(),
-                                                         g.contiguous(), b.contiguous(), scale)
+        return iso_kdn_chunk._chunk_kda_precumsum_paired(qq, kk, vv, g, b, scale)
 
-    return map_sequences(one, (q, k, v, g_cumsum, beta), cu_seqlens, streams=streams)
+    return map_sequences(one, (q, k, v, g_cumsum, beta), cu_seqlens, bucket=bucket, gate=3, chunk=64)
 
 
 def iso_kdn_gain_varlen(a, omega, r, initial_precision, *, head_dim: int, cu_seqlens, out_dtype=None,
-                        info_scale=None, streams: int = 4):
+                        info_scale=None, bucket: int = 1024):
     """``iso_kdn_gain`` over a packed batch: the covariance restarts at every sequence."""
     def one(aa, w, rr):
-        return iso_kdn_chunk.iso_kdn_gain(aa.contiguous(), w.contiguous(), rr.contiguous(), initial_precision,
-                                          head_dim=head_dim, out_dtype=out_dtype, info_scale=info_scale)
+        return iso_kdn_chunk.iso_kdn_gain(aa, w, rr, initial_precision, head_dim=head_dim, out_dtype=out_dtype,
+                                          info_scale=info_scale)
 
-    return map_sequences(one, (a, omega, r), cu_seqlens, streams=streams)
+    return map_sequences(one, (a, omega, r), cu_seqlens, pad=(1.0, 0.0, 1.0), bucket=bucket)
 
 
 __all__ = ("chunk_kalman_varlen", "diag_kdn_gain_varlen", "chunk_kda_precumsum_varlen", "iso_kdn_gain_varlen",
-           "map_sequences", "offsets", "join")
+           "map_sequences", "offsets")
