@@ -277,12 +277,9 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
     tc::ld16(tq + TDQ + 16 * cg, x);
     if (lane < 16) {
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int j = 16 * cg + i;
-        const float d = j <= m ? x[i] : 0.f;
-        *at(Lo::dQu, m, j, C) = __float2bfloat16_rn(d);
-        *at(Lo::dQ, m, j, C) = __float2bfloat16_rn(p.scale * d);
-      }
+      for (int i = 0; i < 16; ++i) x[i] = 16 * cg + i <= m ? x[i] : 0.f;
+      tc::st_row16(base + Lo::dQu, C, m, 16 * cg, x, 1.f);
+      tc::st_row16(base + Lo::dQ, C, m, 16 * cg, x, p.scale);
     }
   }
   publish();
@@ -311,12 +308,14 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
     float x[16];
     tc::ld16(tq + col + 16 * cg, x);
     if (lane < 16) {
+      // this thread's 16 columns of row m are two whole 16-byte granules
       const int m = 16 * q + lane;
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const int j = 16 * cg + i;
-        *at(tile, m, j, C) = __float2bfloat16_rn((strict ? j < m : j <= m) ? sign * x[i] : 0.f);
+        x[i] = (strict ? j < m : j <= m) ? x[i] : 0.f;
       }
+      tc::st_row16(base + tile, C, m, 16 * cg, x, sign);
     }
   };
   cc_tile(TDT, Lo::dT, 1.f, true);
