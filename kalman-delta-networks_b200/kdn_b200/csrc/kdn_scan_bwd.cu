@@ -222,13 +222,13 @@ __global__ void __launch_bounds__(kSeqThreads + 32, 1) scan_bwd_state_kernel(Sca
     if (threadIdx.x == 32) bulk_wait_all();
 }
 
-// Tensor-core reverse sweep (bf16 precision): one CTA per (b, h) stream with
-// the 128 x 128 fp32 adjoint in TMEM; same roles as the tensor-core forward
-// (8 data warps, one MMA thread, one producer warp).  Per chunk, with the
+// Tensor-core reverse sweep (bf16 precision): two CTAs per (b, h) stream, each
+// with 64 value columns of the 128 x 128 fp32 adjoint in TMEM; same roles as
+// the tensor-core forward (8 data warps, one MMA thread, one producer warp).  Per chunk, with the
 // record's folded factors (Qs = scale fr Qr, Kf = fL Kc, Wf = fr W0,
 // Qq = scale Q):
 //   dS -> bf16 operand (saved as dh);  dS <- 2^g_L dS           (TMEM ld / st)
-//   ddelta^T = dO^T Qq + dS^T Kf^T, Qq read as its transpose Qt (MMA, M = 128 values)
+//   ddelta^T = dO^T Qq + dS^T Kf^T, Qq read as its transpose Qt (MMA, M = 64 values)
 //   dS += Qs^T dO - Wf^T ddelta                                  (MMA, M = 128 keys)
 template <class CF>
 struct StateTcLayout {
@@ -237,12 +237,12 @@ struct StateTcLayout {
   static constexpr bool DF32 = !CF::ISO;  // the diagonal variant's cotangent arrives as fp32 rows
   using R = RecTc<CF>;
   static constexpr size_t rec = R::bytes - R::bwd_begin;  // the record from Qs on
-  static constexpr size_t dO = rec;  // iso: [2][C][64] bf16 swizzled; diag: [C][128] fp32
-  static constexpr size_t stage = align_up(dO + (size_t)C * (DF32 ? 512 : 256), 1024);
-  static constexpr size_t dOb = NS * stage;  // diag: the bf16-rounded operand [2][C][64]
-  static constexpr size_t DS = dOb + (DF32 ? align_up((size_t)C * 256, 1024) : 0);  // [2][KD][64] (also dh)
-  static constexpr size_t DD = DS + (size_t)kKD * 256;                               // ddelta [2][C][64]
-  static constexpr size_t bar = DD + align_up((size_t)C * 256, 1024);
+  static constexpr size_t dO = rec;  // iso: [C][64] bf16 swizzled; diag: [C][64] fp32
+  static constexpr size_t stage = align_up(dO + (size_t)C * (DF32 ? 256 : 128), 1024);
+  static constexpr size_t dOb = NS * stage;  // diag: the bf16-rounded operand [C][64]
+  static constexpr size_t DS = dOb + (DF32 ? align_up((size_t)C * 128, 1024) : 0);  // [KD][64] (also dh)
+  static constexpr size_t DD = DS + (size_t)kKD * 128;                               // ddelta [C][64]
+  static constexpr size_t bar = DD + align_up((size_t)C * 128, 1024);
   static constexpr size_t bytes = bar + 128 + 1024;
 };
 
@@ -252,15 +252,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_bwd_state_tc_kernel(ScanPa
   using Lo = StateTcLayout<CF>;
   using R = RecTc<CF>;
   constexpr int C = CF::C, NS = Lo::NS, HC = C / 2;
-  constexpr uint32_t TS = 0, TD = kKD;  // TMEM columns: adjoint, ddelta^T
+  constexpr uint32_t TS = 0, TD = 64;  // TMEM columns: adjoint, ddelta^T
   constexpr int NTH = kTcWarps * 32;
   extern __shared__ __align__(1024) char smem_raw[];
   char* base = align1024(smem_raw);
 
-  const int bh = blockIdx.x, b = bh / p.H, h = bh - b * p.H;
+  const int bh = blockIdx.x, vh = blockIdx.y, V0 = 64 * vh, b = bh / p.H, h = bh - b * p.H;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const char* recs = static_cast<const char*>(p.rec) + (size_t)bh * p.NT * R::bytes;
-  char* dhout = static_cast<char*>(p.dh) + (size_t)bh * p.NT * 2 * hblock_bytes<CF>();
+  char* dhout =
+      static_cast<char*>(p.dh) + (size_t)bh * p.NT * 2 * hblock_bytes<CF>() + (size_t)vh * hblock_bytes<CF>();
   uint64_t* full = reinterpret_cast<uint64_t*>(base + Lo::bar);
   uint64_t* empty = full + NS;
   uint64_t* mmab = empty + NS;
@@ -288,10 +289,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_bwd_state_tc_kernel(ScanPa
       if (it >= NS) mbar_wait(&empty[s], (it / NS - 1) & 1, p.status);
       if (lane == 0) {
         char* st = base + s * Lo::stage;
-        mbar_expect_tx(&full[s], (unsigned)(Lo::rec + (size_t)C * (Lo::DF32 ? 512 : 256)));
+        mbar_expect_tx(&full[s], (unsigned)(Lo::rec + (size_t)C * (Lo::DF32 ? 256 : 128)));
         bulk_g2s(st, recs + (size_t)c * R::bytes + R::bwd_begin, (unsigned)Lo::rec, &full[s]);
-        tma_load_4d(st + Lo::dO, &maps.in, 0, h, c * C, b, &full[s]);
-        if constexpr (!Lo::DF32) tma_load_4d(st + Lo::dO + C * 128, &maps.in, 64, h, c * C, b, &full[s]);
+        tma_load_4d(st + Lo::dO, &maps.in, V0, h, c * C, b, &full[s]);
       }
       __syncwarp();
     }
@@ -299,13 +299,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_bwd_state_tc_kernel(ScanPa
   }
 
   const int q = warp & 3, hf = warp >> 2;
-  const int row = 32 * q + lane;
+  const int row = 32 * q + lane;  // key (adjoint)
+  const int vc = 16 * q + lane;   // value column of this CTA (ddelta^T, M = 64: lanes < 16)
   const uint32_t tl = tmem + ((uint32_t)(32 * q) << 16);
-  for (int j = 0; j < 64; j += 16) {
+  for (int j = 0; j < 32; j += 16) {
     float x[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) x[i] = p.dST ? p.dST[((size_t)bh * kKD + row) * kVD + 64 * hf + j + i] : 0.f;
-    tc::st16(tl + TS + 64 * hf + j, x);
+    for (int i = 0; i < 16; ++i) x[i] = p.dST ? p.dST[((size_t)bh * kKD + row) * kVD + V0 + 32 * hf + j + i] : 0.f;
+    tc::st16(tl + TS + 32 * hf + j, x);
   }
   tc::wait_st();
   uint32_t mph = 0;
@@ -318,24 +319,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_bwd_state_tc_kernel(ScanPa
     if constexpr (Lo::DF32) {
       // the reference rounds the fp32 cotangent to bf16 first (diag_kdn_chunk.py:3277)
       const float* src = reinterpret_cast<const float*>(st + Lo::dO);
-      for (int e = threadIdx.x; e < C * 16; e += NTH) {
-        const int r = e >> 4, g = e & 15;
+      for (int e = threadIdx.x; e < C * 8; e += NTH) {
+        const int r = e >> 3, g = e & 7;
         float x[8];
-        ld8(x, src + r * kVD + 8 * g);
+        ld8(x, src + r * 64 + 8 * g);
         st8(reinterpret_cast<bf16*>(sdO + tc::sw_off(r, 8 * g, C)), x);
       }
     }
     {
       // adjoint operand (and dh), then dS <- 2^g_L dS
       const float gl = reinterpret_cast<const float*>(st + (R::F - R::bwd_begin))[2 * kKD + row];
-#pragma unroll 1
-      for (int j = 0; j < 64; j += 16) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 16) {
         float x[16];
-        tc::ld16(tl + TS + 64 * hf + j, x);
-        tc::st_row16(sDS, kKD, row, 64 * hf + j, x, 1.f);
+        tc::ld16(tl + TS + 32 * hf + j, x);
+        tc::st_row16(sDS, kKD, row, 32 * hf + j, x, 1.f);
 #pragma unroll
         for (int i = 0; i < 16; ++i) x[i] *= gl;
-        tc::st16(tl + TS + 64 * hf + j, x);
+        tc::st16(tl + TS + 32 * hf + j, x);
       }
       tc::wait_st();
     }
@@ -343,12 +344,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_bwd_state_tc_kernel(ScanPa
     tc::fence_before();
     bar_sync(1, NTH);
     if (threadIdx.x == 32) {
-      bulk_s2g(dhout + (size_t)c * 2 * hblock_bytes<CF>(), sDS, (unsigned)(2 * hblock_bytes<CF>()));
+      bulk_s2g(dhout + (size_t)c * 2 * hblock_bytes<CF>(), sDS, (unsigned)hblock_bytes<CF>());
       bulk_commit();
     }
     if (threadIdx.x == 0) {
       tc::fence_after();
-      constexpr uint32_t id2 = tc::idesc(128, C, true, false);
+      constexpr uint32_t id2 = tc::idesc(64, C, true, false);
       for (int ks = 0; ks < C / 16; ++ks)
         tc::mma(tmem + TD, tc::desc_mn(sdO, C, ks), tc::desc_k(st + (R::Qt - R::bwd_begin), C, ks), id2, ks > 0);
       for (int ks = 0; ks < kKD / 16; ++ks)
@@ -358,13 +359,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_bwd_state_tc_kernel(ScanPa
     mbar_wait(mmab, mph, p.status);
     mph ^= 1;
     tc::fence_after();
-#pragma unroll 1
+#pragma unroll
     for (int j = 0; j < HC; j += 16) {
       float x[16];
       tc::ld16(tl + TD + HC * hf + j, x);
+      if (lane < 16) {
 #pragma unroll
-      for (int i = 0; i < 16; ++i)
-        *reinterpret_cast<bf16*>(sDD + tc::sw_off(HC * hf + j + i, row, C)) = __float2bfloat16_rn(x[i]);
+        for (int i = 0; i < 16; ++i)
+          *reinterpret_cast<bf16*>(sDD + tc::sw_off(HC * hf + j + i, vc, C)) = __float2bfloat16_rn(x[i]);
+      }
     }
     if (threadIdx.x == 32) bulk_wait_read<0>();  // dh has left the adjoint operand (rewritten next chunk)
     fence_async_shared();
@@ -372,7 +375,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_bwd_state_tc_kernel(ScanPa
     bar_sync(1, NTH);
     if (threadIdx.x == 0) {
       tc::fence_after();
-      constexpr uint32_t ids = tc::idesc(128, 128, true, true), idn = tc::idesc(128, 128, true, true, true);
+      constexpr uint32_t ids = tc::idesc(128, 64, true, true), idn = tc::idesc(128, 64, true, true, true);
       for (int ks = 0; ks < C / 16; ++ks)
         tc::mma(tmem + TS, tc::desc_mn(st + (R::Qs - R::bwd_begin), C, ks), tc::desc_mn(sdO, C, ks), ids, true);
       for (int ks = 0; ks < C / 16; ++ks)
@@ -385,11 +388,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_bwd_state_tc_kernel(ScanPa
     tc::fence_after();
   }
   if (p.dS0) {
-    for (int j = 0; j < 64; j += 16) {
+    for (int j = 0; j < 32; j += 16) {
       float x[16];
-      tc::ld16(tl + TS + 64 * hf + j, x);
+      tc::ld16(tl + TS + 32 * hf + j, x);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) p.dS0[((size_t)bh * kKD + row) * kVD + 64 * hf + j + i] = x[i];
+      for (int i = 0; i < 16; ++i) p.dS0[((size_t)bh * kKD + row) * kVD + V0 + 32 * hf + j + i] = x[i];
     }
   }
   if (threadIdx.x == 32) bulk_wait_all();
@@ -931,10 +934,10 @@ int launch_bwd_state(const ScanParams& p, cudaStream_t st) {
   } else {
     TcMaps maps;
     int rc = CF::ISO ? encode_bthd(&maps.in, p.dO, true, p.B, p.T, p.H, kVD, 64, CF::C, true)
-                     : encode_bthd(&maps.in, p.dO, false, p.B, p.T, p.H, kVD, kVD, CF::C, false);
+                     : encode_bthd(&maps.in, p.dO, false, p.B, p.T, p.H, kVD, 64, CF::C, false);
     if (rc != KDN_OK) return rc;
     maps.out = maps.in;
-    scan_bwd_state_tc_kernel<CF><<<p.B * p.H, kTcThreads, StateTcLayout<CF>::bytes, st>>>(p, maps);
+    scan_bwd_state_tc_kernel<CF><<<dim3(p.B * p.H, 2), kTcThreads, StateTcLayout<CF>::bytes, st>>>(p, maps);
   }
   return check_launch("scan_bwd_state_kernel");
 }

@@ -200,14 +200,15 @@ __global__ void __launch_bounds__(kSeqThreads + 32, 1) scan_fwd_kernel(ScanParam
 }
 
 // ---------------------------------------------------------------------------
-// Tensor-core sequential pass (bf16 precision): one CTA per (b, h) stream
-// carries the whole 128 x 128 fp32 state in TMEM.  Warps 0-7 move data
-// between TMEM and shared memory, thread 0 issues the MMAs, warp 8 streams
-// the chunk records (bulk copy) and value rows (TMA, 128-byte swizzle) into
-// NS stages.  Per chunk, with the record's folded factors
+// Tensor-core sequential pass (bf16 precision): two CTAs per (b, h) stream,
+// each carrying 64 value columns of the 128 x 128 fp32 state in TMEM (the
+// recurrence does not mix value columns).  Warps 0-7 move data between TMEM
+// and shared memory, thread 0 issues the MMAs, warp 8 streams the chunk
+// records (bulk copy) and the CTA's value columns (TMA, 128-byte swizzle)
+// into NS stages.  Per chunk, with the record's folded factors
 // (Qs = scale fr Qr, Kf = fL Kc, Wf = fr W0, Qq = scale Q):
 //   S -> bf16 operand (saved as h);  S <- 2^g_L S            (TMEM ld / st)
-//   delta^T = v^T T^T - S^T Wf^T                               (MMA, M = 128 values)
+//   delta^T = v^T T^T - S^T Wf^T                               (MMA, M = 64 values)
 //   o^T = S^T Qs^T + delta^T Qq^T;  S += Kf^T delta            (MMA)
 //   o -> shared memory -> one TMA store of the chunk's rows
 // ---------------------------------------------------------------------------
@@ -216,12 +217,12 @@ struct FwdTcLayout {
   static constexpr int C = CF::C;
   static constexpr int NS = CF::ISO ? 2 : 3;
   using R = RecTc<CF>;
-  static constexpr size_t v = R::fwd_end;  // [2][C][64] bf16, swizzled by the TMA engine
-  static constexpr size_t stage = align_up(v + (size_t)C * 256, 1024);
-  static constexpr size_t S = NS * stage;                 // state operand [2][KD][64] bf16 (also h)
-  static constexpr size_t Del = S + (size_t)kKD * 256;    // delta [2][C][64] bf16, then the output rows
-  static constexpr size_t O_bytes = (size_t)C * kVD * (CF::ISO ? 2 : 4);
-  static constexpr size_t bar = Del + align_up(cmax((size_t)C * 256, O_bytes), 1024);
+  static constexpr size_t v = R::fwd_end;  // [C][64] bf16, swizzled by the TMA engine
+  static constexpr size_t stage = align_up(v + (size_t)C * 128, 1024);
+  static constexpr size_t S = NS * stage;                 // state operand [KD][64] bf16 (also h)
+  static constexpr size_t Del = S + (size_t)kKD * 128;    // delta [C][64] bf16, then the output rows
+  static constexpr size_t O_bytes = (size_t)C * 64 * (CF::ISO ? 2 : 4);
+  static constexpr size_t bar = Del + align_up(cmax((size_t)C * 128, O_bytes), 1024);
   static constexpr size_t bytes = bar + 128 + 1024;       // barriers and TMEM slot; alignment slack
 };
 
@@ -231,15 +232,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_fwd_tc_kernel(ScanParams p
   using R = RecTc<CF>;
   using OutT = typename std::conditional<CF::ISO, bf16, float>::type;
   constexpr int C = CF::C, NS = Lo::NS, HC = C / 2;
-  constexpr uint32_t TS = 0, TD = kKD, TO = kKD + C;  // TMEM columns: state, delta^T, o^T
+  constexpr uint32_t TS = 0, TD = 64, TO = 64 + C;  // TMEM columns: state, delta^T, o^T
   constexpr int NTH = kTcWarps * 32;
   extern __shared__ __align__(1024) char smem_raw[];
   char* base = align1024(smem_raw);
 
-  const int bh = blockIdx.x, b = bh / p.H, h = bh - b * p.H;
+  const int bh = blockIdx.x, vh = blockIdx.y, V0 = 64 * vh, b = bh / p.H, h = bh - b * p.H;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const char* recs = static_cast<const char*>(p.rec) + (size_t)bh * p.NT * R::bytes;
-  char* hout = static_cast<char*>(p.h) + (size_t)bh * p.NT * 2 * hblock_bytes<CF>();
+  char* hout = static_cast<char*>(p.h) + (size_t)bh * p.NT * 2 * hblock_bytes<CF>() + (size_t)vh * hblock_bytes<CF>();
   uint64_t* full = reinterpret_cast<uint64_t*>(base + Lo::bar);
   uint64_t* empty = full + NS;
   uint64_t* mmab = empty + NS;
@@ -268,25 +269,27 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_fwd_tc_kernel(ScanParams p
       if (it >= NS) mbar_wait(&empty[s], (it / NS - 1) & 1, p.status);
       if (lane == 0) {
         char* st = base + s * Lo::stage;
-        mbar_expect_tx(&full[s], (unsigned)(R::fwd_end + (size_t)C * 256));
+        mbar_expect_tx(&full[s], (unsigned)(R::fwd_end + (size_t)C * 128));
         bulk_g2s(st, recs + (size_t)c * R::bytes, (unsigned)R::fwd_end, &full[s]);
-        tma_load_4d(st + Lo::v, &maps.in, 0, h, c * C, b, &full[s]);
-        tma_load_4d(st + Lo::v + C * 128, &maps.in, 64, h, c * C, b, &full[s]);
+        tma_load_4d(st + Lo::v, &maps.in, V0, h, c * C, b, &full[s]);
       }
       __syncwarp();
     }
     return;
   }
 
-  // compute warps: warp w reads TMEM lanes 32(w%4).., column half w/4
+  // compute warps: warp w reads TMEM lanes 32(w%4).., column half w/4; the
+  // M = 64 accumulators delta^T, o^T hold value column m in lane
+  // (m % 16) + 32 (m / 16), i.e. lanes 0-15 of each quadrant
   const int q = warp & 3, hf = warp >> 2;
-  const int row = 32 * q + lane;  // key (state) or value channel (delta^T, o^T)
+  const int row = 32 * q + lane;  // key (state)
+  const int vc = 16 * q + lane;   // value column of this CTA (delta^T, o^T; lanes < 16)
   const uint32_t tl = tmem + ((uint32_t)(32 * q) << 16);
-  for (int j = 0; j < 64; j += 16) {
+  for (int j = 0; j < 32; j += 16) {
     float x[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) x[i] = p.S0 ? p.S0[((size_t)bh * kKD + row) * kVD + 64 * hf + j + i] : 0.f;
-    tc::st16(tl + TS + 64 * hf + j, x);
+    for (int i = 0; i < 16; ++i) x[i] = p.S0 ? p.S0[((size_t)bh * kKD + row) * kVD + V0 + 32 * hf + j + i] : 0.f;
+    tc::st16(tl + TS + 32 * hf + j, x);
   }
   tc::wait_st();
   uint32_t mph = 0;
@@ -298,14 +301,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_fwd_tc_kernel(ScanParams p
     {
       // state operand (and h), then S <- 2^g_L S
       const float gl = reinterpret_cast<const float*>(st + R::F)[2 * kKD + row];
-#pragma unroll 1
-      for (int j = 0; j < 64; j += 16) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 16) {
         float x[16];
-        tc::ld16(tl + TS + 64 * hf + j, x);
-        tc::st_row16(sS, kKD, row, 64 * hf + j, x, 1.f);
+        tc::ld16(tl + TS + 32 * hf + j, x);
+        tc::st_row16(sS, kKD, row, 32 * hf + j, x, 1.f);
 #pragma unroll
         for (int i = 0; i < 16; ++i) x[i] *= gl;
-        tc::st16(tl + TS + 64 * hf + j, x);
+        tc::st16(tl + TS + 32 * hf + j, x);
       }
       tc::wait_st();
     }
@@ -314,12 +317,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_fwd_tc_kernel(ScanParams p
     tc::fence_before();
     bar_sync(1, NTH);
     if (threadIdx.x == 32) {
-      bulk_s2g(hout + (size_t)c * 2 * hblock_bytes<CF>(), sS, (unsigned)(2 * hblock_bytes<CF>()));
+      bulk_s2g(hout + (size_t)c * 2 * hblock_bytes<CF>(), sS, (unsigned)hblock_bytes<CF>());
       bulk_commit();
     }
     if (threadIdx.x == 0) {
       tc::fence_after();
-      constexpr uint32_t id = tc::idesc(128, C, true, false), idn = tc::idesc(128, C, true, false, true);
+      constexpr uint32_t id = tc::idesc(64, C, true, false), idn = tc::idesc(64, C, true, false, true);
       for (int ks = 0; ks < C / 16; ++ks)
         tc::mma(tmem + TD, tc::desc_mn(st + Lo::v, C, ks), tc::desc_k(st + R::T, C, ks), id, ks > 0);
       for (int ks = 0; ks < kKD / 16; ++ks)
@@ -329,14 +332,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_fwd_tc_kernel(ScanParams p
     mbar_wait(mmab, mph, p.status);
     mph ^= 1;
     tc::fence_after();
-    // delta (lane = value channel) -> bf16 operand tile [2][C][64]
-#pragma unroll 1
+    // delta (value column vc, lanes < 16) -> bf16 operand tile [C][64]
+#pragma unroll
     for (int j = 0; j < HC; j += 16) {
       float x[16];
       tc::ld16(tl + TD + HC * hf + j, x);
+      if (lane < 16) {
 #pragma unroll
-      for (int i = 0; i < 16; ++i)
-        *reinterpret_cast<bf16*>(sDel + tc::sw_off(HC * hf + j + i, row, C)) = __float2bfloat16_rn(x[i]);
+        for (int i = 0; i < 16; ++i)
+          *reinterpret_cast<bf16*>(sDel + tc::sw_off(HC * hf + j + i, vc, C)) = __float2bfloat16_rn(x[i]);
+      }
     }
     if (threadIdx.x == 32) bulk_wait_read<0>();  // h has left the state operand (rewritten next chunk)
     fence_async_shared();
@@ -344,7 +349,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_fwd_tc_kernel(ScanParams p
     bar_sync(1, NTH);
     if (threadIdx.x == 0) {
       tc::fence_after();
-      constexpr uint32_t ido = tc::idesc(128, C, true, false), ids = tc::idesc(128, 128, true, true);
+      constexpr uint32_t ido = tc::idesc(64, C, true, false), ids = tc::idesc(128, 64, true, true);
       for (int ks = 0; ks < kKD / 16; ++ks)
         tc::mma(tmem + TO, tc::desc_mn(sS, kKD, ks), tc::desc_k(st + R::Qs, C, ks), ido, ks > 0);
       for (int ks = 0; ks < C / 16; ++ks)
@@ -357,30 +362,32 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_fwd_tc_kernel(ScanParams p
     mbar_wait(mmab, mph, p.status);
     mph ^= 1;
     tc::fence_after();
-    // output rows (lane = value channel) over the delta tile, then one TMA store
+    // output rows (value column vc) over the delta tile, then one TMA store
     {
       OutT* sO = reinterpret_cast<OutT*>(sDel);
-#pragma unroll 1
+#pragma unroll
       for (int j = 0; j < HC; j += 16) {
         float x[16];
         tc::ld16(tl + TO + HC * hf + j, x);
+        if (lane < 16) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) sO[(HC * hf + j + i) * kVD + row] = from_f<OutT>(x[i]);
+          for (int i = 0; i < 16; ++i) sO[(HC * hf + j + i) * 64 + vc] = from_f<OutT>(x[i]);
+        }
       }
     }
     fence_async_shared();
     bar_sync(1, NTH);
     if (threadIdx.x == 0) {
-      tc::tma_store_4d(&maps.out, sDel, 0, h, t0, b);
+      tc::tma_store_4d(&maps.out, sDel, V0, h, t0, b);
       bulk_commit();
     }
   }
   if (p.ST) {
-    for (int j = 0; j < 64; j += 16) {
+    for (int j = 0; j < 32; j += 16) {
       float x[16];
-      tc::ld16(tl + TS + 64 * hf + j, x);
+      tc::ld16(tl + TS + 32 * hf + j, x);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) p.ST[((size_t)bh * kKD + row) * kVD + 64 * hf + j + i] = x[i];
+      for (int i = 0; i < 16; ++i) p.ST[((size_t)bh * kKD + row) * kVD + V0 + 32 * hf + j + i] = x[i];
     }
   }
   if (threadIdx.x == 0 || threadIdx.x == 32) bulk_wait_all();
@@ -425,9 +432,9 @@ int launch_fwd_seq(const ScanParams& p, cudaStream_t st) {
     TcMaps maps;
     rc = encode_bthd(&maps.in, p.v, true, p.B, p.T, p.H, kVD, 64, CF::C, true);
     if (rc != KDN_OK) return rc;
-    rc = encode_bthd(&maps.out, p.o, CF::ISO, p.B, p.T, p.H, kVD, kVD, CF::C, false);
+    rc = encode_bthd(&maps.out, p.o, CF::ISO, p.B, p.T, p.H, kVD, 64, CF::C, false);
     if (rc != KDN_OK) return rc;
-    scan_fwd_tc_kernel<CF><<<p.B * p.H, kTcThreads, smem, st>>>(p, maps);
+    scan_fwd_tc_kernel<CF><<<dim3(p.B * p.H, 2), kTcThreads, smem, st>>>(p, maps);
     return check_launch("scan_fwd_tc_kernel");
   }
 }
