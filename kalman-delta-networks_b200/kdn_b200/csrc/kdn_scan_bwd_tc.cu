@@ -25,6 +25,7 @@ namespace kdn {
 struct alignas(64) ChunkMaps {
   CUtensorMap v, dO, dv;  // value rows (128-byte swizzle), dv rows (plain)
   CUtensorMap g, k, q;    // the chunk's raw rows again, plain, for the gate mapping
+  CUtensorMap dk, dq, dg; // gradient rows (plain), stored from their staging tiles
 };
 
 template <class CF>
@@ -379,8 +380,7 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
   float* xs = reinterpret_cast<float*>(base + Lo::Kr);
   static_assert(Lo::Tt + 8192 >= 8 * 4 * 512 * 4, "exact-path scratch");
   // the same 64 KB once the mapping is done (on the fast path already during
-  // it): the dg, dk, dq rows [C][128], written lane = key and copied out with
-  // 16-byte stores
+  // it): the dg, dk, dq rows [C][128], written lane = key and stored by TMA
   float* sdg = xs;
   bf16* sdk = reinterpret_cast<bf16*>(base + Lo::Kr + C * kKD * 4);
   bf16* sdq = sdk + C * kKD;
@@ -505,23 +505,18 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
     }
   }
   if (threadIdx.x < L) p.dbeta[tok_row(p, b, h, t0 + threadIdx.x)] = tsum[threadIdx.x];
+  // the staged rows leave by TMA stores (rows past the sequence's end are clipped)
+  fence_async_shared();
   __syncthreads();
-  // copy-out of the valid rows: 16 bytes per thread and store
-  for (int e = threadIdx.x; e < L * 16; e += 512) {
-    const int r = e >> 4, c8 = 8 * (e & 15);
-    const size_t off = tok_row(p, b, h, t0 + r) * kKD + c8;
-    *reinterpret_cast<uint4*>(p.dk + off) = *reinterpret_cast<const uint4*>(sdk + r * kKD + c8);
-    *reinterpret_cast<uint4*>(p.dq + off) = *reinterpret_cast<const uint4*>(sdq + r * kKD + c8);
-  }
-  if (ch.fast) {
-    for (int e = threadIdx.x; e < L * 32; e += 512) {
-      const int r = e >> 5, c4 = 4 * (e & 31);
-      *reinterpret_cast<float4*>(p.dg + tok_row(p, b, h, t0 + r) * kKD + c4) =
-          *reinterpret_cast<const float4*>(sdg + r * kKD + c4);
-    }
+  if (threadIdx.x == 0) {
+    tc::tma_store_4d(&maps.dk, sdk, 0, h, t0, b);
+    tc::tma_store_4d(&maps.dq, sdq, 0, h, t0, b);
+    if (ch.fast) tc::tma_store_4d(&maps.dg, sdg, 0, h, t0, b);
+    bulk_commit();
   }
 
-  if (threadIdx.x == 0) bulk_wait_all();
+  // shared memory must outlive the stores' reads; their writes complete on their own
+  if (threadIdx.x == 0) bulk_wait_read<0>();
   tc::fence_before();
   __syncthreads();
   if (warp == 0) {
@@ -547,6 +542,9 @@ int launch_bwd_chunk_tc(const ScanParams& p, cudaStream_t st) {
   if (rc == KDN_OK) rc = encode_bthd(&maps.g, p.g, false, p.B, p.T, p.H, kKD, kKD, CF::C, false);
   if (rc == KDN_OK) rc = encode_bthd(&maps.k, p.k, true, p.B, p.T, p.H, kKD, kKD, CF::C, false);
   if (rc == KDN_OK) rc = encode_bthd(&maps.q, p.q, true, p.B, p.T, p.H, kKD, kKD, CF::C, false);
+  if (rc == KDN_OK) rc = encode_bthd(&maps.dk, p.dk, true, p.B, p.T, p.H, kKD, kKD, CF::C, false);
+  if (rc == KDN_OK) rc = encode_bthd(&maps.dq, p.dq, true, p.B, p.T, p.H, kKD, kKD, CF::C, false);
+  if (rc == KDN_OK) rc = encode_bthd(&maps.dg, p.dg, false, p.B, p.T, p.H, kKD, kKD, CF::C, false);
   if (rc != KDN_OK) return rc;
   scan_bwd_chunk_tc_kernel<CF><<<dim3(p.c_hi - p.c_lo, p.B * p.H), 512, smem, st>>>(p, maps);
   return check_launch("scan_bwd_chunk_tc_kernel");
