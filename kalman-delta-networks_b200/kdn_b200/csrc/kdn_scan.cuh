@@ -109,7 +109,7 @@ struct Rec {
 // Tensor-core record (bf16 precision): tiles in the swizzled layout of
 // kdn_tc.cuh, with the chunk's scale factors folded in so that the
 // sequential passes carry the unscaled state:
-//   T, Qq = scale Q, Qt = scale Q^T, Tt = T^T     [C][64] (columns >= C unused)
+//   T, Qq = scale Q, Qt = scale Q^T              [C][64] (columns >= C unused)
 //   Qs = scale fr Qr,  Kf = fL Kc,  Wf = fr W0   [2][C][64] (64 keys per block)
 //   fr, fL, 2^g_L                                  [3][KD] fp32
 // The forward reads [0, fwd_end), the reverse sweep [bwd_begin, bytes).
@@ -123,8 +123,7 @@ struct RecTc {
   static constexpr size_t Wf = Kf + (size_t)C * 256;
   static constexpr size_t F = Wf + (size_t)C * 256;
   static constexpr size_t Qt = F + align_up(3 * kKD * 4, 1024);
-  static constexpr size_t Tt = Qt + (size_t)C * 128;
-  static constexpr size_t bytes = Tt + (size_t)C * 128;
+  static constexpr size_t bytes = Qt + (size_t)C * 128;
   static constexpr size_t fwd_end = Qt;
   static constexpr size_t bwd_begin = Qs;
   static_assert(bytes % 1024 == 0 && Qs % 1024 == 0, "1024-byte aligned tiles");

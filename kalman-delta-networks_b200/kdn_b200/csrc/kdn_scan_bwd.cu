@@ -236,7 +236,7 @@ struct StateTcLayout {
   static constexpr int NS = CF::ISO ? 2 : 3;
   static constexpr bool DF32 = !CF::ISO;  // the diagonal variant's cotangent arrives as fp32 rows
   using R = RecTc<CF>;
-  static constexpr size_t rec = R::Tt - R::bwd_begin;  // the record from Qs up to Tt (unused here)
+  static constexpr size_t rec = R::bytes - R::bwd_begin;  // the record from Qs on
   static constexpr size_t dO = rec;  // iso: [C][64] bf16 swizzled; diag: [C][64] fp32
   static constexpr size_t stage = align_up(dO + (size_t)C * (DF32 ? 256 : 128), 1024);
   static constexpr size_t dOb = NS * stage;  // diag: the bf16-rounded operand [C][64]

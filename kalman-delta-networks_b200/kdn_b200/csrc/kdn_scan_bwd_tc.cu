@@ -33,7 +33,7 @@ struct ChunkTcLayout {
   static_assert(CF::ISO && CF::C == 64 && !CF::F32, "isotropic bf16 chunks of 64");
   static constexpr int C = 64;
   // whole kernel
-  static constexpr size_t Kr = 0, Qr = 16384, Kc = 32768, T = 49152, Tt = 57344;
+  static constexpr size_t Kr = 0, Qr = 16384, Kc = 32768, T = 49152, Xs = 57344;  // Xs: 8 KB scratch
   // Qt | Kf Wf (record), then delta | ddelta
   static constexpr size_t G = 65536;
   static constexpr size_t Qt = G, Kf = G + 8192, Wf = G + 8192 + 16384;
@@ -50,7 +50,7 @@ struct ChunkTcLayout {
   static constexpr size_t small = A + 65536;
   static constexpr size_t bar = small + align_up((small_floats<CF>() + 2 * kKD + 3 * C) * 4, 128);
   static constexpr size_t bytes = bar + 64 + 1024;
-  static constexpr unsigned load_bytes = 3 * C * 128 + 2 * C * 256 + 2 * 32768 + 2 * C * 256;
+  static constexpr unsigned load_bytes = 2 * C * 128 + 2 * C * 256 + 2 * 32768 + 2 * C * 256;
 };
 
 // Exact-path score terms of one (token r, key) element: the sum over the
@@ -150,7 +150,6 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
     mbar_expect_tx(ldbar, Lo::load_bytes);
     bulk_g2s(base + Lo::T, rec + RT::T, C * 128, ldbar);
     bulk_g2s(base + Lo::Qt, rec + RT::Qt, C * 128, ldbar);
-    bulk_g2s(base + Lo::Tt, rec + RT::Tt, C * 128, ldbar);
     bulk_g2s(base + Lo::Kf, rec + RT::Kf, 2 * C * 256, ldbar);  // Kf, Wf
     bulk_g2s(base + Lo::S0, hs, 32768, ldbar);
     bulk_g2s(base + Lo::dS, dhs, 32768, ldbar);
@@ -289,12 +288,12 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
     bulk_commit();
   }
 
-  // ---- C: dKr^T = dW^T Tt^T, dT += dW Kr^T
+  // ---- C: dKr^T = dW^T T (T read MN-major as the transposed operand), dT += dW Kr^T
   if (threadIdx.x == 0) {
     tc::fence_after();
-    constexpr uint32_t id_kr = tc::idesc(128, C, true, false);
+    constexpr uint32_t id_kr = tc::idesc(128, C, true, true);
     for (int ks = 0; ks < C / 16; ++ks)
-      tc::mma(tmem + TKR, tc::desc_mn(base + Lo::dW, C, ks), tc::desc_k(base + Lo::Tt, C, ks), id_kr, ks > 0);
+      tc::mma(tmem + TKR, tc::desc_mn(base + Lo::dW, C, ks), tc::desc_mn(base + Lo::T, C, ks), id_kr, ks > 0);
     constexpr uint32_t id_cc = tc::idesc(64, C, false, false);
     for (int ks = 0; ks < kKD / 16; ++ks)
       tc::mma(tmem + TDT, tc::desc_k(base + Lo::dW, C, ks), tc::desc_k(base + Lo::Kr, C, ks), id_cc, true);
@@ -376,15 +375,15 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
   const float last = cfl[key] + cgl[key] * ch.gL[key] / (ch.fr[key] * ch.fL[key]);
   float* part = reinterpret_cast<float*>(base + Lo::X);  // [4 quadrants][3][C] partial token sums
   // exact-path terms of 8 tokens per thread, [8][4][512] fp32 over the operand
-  // tiles Kr .. Tt (dead once the score MMAs are skipped)
+  // tiles Kr .. Xs (dead once the score MMAs are skipped)
   float* xs = reinterpret_cast<float*>(base + Lo::Kr);
-  static_assert(Lo::Tt + 8192 >= 8 * 4 * 512 * 4, "exact-path scratch");
+  static_assert(Lo::Xs + 8192 >= 8 * 4 * 512 * 4, "exact-path scratch");
   // the same 64 KB once the mapping is done (on the fast path already during
   // it): the dg, dk, dq rows [C][128], written lane = key and stored by TMA
   float* sdg = xs;
   bf16* sdk = reinterpret_cast<bf16*>(base + Lo::Kr + C * kKD * 4);
   bf16* sdq = sdk + C * kKD;
-  static_assert(Lo::Kr + C * kKD * 8 <= Lo::Tt + 8192, "output staging");
+  static_assert(Lo::Kr + C * kKD * 8 <= Lo::Xs + 8192, "output staging");
   float kh[16], qh[16];
 #pragma unroll
   for (int half = 0; half < 2; ++half) {

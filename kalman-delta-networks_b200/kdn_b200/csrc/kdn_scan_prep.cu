@@ -32,9 +32,9 @@ struct PrepLayout {
   static constexpr size_t As = Ab + A128((size_t)C * CF::LDC * sz);
   static constexpr size_t small = As + A128((size_t)C * CF::LDA * 4);
   static constexpr size_t base_bytes = small + A128(small_floats<CF>() * 4);
-  // bf16 record tiles T, Qq, Qt, Tt ([C][64] swizzled each), staged for the
+  // bf16 record tiles T, Qq, Qt ([C][64] swizzled each), staged for the
   // bulk stores over Xb .. As (dead after the solve) when they fit there
-  static constexpr size_t rec_tiles = 4 * (size_t)C * 128;
+  static constexpr size_t rec_tiles = 3 * (size_t)C * 128;
   static constexpr bool alias = small - Xb >= rec_tiles;
   static constexpr size_t St = alias ? Xb : base_bytes;
   static constexpr size_t bytes = alias ? base_bytes : base_bytes + rec_tiles;
@@ -138,15 +138,15 @@ __global__ void __launch_bounds__(kPrepThreads, 2) scan_prep_kernel(ScanParams p
           *reinterpret_cast<uint4*>(tiles[m] + tc::sw_off(r0 + 16 * j, 8 * g, C)) = v[m][j];
     }
     // T, Qq = scale Q: thread t owns columns 8(t%8)..+7 of rows t/8, t/8 + 32, ...
-    // (columns >= C zero); Qt = scale Q^T, Tt = T^T: warp w owns output columns
+    // (columns >= C zero); Qt = scale Q^T: warp w owns output columns
     // 8(w%8)..+7 and lane l output row l, l + 32, ..., so the column reads of
     // the source are consecutive along a row (no bank conflicts)
     {
 #pragma unroll 1
-      for (int m = 0; m < 4; ++m) {
-        char* dst = st + (size_t)m * C * 128;  // T, Qq, Qt, Tt: the record's order
-        const float mul = (m == 1 || m == 2) ? p.scale : 1.f;
-        const OpT* src = (m == 0 || m == 3) ? sTb : sQb;
+      for (int m = 0; m < 3; ++m) {
+        char* dst = st + (size_t)m * C * 128;  // T, Qq, Qt: the record's order
+        const float mul = m >= 1 ? p.scale : 1.f;
+        const OpT* src = m == 0 ? sTb : sQb;
         const bool tr = m >= 2;
         const int g = tr ? (warp & 7) : (threadIdx.x & 7);
         const int r0 = tr ? (threadIdx.x & 31) + 32 * (warp >> 3) : threadIdx.x >> 3;
@@ -170,10 +170,10 @@ __global__ void __launch_bounds__(kPrepThreads, 2) scan_prep_kernel(ScanParams p
     fence_async_shared();
     __syncthreads();
     if (threadIdx.x == 0) {
-      static_assert(RT::Qq == RT::T + (size_t)C * 128 && RT::Tt == RT::Qt + (size_t)C * 128, "record tile order");
+      static_assert(RT::Qq == RT::T + (size_t)C * 128, "record tile order");
       static_assert(RT::Kf == RT::Qs + (size_t)C * 256 && RT::Wf == RT::Kf + (size_t)C * 256, "record tile order");
       bulk_s2g(rec + RT::T, st, 2 * C * 128);
-      bulk_s2g(rec + RT::Qt, st + 2 * C * 128, 2 * C * 128);
+      bulk_s2g(rec + RT::Qt, st + 2 * C * 128, C * 128);
       bulk_s2g(rec + RT::Qs, base + Lo::Qr, C * 256);
       bulk_s2g(rec + RT::Kf, base + Lo::Kc, C * 256);
       bulk_s2g(rec + RT::Wf, base + Lo::Kr, C * 256);

@@ -50,11 +50,11 @@ def test_scan_size_queries(lib):
     a.B, a.T, a.H, a.K, a.V = 4, 4096, 18, 128, 128
     saved = lib.kdn_scan_saved_bytes(ctypes.byref(a))
     # status word + one chunk record per 64-chunk (128-byte swizzled bf16
-    # tiles: T, scale*Q, scale*Q^T, T^T [64][64]; Qs, Kf, Wf [2][64][64];
+    # tiles: T, scale*Q, scale*Q^T [64][64]; Qs, Kf, Wf [2][64][64];
     # three [128] fp32 gate factors in a 2 KiB slot) + the chunk-start states,
     # [128][64] bf16 per value tile of 64
     nt, bh = 4096 // 64, 72
-    record = 4 * 64 * 128 + 3 * 64 * 256 + 2048
+    record = 3 * 64 * 128 + 3 * 64 * 256 + 2048
     state = 2 * 128 * 64 * 2
     assert saved == 256 + bh * nt * record + bh * nt * state
     ws = lib.kdn_scan_workspace_bytes(ctypes.byref(a))
