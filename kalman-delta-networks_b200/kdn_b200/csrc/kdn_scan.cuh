@@ -48,7 +48,10 @@ struct Cfg {
   static constexpr int LDC = C + PAD;
   static constexpr int LDA = C + 4;  // fp32 C x C scratch
   static constexpr int CG = ISO ? 64 : 32;  // gate-prefix restart of the boundary convention
-  static_assert(C == CG, "internal chunk must equal the boundary gate chunk");
+  // the bf16 diagonal scan runs 64-token chunks over a 32-local gate prefix:
+  // the C ABI turns the prefix into a 64-local one first (and folds the gate
+  // cotangent back), see kdn_scan_api.cu
+  static_assert(C % CG == 0, "internal chunk must be a multiple of the boundary gate chunk");
 };
 
 struct ScanParams {

@@ -15,12 +15,12 @@ template <class CF> size_t chunk_bytes();
 
 using IsoB = Cfg<true, 64, bf16>;
 using IsoF = Cfg<true, 64, float>;
-using DiagB = Cfg<false, 32, bf16>;
+using DiagB = Cfg<false, 64, bf16>;
 using DiagF = Cfg<false, 32, float>;
 
 namespace {
 
-// saved     = [status word | chunk records | chunk-start states h]
+// saved     = [status word | chunk records | chunk-start states h | 64-local gate prefix (bf16 diag)]
 // workspace = [status word | chunk-end adjoints dh | fp32-precision scratch]
 constexpr size_t kHeader = 256;
 constexpr int kVT = kVD / kBV;
@@ -28,6 +28,7 @@ constexpr int kVT = kVD / kBV;
 struct Sizes {
   int64_t C, NT, BH;
   size_t rec, h, dh;
+  size_t g64;  // bf16 diagonal scan: the gate prefix restarted every 64 tokens
   size_t fwd_stride, bwd_stride;  // per-CTA scratch of the fp32 precision
   size_t dbg_fwd, dbg_bwd;
 };
@@ -45,7 +46,9 @@ bool sizes_of(const KdnScanArgs* a, Sizes* s) {
     return false;
   if (a->B <= 0 || a->T <= 0 || a->H <= 0 || a->K != kKD || a->V != kVD) return false;
   const bool iso = a->variant == KDN_ISO, f32 = a->precision == KDN_PREC_FP32;
-  s->C = iso ? 64 : 32;
+  // the bf16 kernels run 64-token chunks for both variants; the fp32 debug
+  // build of the diagonal scan keeps the boundary's 32-token chunks
+  s->C = (iso || !f32) ? 64 : 32;
   s->NT = (a->T + s->C - 1) / s->C;
   s->BH = a->B * a->H;
   if (iso) {
@@ -54,6 +57,7 @@ bool sizes_of(const KdnScanArgs* a, Sizes* s) {
     f32 ? layout_sizes<DiagF>(s) : layout_sizes<DiagB>(s);
   }
   s->fwd_stride = s->bwd_stride = s->dbg_fwd = s->dbg_bwd = 0;
+  s->g64 = (!iso && !f32) ? align_up((size_t)4 * a->B * a->T * a->H * a->K, 256) : 0;
   if (f32) {
     const size_t pr = iso ? prep_dbg_bytes<IsoF>() : prep_dbg_bytes<DiagF>();
     const size_t f = iso ? fwd_dbg_bytes<IsoF>() : fwd_dbg_bytes<DiagF>();
@@ -106,6 +110,55 @@ int fill_params(const KdnScanArgs* a, const Sizes& s, ScanParams* p) {
   return KDN_OK;
 }
 
+// The diagonal scan's boundary gate prefix g restarts every 32 tokens; the
+// bf16 kernels use 64-token chunks, whose prefix restarts every 64 tokens:
+// g64[t] = g[t] + (t mod 64 >= 32 ? g[31 of the block] : 0).  One float4 of
+// [B, T, H, K] per thread and step.
+__global__ void gate_to64_kernel(const float4* __restrict__ g, float4* __restrict__ g64, int64_t T, int64_t HK4,
+                                 int64_t n4) {
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n4; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = e / HK4, col = e - row * HK4, t = row % T, tb = t & 63;
+    float4 x = g[e];
+    if (tb >= 32) {
+      const float4 y = g[(row - tb + 31) * HK4 + col];
+      x.x += y.x;
+      x.y += y.y;
+      x.z += y.z;
+      x.w += y.w;
+    }
+    g64[e] = x;
+  }
+}
+
+// The cotangent of the 64-local prefix back to the boundary's 32-local one:
+// rows 32..63 of a 64-token block also depend on row 31, which collects their
+// cotangent.  One float4 column of one block per thread.
+__global__ void gate_fold_kernel(float4* __restrict__ dg, int64_t T, int64_t HK4, int64_t NB64, int64_t n) {
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t col = e % HK4, bb = e / HK4, b = bb / NB64, blk = bb - b * NB64;
+    const int64_t t31 = blk * 64 + 31, tend = t31 + 33 < T ? t31 + 33 : T;
+    if (t31 + 1 >= tend) continue;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int64_t t = t31 + 1; t < tend; ++t) {
+      const float4 y = dg[(b * T + t) * HK4 + col];
+      acc.x += y.x;
+      acc.y += y.y;
+      acc.z += y.z;
+      acc.w += y.w;
+    }
+    float4& z = dg[(b * T + t31) * HK4 + col];
+    z.x += acc.x;
+    z.y += acc.y;
+    z.z += acc.z;
+    z.w += acc.w;
+  }
+}
+
+unsigned grid_for(int64_t n) {
+  const int64_t blocks = (n + 255) / 256;
+  return (unsigned)(blocks < 148 * 16 ? (blocks > 0 ? blocks : 1) : 148 * 16);
+}
+
 }  // namespace
 }  // namespace kdn
 
@@ -116,7 +169,7 @@ extern "C" {
 size_t kdn_scan_saved_bytes(const KdnScanArgs* a) {
   Sizes s;
   if (!sizes_of(a, &s)) return 0;
-  return kHeader + s.rec + s.h;
+  return kHeader + s.rec + s.h + s.g64;
 }
 
 size_t kdn_scan_workspace_bytes(const KdnScanArgs* a) {
@@ -144,7 +197,16 @@ int kdn_scan_fwd(const KdnScanArgs* a, kdn_stream_t stream) {
   p.dbg_stride = s.fwd_stride;
   const bool iso = a->variant == KDN_ISO;
   if (a->precision == KDN_PREC_FP32) return iso ? launch_fwd<IsoF>(p, st) : launch_fwd<DiagF>(p, st);
-  return iso ? launch_fwd<IsoB>(p, st) : launch_fwd<DiagB>(p, st);
+  if (iso) return launch_fwd<IsoB>(p, st);
+  // 32-local gate prefix -> 64-local, kept in `saved` for the backward
+  float* g64 = reinterpret_cast<float*>(static_cast<char*>(a->saved) + kHeader + s.rec + s.h);
+  const int64_t HK4 = a->H * a->K / 4, n4 = a->B * a->T * HK4;
+  gate_to64_kernel<<<grid_for(n4), 256, 0, st>>>(reinterpret_cast<const float4*>(a->g), reinterpret_cast<float4*>(g64),
+                                                 a->T, HK4, n4);
+  rc = check_launch("gate_to64_kernel");
+  if (rc != KDN_OK) return rc;
+  p.g = g64;
+  return launch_fwd<DiagB>(p, st);
 }
 
 int kdn_scan_bwd(const KdnScanArgs* a, kdn_stream_t stream) {
@@ -168,7 +230,14 @@ int kdn_scan_bwd(const KdnScanArgs* a, kdn_stream_t stream) {
   const cudaStream_t st = (cudaStream_t)stream;
   if (cudaMemsetAsync(p.status, 0, sizeof(int), st) != cudaSuccess) return check_launch("kdn_scan_bwd: status reset");
   if (a->precision == KDN_PREC_FP32) return iso ? launch_bwd<IsoF>(p, st) : launch_bwd<DiagF>(p, st);
-  return iso ? launch_bwd<IsoB>(p, st) : launch_bwd<DiagB>(p, st);
+  if (iso) return launch_bwd<IsoB>(p, st);
+  p.g = reinterpret_cast<const float*>(static_cast<const char*>(a->saved) + kHeader + s.rec + s.h);
+  rc = launch_bwd<DiagB>(p, st);
+  if (rc != KDN_OK) return rc;
+  // cotangent of the 64-local prefix -> the boundary's 32-local one
+  const int64_t HK4 = a->H * a->K / 4, NB64 = (a->T + 63) / 64, n = a->B * NB64 * HK4;
+  gate_fold_kernel<<<grid_for(n), 256, 0, st>>>(reinterpret_cast<float4*>(a->dg), a->T, HK4, NB64, n);
+  return check_launch("gate_fold_kernel");
 }
 
 }  // extern "C"

@@ -233,7 +233,7 @@ __global__ void __launch_bounds__(kSeqThreads + 32, 1) scan_bwd_state_kernel(Sca
 template <class CF>
 struct StateTcLayout {
   static constexpr int C = CF::C;
-  static constexpr int NS = CF::ISO ? 2 : 3;
+  static constexpr int NS = CF::C == 64 ? 2 : 3;
   static constexpr bool DF32 = !CF::ISO;  // the diagonal variant's cotangent arrives as fp32 rows
   using R = RecTc<CF>;
   static constexpr size_t rec = R::bytes - R::bwd_begin;  // the record from Qs on
@@ -945,7 +945,7 @@ int launch_bwd_state(const ScanParams& p, cudaStream_t st) {
 // The chunk-parallel gradients of chunks [p.c_lo, p.c_hi).
 template <class CF>
 int launch_bwd_chunk(const ScanParams& p, cudaStream_t st) {
-  if constexpr (CF::ISO && !CF::F32) {
+  if constexpr (!CF::F32) {
     return launch_bwd_chunk_tc<CF>(p, st);
   } else {
     const size_t s2 = CF::F32 ? 0 : ChunkLayout<CF>::bytes;
@@ -970,15 +970,15 @@ int launch_bwd(const ScanParams& p, cudaStream_t st) {
 
 template int launch_bwd<Cfg<true, 64, bf16>>(const ScanParams&, cudaStream_t);
 template int launch_bwd<Cfg<true, 64, float>>(const ScanParams&, cudaStream_t);
-template int launch_bwd<Cfg<false, 32, bf16>>(const ScanParams&, cudaStream_t);
+template int launch_bwd<Cfg<false, 64, bf16>>(const ScanParams&, cudaStream_t);
 template int launch_bwd<Cfg<false, 32, float>>(const ScanParams&, cudaStream_t);
 template size_t state_bytes<Cfg<true, 64, float>>();
 template size_t state_bytes<Cfg<false, 32, float>>();
 template size_t chunk_bytes<Cfg<true, 64, float>>();
 template size_t chunk_bytes<Cfg<false, 32, float>>();
 template size_t state_bytes<Cfg<true, 64, bf16>>();
-template size_t state_bytes<Cfg<false, 32, bf16>>();
+template size_t state_bytes<Cfg<false, 64, bf16>>();
 template size_t chunk_bytes<Cfg<true, 64, bf16>>();
-template size_t chunk_bytes<Cfg<false, 32, bf16>>();
+template size_t chunk_bytes<Cfg<false, 64, bf16>>();
 
 }  // namespace kdn

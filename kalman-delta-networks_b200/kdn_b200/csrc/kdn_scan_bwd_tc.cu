@@ -1,5 +1,6 @@
-// Chunk-parallel gradients of the isotropic scan on tcgen05 tensor cores
-// (bf16 precision).  One CTA (16 warps) per (chunk, b*h).  All operands are
+// Chunk-parallel gradients of the memory scan on tcgen05 tensor cores (bf16
+// precision, 64-token chunks, both variants).  One CTA (16 warps) per
+// (chunk, b*h).  All operands are
 // 128-byte-swizzled bf16 tiles in shared memory (kdn_tc.cuh): the chunk
 // record blocks and the saved states arrive by bulk copies, v and dO by TMA,
 // the gated operands Kr, Qr, Kc are built from the raw rows in HBM.  Thread 0
@@ -15,7 +16,12 @@
 // kept transposed (lane = key), so the final gate mapping has one key per
 // lane and every store of a token row is contiguous.  Same mathematics as
 // scan_bwd_chunk_kernel (kdn_scan_bwd.cu); replaces _chunk_kda_bwd_precum
-// (lit_gpt/kdn_ops/iso_kdn_chunk.py:2089-2187) on the fixed-length path.
+// (lit_gpt/kdn_ops/iso_kdn_chunk.py:2089-2187) and the backward of
+// _DiagKdnMemoryFunction (diag_kdn_chunk.py:3258-3312).  The diagonal
+// variant differs in the gate mapping only (kappa is an input, q and k are
+// used as given, dkappa is an output, no token sums) and takes its fp32
+// cotangent through the threads, rounded to bf16 as the reference does
+// (diag_kdn_chunk.py:3277).
 #include "kdn_scan.cuh"
 #include "kdn_tc.cuh"
 #include "kdn_tma.cuh"
@@ -30,7 +36,7 @@ struct alignas(64) ChunkMaps {
 
 template <class CF>
 struct ChunkTcLayout {
-  static_assert(CF::ISO && CF::C == 64 && !CF::F32, "isotropic bf16 chunks of 64");
+  static_assert(CF::C == 64 && !CF::F32, "bf16 chunks of 64");
   static constexpr int C = 64;
   // whole kernel
   static constexpr size_t Kr = 0, Qr = 16384, Kc = 32768, T = 49152, Xs = 57344;  // Xs: 8 KB scratch
@@ -50,7 +56,8 @@ struct ChunkTcLayout {
   static constexpr size_t small = A + 65536;
   static constexpr size_t bar = small + align_up((small_floats<CF>() + 2 * kKD + 3 * C) * 4, 128);
   static constexpr size_t bytes = bar + 64 + 1024;
-  static constexpr unsigned load_bytes = 2 * C * 128 + 2 * C * 256 + 2 * 32768 + 2 * C * 256;
+  // T, Qt | Kf, Wf | S0, dS | v (and dO: the isotropic cotangent arrives by TMA)
+  static constexpr unsigned load_bytes = 2 * C * 128 + 2 * C * 256 + 2 * 32768 + (CF::ISO ? 2 : 1) * C * 256;
 };
 
 // Exact-path score terms of one (token r, key) element: the sum over the
@@ -59,7 +66,9 @@ struct ChunkTcLayout {
 struct ExactTerms {
   float dkh, dqh, dkap, dG;
 };
-__device__ __noinline__ ExactTerms exact_terms(const float* g, const bf16* k, const bf16* qv, const float* beta,
+// gk: beta rows (isotropic, kappa = beta k_hat) or kappa rows (diagonal)
+template <bool ISO>
+__device__ __noinline__ ExactTerms exact_terms(const float* g, const bf16* k, const bf16* qv, const float* gk,
                                               const float* rk, const float* rq, int ldr, int ldb, const char* sdA,
                                               const char* sdQ, int r, int key, int L, float gi, float k1, float q1,
                                               float kap) {
@@ -67,8 +76,8 @@ __device__ __noinline__ ExactTerms exact_terms(const float* g, const bf16* k, co
   for (int j = 0; j < L; ++j) {
     const size_t oj = (size_t)j * ldr + key;
     const float gj = g[oj];
-    const float khj = rk[j] * __bfloat162float(k[oj]), qhj = rq[j] * __bfloat162float(qv[oj]);
-    const float kapj = beta[(size_t)j * ldb] * khj;
+    const float khj = (ISO ? rk[j] : 1.f) * __bfloat162float(k[oj]), qhj = (ISO ? rq[j] : 1.f) * __bfloat162float(qv[oj]);
+    const float kapj = ISO ? gk[(size_t)j * ldb] * khj : gk[oj];
     if (j <= r) {
       const float f = exp2f(gi - gj);
       const float dAij = j < r ? __bfloat162float(*reinterpret_cast<const bf16*>(sdA + tc::sw_off(r, j, 64))) : 0.f;
@@ -155,8 +164,21 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
     bulk_g2s(base + Lo::dS, dhs, 32768, ldbar);
     tma_load_4d(base + Lo::vv, &maps.v, 0, h, t0, b, ldbar);
     tma_load_4d(base + Lo::vv + C * 128, &maps.v, 64, h, t0, b, ldbar);
-    tma_load_4d(base + Lo::dO, &maps.dO, 0, h, t0, b, ldbar);
-    tma_load_4d(base + Lo::dO + C * 128, &maps.dO, 64, h, t0, b, ldbar);
+    if constexpr (CF::ISO) {
+      tma_load_4d(base + Lo::dO, &maps.dO, 0, h, t0, b, ldbar);
+      tma_load_4d(base + Lo::dO + C * 128, &maps.dO, 64, h, t0, b, ldbar);
+    }
+  }
+  if constexpr (!CF::ISO) {
+    // the fp32 cotangent rounded to bf16 into the swizzled operand tile (rows
+    // past the chunk's end zero)
+    const float* dO = static_cast<const float*>(p.dO) + tok_row(p, b, h, t0) * kVD;
+    for (int e = threadIdx.x; e < C * 16; e += 512) {
+      const int r = e >> 4, c8 = 8 * (e & 15);
+      float x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (r < L) ld8(x, dO + (size_t)r * p.H * kVD + c8);
+      *reinterpret_cast<uint4*>(base + Lo::dO + tc::sw_off(r, c8, C)) = pack8(x);
+    }
   }
   mbar_wait(ldbar, 0, p.status);
   fence_async_shared();
@@ -394,22 +416,29 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
         const int r = tok < L ? tok : L - 1;
         const size_t off = (size_t)r * ch.ldr + key;
         const float gi = ch.g[off];
-        const float k1 = ch.rk[r] * to_f(ch.k[off]), q1 = ch.rq[r] * to_f(ch.q[off]);
-        const float kap = ch.beta[(size_t)r * ch.ldb] * k1;
-        const ExactTerms t = exact_terms(ch.g, ch.k, ch.q, ch.beta, ch.rk, ch.rq, ch.ldr, ch.ldb, base + Lo::dA,
-                                         base + Lo::dQ, r, key, L, gi, k1, q1, kap);
+        ExactTerms t;
+        if constexpr (CF::ISO) {
+          const float k1 = ch.rk[r] * to_f(ch.k[off]), q1 = ch.rq[r] * to_f(ch.q[off]);
+          const float kap = ch.beta[(size_t)r * ch.ldb] * k1;
+          t = exact_terms<true>(ch.g, ch.k, ch.q, ch.beta, ch.rk, ch.rq, ch.ldr, ch.ldb, base + Lo::dA, base + Lo::dQ,
+                                r, key, L, gi, k1, q1, kap);
+        } else {
+          t = exact_terms<false>(ch.g, ch.k, ch.q, ch.kap, nullptr, nullptr, ch.ldr, ch.ldb, base + Lo::dA,
+                                 base + Lo::dQ, r, key, L, gi, to_f(ch.k[off]), to_f(ch.q[off]), ch.kap[off]);
+        }
         xs[(i * 4 + 0) * 512 + threadIdx.x] = t.dkh;
         xs[(i * 4 + 1) * 512 + threadIdx.x] = t.dqh;
         xs[(i * 4 + 2) * 512 + threadIdx.x] = t.dkap;
         xs[(i * 4 + 3) * 512 + threadIdx.x] = t.dG;
       }
     }
-    // raw rows of 8 tokens (shared memory), then the arithmetic
-    float gv[8], kv[8], qv[8];
+    // raw rows of 8 tokens (shared memory; kappa from global), then the arithmetic
+    float gv[8], kv[8], qv[8], kapv[CF::ISO ? 1 : 8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int tok = 16 * cg + 8 * half + i;
       const int r = tok < L ? tok : L - 1;
+      if constexpr (!CF::ISO) kapv[i] = ch.kap[(size_t)r * ch.ldr + key];
       gv[i] = reinterpret_cast<const float*>(base + Lo::rg)[r * kKD + key];
       kv[i] = to_f(bf(Lo::rk)[r * kKD + key]);
       qv[i] = to_f(bf(Lo::rq)[r * kKD + key]);
@@ -420,8 +449,18 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
       const int ii = 8 * half + i;
       const int tok = 16 * cg + ii;
       const int r = tok < L ? tok : L - 1;
-      const float rk = ch.rk[r], rq = ch.rq[r], be = ch.rb[r];
-      const float gi = gv[i], k1 = rk * kv[i], q1 = rq * qv[i], kap = be * k1;
+      float k1, q1, kap, be = 0.f;
+      if constexpr (CF::ISO) {
+        be = ch.rb[r];
+        k1 = ch.rk[r] * kv[i];
+        q1 = ch.rq[r] * qv[i];
+        kap = be * k1;
+      } else {
+        k1 = kv[i];
+        q1 = qv[i];
+        kap = kapv[i];
+      }
+      const float gi = gv[i];
       const float er = ex2a(gi - rr), ec = ex2a(rc - gi);
       const float dKr = xk[ii], dQr = p.scale * xq[ii], dKc = xc[ii];
       float dkh = dKr * er, dqh = dQr * er, dkap = dKc * ec;
@@ -434,10 +473,15 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
         dG += xs[(i * 4 + 3) * 512 + threadIdx.x];
       }
       dgv[i] = dG;
-      db[i] = dkap * k1;          // dbeta = <dkappa, k_hat>
-      dkh = fmaf(be, dkap, dkh);  // kappa = beta k_hat
-      dkd[i] = dkh * k1;
-      dqd[i] = dqh * q1;
+      if constexpr (CF::ISO) {
+        db[i] = dkap * k1;          // dbeta = <dkappa, k_hat>
+        dkh = fmaf(be, dkap, dkh);  // kappa = beta k_hat
+        dkd[i] = dkh * k1;
+        dqd[i] = dqh * q1;
+      } else {
+        db[i] = dkap;  // dkappa itself
+        dkd[i] = dqd[i] = 0.f;
+      }
       xk[ii] = dkh;
       xq[ii] = dqh;
       kh[ii] = k1;
@@ -453,9 +497,9 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
         if (tok < L) p.dg[tok_row(p, b, h, t0 + tok) * kKD + key] = dgv[i];
       }
     }
-    // token sums over this warp's 32 keys: one transpose-reduce leaves the sum
-    // of value j in lane j (j = 8 * quantity + token)
-    {
+    if constexpr (CF::ISO) {
+      // token sums over this warp's 32 keys: one transpose-reduce leaves the sum
+      // of value j in lane j (j = 8 * quantity + token)
       float v32[32];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
@@ -475,18 +519,25 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
         }
       }
       if (lane < 24) part[(q * 3 + (lane >> 3)) * C + 16 * cg + 8 * half + (lane & 7)] = v32[0];
+    } else {
+      // dkappa rows straight to HBM (128 bytes per warp and token)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int tok = 16 * cg + 8 * half + i;
+        if (tok < L) p.dkappa[tok_row(p, b, h, t0 + tok) * kKD + key] = db[i];
+      }
     }
   }
   __syncthreads();
-  if (threadIdx.x < 3 * C) {
-    const int sidx = threadIdx.x / C, tok = threadIdx.x % C;
-    float t = 0.f;
+  if constexpr (CF::ISO) {
+    if (threadIdx.x < 3 * C) {
+      const int sidx = threadIdx.x / C, tok = threadIdx.x % C;
+      float t = 0.f;
 #pragma unroll
-    for (int qq = 0; qq < 4; ++qq) t += part[(qq * 3 + sidx) * C + tok];
-    tsum[threadIdx.x] = t;
-  }
-  __syncthreads();
-  {
+      for (int qq = 0; qq < 4; ++qq) t += part[(qq * 3 + sidx) * C + tok];
+      tsum[threadIdx.x] = t;
+    }
+    __syncthreads();
     float rkv[16], rqv[16], dkdot[16], dqdot[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
@@ -502,8 +553,15 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
       sdk[tok * kKD + key] = __float2bfloat16_rn(rkv[i] * (xk[i] - kh[i] * dkdot[i]));
       sdq[tok * kKD + key] = __float2bfloat16_rn(rqv[i] * (xq[i] - qh[i] * dqdot[i]));
     }
+    if (threadIdx.x < L) p.dbeta[tok_row(p, b, h, t0 + threadIdx.x)] = tsum[threadIdx.x];
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int tok = 16 * cg + i;
+      sdk[tok * kKD + key] = __float2bfloat16_rn(xk[i]);
+      sdq[tok * kKD + key] = __float2bfloat16_rn(xq[i]);
+    }
   }
-  if (threadIdx.x < L) p.dbeta[tok_row(p, b, h, t0 + threadIdx.x)] = tsum[threadIdx.x];
   // the staged rows leave by TMA stores (rows past the sequence's end are clipped)
   fence_async_shared();
   __syncthreads();
@@ -536,7 +594,7 @@ int launch_bwd_chunk_tc(const ScanParams& p, cudaStream_t st) {
   }
   ChunkMaps maps;
   int rc = encode_bthd(&maps.v, p.v, true, p.B, p.T, p.H, kVD, 64, CF::C, true);
-  if (rc == KDN_OK) rc = encode_bthd(&maps.dO, p.dO, true, p.B, p.T, p.H, kVD, 64, CF::C, true);
+  if (rc == KDN_OK && CF::ISO) rc = encode_bthd(&maps.dO, p.dO, true, p.B, p.T, p.H, kVD, 64, CF::C, true);
   if (rc == KDN_OK) rc = encode_bthd(&maps.dv, p.dv, true, p.B, p.T, p.H, kVD, kVD, CF::C, false);
   if (rc == KDN_OK) rc = encode_bthd(&maps.g, p.g, false, p.B, p.T, p.H, kKD, kKD, CF::C, false);
   if (rc == KDN_OK) rc = encode_bthd(&maps.k, p.k, true, p.B, p.T, p.H, kKD, kKD, CF::C, false);
@@ -550,5 +608,6 @@ int launch_bwd_chunk_tc(const ScanParams& p, cudaStream_t st) {
 }
 
 template int launch_bwd_chunk_tc<Cfg<true, 64, bf16>>(const ScanParams&, cudaStream_t);
+template int launch_bwd_chunk_tc<Cfg<false, 64, bf16>>(const ScanParams&, cudaStream_t);
 
 }  // namespace kdn

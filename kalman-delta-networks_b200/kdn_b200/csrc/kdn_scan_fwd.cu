@@ -215,7 +215,7 @@ __global__ void __launch_bounds__(kSeqThreads + 32, 1) scan_fwd_kernel(ScanParam
 template <class CF>
 struct FwdTcLayout {
   static constexpr int C = CF::C;
-  static constexpr int NS = CF::ISO ? 2 : 3;
+  static constexpr int NS = CF::C == 64 ? 2 : 3;
   using R = RecTc<CF>;
   static constexpr size_t v = R::fwd_end;  // [C][64] bf16, swizzled by the TMA engine
   static constexpr size_t stage = align_up(v + (size_t)C * 128, 1024);
@@ -448,7 +448,7 @@ int launch_fwd(const ScanParams& p, cudaStream_t st) {
 
 template int launch_fwd<Cfg<true, 64, bf16>>(const ScanParams&, cudaStream_t);
 template int launch_fwd<Cfg<true, 64, float>>(const ScanParams&, cudaStream_t);
-template int launch_fwd<Cfg<false, 32, bf16>>(const ScanParams&, cudaStream_t);
+template int launch_fwd<Cfg<false, 64, bf16>>(const ScanParams&, cudaStream_t);
 template int launch_fwd<Cfg<false, 32, float>>(const ScanParams&, cudaStream_t);
 template size_t fwd_dbg_bytes<Cfg<true, 64, float>>();
 template size_t fwd_dbg_bytes<Cfg<false, 32, float>>();

@@ -205,7 +205,7 @@ int launch_prep(const ScanParams& p, cudaStream_t st) {
 
 template int launch_prep<Cfg<true, 64, bf16>>(const ScanParams&, cudaStream_t);
 template int launch_prep<Cfg<true, 64, float>>(const ScanParams&, cudaStream_t);
-template int launch_prep<Cfg<false, 32, bf16>>(const ScanParams&, cudaStream_t);
+template int launch_prep<Cfg<false, 64, bf16>>(const ScanParams&, cudaStream_t);
 template int launch_prep<Cfg<false, 32, float>>(const ScanParams&, cudaStream_t);
 template size_t prep_dbg_bytes<Cfg<true, 64, float>>();
 template size_t prep_dbg_bytes<Cfg<false, 32, float>>();
