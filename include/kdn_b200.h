@@ -149,7 +149,10 @@ int kdn_diag_gain_bwd(const float* k, const float* alpha, const float* omega,
  *
  * Saved state (caller-owned, sizes from kdn_scan_saved_bytes): the forward
  * writes the chunk-start memory states and the per-chunk triangular solve and
- * query-key scores; the backward reads them.  Optional continuation buffers
+ * query-key scores; the backward reads them.  The first 4 bytes of `saved`
+ * (after kdn_scan_fwd) and of `workspace` (after kdn_scan_bwd) hold a status
+ * word, zeroed by the call: nonzero when a bounded wait inside the kernels
+ * gave up, in which case that call's results are invalid.  Optional continuation buffers
  * (fp32 [B,H,K,V], nullable): initial_state / final_state in the forward,
  * d_final_state / d_initial_state in the backward (sequence parallelism).
  * ------------------------------------------------------------------------ */

@@ -4,6 +4,7 @@ diagonal operator modules and by the sequence-parallel driver."""
 from __future__ import annotations
 
 import ctypes
+import os
 from dataclasses import dataclass
 
 import torch
@@ -11,6 +12,17 @@ import torch
 from . import _native as N
 
 KD = 128
+
+
+def check_status(buf: torch.Tensor, what: str) -> None:
+    """With ``KDN_B200_CHECK_STATUS=1``, synchronise and read the status word
+    at the head of ``saved`` (forward) or the workspace (backward): the
+    kernels' bounded waits set it when they gave up, and the results of that
+    call are then invalid.  Off by default (it costs a device round trip)."""
+    if os.environ.get("KDN_B200_CHECK_STATUS", "0") != "1":
+        return
+    if int(buf[:4].view(torch.int32).item()) != 0:
+        raise RuntimeError(f"{what}: a bounded wait in the kernels gave up (status word set); results are invalid")
 
 
 @dataclass
@@ -58,6 +70,7 @@ def scan_forward(variant, q, k, v, g, gate, scale, initial_state=None, want_fina
     a.workspace = N.ptr(ws)
     a.workspace_bytes = ws.numel() if ws is not None else 0
     N.check(lib.kdn_scan_fwd(ctypes.byref(a), N.stream_of(q)), "kdn_scan_fwd")
+    check_status(saved, "kdn_scan_fwd")
     return o, final, ScanSaved(saved, prec)
 
 
@@ -92,4 +105,5 @@ def scan_backward(variant, q, k, v, g, gate, scale, saved: ScanSaved, dO, d_fina
     a.workspace = ws.data_ptr()
     a.workspace_bytes = ws.numel()
     N.check(lib.kdn_scan_bwd(ctypes.byref(a), N.stream_of(q)), "kdn_scan_bwd")
+    check_status(ws, "kdn_scan_bwd")
     return dq, dk, dv, dg, dgate, dS0

@@ -5,7 +5,7 @@
 // record blocks and the saved states arrive by bulk copies, v and dO by TMA,
 // the gated operands Kr, Qr, Kc are built from the raw rows in HBM.  Thread 0
 // issues six groups of MMAs into tensor memory (512 columns):
-//   A  delta^T  = v^T T^T - S0^T Wf^T,  ddelta^T = dO^T Qq + dS^T Kf^T
+//   A  delta^T  = v^T T^T - S0^T Wf^T,  ddelta^T = dO^T Qq + dS''^T Kc^T
 //   B  dv = T^T ddelta,  (S0' dO^T, S0' ddelta^T, dS'' delta^T)  [K x C],
 //      dO delta^T, ddelta v^T  [C x C]
 //   C  dKr^T = dW^T ... (T^T dW)^T,  dT += dW Kr^T
@@ -40,10 +40,11 @@ struct ChunkTcLayout {
   static constexpr int C = 64;
   // whole kernel
   static constexpr size_t Kr = 0, Qr = 16384, Kc = 32768, T = 49152, Xs = 57344;  // Xs: 8 KB scratch
-  // Qt | Kf Wf (record), then delta | ddelta
+  // the record tiles Qt, Wf and the delta tiles
   static constexpr size_t G = 65536;
-  static constexpr size_t Qt = G, Kf = G + 8192, Wf = G + 8192 + 16384;
-  static constexpr size_t Del = G, DDel = G + 16384;
+  // Qt | delta | Wf, then ddelta over Wf once the delta products are done
+  static constexpr size_t Qt = G, Wf = G + 8192 + 16384;
+  static constexpr size_t Del = G + 8192, DDel = Wf;
   // v | dO, then the dv rows, then the raw k | q rows of the gate mapping
   static constexpr size_t V = G + 40960;
   static constexpr size_t vv = V, dO = V + 16384, dvst = V, rk = V, rq = V + 16384;
@@ -56,8 +57,8 @@ struct ChunkTcLayout {
   static constexpr size_t small = A + 65536;
   static constexpr size_t bar = small + align_up((small_floats<CF>() + 2 * kKD + 3 * C) * 4, 128);
   static constexpr size_t bytes = bar + 64 + 1024;
-  // T, Qt | Kf, Wf | S0, dS | v (and dO: the isotropic cotangent arrives by TMA)
-  static constexpr unsigned load_bytes = 2 * C * 128 + 2 * C * 256 + 2 * 32768 + (CF::ISO ? 2 : 1) * C * 256;
+  // T, Qt | Wf | S0, dS | v (and dO: the isotropic cotangent arrives by TMA)
+  static constexpr unsigned load_bytes = 2 * C * 128 + C * 256 + 2 * 32768 + (CF::ISO ? 2 : 1) * C * 256;
 };
 
 // Exact-path score terms of one (token r, key) element: the sum over the
@@ -118,7 +119,10 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
   uint64_t* ldbar = reinterpret_cast<uint64_t*>(base + Lo::bar);
   uint64_t* mmab = ldbar + 1;
   uint64_t* rawbar = ldbar + 2;  // the raw rows of the gate mapping
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(ldbar + 3);
+  // the ddelta products: their own barrier, since both phase-A commits can land
+  // before the first wait (one barrier would then have moved two phases on)
+  uint64_t* ddbar = ldbar + 3;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(ldbar + 4);
   float* small = reinterpret_cast<float*>(base + Lo::small);
   float* cfl = small + small_floats<CF>();
   float* cgl = cfl + kKD;
@@ -138,6 +142,7 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
     mbar_init(ldbar, 1);
     mbar_init(mmab, 1);
     mbar_init(rawbar, 1);
+    mbar_init(ddbar, 1);
     fence_mbar_init();
   }
   if (warp == 0) tc::alloc(tslot, 512);
@@ -159,7 +164,7 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
     mbar_expect_tx(ldbar, Lo::load_bytes);
     bulk_g2s(base + Lo::T, rec + RT::T, C * 128, ldbar);
     bulk_g2s(base + Lo::Qt, rec + RT::Qt, C * 128, ldbar);
-    bulk_g2s(base + Lo::Kf, rec + RT::Kf, 2 * C * 256, ldbar);  // Kf, Wf
+    bulk_g2s(base + Lo::Wf, rec + RT::Wf, C * 256, ldbar);
     bulk_g2s(base + Lo::S0, hs, 32768, ldbar);
     bulk_g2s(base + Lo::dS, dhs, 32768, ldbar);
     tma_load_4d(base + Lo::vv, &maps.v, 0, h, t0, b, ldbar);
@@ -197,53 +202,74 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
     __syncthreads();
   };
 
-  // ---- A: delta^T, ddelta^T (lane = value channel)
+  // ---- A: delta^T, then ddelta^T (lane = value channel).  The delta products
+  // run while the threads scale dS in place (dS'' = fL dS, so Kc replaces
+  // the record's Kf = fL Kc); the ddelta products run while they read delta
+  // out and scale S0 in place (S0' = fr S0, no longer read by then).
   if (threadIdx.x == 0) {
     tc::fence_after();
     constexpr uint32_t id = tc::idesc(128, C, true, false), idn = tc::idesc(128, C, true, false, true);
-    // the two accumulators alternate so consecutive MMAs are independent
-    for (int ks = 0; ks < C / 16; ++ks) {
+    for (int ks = 0; ks < C / 16; ++ks)
       tc::mma(tmem + TDEL, tc::desc_mn(base + Lo::vv, C, ks), tc::desc_k(base + Lo::T, C, ks), id, ks > 0);
-      tc::mma(tmem + TDD, tc::desc_mn(base + Lo::dO, C, ks), tc::desc_k(base + Lo::Qt, C, ks), id, ks > 0);
-    }
-    for (int ks = 0; ks < kKD / 16; ++ks) {
+    for (int ks = 0; ks < kKD / 16; ++ks)
       tc::mma(tmem + TDEL, tc::desc_mn(base + Lo::S0, kKD, ks), tc::desc_k(base + Lo::Wf, C, ks), idn, true);
-      tc::mma(tmem + TDD, tc::desc_mn(base + Lo::dS, kKD, ks), tc::desc_k(base + Lo::Kf, C, ks), id, true);
-    }
     tc::commit(mmab);
   }
-  mma_wait();
+  for (int e = threadIdx.x; e < kKD * 16; e += 512) {
+    const int r = e >> 4, g = e & 15;
+    bf16* ds = at(Lo::dS, r, 8 * g, kKD);
+    float d[8];
+    ld8(d, ds);
+    const float fl = ch.fL[r];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) d[i] *= fl;
+    st8(ds, d);
+  }
+  publish();
+  if (threadIdx.x == 0) {
+    tc::fence_after();
+    constexpr uint32_t id = tc::idesc(128, C, true, false);
+    for (int ks = 0; ks < C / 16; ++ks)
+      tc::mma(tmem + TDD, tc::desc_mn(base + Lo::dO, C, ks), tc::desc_k(base + Lo::Qt, C, ks), id, ks > 0);
+    for (int ks = 0; ks < kKD / 16; ++ks)
+      tc::mma(tmem + TDD, tc::desc_mn(base + Lo::dS, kKD, ks), tc::desc_k(base + Lo::Kc, C, ks), id, true);
+    tc::commit(ddbar);
+  }
+  mma_wait();  // delta^T done: S0 and Wf are free
   {
     const int v = 32 * q + lane;
     float x[16];
     tc::ld16(tq + TDEL + 16 * cg, x);
 #pragma unroll
     for (int i = 0; i < 16; ++i) *at(Lo::Del, 16 * cg + i, v, C) = __float2bfloat16_rn(x[i]);
-    tc::ld16(tq + TDD + 16 * cg, x);
-#pragma unroll
-    for (int i = 0; i < 16; ++i) *at(Lo::DDel, 16 * cg + i, v, C) = __float2bfloat16_rn(x[i]);
   }
-  // S0' = fr S0, dS'' = fL dS in place, cgl = sum_v S0' dS''  (a half-warp per key row)
+  // S0' = fr S0 in place, cgl = sum_v S0' dS''  (a half-warp per key row)
   for (int e = threadIdx.x; e < kKD * 16; e += 512) {
     const int r = e >> 4, g = e & 15;
     bf16* s0 = at(Lo::S0, r, 8 * g, kKD);
-    bf16* ds = at(Lo::dS, r, 8 * g, kKD);
     float a[8], d[8];
     ld8(a, s0);
-    ld8(d, ds);
-    const float fr = ch.fr[r], fl = ch.fL[r];
+    ld8(d, at(Lo::dS, r, 8 * g, kKD));
+    const float fr = ch.fr[r];
     float acc = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       a[i] *= fr;
-      d[i] *= fl;
       acc = fmaf(a[i], d[i], acc);
     }
     st8(s0, a);
-    st8(ds, d);
 #pragma unroll
     for (int o = 1; o < 16; o <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
     if (g == 0) cgl[r] = acc;
+  }
+  mbar_wait(ddbar, 0, p.status);  // ddelta^T done
+  tc::fence_after();
+  {
+    const int v = 32 * q + lane;
+    float x[16];
+    tc::ld16(tq + TDD + 16 * cg, x);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) *at(Lo::DDel, 16 * cg + i, v, C) = __float2bfloat16_rn(x[i]);
   }
   publish();
 

@@ -4,6 +4,8 @@ import sys
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+# every scan call in the tests checks the kernels' status word (bounded waits)
+os.environ.setdefault("KDN_B200_CHECK_STATUS", "1")
 PKG_ROOT = os.path.join(ROOT, "kalman-delta-networks_b200")
 for path in (ROOT, PKG_ROOT):
     if path not in sys.path:
