@@ -100,6 +100,11 @@ __device__ Aff block_exclusive_suffix_aff(Aff x) {
 // ---------------------------------------------------------------------------
 // Isotropic gain
 // ---------------------------------------------------------------------------
+// A thread's tokens are read TL at a time, all loads of a tile issued before
+// its arithmetic: the reads are strided by H (one float per token and head),
+// so each costs a full memory round trip, which the tile shares.
+constexpr int kIsoTile = 16;
+
 __global__ void __launch_bounds__(kIsoThreads) iso_gain_fwd_kernel(const float* __restrict__ a,
                                                                    const float* __restrict__ omega,
                                                                    const float* __restrict__ r,
@@ -111,23 +116,44 @@ __global__ void __launch_bounds__(kIsoThreads) iso_gain_fwd_kernel(const float* 
   const int seg = (T + blockDim.x - 1) / blockDim.x;
   const int t0 = min(threadIdx.x * seg, T), t1 = min(t0 + seg, T);
   const size_t base = (size_t)b * T * H + h;
+  constexpr int TL = kIsoTile;
   Mob m{1.f, 0.f, 0.f, 1.f};
-  for (int t = t0; t < t1; ++t) {
-    const size_t off = base + (size_t)t * H;
-    const float at = a[off], wt = omega[off], rt = r[off];
-    m = mob_mul(Mob{rt * at, rt * wt, s * at, rt + s * wt}, m);
+  for (int tb = t0; tb < t1; tb += TL) {
+    float av[TL], wv[TL], rv[TL];
+#pragma unroll
+    for (int j = 0; j < TL; ++j) {
+      const size_t off = base + (size_t)(tb + j) * H;
+      av[j] = tb + j < t1 ? a[off] : 0.f;
+      wv[j] = tb + j < t1 ? omega[off] : 0.f;
+      rv[j] = tb + j < t1 ? r[off] : 1.f;
+    }
+#pragma unroll
+    for (int j = 0; j < TL; ++j)
+      if (tb + j < t1) m = mob_mul(Mob{rv[j] * av[j], rv[j] * wv[j], s * av[j], rv[j] + s * wv[j]}, m);
   }
   const Mob pre = block_exclusive_mob(m);
   const float p0 = init_cov ? init_cov[bh] : 1.f / init_prec[h];
   float p = mob_apply(pre, p0);
-  for (int t = t0; t < t1; ++t) {
-    const size_t off = base + (size_t)t * H;
-    const float at = a[off], wt = omega[off], rt = r[off];
-    if (p_prev) p_prev[off] = p;
-    const float z = at * p + wt;
-    const float beta = z / (rt + z);
-    gain[off] = beta;
-    p = (s == 1.f) ? rt * beta : rt * z / (rt + s * z);
+  for (int tb = t0; tb < t1; tb += TL) {
+    float av[TL], wv[TL], rv[TL];
+#pragma unroll
+    for (int j = 0; j < TL; ++j) {
+      const size_t off = base + (size_t)(tb + j) * H;
+      av[j] = tb + j < t1 ? a[off] : 0.f;
+      wv[j] = tb + j < t1 ? omega[off] : 0.f;
+      rv[j] = tb + j < t1 ? r[off] : 1.f;
+    }
+#pragma unroll
+    for (int j = 0; j < TL; ++j) {
+      if (tb + j < t1) {
+        const size_t off = base + (size_t)(tb + j) * H;
+        if (p_prev) p_prev[off] = p;
+        const float z = av[j] * p + wv[j];
+        const float beta = z / (rv[j] + z);
+        gain[off] = beta;
+        p = (s == 1.f) ? rv[j] * beta : rv[j] * z / (rv[j] + s * z);
+      }
+    }
   }
   if (p_final) {
     if (T == 0 && threadIdx.x == 0) p_final[bh] = p0;
@@ -145,39 +171,67 @@ __global__ void __launch_bounds__(kIsoThreads) iso_gain_bwd_kernel(
   const int seg = (T + blockDim.x - 1) / blockDim.x;
   const int t0 = min(threadIdx.x * seg, T), t1 = min(t0 + seg, T);
   const size_t base = (size_t)b * T * H + h;
+  constexpr int TL = kIsoTile;
+  // tokens te-1, te-2, ... of a tile (walking t downwards)
+  auto load_rev = [&](int te, float (&av)[TL], float (&wv)[TL], float (&rv)[TL], float (&dv)[TL], float (&pv)[TL]) {
+#pragma unroll
+    for (int j = 0; j < TL; ++j) {
+      const int t = te - 1 - j;
+      const size_t off = base + (size_t)t * H;
+      const bool in = t >= t0;
+      av[j] = in ? a[off] : 0.f;
+      wv[j] = in ? omega[off] : 0.f;
+      rv[j] = in ? r[off] : 1.f;
+      dv[j] = in ? dgain[off] : 0.f;
+      pv[j] = in ? p_prev[off] : 0.f;
+    }
+  };
   Aff f{1.f, 0.f};
-  for (int t = t1 - 1; t >= t0; --t) {
-    const size_t off = base + (size_t)t * H;
-    const float at = a[off], wt = omega[off], rt = r[off], dbt = dgain[off], pp = p_prev[off];
-    const float z = at * pp + wt;
-    const float gi = 1.f / (rt + z);
-    const float pr = rt / (rt + s * z);
-    // lambda_{t-1} = A_t lambda_t + B_t, so the segment map is
-    // F_{t0} o ... o F_{t1-1}; walking t downwards, F_t goes on the outside.
-    f = aff_after(Aff{at * pr * pr, at * dbt * rt * gi * gi}, f);
+  for (int te = t1; te > t0; te -= TL) {
+    float av[TL], wv[TL], rv[TL], dv[TL], pv[TL];
+    load_rev(te, av, wv, rv, dv, pv);
+#pragma unroll
+    for (int j = 0; j < TL; ++j) {
+      if (te - 1 - j >= t0) {
+        const float at = av[j], wt = wv[j], rt = rv[j], dbt = dv[j], pp = pv[j];
+        const float z = at * pp + wt;
+        const float gi = 1.f / (rt + z);
+        const float pr = rt / (rt + s * z);
+        // lambda_{t-1} = A_t lambda_t + B_t, so the segment map is
+        // F_{t0} o ... o F_{t1-1}; walking t downwards, F_t goes on the outside.
+        f = aff_after(Aff{at * pr * pr, at * dbt * rt * gi * gi}, f);
+      }
+    }
   }
   const Aff suf = block_exclusive_suffix_aff(f);
   // lambda after the last token: the cotangent of the final covariance (0 without one)
   float lam = suf.A * (d_final_cov ? d_final_cov[bh] : 0.f) + suf.B;
-  for (int t = t1 - 1; t >= t0; --t) {
-    const size_t off = base + (size_t)t * H;
-    const float at = a[off], wt = omega[off], rt = r[off], dbt = dgain[off], pp = p_prev[off];
-    const float z = at * pp + wt;
-    float zbar, drt;
-    if (s == 1.f) {
-      const float inv = 1.f / (rt + z), inv2 = inv * inv;
-      zbar = (dbt + rt * lam) * rt * inv2;
-      drt = z * (lam * z - dbt) * inv2;
-    } else {
-      const float gi = 1.f / (rt + z), gi2 = gi * gi;
-      const float pi = 1.f / (rt + s * z), pi2 = pi * pi;
-      zbar = dbt * rt * gi2 + lam * rt * rt * pi2;
-      drt = -dbt * z * gi2 + lam * s * z * z * pi2;
+  for (int te = t1; te > t0; te -= TL) {
+    float av[TL], wv[TL], rv[TL], dv[TL], pv[TL];
+    load_rev(te, av, wv, rv, dv, pv);
+#pragma unroll
+    for (int j = 0; j < TL; ++j) {
+      const int t = te - 1 - j;
+      if (t < t0) break;
+      const size_t off = base + (size_t)t * H;
+      const float at = av[j], wt = wv[j], rt = rv[j], dbt = dv[j], pp = pv[j];
+      const float z = at * pp + wt;
+      float zbar, drt;
+      if (s == 1.f) {
+        const float inv = 1.f / (rt + z), inv2 = inv * inv;
+        zbar = (dbt + rt * lam) * rt * inv2;
+        drt = z * (lam * z - dbt) * inv2;
+      } else {
+        const float gi = 1.f / (rt + z), gi2 = gi * gi;
+        const float pi = 1.f / (rt + s * z), pi2 = pi * pi;
+        zbar = dbt * rt * gi2 + lam * rt * rt * pi2;
+        drt = -dbt * z * gi2 + lam * s * z * z * pi2;
+      }
+      da[off] = zbar * pp;
+      domega[off] = zbar;
+      dr[off] = drt;
+      lam = at * zbar;
     }
-    da[off] = zbar * pp;
-    domega[off] = zbar;
-    dr[off] = drt;
-    lam = at * zbar;
   }
   if (threadIdx.x == 0) {
     if (d_init_cov) d_init_cov[bh] = lam;  // d L / d p_{-1}
