@@ -246,7 +246,10 @@ def step_diag(x):
 
 GRAD_NAMES = {"iso": ("q", "k", "v", "g_cumsum", "a", "omega", "r"),
               "diag": ("q", "k", "v", "g_cumsum", "k_gain", "alpha", "omega_raw", "r_raw")}
-LAUNCHES_PER_STEP = {"iso": 6, "diag": 10}  # gain fwd 1|3, scan fwd 2, scan bwd 2, gain bwd 1|3
+# iso: gain fwd (maps, apply), scan fwd (prep, fwd), scan bwd (state, chunk), gain bwd (maps, apply);
+# diag: gain fwd (map, carry, emit), scan fwd (gate_to64, prep, fwd), scan bwd (state, chunk, gate_fold),
+# gain bwd (map, carry, emit)
+LAUNCHES_PER_STEP = {"iso": 8, "diag": 12}
 
 
 def capture_step(step, x, device):

@@ -57,6 +57,9 @@ const char* kdn_last_error(void);
  * replaces p_{-1} = 1/initial_precision; the backward then takes the
  * cotangent of p_{T-1} in d_final_cov (nullable = 0), writes dL/dp_{-1} to
  * d_initial_cov (nullable) and gives initial_precision no gradient.
+ * Workspace: kdn_iso_gain_workspace_bytes(B, T, H) bytes of device memory
+ * (the composed maps of every 16-token segment; 0 when T = 0), the same size
+ * for both directions; B <= 65535.
  * ------------------------------------------------------------------------ */
 size_t kdn_iso_gain_workspace_bytes(int64_t B, int64_t T, int64_t H);
 int kdn_iso_gain_fwd(const float* a, const float* omega, const float* r,

@@ -19,7 +19,6 @@
 namespace kdn {
 namespace {
 
-constexpr int kIsoThreads = 256;
 constexpr int kDiagSeg = 64;
 
 struct Mob {  // 2x2 Moebius map p -> (A p + B) / (C p + D)
@@ -34,42 +33,6 @@ __device__ __forceinline__ Mob mob_mul(const Mob& x, const Mob& y) {  // x after
 }
 __device__ __forceinline__ float mob_apply(const Mob& m, float p) { return (m.A * p + m.B) / (m.C * p + m.D); }
 
-__device__ __forceinline__ Mob shfl_mob(const Mob& m, int delta, bool up) {
-  Mob r;
-  if (up) {
-    r.A = __shfl_up_sync(0xffffffffu, m.A, delta);
-    r.B = __shfl_up_sync(0xffffffffu, m.B, delta);
-    r.C = __shfl_up_sync(0xffffffffu, m.C, delta);
-    r.D = __shfl_up_sync(0xffffffffu, m.D, delta);
-  } else {
-    r.A = __shfl_down_sync(0xffffffffu, m.A, delta);
-    r.B = __shfl_down_sync(0xffffffffu, m.B, delta);
-    r.C = __shfl_down_sync(0xffffffffu, m.C, delta);
-    r.D = __shfl_down_sync(0xffffffffu, m.D, delta);
-  }
-  return r;
-}
-
-// Exclusive prefix (in token order, later maps on the left) of one Moebius
-// map per thread across the block.
-__device__ Mob block_exclusive_mob(Mob x) {
-  __shared__ Mob warp_tot[32];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  Mob y = x;
-#pragma unroll
-  for (int d = 1; d < 32; d <<= 1) {
-    Mob o = shfl_mob(y, d, true);
-    if (lane >= d) y = mob_mul(y, o);
-  }
-  Mob excl = shfl_mob(y, 1, true);
-  if (lane == 0) excl = Mob{1.f, 0.f, 0.f, 1.f};
-  if (lane == 31) warp_tot[warp] = y;
-  __syncthreads();
-  Mob pre{1.f, 0.f, 0.f, 1.f};
-  for (int w = 0; w < warp; ++w) pre = mob_mul(warp_tot[w], pre);
-  return mob_mul(excl, pre);
-}
-
 struct Aff {  // lambda -> A lambda + B
   float A, B;
 };
@@ -77,143 +40,223 @@ __device__ __forceinline__ Aff aff_after(const Aff& f, const Aff& g) {  // f o g
   return Aff{f.A * g.A, f.A * g.B + f.B};
 }
 
-// Exclusive suffix (reverse token order) of one affine map per thread: thread
-// i receives F_{i+1} o ... o F_{n-1}.
-__device__ Aff block_exclusive_suffix_aff(Aff x) {
-  __shared__ Aff warp_tot[32];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  Aff z = x;
-#pragma unroll
-  for (int d = 1; d < 32; d <<= 1) {
-    Aff o{__shfl_down_sync(0xffffffffu, z.A, d), __shfl_down_sync(0xffffffffu, z.B, d)};
-    if (lane + d < 32) z = aff_after(z, o);
-  }
-  Aff excl{__shfl_down_sync(0xffffffffu, z.A, 1), __shfl_down_sync(0xffffffffu, z.B, 1)};
-  if (lane == 31) excl = Aff{1.f, 0.f};
-  if (lane == 0) warp_tot[warp] = z;
-  __syncthreads();
-  Aff suf{1.f, 0.f};
-  for (int w = nw - 1; w > warp; --w) suf = aff_after(warp_tot[w], suf);
-  return aff_after(excl, suf);
-}
-
 // ---------------------------------------------------------------------------
 // Isotropic gain
 // ---------------------------------------------------------------------------
-// A thread's tokens are read TL at a time, all loads of a tile issued before
-// its arithmetic: the reads are strided by H (one float per token and head),
-// so each costs a full memory round trip, which the tile shares.
-constexpr int kIsoTile = 16;
+// The rows [B,T,H] are contiguous over heads, so a warp takes one head per
+// lane and reads one token of all its heads as one contiguous run (a thread
+// per (b,h) reading its own tokens would touch one 32-byte sector per token
+// and value, and the load unit, not memory, would bound it).  Each warp owns
+// a segment of kIsoSeg tokens, kIsoWarps segments per CTA; the grid is
+// (token blocks, B, head groups of 32).  Two launches per direction:
+//   maps:  each segment's composed map and each CTA's total, to the workspace;
+//   apply: the composition of every map before the segment (after it, in the
+//          backward), then the exact per-token recurrence from that carry.
+// The token blocks before a CTA are composed by its warps in kIsoWarps slices.
+constexpr int kIsoSeg = 16, kIsoWarps = 8, kIsoBlockTok = kIsoSeg * kIsoWarps;
 
-__global__ void __launch_bounds__(kIsoThreads) iso_gain_fwd_kernel(const float* __restrict__ a,
-                                                                   const float* __restrict__ omega,
-                                                                   const float* __restrict__ r,
-                                                                   const float* __restrict__ init_prec,
-                                                                   const float* __restrict__ init_cov,
-                                                                   float* __restrict__ gain, float* __restrict__ p_prev,
-                                                                   float* __restrict__ p_final, int T, int H, float s) {
-  const int bh = blockIdx.x, b = bh / H, h = bh - b * H;
-  const int seg = (T + blockDim.x - 1) / blockDim.x;
-  const int t0 = min(threadIdx.x * seg, T), t1 = min(t0 + seg, T);
-  const size_t base = (size_t)b * T * H + h;
-  constexpr int TL = kIsoTile;
+// Forward map of one token: p -> r z / (r + s z), z = a p + omega.
+__device__ __forceinline__ Mob iso_tok_map(float a, float w, float r, float s) {
+  return Mob{r * a, r * w, s * a, r + s * w};
+}
+// Adjoint of one token: lambda_{t-1} = A lambda_t + B (p_prev = p_{t-1}).
+__device__ __forceinline__ Aff iso_tok_adj(float a, float w, float r, float db, float pp, float s) {
+  const float z = a * pp + w;
+  const float gi = 1.f / (r + z);
+  const float pr = r / (r + s * z);
+  return Aff{a * pr * pr, a * db * r * gi * gi};
+}
+__device__ __forceinline__ Mob as_mob(const float4& x) { return Mob{x.x, x.y, x.z, x.w}; }
+__device__ __forceinline__ Aff as_aff(const float4& x) { return Aff{x.x, x.y}; }
+
+// Workspace layout: [B][nblk][kIsoWarps][H] segment maps, then [B][nblk][H]
+// CTA totals (float4: Moebius (A, B, C, D) or affine (A, B, -, -)).
+struct IsoWs {
+  float4* seg;
+  float4* tot;
+};
+__host__ __device__ inline IsoWs iso_ws(void* ws, int B, int nblk, int H) {
+  float4* seg = static_cast<float4*>(ws);
+  return IsoWs{seg, seg + (size_t)B * nblk * kIsoWarps * H};
+}
+
+__global__ void __launch_bounds__(32 * kIsoWarps) iso_gain_fwd_maps_kernel(
+    const float* __restrict__ a, const float* __restrict__ omega, const float* __restrict__ r, IsoWs ws, int T,
+    int H, float s) {
+  __shared__ Mob sm[kIsoWarps][32];
+  const int blk = blockIdx.x, b = blockIdx.y, nblk = gridDim.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = 32 * blockIdx.z + lane;
+  const int ts = blk * kIsoBlockTok + warp * kIsoSeg;
   Mob m{1.f, 0.f, 0.f, 1.f};
-  for (int tb = t0; tb < t1; tb += TL) {
-    float av[TL], wv[TL], rv[TL];
+  if (h < H) {
+    float av[kIsoSeg], wv[kIsoSeg], rv[kIsoSeg];
 #pragma unroll
-    for (int j = 0; j < TL; ++j) {
-      const size_t off = base + (size_t)(tb + j) * H;
-      av[j] = tb + j < t1 ? a[off] : 0.f;
-      wv[j] = tb + j < t1 ? omega[off] : 0.f;
-      rv[j] = tb + j < t1 ? r[off] : 1.f;
+    for (int j = 0; j < kIsoSeg; ++j) {
+      const bool in = ts + j < T;
+      const size_t off = ((size_t)b * T + ts + j) * H + h;
+      av[j] = in ? a[off] : 0.f;
+      wv[j] = in ? omega[off] : 0.f;
+      rv[j] = in ? r[off] : 1.f;
     }
 #pragma unroll
-    for (int j = 0; j < TL; ++j)
-      if (tb + j < t1) m = mob_mul(Mob{rv[j] * av[j], rv[j] * wv[j], s * av[j], rv[j] + s * wv[j]}, m);
+    for (int j = 0; j < kIsoSeg; ++j)
+      if (ts + j < T) m = mob_mul(iso_tok_map(av[j], wv[j], rv[j], s), m);
   }
-  const Mob pre = block_exclusive_mob(m);
-  const float p0 = init_cov ? init_cov[bh] : 1.f / init_prec[h];
-  float p = mob_apply(pre, p0);
-  for (int tb = t0; tb < t1; tb += TL) {
-    float av[TL], wv[TL], rv[TL];
+  sm[warp][lane] = m;
+  const size_t row = (size_t)b * nblk + blk;
+  if (h < H) ws.seg[(row * kIsoWarps + warp) * H + h] = make_float4(m.A, m.B, m.C, m.D);
+  __syncthreads();
+  if (warp == 0 && h < H) {
+    Mob t{1.f, 0.f, 0.f, 1.f};
 #pragma unroll
-    for (int j = 0; j < TL; ++j) {
-      const size_t off = base + (size_t)(tb + j) * H;
-      av[j] = tb + j < t1 ? a[off] : 0.f;
-      wv[j] = tb + j < t1 ? omega[off] : 0.f;
-      rv[j] = tb + j < t1 ? r[off] : 1.f;
-    }
-#pragma unroll
-    for (int j = 0; j < TL; ++j) {
-      if (tb + j < t1) {
-        const size_t off = base + (size_t)(tb + j) * H;
-        if (p_prev) p_prev[off] = p;
-        const float z = av[j] * p + wv[j];
-        const float beta = z / (rv[j] + z);
-        gain[off] = beta;
-        p = (s == 1.f) ? rv[j] * beta : rv[j] * z / (rv[j] + s * z);
-      }
-    }
-  }
-  if (p_final) {
-    if (T == 0 && threadIdx.x == 0) p_final[bh] = p0;
-    if (t1 == T && t0 < t1) p_final[bh] = p;
+    for (int w = 0; w < kIsoWarps; ++w) t = mob_mul(sm[w][lane], t);
+    ws.tot[row * H + h] = make_float4(t.A, t.B, t.C, t.D);
   }
 }
 
-__global__ void __launch_bounds__(kIsoThreads) iso_gain_bwd_kernel(
+// T = 0 runs with one token block and no maps: only p_final is written.
+__global__ void __launch_bounds__(32 * kIsoWarps) iso_gain_fwd_apply_kernel(
     const float* __restrict__ a, const float* __restrict__ omega, const float* __restrict__ r,
-    const float* __restrict__ init_prec, const float* __restrict__ dgain, const float* __restrict__ p_prev,
-    const float* __restrict__ d_final_cov, const bool has_init_cov, float* __restrict__ d_init_cov,
-    float* __restrict__ da, float* __restrict__ domega, float* __restrict__ dr, float* __restrict__ dinit, int T,
-    int H, float s) {
-  const int bh = blockIdx.x, b = bh / H, h = bh - b * H;
-  const int seg = (T + blockDim.x - 1) / blockDim.x;
-  const int t0 = min(threadIdx.x * seg, T), t1 = min(t0 + seg, T);
-  const size_t base = (size_t)b * T * H + h;
-  constexpr int TL = kIsoTile;
-  // tokens te-1, te-2, ... of a tile (walking t downwards)
-  auto load_rev = [&](int te, float (&av)[TL], float (&wv)[TL], float (&rv)[TL], float (&dv)[TL], float (&pv)[TL]) {
+    const float* __restrict__ init_prec, const float* __restrict__ init_cov, IsoWs ws, float* __restrict__ gain,
+    float* __restrict__ p_prev, float* __restrict__ p_final, int T, int H, float s) {
+  __shared__ Mob part[kIsoWarps][32];
+  const int blk = blockIdx.x, b = blockIdx.y, nblk = gridDim.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = 32 * blockIdx.z + lane;
+  const bool on = h < H;
+  const int ts = blk * kIsoBlockTok + warp * kIsoSeg;
+  // this segment's rows first: their latency overlaps the carry
+  float av[kIsoSeg], wv[kIsoSeg], rv[kIsoSeg];
 #pragma unroll
-    for (int j = 0; j < TL; ++j) {
-      const int t = te - 1 - j;
-      const size_t off = base + (size_t)t * H;
-      const bool in = t >= t0;
+  for (int j = 0; j < kIsoSeg; ++j) {
+    const bool in = on && ts + j < T;
+    const size_t off = ((size_t)b * T + ts + j) * H + h;
+    av[j] = in ? a[off] : 0.f;
+    wv[j] = in ? omega[off] : 0.f;
+    rv[j] = in ? r[off] : 1.f;
+  }
+  // this warp's slice of the token blocks before this one
+  Mob c{1.f, 0.f, 0.f, 1.f};
+  if (on) {
+    const int lo = (int)((int64_t)blk * warp / kIsoWarps), hi = (int)((int64_t)blk * (warp + 1) / kIsoWarps);
+    for (int k = lo; k < hi; ++k) c = mob_mul(as_mob(ws.tot[((size_t)b * nblk + k) * H + h]), c);
+  }
+  part[warp][lane] = c;
+  __syncthreads();
+  const bool first = blk == 0 && warp == 0;
+  if (!on || (ts >= T && !first)) return;
+  Mob pre{1.f, 0.f, 0.f, 1.f};
+#pragma unroll
+  for (int w = 0; w < kIsoWarps; ++w) pre = mob_mul(part[w][lane], pre);
+  const size_t row = (size_t)b * nblk + blk;
+  for (int w = 0; w < warp; ++w) pre = mob_mul(as_mob(ws.seg[(row * kIsoWarps + w) * H + h]), pre);
+  const float p0 = init_cov ? init_cov[(size_t)b * H + h] : 1.f / init_prec[h];
+  float p = mob_apply(pre, p0);
+#pragma unroll
+  for (int j = 0; j < kIsoSeg; ++j) {
+    if (ts + j < T) {
+      const size_t off = ((size_t)b * T + ts + j) * H + h;
+      if (p_prev) p_prev[off] = p;
+      const float z = av[j] * p + wv[j];
+      const float beta = z / (rv[j] + z);
+      gain[off] = beta;
+      p = (s == 1.f) ? rv[j] * beta : rv[j] * z / (rv[j] + s * z);
+    }
+  }
+  if (p_final && (T == 0 || (ts <= T - 1 && T - 1 < ts + kIsoSeg))) p_final[(size_t)b * H + h] = p;
+}
+
+__global__ void __launch_bounds__(32 * kIsoWarps) iso_gain_bwd_maps_kernel(
+    const float* __restrict__ a, const float* __restrict__ omega, const float* __restrict__ r,
+    const float* __restrict__ dgain, const float* __restrict__ p_prev, IsoWs ws, int T, int H, float s) {
+  __shared__ Aff sm[kIsoWarps][32];
+  const int blk = blockIdx.x, b = blockIdx.y, nblk = gridDim.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = 32 * blockIdx.z + lane;
+  const int ts = blk * kIsoBlockTok + warp * kIsoSeg;
+  // lambda_{ts-1} = F_ts o ... o F_{te-1} (lambda_{te-1}): walking t downwards,
+  // F_t goes on the outside
+  Aff f{1.f, 0.f};
+  if (h < H) {
+    float av[kIsoSeg], wv[kIsoSeg], rv[kIsoSeg], dv[kIsoSeg], pv[kIsoSeg];
+#pragma unroll
+    for (int j = 0; j < kIsoSeg; ++j) {
+      const bool in = ts + j < T;
+      const size_t off = ((size_t)b * T + ts + j) * H + h;
       av[j] = in ? a[off] : 0.f;
       wv[j] = in ? omega[off] : 0.f;
       rv[j] = in ? r[off] : 1.f;
       dv[j] = in ? dgain[off] : 0.f;
       pv[j] = in ? p_prev[off] : 0.f;
     }
-  };
-  Aff f{1.f, 0.f};
-  for (int te = t1; te > t0; te -= TL) {
-    float av[TL], wv[TL], rv[TL], dv[TL], pv[TL];
-    load_rev(te, av, wv, rv, dv, pv);
 #pragma unroll
-    for (int j = 0; j < TL; ++j) {
-      if (te - 1 - j >= t0) {
-        const float at = av[j], wt = wv[j], rt = rv[j], dbt = dv[j], pp = pv[j];
-        const float z = at * pp + wt;
-        const float gi = 1.f / (rt + z);
-        const float pr = rt / (rt + s * z);
-        // lambda_{t-1} = A_t lambda_t + B_t, so the segment map is
-        // F_{t0} o ... o F_{t1-1}; walking t downwards, F_t goes on the outside.
-        f = aff_after(Aff{at * pr * pr, at * dbt * rt * gi * gi}, f);
-      }
-    }
+    for (int j = kIsoSeg - 1; j >= 0; --j)
+      if (ts + j < T) f = aff_after(iso_tok_adj(av[j], wv[j], rv[j], dv[j], pv[j], s), f);
   }
-  const Aff suf = block_exclusive_suffix_aff(f);
-  // lambda after the last token: the cotangent of the final covariance (0 without one)
-  float lam = suf.A * (d_final_cov ? d_final_cov[bh] : 0.f) + suf.B;
-  for (int te = t1; te > t0; te -= TL) {
-    float av[TL], wv[TL], rv[TL], dv[TL], pv[TL];
-    load_rev(te, av, wv, rv, dv, pv);
+  sm[warp][lane] = f;
+  const size_t row = (size_t)b * nblk + blk;
+  if (h < H) ws.seg[(row * kIsoWarps + warp) * H + h] = make_float4(f.A, f.B, 0.f, 0.f);
+  __syncthreads();
+  if (warp == 0 && h < H) {
+    Aff t{1.f, 0.f};
 #pragma unroll
-    for (int j = 0; j < TL; ++j) {
-      const int t = te - 1 - j;
-      if (t < t0) break;
-      const size_t off = base + (size_t)t * H;
+    for (int w = kIsoWarps - 1; w >= 0; --w) t = aff_after(sm[w][lane], t);
+    ws.tot[row * H + h] = make_float4(t.A, t.B, 0.f, 0.f);
+  }
+}
+
+// T = 0 runs with one token block and no maps: the cotangent of p_{-1} is
+// d_final_cov itself.
+__global__ void __launch_bounds__(32 * kIsoWarps) iso_gain_bwd_apply_kernel(
+    const float* __restrict__ a, const float* __restrict__ omega, const float* __restrict__ r,
+    const float* __restrict__ init_prec, const float* __restrict__ dgain, const float* __restrict__ p_prev,
+    const float* __restrict__ d_final_cov, const bool has_init_cov, float* __restrict__ d_init_cov, IsoWs ws,
+    float* __restrict__ da, float* __restrict__ domega, float* __restrict__ dr, float* __restrict__ dinit, int T,
+    int H, float s) {
+  __shared__ Aff part[kIsoWarps][32];
+  const int blk = blockIdx.x, b = blockIdx.y, nblk = gridDim.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = 32 * blockIdx.z + lane;
+  const bool on = h < H;
+  const int ts = blk * kIsoBlockTok + warp * kIsoSeg;
+  float av[kIsoSeg], wv[kIsoSeg], rv[kIsoSeg], dv[kIsoSeg], pv[kIsoSeg];
+#pragma unroll
+  for (int j = 0; j < kIsoSeg; ++j) {
+    const bool in = on && ts + j < T;
+    const size_t off = ((size_t)b * T + ts + j) * H + h;
+    av[j] = in ? a[off] : 0.f;
+    wv[j] = in ? omega[off] : 0.f;
+    rv[j] = in ? r[off] : 1.f;
+    dv[j] = in ? dgain[off] : 0.f;
+    pv[j] = in ? p_prev[off] : 0.f;
+  }
+  // this warp's slice of the token blocks after this one, composed as
+  // Tot_lo o ... o Tot_{hi-1}
+  Aff c{1.f, 0.f};
+  if (on) {
+    const int n = nblk - 1 - blk;
+    const int lo = blk + 1 + (int)((int64_t)n * warp / kIsoWarps);
+    const int hi = blk + 1 + (int)((int64_t)n * (warp + 1) / kIsoWarps);
+    for (int k = hi - 1; k >= lo; --k) c = aff_after(as_aff(ws.tot[((size_t)b * nblk + k) * H + h]), c);
+  }
+  part[warp][lane] = c;
+  __syncthreads();
+  const bool first = blk == 0 && warp == 0;
+  if (!on || (ts >= T && !first)) return;
+  Aff suf{1.f, 0.f};
+#pragma unroll
+  for (int w = kIsoWarps - 1; w >= 0; --w) suf = aff_after(part[w][lane], suf);
+  if (T > 0) {
+    const size_t row = (size_t)b * nblk + blk;
+    for (int w = kIsoWarps - 1; w > warp; --w) suf = aff_after(as_aff(ws.seg[(row * kIsoWarps + w) * H + h]), suf);
+  }
+  // lambda after the segment's last token (d_final_cov: the cotangent of p_{T-1}, 0 without one)
+  float lam = suf.A * (d_final_cov ? d_final_cov[(size_t)b * H + h] : 0.f) + suf.B;
+#pragma unroll
+  for (int j = kIsoSeg - 1; j >= 0; --j) {
+    if (ts + j < T) {
+      const size_t off = ((size_t)b * T + ts + j) * H + h;
       const float at = av[j], wt = wv[j], rt = rv[j], dbt = dv[j], pp = pv[j];
       const float z = at * pp + wt;
       float zbar, drt;
@@ -233,13 +276,29 @@ __global__ void __launch_bounds__(kIsoThreads) iso_gain_bwd_kernel(
       lam = at * zbar;
     }
   }
-  if (threadIdx.x == 0) {
-    if (d_init_cov) d_init_cov[bh] = lam;  // d L / d p_{-1}
+  if (first) {
+    if (d_init_cov) d_init_cov[(size_t)b * H + h] = lam;  // d L / d p_{-1}
     if (!has_init_cov) {
       const float ip = init_prec[h];
       atomicAdd(dinit + h, -lam / (ip * ip));
     }
   }
+}
+
+// Host side: workspace size and launch grid.
+size_t iso_ws_bytes(int64_t B, int64_t T, int64_t H) {
+  if (B <= 0 || T <= 0 || H <= 0) return 0;
+  const int64_t nblk = (T + kIsoBlockTok - 1) / kIsoBlockTok;
+  return align_up(sizeof(float4) * (size_t)(B * nblk * (kIsoWarps + 1) * H), 256);
+}
+
+int iso_grid(const char* what, int64_t B, int64_t T, int64_t H, void* ws, size_t ws_bytes, dim3* grid) {
+  if (T > INT32_MAX || B > 65535 || (H + 31) / 32 > 65535 || H > INT32_MAX)
+    return set_error(KDN_ERR_INVALID, "%s: size too large", what);
+  if (ws_bytes < iso_ws_bytes(B, T, H) || (T > 0 && !ws))
+    return set_error(KDN_ERR_WORKSPACE, "%s: workspace too small (kdn_iso_gain_workspace_bytes)", what);
+  *grid = dim3(T > 0 ? (unsigned)((T + kIsoBlockTok - 1) / kIsoBlockTok) : 1u, (unsigned)B, (unsigned)((H + 31) / 32));
+  return KDN_OK;
 }
 
 // ---------------------------------------------------------------------------
@@ -611,33 +670,46 @@ using namespace kdn;
 
 extern "C" {
 
-size_t kdn_iso_gain_workspace_bytes(int64_t, int64_t, int64_t) { return 0; }
+size_t kdn_iso_gain_workspace_bytes(int64_t B, int64_t T, int64_t H) { return iso_ws_bytes(B, T, H); }
 
 int kdn_iso_gain_fwd(const float* a, const float* omega, const float* r, const float* init_prec,
                      const float* init_cov, float* gain, float* p_prev, float* p_final, int64_t B, int64_t T,
-                     int64_t H, float s, void*, size_t, kdn_stream_t stream) {
+                     int64_t H, float s, void* workspace, size_t workspace_bytes, kdn_stream_t stream) {
   if (B <= 0 || H <= 0 || T < 0 || !a || !omega || !r || !init_prec || !gain)
     return set_error(KDN_ERR_INVALID, "kdn_iso_gain_fwd: invalid arguments");
-  if (T > INT32_MAX || B * H > INT32_MAX) return set_error(KDN_ERR_INVALID, "kdn_iso_gain_fwd: size too large");
-  iso_gain_fwd_kernel<<<(unsigned)(B * H), kIsoThreads, 0, (cudaStream_t)stream>>>(
-      a, omega, r, init_prec, init_cov, gain, p_prev, p_final, (int)T, (int)H, s);
-  return check_launch("iso_gain_fwd_kernel");
+  dim3 grid;
+  if (int rc = iso_grid("kdn_iso_gain_fwd", B, T, H, workspace, workspace_bytes, &grid)) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  const IsoWs ws = iso_ws(workspace, (int)B, (int)grid.x, (int)H);
+  if (T > 0) {
+    iso_gain_fwd_maps_kernel<<<grid, 32 * kIsoWarps, 0, st>>>(a, omega, r, ws, (int)T, (int)H, s);
+    if (int rc = check_launch("iso_gain_fwd_maps_kernel")) return rc;
+  }
+  iso_gain_fwd_apply_kernel<<<grid, 32 * kIsoWarps, 0, st>>>(a, omega, r, init_prec, init_cov, ws, gain, p_prev,
+                                                            p_final, (int)T, (int)H, s);
+  return check_launch("iso_gain_fwd_apply_kernel");
 }
 
 int kdn_iso_gain_bwd(const float* a, const float* omega, const float* r, const float* init_prec,
                      const float* init_cov, const float* dgain, const float* p_prev, const float* d_final_cov,
                      float* da, float* domega, float* dr, float* dinit, float* d_init_cov, int64_t B, int64_t T,
-                     int64_t H, float s, void*, size_t, kdn_stream_t stream) {
+                     int64_t H, float s, void* workspace, size_t workspace_bytes, kdn_stream_t stream) {
   if (B <= 0 || H <= 0 || T < 0 || !a || !omega || !r || !init_prec || !dgain || !da || !domega || !dr || !dinit ||
       (T > 0 && !p_prev))
     return set_error(KDN_ERR_INVALID, "kdn_iso_gain_bwd: invalid arguments");
-  if (T > INT32_MAX || B * H > INT32_MAX) return set_error(KDN_ERR_INVALID, "kdn_iso_gain_bwd: size too large");
+  dim3 grid;
+  if (int rc = iso_grid("kdn_iso_gain_bwd", B, T, H, workspace, workspace_bytes, &grid)) return rc;
   cudaStream_t st = (cudaStream_t)stream;
+  const IsoWs ws = iso_ws(workspace, (int)B, (int)grid.x, (int)H);
   if (cudaMemsetAsync(dinit, 0, sizeof(float) * H, st) != cudaSuccess) return check_launch("memset d_initial_precision");
-  iso_gain_bwd_kernel<<<(unsigned)(B * H), kIsoThreads, 0, st>>>(a, omega, r, init_prec, dgain, p_prev, d_final_cov,
-                                                                 init_cov != nullptr, d_init_cov, da, domega, dr,
-                                                                 dinit, (int)T, (int)H, s);
-  return check_launch("iso_gain_bwd_kernel");
+  if (T > 0) {
+    iso_gain_bwd_maps_kernel<<<grid, 32 * kIsoWarps, 0, st>>>(a, omega, r, dgain, p_prev, ws, (int)T, (int)H, s);
+    if (int rc = check_launch("iso_gain_bwd_maps_kernel")) return rc;
+  }
+  iso_gain_bwd_apply_kernel<<<grid, 32 * kIsoWarps, 0, st>>>(a, omega, r, init_prec, dgain, p_prev, d_final_cov,
+                                                            init_cov != nullptr, d_init_cov, ws, da, domega, dr,
+                                                            dinit, (int)T, (int)H, s);
+  return check_launch("iso_gain_bwd_apply_kernel");
 }
 
 int64_t kdn_diag_gain_carry_elems(int64_t B, int64_t T, int64_t H, int64_t K) {

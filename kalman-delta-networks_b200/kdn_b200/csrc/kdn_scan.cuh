@@ -543,18 +543,17 @@ __device__ void chunk_solve(const float* sA, const typename CF::OpT* sAb, typena
   using OpT = typename CF::OpT;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp < NB && lane < 16) {
+    // column j of the block's inverse, right-looking: once col[l] is final it
+    // updates every later row, so consecutive updates are independent (the
+    // terms still accumulate in ascending l, and col[l] = 0 for l < j)
     const int o = warp * 16, j = lane;
     float col[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      float x = (i == j) ? 1.f : 0.f;
-      if (i > j) {
+    for (int i = 0; i < 16; ++i) col[i] = (i == j) ? 1.f : 0.f;
 #pragma unroll
-        for (int l = 0; l < i; ++l)
-          if (l >= j) x = fmaf(-sA[(o + i) * LDA + o + l], col[l], x);
-      }
-      col[i] = x;
-    }
+    for (int l = 0; l < 15; ++l)
+#pragma unroll
+      for (int i = l + 1; i < 16; ++i) col[i] = fmaf(-sA[(o + i) * LDA + o + l], col[l], col[i]);
 #pragma unroll
     for (int i = 0; i < 16; ++i) sTb[(o + i) * LDC + o + j] = from_f<OpT>(col[i]);
   }

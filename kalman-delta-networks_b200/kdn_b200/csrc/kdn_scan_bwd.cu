@@ -338,7 +338,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_bwd_state_tc_kernel(ScanPa
         for (int i = 0; i < 16; ++i) x[i] *= gl;
         tc::st16(tl + TS + 32 * hf + j, x);
       }
-      tc::wait_st();
+      // the scaled adjoint's TMEM stores complete before the adjoint MMAs (wait_st below)
     }
     fence_async_shared();
     tc::fence_before();
@@ -370,6 +370,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_bwd_state_tc_kernel(ScanPa
       }
     }
     if (threadIdx.x == 32) bulk_wait_read<0>();  // dh has left the adjoint operand (rewritten next chunk)
+    tc::wait_st();
     fence_async_shared();
     tc::fence_before();
     bar_sync(1, NTH);

@@ -220,9 +220,10 @@ struct FwdTcLayout {
   static constexpr size_t v = R::fwd_end;  // [C][64] bf16, swizzled by the TMA engine
   static constexpr size_t stage = align_up(v + (size_t)C * 128, 1024);
   static constexpr size_t S = NS * stage;                 // state operand [KD][64] bf16 (also h)
-  static constexpr size_t Del = S + (size_t)kKD * 128;    // delta [C][64] bf16, then the output rows
+  static constexpr size_t Del = S + (size_t)kKD * 128;    // delta [C][64] bf16
+  static constexpr size_t O = Del + (size_t)C * 128;      // output rows [C][64] (bf16 iso, fp32 diag)
   static constexpr size_t O_bytes = (size_t)C * 64 * (CF::ISO ? 2 : 4);
-  static constexpr size_t bar = Del + align_up(cmax((size_t)C * 128, O_bytes), 1024);
+  static constexpr size_t bar = O + align_up(O_bytes, 1024);
   static constexpr size_t bytes = bar + 128 + 1024;       // barriers and TMEM slot; alignment slack
 };
 
@@ -294,25 +295,28 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_fwd_tc_kernel(ScanParams p
   tc::wait_st();
   uint32_t mph = 0;
 
-  for (int c = p.c_lo; c < p.c_hi; ++c) {
-    const int it = c - p.c_lo, s = it % NS, t0 = c * C;
+  // Software-pipelined over chunks: chunk c's output rows are read out of
+  // TMEM while the delta products of chunk c + 1 run.
+  //   head(c):  state operand (and h) from TMEM, S <- 2^g_L S, delta MMAs
+  //   body(c):  delta -> operand tile, o and state MMAs, then head(c + 1),
+  //             then o(c) -> output tile -> TMA store
+  char* sO = base + Lo::O;
+  auto head = [&](int c) {
+    const int it = c - p.c_lo, s = it % NS;
     char* st = base + s * Lo::stage;
     mbar_wait(&full[s], (it / NS) & 1, p.status);
-    {
-      // state operand (and h), then S <- 2^g_L S
-      const float gl = reinterpret_cast<const float*>(st + R::F)[2 * kKD + row];
+    const float gl = reinterpret_cast<const float*>(st + R::F)[2 * kKD + row];
 #pragma unroll
-      for (int j = 0; j < 32; j += 16) {
-        float x[16];
-        tc::ld16(tl + TS + 32 * hf + j, x);
-        tc::st_row16(sS, kKD, row, 32 * hf + j, x, 1.f);
+    for (int j = 0; j < 32; j += 16) {
+      float x[16];
+      tc::ld16(tl + TS + 32 * hf + j, x);
+      tc::st_row16(sS, kKD, row, 32 * hf + j, x, 1.f);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) x[i] *= gl;
-        tc::st16(tl + TS + 32 * hf + j, x);
-      }
-      tc::wait_st();
+      for (int i = 0; i < 16; ++i) x[i] *= gl;
+      tc::st16(tl + TS + 32 * hf + j, x);
     }
-    if (threadIdx.x == 0) bulk_wait_read<0>();  // the previous output tile has left shared memory
+    // (the scaled state's TMEM stores complete before the state MMA: wait_st in the body)
+    if (threadIdx.x == 0) bulk_wait_read<0>();  // the previous output rows have left their tile
     fence_async_shared();
     tc::fence_before();
     bar_sync(1, NTH);
@@ -329,6 +333,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_fwd_tc_kernel(ScanParams p
         tc::mma(tmem + TD, tc::desc_mn(sS, kKD, ks), tc::desc_k(st + R::Wf, C, ks), idn, true);
       tc::commit(mmab);
     }
+  };
+
+  if (p.c_lo < p.c_hi) head(p.c_lo);
+  for (int c = p.c_lo; c < p.c_hi; ++c) {
+    const int it = c - p.c_lo, s = it % NS, t0 = c * C;
+    char* st = base + s * Lo::stage;
     mbar_wait(mmab, mph, p.status);
     mph ^= 1;
     tc::fence_after();
@@ -344,6 +354,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_fwd_tc_kernel(ScanParams p
       }
     }
     if (threadIdx.x == 32) bulk_wait_read<0>();  // h has left the state operand (rewritten next chunk)
+    tc::wait_st();
     fence_async_shared();
     tc::fence_before();
     bar_sync(1, NTH);
@@ -362,23 +373,32 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_fwd_tc_kernel(ScanParams p
     mbar_wait(mmab, mph, p.status);
     mph ^= 1;
     tc::fence_after();
-    // output rows (value column vc) over the delta tile, then one TMA store
+    // the next chunk's delta products go first (they write other TMEM columns
+    // and no tile this chunk still reads) ...
+    if (c + 1 < p.c_hi) {
+      head(c + 1);
+    } else {
+      if (threadIdx.x == 0) bulk_wait_read<0>();
+      bar_sync(1, NTH);
+    }
+    // ... then this chunk's output rows (value column vc) into their tile and one TMA store
     {
-      OutT* sO = reinterpret_cast<OutT*>(sDel);
+      OutT* o = reinterpret_cast<OutT*>(sO);
 #pragma unroll
       for (int j = 0; j < HC; j += 16) {
         float x[16];
         tc::ld16(tl + TO + HC * hf + j, x);
         if (lane < 16) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) sO[(HC * hf + j + i) * 64 + vc] = from_f<OutT>(x[i]);
+          for (int i = 0; i < 16; ++i) o[(HC * hf + j + i) * 64 + vc] = from_f<OutT>(x[i]);
         }
       }
     }
     fence_async_shared();
+    tc::fence_before();
     bar_sync(1, NTH);
     if (threadIdx.x == 0) {
-      tc::tma_store_4d(&maps.out, sDel, V0, h, t0, b);
+      tc::tma_store_4d(&maps.out, sO, V0, h, t0, b);
       bulk_commit();
     }
   }

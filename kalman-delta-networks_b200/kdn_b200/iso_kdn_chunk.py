@@ -44,10 +44,12 @@ def _iso_gain_forward(a, omega, r, initial_precision, *, out_dtype, save_state, 
     gain = torch.empty((B, T, H), dtype=torch.float32, device=a.device)
     p_prev = torch.empty((B, T, H), dtype=torch.float32, device=a.device) if save_state else None
     p_final = torch.empty((B, H), dtype=torch.float32, device=a.device) if want_final else None
+    ws = N.byte_buffer(lib.kdn_iso_gain_workspace_bytes(B, T, H), a.device)
     N.check(
         lib.kdn_iso_gain_fwd(
             a32.data_ptr(), w32.data_ptr(), r32.data_ptr(), p32.data_ptr(), N.ptr(c32), gain.data_ptr(),
-            N.ptr(p_prev), N.ptr(p_final), B, T, H, float(posterior_scale), None, 0, N.stream_of(a),
+            N.ptr(p_prev), N.ptr(p_final), B, T, H, float(posterior_scale), ws.data_ptr(), ws.numel(),
+            N.stream_of(a),
         ),
         "kdn_iso_gain_fwd",
     )
@@ -65,11 +67,12 @@ def _iso_gain_backward(a, omega, r, initial_precision, dgain, p_prev, *, posteri
     dr = torch.empty_like(da)
     dinit = torch.empty((H,), dtype=torch.float32, device=a.device)
     dic = torch.empty((B, H), dtype=torch.float32, device=a.device) if want_d_initial else None
+    ws = N.byte_buffer(lib.kdn_iso_gain_workspace_bytes(B, T, H), a.device)
     N.check(
         lib.kdn_iso_gain_bwd(
             a32.data_ptr(), w32.data_ptr(), r32.data_ptr(), p32.data_ptr(), N.ptr(initial_cov), d32.data_ptr(),
             p_prev.data_ptr(), N.ptr(dfc), da.data_ptr(), domega.data_ptr(), dr.data_ptr(), dinit.data_ptr(),
-            N.ptr(dic), B, T, H, float(posterior_scale), None, 0, N.stream_of(a),
+            N.ptr(dic), B, T, H, float(posterior_scale), ws.data_ptr(), ws.numel(), N.stream_of(a),
         ),
         "kdn_iso_gain_bwd",
     )

@@ -47,11 +47,12 @@ def precision(request):
 # ----------------------------------------------------------------------------- gains
 
 
-@pytest.mark.parametrize("T", [1, 37, 300, 1000])
+# T around the 128-token blocks of the gain kernels; H = 40: two head groups of 32 lanes
+@pytest.mark.parametrize("T,H", [(1, 3), (37, 3), (128, 3), (129, 5), (300, 3), (1000, 3), (4096, 18), (300, 40)])
 @pytest.mark.parametrize("s", [1.0, 0.5])
-def test_iso_gain_fwd_bwd(T, s):
+def test_iso_gain_fwd_bwd(T, H, s):
     torch.manual_seed(T)
-    B, H = 2, 3
+    B = 2
     a = torch.rand(B, T, H) * 0.98 + 0.01
     omega = torch.nn.functional.softplus(torch.randn(B, T, H))
     r = 0.01 + torch.nn.functional.softplus(torch.randn(B, T, H))
