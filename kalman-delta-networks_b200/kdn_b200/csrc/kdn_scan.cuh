@@ -374,25 +374,32 @@ __device__ __forceinline__ void build_operands(const Chunk<CF>& ch, int r, int c
 // from HBM).
 // The operands are built with the fast-path reference (the gate of the
 // middle row, known up front) and built again only when the range check
-// sends the chunk to the exact path.  Contains one barrier; the caller
-// places the barrier that publishes the results.
-template <class CF, int NTH, bool SW = false>
-__device__ void prep_chunk(Chunk<CF>& ch) {
+// sends the chunk to the exact path.  Contains one barrier (two when staged);
+// the caller places the barrier that publishes the results.
+// STAGED: the first build reads the q, k, g rows from shared-memory copies
+// (`src`, rows of kKD) that lie under the operand tiles it writes, so every
+// thread reads all of its rows before a barrier and writes after it; the
+// exact-path rebuild reads `ch` (the rows in HBM).
+template <class CF, int NTH, bool SW = false, bool STAGED = false>
+__device__ void prep_chunk(Chunk<CF>& ch, const Chunk<CF>* src = nullptr) {
   constexpr int C = CF::C, RSTEP = NTH / 16, RPT = C / RSTEP, BATCH = RPT <= 4 ? RPT : 2;
   static_assert(NTH % 32 == 0 && C % RSTEP == 0 && RPT % BATCH == 0, "rows per thread");
+  static_assert(!STAGED || BATCH == RPT, "a staged build holds all of a thread's rows at once");
+  const Chunk<CF>& in = STAGED ? *src : ch;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int L = ch.L;
   ch.m = L >= C ? C / 2 : (((L - 1) / 2) & ~15);
   const int c0 = (threadIdx.x & 15) * 8, rt = threadIdx.x >> 4;
   float gm[8], gl[8];
-  ld8(gm, ch.g + (size_t)ch.m * ch.ldr + c0);
-  ld8(gl, ch.g + (size_t)(L - 1) * ch.ldr + c0);
+  ld8(gm, in.g + (size_t)ch.m * in.ldr + c0);
+  ld8(gl, in.g + (size_t)(L - 1) * in.ldr + c0);
   float rng = 0.f;
 #pragma unroll
   for (int j0 = 0; j0 < RPT; j0 += BATCH) {
     RawRow<CF> x[BATCH];
 #pragma unroll
-    for (int j = 0; j < BATCH; ++j) load_row(x[j], ch, rt + (j0 + j) * RSTEP, c0);
+    for (int j = 0; j < BATCH; ++j) load_row(x[j], in, rt + (j0 + j) * RSTEP, c0);
+    if constexpr (STAGED) __syncthreads();
 #pragma unroll
     for (int j = 0; j < BATCH; ++j) {
       const int r = rt + (j0 + j) * RSTEP;

@@ -13,10 +13,21 @@
 // calls) and of _diag_kdn_memory_forward (diag_kdn_chunk.py:3224-3245).
 #include "kdn_scan.cuh"
 #include "kdn_tc.cuh"
+#include "kdn_tma.cuh"
 
 namespace kdn {
 
 constexpr int kPrepThreads = 256;
+
+// The chunk's raw q, k (bf16) and g (fp32) rows, staged by TMA (isotropic
+// bf16 records): one box of C tokens x 128 channels each.
+struct alignas(64) PrepMaps {
+  CUtensorMap q, k, g;
+};
+template <class CF>
+__host__ __device__ constexpr bool prep_staged() {
+  return CF::ISO && !CF::F32;
+}
 
 template <class CF>
 struct PrepLayout {
@@ -37,11 +48,17 @@ struct PrepLayout {
   static constexpr size_t rec_tiles = 3 * (size_t)C * 128;
   static constexpr bool alias = small - Xb >= rec_tiles;
   static constexpr size_t St = alias ? Xb : base_bytes;
-  static constexpr size_t bytes = alias ? base_bytes : base_bytes + rec_tiles;
+  // staged raw rows (prep_staged): k under Kr, q under Qr, g over Tb .. As
+  // (their first users come after the operand build)
+  static constexpr size_t raw_k = Kr, raw_q = Qr, raw_g = Tb;
+  static_assert(raw_g + (size_t)C * kKD * 4 <= small, "raw g rows fit below the chunk scalars");
+  static_assert((size_t)C * kKD * 2 <= Qr - Kr, "raw k rows fit under Kr");
+  static constexpr size_t bar = (alias ? base_bytes : base_bytes + rec_tiles);
+  static constexpr size_t bytes = bar + 16;
 };
 
 template <class CF>
-__global__ void __launch_bounds__(kPrepThreads, 2) scan_prep_kernel(ScanParams p) {
+__global__ void __launch_bounds__(kPrepThreads, 2) scan_prep_kernel(ScanParams p, const __grid_constant__ PrepMaps maps) {
   using OpT = typename CF::OpT;
   using Lo = PrepLayout<CF>;
   using R = Rec<CF>;
@@ -70,10 +87,35 @@ __global__ void __launch_bounds__(kPrepThreads, 2) scan_prep_kernel(ScanParams p
   OpT* sAb = reinterpret_cast<OpT*>(base + Lo::Ab);
   float* sA = reinterpret_cast<float*>(base + Lo::As);
 
-  zero_upper_blocks<CF>(sQb);
-  zero_upper_blocks<CF>(sTb);
-  prep_chunk<CF, kPrepThreads>(ch);
-  __syncthreads();
+  if constexpr (prep_staged<CF>()) {
+    // raw rows by TMA (rows past T arrive as zeros); the operand build reads
+    // them from shared memory
+    uint64_t* bar = reinterpret_cast<uint64_t*>(base + Lo::bar);
+    if (threadIdx.x == 0) {
+      mbar_init(bar, 1);
+      fence_mbar_init();
+      mbar_expect_tx(bar, (unsigned)(C * kKD * 8));
+      tma_load_4d(base + Lo::raw_k, &maps.k, 0, h, t0, b, bar);
+      tma_load_4d(base + Lo::raw_q, &maps.q, 0, h, t0, b, bar);
+      tma_load_4d(base + Lo::raw_g, &maps.g, 0, h, t0, b, bar);
+    }
+    __syncthreads();  // the barrier's initialisation is visible before anyone waits on it
+    mbar_wait(bar, 0, p.status);
+    Chunk<CF> src = ch;
+    src.k = reinterpret_cast<const bf16*>(base + Lo::raw_k);
+    src.q = reinterpret_cast<const bf16*>(base + Lo::raw_q);
+    src.g = reinterpret_cast<const float*>(base + Lo::raw_g);
+    src.ldr = kKD;
+    prep_chunk<CF, kPrepThreads, false, true>(ch, &src);
+    __syncthreads();
+    zero_upper_blocks<CF>(sQb);  // over the raw g rows, dead now
+    zero_upper_blocks<CF>(sTb);
+  } else {
+    zero_upper_blocks<CF>(sQb);
+    zero_upper_blocks<CF>(sTb);
+    prep_chunk<CF, kPrepThreads>(ch);
+    __syncthreads();
+  }
   chunk_scores(ch, sA, sAb, sQb);
   chunk_solve<CF>(sA, sAb, sTb, sXb);
 
@@ -199,7 +241,16 @@ int launch_prep(const ScanParams& p, cudaStream_t st) {
       return check_launch("cudaFuncSetAttribute(scan_prep_kernel)");
     configured = true;
   }
-  scan_prep_kernel<CF><<<dim3(p.c_hi - p.c_lo, p.B * p.H), kPrepThreads, smem, st>>>(p);
+  PrepMaps maps;
+  if constexpr (prep_staged<CF>()) {
+    int rc = encode_bthd(&maps.q, p.q, true, p.B, p.T, p.H, kKD, kKD, CF::C, false);
+    if (rc == KDN_OK) rc = encode_bthd(&maps.k, p.k, true, p.B, p.T, p.H, kKD, kKD, CF::C, false);
+    if (rc == KDN_OK) rc = encode_bthd(&maps.g, p.g, false, p.B, p.T, p.H, kKD, kKD, CF::C, false);
+    if (rc != KDN_OK) return rc;
+  } else {
+    memset(&maps, 0, sizeof(maps));
+  }
+  scan_prep_kernel<CF><<<dim3(p.c_hi - p.c_lo, p.B * p.H), kPrepThreads, smem, st>>>(p, maps);
   return check_launch("scan_prep_kernel");
 }
 
