@@ -151,13 +151,14 @@ __host__ __device__ constexpr size_t hblock_bytes() {
 template <class CF>
 struct Chunk {
   using OpT = typename CF::OpT;
-  // raw inputs: row i of q, k, g (and kappa) at ptr + i * ldr; beta at beta[i * ldb]
+  // raw inputs: row i of q, k, g at ptr + i * ldr, of kappa at kap + i * ldk;
+  // beta at beta[i * ldb]
   const bf16* q;
   const bf16* k;
   const float* g;
   const float* kap;   // diag
   const float* beta;  // iso
-  int ldr, ldb;
+  int ldr, ldb, ldk;
   // per-row / per-channel scalars
   float* rq;  // iso rstd of q rows
   float* rk;  // iso rstd of k rows
@@ -237,6 +238,7 @@ __device__ __forceinline__ void load_raw(Chunk<CF>& ch, bf16* sq, bf16* sk, floa
   ch.beta = CF::ISO ? skap : nullptr;
   ch.ldr = kKD;
   ch.ldb = 1;
+  ch.ldk = kKD;
 }
 
 // Point the chunk view at the rows in HBM.
@@ -250,6 +252,7 @@ __device__ __forceinline__ void bind_raw_global(Chunk<CF>& ch, const ScanParams&
   ch.beta = CF::ISO ? p.beta + r0 : nullptr;
   ch.ldr = p.H * kKD;
   ch.ldb = p.H;
+  ch.ldk = p.H * kKD;
 }
 
 template <class CF>
@@ -315,7 +318,7 @@ __device__ __forceinline__ void load_row(RawRow<CF>& x, const Chunk<CF>& ch, int
     if constexpr (CF::ISO) {
       x.beta = ch.beta[(size_t)r * ch.ldb];
     } else {
-      ld8(x.kap, ch.kap + o);
+      ld8(x.kap, ch.kap + (size_t)r * ch.ldk + c0);
       x.beta = 1.f;
     }
   } else {
@@ -330,12 +333,14 @@ __device__ __forceinline__ void load_row(RawRow<CF>& x, const Chunk<CF>& ch, int
 }
 
 // Gated operands of one row: Kr = k_hat 2^(g - rr), Qr = q_hat 2^(g - rr),
-// Kc = kappa 2^(rc - g); zero rows past the chunk's end.  SW: the operand
-// buffers are 64-row swizzled tensor-core tiles instead of padded rows.
-template <class CF, bool SW = false>
-__device__ __forceinline__ void build_operands(const Chunk<CF>& ch, int r, int c0, const RawRow<CF>& x,
-                                               const float (&rr)[8], const float (&rc)[8], float qs, float ks) {
-  float kr[8], qr[8], kc[8];
+// Kc = kappa 2^(rc - g); zero rows past the chunk's end.  make_operands
+// leaves them as 8 rounded OpT values per operand (bf16 precision: one 16-byte
+// word each); store_operands writes them, SW: into 64-row swizzled
+// tensor-core tiles instead of padded rows.
+template <class CF>
+__device__ __forceinline__ void make_operands(const Chunk<CF>& ch, int r, const RawRow<CF>& x, const float (&rr)[8],
+                                              const float (&rc)[8], float qs, float ks, float (&kr)[8],
+                                              float (&qr)[8], float (&kc)[8]) {
   if (r < ch.L) {
     const float bs = CF::ISO ? x.beta * ks : 1.f;
     float k8[8], q8[8];
@@ -353,6 +358,10 @@ __device__ __forceinline__ void build_operands(const Chunk<CF>& ch, int r, int c
 #pragma unroll
     for (int i = 0; i < 8; ++i) kr[i] = qr[i] = kc[i] = 0.f;
   }
+}
+template <class CF, bool SW>
+__device__ __forceinline__ void store_operands(const Chunk<CF>& ch, int r, int c0, const float (&kr)[8],
+                                               const float (&qr)[8], const float (&kc)[8]) {
   if constexpr (SW) {
     // byte offset of (r, c0) in a [2][64][64] swizzled tile
     const uint32_t o = (uint32_t)((c0 >> 6) * 64 * 128 + r * 128 + ((((c0 & 63) >> 3) ^ (r & 7)) << 4));
@@ -364,6 +373,13 @@ __device__ __forceinline__ void build_operands(const Chunk<CF>& ch, int r, int c
     st8(ch.Qr + r * CF::LDK + c0, qr);
     st8(ch.Kc + r * CF::LDK + c0, kc);
   }
+}
+template <class CF, bool SW = false>
+__device__ __forceinline__ void build_operands(const Chunk<CF>& ch, int r, int c0, const RawRow<CF>& x,
+                                               const float (&rr)[8], const float (&rc)[8], float qs, float ks) {
+  float kr[8], qr[8], kc[8];
+  make_operands(ch, r, x, rr, rc, qs, ks, kr, qr, kc);
+  store_operands<CF, SW>(ch, r, c0, kr, qr, kc);
 }
 
 // Row norms (iso), range check, per-channel factors and the three gated
@@ -377,14 +393,14 @@ __device__ __forceinline__ void build_operands(const Chunk<CF>& ch, int r, int c
 // sends the chunk to the exact path.  Contains one barrier (two when staged);
 // the caller places the barrier that publishes the results.
 // STAGED: the first build reads the q, k, g rows from shared-memory copies
-// (`src`, rows of kKD) that lie under the operand tiles it writes, so every
-// thread reads all of its rows before a barrier and writes after it; the
-// exact-path rebuild reads `ch` (the rows in HBM).
+// (`src`, rows of kKD; kappa stays where `src.kap` points) that lie under the
+// operand tiles it writes, so every thread builds all of its rows into
+// registers before a barrier and stores them after it; the exact-path rebuild
+// reads `ch` (the rows in HBM).
 template <class CF, int NTH, bool SW = false, bool STAGED = false>
 __device__ void prep_chunk(Chunk<CF>& ch, const Chunk<CF>* src = nullptr) {
   constexpr int C = CF::C, RSTEP = NTH / 16, RPT = C / RSTEP, BATCH = RPT <= 4 ? RPT : 2;
   static_assert(NTH % 32 == 0 && C % RSTEP == 0 && RPT % BATCH == 0, "rows per thread");
-  static_assert(!STAGED || BATCH == RPT, "a staged build holds all of a thread's rows at once");
   const Chunk<CF>& in = STAGED ? *src : ch;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int L = ch.L;
@@ -394,43 +410,76 @@ __device__ void prep_chunk(Chunk<CF>& ch, const Chunk<CF>* src = nullptr) {
   ld8(gm, in.g + (size_t)ch.m * in.ldr + c0);
   ld8(gl, in.g + (size_t)(L - 1) * in.ldr + c0);
   float rng = 0.f;
+  // iso: row scales 1/|q|, 1/|k| (half-warp sums), kept with beta per row
+  auto row_scales = [&](const RawRow<CF>& x, int r, float& qs, float& ks) {
+    qs = ks = 1.f;
+    if constexpr (CF::ISO) {
+      float sq = 0.f, sk = 0.f, k8[8], q8[8];
+      unpack8(k8, x.kp);
+      unpack8(q8, x.qp);
 #pragma unroll
-  for (int j0 = 0; j0 < RPT; j0 += BATCH) {
-    RawRow<CF> x[BATCH];
-#pragma unroll
-    for (int j = 0; j < BATCH; ++j) load_row(x[j], in, rt + (j0 + j) * RSTEP, c0);
-    if constexpr (STAGED) __syncthreads();
-#pragma unroll
-    for (int j = 0; j < BATCH; ++j) {
-      const int r = rt + (j0 + j) * RSTEP;
-      float qs = 1.f, ks = 1.f;
-      if constexpr (CF::ISO) {
-        float sq = 0.f, sk = 0.f, k8[8], q8[8];
-        unpack8(k8, x[j].kp);
-        unpack8(q8, x[j].qp);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          sq = fmaf(q8[i], q8[i], sq);
-          sk = fmaf(k8[i], k8[i], sk);
-        }
-#pragma unroll
-        for (int o = 1; o < 16; o <<= 1) {
-          sq += __shfl_xor_sync(0xffffffffu, sq, o);
-          sk += __shfl_xor_sync(0xffffffffu, sk, o);
-        }
-        qs = rsqrtf(sq + 1e-6f);
-        ks = rsqrtf(sk + 1e-6f);
-        if ((threadIdx.x & 15) == 0) {
-          ch.rq[r] = qs;
-          ch.rk[r] = ks;
-          ch.rb[r] = x[j].beta;
-        }
+      for (int i = 0; i < 8; ++i) {
+        sq = fmaf(q8[i], q8[i], sq);
+        sk = fmaf(k8[i], k8[i], sk);
       }
-      if (r < L) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) rng = fmaxf(rng, fabsf(x[j].g[i] - gm[i]));
+      for (int o = 1; o < 16; o <<= 1) {
+        sq += __shfl_xor_sync(0xffffffffu, sq, o);
+        sk += __shfl_xor_sync(0xffffffffu, sk, o);
       }
-      build_operands<CF, SW>(ch, r, c0, x[j], gm, gm, qs, ks);
+      qs = rsqrtf(sq + 1e-6f);
+      ks = rsqrtf(sk + 1e-6f);
+      if ((threadIdx.x & 15) == 0) {
+        ch.rq[r] = qs;
+        ch.rk[r] = ks;
+        ch.rb[r] = x.beta;
+      }
+    }
+    if (r < L) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) rng = fmaxf(rng, fabsf(x.g[i] - gm[i]));
+    }
+  };
+  if constexpr (STAGED) {
+    // row by row from shared memory into rounded operand words; the stores
+    // wait for every thread's reads
+    static_assert(!CF::F32, "staged build: bf16 operands");
+    uint4 okr[RPT], oqr[RPT], okc[RPT];
+#pragma unroll
+    for (int j = 0; j < RPT; ++j) {
+      const int r = rt + j * RSTEP;
+      RawRow<CF> x;
+      load_row(x, in, r, c0);
+      float qs, ks, kr[8], qr[8], kc[8];
+      row_scales(x, r, qs, ks);
+      make_operands(ch, r, x, gm, gm, qs, ks, kr, qr, kc);
+      okr[j] = pack8(kr);
+      oqr[j] = pack8(qr);
+      okc[j] = pack8(kc);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < RPT; ++j) {
+      const int r = rt + j * RSTEP;
+      float kr[8], qr[8], kc[8];
+      unpack8(kr, okr[j]);
+      unpack8(qr, oqr[j]);
+      unpack8(kc, okc[j]);
+      store_operands<CF, SW>(ch, r, c0, kr, qr, kc);
+    }
+  } else {
+#pragma unroll
+    for (int j0 = 0; j0 < RPT; j0 += BATCH) {
+      RawRow<CF> x[BATCH];
+#pragma unroll
+      for (int j = 0; j < BATCH; ++j) load_row(x[j], in, rt + (j0 + j) * RSTEP, c0);
+#pragma unroll
+      for (int j = 0; j < BATCH; ++j) {
+        const int r = rt + (j0 + j) * RSTEP;
+        float qs, ks;
+        row_scales(x[j], r, qs, ks);
+        build_operands<CF, SW>(ch, r, c0, x[j], gm, gm, qs, ks);
+      }
     }
   }
   rng = warp_max(rng);

@@ -49,9 +49,9 @@ struct ChunkTcLayout {
   static constexpr size_t V = G + 40960;
   static constexpr size_t vv = V, dO = V + 16384, dvst = V, rk = V, rq = V + 16384;
   static constexpr size_t rg = G;  // raw g rows [C][KD] fp32 over delta | ddelta
-  // isotropic: the raw rows of the operand build, staged by TMA with the other
+  // the raw q, k, g rows of the operand build, staged by TMA with the other
   // inputs (g under Kr | Qr, k under Kc, q under delta; read before any of
-  // those tiles is written)
+  // those tiles is written); the diagonal variant's kappa rows stay in HBM
   static constexpr size_t sg = Kr, sk = Kc, sq = Del;
   // S0 | dS (saved states), then dW dQ dQu dT X dA
   static constexpr size_t A = V + 32768;
@@ -127,7 +127,7 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
   // before the first wait (one barrier would then have moved two phases on)
   uint64_t* ddbar = ldbar + 3;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(ldbar + 4);
-  uint64_t* stbar = ldbar + 5;  // the staged raw rows (isotropic)
+  uint64_t* stbar = ldbar + 5;  // the staged raw rows
   float* small = reinterpret_cast<float*>(base + Lo::small);
   float* cfl = small + small_floats<CF>();
   float* cgl = cfl + kKD;
@@ -177,28 +177,23 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
       tma_load_4d(base + Lo::dO + C * 128, &maps.dO, 64, h, t0, b, ldbar);
     }
   };
-  if constexpr (CF::ISO) {
-    // every input in flight at once: the raw rows on their own barrier, so the
-    // operand build starts as soon as they have landed
-    if (threadIdx.x == 0) {
-      mbar_expect_tx(stbar, C * kKD * 8);
-      tma_load_4d(base + Lo::sg, &maps.g, 0, h, t0, b, stbar);
-      tma_load_4d(base + Lo::sk, &maps.k, 0, h, t0, b, stbar);
-      tma_load_4d(base + Lo::sq, &maps.q, 0, h, t0, b, stbar);
-      issue_loads();
-    }
-    mbar_wait(stbar, 0, p.status);
+  // every input in flight at once: the raw rows on their own barrier, so the
+  // operand build starts as soon as they have landed
+  if (threadIdx.x == 0) {
+    mbar_expect_tx(stbar, C * kKD * 8);
+    tma_load_4d(base + Lo::sg, &maps.g, 0, h, t0, b, stbar);
+    tma_load_4d(base + Lo::sk, &maps.k, 0, h, t0, b, stbar);
+    tma_load_4d(base + Lo::sq, &maps.q, 0, h, t0, b, stbar);
+    issue_loads();
+  }
+  mbar_wait(stbar, 0, p.status);
+  {
     Chunk<CF> src = ch;
     src.g = reinterpret_cast<const float*>(base + Lo::sg);
     src.k = reinterpret_cast<const bf16*>(base + Lo::sk);
     src.q = reinterpret_cast<const bf16*>(base + Lo::sq);
     src.ldr = kKD;
     prep_chunk<CF, 512, true, true>(ch, &src);
-  } else {
-    // gated operands from the raw rows (global loads) first: issuing the bulk
-    // copies blocks the issuing thread for about as long as they take to land
-    prep_chunk<CF, 512, true>(ch);
-    if (threadIdx.x == 0) issue_loads();
   }
   if constexpr (!CF::ISO) {
     // the fp32 cotangent rounded to bf16 into the swizzled operand tile (rows

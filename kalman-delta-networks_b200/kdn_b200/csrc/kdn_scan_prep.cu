@@ -19,14 +19,14 @@ namespace kdn {
 
 constexpr int kPrepThreads = 256;
 
-// The chunk's raw q, k (bf16) and g (fp32) rows, staged by TMA (isotropic
-// bf16 records): one box of C tokens x 128 channels each.
+// The chunk's raw q, k (bf16) and g (fp32) rows, staged by TMA (bf16
+// records): one box of C tokens x 128 channels each.
 struct alignas(64) PrepMaps {
   CUtensorMap q, k, g;
 };
 template <class CF>
 __host__ __device__ constexpr bool prep_staged() {
-  return CF::ISO && !CF::F32;
+  return !CF::F32;
 }
 
 template <class CF>
@@ -179,6 +179,17 @@ __global__ void __launch_bounds__(kPrepThreads, 2) scan_prep_kernel(ScanParams p
         for (int j = 0; j < RPT; ++j)
           *reinterpret_cast<uint4*>(tiles[m] + tc::sw_off(r0 + 16 * j, 8 * g, C)) = v[m][j];
     }
+    // those three tiles and the factors leave while T, Qq, Qt are built
+    fence_async_shared();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      static_assert(RT::Kf == RT::Qs + (size_t)C * 256 && RT::Wf == RT::Kf + (size_t)C * 256, "record tile order");
+      bulk_s2g(rec + RT::Qs, base + Lo::Qr, C * 256);
+      bulk_s2g(rec + RT::Kf, base + Lo::Kc, C * 256);
+      bulk_s2g(rec + RT::Wf, base + Lo::Kr, C * 256);
+      bulk_s2g(rec + RT::F, ch.fr, 3 * kKD * 4);
+      bulk_commit();
+    }
     // T, Qq = scale Q: thread t owns columns 8(t%8)..+7 of rows t/8, t/8 + 32, ...
     // (columns >= C zero); Qt = scale Q^T: warp w owns output columns
     // 8(w%8)..+7 and lane l output row l, l + 32, ..., so the column reads of
@@ -213,13 +224,8 @@ __global__ void __launch_bounds__(kPrepThreads, 2) scan_prep_kernel(ScanParams p
     __syncthreads();
     if (threadIdx.x == 0) {
       static_assert(RT::Qq == RT::T + (size_t)C * 128, "record tile order");
-      static_assert(RT::Kf == RT::Qs + (size_t)C * 256 && RT::Wf == RT::Kf + (size_t)C * 256, "record tile order");
       bulk_s2g(rec + RT::T, st, 2 * C * 128);
       bulk_s2g(rec + RT::Qt, st + 2 * C * 128, C * 128);
-      bulk_s2g(rec + RT::Qs, base + Lo::Qr, C * 256);
-      bulk_s2g(rec + RT::Kf, base + Lo::Kc, C * 256);
-      bulk_s2g(rec + RT::Wf, base + Lo::Kr, C * 256);
-      bulk_s2g(rec + RT::F, ch.fr, 3 * kKD * 4);
       bulk_commit();
       bulk_wait_read<0>();  // shared memory stays valid until the stores have read it
     }
