@@ -393,12 +393,14 @@ __device__ __forceinline__ void build_operands(const Chunk<CF>& ch, int r, int c
 // sends the chunk to the exact path.  Contains one barrier (two when staged);
 // the caller places the barrier that publishes the results.
 // STAGED: the first build reads the q, k, g rows from shared-memory copies
-// (`src`, rows of kKD; kappa stays where `src.kap` points) that lie under the
-// operand tiles it writes, so every thread builds all of its rows into
-// registers before a barrier and stores them after it; the exact-path rebuild
-// reads `ch` (the rows in HBM).
+// (`src`, rows of kKD, complete once `staged_bar` completes its first phase;
+// beta and kappa stay where `src` points) that lie under the operand tiles it
+// writes, so every thread builds all of its rows into registers before a
+// barrier and stores them after it; the exact-path rebuild reads `ch` (the
+// rows in HBM).
 template <class CF, int NTH, bool SW = false, bool STAGED = false>
-__device__ void prep_chunk(Chunk<CF>& ch, const Chunk<CF>* src = nullptr) {
+__device__ void prep_chunk(Chunk<CF>& ch, const Chunk<CF>* src = nullptr, uint64_t* staged_bar = nullptr,
+                           int* status = nullptr) {
   constexpr int C = CF::C, RSTEP = NTH / 16, RPT = C / RSTEP, BATCH = RPT <= 4 ? RPT : 2;
   static_assert(NTH % 32 == 0 && C % RSTEP == 0 && RPT % BATCH == 0, "rows per thread");
   const Chunk<CF>& in = STAGED ? *src : ch;
@@ -406,6 +408,26 @@ __device__ void prep_chunk(Chunk<CF>& ch, const Chunk<CF>* src = nullptr) {
   const int L = ch.L;
   ch.m = L >= C ? C / 2 : (((L - 1) / 2) & ~15);
   const int c0 = (threadIdx.x & 15) * 8, rt = threadIdx.x >> 4;
+  // staged: the rows still in HBM (iso beta, diag kappa) are requested before
+  // the wait for the staged ones, so that both latencies overlap
+  float pb[STAGED && CF::ISO ? RPT : 1], pk[STAGED && !CF::ISO ? RPT : 1][8];
+  if constexpr (STAGED) {
+#pragma unroll
+    for (int j = 0; j < RPT; ++j) {
+      const int r = rt + j * RSTEP;
+      if constexpr (CF::ISO) {
+        pb[j] = r < L ? in.beta[(size_t)r * in.ldb] : 0.f;
+      } else {
+        if (r < L) {
+          ld8(pk[j], in.kap + (size_t)r * in.ldk + c0);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) pk[j][i] = 0.f;
+        }
+      }
+    }
+    mbar_wait(staged_bar, 0, status);
+  }
   float gm[8], gl[8];
   ld8(gm, in.g + (size_t)ch.m * in.ldr + c0);
   ld8(gl, in.g + (size_t)(L - 1) * in.ldr + c0);
@@ -449,7 +471,23 @@ __device__ void prep_chunk(Chunk<CF>& ch, const Chunk<CF>* src = nullptr) {
     for (int j = 0; j < RPT; ++j) {
       const int r = rt + j * RSTEP;
       RawRow<CF> x;
-      load_row(x, in, r, c0);
+      if (r < L) {
+        const size_t o = (size_t)r * in.ldr + c0;
+        ld8(x.g, in.g + o);
+        x.kp = *reinterpret_cast<const uint4*>(in.k + o);
+        x.qp = *reinterpret_cast<const uint4*>(in.q + o);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x.g[i] = 0.f;
+        x.kp = x.qp = make_uint4(0, 0, 0, 0);
+      }
+      if constexpr (CF::ISO) {
+        x.beta = pb[j];
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x.kap[i] = pk[j][i];
+        x.beta = 1.f;
+      }
       float qs, ks, kr[8], qr[8], kc[8];
       row_scales(x, r, qs, ks);
       make_operands(ch, r, x, gm, gm, qs, ks, kr, qr, kc);

@@ -186,14 +186,13 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
     tma_load_4d(base + Lo::sq, &maps.q, 0, h, t0, b, stbar);
     issue_loads();
   }
-  mbar_wait(stbar, 0, p.status);
   {
     Chunk<CF> src = ch;
     src.g = reinterpret_cast<const float*>(base + Lo::sg);
     src.k = reinterpret_cast<const bf16*>(base + Lo::sk);
     src.q = reinterpret_cast<const bf16*>(base + Lo::sq);
     src.ldr = kKD;
-    prep_chunk<CF, 512, true, true>(ch, &src);
+    prep_chunk<CF, 512, true, true>(ch, &src, stbar, p.status);
   }
   if constexpr (!CF::ISO) {
     // the fp32 cotangent rounded to bf16 into the swizzled operand tile (rows

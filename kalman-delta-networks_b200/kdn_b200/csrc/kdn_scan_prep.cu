@@ -100,13 +100,12 @@ __global__ void __launch_bounds__(kPrepThreads, 2) scan_prep_kernel(ScanParams p
       tma_load_4d(base + Lo::raw_g, &maps.g, 0, h, t0, b, bar);
     }
     __syncthreads();  // the barrier's initialisation is visible before anyone waits on it
-    mbar_wait(bar, 0, p.status);
     Chunk<CF> src = ch;
     src.k = reinterpret_cast<const bf16*>(base + Lo::raw_k);
     src.q = reinterpret_cast<const bf16*>(base + Lo::raw_q);
     src.g = reinterpret_cast<const float*>(base + Lo::raw_g);
     src.ldr = kKD;
-    prep_chunk<CF, kPrepThreads, false, true>(ch, &src);
+    prep_chunk<CF, kPrepThreads, false, true>(ch, &src, bar, p.status);
     __syncthreads();
     zero_upper_blocks<CF>(sQb);  // over the raw g rows, dead now
     zero_upper_blocks<CF>(sTb);
