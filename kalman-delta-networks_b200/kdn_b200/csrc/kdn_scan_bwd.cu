@@ -241,7 +241,7 @@ struct StateTcLayout {
   static constexpr size_t stage = align_up(dO + (size_t)C * (DF32 ? 256 : 128), 1024);
   static constexpr size_t dOb = NS * stage;  // diag: the bf16-rounded operand [C][64]
   static constexpr size_t DS = dOb + (DF32 ? align_up((size_t)C * 128, 1024) : 0);  // [KD][64] (also dh)
-  static constexpr size_t DD = DS + (size_t)kKD * 128;                               // ddelta [C][64]
+  static constexpr size_t DD = DS + (size_t)kKD * 128;                               // ddelta^T [64][C]
   static constexpr size_t bar = DD + align_up((size_t)C * 128, 1024);
   static constexpr size_t bytes = bar + 128 + 1024;
 };
@@ -359,15 +359,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_bwd_state_tc_kernel(ScanPa
     mbar_wait(mmab, mph, p.status);
     mph ^= 1;
     tc::fence_after();
+    // ddelta^T (value row vc, lanes < 16) -> bf16 operand tile [64][C]
 #pragma unroll
     for (int j = 0; j < HC; j += 16) {
       float x[16];
       tc::ld16(tl + TD + HC * hf + j, x);
-      if (lane < 16) {
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-          *reinterpret_cast<bf16*>(sDD + tc::sw_off(HC * hf + j + i, vc, C)) = __float2bfloat16_rn(x[i]);
-      }
+      if (lane < 16) tc::st_row16(sDD, 64, vc, HC * hf + j, x, 1.f);
     }
     if (threadIdx.x == 32) bulk_wait_read<0>();  // dh has left the adjoint operand (rewritten next chunk)
     tc::wait_st();
@@ -376,11 +373,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_bwd_state_tc_kernel(ScanPa
     bar_sync(1, NTH);
     if (threadIdx.x == 0) {
       tc::fence_after();
-      constexpr uint32_t ids = tc::idesc(128, 64, true, true), idn = tc::idesc(128, 64, true, true, true);
+      constexpr uint32_t ids = tc::idesc(128, 64, true, true), idn = tc::idesc(128, 64, true, false, true);
       for (int ks = 0; ks < C / 16; ++ks)
         tc::mma(tmem + TS, tc::desc_mn(st + (R::Qs - R::bwd_begin), C, ks), tc::desc_mn(sdO, C, ks), ids, true);
       for (int ks = 0; ks < C / 16; ++ks)
-        tc::mma(tmem + TS, tc::desc_mn(st + (R::Wf - R::bwd_begin), C, ks), tc::desc_mn(sDD, C, ks), idn, true);
+        tc::mma(tmem + TS, tc::desc_mn(st + (R::Wf - R::bwd_begin), C, ks), tc::desc_k(sDD, 64, ks), idn, true);
       tc::commit(&empty[s]);
       tc::commit(mmab);
     }

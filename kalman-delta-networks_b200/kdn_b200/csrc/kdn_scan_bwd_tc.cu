@@ -42,16 +42,17 @@ struct ChunkTcLayout {
   static constexpr size_t Kr = 0, Qr = 16384, Kc = 32768, T = 49152, Xs = 57344;  // Xs: 8 KB scratch
   // the record tiles Qt, Wf and the delta tiles
   static constexpr size_t G = 65536;
-  // Qt | delta | Wf, then ddelta over Wf once the delta products are done
+  // Qt | delta^T | Wf, then ddelta^T over Wf once the delta products are done
+  // (delta^T, ddelta^T: [128 values][C tokens], 128 rows of one 64-column block)
   static constexpr size_t Qt = G, Wf = G + 8192 + 16384;
   static constexpr size_t Del = G + 8192, DDel = Wf;
   // v | dO, then the dv rows, then the raw k | q rows of the gate mapping
   static constexpr size_t V = G + 40960;
   static constexpr size_t vv = V, dO = V + 16384, dvst = V, rk = V, rq = V + 16384;
   static constexpr size_t rg = G;  // raw g rows [C][KD] fp32 over delta | ddelta
-  // the raw q, k, g rows of the operand build, staged by TMA with the other
-  // inputs (g under Kr | Qr, k under Kc, q under delta; read before any of
-  // those tiles is written); the diagonal variant's kappa rows stay in HBM
+  // isotropic: the raw q, k, g rows of the operand build, staged by TMA with
+  // the other inputs (g under Kr | Qr, k under Kc, q under delta; read before
+  // any of those tiles is written)
   static constexpr size_t sg = Kr, sk = Kc, sq = Del;
   // S0 | dS (saved states), then dW dQ dQu dT X dA
   static constexpr size_t A = V + 32768;
@@ -127,7 +128,7 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
   // before the first wait (one barrier would then have moved two phases on)
   uint64_t* ddbar = ldbar + 3;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(ldbar + 4);
-  uint64_t* stbar = ldbar + 5;  // the staged raw rows
+  uint64_t* stbar = ldbar + 5;  // the staged raw rows (isotropic)
   float* small = reinterpret_cast<float*>(base + Lo::small);
   float* cfl = small + small_floats<CF>();
   float* cgl = cfl + kKD;
@@ -177,22 +178,29 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
       tma_load_4d(base + Lo::dO + C * 128, &maps.dO, 64, h, t0, b, ldbar);
     }
   };
-  // every input in flight at once: the raw rows on their own barrier, so the
-  // operand build starts as soon as they have landed
-  if (threadIdx.x == 0) {
-    mbar_expect_tx(stbar, C * kKD * 8);
-    tma_load_4d(base + Lo::sg, &maps.g, 0, h, t0, b, stbar);
-    tma_load_4d(base + Lo::sk, &maps.k, 0, h, t0, b, stbar);
-    tma_load_4d(base + Lo::sq, &maps.q, 0, h, t0, b, stbar);
-    issue_loads();
-  }
-  {
+  if constexpr (CF::ISO) {
+    // every input in flight at once: the raw rows on their own barrier, so the
+    // operand build starts as soon as they have landed
+    if (threadIdx.x == 0) {
+      mbar_expect_tx(stbar, C * kKD * 8);
+      tma_load_4d(base + Lo::sg, &maps.g, 0, h, t0, b, stbar);
+      tma_load_4d(base + Lo::sk, &maps.k, 0, h, t0, b, stbar);
+      tma_load_4d(base + Lo::sq, &maps.q, 0, h, t0, b, stbar);
+      issue_loads();
+    }
     Chunk<CF> src = ch;
     src.g = reinterpret_cast<const float*>(base + Lo::sg);
     src.k = reinterpret_cast<const bf16*>(base + Lo::sk);
     src.q = reinterpret_cast<const bf16*>(base + Lo::sq);
     src.ldr = kKD;
     prep_chunk<CF, 512, true, true>(ch, &src, stbar, p.status);
+  } else {
+    // diagonal: the operand build from the rows in HBM first, then the bulk
+    // copies (its kappa rows and fp32 cotangent also come through the threads,
+    // and staging q, k, g measured slower here: 0.807 against 0.842 ms for
+    // kdn_scan_bwd at config 2)
+    prep_chunk<CF, 512, true>(ch);
+    if (threadIdx.x == 0) issue_loads();
   }
   if constexpr (!CF::ISO) {
     // the fp32 cotangent rounded to bf16 into the swizzled operand tile (rows
@@ -222,6 +230,7 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
     __syncthreads();
   };
 
+  float xrow[16];
   // ---- A: delta^T, then ddelta^T (lane = value channel).  The delta products
   // run while the threads scale dS in place (dS'' = fL dS, so Kc replaces
   // the record's Kf = fL Kc); the ddelta products run while they read delta
@@ -256,13 +265,9 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
     tc::commit(ddbar);
   }
   mma_wait();  // delta^T done: S0 and Wf are free
-  {
-    const int v = 32 * q + lane;
-    float x[16];
-    tc::ld16(tq + TDEL + 16 * cg, x);
-#pragma unroll
-    for (int i = 0; i < 16; ++i) *at(Lo::Del, 16 * cg + i, v, C) = __float2bfloat16_rn(x[i]);
-  }
+  // delta^T -> bf16 tile [128 values][C tokens]: row v, 16 tokens per thread
+  tc::ld16(tq + TDEL + 16 * cg, xrow);
+  tc::st_row16(base + Lo::Del, kVD, 32 * q + lane, 16 * cg, xrow, 1.f);
   // S0' = fr S0 in place, cgl = sum_v S0' dS''  (a half-warp per key row)
   for (int e = threadIdx.x; e < kKD * 16; e += 512) {
     const int r = e >> 4, g = e & 15;
@@ -284,29 +289,25 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
   }
   mbar_wait(ddbar, 0, p.status);  // ddelta^T done
   tc::fence_after();
-  {
-    const int v = 32 * q + lane;
-    float x[16];
-    tc::ld16(tq + TDD + 16 * cg, x);
-#pragma unroll
-    for (int i = 0; i < 16; ++i) *at(Lo::DDel, 16 * cg + i, v, C) = __float2bfloat16_rn(x[i]);
-  }
+  tc::ld16(tq + TDD + 16 * cg, xrow);
+  tc::st_row16(base + Lo::DDel, kVD, 32 * q + lane, 16 * cg, xrow, 1.f);
   publish();
 
   // ---- B
   if (threadIdx.x == 0) {
     tc::fence_after();
-    constexpr uint32_t id_dv = tc::idesc(64, 128, true, true);
+    // Del, DDel hold delta^T, ddelta^T [values][tokens]
+    constexpr uint32_t id_dv = tc::idesc(64, 128, true, false);
     for (int ks = 0; ks < C / 16; ++ks)
-      tc::mma(tmem + TDV, tc::desc_mn(base + Lo::T, C, ks), tc::desc_mn(base + Lo::DDel, C, ks), id_dv, ks > 0);
-    constexpr uint32_t id_kc = tc::idesc(128, C, false, false);
-    constexpr uint32_t id_cc = tc::idesc(64, C, false, false);
+      tc::mma(tmem + TDV, tc::desc_mn(base + Lo::T, C, ks), tc::desc_k(base + Lo::DDel, kVD, ks), id_dv, ks > 0);
+    constexpr uint32_t id_kc = tc::idesc(128, C, false, false), id_kt = tc::idesc(128, C, false, true);
+    constexpr uint32_t id_ct = tc::idesc(64, C, false, true), id_tc = tc::idesc(64, C, true, false);
     for (int ks = 0; ks < kVD / 16; ++ks) {
       tc::mma(tmem + TQR, tc::desc_k(base + Lo::S0, kKD, ks), tc::desc_k(base + Lo::dO, C, ks), id_kc, ks > 0);
-      tc::mma(tmem + TW, tc::desc_k(base + Lo::S0, kKD, ks), tc::desc_k(base + Lo::DDel, C, ks), id_kc, ks > 0);
-      tc::mma(tmem + TKC, tc::desc_k(base + Lo::dS, kKD, ks), tc::desc_k(base + Lo::Del, C, ks), id_kc, ks > 0);
-      tc::mma(tmem + TDQ, tc::desc_k(base + Lo::dO, C, ks), tc::desc_k(base + Lo::Del, C, ks), id_cc, ks > 0);
-      tc::mma(tmem + TDT, tc::desc_k(base + Lo::DDel, C, ks), tc::desc_k(base + Lo::vv, C, ks), id_cc, ks > 0);
+      tc::mma(tmem + TW, tc::desc_k(base + Lo::S0, kKD, ks), tc::desc_mn(base + Lo::DDel, kVD, ks), id_kt, ks > 0);
+      tc::mma(tmem + TKC, tc::desc_k(base + Lo::dS, kKD, ks), tc::desc_mn(base + Lo::Del, kVD, ks), id_kt, ks > 0);
+      tc::mma(tmem + TDQ, tc::desc_k(base + Lo::dO, C, ks), tc::desc_mn(base + Lo::Del, kVD, ks), id_ct, ks > 0);
+      tc::mma(tmem + TDT, tc::desc_mn(base + Lo::DDel, kVD, ks), tc::desc_k(base + Lo::vv, C, ks), id_tc, ks > 0);
     }
     tc::commit(mmab);
   }

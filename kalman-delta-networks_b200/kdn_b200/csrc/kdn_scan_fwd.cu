@@ -220,7 +220,7 @@ struct FwdTcLayout {
   static constexpr size_t v = R::fwd_end;  // [C][64] bf16, swizzled by the TMA engine
   static constexpr size_t stage = align_up(v + (size_t)C * 128, 1024);
   static constexpr size_t S = NS * stage;                 // state operand [KD][64] bf16 (also h)
-  static constexpr size_t Del = S + (size_t)kKD * 128;    // delta [C][64] bf16
+  static constexpr size_t Del = S + (size_t)kKD * 128;    // delta^T [64][C] bf16
   static constexpr size_t O = Del + (size_t)C * 128;      // output rows [C][64] (bf16 iso, fp32 diag)
   static constexpr size_t O_bytes = (size_t)C * 64 * (CF::ISO ? 2 : 4);
   static constexpr size_t bar = O + align_up(O_bytes, 1024);
@@ -342,16 +342,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_fwd_tc_kernel(ScanParams p
     mbar_wait(mmab, mph, p.status);
     mph ^= 1;
     tc::fence_after();
-    // delta (value column vc, lanes < 16) -> bf16 operand tile [C][64]
+    // delta^T (value row vc, lanes < 16) -> bf16 operand tile [64][C], 16 tokens
+    // per two 16-byte stores
 #pragma unroll
     for (int j = 0; j < HC; j += 16) {
       float x[16];
       tc::ld16(tl + TD + HC * hf + j, x);
-      if (lane < 16) {
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-          *reinterpret_cast<bf16*>(sDel + tc::sw_off(HC * hf + j + i, vc, C)) = __float2bfloat16_rn(x[i]);
-      }
+      if (lane < 16) tc::st_row16(sDel, 64, vc, HC * hf + j, x, 1.f);
     }
     if (threadIdx.x == 32) bulk_wait_read<0>();  // h has left the state operand (rewritten next chunk)
     tc::wait_st();
@@ -360,13 +357,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_fwd_tc_kernel(ScanParams p
     bar_sync(1, NTH);
     if (threadIdx.x == 0) {
       tc::fence_after();
-      constexpr uint32_t ido = tc::idesc(64, C, true, false), ids = tc::idesc(128, 64, true, true);
+      constexpr uint32_t ido = tc::idesc(64, C, true, false), idd = tc::idesc(64, C, false, false);
+      constexpr uint32_t ids = tc::idesc(128, 64, true, false);
       for (int ks = 0; ks < kKD / 16; ++ks)
         tc::mma(tmem + TO, tc::desc_mn(sS, kKD, ks), tc::desc_k(st + R::Qs, C, ks), ido, ks > 0);
       for (int ks = 0; ks < C / 16; ++ks)
-        tc::mma(tmem + TO, tc::desc_mn(sDel, C, ks), tc::desc_k(st + R::Qq, C, ks), ido, true);
+        tc::mma(tmem + TO, tc::desc_k(sDel, 64, ks), tc::desc_k(st + R::Qq, C, ks), idd, true);
       for (int ks = 0; ks < C / 16; ++ks)
-        tc::mma(tmem + TS, tc::desc_mn(st + R::Kf, C, ks), tc::desc_mn(sDel, C, ks), ids, true);
+        tc::mma(tmem + TS, tc::desc_mn(st + R::Kf, C, ks), tc::desc_k(sDel, 64, ks), ids, true);
       tc::commit(&empty[s]);
       tc::commit(mmab);
     }
