@@ -39,7 +39,7 @@ FLOPS_PER_TH = 540_672  # 3 * 2 * (3 d^2 + 5 C d), C = 64
 # DRAM bytes (read + write) per token-head of one kdn_scan_bwd call (reverse
 # sweep + chunk kernel): ncu dram__bytes_read.sum + dram__bytes_write.sum of
 # the two kernels at B=1 T=4096 H=18, divided by its 73,728 token-heads
-SCAN_BWD_TRAFFIC_PER_TH = {"iso": 5830, "diag": None}
+SCAN_BWD_TRAFFIC_PER_TH = {"iso": 5410, "diag": None}
 
 
 def load_peaks():
