@@ -54,7 +54,7 @@ struct ChunkTcLayout {
   // the other inputs (g under Kr | Qr, k under Kc, q under delta; read before
   // any of those tiles is written)
   static constexpr size_t sg = Kr, sk = Kc, sq = Del;
-  // S0 | dS (saved states), then dW dQ dQu dT X dA
+  // S0 | dS (saved states), then dW^T dQ dQu dT X dA
   static constexpr size_t A = V + 32768;
   static constexpr size_t S0 = A, dS = A + 32768;
   static constexpr size_t dW = A, dQ = A + 16384, dQu = A + 24576, dT = A + 32768, X = A + 40960, dA = A + 49152;
@@ -330,12 +330,12 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
         st8(dvst + m * kVD + 32 * cg + j + 8, y);
       }
     }
-    // dW = -(S0' ddelta^T)^T  (lane = key)
+    // dW = -(S0' ddelta^T)^T (lane = key), stored as dW^T [128 keys][C tokens]:
+    // row key, 16 tokens per thread
     const int key = 32 * q + lane;
     float x[16];
     tc::ld16(tq + TW + 16 * cg, x);
-#pragma unroll
-    for (int i = 0; i < 16; ++i) *at(Lo::dW, 16 * cg + i, key, C) = __float2bfloat16_rn(-x[i]);
+    tc::st_row16(base + Lo::dW, kKD, key, 16 * cg, x, -1.f);
     // cfl[key] = sum_j Kc[j][key] (delta dS''^T)[j][key]
     tc::ld16(tq + TKC + 16 * cg, x);
     float part = 0.f;
@@ -360,12 +360,12 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
   // ---- C: dKr^T = dW^T T (T read MN-major as the transposed operand), dT += dW Kr^T
   if (threadIdx.x == 0) {
     tc::fence_after();
-    constexpr uint32_t id_kr = tc::idesc(128, C, true, true);
+    constexpr uint32_t id_kr = tc::idesc(128, C, false, true);
     for (int ks = 0; ks < C / 16; ++ks)
-      tc::mma(tmem + TKR, tc::desc_mn(base + Lo::dW, C, ks), tc::desc_mn(base + Lo::T, C, ks), id_kr, ks > 0);
-    constexpr uint32_t id_cc = tc::idesc(64, C, false, false);
+      tc::mma(tmem + TKR, tc::desc_k(base + Lo::dW, kKD, ks), tc::desc_mn(base + Lo::T, C, ks), id_kr, ks > 0);
+    constexpr uint32_t id_cc = tc::idesc(64, C, true, false);
     for (int ks = 0; ks < kKD / 16; ++ks)
-      tc::mma(tmem + TDT, tc::desc_k(base + Lo::dW, C, ks), tc::desc_k(base + Lo::Kr, C, ks), id_cc, true);
+      tc::mma(tmem + TDT, tc::desc_mn(base + Lo::dW, kKD, ks), tc::desc_k(base + Lo::Kr, C, ks), id_cc, true);
     tc::commit(mmab);
     // the delta tiles are dead: the raw g rows of the gate mapping come back meanwhile
     mbar_expect_tx(rawbar, C * kKD * 8);
