@@ -280,6 +280,59 @@ def time_region(fn, steps, device):
     return start.elapsed_time(stop) / steps
 
 
+# algorithmic bytes per token-head of the isotropic gate frontend with bf16
+# g_raw / omega_r_raw: fwd reads g_raw (2K) and omega_r_raw (4), writes
+# g_cumsum (4K) and a, omega, r (12); bwd reads g_raw (2K), dg_pre (4K), da,
+# domega, dr (12), omega_r_raw (4) and writes dg_raw (2K), domega_r_raw (4)
+GATE_BYTES_PER_TH = {"fwd": 6 * D + 16, "bwd": 8 * D + 20}
+
+
+def frontend_times(device, hbm, reps=20):
+    """Device time of the isotropic gate frontend's C-ABI calls
+    (kdn_iso_gate_fwd / kdn_iso_gate_bwd, the kernels behind
+    _iso_kdn_gate_precumsum_paired) at the bench shape, bf16 g_raw and
+    omega_r_raw, every buffer allocated up front; CUDA events on the launching
+    stream.  Inputs (≈0.2 GB) are larger than L2."""
+    from kdn_b200 import _native as N
+
+    lib = N.load_library()
+    g = torch.Generator(device=device).manual_seed(99)
+    g_raw = torch.randn(B, T, H, D, generator=g, device=device).bfloat16()
+    wr = torch.randn(B, T, 2 * H, generator=g, device=device).bfloat16()
+    params = [torch.randn(n, generator=g, device=device) * 0.5 for n in (H, H, H, H * D, H)]
+    f32 = dict(dtype=torch.float32, device=device)
+    g_cumsum = torch.empty(B, T, H, D, **f32)
+    a, omega, r = (torch.empty(B, T, H, **f32) for _ in range(3))
+    ip = torch.empty(H, **f32)
+    dg_pre = torch.randn(B, T, H, D, generator=g, device=device)
+    da, dw, dr = (torch.randn(B, T, H, generator=g, device=device) for _ in range(3))
+    dip = torch.randn(H, generator=g, device=device)
+    dg_raw, dwr = torch.empty_like(g_raw), torch.empty_like(wr)
+    pg = [torch.empty(n, **f32) for n in (H, H, H, H * D, H)]
+    ws = N.byte_buffer(lib.kdn_iso_gate_workspace_bytes(B, T, H, D), device)
+    stream = N.stream_of(g_raw)
+    head = (g_raw.data_ptr(), 1, wr.data_ptr(), 1, wr.stride(0), wr.stride(1), *(t.data_ptr() for t in params))
+
+    def fwd():
+        N.check(lib.kdn_iso_gate_fwd(*head, g_cumsum.data_ptr(), a.data_ptr(), omega.data_ptr(), r.data_ptr(),
+                                     ip.data_ptr(), B, T, H, D, 1e-3, 0.01, stream), "kdn_iso_gate_fwd")
+
+    def bwd():
+        N.check(lib.kdn_iso_gate_bwd(*head, dg_pre.data_ptr(), da.data_ptr(), dw.data_ptr(), dr.data_ptr(),
+                                     dip.data_ptr(), dg_raw.data_ptr(), dwr.data_ptr(), *(t.data_ptr() for t in pg),
+                                     B, T, H, D, ws.data_ptr(), ws.numel(), stream), "kdn_iso_gate_bwd")
+
+    fwd()
+    bwd()
+    fms, bms = time_region(fwd, reps, device), time_region(bwd, reps, device)
+    th = B * T * H
+    fgb = GATE_BYTES_PER_TH["fwd"] * th / (fms * 1e-3) / 1e9
+    bgb = GATE_BYTES_PER_TH["bwd"] * th / (bms * 1e-3) / 1e9
+    return {"op": "_iso_kdn_gate_precumsum_paired (bf16 g_raw, omega_r_raw)", "fwd_ms": fms, "bwd_ms": bms,
+            "bound": "hbm", "unit": "GB/s", "fwd_achieved": fgb, "bwd_achieved": bgb, "peak": hbm,
+            "fwd_frac": fgb / hbm, "bwd_frac": bgb / hbm}
+
+
 def per_op_times(variant, x, device, reps=10):
     """Device time of the scan's two C-ABI calls, kdn_scan_fwd (chunk-record
     pass + sequential pass) and kdn_scan_bwd (reverse state sweep +
@@ -577,6 +630,8 @@ def main():
         "roofline": roofline,
         "clocks": clocks,
     }
+    if args.variant == "iso" and not args.varlen:
+        out["frontend"] = frontend_times(device, hbm)
     if rank == 0 and world == 1 and not args.no_cpu and not args.varlen:
         out["cpu_baseline"] = cpu_baseline(args.variant)
     if rank == 0:

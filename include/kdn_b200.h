@@ -68,6 +68,52 @@ int kdn_iso_gain_fwd(const float* a, const float* omega, const float* r,
                      int64_t T, int64_t H, float posterior_scale,
                      void* workspace, size_t workspace_bytes,
                      kdn_stream_t stream);
+
+/* ------------------------------------------------------------------------ *
+ * Isotropic gate frontend.  Replaces the launches behind
+ * _iso_kdn_gate_precumsum_paired (lit_gpt/kdn_ops/iso_kdn_chunk.py:1396):
+ * _iso_kdn_gate_precumsum_fwd (1059) and _iso_kdn_gate_precumsum_bwd (1116).
+ *
+ *   g = -exp(A_log[h]) softplus(g_raw + dt_bias[h*K + k]);
+ *   g_cumsum = log2(e) * (64-token-chunk-local inclusive prefix of g)  [B,T,H,K] fp32
+ *   a = mean_k exp(2 g);  omega = omega_min + softplus(omega_r_raw[..., h] + omega_bias[h]);
+ *   r = r_min + softplus(omega_r_raw[..., H + h] + r_bias[h])            [B,T,H] fp32
+ *   initial_precision = 0.1 + softplus(initial_precision_param)          [H] fp32
+ *
+ * g_raw [B,T,H,K] contiguous, bf16 (g_raw_bf16 = 1) or fp32; omega_r_raw
+ * [B,T,2H] bf16 or fp32 with element strides (stride_b, stride_t, 1); the five
+ * parameter vectors fp32 (dt_bias [H*K]).  K is 64 or 128; B or T may be 0.
+ * The backward takes the memory scan's gate cotangent dg_pre_reverse (fp32
+ * [B,T,H,K], natural-log coordinates before the reverse prefix) and da,
+ * domega, dr ([B,T,H]), d_initial_precision ([H]); every cotangent is
+ * nullable (= zero), and every output is nullable (= not requested).  dg_raw
+ * has g_raw's dtype; domega_r_raw ([B,T,2H] contiguous) has omega_r_raw's
+ * dtype; the parameter gradients are fp32 and overwritten.  Workspace:
+ * kdn_iso_gate_workspace_bytes(B, T, H, K) bytes (per-chunk partial sums,
+ * reduced in a fixed order).
+ * ------------------------------------------------------------------------ */
+size_t kdn_iso_gate_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t K);
+int kdn_iso_gate_fwd(const void* g_raw, int g_raw_bf16, const void* omega_r_raw,
+                     int omega_r_raw_bf16, int64_t omega_r_stride_b,
+                     int64_t omega_r_stride_t, const float* omega_bias,
+                     const float* r_bias, const float* A_log, const float* dt_bias,
+                     const float* initial_precision_param, float* g_cumsum,
+                     float* a, float* omega, float* r, float* initial_precision,
+                     int64_t B, int64_t T, int64_t H, int64_t K, float omega_min,
+                     float r_min, kdn_stream_t stream);
+int kdn_iso_gate_bwd(const void* g_raw, int g_raw_bf16, const void* omega_r_raw,
+                     int omega_r_raw_bf16, int64_t omega_r_stride_b,
+                     int64_t omega_r_stride_t, const float* omega_bias,
+                     const float* r_bias, const float* A_log, const float* dt_bias,
+                     const float* initial_precision_param,
+                     const float* dg_pre_reverse, const float* da,
+                     const float* domega, const float* dr,
+                     const float* d_initial_precision, void* dg_raw,
+                     void* domega_r_raw, float* domega_bias, float* dr_bias,
+                     float* dA_log, float* ddt_bias,
+                     float* d_initial_precision_param, int64_t B, int64_t T,
+                     int64_t H, int64_t K, void* workspace,
+                     size_t workspace_bytes, kdn_stream_t stream);
 int kdn_iso_gain_bwd(const float* a, const float* omega, const float* r,
                      const float* initial_precision, const float* initial_cov,
                      const float* dgain, const float* p_prev,

@@ -73,6 +73,17 @@ _SIGNATURES = {
         [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _F, _P, _SZ, _P],
         ctypes.c_int,
     ),
+    "kdn_iso_gate_workspace_bytes": ([_I64, _I64, _I64, _I64], _SZ),
+    "kdn_iso_gate_fwd": (
+        [_P, ctypes.c_int, _P, ctypes.c_int, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+         _I64, _I64, _I64, _I64, _F, _F, _P],
+        ctypes.c_int,
+    ),
+    "kdn_iso_gate_bwd": (
+        [_P, ctypes.c_int, _P, ctypes.c_int, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+         _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _SZ, _P],
+        ctypes.c_int,
+    ),
     "kdn_diag_gain_carry_elems": ([_I64, _I64, _I64, _I64], _I64),
     "kdn_diag_gain_workspace_bytes": ([_I64, _I64, _I64, _I64], _SZ),
     "kdn_diag_gain_fwd": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _SZ, _P], ctypes.c_int),

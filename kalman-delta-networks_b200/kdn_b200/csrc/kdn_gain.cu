@@ -304,44 +304,6 @@ int iso_grid(const char* what, int64_t B, int64_t T, int64_t H, void* ws, size_t
 // ---------------------------------------------------------------------------
 // Diagonal gain
 // ---------------------------------------------------------------------------
-// Lane l ends with the warp sum of v[l % N] (N = 8, 16 or 32): a butterfly
-// that halves the values exchanged at every step.
-template <int N>
-__device__ __forceinline__ float transpose_reduce(float (&v)[N]) {
-  const int lane = threadIdx.x & 31;
-#pragma unroll
-  for (int off = N / 2; off >= 1; off >>= 1) {
-    const bool upper = lane & off;
-#pragma unroll
-    for (int i = 0; i < off; ++i) {
-      const float send = upper ? v[i] : v[i + off];
-      const float keep = upper ? v[i + off] : v[i];
-      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-    }
-  }
-  float s = v[0];
-#pragma unroll
-  for (int o = N; o < 32; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  return s;
-}
-
-// Sum of v[j] over all K threads of the block for each of N tokens; result in
-// out[j] (shared) after the second barrier.
-template <int K, int N>
-__device__ __forceinline__ void block_token_sums(float (&v)[N], float* red /* [K/32][N] */, float* out /* [N] */) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const float s = transpose_reduce<N>(v);
-  if (lane < N) red[warp * N + lane] = s;
-  __syncthreads();
-  if (threadIdx.x < N) {
-    float acc = 0.f;
-#pragma unroll
-    for (int w = 0; w < K / 32; ++w) acc += red[w * N + threadIdx.x];
-    out[threadIdx.x] = acc;
-  }
-  __syncthreads();
-}
-
 // One channel's inputs for TT consecutive tokens of a segment.  The loads of a
 // tile do not depend on the running covariance, so each kernel issues the next
 // tile before it runs the current one: the memory latency overlaps the

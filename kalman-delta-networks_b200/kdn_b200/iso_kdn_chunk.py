@@ -1,7 +1,8 @@
 """Isotropic KDN operators on B200: drop-in replacements for
 
-* ``iso_kdn_gain``                (lit_gpt/kdn_ops/iso_kdn_chunk.py:1966)
-* ``_chunk_kda_precumsum_paired`` (lit_gpt/kdn_ops/iso_kdn_chunk.py:2242)
+* ``_iso_kdn_gate_precumsum_paired`` (lit_gpt/kdn_ops/iso_kdn_chunk.py:1396)
+* ``iso_kdn_gain``                   (lit_gpt/kdn_ops/iso_kdn_chunk.py:1966)
+* ``_chunk_kda_precumsum_paired``    (lit_gpt/kdn_ops/iso_kdn_chunk.py:2242)
 
 with the reference's signatures, validation messages, tensor layouts and
 autograd contract.  Both run on the sm_100a kernels of ``libkdn_b200.so``;
@@ -247,4 +248,164 @@ def _chunk_kda_precumsum_paired(
     return _ChunkKDAPrecumsumFunction.apply(q, k, v, g_cumsum, beta, scale)
 
 
-__all__ = ("_chunk_kda_precumsum_paired", "iso_kdn_gain")
+# ----------------------------------------------------------------------------- gate frontend
+
+
+def _validate_iso_gate_inputs(g_raw, omega_r_raw, omega_bias, r_bias, A_log, dt_bias, initial_precision_param,
+                              omega_min, r_min):
+    """The reference's checks and messages (iso_kdn_chunk.py:1012-1056)."""
+    if g_raw.ndim != 4:
+        raise ValueError(f"g_raw must have shape [B,T,H,K], got {tuple(g_raw.shape)}")
+    B, T, H, K = g_raw.shape
+    if K == 0:
+        raise ValueError("g_raw's K dimension must be nonzero")
+    if omega_r_raw.shape != (B, T, 2 * H):
+        raise ValueError(f"omega_r_raw must have shape {(B, T, 2 * H)}, got {tuple(omega_r_raw.shape)}")
+    if omega_r_raw.stride(-1) != 1:
+        raise ValueError(f"omega_r_raw's head dimension must be contiguous, got strides={omega_r_raw.stride()}")
+    for name, value in (("omega_bias", omega_bias), ("r_bias", r_bias)):
+        if value.shape != (H,):
+            raise ValueError(f"{name} must have shape [{H}], got {tuple(value.shape)}")
+    if A_log.shape != (H,):
+        raise ValueError(f"A_log must have shape [{H}], got {tuple(A_log.shape)}")
+    if dt_bias.shape != (H * K,):
+        raise ValueError(f"dt_bias must have shape [{H * K}], got {tuple(dt_bias.shape)}")
+    if initial_precision_param.shape != (H,):
+        raise ValueError(f"initial_precision_param must have shape [{H}], got {tuple(initial_precision_param.shape)}")
+    inputs = (g_raw, omega_r_raw, omega_bias, r_bias, A_log, dt_bias, initial_precision_param)
+    if not all(value.is_cuda for value in inputs):
+        raise ValueError("_iso_kdn_gate_precumsum_paired is a CUDA-only op")
+    if any(value.device != g_raw.device for value in inputs[1:]):
+        raise ValueError("all scalar-preparation inputs must be on the same CUDA device")
+    for name, value in (("g_raw", g_raw), ("omega_r_raw", omega_r_raw)):
+        if value.dtype not in (torch.bfloat16, torch.float32):
+            raise TypeError(f"{name} must be bf16 or fp32, got {value.dtype}")
+    if any(value.dtype != torch.float32 for value in (omega_bias, r_bias, A_log, dt_bias, initial_precision_param)):
+        raise TypeError("omega_bias, r_bias, A_log, dt_bias, and initial_precision_param must be FP32")
+    for name, value in (("omega_min", omega_min), ("r_min", r_min)):
+        if not isinstance(value, (int, float)):
+            raise TypeError(f"{name} must be a Python scalar, got {type(value).__name__}")
+        if not math.isfinite(float(value)):
+            raise ValueError(f"{name} must be finite, got {value!r}")
+    if K not in (64, 128):
+        raise ValueError(f"g_raw's K dimension must be 64 or 128 on this backend, got {K}")
+    return B, T, H, K
+
+
+def _gate_common(g_raw, omega_r_raw):
+    return (g_raw.data_ptr() if g_raw.numel() else None, int(g_raw.dtype == torch.bfloat16),
+            omega_r_raw.data_ptr() if omega_r_raw.numel() else None, int(omega_r_raw.dtype == torch.bfloat16),
+            omega_r_raw.stride(0), omega_r_raw.stride(1))
+
+
+def _iso_gate_forward(g_raw, omega_r_raw, omega_bias, r_bias, A_log, dt_bias, initial_precision_param, omega_min,
+                      r_min):
+    B, T, H, K = g_raw.shape
+    lib = N.load_library()
+    dev = g_raw.device
+    g_cumsum = torch.empty((B, T, H, K), dtype=torch.float32, device=dev)
+    a = torch.empty((B, T, H), dtype=torch.float32, device=dev)
+    omega = torch.empty_like(a)
+    r = torch.empty_like(a)
+    initial_precision = torch.empty((H,), dtype=torch.float32, device=dev)
+    N.check(
+        lib.kdn_iso_gate_fwd(
+            *_gate_common(g_raw, omega_r_raw), omega_bias.data_ptr(), r_bias.data_ptr(), A_log.data_ptr(),
+            dt_bias.data_ptr(), initial_precision_param.data_ptr(), N.ptr(g_cumsum) if g_cumsum.numel() else None,
+            N.ptr(a) if a.numel() else None, N.ptr(omega) if a.numel() else None, N.ptr(r) if a.numel() else None,
+            initial_precision.data_ptr(), B, T, H, K, float(omega_min), float(r_min), N.stream_of(g_raw),
+        ),
+        "kdn_iso_gate_fwd",
+    )
+    return g_cumsum, a, omega, r, initial_precision
+
+
+def _iso_gate_backward(g_raw, omega_r_raw, omega_bias, r_bias, A_log, dt_bias, initial_precision_param,
+                       dg_pre_reverse, da, domega, dr, d_initial_precision, needs):
+    B, T, H, K = g_raw.shape
+    lib = N.load_library()
+    (need_dg_raw, need_domega_r_raw, need_domega_bias, need_dr_bias, need_dA_log, need_ddt_bias,
+     need_d_param) = needs
+    dev = g_raw.device
+
+    def cot(x, shape):
+        if x is None:
+            return None
+        if x.shape != shape:
+            raise ValueError(f"cotangent must have shape {shape}, got {tuple(x.shape)}")
+        return x.float().contiguous()
+
+    dg_pre_reverse = cot(dg_pre_reverse, (B, T, H, K))
+    da, domega, dr = (cot(x, (B, T, H)) for x in (da, domega, dr))
+    d_initial_precision = cot(d_initial_precision, (H,))
+    dg_raw = torch.empty_like(g_raw) if need_dg_raw else None
+    domega_r_raw = torch.empty(omega_r_raw.shape, dtype=omega_r_raw.dtype, device=dev) if need_domega_r_raw else None
+    f32 = dict(dtype=torch.float32, device=dev)
+    domega_bias = torch.empty((H,), **f32) if need_domega_bias else None
+    dr_bias = torch.empty((H,), **f32) if need_dr_bias else None
+    dA_log = torch.empty((H,), **f32) if need_dA_log else None
+    ddt_bias = torch.empty((H * K,), **f32) if need_ddt_bias else None
+    d_param = torch.empty((H,), **f32) if need_d_param else None
+    ws = N.byte_buffer(lib.kdn_iso_gate_workspace_bytes(B, T, H, K), dev)
+    nz = lambda t: t.data_ptr() if t is not None and t.numel() else None  # noqa: E731
+    N.check(
+        lib.kdn_iso_gate_bwd(
+            *_gate_common(g_raw, omega_r_raw), omega_bias.data_ptr(), r_bias.data_ptr(), A_log.data_ptr(),
+            dt_bias.data_ptr(), initial_precision_param.data_ptr(), nz(dg_pre_reverse), nz(da), nz(domega), nz(dr),
+            nz(d_initial_precision), nz(dg_raw), nz(domega_r_raw), nz(domega_bias), nz(dr_bias), nz(dA_log),
+            nz(ddt_bias), nz(d_param), B, T, H, K, ws.data_ptr(), ws.numel(), N.stream_of(g_raw),
+        ),
+        "kdn_iso_gate_bwd",
+    )
+    return dg_raw, domega_r_raw, domega_bias, dr_bias, dA_log, ddt_bias, d_param
+
+
+class _IsoKDNGatePrecumsumFunction(torch.autograd.Function):
+    """Autograd contract of the reference's Function (iso_kdn_chunk.py:1317-1393)."""
+
+    @staticmethod
+    def forward(ctx, g_raw, omega_r_raw, omega_bias, r_bias, A_log, dt_bias, initial_precision_param, omega_min,
+                r_min):
+        outs = _iso_gate_forward(g_raw, omega_r_raw, omega_bias, r_bias, A_log, dt_bias, initial_precision_param,
+                                 omega_min, r_min)
+        ctx.save_for_backward(g_raw, omega_r_raw, omega_bias, r_bias, A_log, dt_bias, initial_precision_param)
+        ctx.set_materialize_grads(False)
+        return outs
+
+    @staticmethod
+    def backward(ctx, dg_pre_reverse, da, domega, dr, d_initial_precision):
+        g_raw, omega_r_raw, omega_bias, r_bias, A_log, dt_bias, param = ctx.saved_tensors
+        grads = _iso_gate_backward(g_raw, omega_r_raw, omega_bias, r_bias, A_log, dt_bias, param, dg_pre_reverse,
+                                   da, domega, dr, d_initial_precision, ctx.needs_input_grad[:7])
+        return (*grads, None, None)
+
+
+@torch.compiler.disable
+def _iso_kdn_gate_precumsum_paired(
+    g_raw: torch.Tensor,
+    omega_r_raw: torch.Tensor,
+    omega_bias: torch.Tensor,
+    r_bias: torch.Tensor,
+    A_log: torch.Tensor,
+    dt_bias: torch.Tensor,
+    initial_precision_param: torch.Tensor,
+    omega_min: float,
+    r_min: float,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Return the paired ``(base2_prefix, a, omega, r, initial_precision)`` tensors
+    (iso_kdn_chunk.py:1396-1431).
+
+    ``base2_prefix`` (the 64-token-chunk-local base-2 gate prefix) must have
+    exactly one consumer, ``_chunk_kda_precumsum_paired``: the two Functions
+    exchange the gate cotangent in natural-log coordinates before the reverse
+    prefix sum, not a generic tensor VJP.
+    """
+    _validate_iso_gate_inputs(g_raw, omega_r_raw, omega_bias, r_bias, A_log, dt_bias, initial_precision_param,
+                              omega_min, r_min)
+    return _IsoKDNGatePrecumsumFunction.apply(
+        g_raw.contiguous(), omega_r_raw, omega_bias.contiguous(), r_bias.contiguous(), A_log.contiguous(),
+        dt_bias.contiguous(), initial_precision_param.contiguous(), float(omega_min), float(r_min),
+    )
+
+
+__all__ = ("_chunk_kda_precumsum_paired", "_iso_kdn_gate_precumsum_paired", "iso_kdn_gain")

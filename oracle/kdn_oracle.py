@@ -37,6 +37,9 @@ __all__ = (
     "scan_grads",
     "make_iso_inputs",
     "make_diag_inputs",
+    "iso_gate",
+    "iso_gate_grads",
+    "make_iso_gate_inputs",
 )
 
 LN2 = math.log(2.0)
@@ -326,3 +329,74 @@ def make_diag_inputs(B, T, H, K=128, V=128, seed=0, decay_scale=1.0):
         "initial_precision": torch.ones(H),
         "dO": dO,
     }
+
+
+# ----------------------------------------------------------------------------
+# Isotropic gate frontend (iso_kdn_chunk.py:740-953, the scalar preparation in
+# front of the gain and the memory scan).  softplus is the definition the
+# reference calls (flash-linear-attention 0.5.1, fla/ops/utils/softplus.py):
+# x above 20, else ln(1 + e^x).
+# ----------------------------------------------------------------------------
+
+def _softplus_fla(x):
+    return torch.where(x > 20.0, x, torch.log1p(torch.exp(torch.clamp(x, max=20.0))))
+
+
+def iso_gate(g_raw, omega_r_raw, omega_bias, r_bias, A_log, dt_bias, initial_precision_param, omega_min, r_min,
+             chunk=64):
+    """``(g_cumsum, a, omega, r, initial_precision)`` of the gate frontend
+    (iso_kdn_chunk.py:786-814): g = -exp(A_log) softplus(g_raw + dt_bias), its
+    chunk-local inclusive prefix times log2(e), a = mean_k exp(2 g), omega and r
+    from the two halves of omega_r_raw, initial_precision = 0.1 + softplus."""
+    B, T, H, K = g_raw.shape
+    x = g_raw + dt_bias.view(1, 1, H, K)
+    g = -torch.exp(A_log).view(1, 1, H, 1) * _softplus_fla(x)
+    pad = (-T) % chunk
+    gp = torch.nn.functional.pad(g, (0, 0, 0, 0, 0, pad))
+    g_cumsum = gp.view(B, (T + pad) // chunk, chunk, H, K).cumsum(2).view(B, T + pad, H, K)[:, :T] / LN2
+    a = torch.exp(2.0 * g).mean(-1)
+    omega = omega_min + _softplus_fla(omega_r_raw[..., :H] + omega_bias)
+    r = r_min + _softplus_fla(omega_r_raw[..., H:] + r_bias)
+    initial_precision = 0.1 + _softplus_fla(initial_precision_param)
+    return g_cumsum, a, omega, r, initial_precision
+
+
+def iso_gate_grads(inputs, cotangents, omega_min, r_min, dtype=torch.float64):
+    """Forward outputs and the seven parameter gradients of the gate frontend
+    under the paired-cotangent contract (iso_kdn_chunk.py:817-953): the
+    g_cumsum cotangent arrives as ``dg_pre_reverse`` in natural-log coordinates
+    before the reverse chunk prefix, i.e. ``dL/dg_cumsum = ln(2) dg_pre``.
+    ``inputs``: g_raw, omega_r_raw, omega_bias, r_bias, A_log, dt_bias,
+    initial_precision_param; ``cotangents``: dg_pre_reverse, da, domega, dr,
+    d_initial_precision (None = zero).  Returns (outputs, grads)."""
+    leaves = [t.detach().to(dtype).clone().requires_grad_(True) for t in inputs]
+    outs = iso_gate(*leaves, omega_min, r_min)
+    loss = 0.0
+    for i, (o, c) in enumerate(zip(outs, cotangents)):
+        if c is None:
+            continue
+        c = c.to(dtype)
+        if i == 0:
+            c = c * LN2
+        loss = loss + (o * c).sum()
+    grads = torch.autograd.grad(loss, leaves, allow_unused=True)
+    grads = [torch.zeros_like(l) if g is None else g for l, g in zip(leaves, grads)]
+    return [o.detach() for o in outs], grads
+
+
+def make_iso_gate_inputs(B, T, H, K=128, seed=0, g_dtype=torch.float32, wr_dtype=torch.float32):
+    """Seeded inputs and cotangents of the gate frontend on CPU (fp32 unless
+    the dtypes say otherwise; the parameters always fp32)."""
+    gen = torch.Generator().manual_seed(seed)
+    n = lambda *s: torch.randn(*s, generator=gen)  # noqa: E731
+    inputs = (
+        n(B, T, H, K).to(g_dtype),
+        n(B, T, 2 * H).to(wr_dtype),
+        n(H) * 0.5,
+        n(H) * 0.5,
+        n(H) * 0.5 - 1.0,
+        n(H * K) * 0.5,
+        n(H),
+    )
+    cotangents = (n(B, T, H, K), n(B, T, H), n(B, T, H), n(B, T, H), n(H))
+    return inputs, cotangents

@@ -118,3 +118,37 @@ def test_g_cumsum_roundtrip():
         g = oracle.g_cumsum_from_log_alpha(la, chunk)
         alpha = oracle.alpha_from_g_cumsum(g * oracle.LN2, chunk)
         close(alpha.log(), la, rtol=1e-12, atol=1e-12)
+
+
+GATE_INPUTS = ("g_raw", "omega_r_raw", "omega_bias", "r_bias", "A_log", "dt_bias", "param")
+GATE_COTANGENTS = ("dg_pre", "da", "domega", "dr", "dinit")
+GATE_OUTPUTS = ("g_cumsum", "a", "omega", "r", "initial_precision")
+GATE_GRADS = ("dg_raw", "domega_r_raw", "domega_bias", "dr_bias", "dA_log", "ddt_bias", "dparam")
+
+
+def gate_case(d, ci):
+    """Inputs, cotangents, scalars and the reference's outputs / gradients of
+    one case of ``iso_gate.npz`` (the reference's Triton gate kernels run under
+    Triton's CPU interpreter, ``tests/golden/make_gate_golden.py``)."""
+    p = f"c{ci}_"
+    B, T, H, K, gbf, wbf, wmin, rmin = d[p + "meta"].tolist()
+    inputs = [d[p + n] for n in GATE_INPUTS]
+    cot = [d[p + n] for n in GATE_COTANGENTS]
+    outs = [d[p + n] for n in GATE_OUTPUTS]
+    grads = [d[p + n] for n in GATE_GRADS]
+    return inputs, cot, float(wmin), float(rmin), bool(gbf), bool(wbf), outs, grads
+
+
+@pytest.mark.parametrize("ci", [0, 1])
+def test_iso_gate_matches_reference(ci):
+    d = load("iso_gate")
+    inputs, cot, wmin, rmin, gbf, wbf, ref_outs, ref_grads = gate_case(d, ci)
+    outs, grads = oracle.iso_gate_grads(inputs, cot, wmin, rmin)
+    # the reference evaluates in fp32: agreement to fp32 rounding
+    for o, r in zip(outs, ref_outs):
+        close(o, r, rtol=1e-5, atol=1e-5 * r.abs().max().item())
+    for name, g, r in zip(GATE_GRADS, grads, ref_grads):
+        # dg_raw / domega_r_raw carry the input's dtype: bf16 rounding in the bf16 case
+        bf = (name == "dg_raw" and gbf) or (name == "domega_r_raw" and wbf)
+        tol = 8e-3 if bf else 1e-5
+        close(g, r, rtol=tol, atol=tol * r.abs().max().item())
