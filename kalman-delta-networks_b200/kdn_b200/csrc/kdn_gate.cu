@@ -118,8 +118,9 @@ __global__ void __launch_bounds__(K / 2, 1024 / K) iso_gate_fwd_kernel(GateArgs 
         }
       }
       // a = channel mean of exp(2 g): lane j of each warp sums token j0 + j
+      static_assert(N <= 32, "one token per lane");
       const float ws = transpose_reduce<N>(al);
-      red[warp * N + lane] = ws;
+      if (lane < N) red[warp * N + lane] = ws;  // lanes >= N repeat lane % N
       __syncthreads();
       if (tid < N && j0 + tid < n) {
         float sum = 0.f;
@@ -250,33 +251,56 @@ __global__ void __launch_bounds__(K / 2, 1024 / K) iso_gate_bwd_kernel(GateArgs 
   if (bc == 0 && tid == 0 && d.d_param) d.d_param[h] = d.d_init ? d.d_init[h] * sigmoid_(g.param[h]) : 0.f;
 }
 
-// out[i] = sum over the NP partial rows of part[row][i] (rows of `width`), for
-// the outputs that are requested; one thread per output element.
-__global__ void gate_reduce_kernel(const float* __restrict__ part_dt, float* __restrict__ ddt, int wdt,
-                                   const float* __restrict__ part_A, float* __restrict__ dA, int wA,
-                                   const float* __restrict__ part_wr, float* __restrict__ dwb, float* __restrict__ drb,
-                                   int H, int NP) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < wdt) {
-    if (ddt) {
-      float s = 0.f;
-      for (int p = 0; p < NP; ++p) s += part_dt[(size_t)p * wdt + i];
-      ddt[i] = s;
-    }
-  } else if (i < wdt + wA) {
-    const int j = i - wdt;
-    if (dA) {
-      float s = 0.f;
-      for (int p = 0; p < NP; ++p) s += part_A[(size_t)p * wA + j];
-      dA[j] = s;
-    }
-  } else if (i < wdt + wA + 2 * H) {
-    const int j = i - wdt - wA;
-    float* out = j < H ? dwb : drb;
-    if (out) {
-      float s = 0.f;
-      for (int p = 0; p < NP; ++p) s += part_wr[(size_t)p * 2 * H + j];
-      out[j < H ? j : j - H] = s;
+// out[i] = sum over the NP partial rows of part[row][i] (rows of `width`
+// floats), for the requested outputs.  A CTA sums 32 consecutive outputs
+// (lanes: consecutive addresses) with 8 row groups (warps) of NP / 8 rows
+// each, then adds the 8 group sums in a fixed order.
+constexpr int kRedCols = 32, kRedGroups = 8;
+__device__ __forceinline__ void reduce_cols(const float* __restrict__ part, float* __restrict__ out, int width,
+                                            int col, int NP, float (*sh)[kRedCols]) {
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  float s = 0.f;
+  if (col < width)
+#pragma unroll 4
+    for (int p = ty; p < NP; p += kRedGroups) s += part[(size_t)p * width + col];
+  sh[ty][tx] = s;
+  __syncthreads();
+  if (ty == 0 && col < width) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < kRedGroups; ++w) t += sh[w][tx];
+    out[col] = t;
+  }
+}
+// blockIdx.x: column blocks of ddt (H*K), then of dA (H), then of the two bias
+// gradients (2H, one row of the omega / r partials)
+__global__ void __launch_bounds__(kRedCols * kRedGroups) gate_reduce_kernel(
+    const float* __restrict__ part_dt, float* __restrict__ ddt, int wdt, const float* __restrict__ part_A,
+    float* __restrict__ dA, int wA, const float* __restrict__ part_wr, float* __restrict__ dwb,
+    float* __restrict__ drb, int H, int NP) {
+  __shared__ float sh[kRedGroups][kRedCols];
+  const int nb_dt = (wdt + kRedCols - 1) / kRedCols, nb_A = (wA + kRedCols - 1) / kRedCols;
+  const int blk = blockIdx.x, tx = threadIdx.x & 31;
+  if (blk < nb_dt) {
+    if (ddt) reduce_cols(part_dt, ddt, wdt, blk * kRedCols + tx, NP, sh);
+  } else if (blk < nb_dt + nb_A) {
+    if (dA) reduce_cols(part_A, dA, wA, (blk - nb_dt) * kRedCols + tx, NP, sh);
+  } else if (dwb || drb) {
+    // [NP][2H] partials: omega-bias columns first, then r-bias columns
+    const int col = (blk - nb_dt - nb_A) * kRedCols + tx;
+    const int ty = threadIdx.x >> 5;
+    float s = 0.f;
+    if (col < 2 * H)
+#pragma unroll 4
+      for (int p = ty; p < NP; p += kRedGroups) s += part_wr[(size_t)p * 2 * H + col];
+    sh[ty][tx] = s;
+    __syncthreads();
+    if (ty == 0 && col < 2 * H) {
+      float t = 0.f;
+#pragma unroll
+      for (int w = 0; w < kRedGroups; ++w) t += sh[w][tx];
+      float* out = col < H ? dwb : drb;
+      if (out) out[col < H ? col : col - H] = t;
     }
   }
 }
@@ -371,9 +395,10 @@ int kdn_iso_gate_bwd(const void* g_raw, int g_raw_bf16, const void* omega_r_raw,
     iso_gate_bwd_kernel<64, float><<<grid, 32, 0, st>>>(g, d);
   if (int rc = check_launch("iso_gate_bwd_kernel")) return rc;
   if (ddt_bias || dA_log || need_wr) {
-    const int wdt = (int)(H * K), wA = (int)H, total = wdt + wA + 2 * (int)H;
-    gate_reduce_kernel<<<(total + 255) / 256, 256, 0, st>>>(part_dt, ddt_bias, wdt, part_A, dA_log, wA, part_wr,
-                                                            domega_bias, dr_bias, (int)H, NP);
+    const int wdt = (int)(H * K), wA = (int)H;
+    const int blocks = (wdt + kRedCols - 1) / kRedCols + (wA + kRedCols - 1) / kRedCols + (2 * (int)H + kRedCols - 1) / kRedCols;
+    gate_reduce_kernel<<<blocks, kRedCols * kRedGroups, 0, st>>>(part_dt, ddt_bias, wdt, part_A, dA_log, wA, part_wr,
+                                                                 domega_bias, dr_bias, (int)H, NP);
     return check_launch("gate_reduce_kernel");
   }
   return KDN_OK;
