@@ -75,7 +75,6 @@ __device__ __forceinline__ float2 ld2(const float* p) { return *reinterpret_cast
 __device__ __forceinline__ float gate_of(float x, float negA) {
   return x > 20.f ? negA * x : (negA * kLn2) * __log2f(1.f + ex2a(x * kLog2e));
 }
-__device__ __forceinline__ float sigmoid_fast(float x) { return __fdividef(1.f, 1.f + ex2a(-x * kLog2e)); }
 
 template <int K, class GT>
 __global__ void __launch_bounds__(K / 2, 1024 / K) iso_gate_fwd_kernel(GateArgs g, float omega_min, float r_min,
@@ -175,30 +174,37 @@ __global__ void __launch_bounds__(K / 2, 1024 / K) iso_gate_bwd_kernel(GateArgs 
     for (int j0 = C - N; j0 >= 0; j0 -= N) {
       float2 x[N], dp[N];
       float dav[N];
+      {
+        const size_t off = (size_t)j0 * rs;
+        const GT* px = src + off;
+        const float* pd = dps ? dps + off : nullptr;
+        const float* pa = d.da ? d.da + row0 + (size_t)j0 * g.H : nullptr;
 #pragma unroll
-      for (int j = 0; j < N; ++j) {
-        const int t = j0 + j;
-        const size_t off = (size_t)t * rs;
-        x[j] = t < n ? ld2(src + off) : make_float2(0.f, 0.f);
-        dp[j] = (t < n && dps) ? ld2(dps + off) : make_float2(0.f, 0.f);
-        dav[j] = (t < n && d.da) ? d.da[row0 + (size_t)t * g.H] : 0.f;
+        for (int j = 0; j < N; ++j, px += rs) {
+          const bool in = j0 + j < n;
+          x[j] = in ? ld2(px) : make_float2(0.f, 0.f);
+          dp[j] = (in && pd) ? ld2(pd + (size_t)j * rs) : make_float2(0.f, 0.f);
+          dav[j] = (in && pa) ? pa[(size_t)j * g.H] * (2.f / (float)K) : 0.f;
+        }
       }
+      GT* po = dgr_out ? dgr_out + (size_t)(j0 + N - 1) * rs : nullptr;
 #pragma unroll
-      for (int j = N - 1; j >= 0; --j) {
-        const int t = j0 + j;
-        if (t < n) {
+      for (int j = N - 1; j >= 0; --j, po -= rs) {
+        if (j0 + j < n) {
+          // e = e^x, u = 1 + e: softplus(x) = ln u, sigmoid(x) = e / u
           const float xb0 = x[j].x + bias.x, xb1 = x[j].y + bias.y;
-          const float g0 = gate_of(xb0, negA), g1 = gate_of(xb1, negA);
+          const float e0 = ex2a(xb0 * kLog2e), e1 = ex2a(xb1 * kLog2e);
+          const float u0 = 1.f + e0, u1 = 1.f + e1;
+          const float g0 = xb0 > 20.f ? negA * xb0 : (negA * kLn2) * __log2f(u0);
+          const float g1 = xb1 > 20.f ? negA * xb1 : (negA * kLn2) * __log2f(u1);
+          const float s0 = xb0 > 20.f ? 1.f : __fdividef(e0, u0);
+          const float s1 = xb1 > 20.f ? 1.f : __fdividef(e1, u1);
           acc0 += dp[j].x;
           acc1 += dp[j].y;
-          float dg0 = acc0, dg1 = acc1;
-          if (d.da) {
-            const float w = dav[j] * (2.f / (float)K);
-            dg0 += w * ex2a(2.f * kLog2e * g0);
-            dg1 += w * ex2a(2.f * kLog2e * g1);
-          }
-          const float r0 = dg0 * negA * sigmoid_fast(xb0), r1 = dg1 * negA * sigmoid_fast(xb1);
-          if (dgr_out) st_pair(dgr_out + (size_t)t * rs, r0, r1);
+          const float dg0 = fmaf(dav[j], ex2a(2.f * kLog2e * g0), acc0);
+          const float dg1 = fmaf(dav[j], ex2a(2.f * kLog2e * g1), acc1);
+          const float r0 = dg0 * negA * s0, r1 = dg1 * negA * s1;
+          if (po) st_pair(po, r0, r1);
           dA_acc = fmaf(dg0, g0, fmaf(dg1, g1, dA_acc));
           ddt0 += r0;
           ddt1 += r1;
