@@ -333,6 +333,57 @@ def frontend_times(device, hbm, reps=20):
             "fwd_frac": fgb / hbm, "bwd_frac": bgb / hbm}
 
 
+# algorithmic bytes per token-head of the diagonal frontend (bf16 inputs, f32
+# outputs and cotangents): fwd reads retention_raw, omega_raw (2K each) and
+# r_raw (2), writes g_cumsum, alpha, omega (4K each) and r (4); bwd reads
+# retention_raw, omega_raw (2K each), r_raw (2), d_g_cumsum, d_alpha, d_omega
+# (4K each) and d_r (4), writes dretention_raw, domega_raw (2K each) and
+# dr_raw (2)
+DIAG_GATE_BYTES_PER_TH = {"fwd": 16 * D + 6, "bwd": 20 * D + 8}
+
+
+def diag_frontend_times(device, hbm, reps=20):
+    """Device time of the diagonal frontend's C-ABI calls (kdn_diag_gate_fwd /
+    kdn_diag_gate_bwd, the kernels behind _diag_kdn_frontend_precumsum_paired)
+    at the bench shape with every cotangent present and every gradient asked
+    for; buffers allocated up front; CUDA events on the launching stream.
+    Inputs (≈0.4 GB) are larger than L2."""
+    from kdn_b200 import _native as N
+
+    lib = N.load_library()
+    g = torch.Generator(device=device).manual_seed(98)
+    bthk, bth = (B, T, H, D), (B, T, H)
+    rn = lambda *s: torch.randn(*s, generator=g, device=device)  # noqa: E731
+    ret, wraw, rraw = (rn(*bthk) * 2).bfloat16(), rn(*bthk).bfloat16(), rn(*bth).bfloat16()
+    A_log = torch.log(torch.rand(H, generator=g, device=device) * 19 + 1)
+    dt_bias, param = rn(H, D) * 0.5 - 4.0, rn(H)
+    f32 = dict(dtype=torch.float32, device=device)
+    outs = [torch.empty(*bthk, **f32) for _ in range(3)] + [torch.empty(*bth, **f32), torch.empty(H, **f32)]
+    cots = [rn(*bthk) for _ in range(3)] + [rn(*bth), rn(H)]
+    grads = [torch.empty_like(ret), torch.empty_like(wraw), torch.empty_like(rraw), torch.empty(H, **f32),
+             torch.empty(H, D, **f32), torch.empty(H, **f32)]
+    ws = N.byte_buffer(lib.kdn_diag_gate_workspace_bytes(B, T, H, D), device)
+    stream = N.stream_of(ret)
+    head = tuple(t.data_ptr() for t in (ret, wraw, rraw, A_log, dt_bias, param))
+
+    def fwd():
+        N.check(lib.kdn_diag_gate_fwd(*head, *(t.data_ptr() for t in outs), B, T, H, D, stream), "kdn_diag_gate_fwd")
+
+    def bwd():
+        N.check(lib.kdn_diag_gate_bwd(*head, *(t.data_ptr() for t in cots), *(t.data_ptr() for t in grads),
+                                      B, T, H, D, ws.data_ptr(), ws.numel(), stream), "kdn_diag_gate_bwd")
+
+    fwd()
+    bwd()
+    fms, bms = time_region(fwd, reps, device), time_region(bwd, reps, device)
+    th = B * T * H
+    fgb = DIAG_GATE_BYTES_PER_TH["fwd"] * th / (fms * 1e-3) / 1e9
+    bgb = DIAG_GATE_BYTES_PER_TH["bwd"] * th / (bms * 1e-3) / 1e9
+    return {"op": "_diag_kdn_frontend_precumsum_paired", "fwd_ms": fms, "bwd_ms": bms, "bound": "hbm",
+            "unit": "GB/s", "fwd_achieved": fgb, "bwd_achieved": bgb, "peak": hbm, "fwd_frac": fgb / hbm,
+            "bwd_frac": bgb / hbm}
+
+
 def per_op_times(variant, x, device, reps=10):
     """Device time of the scan's two C-ABI calls, kdn_scan_fwd (chunk-record
     pass + sequential pass) and kdn_scan_bwd (reverse state sweep +
@@ -630,8 +681,8 @@ def main():
         "roofline": roofline,
         "clocks": clocks,
     }
-    if args.variant == "iso" and not args.varlen:
-        out["frontend"] = frontend_times(device, hbm)
+    if not args.varlen:
+        out["frontend"] = (frontend_times if args.variant == "iso" else diag_frontend_times)(device, hbm)
     if rank == 0 and world == 1 and not args.no_cpu and not args.varlen:
         out["cpu_baseline"] = cpu_baseline(args.variant)
     if rank == 0:

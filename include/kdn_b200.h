@@ -114,6 +114,40 @@ int kdn_iso_gate_bwd(const void* g_raw, int g_raw_bf16, const void* omega_r_raw,
                      float* d_initial_precision_param, int64_t B, int64_t T,
                      int64_t H, int64_t K, void* workspace,
                      size_t workspace_bytes, kdn_stream_t stream);
+
+/*
+ * Diagonal gate / noise frontend, 32-token chunks.  Replaces
+ * _diag_kdn_frontend_precumsum_paired (lit_gpt/kdn_ops/diag_kdn_chunk.py:2471):
+ * forward = _frozen_frontend_diag_frontend_fwd_kernel (:1867) as launched by
+ * _diag_kdn_frontend_forward (:2218); backward = _diag_kdn_frontend_backward
+ * (:2265) with its alpha-presence, reduction and local VJP kernels
+ * (:1908-1966, :1969).
+ * retention_raw, omega_raw: bf16 [B,T,H,K]; r_raw: bf16 [B,T,H]; A_log,
+ * initial_precision_param: f32 [H]; dt_bias: f32 [H,K]; all contiguous.
+ * Outputs g_cumsum, alpha, omega: f32 [B,T,H,K]; r: f32 [B,T,H];
+ * initial_precision: f32 [H].  Cotangents are f32 and contiguous, each may be
+ * NULL (absent); gradient outputs may be NULL (not needed), but domega_raw,
+ * dr_raw and d_initial_precision_param need their cotangent.  dretention_raw,
+ * domega_raw, dr_raw are bf16 like their inputs.  The backward needs
+ * kdn_diag_gate_workspace_bytes(B, T, H, K) bytes of workspace.
+ */
+size_t kdn_diag_gate_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t K);
+int kdn_diag_gate_fwd(const void* retention_raw, const void* omega_raw,
+                      const void* r_raw, const float* A_log, const float* dt_bias,
+                      const float* initial_precision_param, float* g_cumsum,
+                      float* alpha, float* omega, float* r,
+                      float* initial_precision, int64_t B, int64_t T, int64_t H,
+                      int64_t K, kdn_stream_t stream);
+int kdn_diag_gate_bwd(const void* retention_raw, const void* omega_raw,
+                      const void* r_raw, const float* A_log, const float* dt_bias,
+                      const float* initial_precision_param,
+                      const float* d_g_cumsum, const float* d_alpha,
+                      const float* d_omega, const float* d_r,
+                      const float* d_initial_precision, void* dretention_raw,
+                      void* domega_raw, void* dr_raw, float* dA_log,
+                      float* ddt_bias, float* d_initial_precision_param,
+                      int64_t B, int64_t T, int64_t H, int64_t K, void* workspace,
+                      size_t workspace_bytes, kdn_stream_t stream);
 int kdn_iso_gain_bwd(const float* a, const float* omega, const float* r,
                      const float* initial_precision, const float* initial_cov,
                      const float* dgain, const float* p_prev,

@@ -3,7 +3,8 @@
 Drop-in operators with the reference ``lit_gpt.kdn_ops`` signatures:
 
 * ``kdn_b200.iso_kdn_chunk``: ``iso_kdn_gain``, ``_chunk_kda_precumsum_paired``
-* ``kdn_b200.diag_kdn_chunk``: ``_diag_kdn_gain``, ``chunk_kalman``
+* ``kdn_b200.diag_kdn_chunk``: ``_diag_kdn_gain``, ``chunk_kalman``,
+  ``_diag_kdn_frontend_precumsum_paired``
 
 The compute runs in ``lib/libkdn_b200.so`` (C ABI, ``include/kdn_b200.h``).
 """

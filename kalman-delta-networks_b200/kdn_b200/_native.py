@@ -84,6 +84,9 @@ _SIGNATURES = {
          _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _SZ, _P],
         ctypes.c_int,
     ),
+    "kdn_diag_gate_workspace_bytes": ([_I64, _I64, _I64, _I64], _SZ),
+    "kdn_diag_gate_fwd": ([_P] * 11 + [_I64, _I64, _I64, _I64, _P], ctypes.c_int),
+    "kdn_diag_gate_bwd": ([_P] * 17 + [_I64, _I64, _I64, _I64, _P, _SZ, _P], ctypes.c_int),
     "kdn_diag_gain_carry_elems": ([_I64, _I64, _I64, _I64], _I64),
     "kdn_diag_gain_workspace_bytes": ([_I64, _I64, _I64, _I64], _SZ),
     "kdn_diag_gain_fwd": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _SZ, _P], ctypes.c_int),

@@ -311,6 +311,180 @@ __global__ void __launch_bounds__(kRedCols * kRedGroups) gate_reduce_kernel(
   }
 }
 
+// ---------------------------------------------------------------------------
+// Diagonal frontend: _diag_kdn_frontend_precumsum_paired
+// (lit_gpt/kdn_ops/diag_kdn_chunk.py:2471; kernels 1867-2051), 32-token chunks:
+//   x = retention_raw + dt_bias[h, k],  ell = -exp(A_log[h]) softplus(x),
+//   alpha = exp(ell),  ell_mem = ln max(alpha, 1e-6) (NaN passes),
+//   g_cumsum = log2(e) * (inclusive prefix of ell_mem over the chunk),
+//   omega = softplus(omega_raw),  r = 0.01 + softplus(r_raw),
+//   initial_precision = 0.1 + softplus(param)
+// Backward: mc = reverse prefix of d_g_cumsum (natural-log coordinates) over
+// the chunk; dell = [alpha >= 1e-6] mc + d_alpha alpha (= (mc / alpha +
+// d_alpha) alpha); dretention_raw = dell (-exp(A_log)) sigmoid(x);
+// dA_log = sum dell ell; ddt_bias = sum_{b,t} dretention_raw;
+// domega_raw = d_omega sigmoid(omega_raw); dr_raw = d_r sigmoid(r_raw);
+// d_param = d_initial_precision sigmoid(param).  alpha is recomputed from
+// retention_raw, so the backward needs no saved output.
+constexpr int kDiagGateChunk = 32;
+constexpr float kAlphaFloor = 1e-6f;
+
+struct DiagGateArgs {
+  const bf16 *ret, *wraw, *rraw;
+  const float *A_log, *dt_bias, *param;
+  int T, H, NT;
+};
+
+// Forward: CTA = (b, 32-token chunk, h), K / 2 threads with two channels
+// each; 8 tokens of retention_raw and omega_raw are loaded per pass.
+template <int K>
+__global__ void __launch_bounds__(K / 2, 1024 / K) diag_gate_fwd_kernel(DiagGateArgs g, float* __restrict__ g_cumsum,
+                                                                        float* __restrict__ alpha,
+                                                                        float* __restrict__ omega,
+                                                                        float* __restrict__ r,
+                                                                        float* __restrict__ init_prec) {
+  constexpr int C = kDiagGateChunk, N = 8, NTH = K / 2;
+  const int bc = blockIdx.x / g.H, h = blockIdx.x - bc * g.H, tid = threadIdx.x, k0 = 2 * tid;
+  const int b = g.NT ? bc / g.NT : 0, c = g.NT ? bc - b * g.NT : 0;
+  const int t0 = c * C, n = min(C, g.T - t0);
+  const size_t row0 = ((size_t)b * g.T + t0) * g.H + h;
+  const size_t rs = (size_t)g.H * K;
+  if (n > 0) {
+    const float negA = -expf(g.A_log[h]);
+    const float log_floor = logf(kAlphaFloor);
+    const float2 bias = ld2(g.dt_bias + (size_t)h * K + k0);
+    const size_t e0 = row0 * K + k0;
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll 1
+    for (int j0 = 0; j0 < C; j0 += N) {
+      float2 x[N], z[N];
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        const bool in = j0 + j < n;
+        const size_t e = e0 + (size_t)(j0 + j) * rs;
+        x[j] = in ? ld2(g.ret + e) : make_float2(0.f, 0.f);
+        z[j] = in ? ld2(g.wraw + e) : make_float2(0.f, 0.f);
+      }
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        if (j0 + j < n) {
+          const size_t e = e0 + (size_t)(j0 + j) * rs;
+          const float l0 = gate_of(x[j].x + bias.x, negA), l1 = gate_of(x[j].y + bias.y, negA);
+          const float a0 = ex2a(l0 * kLog2e), a1 = ex2a(l1 * kLog2e);
+          s0 += a0 < kAlphaFloor ? log_floor : l0;  // a NaN alpha keeps its NaN ell
+          s1 += a1 < kAlphaFloor ? log_floor : l1;
+          st_pair(g_cumsum + e, s0 * kLog2e, s1 * kLog2e);
+          st_pair(alpha + e, a0, a1);
+          st_pair(omega + e, softplus_fla(z[j].x), softplus_fla(z[j].y));
+        }
+      }
+    }
+    for (int t = tid; t < n; t += NTH)
+      r[row0 + (size_t)t * g.H] = 0.01f + softplus_fla(__bfloat162float(g.rraw[row0 + (size_t)t * g.H]));
+  }
+  if (bc == 0 && tid == 0) init_prec[h] = 0.1f + softplus_fla(g.param[h]);
+}
+
+struct DiagGateGrads {
+  const float *d_gc, *d_alpha, *d_omega, *d_r, *d_init;  // nullable cotangents (contiguous)
+  bf16 *dret, *domega_raw, *dr_raw;                      // nullable outputs, bf16 like the inputs
+  float *part_A, *part_dt, *d_param;                     // nullable
+};
+
+// Backward: same CTA map as the forward; the chunk is walked from its last
+// token down in passes of 8 tokens carrying the reverse prefix of d_g_cumsum.
+// dA_log / ddt_bias leave per-CTA partial sums, summed by gate_reduce_kernel.
+template <int K>
+__global__ void __launch_bounds__(K / 2, 1024 / K) diag_gate_bwd_kernel(DiagGateArgs g, DiagGateGrads d) {
+  constexpr int C = kDiagGateChunk, N = 8, NTH = K / 2, NW = NTH / 32;
+  __shared__ float red[NW];
+  const int bc = blockIdx.x / g.H, h = blockIdx.x - bc * g.H, tid = threadIdx.x, k0 = 2 * tid;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int b = g.NT ? bc / g.NT : 0, c = g.NT ? bc - b * g.NT : 0;
+  const int t0 = c * C, n = min(C, g.T - t0);
+  const size_t row0 = ((size_t)b * g.T + t0) * g.H + h;
+  const size_t rs = (size_t)g.H * K;
+  const size_t e0 = row0 * K + k0;
+  float dA_acc = 0.f, ddt0 = 0.f, ddt1 = 0.f;
+  if (n > 0 && (d.d_gc || d.d_alpha) && (d.dret || d.part_A || d.part_dt)) {
+    const float negA = -expf(g.A_log[h]);
+    const float2 bias = ld2(g.dt_bias + (size_t)h * K + k0);
+    float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll 1
+    for (int j0 = C - N; j0 >= 0; j0 -= N) {
+      if (j0 >= n) continue;
+      float2 x[N], dgc[N], da[N];
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        const bool in = j0 + j < n;
+        const size_t e = e0 + (size_t)(j0 + j) * rs;
+        x[j] = in ? ld2(g.ret + e) : make_float2(0.f, 0.f);
+        dgc[j] = (in && d.d_gc) ? ld2(d.d_gc + e) : make_float2(0.f, 0.f);
+        da[j] = (in && d.d_alpha) ? ld2(d.d_alpha + e) : make_float2(0.f, 0.f);
+      }
+#pragma unroll
+      for (int j = N - 1; j >= 0; --j) {
+        if (j0 + j < n) {
+          // one e^x serves softplus (ln u) and sigmoid (e / u)
+          const float xb0 = x[j].x + bias.x, xb1 = x[j].y + bias.y;
+          const float ex0 = ex2a(xb0 * kLog2e), ex1 = ex2a(xb1 * kLog2e);
+          const float u0 = 1.f + ex0, u1 = 1.f + ex1;
+          const float l0 = xb0 > 20.f ? negA * xb0 : (negA * kLn2) * __log2f(u0);
+          const float l1 = xb1 > 20.f ? negA * xb1 : (negA * kLn2) * __log2f(u1);
+          const float sg0 = xb0 > 20.f ? 1.f : __fdividef(ex0, u0);
+          const float sg1 = xb1 > 20.f ? 1.f : __fdividef(ex1, u1);
+          const float a0 = ex2a(l0 * kLog2e), a1 = ex2a(l1 * kLog2e);
+          acc0 += dgc[j].x;
+          acc1 += dgc[j].y;
+          const float dl0 = fmaf(da[j].x, a0, a0 >= kAlphaFloor ? acc0 : 0.f);
+          const float dl1 = fmaf(da[j].y, a1, a1 >= kAlphaFloor ? acc1 : 0.f);
+          const float r0 = dl0 * negA * sg0, r1 = dl1 * negA * sg1;
+          if (d.dret) st_pair(d.dret + e0 + (size_t)(j0 + j) * rs, r0, r1);
+          dA_acc = fmaf(dl0, l0, fmaf(dl1, l1, dA_acc));
+          ddt0 += r0;
+          ddt1 += r1;
+        }
+      }
+    }
+  }
+  const size_t np_row = (size_t)bc * g.H + h;
+  if (d.part_dt) st_pair(d.part_dt + np_row * K + k0, ddt0, ddt1);
+  if (d.part_A) {
+    const float v = warp_sum(dA_acc);
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    if (tid == 0) {
+      float s = 0.f;
+#pragma unroll
+      for (int w = 0; w < NW; ++w) s += red[w];
+      d.part_A[np_row] = s;
+    }
+  }
+  if (d.domega_raw && n > 0) {
+#pragma unroll 1
+    for (int j0 = 0; j0 < n; j0 += N) {
+      float2 z[N], dw[N];
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        const bool in = j0 + j < n;
+        const size_t e = e0 + (size_t)(j0 + j) * rs;
+        z[j] = in ? ld2(g.wraw + e) : make_float2(0.f, 0.f);
+        dw[j] = in ? ld2(d.d_omega + e) : make_float2(0.f, 0.f);
+      }
+#pragma unroll
+      for (int j = 0; j < N; ++j)
+        if (j0 + j < n)
+          st_pair(d.domega_raw + e0 + (size_t)(j0 + j) * rs, dw[j].x * sigmoid_(z[j].x), dw[j].y * sigmoid_(z[j].y));
+    }
+  }
+  if (d.dr_raw)
+    for (int t = tid; t < n; t += NTH) {
+      const size_t row = row0 + (size_t)t * g.H;
+      d.dr_raw[row] = __float2bfloat16_rn(d.d_r[row] * sigmoid_(__bfloat162float(g.rraw[row])));
+    }
+  if (bc == 0 && tid == 0 && d.d_param) d.d_param[h] = d.d_init[h] * sigmoid_(g.param[h]);
+}
+
 int gate_check(const char* what, int64_t B, int64_t T, int64_t H, int64_t K, const void* wr, int64_t sb, int64_t st) {
   if (B < 0 || T < 0 || H <= 0 || (K != 64 && K != 128))
     return set_error(KDN_ERR_INVALID, "%s: need B, T >= 0, H > 0 and K in {64, 128}", what);
@@ -405,6 +579,87 @@ int kdn_iso_gate_bwd(const void* g_raw, int g_raw_bf16, const void* omega_r_raw,
     const int blocks = (wdt + kRedCols - 1) / kRedCols + (wA + kRedCols - 1) / kRedCols + (2 * (int)H + kRedCols - 1) / kRedCols;
     gate_reduce_kernel<<<blocks, kRedCols * kRedGroups, 0, st>>>(part_dt, ddt_bias, wdt, part_A, dA_log, wA, part_wr,
                                                                  domega_bias, dr_bias, (int)H, NP);
+    return check_launch("gate_reduce_kernel");
+  }
+  return KDN_OK;
+}
+
+size_t kdn_diag_gate_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t K) {
+  if (B <= 0 || T <= 0 || H <= 0 || K <= 0) return 0;
+  const int64_t NP = B * ((T + kDiagGateChunk - 1) / kDiagGateChunk);
+  return align_up(sizeof(float) * (size_t)(NP * H * (K + 1)), 256);
+}
+
+static int diag_gate_check(const char* what, int64_t B, int64_t T, int64_t H, int64_t K) {
+  if (B < 0 || T < 0 || H <= 0 || (K != 64 && K != 128))
+    return set_error(KDN_ERR_INVALID, "%s: need B, T >= 0, H > 0 and K in {64, 128}", what);
+  if (T > INT32_MAX || H * B * ((T + kDiagGateChunk - 1) / kDiagGateChunk) > INT32_MAX)
+    return set_error(KDN_ERR_INVALID, "%s: size too large", what);
+  return KDN_OK;
+}
+
+int kdn_diag_gate_fwd(const void* retention_raw, const void* omega_raw, const void* r_raw, const float* A_log,
+                      const float* dt_bias, const float* initial_precision_param, float* g_cumsum, float* alpha,
+                      float* omega, float* r, float* initial_precision, int64_t B, int64_t T, int64_t H, int64_t K,
+                      kdn_stream_t stream) {
+  const char* what = "kdn_diag_gate_fwd";
+  if (int rc = diag_gate_check(what, B, T, H, K)) return rc;
+  const bool empty = B * T == 0;
+  if (!A_log || !dt_bias || !initial_precision_param || !initial_precision ||
+      (!empty && (!retention_raw || !omega_raw || !r_raw || !g_cumsum || !alpha || !omega || !r)))
+    return set_error(KDN_ERR_INVALID, "%s: null pointer", what);
+  const int NT = empty ? 0 : (int)((T + kDiagGateChunk - 1) / kDiagGateChunk);
+  DiagGateArgs g{static_cast<const bf16*>(retention_raw), static_cast<const bf16*>(omega_raw),
+                 static_cast<const bf16*>(r_raw), A_log, dt_bias, initial_precision_param, empty ? 0 : (int)T,
+                 (int)H, NT};
+  const unsigned grid = (unsigned)(H * (empty ? 1 : B * NT));
+  cudaStream_t st = (cudaStream_t)stream;
+  if (K == 128)
+    diag_gate_fwd_kernel<128><<<grid, 64, 0, st>>>(g, g_cumsum, alpha, omega, r, initial_precision);
+  else
+    diag_gate_fwd_kernel<64><<<grid, 32, 0, st>>>(g, g_cumsum, alpha, omega, r, initial_precision);
+  return check_launch("diag_gate_fwd_kernel");
+}
+
+int kdn_diag_gate_bwd(const void* retention_raw, const void* omega_raw, const void* r_raw, const float* A_log,
+                      const float* dt_bias, const float* initial_precision_param, const float* d_g_cumsum,
+                      const float* d_alpha, const float* d_omega, const float* d_r, const float* d_initial_precision,
+                      void* dretention_raw, void* domega_raw, void* dr_raw, float* dA_log, float* ddt_bias,
+                      float* d_initial_precision_param, int64_t B, int64_t T, int64_t H, int64_t K, void* workspace,
+                      size_t workspace_bytes, kdn_stream_t stream) {
+  const char* what = "kdn_diag_gate_bwd";
+  if (int rc = diag_gate_check(what, B, T, H, K)) return rc;
+  const bool empty = B * T == 0;
+  if (!A_log || !dt_bias || !initial_precision_param ||
+      (!empty && (!retention_raw || !omega_raw || !r_raw)) || (domega_raw && !d_omega) || (dr_raw && !d_r) ||
+      (d_initial_precision_param && !d_initial_precision))
+    return set_error(KDN_ERR_INVALID, "%s: null pointer (an output gradient needs its cotangent)", what);
+  if (workspace_bytes < kdn_diag_gate_workspace_bytes(B, T, H, K) || (!empty && !workspace))
+    return set_error(KDN_ERR_WORKSPACE, "%s: workspace too small (kdn_diag_gate_workspace_bytes)", what);
+  const int NT = empty ? 0 : (int)((T + kDiagGateChunk - 1) / kDiagGateChunk);
+  const int NP = (int)B * NT;
+  DiagGateArgs g{static_cast<const bf16*>(retention_raw), static_cast<const bf16*>(omega_raw),
+                 static_cast<const bf16*>(r_raw), A_log, dt_bias, initial_precision_param, empty ? 0 : (int)T,
+                 (int)H, NT};
+  float* part_dt = empty ? nullptr : static_cast<float*>(workspace);
+  float* part_A = empty ? nullptr : part_dt + (size_t)NP * H * K;
+  // without a decay cotangent dretention_raw is zero and dA_log / ddt_bias sum zeros
+  DiagGateGrads d{d_g_cumsum, d_alpha, d_omega, d_r, d_initial_precision,
+                  empty ? nullptr : static_cast<bf16*>(dretention_raw),
+                  empty ? nullptr : static_cast<bf16*>(domega_raw), empty ? nullptr : static_cast<bf16*>(dr_raw),
+                  dA_log ? part_A : nullptr, ddt_bias ? part_dt : nullptr, d_initial_precision_param};
+  cudaStream_t st = (cudaStream_t)stream;
+  const unsigned grid = (unsigned)(H * (empty ? 1 : NP));
+  if (K == 128)
+    diag_gate_bwd_kernel<128><<<grid, 64, 0, st>>>(g, d);
+  else
+    diag_gate_bwd_kernel<64><<<grid, 32, 0, st>>>(g, d);
+  if (int rc = check_launch("diag_gate_bwd_kernel")) return rc;
+  if (ddt_bias || dA_log) {  // with NP = 0 (empty input) the sums are zero
+    const int wdt = (int)(H * K), wA = (int)H;
+    const int blocks = (wdt + kRedCols - 1) / kRedCols + (wA + kRedCols - 1) / kRedCols;
+    gate_reduce_kernel<<<blocks, kRedCols * kRedGroups, 0, st>>>(part_dt, ddt_bias, wdt, part_A, dA_log, wA, nullptr,
+                                                                 nullptr, nullptr, (int)H, NP);
     return check_launch("gate_reduce_kernel");
   }
   return KDN_OK;

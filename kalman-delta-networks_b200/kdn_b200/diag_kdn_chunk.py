@@ -2,6 +2,7 @@
 
 * ``_diag_kdn_gain`` (lit_gpt/kdn_ops/diag_kdn_chunk.py:2737)
 * ``chunk_kalman``   (lit_gpt/kdn_ops/diag_kdn_chunk.py:3315)
+* ``_diag_kdn_frontend_precumsum_paired`` (lit_gpt/kdn_ops/diag_kdn_chunk.py:2471)
 
 with the reference's signatures, validation messages, tensor layouts and
 autograd contract, on the sm_100a kernels of ``libkdn_b200.so``.
@@ -209,4 +210,147 @@ def chunk_kalman(
     return _DiagKdnMemoryFunction.apply(q_memory, k_memory, kappa, v, g_cumsum, scale)
 
 
-__all__ = ("_diag_kdn_gain", "chunk_kalman")
+# --------------------------------------------------------------------------
+# Gate / noise frontend
+
+
+def _validate_diag_kdn_frontend_inputs(retention_raw, omega_raw, r_raw, A_log, dt_bias, initial_precision_param):
+    """The reference's checks and messages (diag_kdn_chunk.py:2171-2215)."""
+    tensors = {
+        "retention_raw": retention_raw,
+        "omega_raw": omega_raw,
+        "r_raw": r_raw,
+        "A_log": A_log,
+        "dt_bias": dt_bias,
+        "initial_precision_param": initial_precision_param,
+    }
+    for name, value in tensors.items():
+        if not isinstance(value, torch.Tensor):
+            raise TypeError(f"{name} must be a torch.Tensor")
+        if not value.is_cuda:
+            raise ValueError(f"{name} must be a CUDA tensor")
+        if value.device != retention_raw.device:
+            raise ValueError("all DiagKDN frontend inputs must share one CUDA device")
+        if not value.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+    if retention_raw.ndim != 4:
+        raise ValueError("retention_raw must have rank 4 [B,T,H,K]")
+    B, T, H, K = retention_raw.shape
+    if min(B, T, H) <= 0 or K not in (64, 128):
+        raise ValueError("DiagKDN frontend requires non-empty B/T/H and K in {64,128}")
+    if omega_raw.shape != (B, T, H, K):
+        raise ValueError("omega_raw must match retention_raw")
+    if r_raw.shape != (B, T, H):
+        raise ValueError("r_raw must have shape [B,T,H]")
+    if A_log.shape != (H,) or initial_precision_param.shape != (H,):
+        raise ValueError("A_log and initial_precision_param must have shape [H]")
+    if dt_bias.shape != (H, K):
+        raise ValueError("dt_bias must have shape [H,K]")
+    for name in ("retention_raw", "omega_raw", "r_raw"):
+        if tensors[name].dtype != _VECTOR_DTYPE:
+            raise TypeError(f"{name} must be torch.bfloat16")
+    for name in ("A_log", "dt_bias", "initial_precision_param"):
+        if tensors[name].dtype != _STATE_DTYPE:
+            raise TypeError(f"{name} must be torch.float32")
+    return B, T, H, K
+
+
+def _diag_frontend_forward(retention_raw, omega_raw, r_raw, A_log, dt_bias, initial_precision_param):
+    B, T, H, K = retention_raw.shape
+    lib = N.load_library()
+    dev = retention_raw.device
+    g_cumsum = torch.empty((B, T, H, K), dtype=_STATE_DTYPE, device=dev)
+    alpha = torch.empty_like(g_cumsum)
+    omega = torch.empty_like(g_cumsum)
+    r = torch.empty((B, T, H), dtype=_STATE_DTYPE, device=dev)
+    initial_precision = torch.empty((H,), dtype=_STATE_DTYPE, device=dev)
+    N.check(
+        lib.kdn_diag_gate_fwd(
+            retention_raw.data_ptr(), omega_raw.data_ptr(), r_raw.data_ptr(), A_log.data_ptr(), dt_bias.data_ptr(),
+            initial_precision_param.data_ptr(), g_cumsum.data_ptr(), alpha.data_ptr(), omega.data_ptr(),
+            r.data_ptr(), initial_precision.data_ptr(), B, T, H, K, N.stream_of(retention_raw),
+        ),
+        "kdn_diag_gate_fwd",
+    )
+    return g_cumsum, alpha, omega, r, initial_precision
+
+
+def _diag_frontend_backward(retention_raw, omega_raw, r_raw, A_log, dt_bias, initial_precision_param, d_g_cumsum,
+                            d_alpha, d_omega, d_r, d_initial_precision, needs):
+    """Gradients for the inputs in ``needs`` whose cotangents are present, None
+    for the others (diag_kdn_chunk.py:2265-2443)."""
+    B, T, H, K = retention_raw.shape
+    lib = N.load_library()
+    dev = retention_raw.device
+    need_retention, need_omega, need_r, need_A, need_dt, need_initial = needs
+
+    def cot(x, shape):
+        if x is None:
+            return None
+        if x.shape != shape:
+            raise ValueError(f"cotangent must have shape {shape}, got {tuple(x.shape)}")
+        return x.to(_STATE_DTYPE).contiguous()
+
+    d_g_cumsum, d_alpha, d_omega = (cot(x, (B, T, H, K)) for x in (d_g_cumsum, d_alpha, d_omega))
+    d_r = cot(d_r, (B, T, H))
+    d_initial_precision = cot(d_initial_precision, (H,))
+    has_decay = d_g_cumsum is not None or d_alpha is not None
+    f32 = dict(dtype=_STATE_DTYPE, device=dev)
+    dretention_raw = torch.empty_like(retention_raw) if has_decay and need_retention else None
+    dA_log = torch.empty((H,), **f32) if has_decay and need_A else None
+    ddt_bias = torch.empty((H, K), **f32) if has_decay and need_dt else None
+    domega_raw = torch.empty_like(omega_raw) if need_omega and d_omega is not None else None
+    dr_raw = torch.empty_like(r_raw) if need_r and d_r is not None else None
+    d_param = torch.empty((H,), **f32) if need_initial and d_initial_precision is not None else None
+    ws = N.byte_buffer(lib.kdn_diag_gate_workspace_bytes(B, T, H, K), dev)
+    N.check(
+        lib.kdn_diag_gate_bwd(
+            retention_raw.data_ptr(), omega_raw.data_ptr(), r_raw.data_ptr(), A_log.data_ptr(), dt_bias.data_ptr(),
+            initial_precision_param.data_ptr(), N.ptr(d_g_cumsum), N.ptr(d_alpha), N.ptr(d_omega), N.ptr(d_r),
+            N.ptr(d_initial_precision), N.ptr(dretention_raw), N.ptr(domega_raw), N.ptr(dr_raw), N.ptr(dA_log),
+            N.ptr(ddt_bias), N.ptr(d_param), B, T, H, K, ws.data_ptr(), ws.numel(), N.stream_of(retention_raw),
+        ),
+        "kdn_diag_gate_bwd",
+    )
+    return dretention_raw, domega_raw, dr_raw, dA_log, ddt_bias, d_param
+
+
+class _DiagKdnFrontendFunction(torch.autograd.Function):
+    """Autograd contract of the reference's Function (diag_kdn_chunk.py:2446-2468)."""
+
+    @staticmethod
+    def forward(ctx, retention_raw, omega_raw, r_raw, A_log, dt_bias, initial_precision_param):
+        outs = _diag_frontend_forward(retention_raw, omega_raw, r_raw, A_log, dt_bias, initial_precision_param)
+        # alpha is recomputed from retention_raw in the backward kernel
+        ctx.save_for_backward(retention_raw, omega_raw, r_raw, A_log, dt_bias, initial_precision_param)
+        ctx.set_materialize_grads(False)
+        return outs
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, d_g_cumsum, d_alpha, d_omega, d_r, d_initial_precision):
+        return _diag_frontend_backward(*ctx.saved_tensors, d_g_cumsum, d_alpha, d_omega, d_r, d_initial_precision,
+                                       ctx.needs_input_grad)
+
+
+def _diag_kdn_frontend_precumsum_paired(
+    retention_raw: torch.Tensor,
+    omega_raw: torch.Tensor,
+    r_raw: torch.Tensor,
+    A_log: torch.Tensor,
+    dt_bias: torch.Tensor,
+    initial_precision_param: torch.Tensor,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Apply the fixed uncoupled omega=0 / r=0.01 32-token frontend
+    (diag_kdn_chunk.py:2471-2494): returns ``(g_cumsum, alpha, omega, r,
+    initial_precision)``.
+
+    ``g_cumsum`` (the chunk-local base-2 prefix of ln max(alpha, 1e-6)) is
+    paired with its consumer: the cotangent it receives is reverse-prefixed in
+    natural-log coordinates, without the log2(e) factor.
+    """
+    _validate_diag_kdn_frontend_inputs(retention_raw, omega_raw, r_raw, A_log, dt_bias, initial_precision_param)
+    return _DiagKdnFrontendFunction.apply(retention_raw, omega_raw, r_raw, A_log, dt_bias, initial_precision_param)
+
+
+__all__ = ("_diag_kdn_gain", "chunk_kalman", "_diag_kdn_frontend_precumsum_paired")

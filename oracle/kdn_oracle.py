@@ -40,6 +40,10 @@ __all__ = (
     "iso_gate",
     "iso_gate_grads",
     "make_iso_gate_inputs",
+    "DIAG_ALPHA_FLOOR",
+    "diag_gate",
+    "diag_gate_grads",
+    "make_diag_gate_inputs",
 )
 
 LN2 = math.log(2.0)
@@ -382,6 +386,73 @@ def iso_gate_grads(inputs, cotangents, omega_min, r_min, dtype=torch.float64):
     grads = torch.autograd.grad(loss, leaves, allow_unused=True)
     grads = [torch.zeros_like(l) if g is None else g for l, g in zip(leaves, grads)]
     return [o.detach() for o in outs], grads
+
+
+DIAG_ALPHA_FLOOR = 1e-6
+
+
+def diag_gate(retention_raw, omega_raw, r_raw, A_log, dt_bias, initial_precision_param, chunk=32):
+    """``(g_cumsum, alpha, omega, r, initial_precision)`` of the diagonal
+    frontend (diag_kdn_chunk.py:1867-1906 with OMEGA_COUPLING / EMIT_RAW_G off,
+    omega_min 0, r_min 0.01, as launched at :2237): ell = -exp(A_log)
+    softplus(retention_raw + dt_bias), alpha = exp(ell), g_cumsum = log2(e)
+    times the 32-token-chunk inclusive prefix of ln max(alpha, 1e-6)."""
+    B, T, H, K = retention_raw.shape
+    x = retention_raw + dt_bias.view(1, 1, H, K)
+    ell = -torch.exp(A_log).view(1, 1, H, 1) * _softplus_fla(x)
+    alpha = torch.exp(ell)
+    ell_mem = torch.log(torch.clamp(alpha, min=DIAG_ALPHA_FLOOR))
+    pad = (-T) % chunk
+    ep = torch.nn.functional.pad(ell_mem, (0, 0, 0, 0, 0, pad))
+    g_cumsum = ep.view(B, (T + pad) // chunk, chunk, H, K).cumsum(2).view(B, T + pad, H, K)[:, :T] / LN2
+    omega = _softplus_fla(omega_raw)
+    r = 0.01 + _softplus_fla(r_raw)
+    initial_precision = 0.1 + _softplus_fla(initial_precision_param)
+    return g_cumsum, alpha, omega, r, initial_precision
+
+
+def diag_gate_grads(inputs, cotangents, dtype=torch.float64):
+    """Forward outputs and the six input gradients of the diagonal frontend
+    under its paired-cotangent contract (diag_kdn_chunk.py:1969-2051,
+    :2265-2443): the g_cumsum cotangent is reverse-prefixed without the log2(e)
+    factor, i.e. ``dL/dg_cumsum = ln(2) d_g_cumsum``; the memory term is dropped
+    where alpha is below the 1e-6 floor (the clamp's gradient).  ``inputs``:
+    retention_raw, omega_raw, r_raw, A_log, dt_bias, initial_precision_param;
+    ``cotangents``: d_g_cumsum, d_alpha, d_omega, d_r, d_initial_precision
+    (None = zero).  Returns (outputs, grads)."""
+    leaves = [t.detach().to(dtype).clone().requires_grad_(True) for t in inputs]
+    outs = diag_gate(*leaves)
+    loss = 0.0
+    for i, (o, c) in enumerate(zip(outs, cotangents)):
+        if c is None:
+            continue
+        c = c.to(dtype)
+        if i == 0:
+            c = c * LN2
+        loss = loss + (o * c).sum()
+    grads = torch.autograd.grad(loss, leaves, allow_unused=True)
+    grads = [torch.zeros_like(l) if g is None else g for l, g in zip(leaves, grads)]
+    return [o.detach() for o in outs], grads
+
+
+def make_diag_gate_inputs(B, T, H, K=128, seed=0):
+    """Seeded inputs (bf16 vectors, fp32 parameters, as the reference's
+    validation requires) and fp32 cotangents of the diagonal frontend on CPU.
+    A_log spans rates of about 1 to 20 and retention_raw has unit-2 spread, so
+    some alphas fall below the 1e-6 floor."""
+    gen = torch.Generator().manual_seed(seed)
+    n = lambda *s: torch.randn(*s, generator=gen)  # noqa: E731
+    dt = torch.exp(torch.rand(H, K, generator=gen) * (math.log(0.1) - math.log(0.001)) + math.log(0.001))
+    inputs = (
+        (n(B, T, H, K) * 2.0).to(torch.bfloat16),
+        n(B, T, H, K).to(torch.bfloat16),
+        n(B, T, H).to(torch.bfloat16),
+        torch.log(torch.rand(H, generator=gen) * 19.0 + 1.0),
+        dt + torch.log(-torch.expm1(-dt)),
+        n(H),
+    )
+    cotangents = (n(B, T, H, K), n(B, T, H, K), n(B, T, H, K), n(B, T, H), n(H))
+    return inputs, cotangents
 
 
 def make_iso_gate_inputs(B, T, H, K=128, seed=0, g_dtype=torch.float32, wr_dtype=torch.float32):
