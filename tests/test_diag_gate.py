@@ -118,3 +118,56 @@ def test_diag_frontend_validation_messages():
         _diag_kdn_frontend_precumsum_paired(None, *inputs[1:])
     with pytest.raises(ValueError, match="retention_raw must be a CUDA tensor"):
         _diag_kdn_frontend_precumsum_paired(*inputs)
+
+
+@pytest.mark.gpu
+def test_diag_frontend_gain_scan_composition():
+    """The diagonal mixer's wiring (lit_gpt/diag_kdn.py:315-342): frontend ->
+    _diag_kdn_gain (with the raw noise logits) -> chunk_kalman, backward
+    through all three, against one fp64 autograd graph of the oracle.  This
+    checks the paired gate-cotangent exchange between chunk_kalman and the
+    frontend (natural-log coordinates before the reverse 32-token prefix).
+    Tolerance: the bf16 scan's 2e-2 normalised max-abs error (bf16 gradients
+    after forgiving their own rounding)."""
+    from kdn_b200.diag_kdn_chunk import _diag_kdn_gain, chunk_kalman
+
+    B, T, H, K = 1, 100, 2, 128
+    d = oracle.make_diag_inputs(B, T, H, seed=31)
+    gate_in, _ = oracle.make_diag_gate_inputs(B, T, H, K, seed=32)
+    # milder decays than the frontend-only cases: chunk products stay above the
+    # exact-gate regime of the bf16 scan
+    gate_in = ((gate_in[0].float() * 0.5 - 2.0).bfloat16(),) + tuple(gate_in[1:3]) + (gate_in[3] * 0.5,) + tuple(gate_in[4:])
+    dO = d["dO"].bfloat16().float()
+    scale = K ** -0.5
+    # ours
+    G = [t.to("cuda").detach().requires_grad_(True) for t in gate_in]
+    S = {n: d[n].to("cuda").detach().requires_grad_(True) for n in ("q", "k", "v", "k_gain")}
+    g_cumsum, alpha, omega, r, ip = _diag_kdn_frontend_precumsum_paired(*G)
+    kappa = _diag_kdn_gain(S["k_gain"], alpha, omega, r, ip, G[1], G[2])
+    o = chunk_kalman(S["q"], S["k"], kappa, S["v"], g_cumsum, scale)
+    o.backward(dO.to("cuda"))
+    # oracle
+    Gr = [t.detach().double().requires_grad_(True) for t in gate_in]
+    Sr = {n: d[n].detach().double().requires_grad_(True) for n in ("q", "k", "v", "k_gain")}
+    g_r, alpha_r, omega_r, r_r, ip_r = oracle.diag_gate(*Gr)
+    kappa_r, _ = oracle.diag_gain(Sr["k_gain"], alpha_r, omega_r, r_r, ip_r)
+    alpha_mem = oracle.alpha_from_g_cumsum(g_r * oracle.LN2, 32)
+    S0 = torch.zeros(B, H, K, K, dtype=torch.float64)
+    o_r, _ = oracle.memory_recurrence(Sr["q"], Sr["k"], Sr["v"], alpha_mem, kappa_r, S0, scale)
+    (o_r * dO.double()).sum().backward()
+
+    def err(x, ref):
+        bf = x.dtype == torch.bfloat16
+        x, ref = x.detach().double().cpu(), ref.detach().double().cpu()
+        excess = (x - ref).abs()
+        if bf:  # a bf16 output: forgive its own rounding
+            excess = (excess - 2.0 ** -8 * ref.abs()).clamp_min(0)
+        return (excess.max() / ref.abs().max().clamp_min(1e-30)).item()
+
+    errs = {"o": err(o, o_r)}
+    for name, a, b in zip(("retention_raw", "omega_raw", "r_raw", "A_log", "dt_bias", "param"), G, Gr):
+        errs["d" + name] = err(a.grad, b.grad)
+    for n in ("q", "k", "v", "k_gain"):
+        errs["d" + n] = err(S[n].grad, Sr[n].grad)
+    bad = {k: v for k, v in errs.items() if not v < 2e-2}
+    assert not bad, (bad, errs)
