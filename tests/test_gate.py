@@ -132,3 +132,50 @@ def test_gate_validation_messages():
         _iso_kdn_gate_precumsum_paired(*args[:5], torch.zeros(H), args[6], 0.0, 0.01)
     with pytest.raises(ValueError, match="CUDA-only"):
         _iso_kdn_gate_precumsum_paired(*args, 0.0, 0.01)
+
+
+@pytest.mark.gpu
+def test_gate_gain_scan_composition():
+    """The isotropic mixer's wiring (lit_gpt/iso_kdn.py:277-304): gate frontend
+    -> iso_kdn_gain -> _chunk_kda_precumsum_paired, backward through all
+    three, against one fp64 autograd graph of the oracle.  This checks the
+    paired gate-cotangent exchange between the scan and the frontend.
+    Tolerance: the bf16 scan's 2e-2 normalised max-abs error (bf16 gradients
+    after forgiving their own rounding)."""
+    from kdn_b200.iso_kdn_chunk import _chunk_kda_precumsum_paired, iso_kdn_gain
+
+    B, T, H, K = 1, 150, 2, 128
+    d = oracle.make_iso_inputs(B, T, H, seed=41)
+    gate_in, _ = oracle.make_iso_gate_inputs(B, T, H, K, seed=42, g_dtype=torch.bfloat16, wr_dtype=torch.bfloat16)
+    # about -1 nat of gate per 64-token chunk
+    gate_in = ((gate_in[0].float() * 0.5 - 3.0).bfloat16(),) + tuple(gate_in[1:])
+    dO = d["dO"].bfloat16().float()
+    wmin, rmin = 0.0, 0.01
+    G = [t.to("cuda").detach().requires_grad_(True) for t in gate_in]
+    S = {n: d[n].to("cuda").detach().requires_grad_(True) for n in ("q", "k", "v")}
+    g_cumsum, a, omega, r, ip = _iso_kdn_gate_precumsum_paired(*G, wmin, rmin)
+    beta = iso_kdn_gain(a, omega, r, ip, head_dim=K, out_dtype=torch.float32, info_scale=float(K))
+    o = _chunk_kda_precumsum_paired(S["q"], S["k"], S["v"], g_cumsum, beta)
+    o.backward(dO.to("cuda"))
+    Gr = [t.detach().double().requires_grad_(True) for t in gate_in]
+    Sr = {n: d[n].detach().double().requires_grad_(True) for n in ("q", "k", "v")}
+    g_r, a_r, omega_r, r_r, ip_r = oracle.iso_gate(*Gr, wmin, rmin)
+    beta_r = oracle.iso_gain(a_r, omega_r, r_r, ip_r, 1.0)[0]
+    o_r, _ = oracle.iso_scan(Sr["q"], Sr["k"], Sr["v"], g_r, beta_r)
+    (o_r * dO.double()).sum().backward()
+
+    def err(x, ref):
+        bf = x.dtype == torch.bfloat16
+        x, ref = x.detach().double().cpu(), ref.detach().double().cpu()
+        excess = (x - ref).abs()
+        if bf:  # a bf16 output: forgive its own rounding
+            excess = (excess - 2.0 ** -8 * ref.abs()).clamp_min(0)
+        return (excess.max() / ref.abs().max().clamp_min(1e-30)).item()
+
+    errs = {"o": err(o, o_r)}
+    for name, x, y in zip(NAMES, G, Gr):
+        errs["d" + name] = err(x.grad, y.grad)
+    for n in ("q", "k", "v"):
+        errs["d" + n] = err(S[n].grad, Sr[n].grad)
+    bad = {k: v for k, v in errs.items() if not v < 2e-2}
+    assert not bad, (bad, errs)
