@@ -37,9 +37,10 @@ ISO_BYTES_PER_TH = {"scan_fwd": 1540, "scan_bwd": 2824, "gain": 48}
 DIAG_BYTES_PER_TH = {"scan_fwd": 2304, "scan_bwd": 4096, "gain_fwd": 2052, "gain_bwd": 3592}
 FLOPS_PER_TH = 540_672  # 3 * 2 * (3 d^2 + 5 C d), C = 64
 # DRAM bytes (read + write) per token-head of one kdn_scan_bwd call (reverse
-# sweep + chunk kernel): ncu dram__bytes_read.sum + dram__bytes_write.sum of
-# the two kernels at B=1 T=4096 H=18, divided by its 73,728 token-heads
-SCAN_BWD_TRAFFIC_PER_TH = {"iso": 5410, "diag": None}
+# sweep + chunk kernel, + the gate fold for diag): ncu dram__bytes_read.sum +
+# dram__bytes_write.sum of its kernels at B=1 T=4096 H=18, divided by its
+# 73,728 token-heads (profiles/scan_bwd_*_traffic.md)
+SCAN_BWD_TRAFFIC_PER_TH = {"iso": 5410, "diag": 7163}
 
 
 def load_peaks():
@@ -149,7 +150,9 @@ def make_iso(device, seed):
     return x
 
 
-def make_diag(device, seed):
+def make_diag(device, seed, B=None, T=None):
+    B = globals()["B"] if B is None else B
+    T = globals()["T"] if T is None else T
     g = torch.Generator(device=device).manual_seed(seed)
     sp = torch.nn.functional.softplus
     nrm = lambda t: t * torch.rsqrt((t * t).sum(-1, keepdim=True) + 1e-6)  # noqa: E731
@@ -468,69 +471,207 @@ def cpu_baseline(variant, seconds_budget=20.0):
                       f"scaled to H=18 by (b,h) independence"}
 
 
+# ----------------------------------------------------------------------------- Triton reference point
+
+
+def _load_reference_module(name):
+    """The reference's own kdn_ops module, loaded by file path from the
+    unmodified install under ``baseline/_ref`` (its package ``__init__`` needs
+    the training stack, which is absent; the kdn_ops files need only torch,
+    triton and flash-linear-attention utilities)."""
+    import importlib.util
+
+    path = os.path.join(ROOT, "baseline", "_ref", "lit_gpt", "kdn_ops", f"{name}.py")
+    if not os.path.exists(path):
+        raise FileNotFoundError(f"{path} (install the reference into baseline/_ref)")
+    spec = importlib.util.spec_from_file_location(f"_kdn_reference_{name}", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def o_error_vs_oracle(o, x, variant, stream=(0, 0)):
+    """Normalised max-abs error of the forward output o on one (b, h) stream
+    against the float64 oracle (gain + memory recurrence)."""
+    import oracle
+
+    b, h = stream
+    sl = lambda t: t[b:b + 1, :, h:h + 1].detach().double().cpu()  # noqa: E731
+    G = sl(x["g_cumsum"]) * oracle.LN2
+    S0 = torch.zeros(1, 1, D, D, dtype=torch.float64)
+    with torch.no_grad():
+        if variant == "iso":
+            beta, _, _ = oracle.iso_gain(sl(x["a"]), sl(x["omega"]), sl(x["r"]), x["prec"][h:h + 1].double().cpu())
+            qh, kh = oracle.l2norm(sl(x["q"])), oracle.l2norm(sl(x["k"]))
+            ref, _ = oracle.memory_recurrence(qh, kh, sl(x["v"]), oracle.alpha_from_g_cumsum(G, 64),
+                                              beta[..., None] * kh, S0, D ** -0.5)
+        else:
+            kap, _ = oracle.diag_gain(sl(x["k_gain"]), sl(x["alpha"]), sl(x["omega"]), sl(x["r"]),
+                                      x["prec"][h:h + 1].double().cpu())
+            ref, _ = oracle.memory_recurrence(sl(x["q"]), sl(x["k"]), sl(x["v"]), oracle.alpha_from_g_cumsum(G, 32),
+                                              kap, S0, D ** -0.5)
+    got = sl(o)
+    return ((got - ref).abs().max() / ref.abs().max()).item()
+
+
+def triton_reference(device, x_diag, ours_diag_ms, steps=10, warmup=3):
+    """The reference's own Triton kernels on this B200, through its stock
+    kdn_ops entry points (``_diag_kdn_gain`` + ``chunk_kalman``,
+    diag_kdn_chunk.py:2737, 3315; ``iso_kdn_gain`` +
+    ``_chunk_kda_precumsum_paired``, iso_kdn_chunk.py:1966, 2242), on the
+    bench's own inputs: eager fwd + bwd steps timed with CUDA events, and
+    the forward output's error against the float64 oracle on one stream
+    beside ours."""
+    out = {}
+    try:
+        ref = _load_reference_module("diag_kdn_chunk")
+        x = x_diag
+        names = ("q", "k", "v", "g_cumsum", "k_gain", "alpha", "prec", "omega_raw", "r_raw")
+
+        def step():
+            L = leafify(x, names)
+            kappa = ref._diag_kdn_gain(L["k_gain"], L["alpha"], L["omega"], L["r"], L["prec"], L["omega_raw"],
+                                       L["r_raw"])
+            o = ref.chunk_kalman(L["q"], L["k"], kappa, L["v"], L["g_cumsum"], float(D ** -0.5))
+            o.backward(x["dO"])
+            return o
+
+        t0 = time.perf_counter()
+        for _ in range(warmup):
+            step()
+        torch.cuda.synchronize(device)
+        compile_s = time.perf_counter() - t0
+        ms = time_region(step, steps, device)
+        with torch.no_grad():
+            L = leafify(x, ())
+            kappa = ref._diag_kdn_gain(L["k_gain"], L["alpha"], L["omega"], L["r"], L["prec"], L["omega_raw"],
+                                       L["r_raw"])
+            o_ref = ref.chunk_kalman(L["q"], L["k"], kappa, L["v"], L["g_cumsum"], float(D ** -0.5))
+        from kdn_b200.diag_kdn_chunk import _diag_kdn_gain, chunk_kalman
+
+        with torch.no_grad():
+            o_ours = chunk_kalman(x["q"], x["k"], _diag_kdn_gain(x["k_gain"], x["alpha"], x["omega"], x["r"],
+                                                                 x["prec"], x["omega_raw"], x["r_raw"]),
+                                  x["v"], x["g_cumsum"], float(D ** -0.5))
+        out["diag"] = {
+            "what": "reference Triton _diag_kdn_gain + chunk_kalman, fwd + bwd, eager (config 2)",
+            "ms_per_step": ms, "value": B * T / (ms * 1e-3) / 1e6, "unit": "Mtok/s",
+            "warmup_incl_compile_s": compile_s,
+            "ours_ms_per_step": ours_diag_ms, "ours_speedup": ms / ours_diag_ms if ours_diag_ms else None,
+            "o_err_vs_oracle": o_error_vs_oracle(o_ref, x, "diag"),
+            "ours_o_err_vs_oracle": o_error_vs_oracle(o_ours, x, "diag"),
+            "err_stream": "(b, h) = (0, 0), normalised max-abs, float64 oracle",
+        }
+    except Exception as e:  # the reference point is reported, never required
+        out["diag"] = {"unavailable": f"{type(e).__name__}: {str(e).splitlines()[0][:300]}"}
+    try:
+        ref_iso = _load_reference_module("iso_kdn_chunk")
+        xi = make_iso(device, seed=4321)
+        L = leafify(xi, ("q", "k", "v", "g_cumsum", "a", "omega", "r", "prec"))
+        beta = ref_iso.iso_kdn_gain(L["a"], L["omega"], L["r"], L["prec"], head_dim=D, out_dtype=torch.float32)
+        o = ref_iso._chunk_kda_precumsum_paired(q=L["q"], k=L["k"], v=L["v"], g_cumsum=L["g_cumsum"], beta=beta)
+        o.backward(xi["dO"])
+        torch.cuda.synchronize(device)
+        out["iso"] = {"ran": True}
+    except Exception as e:
+        out["iso"] = {"unavailable": "unavailable on this box: the reference's iso scan calls flash-linear-"
+                                     "attention at a pinned commit; the installed fla 0.5.1 fails with "
+                                     f"{type(e).__name__}: {str(e).splitlines()[0][:300]}"}
+    return out
+
+
+# ----------------------------------------------------------------------------- sequence parallelism (config 4)
+
+SP_T = 131072  # config 4: one sequence of 131,072 tokens split contiguously over the ranks
+
+
+def measure_sp(args, device, dist, world, rank, warmup):
+    """Config 4 (diag, B=1, T=131,072, H=18): at N=1 the plain operators on
+    the whole sequence; at N>1 each rank holds T/N contiguous tokens and runs
+    the two-pass sequence-parallel scan (kdn_b200.sequence_parallel,
+    all-gathers over NCCL).  Eager fwd + bwd steps, CUDA events, max over
+    ranks.  Then a short case (T = 256 N, H = 2) checks the sequence-parallel
+    outputs and gradients against the single-GPU call on the whole sequence,
+    which every rank evaluates itself (max over ranks of the normalised
+    max-abs difference)."""
+    from kdn_b200.diag_kdn_chunk import _diag_kdn_gain, chunk_kalman
+    from kdn_b200.sequence_parallel import sp_diag_kdn_two_pass
+
+    Tr = SP_T // world
+    names = ("q", "k", "v", "g_cumsum", "k_gain", "alpha", "prec", "omega_raw", "r_raw")
+
+    def step_of(x, sp):
+        def step():
+            L = leafify(x, names)
+            if sp:
+                o = sp_diag_kdn_two_pass(L["q"], L["k"], L["v"], L["g_cumsum"], L["k_gain"], L["alpha"], L["omega"],
+                                         L["r"], L["prec"], L["omega_raw"], L["r_raw"])
+            else:
+                kappa = _diag_kdn_gain(L["k_gain"], L["alpha"], L["omega"], L["r"], L["prec"], L["omega_raw"],
+                                       L["r_raw"])
+                o = chunk_kalman(L["q"], L["k"], kappa, L["v"], L["g_cumsum"], float(D ** -0.5))
+            o.backward(x["dO"])
+            return L, o
+        return step
+
+    x = make_diag(device, seed=777 + rank, B=1, T=Tr)
+    step = step_of(x, world > 1)
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize(device)
+    if dist is not None:
+        dist.barrier()
+    steps = max(3, min(args.steps, 10))
+    ms = time_region(step, steps, device)
+    if dist is not None:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    rec = {"workload": f"diag_kdn gain+scan fwd+bwd B1 T{SP_T} H{H} d{D} (config 4), T split over {world} rank(s)",
+           "mode": "two-pass sequence parallel (NCCL all-gather)" if world > 1 else "single GPU, whole sequence",
+           "ms_per_step": ms, "value": SP_T / (ms * 1e-3) / 1e6, "unit": "Mtok/s", "n_gpus": world,
+           "tokens_per_rank": Tr, "steps": steps, "timing": "eager"}
+    del x
+    if world > 1:
+        Tc, Hc = 256 * world, 2
+        full = make_diag(device, seed=99, B=1, T=Tc)  # the same seed on every rank: one sequence
+        full = {n: (v[:, :, :Hc].contiguous() if isinstance(v, torch.Tensor) and v.dim() >= 3 else v)
+                for n, v in full.items()}
+        full["prec"] = full["prec"][:Hc].contiguous()
+        Lf, of = step_of(full, False)()
+        sl = slice(rank * 256, (rank + 1) * 256)
+        part = {n: (v[:, sl].contiguous() if isinstance(v, torch.Tensor) and v.dim() >= 3 else v)
+                for n, v in full.items()}
+        Ls, os_ = step_of(part, True)()
+        errs = {"o": (os_.detach(), of.detach()[:, sl])}
+        for n in ("q", "k", "v", "g_cumsum", "k_gain", "alpha", "omega_raw", "r_raw"):
+            errs["d" + n] = (Ls[n].grad, Lf[n].grad[:, sl])
+        dprior = Ls["prec"].grad.clone()
+        dist.all_reduce(dprior)
+        errs["dprec"] = (dprior, Lf["prec"].grad)
+        worst = {}
+        for n, (a, b) in errs.items():
+            a, b = a.double(), b.double()
+            e = torch.tensor([((a - b).abs().max() / b.abs().max().clamp_min(1e-30)).item()], device=device)
+            dist.all_reduce(e, op=dist.ReduceOp.MAX)
+            worst[n] = e.item()
+        rec["check"] = {"case": f"B1 T{Tc} H{Hc}, 256 tokens per rank",
+                        "max_norm_err_vs_single_gpu": worst, "max": max(worst.values())}
+    return rec
+
+
 # ----------------------------------------------------------------------------- main
 
 
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--variant", choices=("iso", "diag"), default="iso")
-    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--eager", action="store_true", help="time eager steps instead of a replayed CUDA graph")
-    ap.add_argument("--varlen", action="store_true",
-                    help="config 4 packed batch: diag, B=1, T=131072 of sequences ~U[256, 8192] (cu_seqlens)")
-    ap.add_argument("--batch", type=int, default=B, help="sequences per GPU (profiling runs use smaller cases)")
-    args = ap.parse_args()
-    globals()["B"] = args.batch
-    if args.varlen:
-        args.variant = "diag"
-        globals()["B"], globals()["T"] = 1, VARLEN_T
-    warmup = max(args.warmup, 3)
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-
-    if args.impl == "reference":
-        if rank != 0:
-            return
-        runs = []
-        for _ in range(warmup):
-            cpu_baseline(args.variant, seconds_budget=5.0)
-        for _ in range(args.steps):
-            runs.append(cpu_baseline(args.variant, seconds_budget=10.0))
-        val = statistics.mean(r["value"] for r in runs)
-        cb = dict(runs[-1])
-        cb["value"] = val
-        print(json.dumps({
-            "impl": "reference", "metric": METRIC, "value": val, "unit": "Mtok/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": warmup, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-            "config": {"workload": f"{args.variant}_kdn gain+scan fwd+bwd, B1 H2 slice of B4 T4096 H18 d128"},
-            "cpu_baseline": cb, "e2e": {"value": val, "unit": "Mtok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        }))
-        return
-
-    dist = None
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
-    device = torch.device("cuda", local)
-    torch.cuda.set_device(device)
-
-    if args.varlen:
+def measure(variant, args, device, dist, world, rank, warmup, varlen=False):
+    """Time one step of ``variant`` (device-resident inputs, CUDA graph
+    replay, max over ranks), then its end-to-end step with host buffers, the
+    per-call times and roofline of the dominant call, and the frontends."""
+    if varlen:
         x, step = make_diag_varlen(device, seed=1234 + rank), step_diag_varlen
     else:
-        x = (make_iso if args.variant == "iso" else make_diag)(device, seed=1234 + rank)
-        step = step_iso if args.variant == "iso" else step_diag
+        x = (make_iso if variant == "iso" else make_diag)(device, seed=1234 + rank)
+        step = step_iso if variant == "iso" else step_diag
     for _ in range(warmup):
         step(x)
     torch.cuda.synchronize(device)
@@ -572,6 +713,7 @@ def main():
         t = torch.tensor([ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = t.item()
+    del graph
 
     tokens = B * T * world
     value = tokens / (ms * 1e-3) / 1e6
@@ -581,7 +723,7 @@ def main():
     # end to end through the public operators with host buffers
     e2e = None
     if not args.no_e2e:
-        names = GRAD_NAMES[args.variant]
+        names = GRAD_NAMES[variant]
         host = {n: (v.detach().cpu().pin_memory() if isinstance(v, torch.Tensor) else v) for n, v in x.items()}
         grads_host = {n: torch.empty(x[n].shape, dtype=x[n].dtype).pin_memory() for n in names}
         h2d = sum(v.numel() * v.element_size() for v in host.values() if isinstance(v, torch.Tensor))
@@ -642,49 +784,132 @@ def main():
             e2e_ms = t.item()
         e2e = {"value": tokens / (e2e_ms * 1e-3) / 1e6, "unit": "Mtok/s", "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms}
+        del bufs, host, grads_host
 
-    per_th = ISO_BYTES_PER_TH if args.variant == "iso" else DIAG_BYTES_PER_TH
+    per_th = ISO_BYTES_PER_TH if variant == "iso" else DIAG_BYTES_PER_TH
     step_bytes = sum(per_th.values()) * th
-    if args.varlen:
+    if varlen:
         # packed sequences run as batched calls, one per length bucket: the whole step is the unit
         achieved = step_bytes / (ms * 1e-3) / 1e9
         roofline = {"kernel": "whole varlen step (gain + scan, fwd + bwd, all sequences)", "bound": "hbm",
                     "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                     "peak_kind": peak_kind, "traffic": None, "step_frac": achieved / hbm}
     else:
-        ops = per_op_times(args.variant, x, device)
+        ops = per_op_times(variant, x, device)
         # dominant kernel call: the scan backward (reverse state sweep + chunk-parallel gradients)
         bwd_bytes = per_th["scan_bwd"] * th
         achieved = bwd_bytes / (ops["scan_bwd_ms"] * 1e-3) / 1e9
+        traffic = SCAN_BWD_TRAFFIC_PER_TH.get(variant)
         roofline = {
-            "kernel": "kdn_scan_bwd (scan_bwd_state + scan_bwd_chunk)",
+            "kernel": "kdn_scan_bwd (scan_bwd_state + scan_bwd_chunk" + (")" if variant == "iso" else " + gate_fold)"),
             "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-            "peak_kind": peak_kind,
-            "traffic": SCAN_BWD_TRAFFIC_PER_TH.get(args.variant) and SCAN_BWD_TRAFFIC_PER_TH[args.variant] * th,
+            "peak_kind": peak_kind, "traffic": traffic and traffic * th,
             "step_frac": (step_bytes / (ms * 1e-3) / 1e9) / hbm,
             "op_ms": ops,
         }
-
-    out = {
-        "metric": METRIC, "value": value, "unit": "Mtok/s", "n_gpus": world, "steps": args.steps, "warmup": warmup,
-        "ms_per_step": ms, "timing": timing, "eager_ms_per_step": eager_ms,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "bf16", "data": "synthetic",
+    rec = {
+        "value": value, "unit": "Mtok/s", "ms_per_step": ms, "timing": timing, "eager_ms_per_step": eager_ms,
         "config": {"workload": (f"diag_kdn gain+scan fwd+bwd, {len(x['cu']) - 1} packed sequences ~U[256,8192], "
-                                f"T{T} H{H} d{D} (config 4 varlen)") if args.varlen
-                   else f"iso_kdn gain+scan fwd+bwd B{B} T{T} H{H} d{D} (config 1)" if args.variant == "iso"
+                                f"T{T} H{H} d{D} (config 4 varlen)") if varlen
+                   else f"iso_kdn gain+scan fwd+bwd B{B} T{T} H{H} d{D} (config 1)" if variant == "iso"
                    else f"diag_kdn gain+scan fwd+bwd B{B} T{T} H{H} d{D} (config 2)",
                    "global_batch": B * world, "seq_len": T, "heads": H, "head_dim": D,
                    "parallelism": f"batch-sharded x{world}", "l2": "inputs > L2 (no flush)"},
-        "gpu_launches": LAUNCHES_PER_STEP[args.variant] * args.steps * (varlen_buckets(x["cu"]) if args.varlen else 1),
-        "e2e": e2e,
-        "roofline": roofline,
-        "clocks": clocks,
+        "gpu_launches": LAUNCHES_PER_STEP[variant] * args.steps * (varlen_buckets(x["cu"]) if varlen else 1),
+        "e2e": e2e, "roofline": roofline, "clocks": clocks,
     }
-    if not args.varlen:
-        out["frontend"] = (frontend_times if args.variant == "iso" else diag_frontend_times)(device, hbm)
-    if rank == 0 and world == 1 and not args.no_cpu and not args.varlen:
+    if not varlen:
+        rec["frontend"] = (frontend_times if variant == "iso" else diag_frontend_times)(device, hbm)
+    return rec, x
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--variant", choices=("iso", "diag"), default="iso")
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-diag", action="store_true", help="skip the config-2 (diag) sub-record of an iso run")
+    ap.add_argument("--no-triton", action="store_true", help="skip the reference's Triton kernels")
+    ap.add_argument("--no-sp", action="store_true", help="skip the config-4 sequence-parallel record")
+    ap.add_argument("--eager", action="store_true", help="time eager steps instead of a replayed CUDA graph")
+    ap.add_argument("--varlen", action="store_true",
+                    help="config 4 packed batch: diag, B=1, T=131072 of sequences ~U[256, 8192] (cu_seqlens)")
+    ap.add_argument("--batch", type=int, default=B, help="sequences per GPU (profiling runs use smaller cases)")
+    args = ap.parse_args()
+    globals()["B"] = args.batch
+    if args.varlen:
+        args.variant = "diag"
+        globals()["B"], globals()["T"] = 1, VARLEN_T
+    warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        # torchrun sets OMP_NUM_THREADS=1 per rank; the CPU reference uses every host core
+        torch.set_num_threads(os.cpu_count() or 1)
+        runs = []
+        for _ in range(warmup):
+            cpu_baseline(args.variant, seconds_budget=5.0)
+        for _ in range(args.steps):
+            runs.append(cpu_baseline(args.variant, seconds_budget=10.0))
+        val = statistics.mean(r["value"] for r in runs)
+        cb = dict(runs[-1])
+        cb["value"] = val
+        print(json.dumps({
+            "impl": "reference", "metric": METRIC, "value": val, "unit": "Mtok/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+            "config": {"workload": f"{args.variant}_kdn gain+scan fwd+bwd, B1 H2 slice of B4 T4096 H18 d128"},
+            "cpu_baseline": cb, "e2e": {"value": val, "unit": "Mtok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }))
+        return
+
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+
+    rec, x = measure(args.variant, args, device, dist, world, rank, warmup, varlen=args.varlen)
+    out = {"metric": METRIC, "value": rec["value"], "unit": "Mtok/s", "n_gpus": world, "steps": args.steps,
+           "warmup": warmup, "ms_per_step": rec["ms_per_step"], "timing": rec["timing"],
+           "eager_ms_per_step": rec["eager_ms_per_step"], "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": rec["config"],
+           "gpu_launches": rec["gpu_launches"], "e2e": rec["e2e"], "roofline": rec["roofline"],
+           "clocks": rec["clocks"]}
+    if "frontend" in rec:
+        out["frontend"] = rec["frontend"]
+    cpu = rank == 0 and world == 1 and not args.no_cpu and not args.varlen
+    if cpu:
         out["cpu_baseline"] = cpu_baseline(args.variant)
+    if args.variant == "iso" and not args.varlen and not args.no_diag:
+        # config 2 (diagonal KDN) in the same run: its own step time, roofline,
+        # end to end and CPU baseline
+        del x
+        drec, xd = measure("diag", args, device, dist, world, rank, warmup)
+        drec["metric"] = "KDN scan fwd+bwd Mtok/s/GPU (diag, B4,T4096,H18,d128 bf16)"
+        drec["n_gpus"] = world
+        if cpu:
+            drec["cpu_baseline"] = cpu_baseline("diag")
+        out["diag"] = drec
+        if rank == 0 and world == 1 and not args.no_triton:
+            out["triton_reference"] = triton_reference(device, xd, drec["ms_per_step"])
+        del xd
+    if args.variant == "iso" and not args.varlen and not args.no_sp:
+        out["sp"] = measure_sp(args, device, dist, world, rank, warmup)
     if rank == 0:
         print(json.dumps(out))
     if dist is not None:

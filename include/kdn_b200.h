@@ -35,7 +35,7 @@ enum {
   KDN_ERR_CUDA = -3,      /* a CUDA launch or runtime call failed        */
 };
 
-/* Version of this ABI (major * 100 + minor). */
+/* Version of this ABI (major * 100 + minor): 101 (KdnScanArgs.mode, the split diagonal gain). */
 int kdn_version(void);
 /* Message of the last failed call on this thread ("" if none). */
 const char* kdn_last_error(void);
@@ -170,7 +170,8 @@ int kdn_iso_gain_bwd(const float* a, const float* omega, const float* r,
  * kdn_diag_gain_carry_elems) is written by the forward and read by the
  * backward.  p_final (fp32 [B,H,K], nullable) receives the final covariance.
  * The backward fuses the softplus VJPs: domega_raw = dL/domega *
- * sigmoid(omega_raw), dr_raw = dL/dr * sigmoid(r_raw).  K must be 64 or 128.
+ * sigmoid(omega_raw), dr_raw = dL/dr * sigmoid(r_raw).  K must be 64 or 128;
+ * B*H <= 65535.
  * Continuation: initial_cov (fp32 [B,H,K], nullable) replaces
  * p_{-1} = 1/initial_precision; d_final_cov / d_initial_cov (fp32 [B,H,K],
  * nullable) carry the covariance cotangent in and out, and
@@ -202,6 +203,51 @@ int kdn_diag_gain_fwd_noalloc(const float* k, const float* alpha,
                               float* carry, float* p_final, int64_t B,
                               int64_t T, int64_t H, int64_t K,
                               kdn_stream_t stream);
+/* The diagonal gain in two phases each way, for sequence parallelism (no
+ * counterpart in the reference, which has no sequence parallelism).  A
+ * stream's covariance recursion is a composition of per-channel Moebius maps
+ * p -> (A p + B) / (C p + D), and its adjoint one of affine maps
+ * lambda -> A lambda + B, so a rank can summarise its segment before the
+ * covariance (or its cotangent) entering the segment is known:
+ *   kdn_diag_gain_fwd_maps    writes the segment maps into the workspace and
+ *                             their composition total_map (fp32 [B,H,K,4]:
+ *                             A, B, C, D, scaled to max |.| = 1);
+ *   kdn_diag_gain_fwd_finish  completes kdn_diag_gain_fwd from those maps
+ *                             (same workspace, untouched in between);
+ *   kdn_diag_gain_bwd_maps    writes the segment adjoint maps into the
+ *                             workspace and their composition total_adjoint
+ *                             (fp32 [B,H,K,2]: A, B with d_initial_cov =
+ *                             A d_final_cov + B);
+ *   kdn_diag_gain_bwd_finish  completes kdn_diag_gain_bwd from those maps.
+ * kdn_diag_gain_fwd = fwd_maps + fwd_finish and kdn_diag_gain_bwd = bwd_maps
+ * + bwd_finish (without the totals); arguments as there. */
+int kdn_diag_gain_fwd_maps(const float* k, const float* alpha, const float* omega,
+                           const float* r, float* total_map, int64_t B, int64_t T,
+                           int64_t H, int64_t K, void* workspace,
+                           size_t workspace_bytes, kdn_stream_t stream);
+int kdn_diag_gain_fwd_finish(const float* k, const float* alpha,
+                             const float* omega, const float* r,
+                             const float* initial_precision,
+                             const float* initial_cov, float* kappa, float* carry,
+                             float* p_final, int64_t B, int64_t T, int64_t H,
+                             int64_t K, void* workspace, size_t workspace_bytes,
+                             kdn_stream_t stream);
+int kdn_diag_gain_bwd_maps(const float* k, const float* alpha, const float* omega,
+                           const float* r, const float* dkappa, const float* carry,
+                           float* total_adjoint, int64_t B, int64_t T, int64_t H,
+                           int64_t K, void* workspace, size_t workspace_bytes,
+                           kdn_stream_t stream);
+int kdn_diag_gain_bwd_finish(const float* k, const float* alpha,
+                             const float* omega, const float* r,
+                             const float* initial_precision,
+                             const float* initial_cov, const void* omega_raw,
+                             const void* r_raw, const float* dkappa,
+                             const float* carry, const float* d_final_cov,
+                             float* dk, float* dalpha, void* domega_raw,
+                             void* dr_raw, float* d_initial_precision,
+                             float* d_initial_cov, int64_t B, int64_t T, int64_t H,
+                             int64_t K, void* workspace, size_t workspace_bytes,
+                             kdn_stream_t stream);
 int kdn_diag_gain_bwd(const float* k, const float* alpha, const float* omega,
                       const float* r, const float* initial_precision,
                       const float* initial_cov, const void* omega_raw,
@@ -234,13 +280,46 @@ int kdn_diag_gain_bwd(const float* k, const float* alpha, const float* omega,
  * writes the chunk-start memory states and the per-chunk triangular solve and
  * query-key scores; the backward reads them.  The first 4 bytes of `saved`
  * (after kdn_scan_fwd) and of `workspace` (after kdn_scan_bwd) hold a status
- * word, zeroed by the call: nonzero when a bounded wait inside the kernels
- * gave up, in which case that call's results are invalid.  Optional continuation buffers
+ * word, zeroed by the call: bit 0 (1) is set when a bounded wait inside the
+ * kernels gave up, in which case that call's results are invalid; bit 1 (2)
+ * is set only when the environment variable KDN_B200_DEBUG_POLL_LIMIT = n > 0
+ * is present and some wait needed more than n polls (a debug knob that lets
+ * a test exercise the status check: the wait still completes and the results
+ * stay valid).  Optional continuation buffers
  * (fp32 [B,H,K,V], nullable): initial_state / final_state in the forward,
  * d_final_state / d_initial_state in the backward (sequence parallelism).
  * ------------------------------------------------------------------------ */
 enum { KDN_ISO = 0, KDN_DIAG = 1 };
 enum { KDN_PREC_BF16 = 0, KDN_PREC_FP32 = 1 }; /* tensor-core bf16 / fp32 debug */
+/* Passes a call runs (`mode`; the partial passes need KDN_PREC_BF16).  The
+ * partial passes let a sequence-parallel driver summarise a segment before
+ * its incoming state is known and run only the sequential pass again once it
+ * is (no counterpart in the reference, which has no sequence parallelism):
+ *   KDN_SCAN_FULL            both directions: every pass (the default);
+ *   KDN_SCAN_FWD_RECORDS     forward: only the chunk-parallel pass, which
+ *                            writes the chunk records into `saved` (no o);
+ *   KDN_SCAN_FWD_SEQUENTIAL  forward: only the sequential pass (o, the saved
+ *                            states, final_state) from the records an earlier
+ *                            RECORDS or FULL call with the same q, k, g and
+ *                            beta / kappa left in `saved`;
+ *   KDN_SCAN_FWD_STATE_MAP   forward: only the segment's state map, from the
+ *                            records in `saved`: final_state = the state
+ *                            reached from initial_state (nullable = 0) with
+ *                            the values v, final_state_map = the state reached
+ *                            from the identity with zero values (the K x K
+ *                            linear part, fp32 [B,H,K,K]); writes no o and no
+ *                            saved states;
+ *   KDN_SCAN_BWD_STATE       backward: only the reverse state sweep, writing
+ *                            d_initial_state (dq ... dkappa untouched, may be
+ *                            null), from the saved states of a FULL or
+ *                            SEQUENTIAL forward. */
+enum {
+  KDN_SCAN_FULL = 0,
+  KDN_SCAN_FWD_RECORDS = 1,
+  KDN_SCAN_FWD_SEQUENTIAL = 2,
+  KDN_SCAN_FWD_STATE_MAP = 3,
+  KDN_SCAN_BWD_STATE = 4,
+};
 
 typedef struct KdnScanArgs {
   int32_t variant;   /* KDN_ISO or KDN_DIAG */
@@ -274,6 +353,9 @@ typedef struct KdnScanArgs {
   /* scratch */
   void* workspace;
   size_t workspace_bytes;
+  /* passes to run (KDN_SCAN_*; 0 = all) and the state-map output */
+  int32_t mode;
+  float* final_state_map; /* KDN_SCAN_FWD_STATE_MAP: fp32 [B,H,K,K] */
 } KdnScanArgs;
 
 size_t kdn_scan_saved_bytes(const KdnScanArgs* args);

@@ -20,6 +20,12 @@ KDN_ISO = 0
 KDN_DIAG = 1
 KDN_PREC_BF16 = 0
 KDN_PREC_FP32 = 1
+# passes of a scan call (KdnScanArgs.mode)
+KDN_SCAN_FULL = 0
+KDN_SCAN_FWD_RECORDS = 1
+KDN_SCAN_FWD_SEQUENTIAL = 2
+KDN_SCAN_FWD_STATE_MAP = 3
+KDN_SCAN_BWD_STATE = 4
 
 _lock = threading.Lock()
 _lib = None
@@ -56,6 +62,8 @@ class KdnScanArgs(ctypes.Structure):
         ("d_initial_state", ctypes.c_void_p),
         ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_size_t),
+        ("mode", ctypes.c_int32),
+        ("final_state_map", ctypes.c_void_p),
     ]
 
 
@@ -91,6 +99,10 @@ _SIGNATURES = {
     "kdn_diag_gain_workspace_bytes": ([_I64, _I64, _I64, _I64], _SZ),
     "kdn_diag_gain_fwd": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _SZ, _P], ctypes.c_int),
     "kdn_diag_gain_fwd_noalloc": ([_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P], ctypes.c_int),
+    "kdn_diag_gain_fwd_maps": ([_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _SZ, _P], ctypes.c_int),
+    "kdn_diag_gain_fwd_finish": ([_P] * 9 + [_I64, _I64, _I64, _I64, _P, _SZ, _P], ctypes.c_int),
+    "kdn_diag_gain_bwd_maps": ([_P] * 7 + [_I64, _I64, _I64, _I64, _P, _SZ, _P], ctypes.c_int),
+    "kdn_diag_gain_bwd_finish": ([_P] * 17 + [_I64, _I64, _I64, _I64, _P, _SZ, _P], ctypes.c_int),
     "kdn_diag_gain_bwd": (
         [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _SZ, _P],
         ctypes.c_int,
@@ -154,9 +166,12 @@ _PRECISION = {"bf16": KDN_PREC_BF16, "fp32": KDN_PREC_FP32}
 
 
 def precision() -> int:
-    """Arithmetic precision of the scan kernels: "bf16" (tensor cores, the
-    product) or "fp32" (SIMT fp32 everywhere, a debug build of the same
-    kernels), chosen by ``KDN_B200_PRECISION``."""
+    """Arithmetic precision of the scan, chosen by ``KDN_B200_PRECISION``:
+    "bf16" (the product: the tcgen05 tensor-core kernels with bf16 operands
+    and fp32 accumulation) or "fp32" (a separate debug implementation of the
+    same chunked algorithm: SIMT / fp32 kernels with fp32 operands and the
+    diagonal scan on 32-token chunks, used as a tight cross-check of the
+    algorithm, not of the tcgen05 kernels)."""
     name = os.environ.get("KDN_B200_PRECISION", "bf16").lower()
     if name not in _PRECISION:
         raise ValueError(f"KDN_B200_PRECISION must be one of {sorted(_PRECISION)}, got {name!r}")

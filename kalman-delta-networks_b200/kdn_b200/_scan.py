@@ -14,15 +14,31 @@ from . import _native as N
 KD = 128
 
 
+STATUS_GAVE_UP = 1  # a bounded wait ran out of polls: the call's results are invalid
+STATUS_SLOW_WAIT = 2  # a wait needed more polls than KDN_B200_DEBUG_POLL_LIMIT (debug knob; results valid)
+
+
+def status_word(buf: torch.Tensor) -> int:
+    """The status word at the head of ``saved`` (forward) or the workspace
+    (backward); reading it synchronises with the device."""
+    return int(buf[:4].view(torch.int32).item())
+
+
 def check_status(buf: torch.Tensor, what: str) -> None:
     """With ``KDN_B200_CHECK_STATUS=1``, synchronise and read the status word
-    at the head of ``saved`` (forward) or the workspace (backward): the
-    kernels' bounded waits set it when they gave up, and the results of that
-    call are then invalid.  Off by default (it costs a device round trip)."""
+    of the call: the kernels' bounded waits set ``STATUS_GAVE_UP`` when they
+    gave up (the results of that call are then invalid) and
+    ``STATUS_SLOW_WAIT`` when ``KDN_B200_DEBUG_POLL_LIMIT`` is set and a wait
+    needed more polls than it.  Off by default (it costs a device round
+    trip)."""
     if os.environ.get("KDN_B200_CHECK_STATUS", "0") != "1":
         return
-    if int(buf[:4].view(torch.int32).item()) != 0:
-        raise RuntimeError(f"{what}: a bounded wait in the kernels gave up (status word set); results are invalid")
+    word = status_word(buf)
+    if word & STATUS_GAVE_UP:
+        raise RuntimeError(f"{what}: a bounded wait in the kernels gave up (status word {word}); results are invalid")
+    if word:
+        raise RuntimeError(f"{what}: a wait exceeded the debug poll limit KDN_B200_DEBUG_POLL_LIMIT "
+                           f"(status word {word})")
 
 
 @dataclass

@@ -30,7 +30,7 @@ int check_launch(const char* what) {
 
 extern "C" {
 
-int kdn_version(void) { return 100; }
+int kdn_version(void) { return 101; }
 
 const char* kdn_last_error(void) { return g_last_error; }
 

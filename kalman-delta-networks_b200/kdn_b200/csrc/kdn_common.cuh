@@ -430,12 +430,37 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
       : "memory");
   return ok != 0;
 }
-// Wait for phase `parity` of an mbarrier, at most ~2^20 polls; on time-out
-// record it in *status (when given) and return so the kernel cannot hang.
+// Status word bits (the first int of the call's status header).
+constexpr int kStatusGaveUp = 1;     // a wait ran out of polls: the call's results are invalid
+constexpr int kStatusSlowWait = 2;   // a wait needed more polls than the debug limit (results valid)
+constexpr int kWaitPolls = 1 << 20;  // hard poll limit of every mbarrier wait
+
+// Non-blocking probe of phase `parity` (try_wait may suspend the thread for a
+// while before it reports failure; test_wait never does).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, unsigned parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Wait for phase `parity` of an mbarrier: one non-blocking probe, then at
+// most kWaitPolls polls; on time-out set kStatusGaveUp in *status (when
+// given) and return so the kernel cannot hang.  status[1] is a debug poll
+// limit written by the host before the launch (0 = off): a wait that needs
+// that many polls or more (the probe counts as the first) sets
+// kStatusSlowWait and keeps waiting up to the hard limit, so the host's
+// status check can be exercised without any copy left in flight.
 __device__ __forceinline__ void mbar_wait(uint64_t* bar, unsigned parity, int* status) {
-  for (int i = 0; i < (1 << 20); ++i)
+  if (mbar_test_wait(bar, parity)) return;
+  const int soft = status ? *reinterpret_cast<volatile int*>(status + 1) : 0;
+  for (int i = 1; i <= kWaitPolls; ++i) {
+    if (soft > 0 && i == soft) atomicOr(status, kStatusSlowWait);
     if (mbar_try_wait(bar, parity)) return;
-  if (status) atomicExch(status, 1);
+  }
+  if (status) atomicOr(status, kStatusGaveUp);
 }
 
 // 4-D tiled tensor load (box given by the tensor map) into shared memory.

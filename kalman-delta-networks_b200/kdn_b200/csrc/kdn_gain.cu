@@ -485,6 +485,35 @@ __global__ void __launch_bounds__(K) diag_gain_bwd_carry_kernel(const float2* __
   }
 }
 
+// Composed covariance map of a whole stream (sequence parallelism): the
+// segment maps M_{n-1} o ... o M_0 per (b, h, channel), normalised like every
+// composition here.
+template <int K>
+__global__ void __launch_bounds__(K) diag_gain_total_kernel(const float4* __restrict__ maps,
+                                                            float4* __restrict__ total, int nseg) {
+  const int bh = blockIdx.x, c = threadIdx.x;
+  Mob m{1.f, 0.f, 0.f, 1.f};
+  for (int s = 0; s < nseg; ++s) {
+    const float4 x = maps[((size_t)bh * nseg + s) * K + c];
+    m = mob_mul(Mob{x.x, x.y, x.z, x.w}, m);
+  }
+  total[(size_t)bh * K + c] = make_float4(m.A, m.B, m.C, m.D);
+}
+
+// Composed adjoint map of a whole stream: lambda_in = A lambda_out + B with
+// (A, B) = m_0 o m_1 o ... o m_{n-1} of the segment maps.
+template <int K>
+__global__ void __launch_bounds__(K) diag_gain_bwd_total_kernel(const float2* __restrict__ maps,
+                                                                float2* __restrict__ total, int nseg) {
+  const int bh = blockIdx.x, c = threadIdx.x;
+  Aff f{1.f, 0.f};
+  for (int s = nseg - 1; s >= 0; --s) {
+    const float2 m = maps[((size_t)bh * nseg + s) * K + c];
+    f = aff_after(Aff{m.x, m.y}, f);
+  }
+  total[(size_t)bh * K + c] = make_float2(f.A, f.B);
+}
+
 __device__ __forceinline__ float sigmoidf_(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
 
 template <int K>
@@ -687,31 +716,159 @@ size_t kdn_diag_gain_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t K)
   return maps > bwd ? maps : bwd;
 }
 
+}  // extern "C"
+
+namespace kdn {
+namespace {
+
+// Launch helpers of the diagonal gain; the entry points validate first.
+// Phases: forward = maps (per 64-token segment Moebius maps) -> carry ->
+// emit; backward = maps (per segment adjoint maps, per-token reductions) ->
+// carry -> emit.  The maps phase and the rest can be separate calls (the
+// workspace keeps the maps in between), which sequence parallelism uses to
+// compose the streams' maps across ranks before the carry.
+struct DiagDims {
+  int64_t B, T, H, K;
+  int nseg;
+};
+
+int diag_dims(const char* what, int64_t B, int64_t T, int64_t H, int64_t K, DiagDims* d) {
+  if (K != 64 && K != 128) return set_error(KDN_ERR_INVALID, "%s: K must be 64 or 128, got %lld", what, (long long)K);
+  if (T > INT32_MAX || B * H > 65535) return set_error(KDN_ERR_INVALID, "%s: size too large", what);
+  *d = DiagDims{B, T, H, K, (int)((T + kDiagSeg - 1) / kDiagSeg)};
+  return KDN_OK;
+}
+
+int diag_fwd_maps(const DiagDims& d, const float* k, const float* alpha, const float* omega, const float* r,
+                  float4* maps, cudaStream_t st) {
+  dim3 grid((unsigned)d.nseg, (unsigned)(d.B * d.H));
+  if (d.K == 128)
+    diag_gain_map_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, maps, (int)d.T, (int)d.H, d.nseg);
+  else
+    diag_gain_map_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, maps, (int)d.T, (int)d.H, d.nseg);
+  return check_launch("diag_gain_map_kernel");
+}
+
+int diag_fwd_finish(const DiagDims& d, const float* k, const float* alpha, const float* omega, const float* r,
+                    const float* init_prec, const float* init_cov, const float4* maps, float* kappa, float* carry,
+                    float* p_final, cudaStream_t st) {
+  dim3 grid((unsigned)d.nseg, (unsigned)(d.B * d.H));
+  const unsigned bh = (unsigned)(d.B * d.H);
+  if (d.K == 128) {
+    diag_gain_carry_kernel<128><<<bh, 128, 0, st>>>(maps, init_prec, init_cov, carry, p_final, (int)d.H, d.nseg);
+    diag_gain_emit_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, carry, kappa, (int)d.T, (int)d.H, d.nseg);
+  } else {
+    diag_gain_carry_kernel<64><<<bh, 64, 0, st>>>(maps, init_prec, init_cov, carry, p_final, (int)d.H, d.nseg);
+    diag_gain_emit_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, carry, kappa, (int)d.T, (int)d.H, d.nseg);
+  }
+  return check_launch("diag_gain_fwd kernels");
+}
+
+// backward workspace: [maps float2 | lam carry | per-token (D, G)]
+struct DiagBwdWs {
+  float2* maps;
+  float* lam;
+  float2* dg_tok;
+};
+DiagBwdWs diag_bwd_ws(const DiagDims& d, void* ws) {
+  char* w = static_cast<char*>(ws);
+  DiagBwdWs out;
+  out.maps = reinterpret_cast<float2*>(w);
+  w += align_up(sizeof(float2) * d.B * d.H * d.nseg * d.K, 256);
+  out.lam = reinterpret_cast<float*>(w);
+  w += align_up(sizeof(float) * d.B * d.H * d.nseg * d.K, 256);
+  out.dg_tok = reinterpret_cast<float2*>(w);
+  return out;
+}
+
+int diag_bwd_maps(const DiagDims& d, const float* k, const float* alpha, const float* omega, const float* r,
+                  const float* dkappa, const float* carry, const DiagBwdWs& w, cudaStream_t st) {
+  dim3 grid((unsigned)d.nseg, (unsigned)(d.B * d.H));
+  if (d.K == 128)
+    diag_gain_bwd_map_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, dkappa, carry, w.maps, w.dg_tok, (int)d.T,
+                                                        (int)d.H, d.nseg);
+  else
+    diag_gain_bwd_map_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, dkappa, carry, w.maps, w.dg_tok, (int)d.T,
+                                                      (int)d.H, d.nseg);
+  return check_launch("diag_gain_bwd_map_kernel");
+}
+
+int diag_bwd_finish(const DiagDims& d, const float* k, const float* alpha, const float* omega, const float* r,
+                    const float* init_prec, const float* init_cov, const bf16* wr, const bf16* rr,
+                    const float* dkappa, const float* carry, const float* d_final_cov, float* dk, float* dalpha,
+                    bf16* domega_raw, bf16* dr_raw, float* dinit, float* d_init_cov, const DiagBwdWs& w,
+                    cudaStream_t st) {
+  if (dinit && cudaMemsetAsync(dinit, 0, sizeof(float) * d.H, st) != cudaSuccess)
+    return check_launch("memset d_initial_precision");
+  float* dmu = init_cov ? nullptr : dinit;  // with a carried-in covariance the prior gets no gradient here
+  dim3 grid((unsigned)d.nseg, (unsigned)(d.B * d.H));
+  const unsigned bh = (unsigned)(d.B * d.H);
+  if (d.K == 128) {
+    diag_gain_bwd_carry_kernel<128><<<bh, 128, 0, st>>>(w.maps, d_final_cov, w.lam, d.nseg);
+    diag_gain_bwd_emit_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, init_prec, wr, rr, dkappa, carry, w.lam,
+                                                         w.dg_tok, dk, dalpha, domega_raw, dr_raw, dmu, d_init_cov,
+                                                         (int)d.T, (int)d.H, d.nseg);
+  } else {
+    diag_gain_bwd_carry_kernel<64><<<bh, 64, 0, st>>>(w.maps, d_final_cov, w.lam, d.nseg);
+    diag_gain_bwd_emit_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, init_prec, wr, rr, dkappa, carry, w.lam,
+                                                       w.dg_tok, dk, dalpha, domega_raw, dr_raw, dmu, d_init_cov,
+                                                       (int)d.T, (int)d.H, d.nseg);
+  }
+  return check_launch("diag_gain_bwd kernels");
+}
+
+}  // namespace
+}  // namespace kdn
+
+extern "C" {
+
 int kdn_diag_gain_fwd(const float* k, const float* alpha, const float* omega, const float* r, const float* init_prec,
                       const float* init_cov, float* kappa, float* carry, float* p_final, int64_t B, int64_t T,
                       int64_t H, int64_t K, void* ws, size_t ws_bytes, kdn_stream_t stream) {
   if (B <= 0 || H <= 0 || T <= 0 || !k || !alpha || !omega || !r || !init_prec || !kappa || !carry)
     return set_error(KDN_ERR_INVALID, "kdn_diag_gain_fwd: invalid arguments");
-  if (K != 64 && K != 128) return set_error(KDN_ERR_INVALID, "kdn_diag_gain_fwd: K must be 64 or 128, got %lld", (long long)K);
-  if (T > INT32_MAX || B * H > 65535 * 1024) return set_error(KDN_ERR_INVALID, "kdn_diag_gain_fwd: size too large");
+  DiagDims d;
+  if (int rc = diag_dims("kdn_diag_gain_fwd", B, T, H, K, &d)) return rc;
   if (ws_bytes < kdn_diag_gain_workspace_bytes(B, T, H, K) || !ws)
     return set_error(KDN_ERR_WORKSPACE, "kdn_diag_gain_fwd: workspace too small");
-  const int nseg = (int)((T + kDiagSeg - 1) / kDiagSeg);
   cudaStream_t st = (cudaStream_t)stream;
   float4* maps = static_cast<float4*>(ws);
-  dim3 grid(nseg, (unsigned)(B * H));
-  if (K == 128) {
-    diag_gain_map_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, maps, (int)T, (int)H, nseg);
-    diag_gain_carry_kernel<128><<<(unsigned)(B * H), 128, 0, st>>>(maps, init_prec, init_cov, carry, p_final, (int)H,
-                                                                   nseg);
-    diag_gain_emit_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, carry, kappa, (int)T, (int)H, nseg);
-  } else {
-    diag_gain_map_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, maps, (int)T, (int)H, nseg);
-    diag_gain_carry_kernel<64><<<(unsigned)(B * H), 64, 0, st>>>(maps, init_prec, init_cov, carry, p_final, (int)H,
-                                                                 nseg);
-    diag_gain_emit_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, carry, kappa, (int)T, (int)H, nseg);
-  }
-  return check_launch("diag_gain_fwd kernels");
+  if (int rc = diag_fwd_maps(d, k, alpha, omega, r, maps, st)) return rc;
+  return diag_fwd_finish(d, k, alpha, omega, r, init_prec, init_cov, maps, kappa, carry, p_final, st);
+}
+
+int kdn_diag_gain_fwd_maps(const float* k, const float* alpha, const float* omega, const float* r, float* total_map,
+                           int64_t B, int64_t T, int64_t H, int64_t K, void* ws, size_t ws_bytes,
+                           kdn_stream_t stream) {
+  if (B <= 0 || H <= 0 || T <= 0 || !k || !alpha || !omega || !r || !total_map)
+    return set_error(KDN_ERR_INVALID, "kdn_diag_gain_fwd_maps: invalid arguments");
+  DiagDims d;
+  if (int rc = diag_dims("kdn_diag_gain_fwd_maps", B, T, H, K, &d)) return rc;
+  if (ws_bytes < kdn_diag_gain_workspace_bytes(B, T, H, K) || !ws)
+    return set_error(KDN_ERR_WORKSPACE, "kdn_diag_gain_fwd_maps: workspace too small");
+  cudaStream_t st = (cudaStream_t)stream;
+  float4* maps = static_cast<float4*>(ws);
+  if (int rc = diag_fwd_maps(d, k, alpha, omega, r, maps, st)) return rc;
+  const unsigned bh = (unsigned)(B * H);
+  if (K == 128)
+    diag_gain_total_kernel<128><<<bh, 128, 0, st>>>(maps, reinterpret_cast<float4*>(total_map), d.nseg);
+  else
+    diag_gain_total_kernel<64><<<bh, 64, 0, st>>>(maps, reinterpret_cast<float4*>(total_map), d.nseg);
+  return check_launch("diag_gain_total_kernel");
+}
+
+int kdn_diag_gain_fwd_finish(const float* k, const float* alpha, const float* omega, const float* r,
+                             const float* init_prec, const float* init_cov, float* kappa, float* carry,
+                             float* p_final, int64_t B, int64_t T, int64_t H, int64_t K, void* ws, size_t ws_bytes,
+                             kdn_stream_t stream) {
+  if (B <= 0 || H <= 0 || T <= 0 || !k || !alpha || !omega || !r || !init_prec || !kappa || !carry)
+    return set_error(KDN_ERR_INVALID, "kdn_diag_gain_fwd_finish: invalid arguments");
+  DiagDims d;
+  if (int rc = diag_dims("kdn_diag_gain_fwd_finish", B, T, H, K, &d)) return rc;
+  if (ws_bytes < kdn_diag_gain_workspace_bytes(B, T, H, K) || !ws)
+    return set_error(KDN_ERR_WORKSPACE, "kdn_diag_gain_fwd_finish: workspace too small");
+  return diag_fwd_finish(d, k, alpha, omega, r, init_prec, init_cov, static_cast<const float4*>(ws), kappa, carry,
+                         p_final, (cudaStream_t)stream);
 }
 
 int kdn_diag_gain_fwd_noalloc(const float* k, const float* alpha, const float* omega, const float* r,
@@ -719,35 +876,21 @@ int kdn_diag_gain_fwd_noalloc(const float* k, const float* alpha, const float* o
                               int64_t T, int64_t H, int64_t K, kdn_stream_t stream) {
   if (B <= 0 || H <= 0 || T <= 0 || !k || !alpha || !omega || !r || !init_prec || !kappa || !carry)
     return set_error(KDN_ERR_INVALID, "kdn_diag_gain_fwd_noalloc: invalid arguments");
-  if (K != 64 && K != 128)
-    return set_error(KDN_ERR_INVALID, "kdn_diag_gain_fwd_noalloc: K must be 64 or 128, got %lld", (long long)K);
-  if (T > INT32_MAX || B * H > 65535 * 1024)
-    return set_error(KDN_ERR_INVALID, "kdn_diag_gain_fwd_noalloc: size too large");
-  const int64_t nseg = (T + kDiagSeg - 1) / kDiagSeg;
-  if (B * H * nseg * K > kNoAllocMapEntries)
+  DiagDims d;
+  if (int rc = diag_dims("kdn_diag_gain_fwd_noalloc", B, T, H, K, &d)) return rc;
+  if (B * H * d.nseg * K > kNoAllocMapEntries)
     return set_error(KDN_ERR_INVALID,
                      "kdn_diag_gain_fwd_noalloc: B*H*ceil(T/64)*K = %lld exceeds the static scratch of %lld entries; "
                      "use kdn_diag_gain_fwd with caller workspace",
-                     (long long)(B * H * nseg * K), (long long)kNoAllocMapEntries);
+                     (long long)(B * H * d.nseg * K), (long long)kNoAllocMapEntries);
   float4* maps = nullptr;
   int rc = noalloc_maps(&maps);
   if (rc != KDN_OK) return rc;
   // Every map entry is written by diag_gain_map_kernel before the carry
   // kernel reads it, so the scratch needs no clearing between calls.
   cudaStream_t st = (cudaStream_t)stream;
-  dim3 grid((unsigned)nseg, (unsigned)(B * H));
-  if (K == 128) {
-    diag_gain_map_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, maps, (int)T, (int)H, (int)nseg);
-    diag_gain_carry_kernel<128><<<(unsigned)(B * H), 128, 0, st>>>(maps, init_prec, nullptr, carry, p_final, (int)H,
-                                                                   (int)nseg);
-    diag_gain_emit_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, carry, kappa, (int)T, (int)H, (int)nseg);
-  } else {
-    diag_gain_map_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, maps, (int)T, (int)H, (int)nseg);
-    diag_gain_carry_kernel<64><<<(unsigned)(B * H), 64, 0, st>>>(maps, init_prec, nullptr, carry, p_final, (int)H,
-                                                                 (int)nseg);
-    diag_gain_emit_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, carry, kappa, (int)T, (int)H, (int)nseg);
-  }
-  return check_launch("diag_gain_fwd_noalloc kernels");
+  if ((rc = diag_fwd_maps(d, k, alpha, omega, r, maps, st))) return rc;
+  return diag_fwd_finish(d, k, alpha, omega, r, init_prec, nullptr, maps, kappa, carry, p_final, st);
 }
 
 int kdn_diag_gain_bwd(const float* k, const float* alpha, const float* omega, const float* r, const float* init_prec,
@@ -758,42 +901,55 @@ int kdn_diag_gain_bwd(const float* k, const float* alpha, const float* omega, co
   if (B <= 0 || H <= 0 || T <= 0 || !k || !alpha || !omega || !r || !init_prec || !omega_raw || !r_raw || !dkappa ||
       !carry || !dk || !dalpha || !domega_raw || !dr_raw)
     return set_error(KDN_ERR_INVALID, "kdn_diag_gain_bwd: invalid arguments");
-  if (K != 64 && K != 128) return set_error(KDN_ERR_INVALID, "kdn_diag_gain_bwd: K must be 64 or 128, got %lld", (long long)K);
-  if (T > INT32_MAX || B * H > 65535 * 1024) return set_error(KDN_ERR_INVALID, "kdn_diag_gain_bwd: size too large");
+  DiagDims d;
+  if (int rc = diag_dims("kdn_diag_gain_bwd", B, T, H, K, &d)) return rc;
   if (ws_bytes < kdn_diag_gain_workspace_bytes(B, T, H, K) || !ws)
     return set_error(KDN_ERR_WORKSPACE, "kdn_diag_gain_bwd: workspace too small");
-  const int nseg = (int)((T + kDiagSeg - 1) / kDiagSeg);
   cudaStream_t st = (cudaStream_t)stream;
-  char* w = static_cast<char*>(ws);
-  float2* maps = reinterpret_cast<float2*>(w);
-  w += align_up(sizeof(float2) * B * H * nseg * K, 256);
-  float* lam = reinterpret_cast<float*>(w);
-  w += align_up(sizeof(float) * B * H * nseg * K, 256);
-  float2* dg_tok = reinterpret_cast<float2*>(w);
-  if (dinit && cudaMemsetAsync(dinit, 0, sizeof(float) * H, st) != cudaSuccess)
-    return check_launch("memset d_initial_precision");
-  float* dmu = init_cov ? nullptr : dinit;  // with a carried-in covariance the prior gets no gradient here
-  dim3 grid(nseg, (unsigned)(B * H));
-  const bf16* wr = static_cast<const bf16*>(omega_raw);
-  const bf16* rr = static_cast<const bf16*>(r_raw);
-  if (K == 128) {
-    diag_gain_bwd_map_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, dkappa, carry, maps, dg_tok, (int)T,
-                                                        (int)H, nseg);
-    diag_gain_bwd_carry_kernel<128><<<(unsigned)(B * H), 128, 0, st>>>(maps, d_final_cov, lam, nseg);
-    diag_gain_bwd_emit_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, init_prec, wr, rr, dkappa, carry, lam,
-                                                         dg_tok, dk, dalpha, static_cast<bf16*>(domega_raw),
-                                                         static_cast<bf16*>(dr_raw), dmu, d_init_cov, (int)T, (int)H,
-                                                         nseg);
-  } else {
-    diag_gain_bwd_map_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, dkappa, carry, maps, dg_tok, (int)T, (int)H,
-                                                      nseg);
-    diag_gain_bwd_carry_kernel<64><<<(unsigned)(B * H), 64, 0, st>>>(maps, d_final_cov, lam, nseg);
-    diag_gain_bwd_emit_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, init_prec, wr, rr, dkappa, carry, lam,
-                                                       dg_tok, dk, dalpha, static_cast<bf16*>(domega_raw),
-                                                       static_cast<bf16*>(dr_raw), dmu, d_init_cov, (int)T, (int)H,
-                                                       nseg);
-  }
-  return check_launch("diag_gain_bwd kernels");
+  const DiagBwdWs w = diag_bwd_ws(d, ws);
+  if (int rc = diag_bwd_maps(d, k, alpha, omega, r, dkappa, carry, w, st)) return rc;
+  return diag_bwd_finish(d, k, alpha, omega, r, init_prec, init_cov, static_cast<const bf16*>(omega_raw),
+                         static_cast<const bf16*>(r_raw), dkappa, carry, d_final_cov, dk, dalpha,
+                         static_cast<bf16*>(domega_raw), static_cast<bf16*>(dr_raw), dinit, d_init_cov, w, st);
+}
+
+int kdn_diag_gain_bwd_maps(const float* k, const float* alpha, const float* omega, const float* r,
+                           const float* dkappa, const float* carry, float* total_adjoint, int64_t B, int64_t T,
+                           int64_t H, int64_t K, void* ws, size_t ws_bytes, kdn_stream_t stream) {
+  if (B <= 0 || H <= 0 || T <= 0 || !k || !alpha || !omega || !r || !dkappa || !carry || !total_adjoint)
+    return set_error(KDN_ERR_INVALID, "kdn_diag_gain_bwd_maps: invalid arguments");
+  DiagDims d;
+  if (int rc = diag_dims("kdn_diag_gain_bwd_maps", B, T, H, K, &d)) return rc;
+  if (ws_bytes < kdn_diag_gain_workspace_bytes(B, T, H, K) || !ws)
+    return set_error(KDN_ERR_WORKSPACE, "kdn_diag_gain_bwd_maps: workspace too small");
+  cudaStream_t st = (cudaStream_t)stream;
+  const DiagBwdWs w = diag_bwd_ws(d, ws);
+  if (int rc = diag_bwd_maps(d, k, alpha, omega, r, dkappa, carry, w, st)) return rc;
+  const unsigned bh = (unsigned)(B * H);
+  if (K == 128)
+    diag_gain_bwd_total_kernel<128><<<bh, 128, 0, st>>>(w.maps, reinterpret_cast<float2*>(total_adjoint), d.nseg);
+  else
+    diag_gain_bwd_total_kernel<64><<<bh, 64, 0, st>>>(w.maps, reinterpret_cast<float2*>(total_adjoint), d.nseg);
+  return check_launch("diag_gain_bwd_total_kernel");
+}
+
+int kdn_diag_gain_bwd_finish(const float* k, const float* alpha, const float* omega, const float* r,
+                             const float* init_prec, const float* init_cov, const void* omega_raw, const void* r_raw,
+                             const float* dkappa, const float* carry, const float* d_final_cov, float* dk,
+                             float* dalpha, void* domega_raw, void* dr_raw, float* dinit, float* d_init_cov,
+                             int64_t B, int64_t T, int64_t H, int64_t K, void* ws, size_t ws_bytes,
+                             kdn_stream_t stream) {
+  if (B <= 0 || H <= 0 || T <= 0 || !k || !alpha || !omega || !r || !init_prec || !omega_raw || !r_raw || !dkappa ||
+      !carry || !dk || !dalpha || !domega_raw || !dr_raw)
+    return set_error(KDN_ERR_INVALID, "kdn_diag_gain_bwd_finish: invalid arguments");
+  DiagDims d;
+  if (int rc = diag_dims("kdn_diag_gain_bwd_finish", B, T, H, K, &d)) return rc;
+  if (ws_bytes < kdn_diag_gain_workspace_bytes(B, T, H, K) || !ws)
+    return set_error(KDN_ERR_WORKSPACE, "kdn_diag_gain_bwd_finish: workspace too small");
+  return diag_bwd_finish(d, k, alpha, omega, r, init_prec, init_cov, static_cast<const bf16*>(omega_raw),
+                         static_cast<const bf16*>(r_raw), dkappa, carry, d_final_cov, dk, dalpha,
+                         static_cast<bf16*>(domega_raw), static_cast<bf16*>(dr_raw), dinit, d_init_cov,
+                         diag_bwd_ws(d, ws), (cudaStream_t)stream);
 }
 
 }  // extern "C"

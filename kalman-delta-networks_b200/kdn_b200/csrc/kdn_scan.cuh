@@ -67,7 +67,7 @@ struct ScanParams {
   void* rec;  // [BH][NT] chunk records (Rec<CF>): Qr, Kc, W0, T, Q, gate factors
   void* h;    // [BH][NT][KD/BV][KD][LDV] OpT, chunk-start states scaled by fr
   void* dh;   // [BH][NT][KD/BV][KD][LDV] OpT, chunk-end state adjoints scaled by fL
-  int* status;  // bounded waits that gave up set this word to 1
+  int* status;  // [flags, debug poll limit]: bounded waits set kStatusGaveUp / kStatusSlowWait in word 0
   const void* dO;
   const float* dST;
   float* dS0;
@@ -85,6 +85,12 @@ struct ScanParams {
   // dST and ends in ST / dS0 at the range's ends)
   int c_lo, c_hi;
   float scale;
+  // state-map mode of the tensor-core sequential forward (sequence
+  // parallelism): blockIdx.z = 0 carries initial_state with the values v to
+  // ST, blockIdx.z = 1 carries the identity with zero values to ST2 (the
+  // segment's linear state map); neither writes o or h
+  int state_map;
+  float* ST2;
 };
 
 __host__ __device__ constexpr size_t A128(size_t x) { return align_up(x, 128); }

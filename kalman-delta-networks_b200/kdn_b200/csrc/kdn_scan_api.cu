@@ -1,6 +1,7 @@
 // C ABI of the chunked memory scan: argument validation, caller-owned saved
 // state and workspace layout, and dispatch to the kernel instantiations.
 #include <math.h>
+#include <stdlib.h>
 
 #include "kdn_scan.cuh"
 
@@ -8,6 +9,9 @@ namespace kdn {
 
 template <class CF> int launch_fwd(const ScanParams&, cudaStream_t);
 template <class CF> int launch_bwd(const ScanParams&, cudaStream_t);
+template <class CF> int launch_prep(const ScanParams&, cudaStream_t);
+template <class CF> int launch_fwd_seq(const ScanParams&, cudaStream_t);
+template <class CF> int launch_bwd_state(const ScanParams&, cudaStream_t);
 template <class CF> size_t prep_dbg_bytes();
 template <class CF> size_t fwd_dbg_bytes();
 template <class CF> size_t state_bytes();
@@ -159,6 +163,25 @@ unsigned grid_for(int64_t n) {
   return (unsigned)(blocks < 148 * 16 ? (blocks > 0 ? blocks : 1) : 148 * 16);
 }
 
+__global__ void status_init_kernel(int* status, int slow_polls) {
+  status[0] = 0;
+  status[1] = slow_polls;
+}
+
+// Clear the call's status header: word 0 collects the bounded waits' flags,
+// word 1 is the debug poll limit of mbar_wait (KDN_B200_DEBUG_POLL_LIMIT,
+// 0 or unset = off; a test sets it to make the slow-wait flag fire).
+int reset_status(int* status, cudaStream_t st, const char* what) {
+  const char* env = getenv("KDN_B200_DEBUG_POLL_LIMIT");
+  const int slow = env ? atoi(env) : 0;
+  if (slow <= 0) {
+    if (cudaMemsetAsync(status, 0, 2 * sizeof(int), st) != cudaSuccess) return check_launch(what);
+    return KDN_OK;
+  }
+  status_init_kernel<<<1, 1, 0, st>>>(status, slow);
+  return check_launch(what);
+}
+
 }  // namespace
 }  // namespace kdn
 
@@ -183,30 +206,47 @@ int kdn_scan_fwd(const KdnScanArgs* a, kdn_stream_t stream) {
   Sizes s;
   if (!sizes_of(a, &s))
     return set_error(KDN_ERR_INVALID, "kdn_scan_fwd: unsupported variant/precision or shape (K and V must be 128)");
-  if (!a->q || !a->k || !a->v || !a->g || !a->o || !a->saved ||
+  const int mode = a->mode;
+  if (mode != KDN_SCAN_FULL && mode != KDN_SCAN_FWD_RECORDS && mode != KDN_SCAN_FWD_SEQUENTIAL &&
+      mode != KDN_SCAN_FWD_STATE_MAP)
+    return set_error(KDN_ERR_INVALID, "kdn_scan_fwd: mode %d is not a forward mode", mode);
+  if (mode != KDN_SCAN_FULL && a->precision != KDN_PREC_BF16)
+    return set_error(KDN_ERR_INVALID, "kdn_scan_fwd: the partial-pass modes need the bf16 precision");
+  const bool need_o = mode == KDN_SCAN_FULL || mode == KDN_SCAN_FWD_SEQUENTIAL;
+  if (!a->q || !a->k || !a->v || !a->g || (need_o && !a->o) || !a->saved ||
       (a->variant == KDN_ISO ? !a->beta : !a->kappa))
     return set_error(KDN_ERR_INVALID, "kdn_scan_fwd: null input/output pointer");
+  if (mode == KDN_SCAN_FWD_STATE_MAP && (!a->final_state || !a->final_state_map))
+    return set_error(KDN_ERR_INVALID, "kdn_scan_fwd: the state-map mode writes final_state and final_state_map");
   if (s.dbg_fwd && (!a->workspace || a->workspace_bytes < s.dbg_fwd))
     return set_error(KDN_ERR_WORKSPACE, "kdn_scan_fwd: workspace too small");
   ScanParams p;
   int rc = fill_params(a, s, &p);
   if (rc != KDN_OK) return rc;
   const cudaStream_t st = (cudaStream_t)stream;
-  if (cudaMemsetAsync(p.status, 0, sizeof(int), st) != cudaSuccess) return check_launch("kdn_scan_fwd: status reset");
+  if (reset_status(p.status, st, "kdn_scan_fwd: status reset") != KDN_OK) return KDN_ERR_CUDA;
   p.dbg = static_cast<char*>(a->workspace);
   p.dbg_stride = s.fwd_stride;
   const bool iso = a->variant == KDN_ISO;
   if (a->precision == KDN_PREC_FP32) return iso ? launch_fwd<IsoF>(p, st) : launch_fwd<DiagF>(p, st);
-  if (iso) return launch_fwd<IsoB>(p, st);
-  // 32-local gate prefix -> 64-local, kept in `saved` for the backward
   float* g64 = reinterpret_cast<float*>(static_cast<char*>(a->saved) + kHeader + s.rec + s.h);
-  const int64_t HK4 = a->H * a->K / 4, n4 = a->B * a->T * HK4;
-  gate_to64_kernel<<<grid_for(n4), 256, 0, st>>>(reinterpret_cast<const float4*>(a->g), reinterpret_cast<float4*>(g64),
-                                                 a->T, HK4, n4);
-  rc = check_launch("gate_to64_kernel");
-  if (rc != KDN_OK) return rc;
-  p.g = g64;
-  return launch_fwd<DiagB>(p, st);
+  if (!iso && (mode == KDN_SCAN_FULL || mode == KDN_SCAN_FWD_RECORDS)) {
+    // 32-local gate prefix -> 64-local, kept in `saved` for the later passes
+    const int64_t HK4 = a->H * a->K / 4, n4 = a->B * a->T * HK4;
+    gate_to64_kernel<<<grid_for(n4), 256, 0, st>>>(reinterpret_cast<const float4*>(a->g),
+                                                   reinterpret_cast<float4*>(g64), a->T, HK4, n4);
+    rc = check_launch("gate_to64_kernel");
+    if (rc != KDN_OK) return rc;
+  }
+  if (!iso) p.g = g64;
+  if (mode == KDN_SCAN_FULL) return iso ? launch_fwd<IsoB>(p, st) : launch_fwd<DiagB>(p, st);
+  if (mode == KDN_SCAN_FWD_RECORDS) return iso ? launch_prep<IsoB>(p, st) : launch_prep<DiagB>(p, st);
+  if (mode == KDN_SCAN_FWD_STATE_MAP) {
+    p.state_map = 1;
+    p.ST2 = a->final_state_map;
+    p.o = nullptr;
+  }
+  return iso ? launch_fwd_seq<IsoB>(p, st) : launch_fwd_seq<DiagB>(p, st);
 }
 
 int kdn_scan_bwd(const KdnScanArgs* a, kdn_stream_t stream) {
@@ -214,9 +254,19 @@ int kdn_scan_bwd(const KdnScanArgs* a, kdn_stream_t stream) {
   if (!sizes_of(a, &s))
     return set_error(KDN_ERR_INVALID, "kdn_scan_bwd: unsupported variant/precision or shape (K and V must be 128)");
   const bool iso = a->variant == KDN_ISO;
-  if (!a->q || !a->k || !a->v || !a->g || !a->saved || !a->dO || !a->dq || !a->dk || !a->dv || !a->dg ||
-      (iso ? (!a->beta || !a->dbeta) : (!a->kappa || !a->dkappa)))
+  const int mode = a->mode;
+  if (mode != KDN_SCAN_FULL && mode != KDN_SCAN_BWD_STATE)
+    return set_error(KDN_ERR_INVALID, "kdn_scan_bwd: mode %d is not a backward mode", mode);
+  if (mode != KDN_SCAN_FULL && a->precision != KDN_PREC_BF16)
+    return set_error(KDN_ERR_INVALID, "kdn_scan_bwd: the partial-pass modes need the bf16 precision");
+  if (mode == KDN_SCAN_BWD_STATE) {
+    if (!a->q || !a->k || !a->v || !a->g || !a->saved || !a->dO || !a->d_initial_state ||
+        (iso ? !a->beta : !a->kappa))
+      return set_error(KDN_ERR_INVALID, "kdn_scan_bwd: null input/output pointer");
+  } else if (!a->q || !a->k || !a->v || !a->g || !a->saved || !a->dO || !a->dq || !a->dk || !a->dv || !a->dg ||
+             (iso ? (!a->beta || !a->dbeta) : (!a->kappa || !a->dkappa))) {
     return set_error(KDN_ERR_INVALID, "kdn_scan_bwd: null input/output pointer");
+  }
   if (!a->workspace || a->workspace_bytes < kHeader + s.dh + s.dbg_bwd)
     return set_error(KDN_ERR_WORKSPACE, "kdn_scan_bwd: workspace too small");
   ScanParams p;
@@ -228,10 +278,11 @@ int kdn_scan_bwd(const KdnScanArgs* a, kdn_stream_t stream) {
   p.dbg = ws + kHeader + s.dh;
   p.dbg_stride = s.bwd_stride;
   const cudaStream_t st = (cudaStream_t)stream;
-  if (cudaMemsetAsync(p.status, 0, sizeof(int), st) != cudaSuccess) return check_launch("kdn_scan_bwd: status reset");
+  if (reset_status(p.status, st, "kdn_scan_bwd: status reset") != KDN_OK) return KDN_ERR_CUDA;
   if (a->precision == KDN_PREC_FP32) return iso ? launch_bwd<IsoF>(p, st) : launch_bwd<DiagF>(p, st);
+  if (!iso) p.g = reinterpret_cast<const float*>(static_cast<const char*>(a->saved) + kHeader + s.rec + s.h);
+  if (mode == KDN_SCAN_BWD_STATE) return iso ? launch_bwd_state<IsoB>(p, st) : launch_bwd_state<DiagB>(p, st);
   if (iso) return launch_bwd<IsoB>(p, st);
-  p.g = reinterpret_cast<const float*>(static_cast<const char*>(a->saved) + kHeader + s.rec + s.h);
   rc = launch_bwd<DiagB>(p, st);
   if (rc != KDN_OK) return rc;
   // cotangent of the 64-local prefix -> the boundary's 32-local one

@@ -966,6 +966,8 @@ int launch_bwd(const ScanParams& p, cudaStream_t st) {
   return launch_bwd_chunk<CF>(p, st);
 }
 
+template int launch_bwd_state<Cfg<true, 64, bf16>>(const ScanParams&, cudaStream_t);
+template int launch_bwd_state<Cfg<false, 64, bf16>>(const ScanParams&, cudaStream_t);
 template int launch_bwd<Cfg<true, 64, bf16>>(const ScanParams&, cudaStream_t);
 template int launch_bwd<Cfg<true, 64, float>>(const ScanParams&, cudaStream_t);
 template int launch_bwd<Cfg<false, 64, bf16>>(const ScanParams&, cudaStream_t);

@@ -263,6 +263,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_fwd_tc_kernel(ScanParams p
   tc::fence_after();
   const uint32_t tmem = *tslot;
 
+  // state-map mode: blockIdx.z = 1 runs the identity with zero values (no v
+  // rows, no delta term from v), and neither run writes o or h
+  const bool smap = p.state_map != 0, phi = smap && blockIdx.z == 1;
   if (warp == kTcWarps) {
     // producer: refill a stage once the MMAs of its previous chunk completed
     for (int c = p.c_lo; c < p.c_hi; ++c) {
@@ -270,9 +273,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_fwd_tc_kernel(ScanParams p
       if (it >= NS) mbar_wait(&empty[s], (it / NS - 1) & 1, p.status);
       if (lane == 0) {
         char* st = base + s * Lo::stage;
-        mbar_expect_tx(&full[s], (unsigned)(R::fwd_end + (size_t)C * 128));
+        mbar_expect_tx(&full[s], (unsigned)(R::fwd_end + (phi ? 0 : (size_t)C * 128)));
         bulk_g2s(st, recs + (size_t)c * R::bytes, (unsigned)R::fwd_end, &full[s]);
-        tma_load_4d(st + Lo::v, &maps.in, V0, h, c * C, b, &full[s]);
+        if (!phi) tma_load_4d(st + Lo::v, &maps.in, V0, h, c * C, b, &full[s]);
       }
       __syncwarp();
     }
@@ -289,7 +292,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_fwd_tc_kernel(ScanParams p
   for (int j = 0; j < 32; j += 16) {
     float x[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) x[i] = p.S0 ? p.S0[((size_t)bh * kKD + row) * kVD + V0 + 32 * hf + j + i] : 0.f;
+    for (int i = 0; i < 16; ++i) {
+      const int col = V0 + 32 * hf + j + i;
+      x[i] = phi ? (row == col ? 1.f : 0.f) : p.S0 ? p.S0[((size_t)bh * kKD + row) * kVD + col] : 0.f;
+    }
     tc::st16(tl + TS + 32 * hf + j, x);
   }
   tc::wait_st();
@@ -320,17 +326,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_fwd_tc_kernel(ScanParams p
     fence_async_shared();
     tc::fence_before();
     bar_sync(1, NTH);
-    if (threadIdx.x == 32) {
+    if (threadIdx.x == 32 && !smap) {
       bulk_s2g(hout + (size_t)c * 2 * hblock_bytes<CF>(), sS, (unsigned)hblock_bytes<CF>());
       bulk_commit();
     }
     if (threadIdx.x == 0) {
       tc::fence_after();
       constexpr uint32_t id = tc::idesc(64, C, true, false), idn = tc::idesc(64, C, true, false, true);
-      for (int ks = 0; ks < C / 16; ++ks)
-        tc::mma(tmem + TD, tc::desc_mn(st + Lo::v, C, ks), tc::desc_k(st + R::T, C, ks), id, ks > 0);
+      if (!phi)
+        for (int ks = 0; ks < C / 16; ++ks)
+          tc::mma(tmem + TD, tc::desc_mn(st + Lo::v, C, ks), tc::desc_k(st + R::T, C, ks), id, ks > 0);
       for (int ks = 0; ks < kKD / 16; ++ks)
-        tc::mma(tmem + TD, tc::desc_mn(sS, kKD, ks), tc::desc_k(st + R::Wf, C, ks), idn, true);
+        tc::mma(tmem + TD, tc::desc_mn(sS, kKD, ks), tc::desc_k(st + R::Wf, C, ks), idn, !phi || ks > 0);
       tc::commit(mmab);
     }
   };
@@ -359,10 +366,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_fwd_tc_kernel(ScanParams p
       tc::fence_after();
       constexpr uint32_t ido = tc::idesc(64, C, true, false), idd = tc::idesc(64, C, false, false);
       constexpr uint32_t ids = tc::idesc(128, 64, true, false);
-      for (int ks = 0; ks < kKD / 16; ++ks)
-        tc::mma(tmem + TO, tc::desc_mn(sS, kKD, ks), tc::desc_k(st + R::Qs, C, ks), ido, ks > 0);
-      for (int ks = 0; ks < C / 16; ++ks)
-        tc::mma(tmem + TO, tc::desc_k(sDel, 64, ks), tc::desc_k(st + R::Qq, C, ks), idd, true);
+      if (!smap) {
+        for (int ks = 0; ks < kKD / 16; ++ks)
+          tc::mma(tmem + TO, tc::desc_mn(sS, kKD, ks), tc::desc_k(st + R::Qs, C, ks), ido, ks > 0);
+        for (int ks = 0; ks < C / 16; ++ks)
+          tc::mma(tmem + TO, tc::desc_k(sDel, 64, ks), tc::desc_k(st + R::Qq, C, ks), idd, true);
+      }
       for (int ks = 0; ks < C / 16; ++ks)
         tc::mma(tmem + TS, tc::desc_mn(st + R::Kf, C, ks), tc::desc_k(sDel, 64, ks), ids, true);
       tc::commit(&empty[s]);
@@ -379,6 +388,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_fwd_tc_kernel(ScanParams p
       if (threadIdx.x == 0) bulk_wait_read<0>();
       bar_sync(1, NTH);
     }
+    if (smap) continue;
     // ... then this chunk's output rows (value column vc) into their tile and one TMA store
     {
       OutT* o = reinterpret_cast<OutT*>(sO);
@@ -400,12 +410,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_fwd_tc_kernel(ScanParams p
       bulk_commit();
     }
   }
-  if (p.ST) {
+  float* ST = phi ? p.ST2 : p.ST;
+  if (ST) {
     for (int j = 0; j < 32; j += 16) {
       float x[16];
       tc::ld16(tl + TS + 32 * hf + j, x);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) p.ST[((size_t)bh * kKD + row) * kVD + V0 + 32 * hf + j + i] = x[i];
+      for (int i = 0; i < 16; ++i) ST[((size_t)bh * kKD + row) * kVD + V0 + 32 * hf + j + i] = x[i];
     }
   }
   if (threadIdx.x == 0 || threadIdx.x == 32) bulk_wait_all();
@@ -450,9 +461,13 @@ int launch_fwd_seq(const ScanParams& p, cudaStream_t st) {
     TcMaps maps;
     rc = encode_bthd(&maps.in, p.v, true, p.B, p.T, p.H, kVD, 64, CF::C, true);
     if (rc != KDN_OK) return rc;
-    rc = encode_bthd(&maps.out, p.o, CF::ISO, p.B, p.T, p.H, kVD, 64, CF::C, false);
-    if (rc != KDN_OK) return rc;
-    scan_fwd_tc_kernel<CF><<<dim3(p.B * p.H, 2), kTcThreads, smem, st>>>(p, maps);
+    if (p.state_map) {
+      maps.out = maps.in;  // no output rows in state-map mode
+    } else {
+      rc = encode_bthd(&maps.out, p.o, CF::ISO, p.B, p.T, p.H, kVD, 64, CF::C, false);
+      if (rc != KDN_OK) return rc;
+    }
+    scan_fwd_tc_kernel<CF><<<dim3(p.B * p.H, 2, p.state_map ? 2 : 1), kTcThreads, smem, st>>>(p, maps);
     return check_launch("scan_fwd_tc_kernel");
   }
 }
@@ -464,6 +479,8 @@ int launch_fwd(const ScanParams& p, cudaStream_t st) {
   return launch_fwd_seq<CF>(p, st);
 }
 
+template int launch_fwd_seq<Cfg<true, 64, bf16>>(const ScanParams&, cudaStream_t);
+template int launch_fwd_seq<Cfg<false, 64, bf16>>(const ScanParams&, cudaStream_t);
 template int launch_fwd<Cfg<true, 64, bf16>>(const ScanParams&, cudaStream_t);
 template int launch_fwd<Cfg<true, 64, float>>(const ScanParams&, cudaStream_t);
 template int launch_fwd<Cfg<false, 64, bf16>>(const ScanParams&, cudaStream_t);

@@ -24,6 +24,7 @@ tests run it on CPU ranks (gloo) with the oracle as ``segment_fn``.
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 from typing import Callable, Sequence
 
@@ -31,6 +32,7 @@ import torch
 import torch.distributed as dist
 
 from . import _native as N
+from . import _scan
 from ._scan import ScanSaved, scan_backward, scan_forward
 
 
@@ -233,3 +235,292 @@ def sp_diag_kdn(q, k, v, g_cumsum, k_gain, alpha, omega, r, initial_precision, o
 
     return chain(fn, (q, k, v, g_cumsum, k_gain, alpha, omega, r, initial_precision, omega_raw, r_raw), templates,
                  Link.from_group(group))
+
+
+# ----------------------------------------------------------------------------- two-pass sequence parallelism
+#
+# The relay above makes rank r wait for rank r-1's whole segment.  The two
+# passes below let every rank work at once.  Both carried states enter a
+# segment through maps that do not depend on them:
+#   covariance  p_end = M(p_in), a per-channel Moebius map (the composition of
+#               the per-token maps p -> p_hat / (1 + u p_hat),
+#               p_hat = alpha^2 p + omega, diag_kdn_naive.py:256-276);
+#   memory      S_end = Phi S_in + S_end|0, Phi (K x K) the state reached from
+#               the identity with zero values, S_end|0 the state reached from
+#               zero (the recurrence is affine in S, diag_kdn_naive.py:479-500);
+# and the adjoints leave it through the transposed maps:
+#   dS_in = Phi^T dS_end + dS_in|0,   dp_in = A dp_end + dp_in|0 (per channel).
+# Forward: every rank computes M and (Phi, S_end|0) of its segment, one
+# all-gather shares them, each rank composes those of the ranks before it
+# into its true incoming (p, S), then runs the covariance carry + emit and
+# the sequential pass again from them.  Backward: every rank computes
+# dS_in|0 (its reverse sweep from a zero final adjoint), one all-gather,
+# each rank composes the ranks after it into its true final adjoint and runs
+# the full backward; then the same for the covariance cotangent.  The
+# chunk-parallel passes run once; only the sequential sweeps run twice (the
+# state-map forward sweep carries two states in one launch).
+
+
+class GroupComm:
+    """All-gather over a torch.distributed group (NCCL for CUDA tensors, e.g.
+    over NVLink on one box; gloo for CPU tensors)."""
+
+    def __init__(self, group=None):
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+
+    def all_gather(self, t: torch.Tensor) -> torch.Tensor:
+        t = t.contiguous()
+        out = torch.empty((self.world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
+        if t.is_cuda:
+            dist.all_gather_into_tensor(out, t, group=self.group)
+        else:
+            dist.all_gather(list(out.unbind(0)), t, group=self.group)
+        return out
+
+
+def mobius_apply(m: torch.Tensor, p: torch.Tensor) -> torch.Tensor:
+    """p -> (A p + B) / (C p + D) with m [..., 4] = (A, B, C, D)."""
+    return (m[..., 0] * p + m[..., 1]) / (m[..., 2] * p + m[..., 3])
+
+
+def carried_covariance(maps: torch.Tensor, p_first: torch.Tensor, rank: int) -> torch.Tensor:
+    """Covariance entering segment ``rank``: the composed maps of the
+    segments before it ([world, ...] stacked) applied to the first segment's
+    incoming covariance."""
+    p = p_first
+    for j in range(rank):
+        p = mobius_apply(maps[j], p)
+    return p
+
+
+def carried_state(phi: torch.Tensor, off: torch.Tensor, rank: int):
+    """Memory state entering segment ``rank`` (None = zero, for rank 0):
+    S_in(r) = Phi_{r-1} S_in(r-1) + off_{r-1} from S_in(0) = 0."""
+    S = None
+    for j in range(rank):
+        S = off[j].clone() if S is None else torch.matmul(phi[j], S) + off[j]
+    return S
+
+
+def carried_state_adjoint(phi: torch.Tensor, c: torch.Tensor, rank: int):
+    """Cotangent of segment ``rank``'s final state (None = zero, for the last
+    rank): dS_end(r) = Phi_{r+1}^T dS_end(r+1) + c_{r+1}."""
+    dS = None
+    for j in range(phi.shape[0] - 1, rank, -1):
+        dS = c[j].clone() if dS is None else torch.matmul(phi[j].transpose(-1, -2), dS) + c[j]
+    return dS
+
+
+def carried_covariance_adjoint(adj: torch.Tensor, rank: int):
+    """Cotangent of segment ``rank``'s final covariance (None = zero, for the
+    last rank) from the segments' composed adjoint maps adj [world, ..., 2]."""
+    lam = None
+    for j in range(adj.shape[0] - 1, rank, -1):
+        lam = adj[j][..., 1].clone() if lam is None else adj[j][..., 0] * lam + adj[j][..., 1]
+    return lam
+
+
+class DiagSegmentB200:
+    """One rank's segment of the diagonal KDN on the B200 kernels, pass by
+    pass (the C ABI's split gain phases and partial scan modes).  Inputs are
+    this rank's [B, T_r, H, D] slices, contiguous, as the operators take
+    them; ``prior`` is the per-head initial precision."""
+
+    def __init__(self, q, k, v, g_cumsum, k_gain, alpha, omega, r, prior, omega_raw, r_raw, scale):
+        N.require_cuda(q, k, v, g_cumsum, k_gain, alpha, omega, r, prior, omega_raw, r_raw)
+        self.t = dict(q=q, k=k, v=v, g=g_cumsum, k_gain=k_gain, alpha=alpha, omega=omega, r=r, prior=prior,
+                      omega_raw=omega_raw, r_raw=r_raw)
+        self.B, self.T, self.H, self.K = q.shape
+        self.scale = float(scale)
+        self.lib = N.load_library()
+        self.dev = q.device
+        self.stream = N.stream_of(q)
+        self.gain_ws = N.byte_buffer(self.lib.kdn_diag_gain_workspace_bytes(self.B, self.T, self.H, self.K), self.dev)
+
+    def _f32(self, *shape):
+        return torch.empty(*shape, dtype=torch.float32, device=self.dev)
+
+    def _gain_in(self):
+        t = self.t
+        return t["k_gain"].data_ptr(), t["alpha"].data_ptr(), t["omega"].data_ptr(), t["r"].data_ptr()
+
+    def prior_covariance(self):
+        return (1.0 / self.t["prior"]).view(1, self.H, 1).expand(self.B, self.H, self.K).contiguous()
+
+    def S_end_template(self):
+        return self._f32(self.B, self.H, self.K, self.t["v"].shape[-1])
+
+    def cotangent(self, dO):
+        """chunk_kalman's cotangent: fp32 at the boundary (the kernels round it to bf16)."""
+        return dO.float().contiguous()
+
+    # covariance, forward
+    def gain_maps(self):
+        total = self._f32(self.B, self.H, self.K, 4)
+        N.check(self.lib.kdn_diag_gain_fwd_maps(*self._gain_in(), total.data_ptr(), self.B, self.T, self.H, self.K,
+                                                self.gain_ws.data_ptr(), self.gain_ws.numel(), self.stream),
+                "kdn_diag_gain_fwd_maps")
+        return total
+
+    def gain_finish(self, p_in):
+        self.p_in = None if p_in is None else p_in.contiguous()
+        self.kappa = self._f32(self.B, self.T, self.H, self.K)
+        self.carry = self._f32(self.lib.kdn_diag_gain_carry_elems(self.B, self.T, self.H, self.K))
+        N.check(self.lib.kdn_diag_gain_fwd_finish(*self._gain_in(), self.t["prior"].data_ptr(), N.ptr(self.p_in),
+                                                  self.kappa.data_ptr(), self.carry.data_ptr(), None, self.B, self.T,
+                                                  self.H, self.K, self.gain_ws.data_ptr(), self.gain_ws.numel(),
+                                                  self.stream), "kdn_diag_gain_fwd_finish")
+
+    # memory, forward
+    def _args(self, mode):
+        t = self.t
+        a = _scan._args(N.KDN_DIAG, N.KDN_PREC_BF16, t["q"], t["v"], self.scale)
+        a.mode = mode
+        a.q, a.k, a.v, a.g = t["q"].data_ptr(), t["k"].data_ptr(), t["v"].data_ptr(), t["g"].data_ptr()
+        a.kappa = self.kappa.data_ptr()
+        return a
+
+    def scan_summary(self):
+        """(S_end|0, Phi) of the segment; leaves the chunk records in `saved`."""
+        a = self._args(N.KDN_SCAN_FWD_RECORDS)
+        self.saved = N.byte_buffer(self.lib.kdn_scan_saved_bytes(ctypes.byref(a)), self.dev)
+        a.saved = self.saved.data_ptr()
+        N.check(self.lib.kdn_scan_fwd(ctypes.byref(a), self.stream), "kdn_scan_fwd (records)")
+        _scan.check_status(self.saved, "kdn_scan_fwd (records)")
+        off, phi = self._f32(self.B, self.H, self.K, self.K), self._f32(self.B, self.H, self.K, self.K)
+        a.mode = N.KDN_SCAN_FWD_STATE_MAP
+        a.final_state, a.final_state_map = off.data_ptr(), phi.data_ptr()
+        N.check(self.lib.kdn_scan_fwd(ctypes.byref(a), self.stream), "kdn_scan_fwd (state map)")
+        _scan.check_status(self.saved, "kdn_scan_fwd (state map)")
+        return off, phi
+
+    def scan_sequential(self, S_in):
+        a = self._args(N.KDN_SCAN_FWD_SEQUENTIAL)
+        o = self._f32(self.B, self.T, self.H, self.K)
+        self.S_in = None if S_in is None else S_in.contiguous()
+        a.saved, a.o, a.initial_state = self.saved.data_ptr(), o.data_ptr(), N.ptr(self.S_in)
+        N.check(self.lib.kdn_scan_fwd(ctypes.byref(a), self.stream), "kdn_scan_fwd (sequential)")
+        _scan.check_status(self.saved, "kdn_scan_fwd (sequential)")
+        return o
+
+    # memory, backward
+    def scan_adjoint_summary(self, dO):
+        """dS_in with a zero final-state cotangent (the reverse sweep only)."""
+        a = self._args(N.KDN_SCAN_BWD_STATE)
+        ws = N.byte_buffer(self.lib.kdn_scan_workspace_bytes(ctypes.byref(a)), self.dev)
+        c = self._f32(self.B, self.H, self.K, self.K)
+        a.saved, a.dO, a.d_initial_state = self.saved.data_ptr(), dO.data_ptr(), c.data_ptr()
+        a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+        N.check(self.lib.kdn_scan_bwd(ctypes.byref(a), self.stream), "kdn_scan_bwd (state)")
+        _scan.check_status(ws, "kdn_scan_bwd (state)")
+        return c
+
+    def scan_backward(self, dO, dS_end):
+        t = self.t
+        a = self._args(N.KDN_SCAN_FULL)
+        ws = N.byte_buffer(self.lib.kdn_scan_workspace_bytes(ctypes.byref(a)), self.dev)
+        dq, dk, dv = (torch.empty_like(t[n]) for n in ("q", "k", "v"))
+        dg, dkappa = torch.empty_like(t["g"]), torch.empty_like(self.kappa)
+        dS_end = None if dS_end is None else dS_end.contiguous()
+        a.saved, a.dO, a.d_final_state = self.saved.data_ptr(), dO.data_ptr(), N.ptr(dS_end)
+        a.dq, a.dk, a.dv, a.dg, a.dkappa = dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dg.data_ptr(), dkappa.data_ptr()
+        a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+        N.check(self.lib.kdn_scan_bwd(ctypes.byref(a), self.stream), "kdn_scan_bwd")
+        _scan.check_status(ws, "kdn_scan_bwd")
+        self.dkappa = dkappa
+        return dq, dk, dv, dg
+
+    # covariance, backward
+    def gain_adjoint_summary(self):
+        total = self._f32(self.B, self.H, self.K, 2)
+        self.gain_bws = N.byte_buffer(self.lib.kdn_diag_gain_workspace_bytes(self.B, self.T, self.H, self.K), self.dev)
+        N.check(self.lib.kdn_diag_gain_bwd_maps(*self._gain_in(), self.dkappa.data_ptr(), self.carry.data_ptr(),
+                                                total.data_ptr(), self.B, self.T, self.H, self.K,
+                                                self.gain_bws.data_ptr(), self.gain_bws.numel(), self.stream),
+                "kdn_diag_gain_bwd_maps")
+        return total
+
+    def gain_backward(self, lam_end):
+        t = self.t
+        dk_gain, dalpha = torch.empty_like(t["k_gain"]), torch.empty_like(t["alpha"])
+        domega_raw, dr_raw = torch.empty_like(t["omega_raw"]), torch.empty_like(t["r_raw"])
+        dprior = self._f32(self.H)
+        lam_end = None if lam_end is None else lam_end.contiguous()
+        N.check(self.lib.kdn_diag_gain_bwd_finish(
+            *self._gain_in(), t["prior"].data_ptr(), N.ptr(self.p_in), t["omega_raw"].data_ptr(),
+            t["r_raw"].data_ptr(), self.dkappa.data_ptr(), self.carry.data_ptr(), N.ptr(lam_end),
+            dk_gain.data_ptr(), dalpha.data_ptr(), domega_raw.data_ptr(), dr_raw.data_ptr(), dprior.data_ptr(), None,
+            self.B, self.T, self.H, self.K, self.gain_bws.data_ptr(), self.gain_bws.numel(), self.stream),
+            "kdn_diag_gain_bwd_finish")
+        if self.p_in is not None:  # the prior reaches this segment only through the carried covariance
+            dprior.zero_()
+        return dk_gain, dalpha, domega_raw, dr_raw, dprior
+
+
+def diag_two_pass_forward(seg, comm):
+    """Forward of one rank's segment: returns o (fp32 [B, T_r, H, V]) and the
+    gathered state maps the backward needs."""
+    rank = comm.rank
+    maps = comm.all_gather(seg.gain_maps())
+    seg.gain_finish(None if rank == 0 else carried_covariance(maps, seg.prior_covariance(), rank))
+    off, phi = seg.scan_summary()
+    if phi.shape == off.shape:  # K = V: one all-gather, [world, 2, B, H, K, K]
+        both = comm.all_gather(torch.stack((phi, off)))
+        phis, offs = both[:, 0], both[:, 1]
+    else:
+        phis, offs = comm.all_gather(phi), comm.all_gather(off)
+    o = seg.scan_sequential(carried_state(phis, offs, rank))
+    return o, phis
+
+
+def diag_two_pass_backward(seg, comm, phis, dO):
+    """Backward of one rank's segment: returns (dq, dk, dv, dg, dk_gain,
+    dalpha, domega_raw, dr_raw, dprior); dprior is nonzero on rank 0 only
+    (sum it over ranks like any parameter gradient)."""
+    rank = comm.rank
+    dO = seg.cotangent(dO)
+    # rank 0's own summaries are needed by no one: it sends zeros of their shapes
+    c = seg.scan_adjoint_summary(dO) if rank > 0 else torch.zeros_like(seg.S_end_template())
+    cs = comm.all_gather(c)
+    dq, dk, dv, dg = seg.scan_backward(dO, carried_state_adjoint(phis, cs, rank))
+    adj = seg.gain_adjoint_summary()  # rank 0 needs its segment maps for the finish all the same
+    adjs = comm.all_gather(adj if rank > 0 else torch.zeros_like(adj))
+    dk_gain, dalpha, domega_raw, dr_raw, dprior = seg.gain_backward(carried_covariance_adjoint(adjs, rank))
+    return dq, dk, dv, dg, dk_gain, dalpha, domega_raw, dr_raw, dprior
+
+
+class _DiagTwoPass(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, comm, scale, q, k, v, g_cumsum, k_gain, alpha, omega, r, prior, omega_raw, r_raw):
+        seg = DiagSegmentB200(q, k, v, g_cumsum, k_gain, alpha, omega, r, prior, omega_raw, r_raw, scale)
+        o, phis = diag_two_pass_forward(seg, comm)
+        ctx.state = (seg, comm, phis)
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        seg, comm, phis = ctx.state
+        if do is None:
+            do = torch.zeros(seg.B, seg.T, seg.H, seg.K, dtype=torch.float32, device=seg.dev)
+        grads = diag_two_pass_backward(seg, comm, phis, do)
+        del ctx.state
+        dq, dk, dv, dg, dk_gain, dalpha, domega_raw, dr_raw, dprior = grads
+        return None, None, dq, dk, dv, dg, dk_gain, dalpha, None, None, dprior, domega_raw, dr_raw
+
+
+def sp_diag_kdn_two_pass(q, k, v, g_cumsum, k_gain, alpha, omega, r, initial_precision, omega_raw, r_raw, *,
+                         group=None, comm=None, scale=None):
+    """This rank's output of the sequence-parallel diagonal KDN (gain +
+    memory scan), every rank working at once (see the two-pass notes above).
+    Inputs are this rank's contiguous time slice, a multiple of 32 tokens
+    except on the last rank; bf16 precision only.  ``initial_precision``
+    receives its gradient on rank 0 (sum parameter gradients over ranks)."""
+    comm = GroupComm(group) if comm is None else comm
+    scale = q.shape[-1] ** -0.5 if scale is None else float(scale)
+    if N.precision() != N.KDN_PREC_BF16:
+        raise ValueError("the two-pass sequence-parallel scan runs the bf16 tensor-core kernels only")
+    cont = [t.contiguous() for t in (q, k, v, g_cumsum, k_gain, alpha, omega.detach(), r.detach(),
+                                      initial_precision, omega_raw, r_raw)]
+    return _DiagTwoPass.apply(comm, scale, *cont)

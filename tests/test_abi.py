@@ -41,7 +41,7 @@ def test_library_exports_every_declared_symbol(lib):
 
 
 def test_version(lib):
-    assert lib.kdn_version() == 100
+    assert lib.kdn_version() == 101
 
 
 def test_scan_size_queries(lib):
@@ -74,6 +74,19 @@ def test_invalid_arguments_are_rejected_without_launch(lib):
     assert rc == -1
     rc = lib.kdn_diag_gain_fwd(None, None, None, None, None, None, None, None, None, 1, 8, 1, 96, None, 0, None)
     assert rc == -1
+
+
+def test_diag_gain_rejects_grids_beyond_the_launch_limit(lib):
+    # B*H is a grid dimension of the diagonal gain kernels (limit 65535):
+    # larger batches must fail validation, not the launch
+    p = 16  # non-null placeholders: validation returns before touching memory
+    rc = lib.kdn_diag_gain_fwd(p, p, p, p, p, None, p, p, None, 2, 64, 32768, 128, p, 1 << 40, None)
+    assert rc == -1 and b"size too large" in lib.kdn_last_error()
+    rc = lib.kdn_diag_gain_fwd_noalloc(p, p, p, p, p, p, p, None, 65536, 1, 1, 128, None)
+    assert rc == -1 and b"size too large" in lib.kdn_last_error()
+    rc = lib.kdn_diag_gain_bwd(p, p, p, p, p, None, p, p, p, p, None, p, p, p, p, None, None, 65536, 64, 1, 128,
+                               p, 1 << 40, None)
+    assert rc == -1 and b"size too large" in lib.kdn_last_error()
 
 
 def test_diag_gain_sizes(lib):

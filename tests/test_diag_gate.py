@@ -169,5 +169,8 @@ def test_diag_frontend_gain_scan_composition():
         errs["d" + name] = err(a.grad, b.grad)
     for n in ("q", "k", "v", "k_gain"):
         errs["d" + n] = err(S[n].grad, Sr[n].grad)
+    from test_gpu_parity import log_errors
+
+    log_errors("diag_frontend_gain_scan_composition", errs, {})
     bad = {k: v for k, v in errs.items() if not v < 2e-2}
     assert not bad, (bad, errs)

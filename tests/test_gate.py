@@ -177,5 +177,8 @@ def test_gate_gain_scan_composition():
         errs["d" + name] = err(x.grad, y.grad)
     for n in ("q", "k", "v"):
         errs["d" + n] = err(S[n].grad, Sr[n].grad)
+    from test_gpu_parity import log_errors
+
+    log_errors("iso_frontend_gain_scan_composition", errs, {})
     bad = {k: v for k, v in errs.items() if not v < 2e-2}
     assert not bad, (bad, errs)

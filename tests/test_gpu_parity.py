@@ -4,8 +4,14 @@ Tolerances (stated per the north star):
 * gains (fp32 arithmetic): normalised max-abs error <= 1e-4;
 * scans, fp32 debug precision (``KDN_B200_PRECISION=fp32``): normalised
   max-abs error <= 1e-4 for o and every gradient;
-* scans, bf16 tensor-core precision (the product): normalised max-abs error
-  <= 2e-2 and relative Frobenius error <= 2e-2.
+* scans, bf16 tensor-core precision (the product, the tcgen05 kernels):
+  normalised max-abs error < 1.2e-2 and relative Frobenius error < 8e-3 for
+  o, the final state and every gradient.  These bars sit about 1.5x above
+  the largest errors measured on a B200 over every case here and at the
+  benchmarked shapes (8.1e-3 and 5.7e-3, both on the gate cotangent dg;
+  typical outputs 3-5e-3), well inside the north star's 2e-2.  The one
+  exception is a 3-token sequence, where the normalisation runs over three
+  rows only (dg 1.8e-2 / 1.4e-2 measured): it keeps the north star's 2e-2.
 normalised max-abs error = max|x - ref| / max|ref|.
 """
 import os
@@ -112,9 +118,11 @@ def run_diag(d, dO, kappa, scale):
 
 
 def nmax_rounded(x, ref):
-    """Like nmax, but first forgives the bf16 rounding of a bf16-typed output
-    (half an ulp, 2^-9 relative, doubled for the tie and the oracle's own
-    rounding)."""
+    """Like nmax, for an output whose dtype is bf16 by contract: each element
+    may differ from the exact value by its own rounding to bf16 (relative
+    2^-8, the unit roundoff of an 8-bit significand), so that much is
+    forgiven per element before the maximum is taken.  fp32-typed outputs
+    get no such allowance (plain ``nmax``)."""
     x = x.detach().double().cpu()
     ref = ref.detach().double().cpu()
     excess = ((x - ref).abs() - 2.0 ** -8 * ref.abs()).clamp_min(0)
@@ -125,25 +133,47 @@ def fmt(d):
     return "{" + ", ".join(f"{k}: {v:.3g}" for k, v in d.items()) + "}"
 
 
-def check(o, grads, ref, names, tol, ftol=None):
-    outs = {"o": o}
-    for n in names:
-        outs["dg" if n == "g_cumsum" else "d" + n] = grads[n]
-    errs = {}
-    for key, x in outs.items():
-        errs[key] = nmax_rounded(x, ref[key]) if x.dtype == torch.bfloat16 else nmax(x, ref[key])
+def log_errors(case, errs, ferrs):
+    """Append the measured errors of one case to ``$KDN_TEST_ERRLOG`` (JSON
+    lines) when that variable is set: the tolerances below were set from
+    these records."""
+    path = os.environ.get("KDN_TEST_ERRLOG")
+    if not path:
+        return
+    import json
+
+    with open(path, "a") as f:
+        f.write(json.dumps({"case": case, "nmax": errs, "frob": ferrs}) + "\n")
+
+
+def check_errors(case, got, ref, bf16_typed, tol, ftol=None):
+    """Normalised max-abs error of every entry of ``got`` against ``ref``
+    (bf16-typed entries after their own rounding, see ``nmax_rounded``) below
+    ``tol``, and relative Frobenius error below ``ftol`` when given."""
+    errs = {k: (nmax_rounded(got[k], ref[k]) if k in bf16_typed else nmax(got[k], ref[k])) for k in got}
+    ferrs = {k: frob(got[k], ref[k]) for k in got}
+    log_errors(case, errs, ferrs)
     bad = {k: v for k, v in errs.items() if not v < tol}
     assert not bad, f"over {tol}: {fmt(bad)}; all: {fmt(errs)}"
     if ftol is not None:
-        ferrs = {"o": frob(o, ref["o"])}
-        for n in names:
-            key = "dg" if n == "g_cumsum" else "d" + n
-            ferrs[key] = frob(grads[n], ref[key])
         badf = {k: v for k, v in ferrs.items() if not v < ftol}
         assert not badf, f"frobenius over {ftol}: {fmt(badf)}; all: {fmt(ferrs)}"
 
 
-TOL = {"fp32": (1e-4, None), "bf16": (2e-2, 2e-2)}
+def check(o, grads, ref, names, tol, ftol=None, case=None):
+    got = {"o": o}
+    for n in names:
+        got["dg" if n == "g_cumsum" else "d" + n] = grads[n]
+    bf16_typed = {k for k, x in got.items() if x.dtype == torch.bfloat16}
+    if case is None:  # the running test's id, parameters included
+        case = os.environ.get("PYTEST_CURRENT_TEST", "").split(" ")[0].split("::")[-1]
+    check_errors(case, got, {k: ref[k] for k in got}, bf16_typed, tol, ftol)
+
+
+# fp32: the SIMT debug kernels; bf16: the tcgen05 product kernels
+BF16_TOL, BF16_FTOL = 1.2e-2, 8e-3
+TOL = {"fp32": (1e-4, None), "bf16": (BF16_TOL, BF16_FTOL)}
+SHORT_TOL = {"fp32": (1e-4, None), "bf16": (2e-2, 2e-2)}  # sequences of a few tokens
 
 
 @pytest.mark.parametrize("precision", ["fp32", "bf16"], indirect=True)
@@ -152,7 +182,7 @@ def test_iso_scan(precision, B, T, H, decay):
     d = oracle.make_iso_inputs(B, T, H, seed=T + B, decay_scale=decay)
     ref = oracle.scan_grads("iso", {n: d[n] for n in ("q", "k", "v", "g_cumsum", "beta")}, d["dO"])
     o, grads = run_iso(d, d["dO"])
-    tol, ftol = TOL[precision]
+    tol, ftol = (SHORT_TOL if T < 16 else TOL)[precision]
     check(o, grads, ref, ("q", "k", "v", "g_cumsum", "beta"), tol, ftol)
 
 
@@ -291,10 +321,16 @@ def test_sp_nccl_two_gpus(tmp_path):
 
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
+    import socket
+
+    with socket.socket() as sock:  # a free port for the rendezvous
+        sock.bind(("127.0.0.1", 0))
+        port = sock.getsockname()[1]
     here = os.path.dirname(os.path.abspath(__file__))
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
-           "--master-addr=127.0.0.1", "--master-port=29533", os.path.join(here, "sp_nccl_worker.py"), str(tmp_path)]
+           "--master-addr=127.0.0.1", f"--master-port={port}", os.path.join(here, "sp_nccl_worker.py"), str(tmp_path)]
     res = subprocess.run(cmd, capture_output=True, text=True, timeout=600,
                          env={**os.environ, "NCCL_NVLS_ENABLE": "0"})
     assert res.returncode == 0, res.stdout[-2000:] + res.stderr[-4000:]
     assert "sp nccl ok" in res.stdout
+    assert "sp two-pass nccl ok" in res.stdout
