@@ -387,6 +387,50 @@ def diag_frontend_times(device, hbm, reps=20):
             "bwd_frac": bgb / hbm}
 
 
+# algorithmic bytes per token-head of the diagonal q / k normalisation (bf16
+# q, k): fwd reads q, k (2K each), writes q_memory, k_memory (2K each),
+# k_gain (4K) and the two norms (8); bwd reads q, k, the bf16 cotangents of
+# q_memory and k_memory (2K each), the fp32 one of k_gain (4K) and the norms
+# (8), writes dq, dk (2K each)
+NORM_BYTES_PER_TH = {"fwd": 12 * D + 8, "bwd": 16 * D + 8}
+
+
+def normalize_times(device, hbm, reps=20):
+    """Device time of the diagonal normalisation's C-ABI calls
+    (kdn_diag_norm_fwd / kdn_diag_norm_bwd, the kernels behind
+    _diag_kdn_normalize) at the bench shape, bf16 q and k, every cotangent
+    present; CUDA events on the launching stream."""
+    from kdn_b200 import _native as N
+
+    lib = N.load_library()
+    g = torch.Generator(device=device).manual_seed(97)
+    rn = lambda dt: torch.randn(B, T, H, D, generator=g, device=device).to(dt)  # noqa: E731
+    q, k = rn(torch.bfloat16), rn(torch.bfloat16)
+    qm, km, kg = torch.empty_like(q), torch.empty_like(k), torch.empty(B, T, H, D, device=device)
+    qn, kn = torch.empty(B, T, H, device=device), torch.empty(B, T, H, device=device)
+    dqm, dkg, dkm = rn(torch.bfloat16), rn(torch.float32), rn(torch.bfloat16)
+    dq, dk = torch.empty_like(q), torch.empty_like(k)
+    rows, stream = B * T * H, N.stream_of(q)
+
+    def fwd():
+        N.check(lib.kdn_diag_norm_fwd(q.data_ptr(), k.data_ptr(), 1, qm.data_ptr(), kg.data_ptr(), km.data_ptr(),
+                                      qn.data_ptr(), kn.data_ptr(), rows, D, stream), "kdn_diag_norm_fwd")
+
+    def bwd():
+        N.check(lib.kdn_diag_norm_bwd(q.data_ptr(), k.data_ptr(), 1, dqm.data_ptr(), dkg.data_ptr(), dkm.data_ptr(),
+                                      qn.data_ptr(), kn.data_ptr(), dq.data_ptr(), dk.data_ptr(), rows, D, stream),
+                "kdn_diag_norm_bwd")
+
+    fwd()
+    bwd()
+    fms, bms = time_region(fwd, reps, device), time_region(bwd, reps, device)
+    th = B * T * H
+    fgb = NORM_BYTES_PER_TH["fwd"] * th / (fms * 1e-3) / 1e9
+    bgb = NORM_BYTES_PER_TH["bwd"] * th / (bms * 1e-3) / 1e9
+    return {"op": "_diag_kdn_normalize (bf16 q, k)", "fwd_ms": fms, "bwd_ms": bms, "bound": "hbm", "unit": "GB/s",
+            "fwd_achieved": fgb, "bwd_achieved": bgb, "peak": hbm, "fwd_frac": fgb / hbm, "bwd_frac": bgb / hbm}
+
+
 def per_op_times(variant, x, device, reps=10):
     """Device time of the scan's two C-ABI calls, kdn_scan_fwd (chunk-record
     pass + sequential pass) and kdn_scan_bwd (reverse state sweep +
@@ -820,6 +864,8 @@ def measure(variant, args, device, dist, world, rank, warmup, varlen=False):
     }
     if not varlen:
         rec["frontend"] = (frontend_times if variant == "iso" else diag_frontend_times)(device, hbm)
+        if variant == "diag":
+            rec["normalize"] = normalize_times(device, hbm)
     return rec, x
 
 

@@ -260,6 +260,33 @@ int kdn_diag_gain_bwd(const float* k, const float* alpha, const float* omega,
                       kdn_stream_t stream);
 
 /* ------------------------------------------------------------------------ *
+ * Diagonal q / k normalisation.  Replaces _diag_kdn_normalize
+ * (lit_gpt/kdn_ops/diag_kdn_chunk.py:2162): forward kernel :194, backward
+ * kernel :235 as launched by _diag_kdn_norm_backward (:2078).
+ *
+ *   norm = |x| over each [K] row,  d = max(norm, 1e-12),
+ *   q_memory = bf16(q / d_q),  k_gain = k / d_k,  k_memory = bf16(k_gain)
+ *
+ * Bit-identical to the reference: round-to-nearest fp32 squares and sums in
+ * its reduction order, IEEE division and square root, round-to-nearest-even
+ * bf16 stores.  q_raw, k_raw: [n_rows, K] contiguous, bf16 (in_bf16 = 1) or
+ * fp32; q_memory, k_memory bf16; k_gain fp32; q_norm, k_norm fp32 [n_rows]
+ * (saved for the backward).  K is 64 or 128.  The backward takes the
+ * cotangents of q_memory (bf16), k_gain (fp32) and k_memory (bf16), each
+ * nullable (= absent), and writes dq_raw (when d_q_memory is given) and
+ * dk_raw (when either key cotangent is), both in the input dtype.
+ * ------------------------------------------------------------------------ */
+int kdn_diag_norm_fwd(const void* q_raw, const void* k_raw, int in_bf16,
+                      void* q_memory, float* k_gain, void* k_memory,
+                      float* q_norm, float* k_norm, int64_t n_rows, int64_t K,
+                      kdn_stream_t stream);
+int kdn_diag_norm_bwd(const void* q_raw, const void* k_raw, int in_bf16,
+                      const void* d_q_memory, const float* d_k_gain,
+                      const void* d_k_memory, const float* q_norm,
+                      const float* k_norm, void* dq_raw, void* dk_raw,
+                      int64_t n_rows, int64_t K, kdn_stream_t stream);
+
+/* ------------------------------------------------------------------------ *
  * Chunked memory scan (both variants).
  *
  *   S_hat = Diag(alpha_t) S,  delta = v_t - k_t^T S_hat,

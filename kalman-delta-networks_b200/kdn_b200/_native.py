@@ -107,6 +107,8 @@ _SIGNATURES = {
         [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _SZ, _P],
         ctypes.c_int,
     ),
+    "kdn_diag_norm_fwd": ([_P, _P, ctypes.c_int, _P, _P, _P, _P, _P, _I64, _I64, _P], ctypes.c_int),
+    "kdn_diag_norm_bwd": ([_P, _P, ctypes.c_int, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _P], ctypes.c_int),
     "kdn_scan_saved_bytes": ([ctypes.POINTER(KdnScanArgs)], _SZ),
     "kdn_scan_workspace_bytes": ([ctypes.POINTER(KdnScanArgs)], _SZ),
     "kdn_scan_fwd": ([ctypes.POINTER(KdnScanArgs), _P], ctypes.c_int),

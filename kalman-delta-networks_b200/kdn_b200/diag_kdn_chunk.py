@@ -3,6 +3,7 @@
 * ``_diag_kdn_gain`` (lit_gpt/kdn_ops/diag_kdn_chunk.py:2737)
 * ``chunk_kalman``   (lit_gpt/kdn_ops/diag_kdn_chunk.py:3315)
 * ``_diag_kdn_frontend_precumsum_paired`` (lit_gpt/kdn_ops/diag_kdn_chunk.py:2471)
+* ``_diag_kdn_normalize`` (lit_gpt/kdn_ops/diag_kdn_chunk.py:2162)
 
 with the reference's signatures, validation messages, tensor layouts and
 autograd contract, on the sm_100a kernels of ``libkdn_b200.so``.
@@ -353,4 +354,85 @@ def _diag_kdn_frontend_precumsum_paired(
     return _DiagKdnFrontendFunction.apply(retention_raw, omega_raw, r_raw, A_log, dt_bias, initial_precision_param)
 
 
-__all__ = ("_diag_kdn_gain", "chunk_kalman", "_diag_kdn_frontend_precumsum_paired")
+# ----------------------------------------------------------------------------- q / k normalisation
+
+
+def _validate_diag_kdn_norm_inputs(q_raw, k_raw):
+    """The reference's checks and messages (diag_kdn_chunk.py:2024-2042)."""
+    for name, value in (("q_raw", q_raw), ("k_raw", k_raw)):
+        if not isinstance(value, torch.Tensor):
+            raise TypeError(f"{name} must be a torch.Tensor")
+        if value.ndim != 4:
+            raise ValueError(f"{name} must have rank 4 [B,T,H,K]")
+        if not value.is_cuda:
+            raise ValueError(f"{name} must be a CUDA tensor")
+        if value.dtype not in (torch.bfloat16, torch.float32):
+            raise TypeError(f"{name} must be BF16 or FP32")
+        if not value.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+    if q_raw.shape != k_raw.shape or q_raw.device != k_raw.device:
+        raise ValueError("q_raw and k_raw must have matching shape and device")
+    if q_raw.dtype != k_raw.dtype or q_raw.requires_grad != k_raw.requires_grad:
+        raise ValueError("q_raw and k_raw must have matching dtype and grad mode")
+    if q_raw.shape[-1] not in (64, 128):
+        raise ValueError("q_raw and k_raw require K in {64,128}")
+
+
+class _DiagKdnNormFunction(torch.autograd.Function):
+    """(q_memory bf16, k_gain fp32, k_memory bf16) = the rows of q and k over
+    their L2 norms (kdn_diag_norm_fwd); the norms are saved for the backward
+    (kdn_diag_norm_bwd).  Absent cotangents stay absent, as in the
+    reference's Function (diag_kdn_chunk.py:2045-2075)."""
+
+    @staticmethod
+    def forward(ctx, q_raw, k_raw):
+        N.require_cuda(q_raw, k_raw)
+        lib = N.load_library()
+        K = q_raw.shape[-1]
+        rows = q_raw.numel() // K
+        q_memory = torch.empty(q_raw.shape, dtype=torch.bfloat16, device=q_raw.device)
+        k_gain = torch.empty(k_raw.shape, dtype=torch.float32, device=k_raw.device)
+        k_memory = torch.empty(k_raw.shape, dtype=torch.bfloat16, device=k_raw.device)
+        q_norm = torch.empty(q_raw.shape[:-1], dtype=torch.float32, device=q_raw.device)
+        k_norm = torch.empty(k_raw.shape[:-1], dtype=torch.float32, device=k_raw.device)
+        N.check(lib.kdn_diag_norm_fwd(q_raw.data_ptr(), k_raw.data_ptr(), int(q_raw.dtype == torch.bfloat16),
+                                      q_memory.data_ptr(), k_gain.data_ptr(), k_memory.data_ptr(), q_norm.data_ptr(),
+                                      k_norm.data_ptr(), rows, K, N.stream_of(q_raw)), "kdn_diag_norm_fwd")
+        ctx.save_for_backward(q_raw, k_raw, q_norm, k_norm)
+        ctx.set_materialize_grads(False)
+        return q_memory, k_gain, k_memory
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, d_q_memory, d_k_gain, d_k_memory):
+        if not ctx.needs_input_grad[0]:
+            d_q_memory = None
+        if not ctx.needs_input_grad[1]:
+            d_k_gain = d_k_memory = None
+        if d_q_memory is None and d_k_gain is None and d_k_memory is None:
+            return None, None
+        q_raw, k_raw, q_norm, k_norm = ctx.saved_tensors
+        lib = N.load_library()
+        K = q_raw.shape[-1]
+        rows = q_raw.numel() // K
+        dqm = None if d_q_memory is None else d_q_memory.to(torch.bfloat16).contiguous()
+        dkg = None if d_k_gain is None else d_k_gain.float().contiguous()
+        dkm = None if d_k_memory is None else d_k_memory.to(torch.bfloat16).contiguous()
+        dq = torch.empty_like(q_raw) if dqm is not None else None
+        dk = torch.empty_like(k_raw) if (dkg is not None or dkm is not None) else None
+        N.check(lib.kdn_diag_norm_bwd(q_raw.data_ptr(), k_raw.data_ptr(), int(q_raw.dtype == torch.bfloat16),
+                                      N.ptr(dqm), N.ptr(dkg), N.ptr(dkm), q_norm.data_ptr(), k_norm.data_ptr(),
+                                      N.ptr(dq), N.ptr(dk), rows, K, N.stream_of(q_raw)), "kdn_diag_norm_bwd")
+        return dq, dk
+
+
+def _diag_kdn_normalize(q_raw, k_raw):
+    """Normalise q and k at the diagonal mixer's bf16 boundary: returns
+    ``(q_memory bf16, k_gain fp32, k_memory bf16)``, bit-identical to the
+    reference (its rounding steps and reduction order, see
+    ``csrc/kdn_norm.cu``).  Replaces diag_kdn_chunk.py:2162."""
+    _validate_diag_kdn_norm_inputs(q_raw, k_raw)
+    return _DiagKdnNormFunction.apply(q_raw, k_raw)
+
+
+__all__ = ("_diag_kdn_gain", "chunk_kalman", "_diag_kdn_frontend_precumsum_paired", "_diag_kdn_normalize")

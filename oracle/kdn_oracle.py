@@ -44,6 +44,8 @@ __all__ = (
     "diag_gate",
     "diag_gate_grads",
     "make_diag_gate_inputs",
+    "diag_normalize",
+    "diag_normalize_backward",
 )
 
 LN2 = math.log(2.0)
@@ -471,3 +473,112 @@ def make_iso_gate_inputs(B, T, H, K=128, seed=0, g_dtype=torch.float32, wr_dtype
     )
     cotangents = (n(B, T, H, K), n(B, T, H), n(B, T, H), n(B, T, H), n(H))
     return inputs, cotangents
+
+
+# ----------------------------------------------------------------------------
+# Diagonal q / k normalisation (_diag_kdn_normalize, diag_kdn_chunk.py:2162;
+# kernels :194 forward, :235 backward).  Unlike the recurrences above this is
+# restated in float32 step by step, because the reference fixes every
+# rounding: squares and sums in round-to-nearest fp32 in PyTorch's reduction
+# order for a row held by one warp (lane l owns elements l, l+32, l+64, l+96:
+# ((a0 + a1) + a2) + a3 for calls of >= 16 rows, (a0 + a2) + (a1 + a3) for
+# fewer, :109-133; then a shuffle-down tree over the 32 lanes with offsets 1,
+# 2, 4, 8, 16, :128-133), IEEE division and square root, round-to-nearest-even
+# bf16 stores (:161-172).  Products and sums are single fp32 torch ops (one
+# correctly rounded operation each); square roots and quotients are taken in
+# float64 and rounded once to fp32, which gives the correctly rounded fp32
+# result (53 >= 2 * 24 + 2 bits), whereas torch's vectorised fp32 sqrt on the
+# CPU is not always correctly rounded.  The outputs are reproduced bit for bit.
+# ----------------------------------------------------------------------------
+
+def _sqrt_rn(x):
+    return torch.sqrt(x.double()).float()
+
+
+def _div_rn(a, b):
+    return (a.double() / b.double()).float()
+
+def _norm_lane_values(a, small_rows):
+    """a [rows, 32, 4] per-lane terms -> [rows, 32] lane values."""
+    f32 = torch.float32
+    if small_rows:
+        return (a[..., 0] + a[..., 2]).to(f32) + (a[..., 1] + a[..., 3]).to(f32)
+    return ((a[..., 0] + a[..., 1]) + a[..., 2]) + a[..., 3]
+
+
+def _norm_row_sum(a, small_rows):
+    """The row total of per-lane terms a [rows, 32, 4] in the reference's order."""
+    v = _norm_lane_values(a, small_rows)
+    for off in (1, 2, 4, 8, 16):
+        shifted = torch.cat((v[:, off:], v[:, 32 - off:]), 1)  # lanes past 31 keep their own value
+        v = v + shifted
+    return v[:, 0]
+
+
+def _norm_lanes(x, K):
+    """[rows, K] -> [rows, 32, 4] with lane l holding elements l + 32 j (zeros past K)."""
+    rows = x.shape[0]
+    out = torch.zeros(rows, 32, 4, dtype=torch.float32)
+    out[..., :K // 32] = x.reshape(rows, K // 32, 32).transpose(1, 2)
+    return out
+
+
+def _norm_unlanes(y, K):
+    return y[..., :K // 32].transpose(1, 2).reshape(y.shape[0], K)
+
+
+def _norm_denominator(norm):
+    return torch.where(torch.isnan(norm), norm, torch.clamp(norm, min=1e-12))
+
+
+def diag_normalize(q_raw, k_raw):
+    """``(q_memory bf16, k_gain fp32, k_memory bf16, q_norm, k_norm)`` of the
+    diagonal boundary normalisation, bit-exact (float32 CPU restatement)."""
+    shape = q_raw.shape
+    K = shape[-1]
+    rows = q_raw.numel() // K
+    small = rows < 16
+    outs = []
+    for x in (q_raw, k_raw):
+        xl = _norm_lanes(x.reshape(rows, K).float(), K)
+        norm = _sqrt_rn(_norm_row_sum(xl * xl, small))
+        d = _norm_denominator(norm)
+        outs.append((_norm_unlanes(_div_rn(xl, d[:, None, None]), K).reshape(shape), norm.reshape(shape[:-1])))
+    (qn, q_norm), (kn, k_norm) = outs
+    return qn.to(torch.bfloat16), kn, kn.to(torch.bfloat16), q_norm, k_norm
+
+
+def _norm_row_vjp(x, u, norm, small, K, out_dtype):
+    rows = norm.shape[0]
+    xl = _norm_lanes(x.reshape(rows, K).float(), K)
+    ul = _norm_lanes(u.reshape(rows, K).float(), K)
+    d = _norm_denominator(norm)[:, None, None]
+    z = (-ul) * _div_rn(_div_rn(xl, d), d)
+    g = _norm_row_sum(0.0 + z, small)[:, None, None]
+    nrm = norm[:, None, None]
+    unit = torch.where(nrm == 0, torch.zeros_like(xl), _div_rn(xl, torch.where(nrm == 0, torch.ones_like(nrm), nrm)))
+    via = torch.where(nrm >= 1e-12, g * unit, torch.zeros_like(xl))
+    total = _div_rn(ul, d) + via
+    return _norm_unlanes(total, K).to(out_dtype)
+
+
+def diag_normalize_backward(q_raw, k_raw, d_q_memory, d_k_gain, d_k_memory, q_norm, k_norm):
+    """``(d_q_raw, d_k_raw)`` of :func:`diag_normalize` (None where no
+    cotangent arrives), bit-exact: z = -u (x / d) / d, g = the ordered row sum
+    of z, dx = u / d + g x / norm, rounded once to the input dtype
+    (diag_kdn_chunk.py:174-191, :235-353)."""
+    shape = q_raw.shape
+    K = shape[-1]
+    rows = q_raw.numel() // K
+    small = rows < 16
+    dq = dk = None
+    if d_q_memory is not None:
+        dq = _norm_row_vjp(q_raw, d_q_memory.float(), q_norm.reshape(rows).float(), small, K,
+                           q_raw.dtype).reshape(shape)
+    if d_k_gain is not None or d_k_memory is not None:
+        if d_k_gain is not None and d_k_memory is not None:
+            u = d_k_gain.float() + d_k_memory.float()
+        else:
+            u = (d_k_gain if d_k_gain is not None else d_k_memory).float()
+        dk = _norm_row_vjp(k_raw, u, k_norm.reshape(rows).float(), small, K, k_raw.dtype).reshape(shape)
+    return dq, dk

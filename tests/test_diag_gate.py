@@ -127,8 +127,9 @@ def test_diag_frontend_gain_scan_composition():
     through all three, against one fp64 autograd graph of the oracle.  This
     checks the paired gate-cotangent exchange between chunk_kalman and the
     frontend (natural-log coordinates before the reverse 32-token prefix).
-    Tolerance: the bf16 scan's 2e-2 normalised max-abs error (bf16 gradients
-    after forgiving their own rounding)."""
+    Tolerance: the bf16 scan's normalised max-abs bar (1.2e-2; bf16 gradients
+    after forgiving their own rounding) for every per-token tensor, 2e-2 for
+    the parameter gradients (sums over every token)."""
     from kdn_b200.diag_kdn_chunk import _diag_kdn_gain, chunk_kalman
 
     B, T, H, K = 1, 100, 2, 128
@@ -169,8 +170,11 @@ def test_diag_frontend_gain_scan_composition():
         errs["d" + name] = err(a.grad, b.grad)
     for n in ("q", "k", "v", "k_gain"):
         errs["d" + n] = err(S[n].grad, Sr[n].grad)
-    from test_gpu_parity import log_errors
+    from test_gpu_parity import BF16_TOL, log_errors
 
     log_errors("diag_frontend_gain_scan_composition", errs, {})
-    bad = {k: v for k, v in errs.items() if not v < 2e-2}
+    # per-token tensors at the bf16 scan's bar; parameter gradients (sums over
+    # every token of the batch) at the north star's 2e-2
+    params = ('dA_log', 'ddt_bias', 'dparam')
+    bad = {k: v for k, v in errs.items() if not v < (2e-2 if k in params else BF16_TOL)}
     assert not bad, (bad, errs)

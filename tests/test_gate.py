@@ -140,8 +140,9 @@ def test_gate_gain_scan_composition():
     -> iso_kdn_gain -> _chunk_kda_precumsum_paired, backward through all
     three, against one fp64 autograd graph of the oracle.  This checks the
     paired gate-cotangent exchange between the scan and the frontend.
-    Tolerance: the bf16 scan's 2e-2 normalised max-abs error (bf16 gradients
-    after forgiving their own rounding)."""
+    Tolerance: the bf16 scan's normalised max-abs bar (1.2e-2; bf16 gradients
+    after forgiving their own rounding) for every per-token tensor, 2e-2 for
+    the parameter gradients (sums over every token)."""
     from kdn_b200.iso_kdn_chunk import _chunk_kda_precumsum_paired, iso_kdn_gain
 
     B, T, H, K = 1, 150, 2, 128
@@ -177,8 +178,11 @@ def test_gate_gain_scan_composition():
         errs["d" + name] = err(x.grad, y.grad)
     for n in ("q", "k", "v"):
         errs["d" + n] = err(S[n].grad, Sr[n].grad)
-    from test_gpu_parity import log_errors
+    from test_gpu_parity import BF16_TOL, log_errors
 
     log_errors("iso_frontend_gain_scan_composition", errs, {})
-    bad = {k: v for k, v in errs.items() if not v < 2e-2}
+    # per-token tensors at the bf16 scan's bar; parameter gradients (sums over
+    # every token of the batch) at the north star's 2e-2
+    params = ('dA_log', 'ddt_bias', 'domega_bias', 'dr_bias', 'dinitial_precision_param')
+    bad = {k: v for k, v in errs.items() if not v < (2e-2 if k in params else BF16_TOL)}
     assert not bad, (bad, errs)
