@@ -431,6 +431,50 @@ def normalize_times(device, hbm, reps=20):
             "fwd_achieved": fgb, "bwd_achieved": bgb, "peak": hbm, "fwd_frac": fgb / hbm, "bwd_frac": bgb / hbm}
 
 
+# algorithmic bytes per token-head of the gated output norm (bf16 o and gate,
+# D = 128): fwd reads o, g (2D each), writes y (2D) and rstd (4); bwd reads o,
+# g, dy (2D each) and rstd (4), writes do, dg (2D each)
+ONORM_BYTES_PER_TH = {"fwd": 6 * D + 4, "bwd": 10 * D + 4}
+
+
+def onorm_times(device, hbm, reps=20):
+    """Device time of the gated output norm's C-ABI calls
+    (kdn_rmsnorm_gated_fwd / _bwd, the kernels behind
+    kdn_b200.norm_gated.FusedRMSNormGated, the mixers' o_norm) at the bench
+    shape: one row per (b, t, h), bf16 o and gate, sigmoid gate, fp32 weight."""
+    from kdn_b200 import _native as N
+
+    lib = N.load_library()
+    g = torch.Generator(device=device).manual_seed(96)
+    rn = lambda: torch.randn(B, T, H, D, generator=g, device=device).bfloat16()  # noqa: E731
+    x, gate, dy = rn(), rn(), rn()
+    w = torch.ones(D, device=device)
+    y, dx, dg = torch.empty_like(x), torch.empty_like(x), torch.empty_like(x)
+    rows = B * T * H
+    rstd, dw = torch.empty(rows, device=device), torch.empty(D, device=device)
+    ws = N.byte_buffer(lib.kdn_rmsnorm_gated_workspace_bytes(rows, D), device)
+    stream = N.stream_of(x)
+
+    def fwd():
+        N.check(lib.kdn_rmsnorm_gated_fwd(x.data_ptr(), 1, gate.data_ptr(), 1, w.data_ptr(), y.data_ptr(),
+                                          rstd.data_ptr(), rows, D, 1e-5, 0, stream), "kdn_rmsnorm_gated_fwd")
+
+    def bwd():
+        N.check(lib.kdn_rmsnorm_gated_bwd(x.data_ptr(), 1, gate.data_ptr(), 1, w.data_ptr(), dy.data_ptr(),
+                                          rstd.data_ptr(), dx.data_ptr(), dg.data_ptr(), dw.data_ptr(), rows, D, 0,
+                                          ws.data_ptr(), ws.numel(), stream), "kdn_rmsnorm_gated_bwd")
+
+    fwd()
+    bwd()
+    fms, bms = time_region(fwd, reps, device), time_region(bwd, reps, device)
+    th = B * T * H
+    fgb = ONORM_BYTES_PER_TH["fwd"] * th / (fms * 1e-3) / 1e9
+    bgb = ONORM_BYTES_PER_TH["bwd"] * th / (bms * 1e-3) / 1e9
+    return {"op": "FusedRMSNormGated (o_norm, bf16, sigmoid gate)", "fwd_ms": fms, "bwd_ms": bms, "bound": "hbm",
+            "unit": "GB/s", "fwd_achieved": fgb, "bwd_achieved": bgb, "peak": hbm, "fwd_frac": fgb / hbm,
+            "bwd_frac": bgb / hbm}
+
+
 def per_op_times(variant, x, device, reps=10):
     """Device time of the scan's two C-ABI calls, kdn_scan_fwd (chunk-record
     pass + sequential pass) and kdn_scan_bwd (reverse state sweep +
@@ -866,6 +910,8 @@ def measure(variant, args, device, dist, world, rank, warmup, varlen=False):
         rec["frontend"] = (frontend_times if variant == "iso" else diag_frontend_times)(device, hbm)
         if variant == "diag":
             rec["normalize"] = normalize_times(device, hbm)
+        else:
+            rec["o_norm"] = onorm_times(device, hbm)
     return rec, x
 
 
@@ -936,8 +982,9 @@ def main():
            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": rec["config"],
            "gpu_launches": rec["gpu_launches"], "e2e": rec["e2e"], "roofline": rec["roofline"],
            "clocks": rec["clocks"]}
-    if "frontend" in rec:
-        out["frontend"] = rec["frontend"]
+    for key in ("frontend", "o_norm", "normalize"):
+        if key in rec:
+            out[key] = rec[key]
     cpu = rank == 0 and world == 1 and not args.no_cpu and not args.varlen
     if cpu:
         out["cpu_baseline"] = cpu_baseline(args.variant)

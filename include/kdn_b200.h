@@ -287,6 +287,60 @@ int kdn_diag_norm_bwd(const void* q_raw, const void* k_raw, int in_bf16,
                       int64_t n_rows, int64_t K, kdn_stream_t stream);
 
 /* ------------------------------------------------------------------------ *
+ * Gated RMS normalisation of the scan output.  Replaces the kernels behind
+ * flash-linear-attention's FusedRMSNormGated / rms_norm_gated
+ * (fla.modules.fused_norm_gate), the mixers' o_norm (lit_gpt/iso_kdn.py:192,
+ * 305; lit_gpt/diag_kdn.py:216, 346).
+ *
+ *   rstd = 1 / sqrt(mean(x^2) + eps),  y = x rstd weight act(g)
+ *   act = sigmoid (activation 0) or g sigmoid(g) (activation 1, "swish")
+ *
+ * x, y, dy, dx: [rows, D] contiguous, bf16 (x_bf16 = 1) or fp32; g, dg:
+ * [rows, D], bf16 (g_bf16 = 1) or fp32; weight: fp32 [D] or NULL (no affine
+ * weight); rstd: fp32 [rows] (written by the forward, read by the backward);
+ * dweight: fp32 [D], overwritten, NULL when not needed (then no workspace).
+ * D is 64 or 128.  Workspace: kdn_rmsnorm_gated_workspace_bytes(rows, D)
+ * (per-CTA partial sums of dweight, reduced in a fixed order).
+ * ------------------------------------------------------------------------ */
+size_t kdn_rmsnorm_gated_workspace_bytes(int64_t rows, int64_t D);
+int kdn_rmsnorm_gated_fwd(const void* x, int x_bf16, const void* g, int g_bf16,
+                          const float* weight, void* y, float* rstd, int64_t rows,
+                          int64_t D, float eps, int activation,
+                          kdn_stream_t stream);
+int kdn_rmsnorm_gated_bwd(const void* x, int x_bf16, const void* g, int g_bf16,
+                          const float* weight, const void* dy, const float* rstd,
+                          void* dx, void* dg, float* dweight, int64_t rows,
+                          int64_t D, int activation, void* workspace,
+                          size_t workspace_bytes, kdn_stream_t stream);
+
+/* ------------------------------------------------------------------------ *
+ * Short causal depthwise convolution with SiLU in front of the scan.
+ * Replaces the packed q/k/v convolution qkv_causal_conv1d
+ * (lit_gpt/kdn_ops/iso_kdn_chunk.py:459, kernels behind :372 and the
+ * installed causal_conv1d it calls) and the diagonal mixer's
+ * _fixed_short_conv (lit_gpt/diag_kdn.py:75).
+ *
+ *   y[b,t,c] = silu(sum_{j<W} w[c,j] x[b, t-W+1+j, c])   (silu = 0: no activation)
+ *
+ * x, dx: [B,T,C] contiguous, bf16 (x_bf16 = 1) or fp32; weight, dweight:
+ * [C][W] contiguous, bf16 (w_bf16 = 1) or fp32; W = 4.  The C channels are
+ * `groups` (1..3) blocks of C / groups (an even count), block g written to
+ * y[g] (and its cotangent read from dy[g], nullable = zero), each a
+ * contiguous [B,T,C/groups] tensor of x's dtype.  dweight is overwritten.
+ * Workspace: kdn_short_conv_workspace_bytes(B, T, C, W) (per-run partial
+ * sums of dweight, reduced in a fixed order).
+ * ------------------------------------------------------------------------ */
+size_t kdn_short_conv_workspace_bytes(int64_t B, int64_t T, int64_t C, int64_t W);
+int kdn_short_conv_fwd(const void* x, int x_bf16, const void* weight, int w_bf16,
+                       void* const* y, int64_t groups, int64_t B, int64_t T,
+                       int64_t C, int64_t W, int silu, kdn_stream_t stream);
+int kdn_short_conv_bwd(const void* x, int x_bf16, const void* weight, int w_bf16,
+                       const void* const* dy, int64_t groups, void* dx,
+                       void* dweight, int64_t B, int64_t T, int64_t C, int64_t W,
+                       int silu, void* workspace, size_t workspace_bytes,
+                       kdn_stream_t stream);
+
+/* ------------------------------------------------------------------------ *
  * Chunked memory scan (both variants).
  *
  *   S_hat = Diag(alpha_t) S,  delta = v_t - k_t^T S_hat,

@@ -109,6 +109,16 @@ _SIGNATURES = {
     ),
     "kdn_diag_norm_fwd": ([_P, _P, ctypes.c_int, _P, _P, _P, _P, _P, _I64, _I64, _P], ctypes.c_int),
     "kdn_diag_norm_bwd": ([_P, _P, ctypes.c_int, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _P], ctypes.c_int),
+    "kdn_rmsnorm_gated_workspace_bytes": ([_I64, _I64], _SZ),
+    "kdn_rmsnorm_gated_fwd": ([_P, ctypes.c_int, _P, ctypes.c_int, _P, _P, _P, _I64, _I64, _F, ctypes.c_int, _P],
+                              ctypes.c_int),
+    "kdn_rmsnorm_gated_bwd": ([_P, ctypes.c_int, _P, ctypes.c_int, _P, _P, _P, _P, _P, _P, _I64, _I64, ctypes.c_int,
+                               _P, _SZ, _P], ctypes.c_int),
+    "kdn_short_conv_workspace_bytes": ([_I64, _I64, _I64, _I64], _SZ),
+    "kdn_short_conv_fwd": ([_P, ctypes.c_int, _P, ctypes.c_int, _P, _I64, _I64, _I64, _I64, _I64, ctypes.c_int, _P],
+                           ctypes.c_int),
+    "kdn_short_conv_bwd": ([_P, ctypes.c_int, _P, ctypes.c_int, _P, _I64, _P, _P, _I64, _I64, _I64, _I64,
+                            ctypes.c_int, _P, _SZ, _P], ctypes.c_int),
     "kdn_scan_saved_bytes": ([ctypes.POINTER(KdnScanArgs)], _SZ),
     "kdn_scan_workspace_bytes": ([ctypes.POINTER(KdnScanArgs)], _SZ),
     "kdn_scan_fwd": ([ctypes.POINTER(KdnScanArgs), _P], ctypes.c_int),

@@ -819,7 +819,10 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_kernel(ScanParams p) {
       dqh[i] = xq * er;
       dkap[i] = xc * ec;
       dG[i] = xk * k8[i] * er + xq * q8[i] * er - xc * kap8[i] * ec;
-      if (r == L - 1) dG[i] += cfl[cu] + cgl[cu] * ch.gL[cu] / (ch.fr[cu] * ch.fL[cu]);
+      // the last row's state term: cgl (formed with S0' = fr S0, dS'' = fL dS)
+      // times 2^g_L / (fr fL) = 2^(rc - rr), which stays finite when the three
+      // factors underflow (a chunk whose total decay passes 2^-149)
+      if (r == L - 1) dG[i] += cfl[cu] + cgl[cu] * ex2(rc - rr);
     }
     if (!ch.fast) {
       // exact gate factors for the score terms

@@ -441,7 +441,11 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
   tc::ld16(tq + TKC + 16 * cg, xc);
   const float rr = ch.fast ? ch.gmid[key] : 0.f;
   const float rc = ch.fast ? ch.gmid[key] : ch.glast[key];
-  const float last = cfl[key] + cgl[key] * ch.gL[key] / (ch.fr[key] * ch.fL[key]);
+  // the last row's state term: cgl was formed with S0' = fr S0 and dS'' = fL dS,
+  // so it carries 2^g_L / (fr fL) = 2^(rc - rr) (1 on the fast path); taken as
+  // that power so it stays finite when 2^g_L, fr and fL all underflow (a chunk
+  // whose total decay passes 2^-149 while its range around rho stays small)
+  const float last = cfl[key] + cgl[key] * ex2(rc - rr);
   float* part = reinterpret_cast<float*>(base + Lo::X);  // [4 quadrants][3][C] partial token sums
   // exact-path terms of 8 tokens per thread, [8][4][512] fp32 over the operand
   // tiles Kr .. Xs (dead once the score MMAs are skipped)

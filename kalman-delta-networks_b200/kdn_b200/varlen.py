@@ -30,13 +30,18 @@ the host: a CUDA tensor costs a device synchronisation).
 """
 from __future__ import annotations
 
+import collections
+
 from typing import Callable, Sequence
 
 import torch
 
 from . import diag_kdn_chunk, iso_kdn_chunk
 
-_INDEX_CACHE: dict = {}
+# gather plans by (offsets, bucket, device), least recently used last; bounded
+# so that a stream of distinct packings cannot grow it without limit
+_INDEX_CACHE: "collections.OrderedDict" = collections.OrderedDict()
+_INDEX_CACHE_MAX = 64
 
 
 def offsets(cu_seqlens) -> list[int]:
@@ -58,6 +63,7 @@ def _plan(cu: list[int], bucket: int, chunk: int, device: torch.device):
     key = (tuple(cu), bucket, chunk, str(device))
     plan = _INDEX_CACHE.get(key)
     if plan is not None:
+        _INDEX_CACHE.move_to_end(key)
         return plan
     groups: dict[int, list[int]] = {}
     for i in range(len(cu) - 1):
@@ -79,6 +85,8 @@ def _plan(cu: list[int], bucket: int, chunk: int, device: torch.device):
     out[(start + pos)[valid]] = torch.nonzero(valid).squeeze(1)
     plan = (shapes, src.to(device), valid.to(device), src_g.to(device), hold.to(device), out.to(device))
     _INDEX_CACHE[key] = plan
+    while len(_INDEX_CACHE) > _INDEX_CACHE_MAX:
+        _INDEX_CACHE.popitem(last=False)
     return plan
 
 

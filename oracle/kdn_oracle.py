@@ -46,6 +46,7 @@ __all__ = (
     "make_diag_gate_inputs",
     "diag_normalize",
     "diag_normalize_backward",
+    "rms_norm_gated",
 )
 
 LN2 = math.log(2.0)
@@ -582,3 +583,21 @@ def diag_normalize_backward(q_raw, k_raw, d_q_memory, d_k_gain, d_k_memory, q_no
             u = (d_k_gain if d_k_gain is not None else d_k_memory).float()
         dk = _norm_row_vjp(k_raw, u, k_norm.reshape(rows).float(), small, K, k_raw.dtype).reshape(shape)
     return dq, dk
+
+
+# ----------------------------------------------------------------------------
+# Gated RMS normalisation of the scan output (the mixers' o_norm:
+# flash-linear-attention's FusedRMSNormGated, lit_gpt/iso_kdn.py:192-197,
+# 305-314; diag_kdn.py:216-221, 346-355): y = x rstd w act(g),
+# rstd = 1 / sqrt(mean(x^2) + eps), act = sigmoid or g sigmoid(g).
+# ----------------------------------------------------------------------------
+
+def rms_norm_gated(x, g, weight, eps=1e-5, activation="sigmoid", dtype=torch.float64):
+    """Forward in ``dtype`` (differentiable); weight may be None."""
+    x, g = x.to(dtype), g.to(dtype)
+    rstd = torch.rsqrt((x * x).mean(-1, keepdim=True) + eps)
+    y = x * rstd
+    if weight is not None:
+        y = y * weight.to(dtype)
+    s = torch.sigmoid(g)
+    return y * (g * s if activation in ("swish", "silu") else s)
