@@ -475,6 +475,52 @@ def onorm_times(device, hbm, reps=20):
             "bwd_frac": bgb / hbm}
 
 
+# algorithmic bytes per token-head of the packed q/k/v short convolution (bf16,
+# 3 x 128 channels per head): fwd reads x (3 * 2D), writes q, k, v (3 * 2D);
+# bwd reads x and dq, dk, dv (3 * 2D each), writes dx (3 * 2D)
+CONV_BYTES_PER_TH = {"fwd": 12 * D, "bwd": 18 * D}
+
+
+def conv_times(device, hbm, reps=20):
+    """Device time of the short convolution's C-ABI calls (kdn_short_conv_fwd /
+    _bwd, the kernels behind kdn_b200.short_conv.qkv_causal_conv1d) on the
+    bench shape's packed projection output: x [B, T, 3 H D] bf16, fp32 weight."""
+    import ctypes
+
+    from kdn_b200 import _native as N
+
+    lib = N.load_library()
+    g = torch.Generator(device=device).manual_seed(95)
+    C = 3 * H * D
+    x = torch.randn(B, T, C, generator=g, device=device).bfloat16()
+    w = torch.randn(C, 4, generator=g, device=device) * 0.5
+    ys = [torch.empty(B, T, H * D, device=device, dtype=torch.bfloat16) for _ in range(3)]
+    dys = [torch.randn(B, T, H * D, generator=g, device=device).bfloat16() for _ in range(3)]
+    dx, dw = torch.empty_like(x), torch.empty_like(w)
+    ws = N.byte_buffer(lib.kdn_short_conv_workspace_bytes(B, T, C, 4), device)
+    yp = (ctypes.c_void_p * 3)(*[t.data_ptr() for t in ys])
+    dyp = (ctypes.c_void_p * 3)(*[t.data_ptr() for t in dys])
+    stream = N.stream_of(x)
+
+    def fwd():
+        N.check(lib.kdn_short_conv_fwd(x.data_ptr(), 1, w.data_ptr(), 0, yp, 3, B, T, C, 4, 1, stream),
+                "kdn_short_conv_fwd")
+
+    def bwd():
+        N.check(lib.kdn_short_conv_bwd(x.data_ptr(), 1, w.data_ptr(), 0, dyp, 3, dx.data_ptr(), dw.data_ptr(), B, T,
+                                       C, 4, 1, ws.data_ptr(), ws.numel(), stream), "kdn_short_conv_bwd")
+
+    fwd()
+    bwd()
+    fms, bms = time_region(fwd, reps, device), time_region(bwd, reps, device)
+    th = B * T * H
+    fgb = CONV_BYTES_PER_TH["fwd"] * th / (fms * 1e-3) / 1e9
+    bgb = CONV_BYTES_PER_TH["bwd"] * th / (bms * 1e-3) / 1e9
+    return {"op": "qkv_causal_conv1d (bf16 x, fp32 weight, SiLU)", "fwd_ms": fms, "bwd_ms": bms, "bound": "hbm",
+            "unit": "GB/s", "fwd_achieved": fgb, "bwd_achieved": bgb, "peak": hbm, "fwd_frac": fgb / hbm,
+            "bwd_frac": bgb / hbm}
+
+
 def per_op_times(variant, x, device, reps=10):
     """Device time of the scan's two C-ABI calls, kdn_scan_fwd (chunk-record
     pass + sequential pass) and kdn_scan_bwd (reverse state sweep +
@@ -912,6 +958,7 @@ def measure(variant, args, device, dist, world, rank, warmup, varlen=False):
             rec["normalize"] = normalize_times(device, hbm)
         else:
             rec["o_norm"] = onorm_times(device, hbm)
+            rec["short_conv"] = conv_times(device, hbm)
     return rec, x
 
 
@@ -927,6 +974,7 @@ def main():
     ap.add_argument("--no-diag", action="store_true", help="skip the config-2 (diag) sub-record of an iso run")
     ap.add_argument("--no-triton", action="store_true", help="skip the reference's Triton kernels")
     ap.add_argument("--no-sp", action="store_true", help="skip the config-4 sequence-parallel record")
+    ap.add_argument("--no-varlen", action="store_true", help="skip the config-4 packed variable-length record")
     ap.add_argument("--eager", action="store_true", help="time eager steps instead of a replayed CUDA graph")
     ap.add_argument("--varlen", action="store_true",
                     help="config 4 packed batch: diag, B=1, T=131072 of sequences ~U[256, 8192] (cu_seqlens)")
@@ -982,7 +1030,7 @@ def main():
            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": rec["config"],
            "gpu_launches": rec["gpu_launches"], "e2e": rec["e2e"], "roofline": rec["roofline"],
            "clocks": rec["clocks"]}
-    for key in ("frontend", "o_norm", "normalize"):
+    for key in ("frontend", "o_norm", "short_conv", "normalize"):
         if key in rec:
             out[key] = rec[key]
     cpu = rank == 0 and world == 1 and not args.no_cpu and not args.varlen
@@ -1003,6 +1051,18 @@ def main():
         del xd
     if args.variant == "iso" and not args.varlen and not args.no_sp:
         out["sp"] = measure_sp(args, device, dist, world, rank, warmup)
+    if args.variant == "iso" and not args.varlen and not args.no_varlen:
+        # config 4's packed variant (31 sequences ~U[256, 8192], 131,072 tokens, diag), per rank
+        saved_bt = globals()["B"], globals()["T"]
+        globals()["B"], globals()["T"] = 1, VARLEN_T
+        no_e2e, args.no_e2e = args.no_e2e, True
+        try:
+            vrec, _ = measure("diag", args, device, dist, world, rank, warmup, varlen=True)
+        finally:
+            globals()["B"], globals()["T"] = saved_bt
+            args.no_e2e = no_e2e
+        out["varlen"] = {k: vrec[k] for k in ("value", "unit", "ms_per_step", "timing", "config", "gpu_launches",
+                                              "roofline", "clocks")}
     if rank == 0:
         print(json.dumps(out))
     if dist is not None:

@@ -47,6 +47,7 @@ __all__ = (
     "diag_normalize",
     "diag_normalize_backward",
     "rms_norm_gated",
+    "short_conv",
 )
 
 LN2 = math.log(2.0)
@@ -601,3 +602,17 @@ def rms_norm_gated(x, g, weight, eps=1e-5, activation="sigmoid", dtype=torch.flo
         y = y * weight.to(dtype)
     s = torch.sigmoid(g)
     return y * (g * s if activation in ("swish", "silu") else s)
+
+
+# ----------------------------------------------------------------------------
+# Short causal depthwise convolution with SiLU (the mixers' q/k/v short
+# convolution: qkv_causal_conv1d, iso_kdn_chunk.py:459; _fixed_short_conv,
+# diag_kdn.py:75): y[t, c] = silu(sum_j w[c, j] x[t - W + 1 + j, c]).
+# ----------------------------------------------------------------------------
+
+def short_conv(x, weight, silu=True, dtype=torch.float64):
+    """x [B, T, C], weight [C, W] -> [B, T, C] in ``dtype`` (differentiable)."""
+    W = weight.shape[-1]
+    xt = torch.nn.functional.pad(x.to(dtype).transpose(1, 2), (W - 1, 0))
+    y = torch.nn.functional.conv1d(xt, weight.to(dtype).unsqueeze(1), groups=x.shape[-1]).transpose(1, 2)
+    return torch.nn.functional.silu(y) if silu else y

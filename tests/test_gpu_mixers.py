@@ -2,15 +2,16 @@
 ``lit_gpt/diag_kdn.py``) run with the B200 operators bound in exactly as
 INTEGRATION.md section 1 shows, forward and backward, and agree with the same
 mixers whose kdn_ops are oracle-backed (float64 CPU autograd).  The mixers'
-output norm is bound to ``kdn_b200.norm_gated.FusedRMSNormGated`` as well, and
-the reference run keeps flash-linear-attention's.
+q/k/v short convolutions and output norm are bound to ``kdn_b200.short_conv``
+and ``kdn_b200.norm_gated`` as well, and the reference run keeps the
+reference's convolution kernels and flash-linear-attention's norm.
 
 The mixers come from the unmodified install of the reference in
 ``baseline/_ref`` (its package ``__init__`` needs ``lightning``, which is not
 installed, so the package object is made without running it; the mixer and
 kdn_ops modules themselves load as shipped).  Everything else inside the
-mixers (projections, the reference's short convolutions) runs unchanged in
-both runs, so the difference measures the bound operators only.  Tolerance: the north star's bf16 bar,
+mixers (the projections) runs unchanged in both runs, so the difference
+measures the bound operators only.  Tolerance: the north star's bf16 bar,
 2e-2, in normalised max-abs and relative Frobenius error, on the mixer output
 and the input gradient; 8e-2 on the parameter gradients, each a sum over
 every token of the batch.  The gate path's (A_log, dt_bias, f_proj) sum the
@@ -27,6 +28,7 @@ import pytest
 import torch
 
 import oracle
+from kdn_b200 import short_conv as our_conv
 from kdn_b200.norm_gated import FusedRMSNormGated as OurNorm
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -154,6 +156,8 @@ def test_reference_iso_mixer_with_b200_ops():
     ops.iso_kdn_gain = ours.iso_kdn_gain
     ops._chunk_kda_precumsum_paired = ours._chunk_kda_precumsum_paired
     ops._iso_kdn_gate_precumsum_paired = ours._iso_kdn_gate_precumsum_paired
+    reference_conv = ops.qkv_causal_conv1d
+    ops.qkv_causal_conv1d = our_conv.qkv_causal_conv1d  # called by PackedQKV.forward at run time
     mod = reference_modules("iso_kdn")
     assert mod._chunk_kda_precumsum_paired is ours._chunk_kda_precumsum_paired
     mod.FusedRMSNormGated = OurNorm  # the mixer's o_norm (its module imports it from fla.modules)
@@ -166,6 +170,7 @@ def test_reference_iso_mixer_with_b200_ops():
 
     ref_mixer = copy.deepcopy(mixer)
     ref_mixer.o_norm = fla_norm_like(mixer.o_norm)
+    ops.qkv_causal_conv1d = reference_conv
     mod._iso_kdn_gate_precumsum_paired = oracle_iso_gate
     mod.iso_kdn_gain = oracle_iso_gain
     mod._chunk_kda_precumsum_paired = oracle_iso_scan
@@ -184,6 +189,8 @@ def test_reference_diag_mixer_with_b200_ops():
             setattr(ops, n, getattr(ours, n))
         mod = reference_modules("diag_kdn")
         mod.FusedRMSNormGated = OurNorm
+        reference_conv = mod._fixed_short_conv
+        mod._fixed_short_conv = our_conv.fixed_short_conv
         torch.manual_seed(0)
         mixer = mod.DiagonalKalmanDeltaNetwork(hidden_size=256, head_dim=128, num_heads=2).cuda().train()
         x = torch.randn(2, 160, 256, generator=torch.Generator().manual_seed(2)).cuda()
@@ -191,6 +198,7 @@ def test_reference_diag_mixer_with_b200_ops():
 
         ref_mixer = copy.deepcopy(mixer)
         ref_mixer.o_norm = fla_norm_like(mixer.o_norm)
+        mod._fixed_short_conv = reference_conv
         ops._diag_kdn_normalize = oracle_diag_normalize
         ops._diag_kdn_frontend_precumsum_paired = oracle_diag_frontend
         ops._diag_kdn_gain = oracle_diag_gain

@@ -130,3 +130,41 @@ def test_iso_varlen_matches_per_sequence(bucket):
         assert close(o[:, sl], o_i), f"seq {i}: o"
         for n in ISO_GRADS:
             assert close(grads[n][:, sl], g_i[n]), f"seq {i}: d{n}"
+
+
+@pytest.mark.gpu
+def test_diag_varlen_against_the_oracle():
+    """The packed call against the float64 oracle directly, sequence by
+    sequence (gain + memory recurrence restarting at every boundary): the
+    bf16 scan's bars, the few-token bar for a 7-token sequence."""
+    from test_gpu_parity import BF16_FTOL, BF16_TOL, check_errors
+
+    lens = [200, 64, 7, 130]
+    ds = [oracle.make_diag_inputs(1, n, 2, seed=300 + i) for i, n in enumerate(lens)]
+    for d in ds:
+        d["dO"] = d["dO"].bfloat16().float()  # chunk_kalman rounds its cotangent to bf16
+    x = pack(ds, DIAG)
+    x["initial_precision"] = ds[0]["initial_precision"]
+    cu = [0]
+    for n in lens:
+        cu.append(cu[-1] + n)
+    o, grads = diag_step(x, torch.tensor(cu), 64)
+    for i, d in enumerate(ds):
+        sl = slice(cu[i], cu[i + 1])
+        L = {n: d[n].double().clone().requires_grad_(True) for n in ("q", "k", "v", "k_gain", "alpha", "omega_raw",
+                                                                      "r_raw")}
+        G = (d["g_cumsum"].double() * oracle.LN2).requires_grad_(True)
+        omega = torch.nn.functional.softplus(L["omega_raw"])
+        r = 0.01 + torch.nn.functional.softplus(L["r_raw"])
+        kappa, _ = oracle.diag_gain(L["k_gain"], L["alpha"], omega, r, x["initial_precision"].double())
+        S0 = torch.zeros(1, 2, 128, 128, dtype=torch.float64)
+        o_r, _ = oracle.memory_recurrence(L["q"], L["k"], L["v"], oracle.alpha_from_g_cumsum(G, 32), kappa, S0,
+                                          128 ** -0.5)
+        (o_r * d["dO"].double()).sum().backward()
+        got = {"o": o[:, sl], "dg": grads["g_cumsum"][:, sl]}
+        ref = {"o": o_r.detach(), "dg": G.grad}
+        for n in ("q", "k", "v", "k_gain", "alpha", "omega_raw", "r_raw"):
+            got["d" + n], ref["d" + n] = grads[n][:, sl], L[n].grad
+        short = lens[i] < 16
+        check_errors(f"varlen_diag_seq{i}", got, ref, {"dq", "dk", "dv", "domega_raw", "dr_raw"},
+                     2e-2 if short else BF16_TOL, 2e-2 if short else BF16_FTOL)
