@@ -794,6 +794,71 @@ def measure_sp(args, device, dist, world, rank, warmup):
     return rec
 
 
+# ----------------------------------------------------------------------------- full training step (config 3)
+
+
+def measure_model(args, device, dist, world, rank, warmup, steps=5):
+    """Config 3: one training step of the reference's own iso_kdn_1.3B model
+    (lit_gpt.model.GPT from the unmodified install in baseline/_ref: 18
+    blocks of RMSNorm -> KDN mixer -> RMSNorm -> SwiGLU MLP, untied 32,000
+    embedding and head) with kdn_b200's kernels bound in
+    (kdn_b200.reference_binding): random-init fp32 weights under bf16
+    autocast (the reference's bf16-mixed), uniform random token ids, micro
+    batch 4 x 4096 per GPU, the reference's fused cross-entropy, backward and
+    a fused AdamW step; data parallel over the ranks (DDP, NCCL all-reduce of
+    the gradients).  CUDA events around the timed steps, max over ranks."""
+    from functools import partial
+
+    from kdn_b200.reference_binding import load_reference
+
+    ref = load_reference(os.path.join(ROOT, "baseline", "_ref"))
+    cfg = ref.config.Config.from_name("iso_kdn_1.3B")
+    torch.manual_seed(0)
+    with torch.device(device):
+        model = ref.model.GPT(cfg)
+    model.apply(partial(model._init_weights, n_layer=cfg.n_layer))
+    n_params = sum(p.numel() for p in model.parameters())
+    ddp = model
+    if dist is not None:
+        ddp = torch.nn.parallel.DistributedDataParallel(model, device_ids=[device.index])
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-4, betas=(0.9, 0.95), weight_decay=0.1, fused=True)
+    loss_fn = ref.FusedCrossEntropyLoss()
+    Bm, Tm = 4, cfg.block_size
+    gen = torch.Generator(device=device).manual_seed(4242 + rank)
+    tokens = torch.randint(0, cfg.vocab_size, (Bm, Tm + 1), generator=gen, device=device)
+    inp, tgt = tokens[:, :-1].contiguous(), tokens[:, 1:].contiguous()
+    losses = []
+
+    def step():
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            logits = ddp(inp)
+            loss = loss_fn(logits.reshape(-1, logits.shape[-1]), tgt.reshape(-1))
+        loss.backward()
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+        losses.append(loss.detach())
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize(device)
+    if dist is not None:
+        dist.barrier()
+    ms = time_region(step, steps, device)
+    if dist is not None:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    loss_vals = [float(x) for x in losses]
+    rec = {"workload": f"iso_kdn_1.3B training step (reference GPT, kdn_b200 kernels bound in), micro batch "
+                       f"{Bm}x{Tm} per GPU, bf16 autocast, fused AdamW, DDP x{world}",
+           "value": Bm * Tm * world / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms, "n_gpus": world,
+           "params": n_params, "steps": steps, "timing": "eager", "loss_first": loss_vals[0],
+           "loss_last": loss_vals[-1], "loss_finite": all(x == x and abs(x) < 1e4 for x in loss_vals)}
+    del ddp, model, opt, tokens, inp, tgt
+    torch.cuda.empty_cache()
+    return rec
+
+
 # ----------------------------------------------------------------------------- main
 
 
@@ -975,6 +1040,7 @@ def main():
     ap.add_argument("--no-triton", action="store_true", help="skip the reference's Triton kernels")
     ap.add_argument("--no-sp", action="store_true", help="skip the config-4 sequence-parallel record")
     ap.add_argument("--no-varlen", action="store_true", help="skip the config-4 packed variable-length record")
+    ap.add_argument("--no-model", action="store_true", help="skip the config-3 full training step record")
     ap.add_argument("--eager", action="store_true", help="time eager steps instead of a replayed CUDA graph")
     ap.add_argument("--varlen", action="store_true",
                     help="config 4 packed batch: diag, B=1, T=131072 of sequences ~U[256, 8192] (cu_seqlens)")
@@ -1063,6 +1129,11 @@ def main():
             args.no_e2e = no_e2e
         out["varlen"] = {k: vrec[k] for k in ("value", "unit", "ms_per_step", "timing", "config", "gpu_launches",
                                               "roofline", "clocks")}
+    if args.variant == "iso" and not args.varlen and not args.no_model:
+        try:
+            out["model"] = measure_model(args, device, dist, world, rank, warmup=3)
+        except Exception as e:  # reported, never fatal to the line
+            out["model"] = {"unavailable": f"{type(e).__name__}: {str(e).splitlines()[0][:300]}"}
     if rank == 0:
         print(json.dumps(out))
     if dist is not None:
