@@ -797,7 +797,7 @@ def measure_sp(args, device, dist, world, rank, warmup):
 # ----------------------------------------------------------------------------- full training step (config 3)
 
 
-def measure_model(args, device, dist, world, rank, warmup, steps=5):
+def measure_model(args, device, dist, world, rank, warmup, steps=5, name="iso_kdn_1.3B", bind=True):
     """Config 3: one training step of the reference's own iso_kdn_1.3B model
     (lit_gpt.model.GPT from the unmodified install in baseline/_ref: 18
     blocks of RMSNorm -> KDN mixer -> RMSNorm -> SwiGLU MLP, untied 32,000
@@ -811,8 +811,8 @@ def measure_model(args, device, dist, world, rank, warmup, steps=5):
 
     from kdn_b200.reference_binding import load_reference
 
-    ref = load_reference(os.path.join(ROOT, "baseline", "_ref"))
-    cfg = ref.config.Config.from_name("iso_kdn_1.3B")
+    ref = load_reference(os.path.join(ROOT, "baseline", "_ref"), bind=bind)
+    cfg = ref.config.Config.from_name(name)
     torch.manual_seed(0)
     with torch.device(device):
         model = ref.model.GPT(cfg)
@@ -849,7 +849,8 @@ def measure_model(args, device, dist, world, rank, warmup, steps=5):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = t.item()
     loss_vals = [float(x) for x in losses]
-    rec = {"workload": f"iso_kdn_1.3B training step (reference GPT, kdn_b200 kernels bound in), micro batch "
+    kernels = "kdn_b200 kernels bound in" if bind else "the reference's own Triton kernels"
+    rec = {"workload": f"{name} training step (reference GPT, {kernels}), micro batch "
                        f"{Bm}x{Tm} per GPU, bf16 autocast, fused AdamW, DDP x{world}",
            "value": Bm * Tm * world / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms, "n_gpus": world,
            "params": n_params, "steps": steps, "timing": "eager", "loss_first": loss_vals[0],
@@ -1130,10 +1131,22 @@ def main():
         out["varlen"] = {k: vrec[k] for k in ("value", "unit", "ms_per_step", "timing", "config", "gpu_launches",
                                               "roofline", "clocks")}
     if args.variant == "iso" and not args.varlen and not args.no_model:
-        try:
-            out["model"] = measure_model(args, device, dist, world, rank, warmup=3)
-        except Exception as e:  # reported, never fatal to the line
-            out["model"] = {"unavailable": f"{type(e).__name__}: {str(e).splitlines()[0][:300]}"}
+        # config 3: the reference's model trained on our kernels; at one GPU also
+        # the diagonal model on the reference's own kernels (its iso scan cannot
+        # run on this box's flash-linear-attention, see triton_reference)
+        out["model"] = {}
+        runs = [("iso_kdn_1.3B", True), ("diag_kdn_1.3B", True)]
+        if world == 1 and not args.no_triton:
+            runs.append(("diag_kdn_1.3B", False))
+        for name, bind in runs:
+            key = name if bind else name + " (reference kernels)"
+            try:
+                out["model"][key] = measure_model(args, device, dist, world, rank, warmup=3, name=name, bind=bind)
+            except Exception as e:  # reported, never fatal to the line
+                out["model"][key] = {"unavailable": f"{type(e).__name__}: {str(e).splitlines()[0][:300]}"}
+        ours_d, ref_d = out["model"].get("diag_kdn_1.3B", {}), out["model"].get("diag_kdn_1.3B (reference kernels)", {})
+        if "ms_per_step" in ours_d and "ms_per_step" in ref_d:
+            out["model"]["diag_speedup_vs_reference_kernels"] = ref_d["ms_per_step"] / ours_d["ms_per_step"]
     if rank == 0:
         print(json.dumps(out))
     if dist is not None:

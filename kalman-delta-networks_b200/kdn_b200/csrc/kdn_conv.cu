@@ -12,9 +12,12 @@
 // x is [B,T,C] with channel stride 1; the channels form `groups` blocks of D
 // (3 for the packed q|k|v input), each written to / read from its own
 // contiguous [B,T,D] tensor.  A thread owns two adjacent channels over a run
-// of kConvRun tokens and slides a W-token window down them in registers, so x
-// and y move once (plus a three-token halo per run).  The backward recomputes
-// pre from x, and leaves per-(b, run) partial rows of dw in the workspace,
+// of kConvRun tokens and slides a W-token window down them; the run's tokens
+// are read in blocks of kConvBlk whose loads are all issued before the
+// block's arithmetic and stores (restrict-qualified pointers, compile-time
+// dtype), so several loads are in flight per thread at high occupancy.  The
+// backward recomputes pre from x, and leaves per-(b, run) partial rows of dw
+// in the workspace,
 // summed in a fixed order by a second kernel (deterministic).  fp32
 // arithmetic; outputs in the input dtype, dw in the weight dtype.
 #include "kdn_common.cuh"
@@ -26,20 +29,22 @@ constexpr int kConvW = 4;
 constexpr int kConvRun = 32;      // tokens per thread
 constexpr int kConvThreads = 128; // 256 channels per CTA
 
-__device__ __forceinline__ float2 ld2(const void* p, size_t i, bool bf) {
-  if (bf) return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(static_cast<const bf16*>(p) + i));
-  return *reinterpret_cast<const float2*>(static_cast<const float*>(p) + i);
+// Two adjacent channels as one 4-byte (bf16) or 8-byte (fp32) element.
+template <bool BF>
+using Pair = typename std::conditional<BF, __nv_bfloat162, float2>::type;
+template <bool BF>
+__device__ __forceinline__ float2 to2(Pair<BF> v) {
+  if constexpr (BF) return __bfloat1622float2(v); else return v;
 }
-__device__ __forceinline__ void st2(void* p, size_t i, float a, float b, bool bf) {
-  if (bf)
-    *reinterpret_cast<__nv_bfloat162*>(static_cast<bf16*>(p) + i) = __floats2bfloat162_rn(a, b);
-  else
-    *reinterpret_cast<float2*>(static_cast<float*>(p) + i) = make_float2(a, b);
+template <bool BF>
+__device__ __forceinline__ Pair<BF> from2(float a, float b) {
+  if constexpr (BF) return __floats2bfloat162_rn(a, b); else return make_float2(a, b);
 }
 __device__ __forceinline__ float wt(const void* w, size_t i, bool bf) {
   return bf ? __bfloat162float(static_cast<const bf16*>(w)[i]) : static_cast<const float*>(w)[i];
 }
-__device__ __forceinline__ float sig(float p) { return 1.f / (1.f + __expf(-p)); }
+// sigmoid with the fast reciprocal (the output is compared at tolerance, not bit for bit)
+__device__ __forceinline__ float sig(float p) { return __fdividef(1.f, 1.f + __expf(-p)); }
 
 struct ConvArgs {
   const void* x;
@@ -49,151 +54,158 @@ struct ConvArgs {
   void* dx;
   float* dw_part;  // [B * nruns][C][W]
   int64_t B, T, C, D;
-  int x_bf16, w_bf16, silu;
+  int w_bf16, silu;
 };
 
-__global__ void __launch_bounds__(kConvThreads) short_conv_fwd_kernel(ConvArgs a) {
+constexpr int kConvBlk = 8;  // tokens whose loads are issued together
+
+// Per-thread views: row t of this thread's channel pair at p[t * stride]
+// (pair units; T * C / 2 < 2^31 is checked on the host).
+template <bool XB>
+struct ConvRows {
+  const Pair<XB>* __restrict__ x;
+  unsigned xs;
+};
+
+template <bool XB>
+__global__ void __launch_bounds__(kConvThreads, 8) short_conv_fwd_kernel(ConvArgs a) {
   const int64_t c = 2 * ((int64_t)blockIdx.x * kConvThreads + threadIdx.x);
   if (c >= a.C) return;
-  const int64_t b = blockIdx.z, t0 = (int64_t)blockIdx.y * kConvRun, t1 = min(t0 + kConvRun, a.T);
-  const bool xb = a.x_bf16 != 0, wb = a.w_bf16 != 0;
+  const int64_t b = blockIdx.z;
+  const int t0 = blockIdx.y * kConvRun, t1 = (int)min((int64_t)t0 + kConvRun, a.T);
+  const bool wb = a.w_bf16 != 0;
   const int grp = (int)(c / a.D);
   const int64_t cd = c - grp * a.D;
+  const Pair<XB>* __restrict__ x = static_cast<const Pair<XB>*>(a.x) + ((size_t)b * a.T * a.C + c) / 2;
+  Pair<XB>* __restrict__ y =
+      static_cast<Pair<XB>*>(grp == 0 ? a.y[0] : grp == 1 ? a.y[1] : a.y[2]) + ((size_t)b * a.T * a.D + cd) / 2;
+  const unsigned xs = (unsigned)(a.C / 2), ys = (unsigned)(a.D / 2);
   float w0[kConvW], w1[kConvW];
 #pragma unroll
   for (int j = 0; j < kConvW; ++j) {
     w0[j] = wt(a.w, (size_t)c * kConvW + j, wb);
     w1[j] = wt(a.w, (size_t)(c + 1) * kConvW + j, wb);
   }
-  // window of the W-1 tokens before t0
-  float h0[kConvW - 1], h1[kConvW - 1];
+  // window of the W-1 tokens before the current block
+  float2 h[kConvW - 1];
 #pragma unroll
   for (int j = 0; j < kConvW - 1; ++j) {
-    const int64_t t = t0 - (kConvW - 1) + j;
-    float2 v = make_float2(0.f, 0.f);
-    if (t >= 0) v = ld2(a.x, ((size_t)b * a.T + t) * a.C + c, xb);
-    h0[j] = v.x;
-    h1[j] = v.y;
+    const int t = t0 - (kConvW - 1) + j;
+    h[j] = t >= 0 ? to2<XB>(x[(unsigned)t * xs]) : make_float2(0.f, 0.f);
   }
-  for (int64_t t = t0; t < t1; ++t) {
-    const float2 v = ld2(a.x, ((size_t)b * a.T + t) * a.C + c, xb);
-    float p0 = w0[kConvW - 1] * v.x, p1 = w1[kConvW - 1] * v.y;
+#pragma unroll 1
+  for (int tb = t0; tb < t1; tb += kConvBlk) {
+    float2 v[kConvBlk];
 #pragma unroll
-    for (int j = 0; j < kConvW - 1; ++j) {
-      p0 = fmaf(w0[j], h0[j], p0);
-      p1 = fmaf(w1[j], h1[j], p1);
+    for (int i = 0; i < kConvBlk; ++i)
+      v[i] = tb + i < t1 ? to2<XB>(x[(unsigned)(tb + i) * xs]) : make_float2(0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < kConvBlk; ++i) {
+      // x[t - W + 1 + j] for j < W - 1 from the window, x[t] = v[i]
+      float p0 = w0[kConvW - 1] * v[i].x, p1 = w1[kConvW - 1] * v[i].y;
+#pragma unroll
+      for (int j = 0; j < kConvW - 1; ++j) {
+        const float2 xj = i + j >= kConvW - 1 ? v[i + j - (kConvW - 1)] : h[i + j];
+        p0 = fmaf(w0[j], xj.x, p0);
+        p1 = fmaf(w1[j], xj.y, p1);
+      }
+      if (a.silu) {
+        p0 *= sig(p0);
+        p1 *= sig(p1);
+      }
+      if (tb + i < t1) y[(unsigned)(tb + i) * ys] = from2<XB>(p0, p1);
     }
 #pragma unroll
-    for (int j = 0; j < kConvW - 2; ++j) {
-      h0[j] = h0[j + 1];
-      h1[j] = h1[j + 1];
-    }
-    h0[kConvW - 2] = v.x;
-    h1[kConvW - 2] = v.y;
-    if (a.silu) {
-      p0 *= sig(p0);
-      p1 *= sig(p1);
-    }
-    st2(a.y[grp], ((size_t)b * a.T + t) * a.D + cd, p0, p1, xb);
+    for (int j = 0; j < kConvW - 1; ++j) h[j] = v[kConvBlk - (kConvW - 1) + j];
   }
 }
 
-__global__ void __launch_bounds__(kConvThreads) short_conv_bwd_kernel(ConvArgs a) {
+template <bool XB>
+__global__ void __launch_bounds__(kConvThreads, 6) short_conv_bwd_kernel(ConvArgs a) {
   const int64_t c = 2 * ((int64_t)blockIdx.x * kConvThreads + threadIdx.x);
   if (c >= a.C) return;
-  const int64_t b = blockIdx.z, t0 = (int64_t)blockIdx.y * kConvRun, t1 = min(t0 + kConvRun, a.T);
-  const bool xb = a.x_bf16 != 0, wb = a.w_bf16 != 0;
+  const int64_t b = blockIdx.z;
+  const int t0 = blockIdx.y * kConvRun, t1 = (int)min((int64_t)t0 + kConvRun, a.T), T = (int)a.T;
+  const bool wb = a.w_bf16 != 0;
   const int grp = (int)(c / a.D);
   const int64_t cd = c - grp * a.D;
-  const void* dyg = a.dy[grp];
+  const Pair<XB>* __restrict__ x = static_cast<const Pair<XB>*>(a.x) + ((size_t)b * a.T * a.C + c) / 2;
+  Pair<XB>* __restrict__ dx = static_cast<Pair<XB>*>(a.dx) + ((size_t)b * a.T * a.C + c) / 2;
+  const void* dyv = grp == 0 ? a.dy[0] : grp == 1 ? a.dy[1] : a.dy[2];
+  const Pair<XB>* __restrict__ dyg = dyv ? static_cast<const Pair<XB>*>(dyv) + ((size_t)b * a.T * a.D + cd) / 2 : nullptr;
+  const unsigned xs = (unsigned)(a.C / 2), ys = (unsigned)(a.D / 2);
   float w0[kConvW], w1[kConvW];
 #pragma unroll
   for (int j = 0; j < kConvW; ++j) {
     w0[j] = wt(a.w, (size_t)c * kConvW + j, wb);
     w1[j] = wt(a.w, (size_t)(c + 1) * kConvW + j, wb);
   }
-  // x[s-W+1 .. s] slides with s; dpre[s-W+1 .. s] too (zero before t0: dx of
-  // tokens >= t0 needs dpre of tokens >= t0 only)
-  float h0[kConvW - 1], h1[kConvW - 1], e0[kConvW - 1], e1[kConvW - 1];
+  // s runs over the dpre indices [t0, min(t1 + W - 1, T)) in blocks; the x
+  // window holds x[s - W + 1 .. s - 1] and the dpre window dpre[s - W + 1 ..
+  // s - 1] (zero before t0: dx of tokens >= t0 needs dpre of tokens >= t0)
+  float2 h[kConvW - 1], e[kConvW - 1];
 #pragma unroll
   for (int j = 0; j < kConvW - 1; ++j) {
-    const int64_t t = t0 - (kConvW - 1) + j;
-    float2 v = make_float2(0.f, 0.f);
-    if (t >= 0) v = ld2(a.x, ((size_t)b * a.T + t) * a.C + c, xb);
-    h0[j] = v.x;
-    h1[j] = v.y;
-    e0[j] = e1[j] = 0.f;
+    const int t = t0 - (kConvW - 1) + j;
+    h[j] = t >= 0 ? to2<XB>(x[(unsigned)t * xs]) : make_float2(0.f, 0.f);
+    e[j] = make_float2(0.f, 0.f);
   }
   float dw0[kConvW], dw1[kConvW];
 #pragma unroll
   for (int j = 0; j < kConvW; ++j) dw0[j] = dw1[j] = 0.f;
-  const int64_t send = min(t1 + kConvW - 1, a.T);
-  for (int64_t s = t0; s < send; ++s) {
-    const size_t row = (size_t)b * a.T + s;
-    const float2 v = ld2(a.x, row * a.C + c, xb);
-    float p0 = w0[kConvW - 1] * v.x, p1 = w1[kConvW - 1] * v.y;
+  const int send = min(t1 + kConvW - 1, T);
+#pragma unroll 1
+  for (int sb = t0; sb < t1 + kConvW - 1; sb += kConvBlk) {
+    float2 v[kConvBlk], g[kConvBlk];
 #pragma unroll
-    for (int j = 0; j < kConvW - 1; ++j) {
-      p0 = fmaf(w0[j], h0[j], p0);
-      p1 = fmaf(w1[j], h1[j], p1);
+    for (int i = 0; i < kConvBlk; ++i) {
+      const bool in = sb + i < send;
+      v[i] = in ? to2<XB>(x[(unsigned)(sb + i) * xs]) : make_float2(0.f, 0.f);
+      g[i] = in && dyg ? to2<XB>(dyg[(unsigned)(sb + i) * ys]) : make_float2(0.f, 0.f);
     }
-    float d0 = 0.f, d1 = 0.f;
-    if (dyg) {
-      const float2 g = ld2(dyg, row * a.D + cd, xb);
-      d0 = g.x;
-      d1 = g.y;
-    }
-    if (a.silu) {
-      const float s0 = sig(p0), s1 = sig(p1);
-      d0 *= s0 * (1.f + p0 * (1.f - s0));
-      d1 *= s1 * (1.f + p1 * (1.f - s1));
-    }
-    if (s < t1) {  // dw over this run's own tokens: dpre[s] x[s-W+1+j]
+#pragma unroll
+    for (int i = 0; i < kConvBlk; ++i) {
+      const int s = sb + i;
+      float p0 = w0[kConvW - 1] * v[i].x, p1 = w1[kConvW - 1] * v[i].y;
 #pragma unroll
       for (int j = 0; j < kConvW - 1; ++j) {
-        dw0[j] = fmaf(d0, h0[j], dw0[j]);
-        dw1[j] = fmaf(d1, h1[j], dw1[j]);
+        const float2 xj = i + j >= kConvW - 1 ? v[i + j - (kConvW - 1)] : h[i + j];
+        p0 = fmaf(w0[j], xj.x, p0);
+        p1 = fmaf(w1[j], xj.y, p1);
       }
-      dw0[kConvW - 1] = fmaf(d0, v.x, dw0[kConvW - 1]);
-      dw1[kConvW - 1] = fmaf(d1, v.y, dw1[kConvW - 1]);
-    }
-    // dx[s-W+1] = sum_j w[j] dpre[s-j]
-    const int64_t tx = s - (kConvW - 1);
-    if (tx >= t0) {
-      float x0 = w0[0] * d0, x1 = w1[0] * d1;
-#pragma unroll
-      for (int j = 1; j < kConvW; ++j) {
-        x0 = fmaf(w0[j], e0[kConvW - 1 - j], x0);
-        x1 = fmaf(w1[j], e1[kConvW - 1 - j], x1);
+      float d0 = g[i].x, d1 = g[i].y;  // dpre[s] (zero at and past the sequence end)
+      if (a.silu) {
+        const float s0 = sig(p0), s1 = sig(p1);
+        d0 *= s0 * (1.f + p0 * (1.f - s0));
+        d1 *= s1 * (1.f + p1 * (1.f - s1));
       }
-      st2(a.dx, ((size_t)b * a.T + tx) * a.C + c, x0, x1, xb);
-    }
+      if (s < t1) {  // dw over the run's own tokens: dpre[s] x[s - W + 1 + j]
 #pragma unroll
-    for (int j = 0; j < kConvW - 2; ++j) {
-      h0[j] = h0[j + 1];
-      h1[j] = h1[j + 1];
-      e0[j] = e0[j + 1];
-      e1[j] = e1[j + 1];
-    }
-    h0[kConvW - 2] = v.x;
-    h1[kConvW - 2] = v.y;
-    e0[kConvW - 2] = d0;
-    e1[kConvW - 2] = d1;
-  }
-  // tokens of the run whose dx still needs dpre past T (zero): the last W-1
-  for (int64_t tx = max(send - (kConvW - 1), t0); tx < t1; ++tx) {
-    // dpre[tx .. send-1] are the newest window entries, dpre[>= T] = 0
-    float x0 = 0.f, x1 = 0.f;
-#pragma unroll
-    for (int j = 0; j < kConvW; ++j) {
-      const int64_t sj = tx + (kConvW - 1) - j;  // dpre index paired with w[j]
-      if (sj < send) {
-        const int idx = (int)(sj - (send - (kConvW - 1)));  // position in the window e[0 .. W-2]
-        x0 = fmaf(w0[j], e0[idx], x0);
-        x1 = fmaf(w1[j], e1[idx], x1);
+        for (int j = 0; j < kConvW - 1; ++j) {
+          const float2 xj = i + j >= kConvW - 1 ? v[i + j - (kConvW - 1)] : h[i + j];
+          dw0[j] = fmaf(d0, xj.x, dw0[j]);
+          dw1[j] = fmaf(d1, xj.y, dw1[j]);
+        }
+        dw0[kConvW - 1] = fmaf(d0, v[i].x, dw0[kConvW - 1]);
+        dw1[kConvW - 1] = fmaf(d1, v[i].y, dw1[kConvW - 1]);
       }
+      // dx[s - W + 1] = w[0] dpre[s] + sum_{j>=1} w[j] dpre[s - j]
+      const int tx = s - (kConvW - 1);
+      if (tx >= t0 && tx < t1) {
+        float x0 = w0[0] * d0, x1 = w1[0] * d1;
+#pragma unroll
+        for (int j = 1; j < kConvW; ++j) {
+          x0 = fmaf(w0[j], e[kConvW - 1 - j].x, x0);
+          x1 = fmaf(w1[j], e[kConvW - 1 - j].y, x1);
+        }
+        dx[(unsigned)tx * xs] = from2<XB>(x0, x1);
+      }
+#pragma unroll
+      for (int j = 0; j < kConvW - 2; ++j) e[j] = e[j + 1];
+      e[kConvW - 2] = make_float2(d0, d1);
     }
-    st2(a.dx, ((size_t)b * a.T + tx) * a.C + c, x0, x1, xb);
+#pragma unroll
+    for (int j = 0; j < kConvW - 1; ++j) h[j] = v[kConvBlk - (kConvW - 1) + j];
   }
   const size_t part = ((size_t)b * gridDim.y + blockIdx.y) * a.C;
 #pragma unroll
@@ -225,7 +237,7 @@ int conv_check(const char* what, int64_t B, int64_t T, int64_t C, int64_t groups
   if (B <= 0 || T <= 0 || groups < 1 || groups > 3 || C <= 0 || C % (2 * groups) != 0 || W != kConvW)
     return set_error(KDN_ERR_INVALID, "%s: B, T > 0, groups in 1..3, C a multiple of 2 * groups, W = 4 required",
                      what);
-  if (B > 65535 || (T + kConvRun - 1) / kConvRun > 65535)
+  if (B > 65535 || (T + kConvRun - 1) / kConvRun > 65535 || T * C / 2 >= (int64_t)1 << 31)
     return set_error(KDN_ERR_INVALID, "%s: size too large", what);
   return KDN_OK;
 }
@@ -253,12 +265,15 @@ int kdn_short_conv_fwd(const void* x, int x_bf16, const void* weight, int w_bf16
   if (!x || !weight || !y) return set_error(KDN_ERR_INVALID, "kdn_short_conv_fwd: null pointer");
   ConvArgs a{};
   a.x = x; a.w = weight; a.B = B; a.T = T; a.C = C; a.D = C / groups;
-  a.x_bf16 = x_bf16; a.w_bf16 = w_bf16; a.silu = silu;
+  a.w_bf16 = w_bf16; a.silu = silu;
   for (int g = 0; g < groups; ++g) {
     if (!y[g]) return set_error(KDN_ERR_INVALID, "kdn_short_conv_fwd: null output %d", g);
     a.y[g] = y[g];
   }
-  short_conv_fwd_kernel<<<conv_grid(B, T, C), kConvThreads, 0, (cudaStream_t)stream>>>(a);
+  if (x_bf16)
+    short_conv_fwd_kernel<true><<<conv_grid(B, T, C), kConvThreads, 0, (cudaStream_t)stream>>>(a);
+  else
+    short_conv_fwd_kernel<false><<<conv_grid(B, T, C), kConvThreads, 0, (cudaStream_t)stream>>>(a);
   return check_launch("short_conv_fwd_kernel");
 }
 
@@ -271,11 +286,14 @@ int kdn_short_conv_bwd(const void* x, int x_bf16, const void* weight, int w_bf16
     return set_error(KDN_ERR_WORKSPACE, "kdn_short_conv_bwd: workspace too small");
   ConvArgs a{};
   a.x = x; a.w = weight; a.dx = dx; a.dw_part = static_cast<float*>(workspace);
-  a.B = B; a.T = T; a.C = C; a.D = C / groups; a.x_bf16 = x_bf16; a.w_bf16 = w_bf16; a.silu = silu;
+  a.B = B; a.T = T; a.C = C; a.D = C / groups; a.w_bf16 = w_bf16; a.silu = silu;
   for (int g = 0; g < groups; ++g) a.dy[g] = dy[g];
   cudaStream_t st = (cudaStream_t)stream;
   const dim3 grid = conv_grid(B, T, C);
-  short_conv_bwd_kernel<<<grid, kConvThreads, 0, st>>>(a);
+  if (x_bf16)
+    short_conv_bwd_kernel<true><<<grid, kConvThreads, 0, st>>>(a);
+  else
+    short_conv_bwd_kernel<false><<<grid, kConvThreads, 0, st>>>(a);
   if (int rc = check_launch("short_conv_bwd_kernel")) return rc;
   const int64_t CW = C * W, nparts = B * grid.y;
   short_conv_dw_kernel<<<(unsigned)((CW + 255) / 256), 256, 0, st>>>(a.dw_part, dweight, nparts, CW, w_bf16);

@@ -113,25 +113,27 @@ __global__ void __launch_bounds__(32 * kNormWarps) diag_norm_bwd_kernel(
   const int64_t warps = (int64_t)gridDim.x * kNormWarps;
   for (int64_t row = (int64_t)blockIdx.x * kNormWarps + (threadIdx.x >> 5); row < n_rows; row += warps) {
     const size_t base = (size_t)row * K + lane;
-    if (dq_memory) {
-      float x[4] = {0.f, 0.f, 0.f, 0.f}, u[4] = {0.f, 0.f, 0.f, 0.f};
+    // every load of the row (q side and k side) requested before any arithmetic
+    float xq[4] = {0.f, 0.f, 0.f, 0.f}, uq[4] = {0.f, 0.f, 0.f, 0.f};
+    float xk[4] = {0.f, 0.f, 0.f, 0.f}, ug[4] = {0.f, 0.f, 0.f, 0.f}, um[4] = {0.f, 0.f, 0.f, 0.f};
+    const bool has_k = dk_gain || dk_memory;
 #pragma unroll
-      for (int j = 0; j < NJ; ++j) {
-        x[j] = load_f(q, base + 32 * j, bf);
-        u[j] = __bfloat162float(dq_memory[base + 32 * j]);
+    for (int j = 0; j < NJ; ++j) {
+      if (dq_memory) {
+        xq[j] = load_f(q, base + 32 * j, bf);
+        uq[j] = __bfloat162float(dq_memory[base + 32 * j]);
       }
-      row_vjp<NJ>(x, u, q_norm[row], small_rows, dq, base, bf);
+      if (has_k) xk[j] = load_f(k, base + 32 * j, bf);
+      if (dk_gain) ug[j] = dk_gain[base + 32 * j];
+      if (dk_memory) um[j] = __bfloat162float(dk_memory[base + 32 * j]);
     }
-    if (dk_gain || dk_memory) {
-      float x[4] = {0.f, 0.f, 0.f, 0.f}, u[4] = {0.f, 0.f, 0.f, 0.f};
+    const float nq = dq_memory ? q_norm[row] : 0.f, nk = has_k ? k_norm[row] : 0.f;
+    if (dq_memory) row_vjp<NJ>(xq, uq, nq, small_rows, dq, base, bf);
+    if (has_k) {
+      float u[4];
 #pragma unroll
-      for (int j = 0; j < NJ; ++j) {
-        x[j] = load_f(k, base + 32 * j, bf);
-        const float g = dk_gain ? dk_gain[base + 32 * j] : 0.f;
-        const float m = dk_memory ? __bfloat162float(dk_memory[base + 32 * j]) : 0.f;
-        u[j] = dk_gain && dk_memory ? __fadd_rn(g, m) : dk_gain ? g : m;
-      }
-      row_vjp<NJ>(x, u, k_norm[row], small_rows, dk, base, bf);
+      for (int j = 0; j < 4; ++j) u[j] = dk_gain && dk_memory ? __fadd_rn(ug[j], um[j]) : dk_gain ? ug[j] : um[j];
+      row_vjp<NJ>(xk, u, nk, small_rows, dk, base, bf);
     }
   }
 }

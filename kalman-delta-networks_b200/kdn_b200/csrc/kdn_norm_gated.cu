@@ -72,7 +72,8 @@ __device__ __forceinline__ void st_vec(void* p, size_t off, const float (&s)[V],
   }
 }
 
-__device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + __expf(-x)); }
+// sigmoid with the fast reciprocal (the output is compared at tolerance, not bit for bit)
+__device__ __forceinline__ float sigmoid_f(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
 
 struct NgArgs {
   const void* x;
@@ -89,39 +90,55 @@ struct NgArgs {
   int x_bf16, g_bf16, swish;
 };
 
+// Each warp takes kNgRows rows per iteration and requests all of their
+// inputs before any arithmetic (more loads in flight per warp).
+constexpr int kNgRows = 2;
+
 template <int D>
 __global__ void __launch_bounds__(32 * kNgWarps) rmsnorm_gated_fwd_kernel(NgArgs a) {
-  constexpr int V = D / 32;
+  constexpr int V = D / 32, R = kNgRows;
   const int lane = threadIdx.x & 31;
   const bool xb = a.x_bf16 != 0, gb = a.g_bf16 != 0;
   float w[V];
 #pragma unroll
   for (int i = 0; i < V; ++i) w[i] = a.w ? a.w[V * lane + i] : 1.f;
-  const int64_t step = (int64_t)gridDim.x * kNgWarps;
-  for (int64_t row = (int64_t)blockIdx.x * kNgWarps + (threadIdx.x >> 5); row < a.rows; row += step) {
-    const size_t off = (size_t)row * D + V * lane;
-    float x[V], g[V];
-    ld_vec<V>(x, a.x, off, xb);
-    ld_vec<V>(g, a.g, off, gb);
-    float ss = 0.f;
+  const int64_t step = (int64_t)gridDim.x * kNgWarps * R;
+  for (int64_t row0 = ((int64_t)blockIdx.x * kNgWarps + (threadIdx.x >> 5)) * R; row0 < a.rows; row0 += step) {
+    float x[R][V], g[R][V];
 #pragma unroll
-    for (int i = 0; i < V; ++i) ss = fmaf(x[i], x[i], ss);
-    ss = warp_sum(ss);
-    const float rstd = rsqrtf(ss / (float)D + a.eps);
-    float y[V];
+    for (int r = 0; r < R; ++r) {
+      if (row0 + r < a.rows) {
+        const size_t off = (size_t)(row0 + r) * D + V * lane;
+        ld_vec<V>(x[r], a.x, off, xb);
+        ld_vec<V>(g[r], a.g, off, gb);
+      } else {
 #pragma unroll
-    for (int i = 0; i < V; ++i) {
-      const float s = sigmoid_f(g[i]);
-      y[i] = x[i] * rstd * w[i] * (a.swish ? g[i] * s : s);
+        for (int i = 0; i < V; ++i) x[r][i] = g[r][i] = 0.f;
+      }
     }
-    st_vec<V>(a.y, off, y, xb);
-    if (lane == 0) a.rstd[row] = rstd;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      if (row0 + r >= a.rows) break;
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < V; ++i) ss = fmaf(x[r][i], x[r][i], ss);
+      ss = warp_sum(ss);
+      const float rstd = rsqrtf(ss * (1.f / (float)D) + a.eps);
+      float y[V];
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        const float sg = sigmoid_f(g[r][i]);
+        y[i] = x[r][i] * rstd * w[i] * (a.swish ? g[r][i] * sg : sg);
+      }
+      st_vec<V>(a.y, (size_t)(row0 + r) * D + V * lane, y, xb);
+      if (lane == 0) a.rstd[row0 + r] = rstd;
+    }
   }
 }
 
 template <int D>
 __global__ void __launch_bounds__(32 * kNgWarps) rmsnorm_gated_bwd_kernel(NgArgs a) {
-  constexpr int V = D / 32;
+  constexpr int V = D / 32, R = kNgRows;
   __shared__ float red[kNgWarps][D];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const bool xb = a.x_bf16 != 0, gb = a.g_bf16 != 0;
@@ -131,48 +148,63 @@ __global__ void __launch_bounds__(32 * kNgWarps) rmsnorm_gated_bwd_kernel(NgArgs
     w[i] = a.w ? a.w[V * lane + i] : 1.f;
     dw[i] = 0.f;
   }
-  const int64_t step = (int64_t)gridDim.x * kNgWarps;
-  for (int64_t row = (int64_t)blockIdx.x * kNgWarps + warp; row < a.rows; row += step) {
-    const size_t off = (size_t)row * D + V * lane;
-    float x[V], g[V], dy[V];
-    ld_vec<V>(x, a.x, off, xb);
-    ld_vec<V>(g, a.g, off, gb);
-    ld_vec<V>(dy, a.dy, off, xb);  // the output (and its cotangent) has x's dtype
-    const float rstd = a.rstd[row];
-    float dgo[V], wdy[V], xh[V], c = 0.f;
+  const int64_t step = (int64_t)gridDim.x * kNgWarps * R;
+  for (int64_t row0 = ((int64_t)blockIdx.x * kNgWarps + warp) * R; row0 < a.rows; row0 += step) {
+    float x[R][V], g[R][V], dy[R][V], rs[R];
 #pragma unroll
-    for (int i = 0; i < V; ++i) {
-      const float s = sigmoid_f(g[i]);
-      xh[i] = x[i] * rstd;
-      const float y0 = xh[i] * w[i];
-      float d;
-      if (a.swish) {
-        dgo[i] = dy[i] * y0 * (s + g[i] * s * (1.f - s));
-        d = dy[i] * g[i] * s;
+    for (int r = 0; r < R; ++r) {
+      if (row0 + r < a.rows) {
+        const size_t off = (size_t)(row0 + r) * D + V * lane;
+        ld_vec<V>(x[r], a.x, off, xb);
+        ld_vec<V>(g[r], a.g, off, gb);
+        ld_vec<V>(dy[r], a.dy, off, xb);  // the output (and its cotangent) has x's dtype
+        rs[r] = a.rstd[row0 + r];
       } else {
-        dgo[i] = dy[i] * y0 * s * (1.f - s);
-        d = dy[i] * s;
-      }
-      dw[i] = fmaf(d, xh[i], dw[i]);
-      wdy[i] = d * w[i];
-      c = fmaf(xh[i], wdy[i], c);
-    }
-    c = warp_sum(c) / (float)D;
-    float dxo[V];
 #pragma unroll
-    for (int i = 0; i < V; ++i) dxo[i] = (wdy[i] - xh[i] * c) * rstd;
-    st_vec<V>(a.dx, off, dxo, xb);
-    st_vec<V>(a.dg, off, dgo, gb);
+        for (int i = 0; i < V; ++i) x[r][i] = g[r][i] = dy[r][i] = 0.f;
+        rs[r] = 0.f;
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      if (row0 + r >= a.rows) break;
+      const float rstd = rs[r];
+      float dgo[V], wdy[V], xh[V], c = 0.f;
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        const float sg = sigmoid_f(g[r][i]);
+        xh[i] = x[r][i] * rstd;
+        const float y0 = xh[i] * w[i];
+        float d;
+        if (a.swish) {
+          dgo[i] = dy[r][i] * y0 * (sg + g[r][i] * sg * (1.f - sg));
+          d = dy[r][i] * g[r][i] * sg;
+        } else {
+          dgo[i] = dy[r][i] * y0 * sg * (1.f - sg);
+          d = dy[r][i] * sg;
+        }
+        dw[i] = fmaf(d, xh[i], dw[i]);
+        wdy[i] = d * w[i];
+        c = fmaf(xh[i], wdy[i], c);
+      }
+      c = warp_sum(c) * (1.f / (float)D);
+      float dxo[V];
+#pragma unroll
+      for (int i = 0; i < V; ++i) dxo[i] = (wdy[i] - xh[i] * c) * rstd;
+      const size_t off = (size_t)(row0 + r) * D + V * lane;
+      st_vec<V>(a.dx, off, dxo, xb);
+      st_vec<V>(a.dg, off, dgo, gb);
+    }
   }
   if (a.dw_part) {
 #pragma unroll
     for (int i = 0; i < V; ++i) red[warp][V * lane + i] = dw[i];
     __syncthreads();
     for (int d = threadIdx.x; d < D; d += blockDim.x) {
-      float s = 0.f;
+      float sum = 0.f;
 #pragma unroll
-      for (int k = 0; k < kNgWarps; ++k) s += red[k][d];
-      a.dw_part[(size_t)blockIdx.x * D + d] = s;
+      for (int k = 0; k < kNgWarps; ++k) sum += red[k][d];
+      a.dw_part[(size_t)blockIdx.x * D + d] = sum;
     }
   }
 }
@@ -191,7 +223,7 @@ __global__ void rmsnorm_gated_dw_kernel(const float* __restrict__ part, float* _
 }
 
 unsigned ng_grid(int64_t rows) {
-  const int64_t blocks = (rows + kNgWarps - 1) / kNgWarps;
+  const int64_t blocks = (rows + kNgWarps * kNgRows - 1) / (kNgWarps * kNgRows);
   return (unsigned)(blocks < kNgMaxCtas ? (blocks > 0 ? blocks : 1) : kNgMaxCtas);
 }
 
