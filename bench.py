@@ -206,12 +206,6 @@ def make_diag_varlen(device, seed):
     return x
 
 
-def varlen_buckets(cu, bucket=1024):
-    """Number of batched calls of a packed step (sequences grouped by length
-    rounded up to the varlen bucket)."""
-    return len({-(-(b - a) // bucket) for a, b in zip(cu, cu[1:])})
-
-
 def step_diag_varlen(x):
     from kdn_b200 import varlen
 
@@ -989,7 +983,7 @@ def measure(variant, args, device, dist, world, rank, warmup, varlen=False):
     per_th = ISO_BYTES_PER_TH if variant == "iso" else DIAG_BYTES_PER_TH
     step_bytes = sum(per_th.values()) * th
     if varlen:
-        # packed sequences run as batched calls, one per length bucket: the whole step is the unit
+        # the packed step (native: one call per operator over all sequences) is the unit
         achieved = step_bytes / (ms * 1e-3) / 1e9
         roofline = {"kernel": "whole varlen step (gain + scan, fwd + bwd, all sequences)", "bound": "hbm",
                     "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
@@ -1015,7 +1009,7 @@ def measure(variant, args, device, dist, world, rank, warmup, varlen=False):
                    else f"diag_kdn gain+scan fwd+bwd B{B} T{T} H{H} d{D} (config 2)",
                    "global_batch": B * world, "seq_len": T, "heads": H, "head_dim": D,
                    "parallelism": f"batch-sharded x{world}", "l2": "inputs > L2 (no flush)"},
-        "gpu_launches": LAUNCHES_PER_STEP[variant] * args.steps * (varlen_buckets(x["cu"]) if varlen else 1),
+        "gpu_launches": LAUNCHES_PER_STEP[variant] * args.steps,
         "e2e": e2e, "roofline": roofline, "clocks": clocks,
     }
     if not varlen:

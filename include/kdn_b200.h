@@ -35,10 +35,31 @@ enum {
   KDN_ERR_CUDA = -3,      /* a CUDA launch or runtime call failed        */
 };
 
-/* Version of this ABI (major * 100 + minor): 101 (KdnScanArgs.mode, the split diagonal gain). */
+/* Version of this ABI (major * 100 + minor): 102 (101: KdnScanArgs.mode,
+ * the split diagonal gain; 102: packed variable-length batches). */
 int kdn_version(void);
 /* Message of the last failed call on this thread ("" if none). */
 const char* kdn_last_error(void);
+
+/* ------------------------------------------------------------------------ *
+ * Packed variable-length batches (the cu_seqlens convention of
+ * flash-linear-attention's varlen kernels, which the reference's dense path
+ * builds on; its kdn_ops entry points pass cu_seqlens=None, e.g.
+ * lit_gpt/kdn_ops/iso_kdn_chunk.py:2053, diag_kdn_chunk.py:2844).  N
+ * sequences lie back to back along T of a B = 1 batch; sequence i holds
+ * tokens [cu_seqlens[i], cu_seqlens[i+1]) and is an independent stream: its
+ * memory state and covariance start from their initial values, and its
+ * 64-token chunks (and the boundary's gate prefix restarts) count from its
+ * own first token.  kdn_varlen_plan builds, on the host, the int32 table
+ * the varlen entry points take (copied to the device by the caller):
+ *   tok[N+1] = cu_seqlens, chunk[N+1] first global chunk of each sequence,
+ *   order[N] sequences by decreasing length, seq[NC] sequence of each chunk,
+ * NC = sum ceil(len_i / 64).  With table == NULL it only returns NC.
+ * cu_seqlens must start at 0 and increase strictly; total < 2^31.
+ * ------------------------------------------------------------------------ */
+int64_t kdn_varlen_table_len(int64_t num_seqs, int64_t num_chunks);
+int kdn_varlen_plan(const int64_t* cu_seqlens, int64_t num_seqs, int32_t* table,
+                    int64_t table_len, int64_t* num_chunks);
 
 /* ------------------------------------------------------------------------ *
  * Isotropic gain scan.  Replaces the launches behind iso_kdn_gain
@@ -258,6 +279,35 @@ int kdn_diag_gain_bwd(const float* k, const float* alpha, const float* omega,
                       int64_t B, int64_t T, int64_t H, int64_t K,
                       void* workspace, size_t workspace_bytes,
                       kdn_stream_t stream);
+/* The diagonal gain over a packed batch (kdn_varlen_plan): B = 1, tensors
+ * [1,T,H,K] / [1,T,H]; initial_cov, p_final, d_final_cov, d_initial_cov are
+ * per sequence, fp32 [N,H,K]; the covariance of every sequence starts from
+ * 1/initial_precision (or its initial_cov row).  Carry and workspace sizes
+ * from the _varlen queries.  Same results per sequence as separate calls. */
+int64_t kdn_diag_gain_varlen_carry_elems(int64_t H, int64_t K, int64_t num_chunks);
+size_t kdn_diag_gain_varlen_workspace_bytes(int64_t T, int64_t H, int64_t K,
+                                            int64_t num_chunks);
+int kdn_diag_gain_fwd_varlen(const float* k, const float* alpha,
+                             const float* omega, const float* r,
+                             const float* initial_precision,
+                             const float* initial_cov, float* kappa, float* carry,
+                             float* p_final, int64_t T, int64_t H, int64_t K,
+                             const int32_t* varlen_table, int64_t num_seqs,
+                             int64_t num_chunks, void* workspace,
+                             size_t workspace_bytes, kdn_stream_t stream);
+int kdn_diag_gain_bwd_varlen(const float* k, const float* alpha,
+                             const float* omega, const float* r,
+                             const float* initial_precision,
+                             const float* initial_cov, const void* omega_raw,
+                             const void* r_raw, const float* dkappa,
+                             const float* carry, const float* d_final_cov,
+                             float* dk, float* dalpha, void* domega_raw,
+                             void* dr_raw, float* d_initial_precision,
+                             float* d_initial_cov, int64_t T, int64_t H,
+                             int64_t K, const int32_t* varlen_table,
+                             int64_t num_seqs, int64_t num_chunks,
+                             void* workspace, size_t workspace_bytes,
+                             kdn_stream_t stream);
 
 /* ------------------------------------------------------------------------ *
  * Diagonal q / k normalisation.  Replaces _diag_kdn_normalize
@@ -437,6 +487,14 @@ typedef struct KdnScanArgs {
   /* passes to run (KDN_SCAN_*; 0 = all) and the state-map output */
   int32_t mode;
   float* final_state_map; /* KDN_SCAN_FWD_STATE_MAP: fp32 [B,H,K,K] */
+  /* packed variable-length batch: the kdn_varlen_plan table on the device
+   * (NULL = fixed-length batch).  Then B = 1, T = cu_seqlens[N], the bf16
+   * precision and mode 0 only; initial_state, final_state, d_final_state and
+   * d_initial_state are per sequence, fp32 [N,H,K,V].  Zero-initialise the
+   * struct so that older callers leave this off. */
+  const int32_t* varlen_table;
+  int64_t num_seqs;
+  int64_t num_chunks;
 } KdnScanArgs;
 
 size_t kdn_scan_saved_bytes(const KdnScanArgs* args);

@@ -64,6 +64,9 @@ class KdnScanArgs(ctypes.Structure):
         ("workspace_bytes", ctypes.c_size_t),
         ("mode", ctypes.c_int32),
         ("final_state_map", ctypes.c_void_p),
+        ("varlen_table", ctypes.c_void_p),
+        ("num_seqs", ctypes.c_int64),
+        ("num_chunks", ctypes.c_int64),
     ]
 
 
@@ -107,6 +110,12 @@ _SIGNATURES = {
         [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _SZ, _P],
         ctypes.c_int,
     ),
+    "kdn_diag_gain_varlen_carry_elems": ([_I64, _I64, _I64], _I64),
+    "kdn_diag_gain_varlen_workspace_bytes": ([_I64, _I64, _I64, _I64], _SZ),
+    "kdn_diag_gain_fwd_varlen": ([_P] * 9 + [_I64, _I64, _I64, _P, _I64, _I64, _P, _SZ, _P], ctypes.c_int),
+    "kdn_diag_gain_bwd_varlen": ([_P] * 17 + [_I64, _I64, _I64, _P, _I64, _I64, _P, _SZ, _P], ctypes.c_int),
+    "kdn_varlen_table_len": ([_I64, _I64], _I64),
+    "kdn_varlen_plan": ([_P, _I64, _P, _I64, ctypes.POINTER(ctypes.c_int64)], ctypes.c_int),
     "kdn_diag_norm_fwd": ([_P, _P, ctypes.c_int, _P, _P, _P, _P, _P, _I64, _I64, _P], ctypes.c_int),
     "kdn_diag_norm_bwd": ([_P, _P, ctypes.c_int, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _P], ctypes.c_int),
     "kdn_rmsnorm_gated_workspace_bytes": ([_I64, _I64], _SZ),

@@ -49,23 +49,36 @@ class ScanSaved:
     precision: int
 
 
-def _args(variant, precision, q, v, scale) -> N.KdnScanArgs:
+def _args(variant, precision, q, v, scale, plan=None) -> N.KdnScanArgs:
     B, T, H, K = q.shape
     a = N.KdnScanArgs()
     a.variant = variant
     a.precision = precision
     a.B, a.T, a.H, a.K, a.V = B, T, H, K, v.shape[-1]
     a.scale = float(scale)
+    if plan is not None:
+        # packed variable-length batch: the plan's table on the device
+        if precision != N.KDN_PREC_BF16:
+            raise ValueError("packed variable-length batches run the bf16 precision only")
+        a.varlen_table = plan.table.data_ptr()
+        a.num_seqs = plan.num_seqs
+        a.num_chunks = plan.num_chunks
     return a
 
 
-def scan_forward(variant, q, k, v, g, gate, scale, initial_state=None, want_final_state=False):
+def _streams(q, plan) -> int:
+    """Leading size of the per-stream states: B, or the sequences of a packed batch."""
+    return q.shape[0] if plan is None else plan.num_seqs
+
+
+def scan_forward(variant, q, k, v, g, gate, scale, initial_state=None, want_final_state=False, plan=None):
     """Run the forward.  ``gate`` is beta [B,T,H] (iso) or kappa [B,T,H,K]
-    (diag).  Returns ``(o, final_state or None, ScanSaved)``."""
+    (diag).  ``plan`` (a packed batch's ``kdn_b200.varlen.VarlenPlan``) makes
+    the states per sequence.  Returns ``(o, final_state or None, ScanSaved)``."""
     N.require_cuda(q, k, v, g, gate)
     lib = N.load_library()
     prec = N.precision()
-    a = _args(variant, prec, q, v, scale)
+    a = _args(variant, prec, q, v, scale, plan)
     saved = N.byte_buffer(lib.kdn_scan_saved_bytes(ctypes.byref(a)), q.device)
     ws_bytes = lib.kdn_scan_workspace_bytes(ctypes.byref(a))
     if prec == N.KDN_PREC_FP32:
@@ -73,7 +86,8 @@ def scan_forward(variant, q, k, v, g, gate, scale, initial_state=None, want_fina
     else:
         ws = None
     o = torch.empty(v.shape, dtype=torch.bfloat16 if variant == N.KDN_ISO else torch.float32, device=q.device)
-    final = torch.empty(q.shape[0], q.shape[2], KD, v.shape[-1], dtype=torch.float32, device=q.device) if want_final_state else None
+    final = (torch.empty(_streams(q, plan), q.shape[2], KD, v.shape[-1], dtype=torch.float32, device=q.device)
+             if want_final_state else None)
     a.q, a.k, a.v, a.g = q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr()
     if variant == N.KDN_ISO:
         a.beta = gate.data_ptr()
@@ -90,11 +104,12 @@ def scan_forward(variant, q, k, v, g, gate, scale, initial_state=None, want_fina
     return o, final, ScanSaved(saved, prec)
 
 
-def scan_backward(variant, q, k, v, g, gate, scale, saved: ScanSaved, dO, d_final_state=None, want_d_initial=False):
+def scan_backward(variant, q, k, v, g, gate, scale, saved: ScanSaved, dO, d_final_state=None, want_d_initial=False,
+                  plan=None):
     """Run the backward.  Returns ``(dq, dk, dv, dg, dgate, d_initial_state)``
     where dgate is dbeta (iso) or dkappa (diag)."""
     lib = N.load_library()
-    a = _args(variant, saved.precision, q, v, scale)
+    a = _args(variant, saved.precision, q, v, scale, plan)
     ws = N.byte_buffer(lib.kdn_scan_workspace_bytes(ctypes.byref(a)), q.device)
     dq = torch.empty_like(q)
     dk = torch.empty_like(k)
@@ -102,7 +117,7 @@ def scan_backward(variant, q, k, v, g, gate, scale, saved: ScanSaved, dO, d_fina
     dg = torch.empty_like(g)
     dgate = torch.empty_like(gate)
     dS0 = (
-        torch.empty(q.shape[0], q.shape[2], KD, v.shape[-1], dtype=torch.float32, device=q.device)
+        torch.empty(_streams(q, plan), q.shape[2], KD, v.shape[-1], dtype=torch.float32, device=q.device)
         if want_d_initial
         else None
     )

@@ -401,6 +401,43 @@ __device__ __forceinline__ void copy_rows(void* dst, size_t dst_stride, const vo
 __host__ __device__ constexpr size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 // ---------------------------------------------------------------------------
+// Packed variable-length batches.  N sequences lie back to back along T of a
+// B = 1 batch; each is cut into its own 64-token chunks (the last one
+// partial), numbered globally in packed order.  The table (kdn_varlen_plan)
+// is one int32 array: tok[N+1] token offsets (cu_seqlens), chunk[N+1] first
+// global chunk of each sequence, order[N] the sequences longest first (the
+// stream slots of the sequential passes, so that the longest chains start
+// first), seq[NC] the sequence of each global chunk.  n = 0: a fixed-length
+// batch (no table).
+// ---------------------------------------------------------------------------
+constexpr int kVarlenChunk = 64;
+struct Varlen {
+  const int* tok;
+  const int* chunk;
+  const int* order;
+  const int* seq;
+  int n;
+  __host__ __device__ bool on() const { return n > 0; }
+};
+inline Varlen varlen_view(const int32_t* table, int64_t n) {
+  Varlen v{nullptr, nullptr, nullptr, nullptr, 0};
+  if (table && n > 0) {
+    v.tok = table;
+    v.chunk = table + (n + 1);
+    v.order = table + 2 * (n + 1);
+    v.seq = table + 2 * (n + 1) + n;
+    v.n = (int)n;
+  }
+  return v;
+}
+// First token (packed index) and length of global chunk gc, and its sequence.
+__device__ __forceinline__ void varlen_span(const Varlen& v, int gc, int& t0, int& len, int& s) {
+  s = v.seq[gc];
+  t0 = v.tok[s] + (gc - v.chunk[s]) * kVarlenChunk;
+  len = min(kVarlenChunk, v.tok[s + 1] - t0);
+}
+
+// ---------------------------------------------------------------------------
 // Bulk copies (TMA) and mbarriers.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {

@@ -337,13 +337,29 @@ struct GainTile {
   }
 };
 
+// Tokens [t0, t0 + n) of 64-token segment `seg` (a global chunk of a packed
+// batch when v is on) and the index of its (sequence, head) stream.
+__device__ __forceinline__ void seg_span(const Varlen& v, int seg, int T, int H, int bh, int& t0, int& n, int& sh) {
+  if (v.on()) {
+    int s;
+    varlen_span(v, seg, t0, n, s);
+    sh = s * H + bh;  // B = 1: bh is the head
+  } else {
+    t0 = seg * kDiagSeg;
+    n = min(kDiagSeg, T - t0);
+    sh = bh;
+  }
+}
+
 template <int K>
 __global__ void __launch_bounds__(K) diag_gain_map_kernel(const float* __restrict__ k, const float* __restrict__ alpha,
                                                           const float* __restrict__ omega, const float* __restrict__ r,
-                                                          float4* __restrict__ maps, int T, int H, int nseg) {
+                                                          float4* __restrict__ maps, int T, int H, int nseg,
+                                                          Varlen v) {
   constexpr int TT = 4;
   const int seg = blockIdx.x, bh = blockIdx.y, b = bh / H, h = bh - b * H, c = threadIdx.x;
-  const int t0 = seg * kDiagSeg, n = min(kDiagSeg, T - t0);
+  int t0, n, sh;
+  seg_span(v, seg, T, H, bh, t0, n, sh);
   const size_t row0 = ((size_t)b * T + t0) * H + h;
   GainTile<K, TT, false> cu, nx;
   nx.load(k, alpha, omega, r, nullptr, row0, H, n, c);
@@ -367,15 +383,18 @@ __global__ void __launch_bounds__(K) diag_gain_carry_kernel(const float4* __rest
                                                             const float* __restrict__ init_prec,
                                                             const float* __restrict__ init_cov,
                                                             float* __restrict__ carry, float* __restrict__ p_final,
-                                                            int H, int nseg) {
-  const int bh = blockIdx.x, h = bh % H, c = threadIdx.x;
-  float p = init_cov ? init_cov[(size_t)bh * K + c] : 1.f / init_prec[h];
-  for (int s = 0; s < nseg; ++s) {
-    carry[((size_t)bh * nseg + s) * K + c] = p;
-    const float4 m = maps[((size_t)bh * nseg + s) * K + c];
+                                                            int H, int nseg, Varlen v) {
+  // one (sequence, head) stream; its segments are [s0, s1) of the (b, h) row
+  // of segment maps (packed batch: the head's row, the sequence's chunks)
+  const int sh = blockIdx.x, h = sh % H, c = threadIdx.x;
+  const int row = v.on() ? h : sh, s0 = v.on() ? v.chunk[sh / H] : 0, s1 = v.on() ? v.chunk[sh / H + 1] : nseg;
+  float p = init_cov ? init_cov[(size_t)sh * K + c] : 1.f / init_prec[h];
+  for (int s = s0; s < s1; ++s) {
+    carry[((size_t)row * nseg + s) * K + c] = p;
+    const float4 m = maps[((size_t)row * nseg + s) * K + c];
     p = mob_apply(Mob{m.x, m.y, m.z, m.w}, p);
   }
-  if (p_final) p_final[(size_t)bh * K + c] = p;
+  if (p_final) p_final[(size_t)sh * K + c] = p;
 }
 
 template <int K>
@@ -383,12 +402,14 @@ __global__ void __launch_bounds__(K) diag_gain_emit_kernel(const float* __restri
                                                            const float* __restrict__ omega,
                                                            const float* __restrict__ r,
                                                            const float* __restrict__ carry,
-                                                           float* __restrict__ kappa, int T, int H, int nseg) {
+                                                           float* __restrict__ kappa, int T, int H, int nseg,
+                                                           Varlen v) {
   constexpr int TT = 4;
   __shared__ float red[K / 32 * TT];
   __shared__ float tok[TT];
   const int seg = blockIdx.x, bh = blockIdx.y, b = bh / H, h = bh - b * H, c = threadIdx.x;
-  const int t0 = seg * kDiagSeg, n = min(kDiagSeg, T - t0);
+  int t0, n, sh;
+  seg_span(v, seg, T, H, bh, t0, n, sh);
   const size_t row0 = ((size_t)b * T + t0) * H + h;
   GainTile<K, TT, false> cu, nx;
   nx.load(k, alpha, omega, r, nullptr, row0, H, n, c);
@@ -424,12 +445,13 @@ template <int K>
 __global__ void __launch_bounds__(K) diag_gain_bwd_map_kernel(
     const float* __restrict__ k, const float* __restrict__ alpha, const float* __restrict__ omega,
     const float* __restrict__ r, const float* __restrict__ dkappa, const float* __restrict__ carry,
-    float2* __restrict__ maps, float2* __restrict__ dg_tok, int T, int H, int nseg) {
+    float2* __restrict__ maps, float2* __restrict__ dg_tok, int T, int H, int nseg, Varlen v) {
   constexpr int TT = 2;
   __shared__ float red[K / 32 * 2 * TT];
   __shared__ float tok[2 * TT];  // [sum p_hat k^2 | sum dkappa p_hat k] per token
   const int seg = blockIdx.x, bh = blockIdx.y, b = bh / H, h = bh - b * H, c = threadIdx.x;
-  const int t0 = seg * kDiagSeg, n = min(kDiagSeg, T - t0);
+  int t0, n, sh;
+  seg_span(v, seg, T, H, bh, t0, n, sh);
   const size_t row0 = ((size_t)b * T + t0) * H + h;
   const float Kf = (float)K;
   GainTile<K, TT, true> cu, nx;
@@ -475,12 +497,14 @@ __global__ void __launch_bounds__(K) diag_gain_bwd_map_kernel(
 template <int K>
 __global__ void __launch_bounds__(K) diag_gain_bwd_carry_kernel(const float2* __restrict__ maps,
                                                                 const float* __restrict__ d_final_cov,
-                                                                float* __restrict__ lam_carry, int nseg) {
-  const int bh = blockIdx.x, c = threadIdx.x;
-  float lam = d_final_cov ? d_final_cov[(size_t)bh * K + c] : 0.f;
-  for (int s = nseg - 1; s >= 0; --s) {
-    lam_carry[((size_t)bh * nseg + s) * K + c] = lam;
-    const float2 m = maps[((size_t)bh * nseg + s) * K + c];
+                                                                float* __restrict__ lam_carry, int H, int nseg,
+                                                                Varlen v) {
+  const int sh = blockIdx.x, h = sh % H, c = threadIdx.x;
+  const int row = v.on() ? h : sh, s0 = v.on() ? v.chunk[sh / H] : 0, s1 = v.on() ? v.chunk[sh / H + 1] : nseg;
+  float lam = d_final_cov ? d_final_cov[(size_t)sh * K + c] : 0.f;
+  for (int s = s1 - 1; s >= s0; --s) {
+    lam_carry[((size_t)row * nseg + s) * K + c] = lam;
+    const float2 m = maps[((size_t)row * nseg + s) * K + c];
     lam = m.x * lam + m.y;
   }
 }
@@ -523,13 +547,15 @@ __global__ void __launch_bounds__(K) diag_gain_bwd_emit_kernel(
     const bf16* __restrict__ r_raw, const float* __restrict__ dkappa, const float* __restrict__ carry,
     const float* __restrict__ lam_carry, const float2* __restrict__ dg_tok, float* __restrict__ dk_out,
     float* __restrict__ dalpha, bf16* __restrict__ domega_raw, bf16* __restrict__ dr_raw,
-    float* __restrict__ dinit, float* __restrict__ d_init_cov, int T, int H, int nseg) {
+    float* __restrict__ dinit, float* __restrict__ d_init_cov, int T, int H, int nseg, Varlen v) {
   constexpr int TF = 8, TT = 8;
   __shared__ float red[K / 32 * TT];
   __shared__ float tok[TT];
   __shared__ float pprev_s[kDiagSeg][K];
   const int seg = blockIdx.x, bh = blockIdx.y, b = bh / H, h = bh - b * H, c = threadIdx.x;
-  const int t0 = seg * kDiagSeg, n = min(kDiagSeg, T - t0);
+  int t0, n, sh;
+  seg_span(v, seg, T, H, bh, t0, n, sh);
+  const bool first = v.on() ? seg == v.chunk[sh / H] : seg == 0;  // the stream's first segment
   const size_t row0 = ((size_t)b * T + t0) * H + h;
   const float Kf = (float)K;
   // forward re-run of the covariance: p before every token of the segment
@@ -611,8 +637,8 @@ __global__ void __launch_bounds__(K) diag_gain_bwd_emit_kernel(
       dr_raw[row] = __float2bfloat16_rn(drt * sigmoidf_(__bfloat162float(r_raw[row])));
     }
   }
-  if (seg == 0 && d_init_cov) d_init_cov[(size_t)bh * K + c] = lam;  // d L / d p_{-1}
-  if (seg == 0 && dinit) {
+  if (first && d_init_cov) d_init_cov[(size_t)sh * K + c] = lam;  // d L / d p_{-1}
+  if (first && dinit) {
     // p_{-1} = 1/mu, so d mu = -sum_c lambda_{-1,c} p_{-1,c}^2
     const float p0 = pprev_s[0][c];
     float v = -lam * p0 * p0;
@@ -730,12 +756,15 @@ namespace {
 struct DiagDims {
   int64_t B, T, H, K;
   int nseg;
+  Varlen v;  // packed batch (B = 1): segments are the sequences' 64-token chunks
+  // (sequence, head) streams of the carry kernels
+  unsigned streams() const { return (unsigned)(v.on() ? (int64_t)v.n * H : B * H); }
 };
 
 int diag_dims(const char* what, int64_t B, int64_t T, int64_t H, int64_t K, DiagDims* d) {
   if (K != 64 && K != 128) return set_error(KDN_ERR_INVALID, "%s: K must be 64 or 128, got %lld", what, (long long)K);
   if (T > INT32_MAX || B * H > 65535) return set_error(KDN_ERR_INVALID, "%s: size too large", what);
-  *d = DiagDims{B, T, H, K, (int)((T + kDiagSeg - 1) / kDiagSeg)};
+  *d = DiagDims{B, T, H, K, (int)((T + kDiagSeg - 1) / kDiagSeg), Varlen{nullptr, nullptr, nullptr, nullptr, 0}};
   return KDN_OK;
 }
 
@@ -743,9 +772,9 @@ int diag_fwd_maps(const DiagDims& d, const float* k, const float* alpha, const f
                   float4* maps, cudaStream_t st) {
   dim3 grid((unsigned)d.nseg, (unsigned)(d.B * d.H));
   if (d.K == 128)
-    diag_gain_map_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, maps, (int)d.T, (int)d.H, d.nseg);
+    diag_gain_map_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, maps, (int)d.T, (int)d.H, d.nseg, d.v);
   else
-    diag_gain_map_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, maps, (int)d.T, (int)d.H, d.nseg);
+    diag_gain_map_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, maps, (int)d.T, (int)d.H, d.nseg, d.v);
   return check_launch("diag_gain_map_kernel");
 }
 
@@ -753,13 +782,14 @@ int diag_fwd_finish(const DiagDims& d, const float* k, const float* alpha, const
                     const float* init_prec, const float* init_cov, const float4* maps, float* kappa, float* carry,
                     float* p_final, cudaStream_t st) {
   dim3 grid((unsigned)d.nseg, (unsigned)(d.B * d.H));
-  const unsigned bh = (unsigned)(d.B * d.H);
+  const unsigned sh = d.streams();
   if (d.K == 128) {
-    diag_gain_carry_kernel<128><<<bh, 128, 0, st>>>(maps, init_prec, init_cov, carry, p_final, (int)d.H, d.nseg);
-    diag_gain_emit_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, carry, kappa, (int)d.T, (int)d.H, d.nseg);
+    diag_gain_carry_kernel<128><<<sh, 128, 0, st>>>(maps, init_prec, init_cov, carry, p_final, (int)d.H, d.nseg, d.v);
+    diag_gain_emit_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, carry, kappa, (int)d.T, (int)d.H, d.nseg,
+                                                     d.v);
   } else {
-    diag_gain_carry_kernel<64><<<bh, 64, 0, st>>>(maps, init_prec, init_cov, carry, p_final, (int)d.H, d.nseg);
-    diag_gain_emit_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, carry, kappa, (int)d.T, (int)d.H, d.nseg);
+    diag_gain_carry_kernel<64><<<sh, 64, 0, st>>>(maps, init_prec, init_cov, carry, p_final, (int)d.H, d.nseg, d.v);
+    diag_gain_emit_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, carry, kappa, (int)d.T, (int)d.H, d.nseg, d.v);
   }
   return check_launch("diag_gain_fwd kernels");
 }
@@ -786,10 +816,10 @@ int diag_bwd_maps(const DiagDims& d, const float* k, const float* alpha, const f
   dim3 grid((unsigned)d.nseg, (unsigned)(d.B * d.H));
   if (d.K == 128)
     diag_gain_bwd_map_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, dkappa, carry, w.maps, w.dg_tok, (int)d.T,
-                                                        (int)d.H, d.nseg);
+                                                        (int)d.H, d.nseg, d.v);
   else
     diag_gain_bwd_map_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, dkappa, carry, w.maps, w.dg_tok, (int)d.T,
-                                                      (int)d.H, d.nseg);
+                                                      (int)d.H, d.nseg, d.v);
   return check_launch("diag_gain_bwd_map_kernel");
 }
 
@@ -802,17 +832,17 @@ int diag_bwd_finish(const DiagDims& d, const float* k, const float* alpha, const
     return check_launch("memset d_initial_precision");
   float* dmu = init_cov ? nullptr : dinit;  // with a carried-in covariance the prior gets no gradient here
   dim3 grid((unsigned)d.nseg, (unsigned)(d.B * d.H));
-  const unsigned bh = (unsigned)(d.B * d.H);
+  const unsigned sh = d.streams();
   if (d.K == 128) {
-    diag_gain_bwd_carry_kernel<128><<<bh, 128, 0, st>>>(w.maps, d_final_cov, w.lam, d.nseg);
+    diag_gain_bwd_carry_kernel<128><<<sh, 128, 0, st>>>(w.maps, d_final_cov, w.lam, (int)d.H, d.nseg, d.v);
     diag_gain_bwd_emit_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, init_prec, wr, rr, dkappa, carry, w.lam,
                                                          w.dg_tok, dk, dalpha, domega_raw, dr_raw, dmu, d_init_cov,
-                                                         (int)d.T, (int)d.H, d.nseg);
+                                                         (int)d.T, (int)d.H, d.nseg, d.v);
   } else {
-    diag_gain_bwd_carry_kernel<64><<<bh, 64, 0, st>>>(w.maps, d_final_cov, w.lam, d.nseg);
+    diag_gain_bwd_carry_kernel<64><<<sh, 64, 0, st>>>(w.maps, d_final_cov, w.lam, (int)d.H, d.nseg, d.v);
     diag_gain_bwd_emit_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, init_prec, wr, rr, dkappa, carry, w.lam,
                                                        w.dg_tok, dk, dalpha, domega_raw, dr_raw, dmu, d_init_cov,
-                                                       (int)d.T, (int)d.H, d.nseg);
+                                                       (int)d.T, (int)d.H, d.nseg, d.v);
   }
   return check_launch("diag_gain_bwd kernels");
 }
@@ -950,6 +980,76 @@ int kdn_diag_gain_bwd_finish(const float* k, const float* alpha, const float* om
                          static_cast<const bf16*>(r_raw), dkappa, carry, d_final_cov, dk, dalpha,
                          static_cast<bf16*>(domega_raw), static_cast<bf16*>(dr_raw), dinit, d_init_cov,
                          diag_bwd_ws(d, ws), (cudaStream_t)stream);
+}
+
+int64_t kdn_diag_gain_varlen_carry_elems(int64_t H, int64_t K, int64_t num_chunks) {
+  return H > 0 && K > 0 && num_chunks > 0 ? H * num_chunks * K : 0;
+}
+
+size_t kdn_diag_gain_varlen_workspace_bytes(int64_t T, int64_t H, int64_t K, int64_t num_chunks) {
+  if (T <= 0 || H <= 0 || K <= 0 || num_chunks <= 0) return 0;
+  const size_t maps = align_up(sizeof(float4) * H * num_chunks * K, 256);
+  const size_t bwd = align_up(sizeof(float2) * H * num_chunks * K, 256) + align_up(sizeof(float) * H * num_chunks * K, 256) +
+                     align_up(sizeof(float2) * H * T, 256);
+  return maps > bwd ? maps : bwd;
+}
+
+}  // extern "C"
+
+namespace kdn {
+namespace {
+int diag_varlen_dims(const char* what, int64_t T, int64_t H, int64_t K, const int32_t* table, int64_t num_seqs,
+                     int64_t num_chunks, void* ws, size_t ws_bytes, DiagDims* d) {
+  if (!table || num_seqs <= 0 || num_chunks < num_seqs || num_chunks > INT32_MAX)
+    return set_error(KDN_ERR_INVALID, "%s: a kdn_varlen_plan table, num_seqs > 0 and num_chunks required", what);
+  if (int rc = diag_dims(what, 1, T, H, K, d)) return rc;
+  if (num_chunks * kDiagSeg < T) return set_error(KDN_ERR_INVALID, "%s: num_chunks does not cover T", what);
+  if (!ws || ws_bytes < kdn_diag_gain_varlen_workspace_bytes(T, H, K, num_chunks))
+    return set_error(KDN_ERR_WORKSPACE, "%s: workspace too small", what);
+  d->nseg = (int)num_chunks;
+  d->v = varlen_view(table, num_seqs);
+  return KDN_OK;
+}
+}  // namespace
+}  // namespace kdn
+
+extern "C" {
+
+int kdn_diag_gain_fwd_varlen(const float* k, const float* alpha, const float* omega, const float* r,
+                             const float* init_prec, const float* init_cov, float* kappa, float* carry,
+                             float* p_final, int64_t T, int64_t H, int64_t K, const int32_t* varlen_table,
+                             int64_t num_seqs, int64_t num_chunks, void* ws, size_t ws_bytes, kdn_stream_t stream) {
+  if (H <= 0 || T <= 0 || !k || !alpha || !omega || !r || !init_prec || !kappa || !carry)
+    return set_error(KDN_ERR_INVALID, "kdn_diag_gain_fwd_varlen: invalid arguments");
+  DiagDims d;
+  if (int rc = diag_varlen_dims("kdn_diag_gain_fwd_varlen", T, H, K, varlen_table, num_seqs, num_chunks, ws, ws_bytes,
+                                &d))
+    return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  float4* maps = static_cast<float4*>(ws);
+  if (int rc = diag_fwd_maps(d, k, alpha, omega, r, maps, st)) return rc;
+  return diag_fwd_finish(d, k, alpha, omega, r, init_prec, init_cov, maps, kappa, carry, p_final, st);
+}
+
+int kdn_diag_gain_bwd_varlen(const float* k, const float* alpha, const float* omega, const float* r,
+                             const float* init_prec, const float* init_cov, const void* omega_raw, const void* r_raw,
+                             const float* dkappa, const float* carry, const float* d_final_cov, float* dk,
+                             float* dalpha, void* domega_raw, void* dr_raw, float* dinit, float* d_init_cov,
+                             int64_t T, int64_t H, int64_t K, const int32_t* varlen_table, int64_t num_seqs,
+                             int64_t num_chunks, void* ws, size_t ws_bytes, kdn_stream_t stream) {
+  if (H <= 0 || T <= 0 || !k || !alpha || !omega || !r || !init_prec || !omega_raw || !r_raw || !dkappa || !carry ||
+      !dk || !dalpha || !domega_raw || !dr_raw)
+    return set_error(KDN_ERR_INVALID, "kdn_diag_gain_bwd_varlen: invalid arguments");
+  DiagDims d;
+  if (int rc = diag_varlen_dims("kdn_diag_gain_bwd_varlen", T, H, K, varlen_table, num_seqs, num_chunks, ws, ws_bytes,
+                                &d))
+    return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  const DiagBwdWs w = diag_bwd_ws(d, ws);
+  if (int rc = diag_bwd_maps(d, k, alpha, omega, r, dkappa, carry, w, st)) return rc;
+  return diag_bwd_finish(d, k, alpha, omega, r, init_prec, init_cov, static_cast<const bf16*>(omega_raw),
+                         static_cast<const bf16*>(r_raw), dkappa, carry, d_final_cov, dk, dalpha,
+                         static_cast<bf16*>(domega_raw), static_cast<bf16*>(dr_raw), dinit, d_init_cov, w, st);
 }
 
 }  // extern "C"

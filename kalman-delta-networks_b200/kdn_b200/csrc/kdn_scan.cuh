@@ -91,6 +91,10 @@ struct ScanParams {
   // segment's linear state map); neither writes o or h
   int state_map;
   float* ST2;
+  // packed variable-length batch (B = 1, NT = the global chunk count): the
+  // chunk-parallel kernels take chunk c's tokens from the table, the
+  // sequential ones run one (sequence, head) stream per CTA pair
+  Varlen vl;
 };
 
 __host__ __device__ constexpr size_t A128(size_t x) { return align_up(x, 128); }
@@ -219,6 +223,61 @@ __device__ __forceinline__ void load_tile_op(typename CF::OpT* dst, int ld, cons
 
 __device__ __forceinline__ size_t tok_row(const ScanParams& p, int b, int h, int t) {
   return ((size_t)b * p.T + t) * p.H + h;
+}
+
+// First token and length of chunk c (a global chunk of a packed batch).
+template <int C>
+__device__ __forceinline__ void chunk_span(const ScanParams& p, int c, int& t0, int& L) {
+  if (p.vl.on()) {  // (packed batches run the bf16 precision only: C = 64)
+    int s;
+    varlen_span(p.vl, c, t0, L, s);
+  } else {
+    t0 = c * C;
+    L = min(C, p.T - t0);
+  }
+}
+
+// Stream of a sequential-pass CTA (blockIdx.x): its chunk range, the row of
+// the per-(b, h) records and states it reads, and its state index.  A packed
+// batch runs its (sequence, head) streams longest sequence first.
+struct SeqStream {
+  int b, h, c_lo, c_hi;
+  size_t rec_row;  // (b * H + h): chunk c's record is rec_row * NT + c
+  size_t state;    // index of the [K][V] initial / final state
+};
+// CTAs (per value half) of a sequential pass: one per stream.
+inline unsigned seq_streams(const ScanParams& p) {
+  return (unsigned)(p.vl.on() ? (int64_t)p.vl.n * p.H : (int64_t)p.B * p.H);
+}
+__device__ __forceinline__ SeqStream seq_stream(const ScanParams& p, int slot) {
+  SeqStream s;
+  if (p.vl.on()) {
+    const int seq = p.vl.order[slot / p.H];
+    s.b = 0;
+    s.h = slot - (slot / p.H) * p.H;
+    s.c_lo = p.vl.chunk[seq];
+    s.c_hi = p.vl.chunk[seq + 1];
+    s.rec_row = (size_t)s.h;
+    s.state = (size_t)seq * p.H + s.h;
+  } else {
+    s.b = slot / p.H;
+    s.h = slot - s.b * p.H;
+    s.c_lo = p.c_lo;
+    s.c_hi = p.c_hi;
+    s.rec_row = (size_t)slot;
+    s.state = (size_t)slot;
+  }
+  return s;
+}
+
+// Zero rows [L, C) of a 128-byte-swizzled [C][64] bf16 tile (a packed
+// batch's last chunk of a sequence: its TMA box runs into the next sequence).
+template <int C>
+__device__ __forceinline__ void zero_tail_rows(char* tile, int L, int tid, int nth) {
+  for (int e = L * 8 + tid; e < C * 8; e += nth) {
+    const int r = e >> 3, g = e & 7;  // row, 16-byte granule (swizzled by row % 8)
+    *reinterpret_cast<uint4*>(tile + r * 128 + ((g ^ (r & 7)) << 4)) = make_uint4(0, 0, 0, 0);
+  }
 }
 
 // Stage a chunk's q, k, g (and kappa or beta) rows in shared memory (cp.async,

@@ -55,6 +55,13 @@ bool sizes_of(const KdnScanArgs* a, Sizes* s) {
   s->C = (iso || !f32) ? 64 : 32;
   s->NT = (a->T + s->C - 1) / s->C;
   s->BH = a->B * a->H;
+  if (a->num_seqs > 0) {
+    // packed batch: the sequences' own chunks, numbered globally (B = 1, bf16)
+    if (!a->varlen_table || a->B != 1 || f32 || a->num_chunks < a->num_seqs || a->num_chunks * 64 < a->T ||
+        a->num_chunks > a->T)
+      return false;
+    s->NT = a->num_chunks;
+  }
   if (iso) {
     f32 ? layout_sizes<IsoF>(s) : layout_sizes<IsoB>(s);
   } else {
@@ -111,6 +118,7 @@ int fill_params(const KdnScanArgs* a, const Sizes& s, ScanParams* p) {
   p->c_lo = 0;
   p->c_hi = (int)s.NT;
   p->scale = a->scale;
+  p->vl = varlen_view(a->varlen_table, a->num_seqs);
   return KDN_OK;
 }
 
@@ -151,6 +159,49 @@ __global__ void gate_fold_kernel(float4* __restrict__ dg, int64_t T, int64_t HK4
       acc.w += y.w;
     }
     float4& z = dg[(b * T + t31) * HK4 + col];
+    z.x += acc.x;
+    z.y += acc.y;
+    z.z += acc.z;
+    z.w += acc.w;
+  }
+}
+
+// The same two conversions for a packed batch, whose 64-token chunks start
+// at each sequence's first token (global chunk gc: tokens t0 .. t0 + L).
+__global__ void gate_to64_varlen_kernel(const float4* __restrict__ g, float4* __restrict__ g64, Varlen v,
+                                        int64_t HK4, int64_t n4) {
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n4; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t per = 64 * HK4, gc = e / per, rem = e - gc * per, r = rem / HK4, col = rem - r * HK4;
+    int t0, L, sq;
+    varlen_span(v, (int)gc, t0, L, sq);
+    if (r >= L) continue;
+    float4 x = g[(t0 + r) * HK4 + col];
+    if (r >= 32) {
+      const float4 y = g[(t0 + 31) * HK4 + col];
+      x.x += y.x;
+      x.y += y.y;
+      x.z += y.z;
+      x.w += y.w;
+    }
+    g64[(t0 + r) * HK4 + col] = x;
+  }
+}
+
+__global__ void gate_fold_varlen_kernel(float4* __restrict__ dg, Varlen v, int64_t HK4, int64_t n) {
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t gc = e / HK4, col = e - gc * HK4;
+    int t0, L, sq;
+    varlen_span(v, (int)gc, t0, L, sq);
+    if (L <= 32) continue;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int r = 32; r < L; ++r) {
+      const float4 y = dg[(t0 + r) * HK4 + col];
+      acc.x += y.x;
+      acc.y += y.y;
+      acc.z += y.z;
+      acc.w += y.w;
+    }
+    float4& z = dg[(t0 + 31) * HK4 + col];
     z.x += acc.x;
     z.y += acc.y;
     z.z += acc.z;
@@ -205,13 +256,17 @@ size_t kdn_scan_workspace_bytes(const KdnScanArgs* a) {
 int kdn_scan_fwd(const KdnScanArgs* a, kdn_stream_t stream) {
   Sizes s;
   if (!sizes_of(a, &s))
-    return set_error(KDN_ERR_INVALID, "kdn_scan_fwd: unsupported variant/precision or shape (K and V must be 128)");
+    return set_error(KDN_ERR_INVALID,
+                     "kdn_scan_fwd: unsupported variant/precision or shape (K and V must be 128; a packed batch "
+                     "needs B = 1, the bf16 precision and its kdn_varlen_plan table)");
   const int mode = a->mode;
   if (mode != KDN_SCAN_FULL && mode != KDN_SCAN_FWD_RECORDS && mode != KDN_SCAN_FWD_SEQUENTIAL &&
       mode != KDN_SCAN_FWD_STATE_MAP)
     return set_error(KDN_ERR_INVALID, "kdn_scan_fwd: mode %d is not a forward mode", mode);
   if (mode != KDN_SCAN_FULL && a->precision != KDN_PREC_BF16)
     return set_error(KDN_ERR_INVALID, "kdn_scan_fwd: the partial-pass modes need the bf16 precision");
+  if (a->num_seqs > 0 && mode != KDN_SCAN_FULL)
+    return set_error(KDN_ERR_INVALID, "kdn_scan_fwd: a packed batch runs mode 0 only");
   const bool need_o = mode == KDN_SCAN_FULL || mode == KDN_SCAN_FWD_SEQUENTIAL;
   if (!a->q || !a->k || !a->v || !a->g || (need_o && !a->o) || !a->saved ||
       (a->variant == KDN_ISO ? !a->beta : !a->kappa))
@@ -233,8 +288,14 @@ int kdn_scan_fwd(const KdnScanArgs* a, kdn_stream_t stream) {
   if (!iso && (mode == KDN_SCAN_FULL || mode == KDN_SCAN_FWD_RECORDS)) {
     // 32-local gate prefix -> 64-local, kept in `saved` for the later passes
     const int64_t HK4 = a->H * a->K / 4, n4 = a->B * a->T * HK4;
-    gate_to64_kernel<<<grid_for(n4), 256, 0, st>>>(reinterpret_cast<const float4*>(a->g),
-                                                   reinterpret_cast<float4*>(g64), a->T, HK4, n4);
+    if (p.vl.on()) {
+      const int64_t nv = s.NT * 64 * HK4;
+      gate_to64_varlen_kernel<<<grid_for(nv), 256, 0, st>>>(reinterpret_cast<const float4*>(a->g),
+                                                            reinterpret_cast<float4*>(g64), p.vl, HK4, nv);
+    } else {
+      gate_to64_kernel<<<grid_for(n4), 256, 0, st>>>(reinterpret_cast<const float4*>(a->g),
+                                                     reinterpret_cast<float4*>(g64), a->T, HK4, n4);
+    }
     rc = check_launch("gate_to64_kernel");
     if (rc != KDN_OK) return rc;
   }
@@ -252,13 +313,17 @@ int kdn_scan_fwd(const KdnScanArgs* a, kdn_stream_t stream) {
 int kdn_scan_bwd(const KdnScanArgs* a, kdn_stream_t stream) {
   Sizes s;
   if (!sizes_of(a, &s))
-    return set_error(KDN_ERR_INVALID, "kdn_scan_bwd: unsupported variant/precision or shape (K and V must be 128)");
+    return set_error(KDN_ERR_INVALID,
+                     "kdn_scan_bwd: unsupported variant/precision or shape (K and V must be 128; a packed batch "
+                     "needs B = 1, the bf16 precision and its kdn_varlen_plan table)");
   const bool iso = a->variant == KDN_ISO;
   const int mode = a->mode;
   if (mode != KDN_SCAN_FULL && mode != KDN_SCAN_BWD_STATE)
     return set_error(KDN_ERR_INVALID, "kdn_scan_bwd: mode %d is not a backward mode", mode);
   if (mode != KDN_SCAN_FULL && a->precision != KDN_PREC_BF16)
     return set_error(KDN_ERR_INVALID, "kdn_scan_bwd: the partial-pass modes need the bf16 precision");
+  if (a->num_seqs > 0 && mode != KDN_SCAN_FULL)
+    return set_error(KDN_ERR_INVALID, "kdn_scan_bwd: a packed batch runs mode 0 only");
   if (mode == KDN_SCAN_BWD_STATE) {
     if (!a->q || !a->k || !a->v || !a->g || !a->saved || !a->dO || !a->d_initial_state ||
         (iso ? !a->beta : !a->kappa))
@@ -287,7 +352,12 @@ int kdn_scan_bwd(const KdnScanArgs* a, kdn_stream_t stream) {
   if (rc != KDN_OK) return rc;
   // cotangent of the 64-local prefix -> the boundary's 32-local one
   const int64_t HK4 = a->H * a->K / 4, NB64 = (a->T + 63) / 64, n = a->B * NB64 * HK4;
-  gate_fold_kernel<<<grid_for(n), 256, 0, st>>>(reinterpret_cast<float4*>(a->dg), a->T, HK4, NB64, n);
+  if (p.vl.on()) {
+    const int64_t nv = s.NT * HK4;
+    gate_fold_varlen_kernel<<<grid_for(nv), 256, 0, st>>>(reinterpret_cast<float4*>(a->dg), p.vl, HK4, nv);
+  } else {
+    gate_fold_kernel<<<grid_for(n), 256, 0, st>>>(reinterpret_cast<float4*>(a->dg), a->T, HK4, NB64, n);
+  }
   return check_launch("gate_fold_kernel");
 }
 

@@ -257,11 +257,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_bwd_state_tc_kernel(ScanPa
   extern __shared__ __align__(1024) char smem_raw[];
   char* base = align1024(smem_raw);
 
-  const int bh = blockIdx.x, vh = blockIdx.y, V0 = 64 * vh, b = bh / p.H, h = bh - b * p.H;
+  const SeqStream ss = seq_stream(p, blockIdx.x);
+  const int vh = blockIdx.y, V0 = 64 * vh, b = ss.b, h = ss.h, c_lo = ss.c_lo, c_hi = ss.c_hi;
+  const bool vl = p.vl.on();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const char* recs = static_cast<const char*>(p.rec) + (size_t)bh * p.NT * R::bytes;
+  const char* recs = static_cast<const char*>(p.rec) + ss.rec_row * p.NT * R::bytes;
   char* dhout =
-      static_cast<char*>(p.dh) + (size_t)bh * p.NT * 2 * hblock_bytes<CF>() + (size_t)vh * hblock_bytes<CF>();
+      static_cast<char*>(p.dh) + ss.rec_row * p.NT * 2 * hblock_bytes<CF>() + (size_t)vh * hblock_bytes<CF>();
   uint64_t* full = reinterpret_cast<uint64_t*>(base + Lo::bar);
   uint64_t* empty = full + NS;
   uint64_t* mmab = empty + NS;
@@ -284,14 +286,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_bwd_state_tc_kernel(ScanPa
   const uint32_t tmem = *tslot;
 
   if (warp == kTcWarps) {
-    for (int it = 0; it < p.c_hi - p.c_lo; ++it) {
-      const int s = it % NS, c = p.c_hi - 1 - it;
+    for (int it = 0; it < c_hi - c_lo; ++it) {
+      const int s = it % NS, c = c_hi - 1 - it;
       if (it >= NS) mbar_wait(&empty[s], (it / NS - 1) & 1, p.status);
       if (lane == 0) {
         char* st = base + s * Lo::stage;
+        int t0, L;
+        chunk_span<C>(p, c, t0, L);
         mbar_expect_tx(&full[s], (unsigned)(Lo::rec + (size_t)C * (Lo::DF32 ? 256 : 128)));
         bulk_g2s(st, recs + (size_t)c * R::bytes + R::bwd_begin, (unsigned)Lo::rec, &full[s]);
-        tma_load_4d(st + Lo::dO, &maps.in, V0, h, c * C, b, &full[s]);
+        tma_load_4d(st + Lo::dO, &maps.in, V0, h, t0, b, &full[s]);
       }
       __syncwarp();
     }
@@ -305,26 +309,35 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_bwd_state_tc_kernel(ScanPa
   for (int j = 0; j < 32; j += 16) {
     float x[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) x[i] = p.dST ? p.dST[((size_t)bh * kKD + row) * kVD + V0 + 32 * hf + j + i] : 0.f;
+    for (int i = 0; i < 16; ++i) x[i] = p.dST ? p.dST[(ss.state * kKD + row) * kVD + V0 + 32 * hf + j + i] : 0.f;
     tc::st16(tl + TS + 32 * hf + j, x);
   }
   tc::wait_st();
   uint32_t mph = 0;
 
-  for (int it = 0; it < p.c_hi - p.c_lo; ++it) {
-    const int s = it % NS, c = p.c_hi - 1 - it;
+  for (int it = 0; it < c_hi - c_lo; ++it) {
+    const int s = it % NS, c = c_hi - 1 - it;
     char* st = base + s * Lo::stage;
     char* sdO = Lo::DF32 ? base + Lo::dOb : st + Lo::dO;
+    // rows past a packed sequence's end (its last chunk's box ran into the
+    // next sequence) are zeroed
+    int L = C;
+    if (vl) {
+      int t0;
+      chunk_span<C>(p, c, t0, L);
+    }
     mbar_wait(&full[s], (it / NS) & 1, p.status);
     if constexpr (Lo::DF32) {
       // the reference rounds the fp32 cotangent to bf16 first (diag_kdn_chunk.py:3277)
       const float* src = reinterpret_cast<const float*>(st + Lo::dO);
       for (int e = threadIdx.x; e < C * 8; e += NTH) {
         const int r = e >> 3, g = e & 7;
-        float x[8];
-        ld8(x, src + r * 64 + 8 * g);
+        float x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (r < L) ld8(x, src + r * 64 + 8 * g);
         st8(reinterpret_cast<bf16*>(sdO + tc::sw_off(r, 8 * g, C)), x);
       }
+    } else {
+      if (L < C) zero_tail_rows<C>(sdO, L, threadIdx.x, NTH);
     }
     {
       // adjoint operand (and dh), then dS <- 2^g_L dS
@@ -390,7 +403,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_bwd_state_tc_kernel(ScanPa
       float x[16];
       tc::ld16(tl + TS + 32 * hf + j, x);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) p.dS0[((size_t)bh * kKD + row) * kVD + V0 + 32 * hf + j + i] = x[i];
+      for (int i = 0; i < 16; ++i) p.dS0[(ss.state * kKD + row) * kVD + V0 + 32 * hf + j + i] = x[i];
     }
   }
   if (threadIdx.x == 32) bulk_wait_all();
@@ -938,7 +951,7 @@ int launch_bwd_state(const ScanParams& p, cudaStream_t st) {
                      : encode_bthd(&maps.in, p.dO, false, p.B, p.T, p.H, kVD, 64, CF::C, false);
     if (rc != KDN_OK) return rc;
     maps.out = maps.in;
-    scan_bwd_state_tc_kernel<CF><<<dim3(p.B * p.H, 2), kTcThreads, StateTcLayout<CF>::bytes, st>>>(p, maps);
+    scan_bwd_state_tc_kernel<CF><<<dim3(seq_streams(p), 2), kTcThreads, StateTcLayout<CF>::bytes, st>>>(p, maps);
   }
   return check_launch("scan_bwd_state_kernel");
 }

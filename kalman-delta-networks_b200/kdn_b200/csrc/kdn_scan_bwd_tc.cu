@@ -104,6 +104,18 @@ __device__ __noinline__ ExactTerms exact_terms(const float* g, const bf16* k, co
   return t;
 }
 
+// Rows [0, L) of a plain staging tile (row pitch `src_row` bytes) to
+// global rows `dst_pitch` bytes apart, 16 bytes per thread and step (every
+// thread of the block takes part).
+__device__ __forceinline__ void copy_rows_out(void* dst, size_t dst_pitch, const void* src, int src_row, int L) {
+  const int g = src_row / 16;
+  for (int e = threadIdx.x; e < L * g; e += blockDim.x) {
+    const int r = e / g, x = e - r * g;
+    *reinterpret_cast<uint4*>(static_cast<char*>(dst) + r * dst_pitch + 16 * x) =
+        *reinterpret_cast<const uint4*>(static_cast<const char*>(src) + (size_t)r * src_row + 16 * x);
+  }
+}
+
 template <class CF>
 __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p, const __grid_constant__ ChunkMaps maps) {
   using Lo = ChunkTcLayout<CF>;
@@ -119,7 +131,11 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
   const int c = p.c_lo + blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q = warp & 3, cg = warp >> 2;  // TMEM lane quadrant, column group
-  const int t0 = c * C, L = min(C, p.T - t0);
+  int t0, L;
+  chunk_span<C>(p, c, t0, L);
+  // a packed sequence's last chunk: its boxes ran into the next sequence's
+  // rows (zeroed after landing) and its rows leave by plain stores
+  const bool tail = p.vl.on() && L < C;
   const size_t cc = (size_t)bh * p.NT + c;
   uint64_t* ldbar = reinterpret_cast<uint64_t*>(base + Lo::bar);
   uint64_t* mmab = ldbar + 1;
@@ -214,6 +230,14 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
     }
   }
   mbar_wait(ldbar, 0, p.status);
+  if (tail) {
+    zero_tail_rows<C>(base + Lo::vv, L, threadIdx.x, 512);
+    zero_tail_rows<C>(base + Lo::vv + C * 128, L, threadIdx.x, 512);
+    if constexpr (CF::ISO) {
+      zero_tail_rows<C>(base + Lo::dO, L, threadIdx.x, 512);
+      zero_tail_rows<C>(base + Lo::dO + C * 128, L, threadIdx.x, 512);
+    }
+  }
   fence_async_shared();
   tc::fence_before();
   __syncthreads();
@@ -352,7 +376,9 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
     }
   }
   publish();
-  if (threadIdx.x == 0) {
+  if (tail) {
+    copy_rows_out(p.dv + tok_row(p, b, h, t0) * kVD, (size_t)p.H * kVD * 2, base + Lo::dvst, kVD * 2, L);
+  } else if (threadIdx.x == 0) {
     tc::tma_store_4d(&maps.dv, base + Lo::dvst, 0, h, t0, b);
     bulk_commit();
   }
@@ -616,7 +642,12 @@ __global__ void __launch_bounds__(512, 1) scan_bwd_chunk_tc_kernel(ScanParams p,
   // the staged rows leave by TMA stores (rows past the sequence's end are clipped)
   fence_async_shared();
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (tail) {
+    const size_t r0 = tok_row(p, b, h, t0);
+    copy_rows_out(p.dk + r0 * kKD, (size_t)p.H * kKD * 2, sdk, kKD * 2, L);
+    copy_rows_out(p.dq + r0 * kKD, (size_t)p.H * kKD * 2, sdq, kKD * 2, L);
+    if (ch.fast) copy_rows_out(p.dg + r0 * kKD, (size_t)p.H * kKD * 4, sdg, kKD * 4, L);
+  } else if (threadIdx.x == 0) {
     tc::tma_store_4d(&maps.dk, sdk, 0, h, t0, b);
     tc::tma_store_4d(&maps.dq, sdq, 0, h, t0, b);
     if (ch.fast) tc::tma_store_4d(&maps.dg, sdg, 0, h, t0, b);

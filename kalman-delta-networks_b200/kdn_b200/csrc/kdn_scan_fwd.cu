@@ -238,10 +238,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_fwd_tc_kernel(ScanParams p
   extern __shared__ __align__(1024) char smem_raw[];
   char* base = align1024(smem_raw);
 
-  const int bh = blockIdx.x, vh = blockIdx.y, V0 = 64 * vh, b = bh / p.H, h = bh - b * p.H;
+  const SeqStream ss = seq_stream(p, blockIdx.x);
+  const int vh = blockIdx.y, V0 = 64 * vh, b = ss.b, h = ss.h, c_lo = ss.c_lo, c_hi = ss.c_hi;
+  const bool vl = p.vl.on();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const char* recs = static_cast<const char*>(p.rec) + (size_t)bh * p.NT * R::bytes;
-  char* hout = static_cast<char*>(p.h) + (size_t)bh * p.NT * 2 * hblock_bytes<CF>() + (size_t)vh * hblock_bytes<CF>();
+  const char* recs = static_cast<const char*>(p.rec) + ss.rec_row * p.NT * R::bytes;
+  char* hout = static_cast<char*>(p.h) + ss.rec_row * p.NT * 2 * hblock_bytes<CF>() + (size_t)vh * hblock_bytes<CF>();
   uint64_t* full = reinterpret_cast<uint64_t*>(base + Lo::bar);
   uint64_t* empty = full + NS;
   uint64_t* mmab = empty + NS;
@@ -268,14 +270,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_fwd_tc_kernel(ScanParams p
   const bool smap = p.state_map != 0, phi = smap && blockIdx.z == 1;
   if (warp == kTcWarps) {
     // producer: refill a stage once the MMAs of its previous chunk completed
-    for (int c = p.c_lo; c < p.c_hi; ++c) {
-      const int it = c - p.c_lo, s = it % NS;
+    for (int c = c_lo; c < c_hi; ++c) {
+      const int it = c - c_lo, s = it % NS;
       if (it >= NS) mbar_wait(&empty[s], (it / NS - 1) & 1, p.status);
       if (lane == 0) {
         char* st = base + s * Lo::stage;
+        int t0, L;
+        chunk_span<C>(p, c, t0, L);
         mbar_expect_tx(&full[s], (unsigned)(R::fwd_end + (phi ? 0 : (size_t)C * 128)));
         bulk_g2s(st, recs + (size_t)c * R::bytes, (unsigned)R::fwd_end, &full[s]);
-        if (!phi) tma_load_4d(st + Lo::v, &maps.in, V0, h, c * C, b, &full[s]);
+        if (!phi) tma_load_4d(st + Lo::v, &maps.in, V0, h, t0, b, &full[s]);
       }
       __syncwarp();
     }
@@ -294,7 +298,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_fwd_tc_kernel(ScanParams p
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
       const int col = V0 + 32 * hf + j + i;
-      x[i] = phi ? (row == col ? 1.f : 0.f) : p.S0 ? p.S0[((size_t)bh * kKD + row) * kVD + col] : 0.f;
+      x[i] = phi ? (row == col ? 1.f : 0.f) : p.S0 ? p.S0[(ss.state * kKD + row) * kVD + col] : 0.f;
     }
     tc::st16(tl + TS + 32 * hf + j, x);
   }
@@ -308,9 +312,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_fwd_tc_kernel(ScanParams p
   //             then o(c) -> output tile -> TMA store
   char* sO = base + Lo::O;
   auto head = [&](int c) {
-    const int it = c - p.c_lo, s = it % NS;
+    const int it = c - c_lo, s = it % NS;
     char* st = base + s * Lo::stage;
     mbar_wait(&full[s], (it / NS) & 1, p.status);
+    if (vl) {
+      // a sequence's last chunk: the box ran into the next sequence's rows
+      int t0, L;
+      chunk_span<C>(p, c, t0, L);
+      if (L < C) zero_tail_rows<C>(st + Lo::v, L, threadIdx.x, NTH);
+    }
     const float gl = reinterpret_cast<const float*>(st + R::F)[2 * kKD + row];
 #pragma unroll
     for (int j = 0; j < 32; j += 16) {
@@ -342,9 +352,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_fwd_tc_kernel(ScanParams p
     }
   };
 
-  if (p.c_lo < p.c_hi) head(p.c_lo);
-  for (int c = p.c_lo; c < p.c_hi; ++c) {
-    const int it = c - p.c_lo, s = it % NS, t0 = c * C;
+  if (c_lo < c_hi) head(c_lo);
+  for (int c = c_lo; c < c_hi; ++c) {
+    const int it = c - c_lo, s = it % NS;
+    int t0, L;
+    chunk_span<C>(p, c, t0, L);
     char* st = base + s * Lo::stage;
     mbar_wait(mmab, mph, p.status);
     mph ^= 1;
@@ -382,7 +394,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_fwd_tc_kernel(ScanParams p
     tc::fence_after();
     // the next chunk's delta products go first (they write other TMEM columns
     // and no tile this chunk still reads) ...
-    if (c + 1 < p.c_hi) {
+    if (c + 1 < c_hi) {
       head(c + 1);
     } else {
       if (threadIdx.x == 0) bulk_wait_read<0>();
@@ -405,7 +417,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_fwd_tc_kernel(ScanParams p
     fence_async_shared();
     tc::fence_before();
     bar_sync(1, NTH);
-    if (threadIdx.x == 0) {
+    if (vl && L < C) {
+      // a sequence's last chunk of a packed batch: rows past its end belong
+      // to the next sequence, so the rows leave by plain stores
+      constexpr int G = 64 * (int)sizeof(OutT) / 16;  // 16-byte granules per row
+      for (int e = threadIdx.x; e < L * G; e += NTH) {
+        const int r = e / G, gi = e - r * G;
+        *reinterpret_cast<uint4*>(static_cast<OutT*>(p.o) + tok_row(p, b, h, t0 + r) * kVD + V0 + gi * (16 / sizeof(OutT))) =
+            *reinterpret_cast<const uint4*>(sO + (size_t)r * 64 * sizeof(OutT) + gi * 16);
+      }
+    } else if (threadIdx.x == 0) {
       tc::tma_store_4d(&maps.out, sO, V0, h, t0, b);
       bulk_commit();
     }
@@ -416,7 +437,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) scan_fwd_tc_kernel(ScanParams p
       float x[16];
       tc::ld16(tl + TS + 32 * hf + j, x);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) ST[((size_t)bh * kKD + row) * kVD + V0 + 32 * hf + j + i] = x[i];
+      for (int i = 0; i < 16; ++i) ST[(ss.state * kKD + row) * kVD + V0 + 32 * hf + j + i] = x[i];
     }
   }
   if (threadIdx.x == 0 || threadIdx.x == 32) bulk_wait_all();
@@ -467,7 +488,7 @@ int launch_fwd_seq(const ScanParams& p, cudaStream_t st) {
       rc = encode_bthd(&maps.out, p.o, CF::ISO, p.B, p.T, p.H, kVD, 64, CF::C, false);
       if (rc != KDN_OK) return rc;
     }
-    scan_fwd_tc_kernel<CF><<<dim3(p.B * p.H, 2, p.state_map ? 2 : 1), kTcThreads, smem, st>>>(p, maps);
+    scan_fwd_tc_kernel<CF><<<dim3(seq_streams(p), 2, p.state_map ? 2 : 1), kTcThreads, smem, st>>>(p, maps);
     return check_launch("scan_fwd_tc_kernel");
   }
 }

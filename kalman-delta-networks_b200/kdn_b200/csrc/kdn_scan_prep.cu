@@ -70,12 +70,13 @@ __global__ void __launch_bounds__(kPrepThreads, 2) scan_prep_kernel(ScanParams p
 
   const int c = p.c_lo + blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
   const int warp = threadIdx.x >> 5;
-  const int t0 = c * C;
+  int t0, L;
+  chunk_span<C>(p, c, t0, L);
   const size_t cc = (size_t)bh * p.NT + c;
 
   Chunk<CF> ch;
   bind_raw_global(ch, p, b, h, t0);
-  ch.L = min(C, p.T - t0);
+  ch.L = L;
   float* small = reinterpret_cast<float*>(base + Lo::small);
   bind_small(ch, small);
   ch.Kr = reinterpret_cast<OpT*>(base + Lo::Kr);

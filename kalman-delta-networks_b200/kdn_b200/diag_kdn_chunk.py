@@ -22,29 +22,45 @@ _VECTOR_DTYPE = torch.bfloat16
 _STATE_DTYPE = torch.float32
 
 
-def _gain_forward(k, alpha, omega, r, initial_precision, initial_cov=None, want_final=False):
+def _gain_forward(k, alpha, omega, r, initial_precision, initial_cov=None, want_final=False, plan=None):
     """Forward per-channel covariance scan; optional carried-in covariance
-    [B,H,K] and final covariance out (sequence parallelism)."""
+    [B,H,K] and final covariance out (sequence parallelism).  ``plan`` (a
+    packed batch's ``kdn_b200.varlen.VarlenPlan``): every sequence restarts
+    the covariance, states are [N,H,K]."""
     B, T, H, K = k.shape
     N.require_cuda(k)
     lib = N.load_library()
     kappa = torch.empty_like(k, dtype=_STATE_DTYPE)
-    carry = torch.empty(lib.kdn_diag_gain_carry_elems(B, T, H, K), dtype=torch.float32, device=k.device)
-    p_final = torch.empty((B, H, K), dtype=torch.float32, device=k.device) if want_final else None
-    ws = N.byte_buffer(lib.kdn_diag_gain_workspace_bytes(B, T, H, K), k.device)
-    N.check(
-        lib.kdn_diag_gain_fwd(
-            k.data_ptr(), alpha.data_ptr(), omega.data_ptr(), r.data_ptr(), initial_precision.data_ptr(),
-            N.ptr(initial_cov), kappa.data_ptr(), carry.data_ptr(), N.ptr(p_final), B, T, H, K, ws.data_ptr(),
-            ws.numel(), N.stream_of(k),
-        ),
-        "kdn_diag_gain_fwd",
-    )
+    streams = B if plan is None else plan.num_seqs
+    p_final = torch.empty((streams, H, K), dtype=torch.float32, device=k.device) if want_final else None
+    if plan is None:
+        carry = torch.empty(lib.kdn_diag_gain_carry_elems(B, T, H, K), dtype=torch.float32, device=k.device)
+        ws = N.byte_buffer(lib.kdn_diag_gain_workspace_bytes(B, T, H, K), k.device)
+        N.check(
+            lib.kdn_diag_gain_fwd(
+                k.data_ptr(), alpha.data_ptr(), omega.data_ptr(), r.data_ptr(), initial_precision.data_ptr(),
+                N.ptr(initial_cov), kappa.data_ptr(), carry.data_ptr(), N.ptr(p_final), B, T, H, K, ws.data_ptr(),
+                ws.numel(), N.stream_of(k),
+            ),
+            "kdn_diag_gain_fwd",
+        )
+    else:
+        nc = plan.num_chunks
+        carry = torch.empty(lib.kdn_diag_gain_varlen_carry_elems(H, K, nc), dtype=torch.float32, device=k.device)
+        ws = N.byte_buffer(lib.kdn_diag_gain_varlen_workspace_bytes(T, H, K, nc), k.device)
+        N.check(
+            lib.kdn_diag_gain_fwd_varlen(
+                k.data_ptr(), alpha.data_ptr(), omega.data_ptr(), r.data_ptr(), initial_precision.data_ptr(),
+                N.ptr(initial_cov), kappa.data_ptr(), carry.data_ptr(), N.ptr(p_final), T, H, K,
+                plan.table.data_ptr(), plan.num_seqs, nc, ws.data_ptr(), ws.numel(), N.stream_of(k),
+            ),
+            "kdn_diag_gain_fwd_varlen",
+        )
     return kappa, carry, p_final
 
 
 def _gain_backward(k, alpha, omega, r, initial_precision, omega_raw, r_raw, dkappa, carry, need_initial,
-                   initial_cov=None, d_final_cov=None, want_d_initial=False):
+                   initial_cov=None, d_final_cov=None, want_d_initial=False, plan=None):
     B, T, H, K = k.shape
     lib = N.load_library()
     dkappa = torch.zeros_like(k) if dkappa is None else dkappa.float().contiguous()
@@ -53,18 +69,23 @@ def _gain_backward(k, alpha, omega, r, initial_precision, omega_raw, r_raw, dkap
     domega_raw = torch.empty_like(omega_raw)
     dr_raw = torch.empty_like(r_raw)
     dinit = torch.empty((H,), dtype=_STATE_DTYPE, device=k.device) if need_initial else None
-    dic = torch.empty((B, H, K), dtype=_STATE_DTYPE, device=k.device) if want_d_initial else None
+    streams = B if plan is None else plan.num_seqs
+    dic = torch.empty((streams, H, K), dtype=_STATE_DTYPE, device=k.device) if want_d_initial else None
     dfc = None if d_final_cov is None else d_final_cov.float().contiguous()
-    ws = N.byte_buffer(lib.kdn_diag_gain_workspace_bytes(B, T, H, K), k.device)
-    N.check(
-        lib.kdn_diag_gain_bwd(
-            k.data_ptr(), alpha.data_ptr(), omega.data_ptr(), r.data_ptr(), initial_precision.data_ptr(),
+    head = (k.data_ptr(), alpha.data_ptr(), omega.data_ptr(), r.data_ptr(), initial_precision.data_ptr(),
             N.ptr(initial_cov), omega_raw.data_ptr(), r_raw.data_ptr(), dkappa.data_ptr(), carry.data_ptr(),
             N.ptr(dfc), dk.data_ptr(), dalpha.data_ptr(), domega_raw.data_ptr(), dr_raw.data_ptr(), N.ptr(dinit),
-            N.ptr(dic), B, T, H, K, ws.data_ptr(), ws.numel(), N.stream_of(k),
-        ),
-        "kdn_diag_gain_bwd",
-    )
+            N.ptr(dic))
+    if plan is None:
+        ws = N.byte_buffer(lib.kdn_diag_gain_workspace_bytes(B, T, H, K), k.device)
+        N.check(lib.kdn_diag_gain_bwd(*head, B, T, H, K, ws.data_ptr(), ws.numel(), N.stream_of(k)),
+                "kdn_diag_gain_bwd")
+    else:
+        nc = plan.num_chunks
+        ws = N.byte_buffer(lib.kdn_diag_gain_varlen_workspace_bytes(T, H, K, nc), k.device)
+        N.check(lib.kdn_diag_gain_bwd_varlen(*head, T, H, K, plan.table.data_ptr(), plan.num_seqs, nc,
+                                             ws.data_ptr(), ws.numel(), N.stream_of(k)),
+                "kdn_diag_gain_bwd_varlen")
     return dk, dalpha, domega_raw, dr_raw, dinit, dic
 
 
@@ -97,6 +118,14 @@ class _DiagKdnGainFunction(torch.autograd.Function):
 
 def _diag_kdn_gain(k_gain, alpha, omega, r, initial_precision, omega_raw, r_raw):
     """Fixed-scale FP32 diagonal gain with fused raw-logit VJPs (diag_kdn_chunk.py:2737-2791)."""
+    _validate_diag_kdn_gain_inputs(k_gain, alpha, omega, r, initial_precision, omega_raw, r_raw)
+    return _DiagKdnGainFunction.apply(
+        k_gain, alpha, omega.detach(), r.detach(), initial_precision, omega_raw, r_raw
+    )
+
+
+def _validate_diag_kdn_gain_inputs(k_gain, alpha, omega, r, initial_precision, omega_raw, r_raw):
+    """The reference's checks and messages (diag_kdn_chunk.py:2747-2791); returns (B, T, H, K)."""
     tensors = {
         "k_gain": k_gain,
         "alpha": alpha,
@@ -133,9 +162,7 @@ def _diag_kdn_gain(k_gain, alpha, omega, r, initial_precision, omega_raw, r_raw)
             raise TypeError(f"{name} must be torch.float32")
     if omega_raw.dtype != _VECTOR_DTYPE or r_raw.dtype != _VECTOR_DTYPE:
         raise TypeError("omega_raw and r_raw must be torch.bfloat16")
-    return _DiagKdnGainFunction.apply(
-        k_gain, alpha, omega.detach(), r.detach(), initial_precision, omega_raw, r_raw
-    )
+    return B, T, H, K
 
 
 def _validate_diag_kdn_memory_inputs(q, k, kappa, v, g_cumsum, scale):

@@ -217,6 +217,13 @@ def _chunk_kda_precumsum_paired(
     bf16 q/k/v (other floating dtypes are rounded to bf16) with
     K = V = 128.
     """
+    scale = _validate_chunk_kda_inputs(q, k, v, g_cumsum, beta, scale)
+    return _ChunkKDAPrecumsumFunction.apply(q, k, v, g_cumsum, beta, scale)
+
+
+def _validate_chunk_kda_inputs(q, k, v, g_cumsum, beta, scale):
+    """The reference's checks and messages (iso_kdn_chunk.py:2257-2285) plus
+    the kernels' K = V = 128; returns the scale (K^-0.5 when None)."""
     if q.ndim != 4 or q.shape != k.shape:
         raise ValueError(f"q and k must share [B,T,H,K], got {tuple(q.shape)} and {tuple(k.shape)}")
     B, T, H, K = q.shape
@@ -245,7 +252,7 @@ def _chunk_kda_precumsum_paired(
         raise ValueError(f"kdn_b200 kernels support K = V = 128, got K={K}, V={v.shape[-1]}")
     if scale is None:
         scale = K ** -0.5
-    return _ChunkKDAPrecumsumFunction.apply(q, k, v, g_cumsum, beta, scale)
+    return scale
 
 
 # ----------------------------------------------------------------------------- gate frontend

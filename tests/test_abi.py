@@ -41,7 +41,7 @@ def test_library_exports_every_declared_symbol(lib):
 
 
 def test_version(lib):
-    assert lib.kdn_version() == 101
+    assert lib.kdn_version() == 102
 
 
 def test_scan_size_queries(lib):

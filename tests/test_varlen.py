@@ -1,14 +1,22 @@
 """Packed variable-length batches (config 4's varlen variant).
 
-The varlen operators must give, sequence by sequence, what the fixed-length
-operators give for that sequence alone (which the parity tests pin to the
-oracle): the memory state, covariance and chunk-local gate prefix all restart
-at each ``cu_seqlens`` boundary.  The packed call runs each sequence as a row
-of a padded batch, which rounds a sequence's last partial chunk like a full
-chunk, so the comparison uses the bf16 parity tolerance (normalised max-abs
-error and relative Frobenius error <= 2e-2); the fp32 gain outputs agree to
-1e-5.
+The memory scans and the diagonal gain run natively over the packed batch
+(a chunk table from ``kdn_varlen_plan``): every sequence owns its 64-token
+chunks, so each sequence gets the arithmetic of a separate fixed-length call
+of that sequence alone, which the parity tests pin to the oracle.  The
+comparison bar is therefore tight: normalised max-abs error 1e-5 for fp32
+outputs, and one bf16 unit in the last place per element for bf16 outputs
+(the chunk-parallel backward sums some partial products with shared-memory
+atomics, whose order varies from run to run, so even two identical calls
+can round an element differently; the per-head prior's gradient sums the
+sequences in another order than a sum of separate calls).  The isotropic
+gain runs the padded length buckets, whose segment maps compose in another
+order than a call of the sequence alone: 1e-4 for the fp32 outputs there.
+The packed call is also checked against the float64 oracle directly at the
+bf16 bars.
 """
+import ctypes
+
 import pytest
 import torch
 
@@ -18,7 +26,7 @@ from kdn_b200.diag_kdn_chunk import _diag_kdn_gain, chunk_kalman
 from kdn_b200.iso_kdn_chunk import _chunk_kda_precumsum_paired, iso_kdn_gain
 
 DEV = "cuda"
-TOL = 2e-2
+TOL = 1e-5
 
 
 def nmax(x, ref):
@@ -26,17 +34,24 @@ def nmax(x, ref):
     return ((x - ref).abs().max() / ref.abs().max().clamp_min(1e-30)).item()
 
 
-def frob(x, ref):
+def agree(x, ref, tol=TOL):
+    """fp32: normalised max-abs error below tol; bf16: every element within
+    one bf16 ulp of the other call's (plus tol of the largest magnitude)."""
+    if x.dtype != torch.bfloat16:
+        return nmax(x, ref) < tol
     x, ref = x.detach().double().cpu(), ref.detach().double().cpu()
-    return ((x - ref).norm() / ref.norm().clamp_min(1e-30)).item()
-
-
-def close(x, ref, tol=TOL):
-    return nmax(x, ref) < tol and frob(x, ref) < tol
+    return bool(((x - ref).abs() <= ref.abs() * 2.0 ** -7 + tol * ref.abs().max()).all())
 
 
 def pack(ds, names):
     return {n: torch.cat([d[n] for d in ds], dim=1) for n in names}
+
+
+def offsets_of(lens):
+    cu = [0]
+    for n in lens:
+        cu.append(cu[-1] + n)
+    return cu
 
 
 def test_offsets_validation():
@@ -47,11 +62,43 @@ def test_offsets_validation():
             varlen.offsets(bad)
 
 
+def test_plan_table():
+    """kdn_varlen_plan (host code of the library, no GPU): chunk offsets, the
+    longest-first order and each chunk's sequence."""
+    lens = [70, 5, 128, 64, 1]
+    p = varlen.plan(offsets_of(lens), "cpu")
+    n, nc = len(lens), sum(-(-x // 64) for x in lens)
+    assert (p.num_seqs, p.num_chunks) == (n, nc)
+    t = p.table.tolist()
+    assert len(t) == 3 * n + 2 + nc
+    tok, chunk, order, seq = t[:n + 1], t[n + 1:2 * n + 2], t[2 * n + 2:3 * n + 2], t[3 * n + 2:]
+    assert tok == offsets_of(lens)
+    assert chunk == offsets_of([-(-x // 64) for x in lens])
+    assert order == [2, 0, 3, 1, 4]  # by decreasing length, ties in packed order
+    assert seq == [i for i, x in enumerate(lens) for _ in range(-(-x // 64))]
+    assert varlen.plan(offsets_of(lens), "cpu") is p  # cached
+
+
+def test_plan_validation():
+    from kdn_b200 import _native as N
+
+    lib = N.load_library()
+    nc = ctypes.c_int64(0)
+    for bad in ([1, 4], [0, 4, 4], [0, 5, 3]):
+        arr = (ctypes.c_int64 * len(bad))(*bad)
+        assert lib.kdn_varlen_plan(ctypes.cast(arr, ctypes.c_void_p), len(bad) - 1, None, 0, ctypes.byref(nc)) != 0
+    arr = (ctypes.c_int64 * 3)(0, 65, 70)
+    assert lib.kdn_varlen_plan(ctypes.cast(arr, ctypes.c_void_p), 2, None, 0, ctypes.byref(nc)) == 0
+    assert nc.value == 3
+    small = torch.empty(4, dtype=torch.int32)  # 3 * 2 + 2 + 3 = 11 entries needed
+    assert lib.kdn_varlen_plan(ctypes.cast(arr, ctypes.c_void_p), 2, small.data_ptr(), 4, ctypes.byref(nc)) != 0
+
+
 DIAG = ("q", "k", "v", "g_cumsum", "k_gain", "alpha", "omega", "r", "omega_raw", "r_raw", "dO")
 DIAG_GRADS = ("q", "k", "v", "g_cumsum", "k_gain", "alpha", "omega_raw", "r_raw", "initial_precision")
 
 
-def diag_step(x, cu=None, bucket=1024):
+def diag_step(x, cu=None):
     L = {n: x[n].to(DEV).clone().requires_grad_(n in DIAG_GRADS) for n in DIAG_GRADS + ("omega", "r")}
     scale = 128 ** -0.5
     if cu is None:
@@ -60,37 +107,39 @@ def diag_step(x, cu=None, bucket=1024):
         o = chunk_kalman(L["q"], L["k"], kappa, L["v"], L["g_cumsum"], scale)
     else:
         kappa = varlen.diag_kdn_gain_varlen(L["k_gain"], L["alpha"], L["omega"], L["r"], L["initial_precision"],
-                                            L["omega_raw"], L["r_raw"], cu, bucket=bucket)
-        o = varlen.chunk_kalman_varlen(L["q"], L["k"], kappa, L["v"], L["g_cumsum"], scale, cu, bucket=bucket)
+                                            L["omega_raw"], L["r_raw"], cu)
+        o = varlen.chunk_kalman_varlen(L["q"], L["k"], kappa, L["v"], L["g_cumsum"], scale, cu)
     o.backward(x["dO"].to(DEV))
     torch.cuda.synchronize()
     return o.detach(), {n: L[n].grad for n in DIAG_GRADS}
 
 
+# sequences ending inside a chunk, on a chunk boundary, inside the first
+# 32-token gate block, single tokens, and many short sequences in a row
+LENGTHS = {"mixed": [40, 96, 33, 7], "edges": [64, 1, 65, 63, 128, 32, 31], "many": [3, 17, 9, 70, 2, 5, 64, 11]}
+
+
 @pytest.mark.gpu
-@pytest.mark.parametrize("bucket", [64, 1024])  # 64: two length groups; 1024: one
-def test_diag_varlen_matches_per_sequence(bucket):
-    lens = [40, 96, 33, 7]
+@pytest.mark.parametrize("case", sorted(LENGTHS))
+def test_diag_varlen_matches_per_sequence(case):
+    lens = LENGTHS[case]
     ds = [oracle.make_diag_inputs(1, n, 2, seed=100 + i) for i, n in enumerate(lens)]
     x = pack(ds, DIAG)
     x["initial_precision"] = ds[0]["initial_precision"]
-    cu = [0]
-    for n in lens:
-        cu.append(cu[-1] + n)
-    o, grads = diag_step(x, torch.tensor(cu), bucket)
+    cu = offsets_of(lens)
+    o, grads = diag_step(x, torch.tensor(cu))
+    total = None
     for i, d in enumerate(ds):
         d = dict(d, initial_precision=x["initial_precision"])
         o_i, g_i = diag_step(d)
         sl = slice(cu[i], cu[i + 1])
-        assert close(o[:, sl], o_i), f"seq {i}: o"
+        assert agree(o[:, sl], o_i), f"seq {i}: o"
         for n in DIAG_GRADS:
-            if n == "initial_precision":
-                continue
-            assert close(grads[n][:, sl], g_i[n]), f"seq {i}: d{n}"
-    # the per-head prior collects every sequence's cotangent (through the
-    # bf16 scan's dkappa, hence the bf16 tolerance)
-    total = sum(diag_step(dict(d, initial_precision=x["initial_precision"]))[1]["initial_precision"] for d in ds)
-    assert close(grads["initial_precision"], total)
+            if n != "initial_precision":
+                assert agree(grads[n][:, sl], g_i[n]), f"seq {i}: d{n}"
+        total = g_i["initial_precision"] if total is None else total + g_i["initial_precision"]
+    # the per-head prior collects every sequence's cotangent
+    assert nmax(grads["initial_precision"], total) < TOL
 
 
 ISO = ("q", "k", "v", "g_cumsum", "a", "omega", "r", "dO")
@@ -106,30 +155,43 @@ def iso_step(x, prec, cu=None, bucket=1024):
     else:
         beta = varlen.iso_kdn_gain_varlen(L["a"], L["omega"], L["r"], p, head_dim=128, cu_seqlens=cu,
                                           out_dtype=torch.float32, bucket=bucket)
-        o = varlen.chunk_kda_precumsum_varlen(L["q"], L["k"], L["v"], L["g_cumsum"], beta, cu_seqlens=cu,
-                                              bucket=bucket)
+        o = varlen.chunk_kda_precumsum_varlen(L["q"], L["k"], L["v"], L["g_cumsum"], beta, cu_seqlens=cu)
     o.float().backward(x["dO"].to(DEV).float())
     torch.cuda.synchronize()
     return o.detach(), {n: L[n].grad for n in ISO_GRADS}
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("bucket", [64, 1024])
-def test_iso_varlen_matches_per_sequence(bucket):
-    lens = [70, 130, 64, 5]
+@pytest.mark.parametrize("case,bucket", [("mixed", 64), ("edges", 1024), ("many", 1024)])
+def test_iso_varlen_matches_per_sequence(case, bucket):
+    lens = LENGTHS[case]
     ds = [oracle.make_iso_inputs(1, n, 2, seed=200 + i, dtype=torch.bfloat16) for i, n in enumerate(lens)]
     x = pack(ds, ISO)
     prec = torch.ones(2)
-    cu = [0]
-    for n in lens:
-        cu.append(cu[-1] + n)
+    cu = offsets_of(lens)
     o, grads = iso_step(x, prec, cu, bucket)
     for i, d in enumerate(ds):
         o_i, g_i = iso_step(d, prec)
         sl = slice(cu[i], cu[i + 1])
-        assert close(o[:, sl], o_i), f"seq {i}: o"
+        assert agree(o[:, sl], o_i, 1e-4), f"seq {i}: o"
         for n in ISO_GRADS:
-            assert close(grads[n][:, sl], g_i[n]), f"seq {i}: d{n}"
+            assert agree(grads[n][:, sl], g_i[n], 1e-4), f"seq {i}: d{n}"
+
+
+@pytest.mark.gpu
+def test_varlen_validation():
+    lens = [40, 30]
+    d = oracle.make_diag_inputs(1, 70, 2, seed=7)
+    q, k, v = (d[n].to(DEV) for n in ("q", "k", "v"))
+    kappa, g = torch.rand(1, 70, 2, 128, device=DEV), d["g_cumsum"].to(DEV)
+    with pytest.raises(ValueError, match="cu_seqlens"):
+        varlen.chunk_kalman_varlen(q, k, kappa, v, g, 128 ** -0.5, [0, 40, 69])
+    with pytest.raises(ValueError):
+        varlen.chunk_kalman_varlen(q, k, kappa, v, g, 128 ** -0.5, [0, 40, 40, 70])
+    q2 = torch.cat([q, q])
+    with pytest.raises(ValueError, match="packed"):
+        varlen.chunk_kalman_varlen(q2, torch.cat([k, k]), torch.cat([kappa, kappa]), torch.cat([v, v]),
+                                   torch.cat([g, g]), 128 ** -0.5, offsets_of(lens))
 
 
 @pytest.mark.gpu
@@ -145,10 +207,8 @@ def test_diag_varlen_against_the_oracle():
         d["dO"] = d["dO"].bfloat16().float()  # chunk_kalman rounds its cotangent to bf16
     x = pack(ds, DIAG)
     x["initial_precision"] = ds[0]["initial_precision"]
-    cu = [0]
-    for n in lens:
-        cu.append(cu[-1] + n)
-    o, grads = diag_step(x, torch.tensor(cu), 64)
+    cu = offsets_of(lens)
+    o, grads = diag_step(x, torch.tensor(cu))
     for i, d in enumerate(ds):
         sl = slice(cu[i], cu[i + 1])
         L = {n: d[n].double().clone().requires_grad_(True) for n in ("q", "k", "v", "k_gain", "alpha", "omega_raw",
