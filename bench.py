@@ -17,6 +17,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import sys
@@ -239,6 +240,79 @@ def step_diag(x):
     o = chunk_kalman(L["q"], L["k"], kappa, L["v"], L["g_cumsum"], float(D ** -0.5))
     o.backward(x["dO"])
     return L
+
+
+# initial_precision_param with 0.1 + softplus(.) = 1, the unit prior of make_iso / make_diag
+UNIT_PRIOR_PARAM = math.log(math.expm1(0.9))
+
+
+def make_iso_mixer(device, seed):
+    """The isotropic mixer's own inputs to its kernels (lit_gpt/iso_kdn.py:
+    277-304): q, k, v and the raw gate logits g_raw (bf16), the raw noise
+    logits omega_r_raw (bf16 [B,T,2H]), the per-head parameters (fp32) and a
+    bf16 output cotangent.  Zero A_log, dt_bias and noise biases make the
+    frontend's outputs follow config 1's statistics: ln(alpha) =
+    -softplus(N(0,1)) per channel, omega = softplus(N(0,1)), r = 0.01 +
+    softplus(N(0,1)), unit prior."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    n = lambda *s: torch.randn(*s, generator=g, device=device)  # noqa: E731
+    z = lambda *s: torch.zeros(*s, device=device)  # noqa: E731
+    x = {"q": n(B, T, H, D).bfloat16(), "k": n(B, T, H, D).bfloat16(), "v": n(B, T, H, D).bfloat16(),
+         "g_raw": n(B, T, H, D).bfloat16(), "omega_r_raw": n(B, T, 2 * H).bfloat16(),
+         "omega_bias": z(H), "r_bias": z(H), "A_log": z(H), "dt_bias": z(H * D),
+         "initial_precision_param": torch.full((H,), UNIT_PRIOR_PARAM, device=device), "dO": n(B, T, H, D).bfloat16()}
+    return x
+
+
+def step_iso_mixer(x):
+    from kdn_b200.iso_kdn_chunk import _chunk_kda_precumsum_paired, _iso_kdn_gate_precumsum_paired, iso_kdn_gain
+
+    L = leafify(x, MIXER_GRAD_NAMES["iso"])
+    g_cumsum, a, omega, r, ip = _iso_kdn_gate_precumsum_paired(
+        L["g_raw"], L["omega_r_raw"], L["omega_bias"], L["r_bias"], L["A_log"], L["dt_bias"],
+        L["initial_precision_param"], 0.0, 0.01)
+    beta = iso_kdn_gain(a, omega, r, ip, head_dim=D, out_dtype=torch.float32)
+    o = _chunk_kda_precumsum_paired(q=L["q"], k=L["k"], v=L["v"], g_cumsum=g_cumsum, beta=beta)
+    o.backward(x["dO"])
+    return L
+
+
+def make_diag_mixer(device, seed):
+    """The diagonal mixer's own inputs to its kernels (lit_gpt/diag_kdn.py:
+    315-345): raw q, k, v (bf16), the raw retention, process- and
+    observation-noise logits (bf16), the per-head parameters (fp32) and a bf16
+    output cotangent (the mixer casts the fp32 scan output to v's dtype).
+    Zero A_log and dt_bias make the frontend's outputs follow config 2's
+    statistics: ln(alpha) = -softplus(N(0,1)) per channel, q and k
+    L2-normalised N(0,1), unit prior."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    n = lambda *s: torch.randn(*s, generator=g, device=device)  # noqa: E731
+    x = {"q": n(B, T, H, D).bfloat16(), "k": n(B, T, H, D).bfloat16(), "v": n(B, T, H, D).bfloat16(),
+         "retention_raw": n(B, T, H, D).bfloat16(), "omega_raw": n(B, T, H, D).bfloat16(),
+         "r_raw": n(B, T, H).bfloat16(), "A_log": torch.zeros(H, device=device),
+         "dt_bias": torch.zeros(H, D, device=device),
+         "initial_precision_param": torch.full((H,), UNIT_PRIOR_PARAM, device=device), "dO": n(B, T, H, D).bfloat16()}
+    return x
+
+
+def step_diag_mixer(x):
+    from kdn_b200.diag_kdn_chunk import (_diag_kdn_frontend_precumsum_paired, _diag_kdn_gain, _diag_kdn_normalize,
+                                         chunk_kalman)
+
+    L = leafify(x, MIXER_GRAD_NAMES["diag"])
+    q_mem, k_gain, k_mem = _diag_kdn_normalize(L["q"], L["k"])
+    g_cumsum, alpha, omega, r, ip = _diag_kdn_frontend_precumsum_paired(
+        L["retention_raw"], L["omega_raw"], L["r_raw"], L["A_log"], L["dt_bias"], L["initial_precision_param"])
+    kappa = _diag_kdn_gain(k_gain, alpha, omega, r, ip, L["omega_raw"], L["r_raw"])
+    o = chunk_kalman(q_mem, k_mem, kappa, L["v"], g_cumsum, float(D ** -0.5))
+    o.to(torch.bfloat16).backward(x["dO"])
+    return L
+
+
+MIXER_GRAD_NAMES = {"iso": ("q", "k", "v", "g_raw", "omega_r_raw", "omega_bias", "r_bias", "A_log", "dt_bias",
+                            "initial_precision_param"),
+                    "diag": ("q", "k", "v", "retention_raw", "omega_raw", "r_raw", "A_log", "dt_bias",
+                             "initial_precision_param")}
 
 
 GRAD_NAMES = {"iso": ("q", "k", "v", "g_cumsum", "a", "omega", "r"),
@@ -857,6 +931,71 @@ def measure_model(args, device, dist, world, rank, warmup, steps=5, name="iso_kd
 # ----------------------------------------------------------------------------- main
 
 
+def measure_e2e(step, x, names, args, device, dist, tokens):
+    """End-to-end time of ``step`` through the public operators with host
+    buffers: every step uploads its inputs ``x`` from pinned host memory and
+    downloads the gradients ``names``; uploads run on one copy stream and
+    downloads on another, so PCIe carries the next step's inputs and the
+    previous step's gradients at once while the compute stream runs the step.
+    Max over ranks."""
+    host = {n: (v.detach().cpu().pin_memory() if isinstance(v, torch.Tensor) else v) for n, v in x.items()}
+    grads_host = {n: torch.empty(x[n].shape, dtype=x[n].dtype).pin_memory() for n in names}
+    h2d = sum(v.numel() * v.element_size() for v in host.values() if isinstance(v, torch.Tensor))
+    d2h = sum(v.numel() * v.element_size() for v in grads_host.values())
+    cin, cout = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    tens = [n for n, v in host.items() if isinstance(v, torch.Tensor)]
+    bufs = [{n: torch.empty(host[n].shape, dtype=host[n].dtype, device=device) for n in tens} for _ in range(2)]
+
+    def e2e_run(steps):
+        main = torch.cuda.current_stream(device)
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev_in = [torch.cuda.Event(), torch.cuda.Event()]
+        ev_done = [None, None]
+        torch.cuda.synchronize(device)
+        start.record(main)
+
+        def upload(i):
+            with torch.cuda.stream(cin):
+                cin.wait_event(start)
+                if ev_done[i % 2] is not None:  # step i - 2 is done with this buffer
+                    cin.wait_event(ev_done[i % 2])
+                for n in tens:
+                    bufs[i % 2][n].copy_(host[n], non_blocking=True)
+                ev_in[i % 2].record(cin)
+
+        upload(0)
+        for i in range(steps):
+            if i + 1 < steps:
+                upload(i + 1)
+            main.wait_event(ev_in[i % 2])
+            xd = dict(host)
+            xd.update(bufs[i % 2])
+            L = step(xd)
+            ev_done[i % 2] = torch.cuda.Event()
+            ev_done[i % 2].record(main)
+            with torch.cuda.stream(cout):
+                cout.wait_event(ev_done[i % 2])
+                for n in names:
+                    g = L[n].grad
+                    g.record_stream(cout)
+                    grads_host[n].copy_(g, non_blocking=True)
+        main.wait_stream(cout)
+        stop.record(main)
+        torch.cuda.synchronize(device)
+        return start.elapsed_time(stop) / steps
+
+    e2e_run(2)
+    if dist is not None:
+        dist.barrier()
+    e2e_ms = e2e_run(max(2, min(args.steps, 5)))
+    if dist is not None:
+        t = torch.tensor([e2e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = t.item()
+    return {"value": tokens / (e2e_ms * 1e-3) / 1e6, "unit": "Mtok/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms}
+
+
 def measure(variant, args, device, dist, world, rank, warmup, varlen=False):
     """Time one step of ``variant`` (device-resident inputs, CUDA graph
     replay, max over ranks), then its end-to-end step with host buffers, the
@@ -914,71 +1053,24 @@ def measure(variant, args, device, dist, world, rank, warmup, varlen=False):
     hbm, tc, peak_kind = load_peaks()
     th = B * T * H
 
-    # end to end through the public operators with host buffers
+    # end to end through the public operators with host buffers: the mixer's
+    # own inputs (raw q, k, v and gate / noise logits) through the frontends,
+    # the gain and the scan, and, for reference, the scan's boundary inputs
     e2e = None
-    if not args.no_e2e:
-        names = GRAD_NAMES[variant]
-        host = {n: (v.detach().cpu().pin_memory() if isinstance(v, torch.Tensor) else v) for n, v in x.items()}
-        grads_host = {n: torch.empty(x[n].shape, dtype=x[n].dtype).pin_memory() for n in names}
-        h2d = sum(v.numel() * v.element_size() for v in host.values() if isinstance(v, torch.Tensor))
-        d2h = sum(v.numel() * v.element_size() for v in grads_host.values())
-
-        # every step uploads its inputs from pinned host memory and downloads
-        # its gradients; uploads run on one copy stream and downloads on
-        # another, so PCIe carries the next step's inputs and the previous
-        # step's gradients at once while the compute stream runs the step
-        cin, cout = torch.cuda.Stream(device), torch.cuda.Stream(device)
-        tens = [n for n, v in host.items() if isinstance(v, torch.Tensor)]
-        bufs = [{n: torch.empty(host[n].shape, dtype=host[n].dtype, device=device) for n in tens} for _ in range(2)]
-
-        def e2e_run(steps):
-            main = torch.cuda.current_stream(device)
-            start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            ev_in = [torch.cuda.Event(), torch.cuda.Event()]
-            ev_done = [None, None]
-            torch.cuda.synchronize(device)
-            start.record(main)
-
-            def upload(i):
-                with torch.cuda.stream(cin):
-                    cin.wait_event(start)
-                    if ev_done[i % 2] is not None:  # step i - 2 is done with this buffer
-                        cin.wait_event(ev_done[i % 2])
-                    for n in tens:
-                        bufs[i % 2][n].copy_(host[n], non_blocking=True)
-                    ev_in[i % 2].record(cin)
-
-            upload(0)
-            for i in range(steps):
-                if i + 1 < steps:
-                    upload(i + 1)
-                main.wait_event(ev_in[i % 2])
-                xd = dict(host)
-                xd.update(bufs[i % 2])
-                L = step(xd)
-                ev_done[i % 2] = torch.cuda.Event()
-                ev_done[i % 2].record(main)
-                with torch.cuda.stream(cout):
-                    cout.wait_event(ev_done[i % 2])
-                    for n in names:
-                        g = L[n].grad
-                        g.record_stream(cout)
-                        grads_host[n].copy_(g, non_blocking=True)
-            main.wait_stream(cout)
-            stop.record(main)
-            torch.cuda.synchronize(device)
-            return start.elapsed_time(stop) / steps
-
-        e2e_run(2)
-        barrier()
-        e2e_ms = e2e_run(max(2, min(args.steps, 5)))
-        if dist is not None:
-            t = torch.tensor([e2e_ms], device=device)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            e2e_ms = t.item()
-        e2e = {"value": tokens / (e2e_ms * 1e-3) / 1e6, "unit": "Mtok/s", "h2d_bytes_per_step": h2d,
-               "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms}
-        del bufs, host, grads_host
+    if not args.no_e2e and not varlen:
+        del x
+        xm = (make_iso_mixer if variant == "iso" else make_diag_mixer)(device, seed=4321 + rank)
+        e2e = measure_e2e(step_iso_mixer if variant == "iso" else step_diag_mixer, xm, MIXER_GRAD_NAMES[variant],
+                          args, device, dist, tokens)
+        e2e["path"] = ("public operators from the mixer's raw inputs: " +
+                       ("_iso_kdn_gate_precumsum_paired -> iso_kdn_gain -> _chunk_kda_precumsum_paired"
+                        if variant == "iso" else
+                        "_diag_kdn_normalize, _diag_kdn_frontend_precumsum_paired -> _diag_kdn_gain -> chunk_kalman"))
+        del xm
+        x = (make_iso if variant == "iso" else make_diag)(device, seed=1234 + rank)
+        scan = measure_e2e(step, x, GRAD_NAMES[variant], args, device, dist, tokens)
+        scan["path"] = "public gain + scan operators from the scan's boundary inputs (g_cumsum, gain inputs in fp32)"
+        e2e["scan_inputs"] = scan
 
     per_th = ISO_BYTES_PER_TH if variant == "iso" else DIAG_BYTES_PER_TH
     step_bytes = sum(per_th.values()) * th
