@@ -668,9 +668,48 @@ def cpu_baseline(variant, seconds_budget=20.0):
         Tc *= 2
     token_heads_per_s = (Tc * 2) / dt
     mtok = token_heads_per_s / H / 1e6
-    return {"value": mtok, "unit": "Mtok/s", "cores": threads, "kind": "port",
-            "sample": f"{variant} oracle fwd+bwd (fp32, autograd) on B=1,H=2,T={Tc}: {dt:.2f} s; "
-                      f"scaled to H=18 by (b,h) independence"}
+    out = {"value": mtok, "unit": "Mtok/s", "cores": threads, "kind": "port",
+           "sample": f"{variant} oracle fwd+bwd (fp32, autograd) on B=1,H=2,T={Tc}: {dt:.2f} s; "
+                     f"scaled to H=18 by (b,h) independence"}
+    try:
+        out["reference_naive"] = reference_naive_cpu(variant, seconds_budget)
+    except Exception as e:  # the reference's install is optional on a box
+        out["reference_naive"] = {"unavailable": f"{type(e).__name__}: {str(e).splitlines()[0][:200]}"}
+    return out
+
+
+def reference_naive_cpu(variant, seconds_budget=20.0):
+    """The reference's own chunked PyTorch oracle of the path
+    (``_naive_chunk_iso_kdn``, lit_gpt/kdn_ops/iso_kdn_naive.py:536;
+    ``_naive_chunk_diag_kdn``, diag_kdn_naive.py:658: gain and memory scans),
+    loaded by path from the unmodified install under ``baseline/_ref``, forward
+    plus autograd backward in fp32 on the host cores, on the same kind of
+    B=1, H=2 slice as the port; tokens/s scaled to 18 heads."""
+    mod = _load_reference_module("iso_kdn_naive" if variant == "iso" else "diag_kdn_naive")
+    fn = mod._naive_chunk_iso_kdn if variant == "iso" else mod._naive_chunk_diag_kdn
+    threads = torch.get_num_threads()
+    g = torch.Generator().manual_seed(0)
+    sp = torch.nn.functional.softplus
+    nrm = lambda t: t * torch.rsqrt((t * t).sum(-1, keepdim=True) + 1e-6)  # noqa: E731
+    Tc = 128
+    while True:
+        n = lambda *s: torch.randn(*s, generator=g)  # noqa: E731
+        x = {"q": nrm(n(1, Tc, 2, D)), "k": nrm(n(1, Tc, 2, D)), "v": n(1, Tc, 2, D),
+             "alpha": torch.exp(-sp(n(1, Tc, 2, D))),
+             "omega": sp(n(1, Tc, 2) if variant == "iso" else n(1, Tc, 2, D)), "r": 0.01 + sp(n(1, Tc, 2))}
+        leaves = {k_: v_.requires_grad_(True) for k_, v_ in x.items()}
+        dO = n(1, Tc, 2, D)
+        t0 = time.perf_counter()
+        o, _ = fn(leaves["q"], leaves["k"], leaves["v"], leaves["alpha"], leaves["omega"], leaves["r"],
+                  chunk_size=64 if variant == "iso" else 32)
+        o.backward(dO)
+        dt = time.perf_counter() - t0
+        if dt > 2.0 or Tc >= T or dt * 2 > seconds_budget:
+            break
+        Tc *= 2
+    return {"value": Tc * 2 / dt / H / 1e6, "unit": "Mtok/s", "cores": threads, "kind": "reference",
+            "sample": f"{variant} reference _naive_chunk_{variant}_kdn fwd + autograd bwd (fp32) on B=1,H=2,T={Tc}: "
+                      f"{dt:.2f} s; scaled to H=18 by (b,h) independence"}
 
 
 # ----------------------------------------------------------------------------- Triton reference point
