@@ -273,6 +273,8 @@ def step_iso_mixer(x):
         L["initial_precision_param"], 0.0, 0.01)
     beta = iso_kdn_gain(a, omega, r, ip, head_dim=D, out_dtype=torch.float32)
     o = _chunk_kda_precumsum_paired(q=L["q"], k=L["k"], v=L["v"], g_cumsum=g_cumsum, beta=beta)
+    # the step's loss <o, dO>, whose gradient with respect to o is dO
+    L[LOSS] = torch.dot(o.detach().float().flatten(), x["dO"].float().flatten())
     o.backward(x["dO"])
     return L
 
@@ -304,9 +306,13 @@ def step_diag_mixer(x):
     g_cumsum, alpha, omega, r, ip = _diag_kdn_frontend_precumsum_paired(
         L["retention_raw"], L["omega_raw"], L["r_raw"], L["A_log"], L["dt_bias"], L["initial_precision_param"])
     kappa = _diag_kdn_gain(k_gain, alpha, omega, r, ip, L["omega_raw"], L["r_raw"])
-    o = chunk_kalman(q_mem, k_mem, kappa, L["v"], g_cumsum, float(D ** -0.5))
-    o.to(torch.bfloat16).backward(x["dO"])
+    o = chunk_kalman(q_mem, k_mem, kappa, L["v"], g_cumsum, float(D ** -0.5)).to(torch.bfloat16)
+    L[LOSS] = torch.dot(o.detach().float().flatten(), x["dO"].float().flatten())
+    o.backward(x["dO"])
     return L
+
+
+LOSS = "__loss__"  # the step result a mixer-level step leaves in its dict
 
 
 MIXER_GRAD_NAMES = {"iso": ("q", "k", "v", "g_raw", "omega_r_raw", "omega_bias", "r_bias", "A_log", "dt_bias",
@@ -970,15 +976,21 @@ def measure_model(args, device, dist, world, rank, warmup, steps=5, name="iso_kd
 # ----------------------------------------------------------------------------- main
 
 
-def measure_e2e(step, x, names, args, device, dist, tokens):
+def measure_e2e(step, x, names, args, device, dist, tokens, result="grads"):
     """End-to-end time of ``step`` through the public operators with host
     buffers: every step uploads its inputs ``x`` from pinned host memory and
-    downloads the gradients ``names``; uploads run on one copy stream and
-    downloads on another, so PCIe carries the next step's inputs and the
-    previous step's gradients at once while the compute stream runs the step.
-    Max over ranks."""
+    reads back its result: the gradients ``names`` (``result="grads"``) or
+    the step's loss (``"loss"``: the gradients stay on the device, where a
+    training step leaves them for its optimizer).  Uploads run on one copy
+    stream and downloads on another, so the host link carries the next step's
+    inputs and the previous step's results at once while the compute stream
+    runs the step.  Max over ranks."""
     host = {n: (v.detach().cpu().pin_memory() if isinstance(v, torch.Tensor) else v) for n, v in x.items()}
-    grads_host = {n: torch.empty(x[n].shape, dtype=x[n].dtype).pin_memory() for n in names}
+    if result == "loss":
+        names = (LOSS,)
+        grads_host = {LOSS: torch.empty((), dtype=torch.float32).pin_memory()}
+    else:
+        grads_host = {n: torch.empty(x[n].shape, dtype=x[n].dtype).pin_memory() for n in names}
     h2d = sum(v.numel() * v.element_size() for v in host.values() if isinstance(v, torch.Tensor))
     d2h = sum(v.numel() * v.element_size() for v in grads_host.values())
     cin, cout = torch.cuda.Stream(device), torch.cuda.Stream(device)
@@ -1015,7 +1027,7 @@ def measure_e2e(step, x, names, args, device, dist, tokens):
             with torch.cuda.stream(cout):
                 cout.wait_event(ev_done[i % 2])
                 for n in names:
-                    g = L[n].grad
+                    g = L[n] if n == LOSS else L[n].grad
                     g.record_stream(cout)
                     grads_host[n].copy_(g, non_blocking=True)
         main.wait_stream(cout)
@@ -1099,12 +1111,16 @@ def measure(variant, args, device, dist, world, rank, warmup, varlen=False):
     if not args.no_e2e and not varlen:
         del x
         xm = (make_iso_mixer if variant == "iso" else make_diag_mixer)(device, seed=4321 + rank)
-        e2e = measure_e2e(step_iso_mixer if variant == "iso" else step_diag_mixer, xm, MIXER_GRAD_NAMES[variant],
-                          args, device, dist, tokens)
-        e2e["path"] = ("public operators from the mixer's raw inputs: " +
-                       ("_iso_kdn_gate_precumsum_paired -> iso_kdn_gain -> _chunk_kda_precumsum_paired"
-                        if variant == "iso" else
-                        "_diag_kdn_normalize, _diag_kdn_frontend_precumsum_paired -> _diag_kdn_gain -> chunk_kalman"))
+        mstep = step_iso_mixer if variant == "iso" else step_diag_mixer
+        path = ("public operators from the mixer's raw inputs: " +
+                ("_iso_kdn_gate_precumsum_paired -> iso_kdn_gain -> _chunk_kda_precumsum_paired"
+                 if variant == "iso" else
+                 "_diag_kdn_normalize, _diag_kdn_frontend_precumsum_paired -> _diag_kdn_gain -> chunk_kalman"))
+        e2e = measure_e2e(mstep, xm, MIXER_GRAD_NAMES[variant], args, device, dist, tokens, result="loss")
+        e2e["path"] = path + "; result read back: the loss <o, dO> (gradients stay on the device)"
+        grads = measure_e2e(mstep, xm, MIXER_GRAD_NAMES[variant], args, device, dist, tokens)
+        grads["path"] = path + "; result read back: every input gradient"
+        e2e["gradients_read_back"] = grads
         del xm
         x = (make_iso if variant == "iso" else make_diag)(device, seed=1234 + rank)
         scan = measure_e2e(step, x, GRAD_NAMES[variant], args, device, dist, tokens)
