@@ -177,6 +177,30 @@ int kdn_iso_gain_bwd(const float* a, const float* omega, const float* r,
                      int64_t B, int64_t T, int64_t H, float posterior_scale,
                      void* workspace, size_t workspace_bytes,
                      kdn_stream_t stream);
+/* The isotropic gain over a packed batch (kdn_varlen_plan): rows [1,T,H];
+ * sequence i runs its own covariance stream from 1/initial_precision (or its
+ * initial_cov row); initial_cov, p_final, d_final_cov, d_initial_cov are per
+ * sequence, fp32 [N,H]; max_seq_len is the longest sequence (it sizes the
+ * launch and kdn_iso_gain_varlen_workspace_bytes).  Same results per
+ * sequence as separate calls. */
+size_t kdn_iso_gain_varlen_workspace_bytes(int64_t num_seqs, int64_t max_seq_len,
+                                           int64_t H);
+int kdn_iso_gain_fwd_varlen(const float* a, const float* omega, const float* r,
+                            const float* initial_precision,
+                            const float* initial_cov, float* gain, float* p_prev,
+                            float* p_final, int64_t T, int64_t H,
+                            float posterior_scale, const int32_t* varlen_table,
+                            int64_t num_seqs, int64_t max_seq_len, void* workspace,
+                            size_t workspace_bytes, kdn_stream_t stream);
+int kdn_iso_gain_bwd_varlen(const float* a, const float* omega, const float* r,
+                            const float* initial_precision,
+                            const float* initial_cov, const float* dgain,
+                            const float* p_prev, const float* d_final_cov, float* da,
+                            float* domega, float* dr, float* d_initial_precision,
+                            float* d_initial_cov, int64_t T, int64_t H,
+                            float posterior_scale, const int32_t* varlen_table,
+                            int64_t num_seqs, int64_t max_seq_len, void* workspace,
+                            size_t workspace_bytes, kdn_stream_t stream);
 
 /* ------------------------------------------------------------------------ *
  * Diagonal gain scan.  Replaces _diag_kdn_gain (diag_kdn_chunk.py:2737) ->

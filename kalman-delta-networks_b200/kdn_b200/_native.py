@@ -84,6 +84,9 @@ _SIGNATURES = {
         [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _F, _P, _SZ, _P],
         ctypes.c_int,
     ),
+    "kdn_iso_gain_varlen_workspace_bytes": ([_I64, _I64, _I64], _SZ),
+    "kdn_iso_gain_fwd_varlen": ([_P] * 8 + [_I64, _I64, _F, _P, _I64, _I64, _P, _SZ, _P], ctypes.c_int),
+    "kdn_iso_gain_bwd_varlen": ([_P] * 13 + [_I64, _I64, _F, _P, _I64, _I64, _P, _SZ, _P], ctypes.c_int),
     "kdn_iso_gate_workspace_bytes": ([_I64, _I64, _I64, _I64], _SZ),
     "kdn_iso_gate_fwd": (
         [_P, ctypes.c_int, _P, ctypes.c_int, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,

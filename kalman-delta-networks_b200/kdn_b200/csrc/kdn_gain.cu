@@ -82,9 +82,12 @@ __host__ __device__ inline IsoWs iso_ws(void* ws, int B, int nblk, int H) {
 
 __global__ void __launch_bounds__(32 * kIsoWarps) iso_gain_fwd_maps_kernel(
     const float* __restrict__ a, const float* __restrict__ omega, const float* __restrict__ r, IsoWs ws, int T,
-    int H, float s) {
+    int H, float s, const int* __restrict__ tok) {
   __shared__ Mob sm[kIsoWarps][32];
   const int blk = blockIdx.x, b = blockIdx.y, nblk = gridDim.x;
+  // stream b: tokens [base, base + Tb) of the rows (a packed batch's sequence b)
+  const int Tb = tok ? tok[b + 1] - tok[b] : T;
+  const size_t base = tok ? (size_t)tok[b] : (size_t)b * T;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = 32 * blockIdx.z + lane;
   const int ts = blk * kIsoBlockTok + warp * kIsoSeg;
@@ -93,15 +96,15 @@ __global__ void __launch_bounds__(32 * kIsoWarps) iso_gain_fwd_maps_kernel(
     float av[kIsoSeg], wv[kIsoSeg], rv[kIsoSeg];
 #pragma unroll
     for (int j = 0; j < kIsoSeg; ++j) {
-      const bool in = ts + j < T;
-      const size_t off = ((size_t)b * T + ts + j) * H + h;
+      const bool in = ts + j < Tb;
+      const size_t off = (base + ts + j) * H + h;
       av[j] = in ? a[off] : 0.f;
       wv[j] = in ? omega[off] : 0.f;
       rv[j] = in ? r[off] : 1.f;
     }
 #pragma unroll
     for (int j = 0; j < kIsoSeg; ++j)
-      if (ts + j < T) m = mob_mul(iso_tok_map(av[j], wv[j], rv[j], s), m);
+      if (ts + j < Tb) m = mob_mul(iso_tok_map(av[j], wv[j], rv[j], s), m);
   }
   sm[warp][lane] = m;
   const size_t row = (size_t)b * nblk + blk;
@@ -119,9 +122,12 @@ __global__ void __launch_bounds__(32 * kIsoWarps) iso_gain_fwd_maps_kernel(
 __global__ void __launch_bounds__(32 * kIsoWarps) iso_gain_fwd_apply_kernel(
     const float* __restrict__ a, const float* __restrict__ omega, const float* __restrict__ r,
     const float* __restrict__ init_prec, const float* __restrict__ init_cov, IsoWs ws, float* __restrict__ gain,
-    float* __restrict__ p_prev, float* __restrict__ p_final, int T, int H, float s) {
+    float* __restrict__ p_prev, float* __restrict__ p_final, int T, int H, float s, const int* __restrict__ tok) {
   __shared__ Mob part[kIsoWarps][32];
   const int blk = blockIdx.x, b = blockIdx.y, nblk = gridDim.x;
+  // stream b: tokens [base, base + Tb) of the rows (a packed batch's sequence b)
+  const int Tb = tok ? tok[b + 1] - tok[b] : T;
+  const size_t base = tok ? (size_t)tok[b] : (size_t)b * T;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = 32 * blockIdx.z + lane;
   const bool on = h < H;
@@ -130,8 +136,8 @@ __global__ void __launch_bounds__(32 * kIsoWarps) iso_gain_fwd_apply_kernel(
   float av[kIsoSeg], wv[kIsoSeg], rv[kIsoSeg];
 #pragma unroll
   for (int j = 0; j < kIsoSeg; ++j) {
-    const bool in = on && ts + j < T;
-    const size_t off = ((size_t)b * T + ts + j) * H + h;
+    const bool in = on && ts + j < Tb;
+    const size_t off = (base + ts + j) * H + h;
     av[j] = in ? a[off] : 0.f;
     wv[j] = in ? omega[off] : 0.f;
     rv[j] = in ? r[off] : 1.f;
@@ -145,7 +151,7 @@ __global__ void __launch_bounds__(32 * kIsoWarps) iso_gain_fwd_apply_kernel(
   part[warp][lane] = c;
   __syncthreads();
   const bool first = blk == 0 && warp == 0;
-  if (!on || (ts >= T && !first)) return;
+  if (!on || (ts >= Tb && !first)) return;
   Mob pre{1.f, 0.f, 0.f, 1.f};
 #pragma unroll
   for (int w = 0; w < kIsoWarps; ++w) pre = mob_mul(part[w][lane], pre);
@@ -155,8 +161,8 @@ __global__ void __launch_bounds__(32 * kIsoWarps) iso_gain_fwd_apply_kernel(
   float p = mob_apply(pre, p0);
 #pragma unroll
   for (int j = 0; j < kIsoSeg; ++j) {
-    if (ts + j < T) {
-      const size_t off = ((size_t)b * T + ts + j) * H + h;
+    if (ts + j < Tb) {
+      const size_t off = (base + ts + j) * H + h;
       if (p_prev) p_prev[off] = p;
       const float z = av[j] * p + wv[j];
       const float beta = z / (rv[j] + z);
@@ -164,14 +170,18 @@ __global__ void __launch_bounds__(32 * kIsoWarps) iso_gain_fwd_apply_kernel(
       p = (s == 1.f) ? rv[j] * beta : rv[j] * z / (rv[j] + s * z);
     }
   }
-  if (p_final && (T == 0 || (ts <= T - 1 && T - 1 < ts + kIsoSeg))) p_final[(size_t)b * H + h] = p;
+  if (p_final && (Tb == 0 || (ts <= Tb - 1 && Tb - 1 < ts + kIsoSeg))) p_final[(size_t)b * H + h] = p;
 }
 
 __global__ void __launch_bounds__(32 * kIsoWarps) iso_gain_bwd_maps_kernel(
     const float* __restrict__ a, const float* __restrict__ omega, const float* __restrict__ r,
-    const float* __restrict__ dgain, const float* __restrict__ p_prev, IsoWs ws, int T, int H, float s) {
+    const float* __restrict__ dgain, const float* __restrict__ p_prev, IsoWs ws, int T, int H, float s,
+    const int* __restrict__ tok) {
   __shared__ Aff sm[kIsoWarps][32];
   const int blk = blockIdx.x, b = blockIdx.y, nblk = gridDim.x;
+  // stream b: tokens [base, base + Tb) of the rows (a packed batch's sequence b)
+  const int Tb = tok ? tok[b + 1] - tok[b] : T;
+  const size_t base = tok ? (size_t)tok[b] : (size_t)b * T;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = 32 * blockIdx.z + lane;
   const int ts = blk * kIsoBlockTok + warp * kIsoSeg;
@@ -182,8 +192,8 @@ __global__ void __launch_bounds__(32 * kIsoWarps) iso_gain_bwd_maps_kernel(
     float av[kIsoSeg], wv[kIsoSeg], rv[kIsoSeg], dv[kIsoSeg], pv[kIsoSeg];
 #pragma unroll
     for (int j = 0; j < kIsoSeg; ++j) {
-      const bool in = ts + j < T;
-      const size_t off = ((size_t)b * T + ts + j) * H + h;
+      const bool in = ts + j < Tb;
+      const size_t off = (base + ts + j) * H + h;
       av[j] = in ? a[off] : 0.f;
       wv[j] = in ? omega[off] : 0.f;
       rv[j] = in ? r[off] : 1.f;
@@ -192,7 +202,7 @@ __global__ void __launch_bounds__(32 * kIsoWarps) iso_gain_bwd_maps_kernel(
     }
 #pragma unroll
     for (int j = kIsoSeg - 1; j >= 0; --j)
-      if (ts + j < T) f = aff_after(iso_tok_adj(av[j], wv[j], rv[j], dv[j], pv[j], s), f);
+      if (ts + j < Tb) f = aff_after(iso_tok_adj(av[j], wv[j], rv[j], dv[j], pv[j], s), f);
   }
   sm[warp][lane] = f;
   const size_t row = (size_t)b * nblk + blk;
@@ -213,9 +223,12 @@ __global__ void __launch_bounds__(32 * kIsoWarps) iso_gain_bwd_apply_kernel(
     const float* __restrict__ init_prec, const float* __restrict__ dgain, const float* __restrict__ p_prev,
     const float* __restrict__ d_final_cov, const bool has_init_cov, float* __restrict__ d_init_cov, IsoWs ws,
     float* __restrict__ da, float* __restrict__ domega, float* __restrict__ dr, float* __restrict__ dinit, int T,
-    int H, float s) {
+    int H, float s, const int* __restrict__ tok) {
   __shared__ Aff part[kIsoWarps][32];
   const int blk = blockIdx.x, b = blockIdx.y, nblk = gridDim.x;
+  // stream b: tokens [base, base + Tb) of the rows (a packed batch's sequence b)
+  const int Tb = tok ? tok[b + 1] - tok[b] : T;
+  const size_t base = tok ? (size_t)tok[b] : (size_t)b * T;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = 32 * blockIdx.z + lane;
   const bool on = h < H;
@@ -223,8 +236,8 @@ __global__ void __launch_bounds__(32 * kIsoWarps) iso_gain_bwd_apply_kernel(
   float av[kIsoSeg], wv[kIsoSeg], rv[kIsoSeg], dv[kIsoSeg], pv[kIsoSeg];
 #pragma unroll
   for (int j = 0; j < kIsoSeg; ++j) {
-    const bool in = on && ts + j < T;
-    const size_t off = ((size_t)b * T + ts + j) * H + h;
+    const bool in = on && ts + j < Tb;
+    const size_t off = (base + ts + j) * H + h;
     av[j] = in ? a[off] : 0.f;
     wv[j] = in ? omega[off] : 0.f;
     rv[j] = in ? r[off] : 1.f;
@@ -243,11 +256,11 @@ __global__ void __launch_bounds__(32 * kIsoWarps) iso_gain_bwd_apply_kernel(
   part[warp][lane] = c;
   __syncthreads();
   const bool first = blk == 0 && warp == 0;
-  if (!on || (ts >= T && !first)) return;
+  if (!on || (ts >= Tb && !first)) return;
   Aff suf{1.f, 0.f};
 #pragma unroll
   for (int w = kIsoWarps - 1; w >= 0; --w) suf = aff_after(part[w][lane], suf);
-  if (T > 0) {
+  if (Tb > 0) {
     const size_t row = (size_t)b * nblk + blk;
     for (int w = kIsoWarps - 1; w > warp; --w) suf = aff_after(as_aff(ws.seg[(row * kIsoWarps + w) * H + h]), suf);
   }
@@ -255,8 +268,8 @@ __global__ void __launch_bounds__(32 * kIsoWarps) iso_gain_bwd_apply_kernel(
   float lam = suf.A * (d_final_cov ? d_final_cov[(size_t)b * H + h] : 0.f) + suf.B;
 #pragma unroll
   for (int j = kIsoSeg - 1; j >= 0; --j) {
-    if (ts + j < T) {
-      const size_t off = ((size_t)b * T + ts + j) * H + h;
+    if (ts + j < Tb) {
+      const size_t off = (base + ts + j) * H + h;
       const float at = av[j], wt = wv[j], rt = rv[j], dbt = dv[j], pp = pv[j];
       const float z = at * pp + wt;
       float zbar, drt;
@@ -689,22 +702,57 @@ extern "C" {
 
 size_t kdn_iso_gain_workspace_bytes(int64_t B, int64_t T, int64_t H) { return iso_ws_bytes(B, T, H); }
 
+}  // extern "C"
+
+namespace kdn {
+namespace {
+// Launches of the isotropic gain over B streams of the [.,T,H] rows: a
+// fixed-length batch (tok = null, stream b = rows b*T ..) or a packed batch
+// (tok = the sequences' token offsets, B = their count, Tgrid = the longest).
+int iso_fwd(const char* what, const float* a, const float* omega, const float* r, const float* init_prec,
+            const float* init_cov, float* gain, float* p_prev, float* p_final, int64_t B, int64_t T, int64_t Tgrid,
+            int64_t H, float s, const int* tok, void* workspace, size_t workspace_bytes, cudaStream_t st) {
+  dim3 grid;
+  if (int rc = iso_grid(what, B, Tgrid, H, workspace, workspace_bytes, &grid)) return rc;
+  const IsoWs ws = iso_ws(workspace, (int)B, (int)grid.x, (int)H);
+  if (Tgrid > 0) {
+    iso_gain_fwd_maps_kernel<<<grid, 32 * kIsoWarps, 0, st>>>(a, omega, r, ws, (int)T, (int)H, s, tok);
+    if (int rc = check_launch("iso_gain_fwd_maps_kernel")) return rc;
+  }
+  iso_gain_fwd_apply_kernel<<<grid, 32 * kIsoWarps, 0, st>>>(a, omega, r, init_prec, init_cov, ws, gain, p_prev,
+                                                            p_final, (int)T, (int)H, s, tok);
+  return check_launch("iso_gain_fwd_apply_kernel");
+}
+
+int iso_bwd(const char* what, const float* a, const float* omega, const float* r, const float* init_prec,
+            const float* init_cov, const float* dgain, const float* p_prev, const float* d_final_cov, float* da,
+            float* domega, float* dr, float* dinit, float* d_init_cov, int64_t B, int64_t T, int64_t Tgrid, int64_t H,
+            float s, const int* tok, void* workspace, size_t workspace_bytes, cudaStream_t st) {
+  dim3 grid;
+  if (int rc = iso_grid(what, B, Tgrid, H, workspace, workspace_bytes, &grid)) return rc;
+  const IsoWs ws = iso_ws(workspace, (int)B, (int)grid.x, (int)H);
+  if (cudaMemsetAsync(dinit, 0, sizeof(float) * H, st) != cudaSuccess) return check_launch("memset d_initial_precision");
+  if (Tgrid > 0) {
+    iso_gain_bwd_maps_kernel<<<grid, 32 * kIsoWarps, 0, st>>>(a, omega, r, dgain, p_prev, ws, (int)T, (int)H, s, tok);
+    if (int rc = check_launch("iso_gain_bwd_maps_kernel")) return rc;
+  }
+  iso_gain_bwd_apply_kernel<<<grid, 32 * kIsoWarps, 0, st>>>(a, omega, r, init_prec, dgain, p_prev, d_final_cov,
+                                                            init_cov != nullptr, d_init_cov, ws, da, domega, dr,
+                                                            dinit, (int)T, (int)H, s, tok);
+  return check_launch("iso_gain_bwd_apply_kernel");
+}
+}  // namespace
+}  // namespace kdn
+
+extern "C" {
+
 int kdn_iso_gain_fwd(const float* a, const float* omega, const float* r, const float* init_prec,
                      const float* init_cov, float* gain, float* p_prev, float* p_final, int64_t B, int64_t T,
                      int64_t H, float s, void* workspace, size_t workspace_bytes, kdn_stream_t stream) {
   if (B <= 0 || H <= 0 || T < 0 || !a || !omega || !r || !init_prec || !gain)
     return set_error(KDN_ERR_INVALID, "kdn_iso_gain_fwd: invalid arguments");
-  dim3 grid;
-  if (int rc = iso_grid("kdn_iso_gain_fwd", B, T, H, workspace, workspace_bytes, &grid)) return rc;
-  cudaStream_t st = (cudaStream_t)stream;
-  const IsoWs ws = iso_ws(workspace, (int)B, (int)grid.x, (int)H);
-  if (T > 0) {
-    iso_gain_fwd_maps_kernel<<<grid, 32 * kIsoWarps, 0, st>>>(a, omega, r, ws, (int)T, (int)H, s);
-    if (int rc = check_launch("iso_gain_fwd_maps_kernel")) return rc;
-  }
-  iso_gain_fwd_apply_kernel<<<grid, 32 * kIsoWarps, 0, st>>>(a, omega, r, init_prec, init_cov, ws, gain, p_prev,
-                                                            p_final, (int)T, (int)H, s);
-  return check_launch("iso_gain_fwd_apply_kernel");
+  return iso_fwd("kdn_iso_gain_fwd", a, omega, r, init_prec, init_cov, gain, p_prev, p_final, B, T, T, H, s, nullptr,
+                 workspace, workspace_bytes, (cudaStream_t)stream);
 }
 
 int kdn_iso_gain_bwd(const float* a, const float* omega, const float* r, const float* init_prec,
@@ -714,19 +762,36 @@ int kdn_iso_gain_bwd(const float* a, const float* omega, const float* r, const f
   if (B <= 0 || H <= 0 || T < 0 || !a || !omega || !r || !init_prec || !dgain || !da || !domega || !dr || !dinit ||
       (T > 0 && !p_prev))
     return set_error(KDN_ERR_INVALID, "kdn_iso_gain_bwd: invalid arguments");
-  dim3 grid;
-  if (int rc = iso_grid("kdn_iso_gain_bwd", B, T, H, workspace, workspace_bytes, &grid)) return rc;
-  cudaStream_t st = (cudaStream_t)stream;
-  const IsoWs ws = iso_ws(workspace, (int)B, (int)grid.x, (int)H);
-  if (cudaMemsetAsync(dinit, 0, sizeof(float) * H, st) != cudaSuccess) return check_launch("memset d_initial_precision");
-  if (T > 0) {
-    iso_gain_bwd_maps_kernel<<<grid, 32 * kIsoWarps, 0, st>>>(a, omega, r, dgain, p_prev, ws, (int)T, (int)H, s);
-    if (int rc = check_launch("iso_gain_bwd_maps_kernel")) return rc;
-  }
-  iso_gain_bwd_apply_kernel<<<grid, 32 * kIsoWarps, 0, st>>>(a, omega, r, init_prec, dgain, p_prev, d_final_cov,
-                                                            init_cov != nullptr, d_init_cov, ws, da, domega, dr,
-                                                            dinit, (int)T, (int)H, s);
-  return check_launch("iso_gain_bwd_apply_kernel");
+  return iso_bwd("kdn_iso_gain_bwd", a, omega, r, init_prec, init_cov, dgain, p_prev, d_final_cov, da, domega, dr,
+                 dinit, d_init_cov, B, T, T, H, s, nullptr, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+size_t kdn_iso_gain_varlen_workspace_bytes(int64_t num_seqs, int64_t max_seq_len, int64_t H) {
+  return iso_ws_bytes(num_seqs, max_seq_len, H);
+}
+
+int kdn_iso_gain_fwd_varlen(const float* a, const float* omega, const float* r, const float* init_prec,
+                            const float* init_cov, float* gain, float* p_prev, float* p_final, int64_t T, int64_t H,
+                            float s, const int32_t* varlen_table, int64_t num_seqs, int64_t max_seq_len,
+                            void* workspace, size_t workspace_bytes, kdn_stream_t stream) {
+  if (H <= 0 || T <= 0 || !a || !omega || !r || !init_prec || !gain || !varlen_table || num_seqs <= 0 ||
+      max_seq_len <= 0 || max_seq_len > T)
+    return set_error(KDN_ERR_INVALID, "kdn_iso_gain_fwd_varlen: invalid arguments");
+  return iso_fwd("kdn_iso_gain_fwd_varlen", a, omega, r, init_prec, init_cov, gain, p_prev, p_final, num_seqs, T,
+                 max_seq_len, H, s, varlen_table, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+int kdn_iso_gain_bwd_varlen(const float* a, const float* omega, const float* r, const float* init_prec,
+                            const float* init_cov, const float* dgain, const float* p_prev, const float* d_final_cov,
+                            float* da, float* domega, float* dr, float* dinit, float* d_init_cov, int64_t T, int64_t H,
+                            float s, const int32_t* varlen_table, int64_t num_seqs, int64_t max_seq_len,
+                            void* workspace, size_t workspace_bytes, kdn_stream_t stream) {
+  if (H <= 0 || T <= 0 || !a || !omega || !r || !init_prec || !dgain || !p_prev || !da || !domega || !dr ||
+      !dinit || !varlen_table || num_seqs <= 0 || max_seq_len <= 0 || max_seq_len > T)
+    return set_error(KDN_ERR_INVALID, "kdn_iso_gain_bwd_varlen: invalid arguments");
+  return iso_bwd("kdn_iso_gain_bwd_varlen", a, omega, r, init_prec, init_cov, dgain, p_prev, d_final_cov, da, domega,
+                 dr, dinit, d_init_cov, num_seqs, T, max_seq_len, H, s, varlen_table, workspace, workspace_bytes,
+                 (cudaStream_t)stream);
 }
 
 int64_t kdn_diag_gain_carry_elems(int64_t B, int64_t T, int64_t H, int64_t K) {

@@ -34,9 +34,11 @@ def _require_same_cuda_device(a: torch.Tensor, *named_tensors: tuple[str, torch.
 
 
 def _iso_gain_forward(a, omega, r, initial_precision, *, out_dtype, save_state, posterior_scale,
-                      initial_cov=None, want_final=False):
+                      initial_cov=None, want_final=False, plan=None):
     """Forward scalar covariance scan; optional carried-in covariance [B,H] and
-    final covariance out (sequence parallelism)."""
+    final covariance out (sequence parallelism).  ``plan`` (a packed batch's
+    ``kdn_b200.varlen.VarlenPlan``): every sequence restarts the covariance,
+    states are [N,H]."""
     B, T, H = a.shape
     N.require_cuda(a)
     lib = N.load_library()
@@ -44,21 +46,24 @@ def _iso_gain_forward(a, omega, r, initial_precision, *, out_dtype, save_state, 
     c32 = None if initial_cov is None else initial_cov.float().contiguous()
     gain = torch.empty((B, T, H), dtype=torch.float32, device=a.device)
     p_prev = torch.empty((B, T, H), dtype=torch.float32, device=a.device) if save_state else None
-    p_final = torch.empty((B, H), dtype=torch.float32, device=a.device) if want_final else None
-    ws = N.byte_buffer(lib.kdn_iso_gain_workspace_bytes(B, T, H), a.device)
-    N.check(
-        lib.kdn_iso_gain_fwd(
-            a32.data_ptr(), w32.data_ptr(), r32.data_ptr(), p32.data_ptr(), N.ptr(c32), gain.data_ptr(),
-            N.ptr(p_prev), N.ptr(p_final), B, T, H, float(posterior_scale), ws.data_ptr(), ws.numel(),
-            N.stream_of(a),
-        ),
-        "kdn_iso_gain_fwd",
-    )
+    streams = B if plan is None else plan.num_seqs
+    p_final = torch.empty((streams, H), dtype=torch.float32, device=a.device) if want_final else None
+    head = (a32.data_ptr(), w32.data_ptr(), r32.data_ptr(), p32.data_ptr(), N.ptr(c32), gain.data_ptr(),
+            N.ptr(p_prev), N.ptr(p_final))
+    if plan is None:
+        ws = N.byte_buffer(lib.kdn_iso_gain_workspace_bytes(B, T, H), a.device)
+        N.check(lib.kdn_iso_gain_fwd(*head, B, T, H, float(posterior_scale), ws.data_ptr(), ws.numel(),
+                                     N.stream_of(a)), "kdn_iso_gain_fwd")
+    else:
+        ws = N.byte_buffer(lib.kdn_iso_gain_varlen_workspace_bytes(plan.num_seqs, plan.max_len, H), a.device)
+        N.check(lib.kdn_iso_gain_fwd_varlen(*head, T, H, float(posterior_scale), plan.table.data_ptr(),
+                                            plan.num_seqs, plan.max_len, ws.data_ptr(), ws.numel(), N.stream_of(a)),
+                "kdn_iso_gain_fwd_varlen")
     return gain.to(out_dtype), p_prev, p_final
 
 
 def _iso_gain_backward(a, omega, r, initial_precision, dgain, p_prev, *, posterior_scale, initial_cov=None,
-                       d_final_cov=None, want_d_initial=False):
+                       d_final_cov=None, want_d_initial=False, plan=None):
     B, T, H = a.shape
     lib = N.load_library()
     a32, w32, r32, p32, d32 = (x.float().contiguous() for x in (a, omega, r, initial_precision, dgain))
@@ -67,16 +72,20 @@ def _iso_gain_backward(a, omega, r, initial_precision, dgain, p_prev, *, posteri
     domega = torch.empty_like(da)
     dr = torch.empty_like(da)
     dinit = torch.empty((H,), dtype=torch.float32, device=a.device)
-    dic = torch.empty((B, H), dtype=torch.float32, device=a.device) if want_d_initial else None
-    ws = N.byte_buffer(lib.kdn_iso_gain_workspace_bytes(B, T, H), a.device)
-    N.check(
-        lib.kdn_iso_gain_bwd(
-            a32.data_ptr(), w32.data_ptr(), r32.data_ptr(), p32.data_ptr(), N.ptr(initial_cov), d32.data_ptr(),
+    streams = B if plan is None else plan.num_seqs
+    dic = torch.empty((streams, H), dtype=torch.float32, device=a.device) if want_d_initial else None
+    head = (a32.data_ptr(), w32.data_ptr(), r32.data_ptr(), p32.data_ptr(), N.ptr(initial_cov), d32.data_ptr(),
             p_prev.data_ptr(), N.ptr(dfc), da.data_ptr(), domega.data_ptr(), dr.data_ptr(), dinit.data_ptr(),
-            N.ptr(dic), B, T, H, float(posterior_scale), ws.data_ptr(), ws.numel(), N.stream_of(a),
-        ),
-        "kdn_iso_gain_bwd",
-    )
+            N.ptr(dic))
+    if plan is None:
+        ws = N.byte_buffer(lib.kdn_iso_gain_workspace_bytes(B, T, H), a.device)
+        N.check(lib.kdn_iso_gain_bwd(*head, B, T, H, float(posterior_scale), ws.data_ptr(), ws.numel(),
+                                     N.stream_of(a)), "kdn_iso_gain_bwd")
+    else:
+        ws = N.byte_buffer(lib.kdn_iso_gain_varlen_workspace_bytes(plan.num_seqs, plan.max_len, H), a.device)
+        N.check(lib.kdn_iso_gain_bwd_varlen(*head, T, H, float(posterior_scale), plan.table.data_ptr(),
+                                            plan.num_seqs, plan.max_len, ws.data_ptr(), ws.numel(), N.stream_of(a)),
+                "kdn_iso_gain_bwd_varlen")
     return da.to(a.dtype), domega.to(omega.dtype), dr.to(r.dtype), dinit.to(initial_precision.dtype), dic
 
 
@@ -131,6 +140,20 @@ def iso_kdn_gain(
     a, omega, r: [B, T, H]; initial_precision: [H].  The scalar covariance
     scan runs in fp32 on the GPU; ``posterior_scale = info_scale / head_dim``.
     """
+    out_dtype, posterior_scale = _validate_iso_gain_inputs(a, omega, r, initial_precision, head_dim, out_dtype,
+                                                           info_scale)
+    needs_backward = torch.is_grad_enabled() and any(
+        t.requires_grad for t in (a, omega, r, initial_precision)
+    )
+    return _IsoKDNGainFunction.apply(
+        a.contiguous(), omega.contiguous(), r.contiguous(), initial_precision.contiguous(),
+        out_dtype, posterior_scale, needs_backward,
+    )
+
+
+def _validate_iso_gain_inputs(a, omega, r, initial_precision, head_dim, out_dtype, info_scale):
+    """The reference's checks and messages (iso_kdn_chunk.py:1990-2031);
+    returns (out_dtype, posterior_scale = info_scale / head_dim)."""
     if a.ndim != 3:
         raise ValueError(f"a must have shape [B,T,H], got {tuple(a.shape)}")
     if omega.shape != a.shape or r.shape != a.shape:
@@ -157,13 +180,7 @@ def iso_kdn_gain(
         if not math.isfinite(resolved_info_scale) or resolved_info_scale <= 0:
             raise ValueError(f"info_scale must be positive and finite, got {info_scale!r}")
     posterior_scale = resolved_info_scale / float(head_dim)
-    needs_backward = torch.is_grad_enabled() and any(
-        t.requires_grad for t in (a, omega, r, initial_precision)
-    )
-    return _IsoKDNGainFunction.apply(
-        a.contiguous(), omega.contiguous(), r.contiguous(), initial_precision.contiguous(),
-        out_dtype, posterior_scale, needs_backward,
-    )
+    return out_dtype, posterior_scale
 
 
 class _ChunkKDAPrecumsumFunction(torch.autograd.Function):

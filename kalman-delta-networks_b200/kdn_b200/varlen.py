@@ -9,23 +9,14 @@ zero, its covariance at 1 / initial_precision, and its gate prefix
 from the sequence's own first token.
 
 The memory scans (``chunk_kalman_varlen``, ``chunk_kda_precumsum_varlen``)
-and the diagonal gain (``diag_kdn_gain_varlen``) run natively: the kernels
-walk a chunk table (``kdn_varlen_plan``, cached per offsets and device in a
-``VarlenPlan``) in which every sequence owns its 64-token chunks, the last
-one partial; the chunk-parallel kernels take one CTA per (chunk, head), the
-sequential passes one CTA pair per (sequence, head), longest sequence first.
+and the gains (``diag_kdn_gain_varlen``, ``iso_kdn_gain_varlen``) run
+natively: the kernels walk a table (``kdn_varlen_plan``, cached per offsets
+and device in a ``VarlenPlan``) in which every sequence owns its 64-token
+chunks, the last one partial; the chunk-parallel kernels take one CTA per
+(chunk, head), the sequential passes one CTA pair per (sequence, head),
+longest sequence first, and the isotropic gain one stream per sequence.
 Each sequence gets exactly the arithmetic of a separate fixed-length call,
 with no padding and no gathers.
-
-The isotropic gain (``iso_kdn_gain_varlen``) runs the sequences as rows of
-fixed-length batched calls (``map_sequences``): sequences are grouped by
-length rounded up to ``bucket`` tokens (a multiple of 64); each group is
-gathered into a ``[n_seq, L, ...]`` batch whose rows start at a sequence's
-first token and are padded after its end with neutral tokens (unit
-retention and observation noise, zero process noise), so that no padding
-token changes a real token's output or gradient.  Outputs are gathered back
-to the packed layout.  Its tensors are per-token scalars [1, T, H], so the
-gathers are small.
 
 ``cu_seqlens`` may be a list, a CPU tensor or a CUDA tensor (read once on
 the host: a CUDA tensor costs a device synchronisation).
@@ -35,8 +26,6 @@ from __future__ import annotations
 import collections
 import ctypes
 
-from typing import Callable, Sequence
-
 import torch
 from torch.autograd.function import once_differentiable
 
@@ -44,10 +33,7 @@ from . import _native as N
 from . import diag_kdn_chunk, iso_kdn_chunk
 from ._scan import ScanSaved, scan_backward, scan_forward
 
-# gather plans by (offsets, bucket, device), least recently used last; bounded
-# so that a stream of distinct packings cannot grow it without limit
-_INDEX_CACHE: "collections.OrderedDict" = collections.OrderedDict()
-_INDEX_CACHE_MAX = 64
+_PLAN_CACHE_MAX = 64  # plans cached per (offsets, device), least recently used first out
 
 
 def offsets(cu_seqlens) -> list[int]:
@@ -57,121 +43,6 @@ def offsets(cu_seqlens) -> list[int]:
     if len(cu) < 2 or cu[0] != 0 or any(b <= a for a, b in zip(cu, cu[1:])):
         raise ValueError("cu_seqlens must start at 0 and increase strictly")
     return cu
-
-
-def _plan(cu: list[int], bucket: int, chunk: int, device: torch.device):
-    """Groups of sequences by padded length and the device index tensors that
-    gather every group's padded rows in one pass (cached per offsets, bucket,
-    gate chunk and device).  Returns ``(shapes, src, valid, src_g, hold, out)``:
-    ``shapes`` lists ``(L, n_seq)`` per group; the gathered rows of all groups
-    are concatenated, row i reading packed token ``src[i]`` (``valid[i]``) or
-    padding; ``out[t]`` is the gathered row of packed token t."""
-    key = (tuple(cu), bucket, chunk, str(device))
-    plan = _INDEX_CACHE.get(key)
-    if plan is not None:
-        _INDEX_CACHE.move_to_end(key)
-        return plan
-    groups: dict[int, list[int]] = {}
-    for i in range(len(cu) - 1):
-        n = cu[i + 1] - cu[i]
-        groups.setdefault(-(-n // bucket) * bucket, []).append(i)
-    shapes, pos_l, start_l, len_l = [], [], [], []
-    for L, seqs in sorted(groups.items()):
-        shapes.append((L, len(seqs)))
-        pos_l.append(torch.arange(L).repeat(len(seqs)))  # position inside the padded row
-        start_l.append(torch.tensor([cu[i] for i in seqs]).repeat_interleave(L))
-        len_l.append(torch.tensor([cu[i + 1] - cu[i] for i in seqs]).repeat_interleave(L))
-    pos, start, length = torch.cat(pos_l), torch.cat(start_l), torch.cat(len_l)
-    valid = pos < length
-    src = torch.where(valid, start + pos, torch.zeros_like(pos))  # any in-range row where padded
-    # gate prefix: the last real token's value up to the end of its chunk
-    hold = pos < (length + chunk - 1) // chunk * chunk
-    src_g = start + torch.minimum(pos, length - 1)
-    out = torch.empty(cu[-1], dtype=torch.long)
-    out[(start + pos)[valid]] = torch.nonzero(valid).squeeze(1)
-    plan = (shapes, src.to(device), valid.to(device), src_g.to(device), hold.to(device), out.to(device))
-    _INDEX_CACHE[key] = plan
-    while len(_INDEX_CACHE) > _INDEX_CACHE_MAX:
-        _INDEX_CACHE.popitem(last=False)
-    return plan
-
-
-class _Gather(torch.autograd.Function):
-    """rows[i] = x[src[i]] where keep[i], else ``fill``.  Every token is the
-    source of exactly one real row (``inv[t]``), so the gradient of x is a
-    gather as well (held padding copies of a gate row carry no cotangent)."""
-
-    @staticmethod
-    def forward(ctx, x, src, keep, fill, inv):
-        ctx.save_for_backward(inv)
-        rows = x.index_select(0, src)
-        mask = keep.view(-1, *([1] * (rows.dim() - 1)))
-        return torch.where(mask, rows, torch.full((), fill, dtype=x.dtype, device=x.device))
-
-    @staticmethod
-    def backward(ctx, g):
-        (inv,) = ctx.saved_tensors
-        return g.index_select(0, inv), None, None, None, None
-
-
-class _Scatter(torch.autograd.Function):
-    """out[t] = rows[inv[t]]: the real rows back in packed order; the gradient
-    of the rows is the gather of the packed gradient, zero on padding rows."""
-
-    @staticmethod
-    def forward(ctx, rows, inv, src, valid):
-        ctx.save_for_backward(src, valid)
-        return rows.index_select(0, inv)
-
-    @staticmethod
-    def backward(ctx, g):
-        src, valid = ctx.saved_tensors
-        d = g.index_select(0, src)
-        mask = valid.view(-1, *([1] * (d.dim() - 1)))
-        return torch.where(mask, d, torch.zeros((), dtype=d.dtype, device=d.device)), None, None, None
-
-
-def map_sequences(fn: Callable, tensors: Sequence, cu_seqlens, *, pad: Sequence = (), bucket: int = 1024,
-                  gate: int | None = None, chunk: int = 64):
-    """Apply ``fn(*batched)`` to the sequences of packed ``[1, total, ...]``
-    tensors (other arguments pass through unchanged) and return its output(s)
-    in the packed layout.  ``pad[i]`` is the fill value of ``tensors[i]`` after
-    a sequence's end (default 0); ``tensors[gate]``, a chunk-local gate prefix
-    restarting every ``chunk`` tokens, is held at its last real value to the
-    end of that chunk instead.  ``fn`` receives ``[n_seq, L, ...]`` batches and
-    must return tensors of the same leading shape.  Each packed tensor is
-    gathered once for all groups, and every gradient moves by a gather too
-    (no scatter-add)."""
-    if bucket <= 0 or bucket % 64:
-        raise ValueError("bucket must be a positive multiple of 64")
-    cu = offsets(cu_seqlens)
-    packed = [t for t in tensors if isinstance(t, torch.Tensor) and t.dim() >= 2]
-    if not packed:
-        raise ValueError("no packed [1, T, ...] tensor")
-    total = packed[0].shape[1]
-    if cu[-1] != total or any(t.shape[0] != 1 or t.shape[1] != total for t in packed):
-        raise ValueError(f"packed tensors must be [1, {cu[-1]}, ...] to match cu_seqlens")
-    shapes, src, valid, src_g, hold, out_rows = _plan(cu, bucket, chunk, packed[0].device)
-    sizes = [L * n for L, n in shapes]
-    fills = list(pad) + [0.0] * (len(tensors) - len(pad))
-    per_group = []  # per tensor: its [n, L, ...] batches, or the pass-through argument
-    for i, (t, fill) in enumerate(zip(tensors, fills)):
-        if isinstance(t, torch.Tensor) and t.dim() >= 2:
-            rows = _Gather.apply(t[0], src_g if i == gate else src, hold if i == gate else valid, fill, out_rows)
-            per_group.append([part.view(n, L, *t.shape[2:])
-                              for part, (L, n) in zip(torch.split(rows, sizes), shapes)])
-        else:
-            per_group.append([t] * len(shapes))
-    results, is_tuple = [], False
-    for gi in range(len(shapes)):
-        out = fn(*(arg[gi] for arg in per_group))
-        is_tuple = isinstance(out, tuple)
-        results.append(out if is_tuple else (out,))
-    outs = []
-    for j in range(len(results[0])):
-        cat = torch.cat([res[j].reshape(-1, *res[j].shape[2:]) for res in results], 0)
-        outs.append(_Scatter.apply(cat, out_rows, src, valid).unsqueeze(0))
-    return tuple(outs) if is_tuple else outs[0]
 
 
 # --------------------------------------------------------------------------
@@ -199,6 +70,7 @@ class VarlenPlan:
         self.cu = tuple(cu)
         self.num_seqs = n
         self.num_chunks = int(nc.value)
+        self.max_len = max(b - a for a, b in zip(cu, cu[1:]))
         self.table = host.to(device)
 
 
@@ -210,7 +82,7 @@ def plan(cu_seqlens, device) -> VarlenPlan:
     if p is None:
         p = VarlenPlan(cu, torch.device(device))
         _PLAN_CACHE[key] = p
-        while len(_PLAN_CACHE) > _INDEX_CACHE_MAX:
+        while len(_PLAN_CACHE) > _PLAN_CACHE_MAX:
             _PLAN_CACHE.popitem(last=False)
     else:
         _PLAN_CACHE.move_to_end(key)
@@ -316,16 +188,37 @@ def chunk_kda_precumsum_varlen(q, k, v, g_cumsum, beta, scale: float | None = No
     return _IsoMemoryVarlenFunction.apply(q, k, v, g_cumsum, beta, scale, vp)
 
 
-def iso_kdn_gain_varlen(a, omega, r, initial_precision, *, head_dim: int, cu_seqlens, out_dtype=None,
-                        info_scale=None, bucket: int = 1024):
-    """``iso_kdn_gain`` over a packed batch: the covariance restarts at every sequence."""
-    def one(aa, w, rr):
-        return iso_kdn_chunk.iso_kdn_gain(aa, w, rr, initial_precision, head_dim=head_dim, out_dtype=out_dtype,
-                                          info_scale=info_scale)
+class _IsoGainVarlenFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, a, omega, r, initial_precision, out_dtype, posterior_scale, vp):
+        gain, p_prev, _ = iso_kdn_chunk._iso_gain_forward(a, omega, r, initial_precision, out_dtype=out_dtype,
+                                                          save_state=True, posterior_scale=posterior_scale, plan=vp)
+        ctx.save_for_backward(a, omega, r, initial_precision, p_prev)
+        ctx.posterior_scale, ctx.vp = posterior_scale, vp
+        return gain
 
-    return map_sequences(one, (a, omega, r), cu_seqlens, pad=(1.0, 0.0, 1.0), bucket=bucket)
+    @staticmethod
+    def backward(ctx, dgain):
+        if dgain is None:
+            return None, None, None, None, None, None, None
+        a, omega, r, initial_precision, p_prev = ctx.saved_tensors
+        da, domega, dr, dinit, _ = iso_kdn_chunk._iso_gain_backward(
+            a, omega, r, initial_precision, dgain, p_prev, posterior_scale=ctx.posterior_scale, plan=ctx.vp)
+        return da, domega, dr, dinit, None, None, None
+
+
+def iso_kdn_gain_varlen(a, omega, r, initial_precision, *, head_dim: int, cu_seqlens, out_dtype=None,
+                        info_scale=None):
+    """``iso_kdn_gain`` over a packed batch: the covariance restarts at every
+    sequence; ``initial_precision`` [H] is shared and collects every
+    sequence's cotangent."""
+    out_dtype, posterior_scale = iso_kdn_chunk._validate_iso_gain_inputs(a, omega, r, initial_precision, head_dim,
+                                                                         out_dtype, info_scale)
+    vp = plan(cu_seqlens, a.device)
+    _check_packed("a", a, vp.cu)
+    return _IsoGainVarlenFunction.apply(a.contiguous(), omega.contiguous(), r.contiguous(),
+                                        initial_precision.contiguous(), out_dtype, posterior_scale, vp)
 
 
 __all__ = ("chunk_kalman_varlen", "diag_kdn_gain_varlen", "chunk_kda_precumsum_varlen", "iso_kdn_gain_varlen",
-           "VarlenPlan", "plan",
-           "map_sequences", "offsets")
+           "VarlenPlan", "plan", "offsets")
