@@ -212,8 +212,9 @@ int kdn_iso_gain_bwd_varlen(const float* a, const float* omega, const float* r,
  * k, alpha, omega, kappa, dkappa, dk, dalpha: fp32 [B,T,H,K]; r: fp32 [B,T,H];
  * omega_raw, domega_raw: bf16 [B,T,H,K]; r_raw, dr_raw: bf16 [B,T,H];
  * initial_precision, d_initial_precision: fp32 [H].  `carry` (fp32, size from
- * kdn_diag_gain_carry_elems) is written by the forward and read by the
- * backward.  p_final (fp32 [B,H,K], nullable) receives the final covariance.
+ * kdn_diag_gain_carry_elems: the covariance entering every 64-token segment,
+ * then the covariance before every token, [B,T,H,K]) is written by the
+ * forward and read by the backward.  p_final (fp32 [B,H,K], nullable) receives the final covariance.
  * The backward fuses the softplus VJPs: domega_raw = dL/domega *
  * sigmoid(omega_raw), dr_raw = dL/dr * sigmoid(r_raw).  K must be 64 or 128;
  * B*H <= 65535.
@@ -308,7 +309,8 @@ int kdn_diag_gain_bwd(const float* k, const float* alpha, const float* omega,
  * per sequence, fp32 [N,H,K]; the covariance of every sequence starts from
  * 1/initial_precision (or its initial_cov row).  Carry and workspace sizes
  * from the _varlen queries.  Same results per sequence as separate calls. */
-int64_t kdn_diag_gain_varlen_carry_elems(int64_t H, int64_t K, int64_t num_chunks);
+int64_t kdn_diag_gain_varlen_carry_elems(int64_t T, int64_t H, int64_t K,
+                                         int64_t num_chunks);
 size_t kdn_diag_gain_varlen_workspace_bytes(int64_t T, int64_t H, int64_t K,
                                             int64_t num_chunks);
 int kdn_diag_gain_fwd_varlen(const float* k, const float* alpha,

@@ -113,7 +113,7 @@ _SIGNATURES = {
         [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _SZ, _P],
         ctypes.c_int,
     ),
-    "kdn_diag_gain_varlen_carry_elems": ([_I64, _I64, _I64], _I64),
+    "kdn_diag_gain_varlen_carry_elems": ([_I64, _I64, _I64, _I64], _I64),
     "kdn_diag_gain_varlen_workspace_bytes": ([_I64, _I64, _I64, _I64], _SZ),
     "kdn_diag_gain_fwd_varlen": ([_P] * 9 + [_I64, _I64, _I64, _P, _I64, _I64, _P, _SZ, _P], ctypes.c_int),
     "kdn_diag_gain_bwd_varlen": ([_P] * 17 + [_I64, _I64, _I64, _P, _I64, _I64, _P, _SZ, _P], ctypes.c_int),

@@ -324,12 +324,14 @@ int iso_grid(const char* what, int64_t B, int64_t T, int64_t H, void* ws, size_t
 // neutral values and are skipped by the callers.  Tile sizes (2 to 8 tokens)
 // were chosen by timing at B=4, T=4096, H=18, K=128: larger tiles cost
 // occupancy (registers) and lost more than the deeper prefetch gained.
-template <int K, int TT, bool DK>
+template <int K, int TT, bool DK, bool PP = false>
 struct GainTile {
-  float k[TT], a[TT], w[TT], r[TT], dk[DK ? TT : 1];
+  // PP: the covariance before each token (p_{t-1}), saved by the forward
+  float k[TT], a[TT], w[TT], r[TT], dk[DK ? TT : 1], pp[PP ? TT : 1];
   __device__ __forceinline__ void load(const float* __restrict__ kk, const float* __restrict__ al,
                                        const float* __restrict__ om, const float* __restrict__ rr,
-                                       const float* __restrict__ dkap, size_t row0, int H, int n, int c) {
+                                       const float* __restrict__ dkap, size_t row0, int H, int n, int c,
+                                       const float* __restrict__ ppv = nullptr) {
 #pragma unroll
     for (int j = 0; j < TT; ++j) {
       if (j < n) {
@@ -339,12 +341,14 @@ struct GainTile {
         w[j] = om[row * K + c];
         r[j] = rr[row];
         if constexpr (DK) dk[j] = dkap[row * K + c];
+        if constexpr (PP) pp[j] = ppv[row * K + c];
       } else {
         k[j] = 0.f;
         a[j] = 1.f;
         w[j] = 0.f;
         r[j] = 1.f;
         if constexpr (DK) dk[j] = 0.f;
+        if constexpr (PP) pp[j] = 0.f;
       }
     }
   }
@@ -415,8 +419,8 @@ __global__ void __launch_bounds__(K) diag_gain_emit_kernel(const float* __restri
                                                            const float* __restrict__ omega,
                                                            const float* __restrict__ r,
                                                            const float* __restrict__ carry,
-                                                           float* __restrict__ kappa, int T, int H, int nseg,
-                                                           Varlen v) {
+                                                           float* __restrict__ kappa, float* __restrict__ p_prev,
+                                                           int T, int H, int nseg, Varlen v) {
   constexpr int TT = 4;
   __shared__ float red[K / 32 * TT];
   __shared__ float tok[TT];
@@ -436,6 +440,7 @@ __global__ void __launch_bounds__(K) diag_gain_emit_kernel(const float* __restri
       num[j] = 0.f;
       pk2[j] = 0.f;
       if (ts + j < n) {
+        p_prev[(row0 + (size_t)(ts + j) * H) * K + c] = p;  // for the backward
         const float ph = cu.a[j] * cu.a[j] * p + cu.w[j];
         const float ksq = cu.k[j] * cu.k[j];
         num[j] = ph * cu.k[j];
@@ -457,7 +462,7 @@ __global__ void __launch_bounds__(K) diag_gain_emit_kernel(const float* __restri
 template <int K>
 __global__ void __launch_bounds__(K) diag_gain_bwd_map_kernel(
     const float* __restrict__ k, const float* __restrict__ alpha, const float* __restrict__ omega,
-    const float* __restrict__ r, const float* __restrict__ dkappa, const float* __restrict__ carry,
+    const float* __restrict__ r, const float* __restrict__ dkappa, const float* __restrict__ p_prev,
     float2* __restrict__ maps, float2* __restrict__ dg_tok, int T, int H, int nseg, Varlen v) {
   constexpr int TT = 2;
   __shared__ float red[K / 32 * 2 * TT];
@@ -467,25 +472,23 @@ __global__ void __launch_bounds__(K) diag_gain_bwd_map_kernel(
   seg_span(v, seg, T, H, bh, t0, n, sh);
   const size_t row0 = ((size_t)b * T + t0) * H + h;
   const float Kf = (float)K;
-  GainTile<K, TT, true> cu, nx;
-  nx.load(k, alpha, omega, r, dkappa, row0, H, n, c);
-  float p = carry[((size_t)bh * nseg + seg) * K + c];
+  // the covariance before every token comes from the forward (p_prev): the
+  // tokens of a tile are independent, only the adjoint maps compose in order
+  GainTile<K, TT, true, true> cu, nx;
+  nx.load(k, alpha, omega, r, dkappa, row0, H, n, c, p_prev);
   Aff comp{1.f, 0.f};
   for (int ts = 0; ts < n; ts += TT) {
     cu = nx;
-    if (ts + TT < n) nx.load(k, alpha, omega, r, dkappa, row0 + (size_t)(ts + TT) * H, H, n - ts - TT, c);
-    float v[2 * TT], pp[TT];
+    if (ts + TT < n) nx.load(k, alpha, omega, r, dkappa, row0 + (size_t)(ts + TT) * H, H, n - ts - TT, c, p_prev);
+    float v[2 * TT];
 #pragma unroll
     for (int j = 0; j < TT; ++j) {
-      pp[j] = p;
       v[j] = 0.f;
       v[TT + j] = 0.f;
       if (ts + j < n) {
-        const float ph = cu.a[j] * cu.a[j] * p + cu.w[j];
+        const float ph = cu.a[j] * cu.a[j] * cu.pp[j] + cu.w[j];
         v[j] = ph * cu.k[j] * cu.k[j];
         v[TT + j] = cu.dk[j] * ph * cu.k[j];
-        const float u = __fdividef(Kf * cu.k[j] * cu.k[j], cu.r[j]);
-        p = __fdividef(ph, 1.f + u * ph);
       }
     }
     block_token_sums<K, 2 * TT>(v, red, tok);
@@ -497,7 +500,7 @@ __global__ void __launch_bounds__(K) diag_gain_bwd_map_kernel(
         const float G = tok[TT + j] * iD;
         if (c == 0) dg_tok[(size_t)bh * T + t0 + ts + j] = make_float2(D, G);
         const float a2 = cu.a[j] * cu.a[j];
-        const float ph = a2 * pp[j] + cu.w[j];
+        const float ph = a2 * cu.pp[j] + cu.w[j];
         const float ihh = __fdividef(1.f, 1.f + __fdividef(Kf * kt * kt, rt) * ph);
         const float pbar_gain = (cu.dk[j] * kt - kt * kt * G) * iD;
         comp = aff_after(comp, Aff{a2 * ihh * ihh, a2 * pbar_gain});
@@ -557,47 +560,29 @@ template <int K>
 __global__ void __launch_bounds__(K) diag_gain_bwd_emit_kernel(
     const float* __restrict__ k, const float* __restrict__ alpha, const float* __restrict__ omega,
     const float* __restrict__ r, const float* __restrict__ init_prec, const bf16* __restrict__ omega_raw,
-    const bf16* __restrict__ r_raw, const float* __restrict__ dkappa, const float* __restrict__ carry,
+    const bf16* __restrict__ r_raw, const float* __restrict__ dkappa, const float* __restrict__ p_prev,
     const float* __restrict__ lam_carry, const float2* __restrict__ dg_tok, float* __restrict__ dk_out,
     float* __restrict__ dalpha, bf16* __restrict__ domega_raw, bf16* __restrict__ dr_raw,
     float* __restrict__ dinit, float* __restrict__ d_init_cov, int T, int H, int nseg, Varlen v) {
-  constexpr int TF = 8, TT = 8;
+  constexpr int TT = 4;  // 4-token reverse tiles: about 100 registers, five CTAs per SM
   __shared__ float red[K / 32 * TT];
   __shared__ float tok[TT];
-  __shared__ float pprev_s[kDiagSeg][K];
   const int seg = blockIdx.x, bh = blockIdx.y, b = bh / H, h = bh - b * H, c = threadIdx.x;
   int t0, n, sh;
   seg_span(v, seg, T, H, bh, t0, n, sh);
   const bool first = v.on() ? seg == v.chunk[sh / H] : seg == 0;  // the stream's first segment
   const size_t row0 = ((size_t)b * T + t0) * H + h;
   const float Kf = (float)K;
-  // forward re-run of the covariance: p before every token of the segment
-  {
-    GainTile<K, TF, false> cu, nx;
-    nx.load(k, alpha, omega, r, nullptr, row0, H, n, c);
-    float p = carry[((size_t)bh * nseg + seg) * K + c];
-    for (int ts = 0; ts < n; ts += TF) {
-      cu = nx;
-      if (ts + TF < n) nx.load(k, alpha, omega, r, nullptr, row0 + (size_t)(ts + TF) * H, H, n - ts - TF, c);
-#pragma unroll
-      for (int j = 0; j < TF; ++j) {
-        if (ts + j < n) {
-          pprev_s[ts + j][c] = p;
-          const float ph = cu.a[j] * cu.a[j] * p + cu.w[j];
-          p = __fdividef(ph, 1.f + __fdividef(Kf * cu.k[j] * cu.k[j], cu.r[j]) * ph);
-        }
-      }
-    }
-  }
-  // reverse adjoint over tiles of TT tokens, last tile first
+  // reverse adjoint over tiles of TT tokens, last tile first; the covariance
+  // before every token (p_prev) was saved by the forward
   struct Rev {
-    GainTile<K, TT, true> g;
+    GainTile<K, TT, true, true> g;
     float2 DG[TT];
     float wr[TT];
   };
   auto load_rev = [&](Rev& x, int ts) {
     const int m = min(TT, n - ts);
-    x.g.load(k, alpha, omega, r, dkappa, row0 + (size_t)ts * H, H, m, c);
+    x.g.load(k, alpha, omega, r, dkappa, row0 + (size_t)ts * H, H, m, c, p_prev);
 #pragma unroll
     for (int j = 0; j < TT; ++j) {
       if (j < m) {
@@ -625,7 +610,7 @@ __global__ void __launch_bounds__(K) diag_gain_bwd_emit_kernel(
         const size_t row = row0 + (size_t)(ts + jj) * H;
         const float kt = cu.g.k[jj], at = cu.g.a[jj], wt = cu.g.w[jj], rt = cu.g.r[jj], dk = cu.g.dk[jj];
         const float D = cu.DG[jj].x, G = cu.DG[jj].y, iD = __fdividef(1.f, D), ir = __fdividef(1.f, rt);
-        const float pp = pprev_s[ts + jj][c];
+        const float pp = cu.g.pp[jj];
         const float a2 = at * at, ksq = kt * kt;
         const float ph = a2 * pp + wt;
         const float u = Kf * ksq * ir;
@@ -653,7 +638,7 @@ __global__ void __launch_bounds__(K) diag_gain_bwd_emit_kernel(
   if (first && d_init_cov) d_init_cov[(size_t)sh * K + c] = lam;  // d L / d p_{-1}
   if (first && dinit) {
     // p_{-1} = 1/mu, so d mu = -sum_c lambda_{-1,c} p_{-1,c}^2
-    const float p0 = pprev_s[0][c];
+    const float p0 = p_prev[row0 * K + c];
     float v = -lam * p0 * p0;
     v = warp_sum(v);
     if ((c & 31) == 0) atomicAdd(dinit + h, v);
@@ -794,9 +779,12 @@ int kdn_iso_gain_bwd_varlen(const float* a, const float* omega, const float* r, 
                  (cudaStream_t)stream);
 }
 
+// carry = [the covariance entering every 64-token segment, B*H*nseg*K |
+//          the covariance before every token (p_prev), B*T*H*K]; the
+// backward reads p_prev instead of re-running the recursion
 int64_t kdn_diag_gain_carry_elems(int64_t B, int64_t T, int64_t H, int64_t K) {
   const int64_t nseg = (T + kDiagSeg - 1) / kDiagSeg;
-  return B * H * nseg * K;
+  return B * H * nseg * K + B * T * H * K;
 }
 
 size_t kdn_diag_gain_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t K) {
@@ -824,6 +812,9 @@ struct DiagDims {
   Varlen v;  // packed batch (B = 1): segments are the sequences' 64-token chunks
   // (sequence, head) streams of the carry kernels
   unsigned streams() const { return (unsigned)(v.on() ? (int64_t)v.n * H : B * H); }
+  // the covariance before every token, after the segment carries in `carry`
+  float* p_prev(float* carry) const { return carry + B * H * nseg * K; }
+  const float* p_prev(const float* carry) const { return carry + B * H * nseg * K; }
 };
 
 int diag_dims(const char* what, int64_t B, int64_t T, int64_t H, int64_t K, DiagDims* d) {
@@ -850,11 +841,13 @@ int diag_fwd_finish(const DiagDims& d, const float* k, const float* alpha, const
   const unsigned sh = d.streams();
   if (d.K == 128) {
     diag_gain_carry_kernel<128><<<sh, 128, 0, st>>>(maps, init_prec, init_cov, carry, p_final, (int)d.H, d.nseg, d.v);
-    diag_gain_emit_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, carry, kappa, (int)d.T, (int)d.H, d.nseg,
+    diag_gain_emit_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, carry, kappa, d.p_prev(carry), (int)d.T,
+                                                     (int)d.H, d.nseg,
                                                      d.v);
   } else {
     diag_gain_carry_kernel<64><<<sh, 64, 0, st>>>(maps, init_prec, init_cov, carry, p_final, (int)d.H, d.nseg, d.v);
-    diag_gain_emit_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, carry, kappa, (int)d.T, (int)d.H, d.nseg, d.v);
+    diag_gain_emit_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, carry, kappa, d.p_prev(carry), (int)d.T,
+                                                   (int)d.H, d.nseg, d.v);
   }
   return check_launch("diag_gain_fwd kernels");
 }
@@ -880,10 +873,10 @@ int diag_bwd_maps(const DiagDims& d, const float* k, const float* alpha, const f
                   const float* dkappa, const float* carry, const DiagBwdWs& w, cudaStream_t st) {
   dim3 grid((unsigned)d.nseg, (unsigned)(d.B * d.H));
   if (d.K == 128)
-    diag_gain_bwd_map_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, dkappa, carry, w.maps, w.dg_tok, (int)d.T,
+    diag_gain_bwd_map_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, dkappa, d.p_prev(carry), w.maps, w.dg_tok, (int)d.T,
                                                         (int)d.H, d.nseg, d.v);
   else
-    diag_gain_bwd_map_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, dkappa, carry, w.maps, w.dg_tok, (int)d.T,
+    diag_gain_bwd_map_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, dkappa, d.p_prev(carry), w.maps, w.dg_tok, (int)d.T,
                                                       (int)d.H, d.nseg, d.v);
   return check_launch("diag_gain_bwd_map_kernel");
 }
@@ -900,12 +893,12 @@ int diag_bwd_finish(const DiagDims& d, const float* k, const float* alpha, const
   const unsigned sh = d.streams();
   if (d.K == 128) {
     diag_gain_bwd_carry_kernel<128><<<sh, 128, 0, st>>>(w.maps, d_final_cov, w.lam, (int)d.H, d.nseg, d.v);
-    diag_gain_bwd_emit_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, init_prec, wr, rr, dkappa, carry, w.lam,
+    diag_gain_bwd_emit_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, init_prec, wr, rr, dkappa, d.p_prev(carry), w.lam,
                                                          w.dg_tok, dk, dalpha, domega_raw, dr_raw, dmu, d_init_cov,
                                                          (int)d.T, (int)d.H, d.nseg, d.v);
   } else {
     diag_gain_bwd_carry_kernel<64><<<sh, 64, 0, st>>>(w.maps, d_final_cov, w.lam, (int)d.H, d.nseg, d.v);
-    diag_gain_bwd_emit_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, init_prec, wr, rr, dkappa, carry, w.lam,
+    diag_gain_bwd_emit_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, init_prec, wr, rr, dkappa, d.p_prev(carry), w.lam,
                                                        w.dg_tok, dk, dalpha, domega_raw, dr_raw, dmu, d_init_cov,
                                                        (int)d.T, (int)d.H, d.nseg, d.v);
   }
@@ -1047,8 +1040,8 @@ int kdn_diag_gain_bwd_finish(const float* k, const float* alpha, const float* om
                          diag_bwd_ws(d, ws), (cudaStream_t)stream);
 }
 
-int64_t kdn_diag_gain_varlen_carry_elems(int64_t H, int64_t K, int64_t num_chunks) {
-  return H > 0 && K > 0 && num_chunks > 0 ? H * num_chunks * K : 0;
+int64_t kdn_diag_gain_varlen_carry_elems(int64_t T, int64_t H, int64_t K, int64_t num_chunks) {
+  return T > 0 && H > 0 && K > 0 && num_chunks > 0 ? H * num_chunks * K + T * H * K : 0;
 }
 
 size_t kdn_diag_gain_varlen_workspace_bytes(int64_t T, int64_t H, int64_t K, int64_t num_chunks) {

@@ -46,7 +46,7 @@ def _gain_forward(k, alpha, omega, r, initial_precision, initial_cov=None, want_
         )
     else:
         nc = plan.num_chunks
-        carry = torch.empty(lib.kdn_diag_gain_varlen_carry_elems(H, K, nc), dtype=torch.float32, device=k.device)
+        carry = torch.empty(lib.kdn_diag_gain_varlen_carry_elems(T, H, K, nc), dtype=torch.float32, device=k.device)
         ws = N.byte_buffer(lib.kdn_diag_gain_varlen_workspace_bytes(T, H, K, nc), k.device)
         N.check(
             lib.kdn_diag_gain_fwd_varlen(

@@ -90,7 +90,9 @@ def test_diag_gain_rejects_grids_beyond_the_launch_limit(lib):
 
 
 def test_diag_gain_sizes(lib):
-    assert lib.kdn_diag_gain_carry_elems(2, 130, 3, 128) == 2 * 3 * 3 * 128
+    # segment carries (3 segments of 64 tokens) + the covariance before every token
+    assert lib.kdn_diag_gain_carry_elems(2, 130, 3, 128) == 2 * 3 * 3 * 128 + 2 * 130 * 3 * 128
+    assert lib.kdn_diag_gain_varlen_carry_elems(130, 3, 128, 4) == 3 * 4 * 128 + 130 * 3 * 128
     assert lib.kdn_diag_gain_workspace_bytes(2, 130, 3, 128) > 0
 
 
