@@ -109,3 +109,51 @@ def test_operators_fail_loudly_without_cuda():
     q = torch.randn(1, 4, 2, 128, dtype=torch.bfloat16)
     with pytest.raises(ValueError, match="CUDA-only"):
         _chunk_kda_precumsum_paired(q, q, q, torch.zeros(1, 4, 2, 128), torch.rand(1, 4, 2))
+
+
+def test_varlen_scan_sizes_and_validation(lib):
+    """A packed batch sizes its saved state by global chunks; the C ABI
+    rejects a packed batch with B > 1, the fp32 precision, a missing table or
+    a partial-pass mode before launching anything."""
+    cu = (ctypes.c_int64 * 4)(0, 70, 75, 203)  # chunks: 2 + 1 + 2
+    nc = ctypes.c_int64(0)
+    assert lib.kdn_varlen_plan(ctypes.cast(cu, ctypes.c_void_p), 3, None, 0, ctypes.byref(nc)) == 0
+    assert nc.value == 5
+    table = (ctypes.c_int32 * lib.kdn_varlen_table_len(3, 5))()
+    assert lib.kdn_varlen_plan(ctypes.cast(cu, ctypes.c_void_p), 3, ctypes.cast(table, ctypes.c_void_p),
+                               len(table), ctypes.byref(nc)) == 0
+    assert list(table) == [0, 70, 75, 203, 0, 2, 3, 5, 2, 0, 1, 0, 0, 1, 2, 2]
+
+    def args(**kw):
+        a = N.KdnScanArgs()
+        a.variant, a.precision = N.KDN_DIAG, N.KDN_PREC_BF16
+        a.B, a.T, a.H, a.K, a.V = 1, 203, 2, 128, 128
+        a.varlen_table, a.num_seqs, a.num_chunks = ctypes.addressof(table), 3, 5
+        for k, v in kw.items():
+            setattr(a, k, v)
+        return a
+
+    fixed = N.KdnScanArgs()
+    fixed.variant, fixed.precision = N.KDN_DIAG, N.KDN_PREC_BF16
+    fixed.B, fixed.T, fixed.H, fixed.K, fixed.V = 1, 5 * 64, 2, 128, 128
+    # five global chunks hold what a 320-token fixed batch's five chunks hold
+    # (records and states), the gate prefix copy is per token
+    packed = lib.kdn_scan_saved_bytes(ctypes.byref(args()))
+    assert packed > 0 and packed < lib.kdn_scan_saved_bytes(ctypes.byref(fixed))
+    for bad in (dict(B=2), dict(precision=N.KDN_PREC_FP32), dict(varlen_table=None), dict(num_chunks=2)):
+        assert lib.kdn_scan_saved_bytes(ctypes.byref(args(**bad))) == 0, bad
+        assert lib.kdn_scan_fwd(ctypes.byref(args(**bad)), None) == -1, bad
+        assert b"packed batch" in lib.kdn_last_error()
+    a = args(mode=N.KDN_SCAN_FWD_RECORDS, q=1, k=1, v=1, g=1, kappa=1, saved=1)
+    assert lib.kdn_scan_fwd(ctypes.byref(a), None) == -1
+    assert b"mode 0 only" in lib.kdn_last_error()
+
+
+def test_varlen_gain_validation(lib):
+    p = ctypes.c_void_p(16)
+    assert lib.kdn_diag_gain_fwd_varlen(p, p, p, p, p, None, p, p, None, 100, 2, 128, None, 2, 3, p, 1 << 30,
+                                        None) == -1
+    assert b"kdn_varlen_plan table" in lib.kdn_last_error()
+    assert lib.kdn_iso_gain_fwd_varlen(p, p, p, p, None, p, p, None, 100, 2, 1.0, p, 2, 101, p, 1 << 30,
+                                       None) == -1  # longest sequence longer than T
+    assert lib.kdn_iso_gain_varlen_workspace_bytes(3, 130, 2) == lib.kdn_iso_gain_workspace_bytes(3, 130, 2)
