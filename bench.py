@@ -976,6 +976,29 @@ def measure_model(args, device, dist, world, rank, warmup, steps=5, name="iso_kd
 # ----------------------------------------------------------------------------- main
 
 
+def bind_host_to_gpu(device):
+    """Restrict this process to the CPU cores NVML reports as local to its GPU
+    (the socket its PCIe root hangs off), so that the pinned host buffers of
+    the end-to-end measurement are allocated on that node and its copies do
+    not cross the socket interconnect, as `numactl --cpunodebind` does for a
+    launcher.  Reads NVML only; changes no GPU setting.  Returns the number
+    of cores kept, or None when NVML or the affinity call is unavailable."""
+    try:
+        import pynvml as nvml
+
+        nvml.nvmlInit()
+        handle = ClockSampler(device)._handle(nvml)
+        words = nvml.nvmlDeviceGetCpuAffinity(handle, (os.cpu_count() + 63) // 64)
+        cpus = {64 * w + bit for w, word in enumerate(words) for bit in range(64) if (int(word) >> bit) & 1}
+        cpus &= os.sched_getaffinity(0)
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+            return len(cpus)
+    except Exception:
+        pass
+    return None
+
+
 def measure_e2e(step, x, names, args, device, dist, tokens, result="grads"):
     """End-to-end time of ``step`` through the public operators with host
     buffers: every step uploads its inputs ``x`` from pinned host memory and
@@ -1230,8 +1253,13 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    # one process per GPU: keep each rank's host side on its GPU's socket (at
+    # N = 1 the process keeps every core, which the CPU baseline uses)
+    host_cores = bind_host_to_gpu(device) if world > 1 else None
 
     rec, x = measure(args.variant, args, device, dist, world, rank, warmup, varlen=args.varlen)
+    if rec["e2e"] is not None:
+        rec["e2e"]["host_cores_bound"] = host_cores
     out = {"metric": METRIC, "value": rec["value"], "unit": "Mtok/s", "n_gpus": world, "steps": args.steps,
            "warmup": warmup, "ms_per_step": rec["ms_per_step"], "timing": rec["timing"],
            "eager_ms_per_step": rec["eager_ms_per_step"], "higher_is_better": True, "scaling": "weak",
