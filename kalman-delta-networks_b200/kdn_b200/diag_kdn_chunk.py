@@ -20,6 +20,7 @@ from ._scan import ScanSaved, scan_backward, scan_forward
 
 _VECTOR_DTYPE = torch.bfloat16
 _STATE_DTYPE = torch.float32
+_KD = 128  # the kernels' key and value width
 
 
 def _gain_forward(k, alpha, omega, r, initial_precision, initial_cov=None, want_final=False, plan=None):
@@ -192,8 +193,6 @@ def _validate_diag_kdn_memory_inputs(q, k, kappa, v, g_cumsum, scale):
         raise TypeError("kappa and g_cumsum must be torch.float32")
     if type(scale) is not float or not math.isfinite(scale):
         raise TypeError("scale must be an exact finite float")
-    if K != 128:
-        raise ValueError(f"kdn_b200 kernels support K = V = 128, got K={K}")
     return B, T, H, K
 
 
@@ -233,8 +232,17 @@ def chunk_kalman(
 ) -> torch.Tensor:
     """Diagonal KDN memory scan (diag_kdn_chunk.py:3315-3332): fp32 output;
     backward returns (dq bf16, dk bf16, dkappa fp32, dv bf16, dG fp32, None)
-    with dG the natural-log cotangent before the reverse 32-chunk cumsum."""
-    _validate_diag_kdn_memory_inputs(q_memory, k_memory, kappa, v, g_cumsum, scale)
+    with dG the natural-log cotangent before the reverse 32-chunk cumsum.
+    K = V in {64, 128}, as the reference (64 runs zero-padded to 128)."""
+    K = _validate_diag_kdn_memory_inputs(q_memory, k_memory, kappa, v, g_cumsum, scale)[3]
+    if K < _KD:
+        # K = V = 64: the kernels' 128 channels with zeros in the upper half
+        # (zero keys, gains and values leave those state rows and columns at
+        # zero and add nothing to any product); the pads' backward drops
+        # their gradients, the slice's pads the cotangent with zeros
+        pad = lambda t: torch.nn.functional.pad(t, (0, _KD - K))  # noqa: E731
+        o = _DiagKdnMemoryFunction.apply(pad(q_memory), pad(k_memory), pad(kappa), pad(v), pad(g_cumsum), scale)
+        return o[..., :K]
     return _DiagKdnMemoryFunction.apply(q_memory, k_memory, kappa, v, g_cumsum, scale)
 
 

@@ -231,16 +231,26 @@ def _chunk_kda_precumsum_paired(
 
     ``g_cumsum`` is the 64-local base-2 prefix of ln(alpha); the backward
     returns the natural-log cotangent its producer expects.  The kernels take
-    bf16 q/k/v (other floating dtypes are rounded to bf16) with
-    K = V = 128.
+    bf16 q/k/v (other floating dtypes are rounded to bf16) with K = V = 128;
+    narrower K or V (the reference accepts K <= 256) run zero-padded to 128.
     """
     scale = _validate_chunk_kda_inputs(q, k, v, g_cumsum, beta, scale)
+    K, V = q.shape[-1], v.shape[-1]
+    if K < 128 or V < 128:
+        # narrower heads run in the kernels' 128 channels with zeros above
+        # (zero keys and queries keep their norms and leave those state rows
+        # at zero, zero values those columns); the pads' backward drops their
+        # gradients, the slice's pads the cotangent with zeros
+        pk = lambda t: torch.nn.functional.pad(t, (0, 128 - K))  # noqa: E731
+        o = _ChunkKDAPrecumsumFunction.apply(pk(q), pk(k), torch.nn.functional.pad(v, (0, 128 - V)),
+                                             pk(g_cumsum), beta, scale)
+        return o[..., :V]
     return _ChunkKDAPrecumsumFunction.apply(q, k, v, g_cumsum, beta, scale)
 
 
 def _validate_chunk_kda_inputs(q, k, v, g_cumsum, beta, scale):
     """The reference's checks and messages (iso_kdn_chunk.py:2257-2285) plus
-    the kernels' K = V = 128; returns the scale (K^-0.5 when None)."""
+    the kernels' K, V <= 128; returns the scale (K^-0.5 when None)."""
     if q.ndim != 4 or q.shape != k.shape:
         raise ValueError(f"q and k must share [B,T,H,K], got {tuple(q.shape)} and {tuple(k.shape)}")
     B, T, H, K = q.shape
@@ -265,8 +275,8 @@ def _validate_chunk_kda_inputs(q, k, v, g_cumsum, beta, scale):
         raise ValueError("_chunk_kda_precumsum_paired is CUDA-only")
     if len({x.device for x in tensors}) != 1:
         raise ValueError("all _chunk_kda_precumsum_paired tensors must be on the same CUDA device")
-    if K != 128 or v.shape[-1] != 128:
-        raise ValueError(f"kdn_b200 kernels support K = V = 128, got K={K}, V={v.shape[-1]}")
+    if K > 128 or v.shape[-1] > 128:
+        raise ValueError(f"kdn_b200 kernels support K, V <= 128, got K={K}, V={v.shape[-1]}")
     if scale is None:
         scale = K ** -0.5
     return scale

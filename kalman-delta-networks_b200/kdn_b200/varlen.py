@@ -94,6 +94,11 @@ def _check_packed(name: str, t: torch.Tensor, cu: tuple) -> None:
         raise ValueError(f"{name} must be a packed [1, {cu[-1]}, ...] batch to match cu_seqlens")
 
 
+def _check_width(*tensors: torch.Tensor) -> None:
+    if any(t.shape[-1] != 128 for t in tensors):
+        raise ValueError("packed batches run K = V = 128")
+
+
 class _DiagGainVarlenFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, k, alpha, omega, r, initial_precision, omega_raw, r_raw, vp):
@@ -153,6 +158,7 @@ def chunk_kalman_varlen(q_memory, k_memory, kappa, v, g_cumsum, scale: float, cu
     """``chunk_kalman`` over a packed batch (fp32 output [1, T, H, V]); the
     gate prefix restarts every 32 tokens from each sequence's first token."""
     diag_kdn_chunk._validate_diag_kdn_memory_inputs(q_memory, k_memory, kappa, v, g_cumsum, scale)
+    _check_width(q_memory, v)
     vp = plan(cu_seqlens, q_memory.device)
     _check_packed("q_memory", q_memory, vp.cu)
     return _DiagMemoryVarlenFunction.apply(q_memory, k_memory, kappa, v, g_cumsum, scale, vp)
@@ -183,6 +189,7 @@ def chunk_kda_precumsum_varlen(q, k, v, g_cumsum, beta, scale: float | None = No
     """``_chunk_kda_precumsum_paired`` over a packed batch; the 64-local gate
     prefix restarts at every sequence's first token."""
     scale = iso_kdn_chunk._validate_chunk_kda_inputs(q, k, v, g_cumsum, beta, scale)
+    _check_width(q, v)
     vp = plan(cu_seqlens, q.device)
     _check_packed("q", q, vp.cu)
     return _IsoMemoryVarlenFunction.apply(q, k, v, g_cumsum, beta, scale, vp)

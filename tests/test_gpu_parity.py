@@ -208,6 +208,35 @@ def test_diag_scan(precision, B, T, H, decay):
     check(o, grads, ref, ("q", "k", "kappa", "v", "g_cumsum"), tol, ftol)
 
 
+# Narrower heads than the kernels' 128 channels (the reference's diagonal
+# scan takes K = V in {64, 128}, its isotropic one K <= 256): the operators
+# run them zero-padded to 128 and slice the results.
+@pytest.mark.parametrize("precision", ["fp32", "bf16"], indirect=True)
+@pytest.mark.parametrize("K,V", [(64, 64), (64, 128), (128, 64), (96, 32)])
+def test_iso_scan_narrow_heads(precision, K, V):
+    d = oracle.make_iso_inputs(1, 150, 2, K=K, V=V, seed=K + V)
+    ref = oracle.scan_grads("iso", {n: d[n] for n in ("q", "k", "v", "g_cumsum", "beta")}, d["dO"])
+    o, grads = run_iso(d, d["dO"])
+    assert o.shape == (1, 150, 2, V)
+    tol, ftol = TOL[precision]
+    check(o, grads, ref, ("q", "k", "v", "g_cumsum", "beta"), tol, ftol)
+
+
+@pytest.mark.parametrize("precision", ["fp32", "bf16"], indirect=True)
+def test_diag_scan_k64(precision):
+    d = oracle.make_diag_inputs(1, 150, 2, K=64, V=64, seed=64)
+    d["dO"] = d["dO"].bfloat16().float()
+    kappa = oracle.diag_gain(d["k_gain"].double(), d["alpha"].double(), d["omega"].double(), d["r"].double(),
+                             d["initial_precision"].double())[0].float()
+    scale = 64 ** -0.5
+    ref = oracle.scan_grads("diag", {"q": d["q"], "k": d["k"], "kappa": kappa, "v": d["v"], "g_cumsum": d["g_cumsum"]},
+                            d["dO"], scale=scale)
+    o, grads = run_diag(d, d["dO"], kappa, scale)
+    assert o.shape == (1, 150, 2, 64)
+    tol, ftol = TOL[precision]
+    check(o, grads, ref, ("q", "k", "kappa", "v", "g_cumsum"), tol, ftol)
+
+
 # Longer sequences (17 to 66 chunks): the sequential passes' multi-stage
 # pipelines wrap around their stage rings several times.
 @pytest.mark.parametrize("precision", ["bf16"], indirect=True)
