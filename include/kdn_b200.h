@@ -177,6 +177,45 @@ int kdn_iso_gain_bwd(const float* a, const float* omega, const float* r,
                      int64_t B, int64_t T, int64_t H, float posterior_scale,
                      void* workspace, size_t workspace_bytes,
                      kdn_stream_t stream);
+/* The isotropic gain in two phases each way, for sequence parallelism (no
+ * counterpart in the reference): the covariance recursion of a (b, h) stream
+ * is a composition of scalar Moebius maps p -> (A p + B) / (C p + D), its
+ * adjoint one of affine maps lambda -> A lambda + B, so a rank summarises
+ * its segment before the covariance (or its cotangent) entering it is known:
+ *   kdn_iso_gain_fwd_maps    the segment maps into the workspace and their
+ *                            composition total_map (fp32 [B,H,4], scaled to
+ *                            max |.| = 1);
+ *   kdn_iso_gain_fwd_finish  completes kdn_iso_gain_fwd from those maps (same
+ *                            workspace, untouched in between);
+ *   kdn_iso_gain_bwd_maps    the adjoint maps and their composition
+ *                            total_adjoint (fp32 [B,H,2]: d_initial_cov =
+ *                            A d_final_cov + B);
+ *   kdn_iso_gain_bwd_finish  completes kdn_iso_gain_bwd from those maps.
+ * kdn_iso_gain_fwd = fwd_maps + fwd_finish, kdn_iso_gain_bwd = bwd_maps +
+ * bwd_finish (without the totals); arguments as there, T > 0. */
+int kdn_iso_gain_fwd_maps(const float* a, const float* omega, const float* r,
+                          float* total_map, int64_t B, int64_t T, int64_t H,
+                          float posterior_scale, void* workspace,
+                          size_t workspace_bytes, kdn_stream_t stream);
+int kdn_iso_gain_fwd_finish(const float* a, const float* omega, const float* r,
+                            const float* initial_precision,
+                            const float* initial_cov, float* gain, float* p_prev,
+                            float* p_final, int64_t B, int64_t T, int64_t H,
+                            float posterior_scale, void* workspace,
+                            size_t workspace_bytes, kdn_stream_t stream);
+int kdn_iso_gain_bwd_maps(const float* a, const float* omega, const float* r,
+                          const float* dgain, const float* p_prev,
+                          float* total_adjoint, int64_t B, int64_t T, int64_t H,
+                          float posterior_scale, void* workspace,
+                          size_t workspace_bytes, kdn_stream_t stream);
+int kdn_iso_gain_bwd_finish(const float* a, const float* omega, const float* r,
+                            const float* initial_precision,
+                            const float* initial_cov, const float* dgain,
+                            const float* p_prev, const float* d_final_cov, float* da,
+                            float* domega, float* dr, float* d_initial_precision,
+                            float* d_initial_cov, int64_t B, int64_t T, int64_t H,
+                            float posterior_scale, void* workspace,
+                            size_t workspace_bytes, kdn_stream_t stream);
 /* The isotropic gain over a packed batch (kdn_varlen_plan): rows [1,T,H];
  * sequence i runs its own covariance stream from 1/initial_precision (or its
  * initial_cov row); initial_cov, p_final, d_final_cov, d_initial_cov are per

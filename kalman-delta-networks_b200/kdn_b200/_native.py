@@ -84,6 +84,10 @@ _SIGNATURES = {
         [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _F, _P, _SZ, _P],
         ctypes.c_int,
     ),
+    "kdn_iso_gain_fwd_maps": ([_P, _P, _P, _P, _I64, _I64, _I64, _F, _P, _SZ, _P], ctypes.c_int),
+    "kdn_iso_gain_fwd_finish": ([_P] * 8 + [_I64, _I64, _I64, _F, _P, _SZ, _P], ctypes.c_int),
+    "kdn_iso_gain_bwd_maps": ([_P] * 6 + [_I64, _I64, _I64, _F, _P, _SZ, _P], ctypes.c_int),
+    "kdn_iso_gain_bwd_finish": ([_P] * 13 + [_I64, _I64, _I64, _F, _P, _SZ, _P], ctypes.c_int),
     "kdn_iso_gain_varlen_workspace_bytes": ([_I64, _I64, _I64], _SZ),
     "kdn_iso_gain_fwd_varlen": ([_P] * 8 + [_I64, _I64, _F, _P, _I64, _I64, _P, _SZ, _P], ctypes.c_int),
     "kdn_iso_gain_bwd_varlen": ([_P] * 13 + [_I64, _I64, _F, _P, _I64, _I64, _P, _SZ, _P], ctypes.c_int),

@@ -298,6 +298,27 @@ __global__ void __launch_bounds__(32 * kIsoWarps) iso_gain_bwd_apply_kernel(
   }
 }
 
+// The whole segment's map per (b, h) from the block totals of a maps launch
+// (sequence parallelism): forward M_{n-1} o ... o M_0 as (A, B, C, D);
+// backward (A, B) with lambda_in = A lambda_end + B, composed from the last
+// block down, the order of the apply kernels.
+__global__ void iso_gain_fwd_total_kernel(IsoWs ws, float4* __restrict__ total, int nblk, int B, int H) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= B * H) return;
+  const int b = i / H, h = i - b * H;
+  Mob m{1.f, 0.f, 0.f, 1.f};
+  for (int k = 0; k < nblk; ++k) m = mob_mul(as_mob(ws.tot[((size_t)b * nblk + k) * H + h]), m);
+  total[i] = make_float4(m.A, m.B, m.C, m.D);
+}
+__global__ void iso_gain_bwd_total_kernel(IsoWs ws, float2* __restrict__ total, int nblk, int B, int H) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= B * H) return;
+  const int b = i / H, h = i - b * H;
+  Aff f{1.f, 0.f};
+  for (int k = nblk - 1; k >= 0; --k) f = aff_after(as_aff(ws.tot[((size_t)b * nblk + k) * H + h]), f);
+  total[i] = make_float2(f.A, f.B);
+}
+
 // Host side: workspace size and launch grid.
 size_t iso_ws_bytes(int64_t B, int64_t T, int64_t H) {
   if (B <= 0 || T <= 0 || H <= 0) return 0;
@@ -694,16 +715,27 @@ namespace {
 // Launches of the isotropic gain over B streams of the [.,T,H] rows: a
 // fixed-length batch (tok = null, stream b = rows b*T ..) or a packed batch
 // (tok = the sequences' token offsets, B = their count, Tgrid = the longest).
+// phases: kIsoMaps (the segment maps, and their composition into `total`
+// when given), kIsoFinish (the apply pass from the maps in the workspace).
+constexpr int kIsoMaps = 1, kIsoFinish = 2, kIsoAll = 3;
+
 int iso_fwd(const char* what, const float* a, const float* omega, const float* r, const float* init_prec,
             const float* init_cov, float* gain, float* p_prev, float* p_final, int64_t B, int64_t T, int64_t Tgrid,
-            int64_t H, float s, const int* tok, void* workspace, size_t workspace_bytes, cudaStream_t st) {
+            int64_t H, float s, const int* tok, void* workspace, size_t workspace_bytes, cudaStream_t st,
+            int phases = kIsoAll, float* total = nullptr) {
   dim3 grid;
   if (int rc = iso_grid(what, B, Tgrid, H, workspace, workspace_bytes, &grid)) return rc;
   const IsoWs ws = iso_ws(workspace, (int)B, (int)grid.x, (int)H);
-  if (Tgrid > 0) {
+  if ((phases & kIsoMaps) && Tgrid > 0) {
     iso_gain_fwd_maps_kernel<<<grid, 32 * kIsoWarps, 0, st>>>(a, omega, r, ws, (int)T, (int)H, s, tok);
     if (int rc = check_launch("iso_gain_fwd_maps_kernel")) return rc;
+    if (total) {
+      iso_gain_fwd_total_kernel<<<(unsigned)((B * H + 127) / 128), 128, 0, st>>>(
+          ws, reinterpret_cast<float4*>(total), (int)grid.x, (int)B, (int)H);
+      if (int rc = check_launch("iso_gain_fwd_total_kernel")) return rc;
+    }
   }
+  if (!(phases & kIsoFinish)) return KDN_OK;
   iso_gain_fwd_apply_kernel<<<grid, 32 * kIsoWarps, 0, st>>>(a, omega, r, init_prec, init_cov, ws, gain, p_prev,
                                                             p_final, (int)T, (int)H, s, tok);
   return check_launch("iso_gain_fwd_apply_kernel");
@@ -712,15 +744,22 @@ int iso_fwd(const char* what, const float* a, const float* omega, const float* r
 int iso_bwd(const char* what, const float* a, const float* omega, const float* r, const float* init_prec,
             const float* init_cov, const float* dgain, const float* p_prev, const float* d_final_cov, float* da,
             float* domega, float* dr, float* dinit, float* d_init_cov, int64_t B, int64_t T, int64_t Tgrid, int64_t H,
-            float s, const int* tok, void* workspace, size_t workspace_bytes, cudaStream_t st) {
+            float s, const int* tok, void* workspace, size_t workspace_bytes, cudaStream_t st, int phases = kIsoAll,
+            float* total = nullptr) {
   dim3 grid;
   if (int rc = iso_grid(what, B, Tgrid, H, workspace, workspace_bytes, &grid)) return rc;
   const IsoWs ws = iso_ws(workspace, (int)B, (int)grid.x, (int)H);
-  if (cudaMemsetAsync(dinit, 0, sizeof(float) * H, st) != cudaSuccess) return check_launch("memset d_initial_precision");
-  if (Tgrid > 0) {
+  if ((phases & kIsoMaps) && Tgrid > 0) {
     iso_gain_bwd_maps_kernel<<<grid, 32 * kIsoWarps, 0, st>>>(a, omega, r, dgain, p_prev, ws, (int)T, (int)H, s, tok);
     if (int rc = check_launch("iso_gain_bwd_maps_kernel")) return rc;
+    if (total) {
+      iso_gain_bwd_total_kernel<<<(unsigned)((B * H + 127) / 128), 128, 0, st>>>(
+          ws, reinterpret_cast<float2*>(total), (int)grid.x, (int)B, (int)H);
+      if (int rc = check_launch("iso_gain_bwd_total_kernel")) return rc;
+    }
   }
+  if (!(phases & kIsoFinish)) return KDN_OK;
+  if (cudaMemsetAsync(dinit, 0, sizeof(float) * H, st) != cudaSuccess) return check_launch("memset d_initial_precision");
   iso_gain_bwd_apply_kernel<<<grid, 32 * kIsoWarps, 0, st>>>(a, omega, r, init_prec, dgain, p_prev, d_final_cov,
                                                             init_cov != nullptr, d_init_cov, ws, da, domega, dr,
                                                             dinit, (int)T, (int)H, s, tok);
@@ -749,6 +788,45 @@ int kdn_iso_gain_bwd(const float* a, const float* omega, const float* r, const f
     return set_error(KDN_ERR_INVALID, "kdn_iso_gain_bwd: invalid arguments");
   return iso_bwd("kdn_iso_gain_bwd", a, omega, r, init_prec, init_cov, dgain, p_prev, d_final_cov, da, domega, dr,
                  dinit, d_init_cov, B, T, T, H, s, nullptr, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+int kdn_iso_gain_fwd_maps(const float* a, const float* omega, const float* r, float* total_map, int64_t B, int64_t T,
+                          int64_t H, float s, void* workspace, size_t workspace_bytes, kdn_stream_t stream) {
+  if (B <= 0 || H <= 0 || T <= 0 || !a || !omega || !r || !total_map)
+    return set_error(KDN_ERR_INVALID, "kdn_iso_gain_fwd_maps: invalid arguments");
+  return iso_fwd("kdn_iso_gain_fwd_maps", a, omega, r, nullptr, nullptr, nullptr, nullptr, nullptr, B, T, T, H, s,
+                 nullptr, workspace, workspace_bytes, (cudaStream_t)stream, kIsoMaps, total_map);
+}
+
+int kdn_iso_gain_fwd_finish(const float* a, const float* omega, const float* r, const float* init_prec,
+                            const float* init_cov, float* gain, float* p_prev, float* p_final, int64_t B, int64_t T,
+                            int64_t H, float s, void* workspace, size_t workspace_bytes, kdn_stream_t stream) {
+  if (B <= 0 || H <= 0 || T <= 0 || !a || !omega || !r || !init_prec || !gain)
+    return set_error(KDN_ERR_INVALID, "kdn_iso_gain_fwd_finish: invalid arguments");
+  return iso_fwd("kdn_iso_gain_fwd_finish", a, omega, r, init_prec, init_cov, gain, p_prev, p_final, B, T, T, H, s,
+                 nullptr, workspace, workspace_bytes, (cudaStream_t)stream, kIsoFinish);
+}
+
+int kdn_iso_gain_bwd_maps(const float* a, const float* omega, const float* r, const float* dgain, const float* p_prev,
+                          float* total_adjoint, int64_t B, int64_t T, int64_t H, float s, void* workspace,
+                          size_t workspace_bytes, kdn_stream_t stream) {
+  if (B <= 0 || H <= 0 || T <= 0 || !a || !omega || !r || !dgain || !p_prev || !total_adjoint)
+    return set_error(KDN_ERR_INVALID, "kdn_iso_gain_bwd_maps: invalid arguments");
+  return iso_bwd("kdn_iso_gain_bwd_maps", a, omega, r, nullptr, nullptr, dgain, p_prev, nullptr, nullptr, nullptr,
+                 nullptr, nullptr, nullptr, B, T, T, H, s, nullptr, workspace, workspace_bytes, (cudaStream_t)stream,
+                 kIsoMaps, total_adjoint);
+}
+
+int kdn_iso_gain_bwd_finish(const float* a, const float* omega, const float* r, const float* init_prec,
+                            const float* init_cov, const float* dgain, const float* p_prev, const float* d_final_cov,
+                            float* da, float* domega, float* dr, float* dinit, float* d_init_cov, int64_t B, int64_t T,
+                            int64_t H, float s, void* workspace, size_t workspace_bytes, kdn_stream_t stream) {
+  if (B <= 0 || H <= 0 || T <= 0 || !a || !omega || !r || !init_prec || !dgain || !p_prev || !da || !domega ||
+      !dr || !dinit)
+    return set_error(KDN_ERR_INVALID, "kdn_iso_gain_bwd_finish: invalid arguments");
+  return iso_bwd("kdn_iso_gain_bwd_finish", a, omega, r, init_prec, init_cov, dgain, p_prev, d_final_cov, da, domega,
+                 dr, dinit, d_init_cov, B, T, T, H, s, nullptr, workspace, workspace_bytes, (cudaStream_t)stream,
+                 kIsoFinish);
 }
 
 size_t kdn_iso_gain_varlen_workspace_bytes(int64_t num_seqs, int64_t max_seq_len, int64_t H) {

@@ -459,9 +459,125 @@ class DiagSegmentB200:
         return dk_gain, dalpha, domega_raw, dr_raw, dprior
 
 
-def diag_two_pass_forward(seg, comm):
-    """Forward of one rank's segment: returns o (fp32 [B, T_r, H, V]) and the
-    gathered state maps the backward needs."""
+class IsoSegmentB200:
+    """One rank's segment of the isotropic KDN on the B200 kernels, pass by
+    pass (the C ABI's split gain phases and partial scan modes); the same
+    interface as DiagSegmentB200 with a scalar covariance per (b, h).  Inputs
+    are this rank's [B, T_r, H, *] slices (q, k, v bf16; g_cumsum fp32
+    64-local; a, omega, r fp32 [B, T_r, H]); ``prior`` is the per-head initial
+    precision."""
+
+    def __init__(self, q, k, v, g_cumsum, a, omega, r, prior, scale, posterior_scale=1.0):
+        N.require_cuda(q, k, v, g_cumsum, a, omega, r, prior)
+        self.t = dict(q=q, k=k, v=v, g=g_cumsum, a=a, omega=omega, r=r, prior=prior)
+        self.B, self.T, self.H, self.K = q.shape
+        self.scale, self.s = float(scale), float(posterior_scale)
+        self.lib = N.load_library()
+        self.dev = q.device
+        self.stream = N.stream_of(q)
+        self.gain_ws = N.byte_buffer(self.lib.kdn_iso_gain_workspace_bytes(self.B, self.T, self.H), self.dev)
+
+    def _f32(self, *shape):
+        return torch.empty(*shape, dtype=torch.float32, device=self.dev)
+
+    def _gain_in(self):
+        t = self.t
+        return t["a"].data_ptr(), t["omega"].data_ptr(), t["r"].data_ptr()
+
+    def prior_covariance(self):
+        return (1.0 / self.t["prior"]).view(1, self.H).expand(self.B, self.H).contiguous()
+
+    def S_end_template(self):
+        return self._f32(self.B, self.H, self.K, self.t["v"].shape[-1])
+
+    def cotangent(self, dO):
+        """The isotropic scan's cotangent is bf16, like its output."""
+        return dO.to(torch.bfloat16).contiguous()
+
+    # covariance, forward
+    def gain_maps(self):
+        total = self._f32(self.B, self.H, 4)
+        N.check(self.lib.kdn_iso_gain_fwd_maps(*self._gain_in(), total.data_ptr(), self.B, self.T, self.H, self.s,
+                                               self.gain_ws.data_ptr(), self.gain_ws.numel(), self.stream),
+                "kdn_iso_gain_fwd_maps")
+        return total
+
+    def gain_finish(self, p_in):
+        self.p_in = None if p_in is None else p_in.contiguous()
+        self.beta = self._f32(self.B, self.T, self.H)
+        self.p_prev = self._f32(self.B, self.T, self.H)
+        N.check(self.lib.kdn_iso_gain_fwd_finish(*self._gain_in(), self.t["prior"].data_ptr(), N.ptr(self.p_in),
+                                                 self.beta.data_ptr(), self.p_prev.data_ptr(), None, self.B, self.T,
+                                                 self.H, self.s, self.gain_ws.data_ptr(), self.gain_ws.numel(),
+                                                 self.stream), "kdn_iso_gain_fwd_finish")
+
+    # memory, forward
+    def _args(self, mode):
+        t = self.t
+        a = _scan._args(N.KDN_ISO, N.KDN_PREC_BF16, t["q"], t["v"], self.scale)
+        a.mode = mode
+        a.q, a.k, a.v, a.g = t["q"].data_ptr(), t["k"].data_ptr(), t["v"].data_ptr(), t["g"].data_ptr()
+        a.beta = self.beta.data_ptr()
+        return a
+
+    def scan_summary(self):
+        return DiagSegmentB200.scan_summary(self)
+
+    def scan_sequential(self, S_in):
+        a = self._args(N.KDN_SCAN_FWD_SEQUENTIAL)
+        o = torch.empty(self.B, self.T, self.H, self.t["v"].shape[-1], dtype=torch.bfloat16, device=self.dev)
+        self.S_in = None if S_in is None else S_in.contiguous()
+        a.saved, a.o, a.initial_state = self.saved.data_ptr(), o.data_ptr(), N.ptr(self.S_in)
+        N.check(self.lib.kdn_scan_fwd(ctypes.byref(a), self.stream), "kdn_scan_fwd (sequential)")
+        _scan.check_status(self.saved, "kdn_scan_fwd (sequential)")
+        return o
+
+    # memory, backward
+    def scan_adjoint_summary(self, dO):
+        return DiagSegmentB200.scan_adjoint_summary(self, dO)
+
+    def scan_backward(self, dO, dS_end):
+        t = self.t
+        a = self._args(N.KDN_SCAN_FULL)
+        ws = N.byte_buffer(self.lib.kdn_scan_workspace_bytes(ctypes.byref(a)), self.dev)
+        dq, dk, dv = (torch.empty_like(t[n]) for n in ("q", "k", "v"))
+        dg, dbeta = torch.empty_like(t["g"]), torch.empty_like(self.beta)
+        dS_end = None if dS_end is None else dS_end.contiguous()
+        a.saved, a.dO, a.d_final_state = self.saved.data_ptr(), dO.data_ptr(), N.ptr(dS_end)
+        a.dq, a.dk, a.dv, a.dg, a.dbeta = dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dg.data_ptr(), dbeta.data_ptr()
+        a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+        N.check(self.lib.kdn_scan_bwd(ctypes.byref(a), self.stream), "kdn_scan_bwd")
+        _scan.check_status(ws, "kdn_scan_bwd")
+        self.dbeta = dbeta
+        return dq, dk, dv, dg
+
+    # covariance, backward
+    def gain_adjoint_summary(self):
+        total = self._f32(self.B, self.H, 2)
+        self.gain_bws = N.byte_buffer(self.lib.kdn_iso_gain_workspace_bytes(self.B, self.T, self.H), self.dev)
+        N.check(self.lib.kdn_iso_gain_bwd_maps(*self._gain_in(), self.dbeta.data_ptr(), self.p_prev.data_ptr(),
+                                               total.data_ptr(), self.B, self.T, self.H, self.s,
+                                               self.gain_bws.data_ptr(), self.gain_bws.numel(), self.stream),
+                "kdn_iso_gain_bwd_maps")
+        return total
+
+    def gain_backward(self, lam_end):
+        t = self.t
+        da, domega, dr = (torch.empty_like(t[n]) for n in ("a", "omega", "r"))
+        dprior = self._f32(self.H)
+        lam_end = None if lam_end is None else lam_end.contiguous()
+        N.check(self.lib.kdn_iso_gain_bwd_finish(
+            *self._gain_in(), t["prior"].data_ptr(), N.ptr(self.p_in), self.dbeta.data_ptr(), self.p_prev.data_ptr(),
+            N.ptr(lam_end), da.data_ptr(), domega.data_ptr(), dr.data_ptr(), dprior.data_ptr(), None, self.B, self.T,
+            self.H, self.s, self.gain_bws.data_ptr(), self.gain_bws.numel(), self.stream), "kdn_iso_gain_bwd_finish")
+        if self.p_in is not None:  # the prior reaches this segment only through the carried covariance
+            dprior.zero_()
+        return da, domega, dr, dprior
+
+
+def two_pass_forward(seg, comm):
+    """Forward of one rank's segment (diagonal or isotropic segment object):
+    returns o and the gathered state maps the backward needs."""
     rank = comm.rank
     maps = comm.all_gather(seg.gain_maps())
     seg.gain_finish(None if rank == 0 else carried_covariance(maps, seg.prior_covariance(), rank))
@@ -475,10 +591,11 @@ def diag_two_pass_forward(seg, comm):
     return o, phis
 
 
-def diag_two_pass_backward(seg, comm, phis, dO):
-    """Backward of one rank's segment: returns (dq, dk, dv, dg, dk_gain,
-    dalpha, domega_raw, dr_raw, dprior); dprior is nonzero on rank 0 only
-    (sum it over ranks like any parameter gradient)."""
+def two_pass_backward(seg, comm, phis, dO):
+    """Backward of one rank's segment: returns (dq, dk, dv, dg) followed by
+    the segment's gain gradients (diagonal: dk_gain, dalpha, domega_raw,
+    dr_raw, dprior; isotropic: da, domega, dr, dprior); dprior is nonzero on
+    rank 0 only (sum it over ranks like any parameter gradient)."""
     rank = comm.rank
     dO = seg.cotangent(dO)
     # rank 0's own summaries are needed by no one: it sends zeros of their shapes
@@ -487,8 +604,12 @@ def diag_two_pass_backward(seg, comm, phis, dO):
     dq, dk, dv, dg = seg.scan_backward(dO, carried_state_adjoint(phis, cs, rank))
     adj = seg.gain_adjoint_summary()  # rank 0 needs its segment maps for the finish all the same
     adjs = comm.all_gather(adj if rank > 0 else torch.zeros_like(adj))
-    dk_gain, dalpha, domega_raw, dr_raw, dprior = seg.gain_backward(carried_covariance_adjoint(adjs, rank))
-    return dq, dk, dv, dg, dk_gain, dalpha, domega_raw, dr_raw, dprior
+    return (dq, dk, dv, dg) + tuple(seg.gain_backward(carried_covariance_adjoint(adjs, rank)))
+
+
+# the diagonal names of the drivers
+diag_two_pass_forward = two_pass_forward
+diag_two_pass_backward = two_pass_backward
 
 
 class _DiagTwoPass(torch.autograd.Function):
@@ -524,3 +645,40 @@ def sp_diag_kdn_two_pass(q, k, v, g_cumsum, k_gain, alpha, omega, r, initial_pre
     cont = [t.contiguous() for t in (q, k, v, g_cumsum, k_gain, alpha, omega.detach(), r.detach(),
                                       initial_precision, omega_raw, r_raw)]
     return _DiagTwoPass.apply(comm, scale, *cont)
+
+
+class _IsoTwoPass(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, comm, scale, posterior_scale, q, k, v, g_cumsum, a, omega, r, prior):
+        seg = IsoSegmentB200(q, k, v, g_cumsum, a, omega, r, prior, scale, posterior_scale)
+        o, phis = two_pass_forward(seg, comm)
+        ctx.state = (seg, comm, phis)
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        seg, comm, phis = ctx.state
+        if do is None:
+            do = torch.zeros(seg.B, seg.T, seg.H, seg.K, dtype=torch.bfloat16, device=seg.dev)
+        dq, dk, dv, dg, da, domega, dr, dprior = two_pass_backward(seg, comm, phis, do)
+        del ctx.state
+        return None, None, None, dq, dk, dv, dg, da, domega, dr, dprior
+
+
+def sp_iso_kdn_two_pass(q, k, v, g_cumsum, a, omega, r, initial_precision, *, group=None, comm=None, head_dim=128,
+                        info_scale=None, scale=None):
+    """This rank's output (bf16) of the sequence-parallel isotropic KDN
+    (``iso_kdn_gain`` + ``_chunk_kda_precumsum_paired``), every rank working
+    at once (the two passes above with a scalar covariance per (b, h)).
+    Inputs are this rank's contiguous time slice, a multiple of 64 tokens
+    except on the last rank; q, k, v bf16 with K = V = 128; bf16 precision
+    only.  ``initial_precision`` receives its gradient on rank 0 (sum
+    parameter gradients over ranks)."""
+    comm = GroupComm(group) if comm is None else comm
+    scale = q.shape[-1] ** -0.5 if scale is None else float(scale)
+    posterior_scale = (float(head_dim) if info_scale is None else float(info_scale)) / float(head_dim)
+    if N.precision() != N.KDN_PREC_BF16:
+        raise ValueError("the two-pass sequence-parallel scan runs the bf16 tensor-core kernels only")
+    cont = [t.contiguous() for t in (q.to(torch.bfloat16), k.to(torch.bfloat16), v.to(torch.bfloat16), g_cumsum,
+                                      a.float(), omega.float(), r.float(), initial_precision.float())]
+    return _IsoTwoPass.apply(comm, scale, posterior_scale, *cont)

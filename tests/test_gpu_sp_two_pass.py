@@ -15,7 +15,7 @@ import pytest
 import torch
 
 import oracle
-from kdn_b200.sequence_parallel import DiagSegmentB200, diag_two_pass_backward, diag_two_pass_forward
+from kdn_b200.sequence_parallel import DiagSegmentB200, IsoSegmentB200, diag_two_pass_backward, diag_two_pass_forward
 
 from test_gpu_parity import BF16_FTOL, BF16_TOL, check_errors
 
@@ -39,17 +39,27 @@ class ThreadComm:
         return out
 
 
-def run_ranks(world, d, seg_len):
+def diag_segment(d, sl):
+    t = {n: d[n][:, sl].contiguous().to(DEV) for n in
+         ("q", "k", "v", "g_cumsum", "k_gain", "alpha", "omega", "r", "omega_raw", "r_raw")}
+    return DiagSegmentB200(t["q"], t["k"], t["v"], t["g_cumsum"], t["k_gain"], t["alpha"], t["omega"], t["r"],
+                           d["initial_precision"].to(DEV), t["omega_raw"], t["r_raw"], K ** -0.5)
+
+
+def iso_segment(d, sl):
+    t = {n: d[n][:, sl].contiguous().to(DEV) for n in ("q", "k", "v", "g_cumsum", "a", "omega", "r")}
+    return IsoSegmentB200(t["q"], t["k"], t["v"], t["g_cumsum"], t["a"], t["omega"], t["r"],
+                          d["initial_precision"].to(DEV), K ** -0.5, 1.0)
+
+
+def run_ranks(world, d, seg_len, make_segment=diag_segment):
     shared = {"slots": [None] * world, "barrier": threading.Barrier(world, timeout=120)}
     results, errors = [None] * world, []
 
     def rank_main(rank):
         try:
             sl = slice(rank * seg_len, (rank + 1) * seg_len)
-            t = {n: d[n][:, sl].contiguous().to(DEV) for n in
-                 ("q", "k", "v", "g_cumsum", "k_gain", "alpha", "omega", "r", "omega_raw", "r_raw")}
-            seg = DiagSegmentB200(t["q"], t["k"], t["v"], t["g_cumsum"], t["k_gain"], t["alpha"], t["omega"], t["r"],
-                                  d["initial_precision"].to(DEV), t["omega_raw"], t["r_raw"], K ** -0.5)
+            seg = make_segment(d, sl)
             comm = ThreadComm(rank, world, shared)
             o, phis = diag_two_pass_forward(seg, comm)
             grads = diag_two_pass_backward(seg, comm, phis, d["dO"][:, sl].to(DEV))
@@ -95,3 +105,31 @@ def test_two_pass_on_b200_matches_oracle(world, seg_len):
         ref["d" + n] = L[n].grad
     check_errors(f"sp_two_pass_world{world}", got, ref, {"dq", "dk", "dv", "domega_raw", "dr_raw"}, BF16_TOL,
                  BF16_FTOL)
+
+
+@pytest.mark.parametrize("world,seg_len", [(2, 320), (3, 192)])
+def test_iso_two_pass_on_b200_matches_oracle(world, seg_len):
+    """The isotropic segments (split scalar gain phases, the same scan modes)."""
+    T, H = world * seg_len, 2
+    d = oracle.make_iso_inputs(1, T, H, seed=world + 50, dtype=torch.bfloat16)
+    d["initial_precision"] = torch.tensor([1.0, 0.7])
+    parts = run_ranks(world, d, seg_len, iso_segment)
+    names = ("dq", "dk", "dv", "dg", "da", "domega", "dr")
+    got = {"o": torch.cat([p[0] for p in parts], 1)}
+    for i, n in enumerate(names):
+        got[n] = torch.cat([p[1][i] for p in parts], 1)
+    got["dprior"] = sum(p[1][7] for p in parts)
+
+    L = {n: d[n].double().clone().requires_grad_(True) for n in ("q", "k", "v", "a", "omega", "r")}
+    P = d["initial_precision"].double().clone().requires_grad_(True)
+    G = (d["g_cumsum"].double() * oracle.LN2).requires_grad_(True)
+    beta, _, _ = oracle.iso_gain(L["a"], L["omega"], L["r"], P, 1.0)
+    qh, kh = oracle.l2norm(L["q"]), oracle.l2norm(L["k"])
+    S0 = torch.zeros(1, H, K, K, dtype=torch.float64)
+    o, _ = oracle.memory_recurrence(qh, kh, L["v"], oracle.alpha_from_g_cumsum(G, 64), beta[..., None] * kh, S0,
+                                    K ** -0.5)
+    (o * d["dO"].double()).sum().backward()
+    ref = {"o": o.detach(), "dg": G.grad, "dprior": P.grad}
+    for n in ("q", "k", "v", "a", "omega", "r"):
+        ref["d" + n] = L[n].grad
+    check_errors(f"sp_iso_two_pass_world{world}", got, ref, {"o", "dq", "dk", "dv"}, BF16_TOL, BF16_FTOL)

@@ -99,6 +99,70 @@ def test_two_pass_matches_full_sequence(world, tmp_path):
     assert not bad, errs
 
 
+ISO_NAMES = ("q", "k", "v", "g", "a", "omega", "r")
+
+
+def make_iso_inputs(T):
+    gen = torch.Generator().manual_seed(12)
+    sp = torch.nn.functional.softplus
+    n = lambda *s: torch.randn(*s, generator=gen, dtype=torch.float64)  # noqa: E731
+    la = -sp(n(B, T, H, K))
+    return {"q": n(B, T, H, K), "k": n(B, T, H, K), "v": n(B, T, H, V), "g": oracle.g_cumsum_from_log_alpha(la, 64),
+            "a": torch.exp(2 * la).mean(-1), "omega": sp(n(B, T, H)), "r": 0.01 + sp(n(B, T, H)),
+            "prior": 0.5 + torch.rand(H, generator=gen, dtype=torch.float64), "dO": n(B, T, H, V)}
+
+
+def _iso_worker(rank, world, port, out_dir):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from kdn_b200.sequence_parallel import GroupComm, two_pass_backward, two_pass_forward
+    from sp_oracle_segment import IsoSegmentOracle
+
+    x = make_iso_inputs(world * SEG)
+    sl = slice(rank * SEG, (rank + 1) * SEG)
+    s = {n: x[n][:, sl] for n in ISO_NAMES}
+    seg = IsoSegmentOracle(s["q"], s["k"], s["v"], s["g"], s["a"], s["omega"], s["r"], x["prior"], K ** -0.5, 0.5)
+    comm = GroupComm()
+    o, phis = two_pass_forward(seg, comm)
+    grads = two_pass_backward(seg, comm, phis, x["dO"][:, sl])
+    torch.save({"o": o, **dict(zip(("dq", "dk", "dv", "dg", "da", "domega", "dr", "dprior"), grads))},
+               os.path.join(out_dir, f"rank{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def iso_full_reference(x):
+    L = {n: x[n].clone().requires_grad_(True) for n in ISO_NAMES + ("prior",)}
+    beta, _, _ = oracle.iso_gain(L["a"], L["omega"], L["r"], L["prior"], 0.5)
+    G = L["g"] * oracle.LN2
+    G.retain_grad()
+    qh, kh = oracle.l2norm(L["q"]), oracle.l2norm(L["k"])
+    S0 = torch.zeros(B, H, K, V, dtype=torch.float64)
+    o, _ = oracle.memory_recurrence(qh, kh, L["v"], oracle.alpha_from_g_cumsum(G, 64), beta[..., None] * kh, S0,
+                                    K ** -0.5)
+    (o * x["dO"]).sum().backward()
+    ref = {"o": o.detach(), "dg": G.grad, "dprior": L["prior"].grad}
+    ref.update({"d" + n: L[n].grad for n in ISO_NAMES if n != "g"})
+    return ref
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_iso_two_pass_matches_full_sequence(world, tmp_path):
+    """The isotropic two-pass driver (scalar covariance maps, the same state
+    maps) against one oracle graph over the whole sequence."""
+    mp.spawn(_iso_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    x = make_iso_inputs(world * SEG)
+    ref = iso_full_reference(x)
+    parts = [torch.load(tmp_path / f"rank{r}.pt") for r in range(world)]
+    errs = {}
+    for key, full in ref.items():
+        got = sum(p[key] for p in parts) if key == "dprior" else torch.cat([p[key] for p in parts], 1)
+        errs[key] = ((got - full).abs().max() / full.abs().max()).item()
+    bad = {k: v for k, v in errs.items() if not v < (1e-7 if k == "dg" else 1e-9)}
+    assert not bad, errs
+
+
 def test_composition_helpers_match_sequential_evaluation():
     from kdn_b200.sequence_parallel import (carried_covariance, carried_covariance_adjoint, carried_state,
                                             carried_state_adjoint, mobius_apply)
