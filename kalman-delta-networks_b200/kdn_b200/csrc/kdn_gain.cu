@@ -338,39 +338,63 @@ int iso_grid(const char* what, int64_t B, int64_t T, int64_t H, void* ws, size_t
 // ---------------------------------------------------------------------------
 // Diagonal gain
 // ---------------------------------------------------------------------------
-// One channel's inputs for TT consecutive tokens of a segment.  The loads of a
-// tile do not depend on the running covariance, so each kernel issues the next
-// tile before it runs the current one: the memory latency overlaps the
-// sequential chain (one division per token).  Rows past the segment read as
-// neutral values and are skipped by the callers.  Tile sizes (2 to 8 tokens)
-// were chosen by timing at B=4, T=4096, H=18, K=128: larger tiles cost
-// occupancy (registers) and lost more than the deeper prefetch gained.
-template <int K, int TT, bool DK, bool PP = false>
-struct GainTile {
-  // PP: the covariance before each token (p_{t-1}), saved by the forward
-  float k[TT], a[TT], w[TT], r[TT], dk[DK ? TT : 1], pp[PP ? TT : 1];
-  __device__ __forceinline__ void load(const float* __restrict__ kk, const float* __restrict__ al,
-                                       const float* __restrict__ om, const float* __restrict__ rr,
-                                       const float* __restrict__ dkap, size_t row0, int H, int n, int c,
-                                       const float* __restrict__ ppv = nullptr) {
+// The diagonal kernels' inputs for TT consecutive tokens of a segment, staged
+// in shared memory by cp.async: NA per-channel fp32 rows (k, alpha, omega, and
+// in the backward dkappa and p_prev), optionally the bf16 omega_raw rows (WR)
+// and the per-token (D, G) (DG), and r.  NS - 1 tiles are in flight while a
+// CTA runs the sequential chain of the current one, and none of them occupies
+// registers.  Every stage is refilled only after the block barrier that ends
+// the previous use of it.  V16: every row pointer is 16-byte aligned and a
+// thread copies 16 bytes (four channels) at a time; otherwise each thread
+// copies its own channel's 4 bytes (omega_raw is then read where it is used),
+// which is slower (gain backward 0.61 against 0.34 ms at B=4, T=4096, H=18).
+// Tile and stage counts by timing at that shape: backward 8 x 2 (0.334 ms;
+// 4 x 3: 0.347, 4 x 2: 0.343, 2 x 3: 0.356; the register-tile kernels they
+// replaced: 0.494), forward 8 x 2 (0.241 ms; 4 x 3: 0.244, 2 x 4: 0.247,
+// 4 x 2: 0.248; register tiles: 0.269-0.302).
+constexpr int kGainTile = 8, kGainStages = 2;   // backward kernels
+constexpr int kGainTileF = 8, kGainStagesF = 2;  // forward kernels
+template <int K, int TT, int NA, bool WR, bool DG>
+struct alignas(16) GainStage {
+  float row[NA][TT][K];
+  bf16 wr[WR ? TT : 1][K];
+  float2 dg[TT];
+  float r[TT];
+
+  // rows [ts, ts + m) of the segment starting at row0 (row stride H); tok0
+  // indexes (D, G) of the segment's first token
+  template <bool V16>
+  __device__ __forceinline__ void load(const float* const (&src)[NA], const bf16* __restrict__ omega_raw,
+                                       const float* __restrict__ rr, const float2* __restrict__ dg_tok, size_t row0,
+                                       int H, int ts, int m, size_t tok0) {
+    const int c = threadIdx.x;
+    if constexpr (V16) {
+      constexpr int P = K / 4, NP = (TT * P + K - 1) / K;  // 16-byte pieces per fp32 row; per thread
 #pragma unroll
-    for (int j = 0; j < TT; ++j) {
-      if (j < n) {
-        const size_t row = row0 + (size_t)j * H;
-        k[j] = kk[row * K + c];
-        a[j] = al[row * K + c];
-        w[j] = om[row * K + c];
-        r[j] = rr[row];
-        if constexpr (DK) dk[j] = dkap[row * K + c];
-        if constexpr (PP) pp[j] = ppv[row * K + c];
-      } else {
-        k[j] = 0.f;
-        a[j] = 1.f;
-        w[j] = 0.f;
-        r[j] = 1.f;
-        if constexpr (DK) dk[j] = 0.f;
-        if constexpr (PP) pp[j] = 0.f;
+      for (int a = 0; a < NA; ++a)
+#pragma unroll
+        for (int i = 0; i < NP; ++i) {
+          const int e = c + i * K, j = e / P, pc = e - j * P;
+          if (e < TT * P && j < m) cp_async16(&row[a][j][4 * pc], src[a] + (row0 + (size_t)(ts + j) * H) * K + 4 * pc);
+        }
+      if constexpr (WR) {
+        constexpr int PW = K / 8, NW = (TT * PW + K - 1) / K;
+#pragma unroll
+        for (int i = 0; i < NW; ++i) {
+          const int e = c + i * K, j = e / PW, pc = e - j * PW;
+          if (e < TT * PW && j < m) cp_async16(&wr[j][8 * pc], omega_raw + (row0 + (size_t)(ts + j) * H) * K + 8 * pc);
+        }
       }
+    } else {
+#pragma unroll
+      for (int a = 0; a < NA; ++a)
+#pragma unroll
+        for (int j = 0; j < TT; ++j)
+          if (j < m) cp_async4(&row[a][j][c], src[a] + (row0 + (size_t)(ts + j) * H) * K + c);
+    }
+    if (c < m) {
+      cp_async4(&r[c], rr + row0 + (size_t)(ts + c) * H);
+      if constexpr (DG) cp_async8(&dg[c], dg_tok + tok0 + ts + c);
     }
   }
 };
@@ -389,30 +413,44 @@ __device__ __forceinline__ void seg_span(const Varlen& v, int seg, int T, int H,
   }
 }
 
-template <int K>
+// Forward pass A: each segment's composed covariance map.
+template <int K, bool V16>
 __global__ void __launch_bounds__(K) diag_gain_map_kernel(const float* __restrict__ k, const float* __restrict__ alpha,
                                                           const float* __restrict__ omega, const float* __restrict__ r,
                                                           float4* __restrict__ maps, int T, int H, int nseg,
                                                           Varlen v) {
-  constexpr int TT = 4;
+  constexpr int TT = kGainTileF, NS = kGainStagesF;
+  using Stage = GainStage<K, TT, 3, false, false>;
+  __shared__ Stage stg[NS];
   const int seg = blockIdx.x, bh = blockIdx.y, b = bh / H, h = bh - b * H, c = threadIdx.x;
   int t0, n, sh;
   seg_span(v, seg, T, H, bh, t0, n, sh);
   const size_t row0 = ((size_t)b * T + t0) * H + h;
-  GainTile<K, TT, false> cu, nx;
-  nx.load(k, alpha, omega, r, nullptr, row0, H, n, c);
+  const float* const src[3] = {k, alpha, omega};
+  const int ntiles = (n + TT - 1) / TT;
+  auto issue = [&](int it) {
+    if (it < ntiles) stg[it % NS].template load<V16>(src, nullptr, r, nullptr, row0, H, it * TT, min(TT, n - it * TT), 0);
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int i = 0; i < NS - 1; ++i) issue(i);
   Mob m{1.f, 0.f, 0.f, 1.f};
-  for (int ts = 0; ts < n; ts += TT) {
-    cu = nx;
-    if (ts + TT < n) nx.load(k, alpha, omega, r, nullptr, row0 + (size_t)(ts + TT) * H, H, n - ts - TT, c);
+  for (int it = 0; it < ntiles; ++it) {
+    cp_async_wait_group<NS - 2>();
+    __syncthreads();
+    issue(it + NS - 1);
+    const Stage& S = stg[it % NS];
+    const int ts = it * TT;
 #pragma unroll
     for (int j = 0; j < TT; ++j) {
       if (ts + j < n) {
-        const float a2 = cu.a[j] * cu.a[j], u = __fdividef((float)K * cu.k[j] * cu.k[j], cu.r[j]);
-        m = mob_mul(Mob{a2, cu.w[j], u * a2, 1.f + u * cu.w[j]}, m);
+        const float kt = S.row[0][j][c], at = S.row[1][j][c], wt = S.row[2][j][c];
+        const float a2 = at * at, u = __fdividef((float)K * kt * kt, S.r[j]);
+        m = mob_mul(Mob{a2, wt, u * a2, 1.f + u * wt}, m);
       }
     }
   }
+  cp_async_wait_all();
   maps[((size_t)bh * nseg + seg) * K + c] = make_float4(m.A, m.B, m.C, m.D);
 }
 
@@ -435,26 +473,39 @@ __global__ void __launch_bounds__(K) diag_gain_carry_kernel(const float4* __rest
   if (p_final) p_final[(size_t)sh * K + c] = p;
 }
 
-template <int K>
+// Forward pass C: the exact per-token recurrence of every segment from its
+// carried covariance; writes kappa and the covariance before every token.
+template <int K, bool V16>
 __global__ void __launch_bounds__(K) diag_gain_emit_kernel(const float* __restrict__ k, const float* __restrict__ alpha,
                                                            const float* __restrict__ omega,
                                                            const float* __restrict__ r,
                                                            const float* __restrict__ carry,
                                                            float* __restrict__ kappa, float* __restrict__ p_prev,
                                                            int T, int H, int nseg, Varlen v) {
-  constexpr int TT = 4;
+  constexpr int TT = kGainTileF, NS = kGainStagesF;
+  using Stage = GainStage<K, TT, 3, false, false>;
+  __shared__ Stage stg[NS];
   __shared__ float red[K / 32 * TT];
   __shared__ float tok[TT];
   const int seg = blockIdx.x, bh = blockIdx.y, b = bh / H, h = bh - b * H, c = threadIdx.x;
   int t0, n, sh;
   seg_span(v, seg, T, H, bh, t0, n, sh);
   const size_t row0 = ((size_t)b * T + t0) * H + h;
-  GainTile<K, TT, false> cu, nx;
-  nx.load(k, alpha, omega, r, nullptr, row0, H, n, c);
+  const float* const src[3] = {k, alpha, omega};
+  const int ntiles = (n + TT - 1) / TT;
+  auto issue = [&](int it) {
+    if (it < ntiles) stg[it % NS].template load<V16>(src, nullptr, r, nullptr, row0, H, it * TT, min(TT, n - it * TT), 0);
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int i = 0; i < NS - 1; ++i) issue(i);
   float p = carry[((size_t)bh * nseg + seg) * K + c];
-  for (int ts = 0; ts < n; ts += TT) {
-    cu = nx;
-    if (ts + TT < n) nx.load(k, alpha, omega, r, nullptr, row0 + (size_t)(ts + TT) * H, H, n - ts - TT, c);
+  for (int it = 0; it < ntiles; ++it) {
+    cp_async_wait_group<NS - 2>();
+    __syncthreads();
+    issue(it + NS - 1);
+    const Stage& S = stg[it % NS];
+    const int ts = it * TT;
     float num[TT], pk2[TT];
 #pragma unroll
     for (int j = 0; j < TT; ++j) {
@@ -462,30 +513,36 @@ __global__ void __launch_bounds__(K) diag_gain_emit_kernel(const float* __restri
       pk2[j] = 0.f;
       if (ts + j < n) {
         p_prev[(row0 + (size_t)(ts + j) * H) * K + c] = p;  // for the backward
-        const float ph = cu.a[j] * cu.a[j] * p + cu.w[j];
-        const float ksq = cu.k[j] * cu.k[j];
-        num[j] = ph * cu.k[j];
+        const float kt = S.row[0][j][c], at = S.row[1][j][c];
+        const float ph = at * at * p + S.row[2][j][c];
+        const float ksq = kt * kt;
+        num[j] = ph * kt;
         pk2[j] = ph * ksq;
-        const float u = __fdividef((float)K * ksq, cu.r[j]);
+        const float u = __fdividef((float)K * ksq, S.r[j]);
         p = __fdividef(ph, 1.f + u * ph);
       }
     }
     block_token_sums<K, TT>(pk2, red, tok);
 #pragma unroll
     for (int j = 0; j < TT; ++j)
-      if (ts + j < n) kappa[(row0 + (size_t)(ts + j) * H) * K + c] = __fdividef(num[j], cu.r[j] + tok[j]);
+      if (ts + j < n) kappa[(row0 + (size_t)(ts + j) * H) * K + c] = __fdividef(num[j], S.r[j] + tok[j]);
   }
+  cp_async_wait_all();
 }
 
-// Backward pass A: per segment, re-run the covariance from the saved carry,
-// form the per-token channel reductions D_t = r_t + sum p_hat k^2 and
-// G_t = sum dkappa * kappa, and compose the reverse affine maps.
-template <int K>
+// Backward pass A: per segment, form the per-token channel reductions
+// D_t = r_t + sum p_hat k^2 and G_t = sum dkappa * kappa from the covariance
+// before every token (p_prev, saved by the forward), and compose the reverse
+// affine maps.  The tokens of a tile are independent; only the maps compose in
+// order.
+template <int K, bool V16>
 __global__ void __launch_bounds__(K) diag_gain_bwd_map_kernel(
     const float* __restrict__ k, const float* __restrict__ alpha, const float* __restrict__ omega,
     const float* __restrict__ r, const float* __restrict__ dkappa, const float* __restrict__ p_prev,
     float2* __restrict__ maps, float2* __restrict__ dg_tok, int T, int H, int nseg, Varlen v) {
-  constexpr int TT = 2;
+  constexpr int TT = kGainTile, NS = kGainStages;
+  using Stage = GainStage<K, TT, 5, false, false>;
+  __shared__ Stage stg[NS];
   __shared__ float red[K / 32 * 2 * TT];
   __shared__ float tok[2 * TT];  // [sum p_hat k^2 | sum dkappa p_hat k] per token
   const int seg = blockIdx.x, bh = blockIdx.y, b = bh / H, h = bh - b * H, c = threadIdx.x;
@@ -493,41 +550,51 @@ __global__ void __launch_bounds__(K) diag_gain_bwd_map_kernel(
   seg_span(v, seg, T, H, bh, t0, n, sh);
   const size_t row0 = ((size_t)b * T + t0) * H + h;
   const float Kf = (float)K;
-  // the covariance before every token comes from the forward (p_prev): the
-  // tokens of a tile are independent, only the adjoint maps compose in order
-  GainTile<K, TT, true, true> cu, nx;
-  nx.load(k, alpha, omega, r, dkappa, row0, H, n, c, p_prev);
+  const float* const src[5] = {k, alpha, omega, dkappa, p_prev};
+  const int ntiles = (n + TT - 1) / TT;
+  // tile it into stage it % NS; every call commits one group (empty past the end)
+  auto issue = [&](int it) {
+    if (it < ntiles) stg[it % NS].template load<V16>(src, nullptr, r, nullptr, row0, H, it * TT, min(TT, n - it * TT), 0);
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int i = 0; i < NS - 1; ++i) issue(i);
   Aff comp{1.f, 0.f};
-  for (int ts = 0; ts < n; ts += TT) {
-    cu = nx;
-    if (ts + TT < n) nx.load(k, alpha, omega, r, dkappa, row0 + (size_t)(ts + TT) * H, H, n - ts - TT, c, p_prev);
-    float v[2 * TT];
+  for (int it = 0; it < ntiles; ++it) {
+    cp_async_wait_group<NS - 2>();  // tile it has landed (this thread's copies) ...
+    __syncthreads();                // ... everyone's, and no thread still reads tile it - 1
+    issue(it + NS - 1);             // into the stage of tile it - 1
+    const Stage& S = stg[it % NS];
+    const int ts = it * TT;
+    float x[2 * TT];
 #pragma unroll
     for (int j = 0; j < TT; ++j) {
-      v[j] = 0.f;
-      v[TT + j] = 0.f;
+      x[j] = 0.f;
+      x[TT + j] = 0.f;
       if (ts + j < n) {
-        const float ph = cu.a[j] * cu.a[j] * cu.pp[j] + cu.w[j];
-        v[j] = ph * cu.k[j] * cu.k[j];
-        v[TT + j] = cu.dk[j] * ph * cu.k[j];
+        const float kt = S.row[0][j][c], at = S.row[1][j][c];
+        const float ph = at * at * S.row[4][j][c] + S.row[2][j][c];
+        x[j] = ph * kt * kt;
+        x[TT + j] = S.row[3][j][c] * ph * kt;
       }
     }
-    block_token_sums<K, 2 * TT>(v, red, tok);
+    block_token_sums<K, 2 * TT>(x, red, tok);
 #pragma unroll
     for (int j = 0; j < TT; ++j) {
       if (ts + j < n) {
-        const float kt = cu.k[j], rt = cu.r[j];
+        const float kt = S.row[0][j][c], rt = S.r[j];
         const float D = rt + tok[j], iD = __fdividef(1.f, D);
         const float G = tok[TT + j] * iD;
         if (c == 0) dg_tok[(size_t)bh * T + t0 + ts + j] = make_float2(D, G);
-        const float a2 = cu.a[j] * cu.a[j];
-        const float ph = a2 * cu.pp[j] + cu.w[j];
+        const float a2 = S.row[1][j][c] * S.row[1][j][c];
+        const float ph = a2 * S.row[4][j][c] + S.row[2][j][c];
         const float ihh = __fdividef(1.f, 1.f + __fdividef(Kf * kt * kt, rt) * ph);
-        const float pbar_gain = (cu.dk[j] * kt - kt * kt * G) * iD;
+        const float pbar_gain = (S.row[3][j][c] * kt - kt * kt * G) * iD;
         comp = aff_after(comp, Aff{a2 * ihh * ihh, a2 * pbar_gain});
       }
     }
   }
+  cp_async_wait_all();  // only empty groups can be left
   maps[((size_t)bh * nseg + seg) * K + c] = make_float2(comp.A, comp.B);
 }
 
@@ -577,7 +644,10 @@ __global__ void __launch_bounds__(K) diag_gain_bwd_total_kernel(const float2* __
 
 __device__ __forceinline__ float sigmoidf_(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
 
-template <int K>
+// Backward pass B: the reverse adjoint per channel over tiles of TT tokens,
+// last tile first, from the carried lambda of the segment, with the input
+// gradients and the fused softplus VJPs.
+template <int K, bool V16>
 __global__ void __launch_bounds__(K) diag_gain_bwd_emit_kernel(
     const float* __restrict__ k, const float* __restrict__ alpha, const float* __restrict__ omega,
     const float* __restrict__ r, const float* __restrict__ init_prec, const bf16* __restrict__ omega_raw,
@@ -585,53 +655,51 @@ __global__ void __launch_bounds__(K) diag_gain_bwd_emit_kernel(
     const float* __restrict__ lam_carry, const float2* __restrict__ dg_tok, float* __restrict__ dk_out,
     float* __restrict__ dalpha, bf16* __restrict__ domega_raw, bf16* __restrict__ dr_raw,
     float* __restrict__ dinit, float* __restrict__ d_init_cov, int T, int H, int nseg, Varlen v) {
-  constexpr int TT = 4;  // 4-token reverse tiles: about 100 registers, five CTAs per SM
+  constexpr int TT = kGainTile, NS = kGainStages;
+  using Stage = GainStage<K, TT, 5, V16, true>;
+  __shared__ Stage stg[NS];
   __shared__ float red[K / 32 * TT];
   __shared__ float tok[TT];
   const int seg = blockIdx.x, bh = blockIdx.y, b = bh / H, h = bh - b * H, c = threadIdx.x;
   int t0, n, sh;
   seg_span(v, seg, T, H, bh, t0, n, sh);
   const bool first = v.on() ? seg == v.chunk[sh / H] : seg == 0;  // the stream's first segment
-  const size_t row0 = ((size_t)b * T + t0) * H + h;
+  const size_t row0 = ((size_t)b * T + t0) * H + h, tok0 = (size_t)bh * T + t0;
   const float Kf = (float)K;
-  // reverse adjoint over tiles of TT tokens, last tile first; the covariance
-  // before every token (p_prev) was saved by the forward
-  struct Rev {
-    GainTile<K, TT, true, true> g;
-    float2 DG[TT];
-    float wr[TT];
-  };
-  auto load_rev = [&](Rev& x, int ts) {
-    const int m = min(TT, n - ts);
-    x.g.load(k, alpha, omega, r, dkappa, row0 + (size_t)ts * H, H, m, c, p_prev);
-#pragma unroll
-    for (int j = 0; j < TT; ++j) {
-      if (j < m) {
-        const size_t row = row0 + (size_t)(ts + j) * H;
-        x.DG[j] = dg_tok[(size_t)bh * T + t0 + ts + j];
-        x.wr[j] = __bfloat162float(omega_raw[row * K + c]);
-      } else {
-        x.DG[j] = make_float2(1.f, 0.f);
-        x.wr[j] = 0.f;
-      }
+  const float* const src[5] = {k, alpha, omega, dkappa, p_prev};
+  const int ntiles = (n + TT - 1) / TT, last = (ntiles - 1) * TT;
+  // tile it (tokens from last - it * TT) into stage it % NS; one group per call
+  auto issue = [&](int it) {
+    if (it < ntiles) {
+      const int ts = last - it * TT;
+      stg[it % NS].template load<V16>(src, omega_raw, r, dg_tok, row0, H, ts, min(TT, n - ts), tok0);
     }
+    cp_async_commit();
   };
   float lam = lam_carry[((size_t)bh * nseg + seg) * K + c];
-  const int last = ((n - 1) / TT) * TT;
-  Rev cu, nx;
-  load_rev(nx, last);
-  for (int ts = last; ts >= 0; ts -= TT) {
-    cu = nx;
-    if (ts > 0) load_rev(nx, ts - TT);
+#pragma unroll
+  for (int i = 0; i < NS - 1; ++i) issue(i);
+  for (int it = 0; it < ntiles; ++it) {
+    cp_async_wait_group<NS - 2>();
+    __syncthreads();
+    issue(it + NS - 1);
+    const Stage& S = stg[it % NS];
+    const int ts = last - it * TT;
     float ur[TT];
 #pragma unroll
     for (int jj = TT - 1; jj >= 0; --jj) {
       ur[jj] = 0.f;
       if (ts + jj < n) {
         const size_t row = row0 + (size_t)(ts + jj) * H;
-        const float kt = cu.g.k[jj], at = cu.g.a[jj], wt = cu.g.w[jj], rt = cu.g.r[jj], dk = cu.g.dk[jj];
-        const float D = cu.DG[jj].x, G = cu.DG[jj].y, iD = __fdividef(1.f, D), ir = __fdividef(1.f, rt);
-        const float pp = cu.g.pp[jj];
+        const float kt = S.row[0][jj][c], at = S.row[1][jj][c], wt = S.row[2][jj][c], rt = S.r[jj];
+        const float dk = S.row[3][jj][c], pp = S.row[4][jj][c];
+        const float D = S.dg[jj].x, G = S.dg[jj].y, iD = __fdividef(1.f, D), ir = __fdividef(1.f, rt);
+        float wr;
+        if constexpr (V16) {
+          wr = __bfloat162float(S.wr[jj][c]);
+        } else {
+          wr = __bfloat162float(omega_raw[row * K + c]);
+        }
         const float a2 = at * at, ksq = kt * kt;
         const float ph = a2 * pp + wt;
         const float u = Kf * ksq * ir;
@@ -643,7 +711,7 @@ __global__ void __launch_bounds__(K) diag_gain_bwd_emit_kernel(
         const float ubar = -lam * pnext * pnext;
         dk_out[row * K + c] = kbar_gain + ubar * (2.f * Kf * kt * ir);
         dalpha[row * K + c] = 2.f * at * pp * pbar_tot;
-        domega_raw[row * K + c] = __float2bfloat16_rn(pbar_tot * sigmoidf_(cu.wr[jj]));
+        domega_raw[row * K + c] = __float2bfloat16_rn(pbar_tot * sigmoidf_(wr));
         ur[jj] = -ubar * u * ir;
         lam = a2 * pbar_tot;
       }
@@ -651,18 +719,19 @@ __global__ void __launch_bounds__(K) diag_gain_bwd_emit_kernel(
     block_token_sums<K, TT>(ur, red, tok);
     if (c < TT && ts + c < n) {
       const size_t row = row0 + (size_t)(ts + c) * H;
-      const float2 DG = dg_tok[(size_t)bh * T + t0 + ts + c];
+      const float2 DG = S.dg[c];
       const float drt = tok[c] - __fdividef(DG.y, DG.x);
       dr_raw[row] = __float2bfloat16_rn(drt * sigmoidf_(__bfloat162float(r_raw[row])));
     }
   }
+  cp_async_wait_all();
   if (first && d_init_cov) d_init_cov[(size_t)sh * K + c] = lam;  // d L / d p_{-1}
   if (first && dinit) {
     // p_{-1} = 1/mu, so d mu = -sum_c lambda_{-1,c} p_{-1,c}^2
     const float p0 = p_prev[row0 * K + c];
-    float v = -lam * p0 * p0;
-    v = warp_sum(v);
-    if ((c & 31) == 0) atomicAdd(dinit + h, v);
+    float x = -lam * p0 * p0;
+    x = warp_sum(x);
+    if ((c & 31) == 0) atomicAdd(dinit + h, x);
   }
 }
 
@@ -902,14 +971,29 @@ int diag_dims(const char* what, int64_t B, int64_t T, int64_t H, int64_t K, Diag
   return KDN_OK;
 }
 
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+template <int K, bool V16>
+void launch_fwd_map(dim3 grid, const DiagDims& d, const float* k, const float* alpha, const float* omega,
+                    const float* r, float4* maps, cudaStream_t st) {
+  diag_gain_map_kernel<K, V16><<<grid, K, 0, st>>>(k, alpha, omega, r, maps, (int)d.T, (int)d.H, d.nseg, d.v);
+}
+
 int diag_fwd_maps(const DiagDims& d, const float* k, const float* alpha, const float* omega, const float* r,
                   float4* maps, cudaStream_t st) {
   dim3 grid((unsigned)d.nseg, (unsigned)(d.B * d.H));
-  if (d.K == 128)
-    diag_gain_map_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, maps, (int)d.T, (int)d.H, d.nseg, d.v);
-  else
-    diag_gain_map_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, maps, (int)d.T, (int)d.H, d.nseg, d.v);
+  const bool v16 = aligned16(k) && aligned16(alpha) && aligned16(omega);
+  auto f = d.K == 128 ? (v16 ? launch_fwd_map<128, true> : launch_fwd_map<128, false>)
+                      : (v16 ? launch_fwd_map<64, true> : launch_fwd_map<64, false>);
+  f(grid, d, k, alpha, omega, r, maps, st);
   return check_launch("diag_gain_map_kernel");
+}
+
+template <int K, bool V16>
+void launch_fwd_emit(dim3 grid, const DiagDims& d, const float* k, const float* alpha, const float* omega,
+                     const float* r, float* carry, float* kappa, cudaStream_t st) {
+  diag_gain_emit_kernel<K, V16><<<grid, K, 0, st>>>(k, alpha, omega, r, carry, kappa, d.p_prev(carry), (int)d.T,
+                                                    (int)d.H, d.nseg, d.v);
 }
 
 int diag_fwd_finish(const DiagDims& d, const float* k, const float* alpha, const float* omega, const float* r,
@@ -917,16 +1001,14 @@ int diag_fwd_finish(const DiagDims& d, const float* k, const float* alpha, const
                     float* p_final, cudaStream_t st) {
   dim3 grid((unsigned)d.nseg, (unsigned)(d.B * d.H));
   const unsigned sh = d.streams();
-  if (d.K == 128) {
+  if (d.K == 128)
     diag_gain_carry_kernel<128><<<sh, 128, 0, st>>>(maps, init_prec, init_cov, carry, p_final, (int)d.H, d.nseg, d.v);
-    diag_gain_emit_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, carry, kappa, d.p_prev(carry), (int)d.T,
-                                                     (int)d.H, d.nseg,
-                                                     d.v);
-  } else {
+  else
     diag_gain_carry_kernel<64><<<sh, 64, 0, st>>>(maps, init_prec, init_cov, carry, p_final, (int)d.H, d.nseg, d.v);
-    diag_gain_emit_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, carry, kappa, d.p_prev(carry), (int)d.T,
-                                                   (int)d.H, d.nseg, d.v);
-  }
+  const bool v16 = aligned16(k) && aligned16(alpha) && aligned16(omega);
+  auto f = d.K == 128 ? (v16 ? launch_fwd_emit<128, true> : launch_fwd_emit<128, false>)
+                      : (v16 ? launch_fwd_emit<64, true> : launch_fwd_emit<64, false>);
+  f(grid, d, k, alpha, omega, r, carry, kappa, st);
   return check_launch("diag_gain_fwd kernels");
 }
 
@@ -947,16 +1029,32 @@ DiagBwdWs diag_bwd_ws(const DiagDims& d, void* ws) {
   return out;
 }
 
+template <int K, bool V16>
+void launch_bwd_map(dim3 grid, const DiagDims& d, const float* k, const float* alpha, const float* omega,
+                    const float* r, const float* dkappa, const float* carry, const DiagBwdWs& w, cudaStream_t st) {
+  diag_gain_bwd_map_kernel<K, V16><<<grid, K, 0, st>>>(k, alpha, omega, r, dkappa, d.p_prev(carry), w.maps, w.dg_tok,
+                                                       (int)d.T, (int)d.H, d.nseg, d.v);
+}
+
 int diag_bwd_maps(const DiagDims& d, const float* k, const float* alpha, const float* omega, const float* r,
                   const float* dkappa, const float* carry, const DiagBwdWs& w, cudaStream_t st) {
   dim3 grid((unsigned)d.nseg, (unsigned)(d.B * d.H));
-  if (d.K == 128)
-    diag_gain_bwd_map_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, dkappa, d.p_prev(carry), w.maps, w.dg_tok, (int)d.T,
-                                                        (int)d.H, d.nseg, d.v);
-  else
-    diag_gain_bwd_map_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, dkappa, d.p_prev(carry), w.maps, w.dg_tok, (int)d.T,
-                                                      (int)d.H, d.nseg, d.v);
+  const bool v16 = aligned16(k) && aligned16(alpha) && aligned16(omega) && aligned16(dkappa) &&
+                   aligned16(d.p_prev(carry));
+  auto f = d.K == 128 ? (v16 ? launch_bwd_map<128, true> : launch_bwd_map<128, false>)
+                      : (v16 ? launch_bwd_map<64, true> : launch_bwd_map<64, false>);
+  f(grid, d, k, alpha, omega, r, dkappa, carry, w, st);
   return check_launch("diag_gain_bwd_map_kernel");
+}
+
+template <int K, bool V16>
+void launch_bwd_emit(dim3 grid, const DiagDims& d, const float* k, const float* alpha, const float* omega,
+                     const float* r, const float* init_prec, const bf16* wr, const bf16* rr, const float* dkappa,
+                     const float* carry, float* dk, float* dalpha, bf16* domega_raw, bf16* dr_raw, float* dmu,
+                     float* d_init_cov, const DiagBwdWs& w, cudaStream_t st) {
+  diag_gain_bwd_emit_kernel<K, V16><<<grid, K, 0, st>>>(k, alpha, omega, r, init_prec, wr, rr, dkappa,
+                                                        d.p_prev(carry), w.lam, w.dg_tok, dk, dalpha, domega_raw,
+                                                        dr_raw, dmu, d_init_cov, (int)d.T, (int)d.H, d.nseg, d.v);
 }
 
 int diag_bwd_finish(const DiagDims& d, const float* k, const float* alpha, const float* omega, const float* r,
@@ -969,17 +1067,16 @@ int diag_bwd_finish(const DiagDims& d, const float* k, const float* alpha, const
   float* dmu = init_cov ? nullptr : dinit;  // with a carried-in covariance the prior gets no gradient here
   dim3 grid((unsigned)d.nseg, (unsigned)(d.B * d.H));
   const unsigned sh = d.streams();
-  if (d.K == 128) {
+  if (d.K == 128)
     diag_gain_bwd_carry_kernel<128><<<sh, 128, 0, st>>>(w.maps, d_final_cov, w.lam, (int)d.H, d.nseg, d.v);
-    diag_gain_bwd_emit_kernel<128><<<grid, 128, 0, st>>>(k, alpha, omega, r, init_prec, wr, rr, dkappa, d.p_prev(carry), w.lam,
-                                                         w.dg_tok, dk, dalpha, domega_raw, dr_raw, dmu, d_init_cov,
-                                                         (int)d.T, (int)d.H, d.nseg, d.v);
-  } else {
+  else
     diag_gain_bwd_carry_kernel<64><<<sh, 64, 0, st>>>(w.maps, d_final_cov, w.lam, (int)d.H, d.nseg, d.v);
-    diag_gain_bwd_emit_kernel<64><<<grid, 64, 0, st>>>(k, alpha, omega, r, init_prec, wr, rr, dkappa, d.p_prev(carry), w.lam,
-                                                       w.dg_tok, dk, dalpha, domega_raw, dr_raw, dmu, d_init_cov,
-                                                       (int)d.T, (int)d.H, d.nseg, d.v);
-  }
+  const bool v16 = aligned16(k) && aligned16(alpha) && aligned16(omega) && aligned16(dkappa) &&
+                   aligned16(d.p_prev(carry)) && aligned16(wr);
+  auto f = d.K == 128 ? (v16 ? launch_bwd_emit<128, true> : launch_bwd_emit<128, false>)
+                      : (v16 ? launch_bwd_emit<64, true> : launch_bwd_emit<64, false>);
+  f(grid, d, k, alpha, omega, r, init_prec, wr, rr, dkappa, carry, dk, dalpha, domega_raw, dr_raw, dmu, d_init_cov, w,
+    st);
   return check_launch("diag_gain_bwd kernels");
 }
 

@@ -99,6 +99,41 @@ def test_diag_gain_fwd_bwd(T, K):
     assert nmax(rr.grad, drr_ref) < 1e-2
 
 
+def _off16(x):
+    """The same values at an address one element past a 16-byte boundary."""
+    buf = torch.empty(x.numel() + 1, dtype=x.dtype, device=DEV)
+    y = buf[1:].view(x.shape)
+    y.copy_(x)
+    return y
+
+
+@pytest.mark.parametrize("T,K", [(200, 128), (77, 64)])
+def test_diag_gain_unaligned_rows(T, K):
+    """Rows that are not 16-byte aligned take the kernels' 4-byte copy path;
+    it must give what the 16-byte path gives."""
+    torch.manual_seed(T)
+    B, H = 2, 3
+    d = oracle.make_diag_inputs(B, T, H, K=K, V=K, seed=T)
+    prec = (0.1 + torch.nn.functional.softplus(torch.randn(H))).to(DEV)
+    dkappa = torch.randn(B, T, H, K).to(DEV)
+    base = {n: d[n].to(DEV) for n in ("k_gain", "alpha", "omega", "r", "omega_raw", "r_raw")}
+    outs = []
+    for shift in (False, True):
+        x = {n: (_off16(v) if shift and n != "r" and n != "r_raw" else v.clone()) for n, v in base.items()}
+        if shift:
+            assert x["k_gain"].data_ptr() % 16 != 0 and x["omega_raw"].data_ptr() % 16 != 0
+        k = x["k_gain"].requires_grad_(True)
+        alpha = x["alpha"].requires_grad_(True)
+        p = prec.clone().requires_grad_(True)
+        wr = x["omega_raw"].requires_grad_(True)
+        rr = x["r_raw"].requires_grad_(True)
+        kappa = _diag_kdn_gain(k, alpha, x["omega"], x["r"], p, wr, rr)
+        kappa.backward(_off16(dkappa) if shift else dkappa)
+        outs.append([kappa.detach(), k.grad, alpha.grad, p.grad, wr.grad.float(), rr.grad.float()])
+    for a, b in zip(*outs):
+        assert nmax(b, a) < 1e-6
+
+
 # ----------------------------------------------------------------------------- scans
 
 
