@@ -354,6 +354,8 @@ int iso_grid(const char* what, int64_t B, int64_t T, int64_t H, void* ws, size_t
 // 4 x 2: 0.248; register tiles: 0.269-0.302).
 constexpr int kGainTile = 8, kGainStages = 2;   // backward kernels
 constexpr int kGainTileF = 8, kGainStagesF = 2;  // forward kernels
+// Segment maps a carry kernel loads ahead of the sequential chain that applies them.
+constexpr int kCarryBatch = 16;
 template <int K, int TT, int NA, bool WR, bool DG>
 struct alignas(16) GainStage {
   float row[NA][TT][K];
@@ -465,10 +467,18 @@ __global__ void __launch_bounds__(K) diag_gain_carry_kernel(const float4* __rest
   const int sh = blockIdx.x, h = sh % H, c = threadIdx.x;
   const int row = v.on() ? h : sh, s0 = v.on() ? v.chunk[sh / H] : 0, s1 = v.on() ? v.chunk[sh / H + 1] : nseg;
   float p = init_cov ? init_cov[(size_t)sh * K + c] : 1.f / init_prec[h];
-  for (int s = s0; s < s1; ++s) {
-    carry[((size_t)row * nseg + s) * K + c] = p;
-    const float4 m = maps[((size_t)row * nseg + s) * K + c];
-    p = mob_apply(Mob{m.x, m.y, m.z, m.w}, p);
+  // the maps do not depend on p: kCarryBatch of them are loaded before they are applied
+  for (int s = s0; s < s1; s += kCarryBatch) {
+    float4 m[kCarryBatch];
+#pragma unroll
+    for (int i = 0; i < kCarryBatch; ++i)
+      if (s + i < s1) m[i] = maps[((size_t)row * nseg + s + i) * K + c];
+#pragma unroll
+    for (int i = 0; i < kCarryBatch; ++i)
+      if (s + i < s1) {
+        carry[((size_t)row * nseg + s + i) * K + c] = p;
+        p = mob_apply(Mob{m[i].x, m[i].y, m[i].z, m[i].w}, p);
+      }
   }
   if (p_final) p_final[(size_t)sh * K + c] = p;
 }
@@ -606,10 +616,17 @@ __global__ void __launch_bounds__(K) diag_gain_bwd_carry_kernel(const float2* __
   const int sh = blockIdx.x, h = sh % H, c = threadIdx.x;
   const int row = v.on() ? h : sh, s0 = v.on() ? v.chunk[sh / H] : 0, s1 = v.on() ? v.chunk[sh / H + 1] : nseg;
   float lam = d_final_cov ? d_final_cov[(size_t)sh * K + c] : 0.f;
-  for (int s = s1 - 1; s >= s0; --s) {
-    lam_carry[((size_t)row * nseg + s) * K + c] = lam;
-    const float2 m = maps[((size_t)row * nseg + s) * K + c];
-    lam = m.x * lam + m.y;
+  for (int s = s1 - 1; s >= s0; s -= kCarryBatch) {
+    float2 m[kCarryBatch];
+#pragma unroll
+    for (int i = 0; i < kCarryBatch; ++i)
+      if (s - i >= s0) m[i] = maps[((size_t)row * nseg + s - i) * K + c];
+#pragma unroll
+    for (int i = 0; i < kCarryBatch; ++i)
+      if (s - i >= s0) {
+        lam_carry[((size_t)row * nseg + s - i) * K + c] = lam;
+        lam = m[i].x * lam + m[i].y;
+      }
   }
 }
 
