@@ -558,7 +558,14 @@ __device__ void prep_chunk(Chunk<CF>& ch, const Chunk<CF>* src = nullptr, uint64
       make_operands(ch, r, x, gm, gm, qs, ks, kr, qr, kc);
       okr[j] = pack8(kr);
       oqr[j] = pack8(qr);
-      okc[j] = pack8(kc);
+      if constexpr (!SW) {
+        // chunk prep (padded tiles): no raw row is staged under Kc, so Kc is
+        // stored now and only Kr, Qr wait for the barrier (16 registers fewer;
+        // the kernel spilled at its 128-register cap when all three waited)
+        st8(ch.Kc + r * CF::LDK + c0, kc);
+      } else {
+        okc[j] = pack8(kc);
+      }
     }
     __syncthreads();
 #pragma unroll
@@ -567,8 +574,13 @@ __device__ void prep_chunk(Chunk<CF>& ch, const Chunk<CF>* src = nullptr, uint64
       float kr[8], qr[8], kc[8];
       unpack8(kr, okr[j]);
       unpack8(qr, oqr[j]);
-      unpack8(kc, okc[j]);
-      store_operands<CF, SW>(ch, r, c0, kr, qr, kc);
+      if constexpr (!SW) {
+        st8(ch.Kr + r * CF::LDK + c0, kr);
+        st8(ch.Qr + r * CF::LDK + c0, qr);
+      } else {
+        unpack8(kc, okc[j]);
+        store_operands<CF, SW>(ch, r, c0, kr, qr, kc);
+      }
     }
   } else {
 #pragma unroll

@@ -53,6 +53,7 @@ struct PrepLayout {
   static constexpr size_t raw_k = Kr, raw_q = Qr, raw_g = Tb;
   static_assert(raw_g + (size_t)C * kKD * 4 <= small, "raw g rows fit below the chunk scalars");
   static_assert((size_t)C * kKD * 2 <= Qr - Kr, "raw k rows fit under Kr");
+  static_assert(raw_q + (size_t)C * kKD * 2 <= Kc && raw_g >= Tb, "no raw row is staged under Kc (prep_chunk stores Kc early)");
   static constexpr size_t bar = (alias ? base_bytes : base_bytes + rec_tiles);
   static constexpr size_t bytes = bar + 16;
 };
