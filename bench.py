@@ -1060,10 +1060,12 @@ def measure_e2e(step, x, names, args, device, dist, tokens, result="grads"):
         torch.cuda.synchronize(device)
         return start.elapsed_time(stop) / steps
 
-    e2e_run(2)
+    # as many warm-up and timed steps as the main timing: the first uploads
+    # from freshly pinned buffers ran up to twice as slow on a two-GPU box
+    e2e_run(max(3, args.warmup))
     if dist is not None:
         dist.barrier()
-    e2e_ms = e2e_run(max(2, min(args.steps, 5)))
+    e2e_ms = e2e_run(max(3, args.steps))
     if dist is not None:
         t = torch.tensor([e2e_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
